@@ -1,0 +1,388 @@
+"""Benchmark of the nest-splatting render hot path on B200.
+
+One step = one frame of config 2: 1,000,000 surfels whose attributes come from
+an RVQ stream decoded on the fly (6 stages x 256 x 59 fp32 codebooks), rendered
+at 1297x840 (decode -> activate -> preprocess -> tile binning + onesweep sort
+-> blend + 16-level hash grid -> tensor-core MLP -> mask). Synthetic seeded
+scene (no dataset exists on this machine).
+
+N GPUs (torchrun, one rank per GPU, NCCL): every rank renders its own camera of
+the orbit (weak scaling: one frame per GPU per step). RVQ decode is sharded by
+surfel range and followed by an NCCL all-gather of the decoded attributes (the
+only collective). value = total megapixels rendered by all ranks / max-over-
+ranks step time.
+
+--impl reference: the reference's CPU implementation of the path on the host
+cores. The reference CUDA rasterizer cannot be built on this image (its glm
+dependency is absent), so the CPU oracle restatement (oracle/, C++ + OpenMP)
+stands in for it, timed on a bounded sample of the same workload.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "nest-splatting_b200"))
+sys.path.insert(0, ROOT)
+
+METRIC = "frames/s & Mpix/s, 1M surfels 1297×840 @1/2/4/8 B200; RVQ decode GB/s vs HBM"
+UNIT = "Mpix/s"
+WORKLOAD = "config2: 1M RVQ-decoded surfels, 1297x840, 16x2 fp16 hash grid, MLP 32-64-64-3"
+
+
+def peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), float(p["bf16_tflops"]), "measured"
+    except Exception:
+        return 6650.0, 1590.0, "fallback"
+
+
+class ClockSampler:
+    """Samples SM clocks and throttle reasons with nvidia-smi during the timed region."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.samples = []
+        self._stop = threading.Event()
+        self._t = None
+
+    def _run(self):
+        while not self._stop.is_set():
+            try:
+                out = subprocess.run(["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.QUERY}",
+                                      "--format=csv,noheader,nounits"], capture_output=True, text=True,
+                                     timeout=5).stdout.strip()
+                if out:
+                    self.samples.append([x.strip() for x in out.split(",")])
+            except Exception:
+                pass
+            self._stop.wait(0.2)
+
+    def __enter__(self):
+        self._t = threading.Thread(target=self._run, daemon=True)
+        self._t.start()
+        return self
+
+    def __exit__(self, *a):
+        self._stop.set()
+        self._t.join(timeout=10)
+
+    def summary(self):
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        sm = [float(s[1]) for s in self.samples if s[1].replace(".", "").isdigit()]
+        mx = [float(s[2]) for s in self.samples if s[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for s in self.samples for i in range(4) if len(s) > 5 + i and
+                          s[5 + i].lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(self.samples)}
+
+
+def dist_setup(n_gpus):
+    import torch
+    import torch.distributed as dist
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        from datetime import timedelta
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local))
+    elif torch.cuda.is_available():
+        torch.cuda.set_device(0)
+    return world, rank, local
+
+
+def flush_l2(buf):
+    buf.add_(1)  # 256 MB read+write evicts the 126 MB L2
+
+
+def blend_algorithmic_bytes(num_rendered, width, height, channels, table_bytes):
+    """Per blend launch: gathered records (112 B) + point list (4 B) per instance, tile
+    ranges, the per-pixel outputs (C features + 14 aux + 3 final T + 2 counts, fp32)
+    and one pass over the hash table."""
+    tiles = ((width + 15) // 16) * ((height + 15) // 16)
+    return num_rendered * (112 + 4) + tiles * 8 + width * height * (channels + 14 + 5) * 4 + table_bytes
+
+
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+
+    from nest_b200 import _lib, synth
+    from nest_b200.camera import orbit_camera
+    from nest_b200.frame import FrameRenderer
+
+    world, rank, local = dist_setup(args.gpus)
+    dev = torch.device("cuda", local)
+    lib = _lib.load()
+    sc = synth.config2()
+    W, H = sc.camera.width, sc.camera.height
+    cam = orbit_camera(W, H, 60.0, 4.0, 360.0 * rank / max(world, 1))
+    fr = FrameRenderer(sc, device=dev, capacity=10_000_000)
+    view = cam.world_view_transform.to(dev).contiguous()
+    proj = cam.full_proj_transform.to(dev).contiguous()
+    P = sc.P
+    shard = (P + world - 1) // world
+    lo, hi = rank * shard, min(P, (rank + 1) * shard)
+    dec_full = fr.decoded
+    if world > 1:
+        dec_full = torch.empty((shard * world, fr.dims), dtype=torch.float32, device=dev)
+        fr.decoded = dec_full[:P]
+        dec_shard = torch.empty((shard, fr.dims), dtype=torch.float32, device=dev)
+        idx_shard = torch.zeros((shard, fr.stages), dtype=torch.uint8, device=dev)
+        idx_shard[: hi - lo].copy_(fr.rvq_idx[lo:hi])
+
+    from nest_b200 import raster
+
+    def step(events=None):
+        if world > 1:
+            raster.rvq_decode(idx_shard, fr.codebooks, out=dec_shard)
+            dist.all_gather_into_tensor(dec_full, dec_shard)
+            return fr.render(cam, view, proj, events=events, skip_decode=True)
+        return fr.render(cam, view, proj, events=events)
+
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    nst = _lib.NS_FRAME_STAGES
+    stage_ev = [[torch.cuda.Event(enable_timing=True) for _ in range(2 * nst)] for _ in range(args.steps)]
+    for evs in stage_ev:
+        for e in evs:
+            e.record()  # creates the underlying cudaEvent
+    for _ in range(max(args.warmup, 3)):
+        step()
+    torch.cuda.synchronize()
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    launches0 = lib.ns_kernel_launches()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clk:
+        for i in range(args.steps):
+            flush_l2(flush)
+            starts[i].record()
+            step(stage_ev[i])
+            ends[i].record()
+        torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    launches = lib.ns_kernel_launches() - launches0
+    step_ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
+    stage_ms = {name: statistics.mean(ev[2 * k].elapsed_time(ev[2 * k + 1]) for ev in stage_ev)
+                for k, name in enumerate(_lib.STAGE_NAMES)}
+    total_ms = sum(step_ms)
+    t = torch.tensor([total_ms], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    total_ms = float(t.item())
+    ms_per_step = total_ms / args.steps
+    mpix = W * H / 1e6
+    value = world * mpix * 1000.0 / ms_per_step
+
+    # End to end through the public API with host buffers: H2D of the frame's RVQ
+    # index stream and camera, render, D2H of the RGB image, every step.
+    host_idx = sc.rvq_idx.clone().pin_memory()
+    host_cam = torch.stack([cam.world_view_transform, cam.full_proj_transform]).contiguous().pin_memory()
+    host_rgb = torch.empty((3, H, W), dtype=torch.float32).pin_memory()
+    dev_cam = torch.empty((2, 4, 4), dtype=torch.float32, device=dev)
+    e2e_starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    e2e_ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+
+    def e2e_step():
+        if world > 1:
+            idx_shard[: hi - lo].copy_(host_idx[lo:hi], non_blocking=True)
+        else:
+            fr.upload_indices(host_idx)
+        dev_cam.copy_(host_cam, non_blocking=True)
+        if world > 1:
+            raster.rvq_decode(idx_shard, fr.codebooks, out=dec_shard)
+            dist.all_gather_into_tensor(dec_full, dec_shard)
+            rgb = fr.render(cam, dev_cam[0], dev_cam[1], skip_decode=True)
+        else:
+            rgb = fr.render(cam, dev_cam[0], dev_cam[1])
+        host_rgb.copy_(rgb, non_blocking=True)
+
+    for _ in range(2):
+        e2e_step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    for i in range(args.steps):
+        flush_l2(flush)
+        e2e_starts[i].record()
+        e2e_step()
+        e2e_ends[i].record()
+    torch.cuda.synchronize()
+    e2e_ms = sum(s.elapsed_time(e) for s, e in zip(e2e_starts, e2e_ends))
+    t = torch.tensor([e2e_ms], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    e2e_ms_step = float(t.item()) / args.steps
+    h2d = host_idx[lo:hi].numel() if world > 1 else host_idx.numel()
+    h2d += host_cam.numel() * 4
+    d2h = host_rgb.numel() * 4
+
+    # Work statistics of the (identical) frames.
+    samples = float(fr.others[7].sum().item())
+    num_rendered = fr.num_rendered
+    hbm_peak, _, peak_kind = peaks()
+    table_bytes = fr.table.numel() * fr.table.element_size()
+    blend_bytes = blend_algorithmic_bytes(num_rendered, W, H, fr.grid.channels, table_bytes)
+    blend_ms = stage_ms["blend"]
+    achieved = blend_bytes / (blend_ms * 1e-3) / 1e9
+    traffic = None
+    tfile = os.path.join(ROOT, "profiles", "blend_traffic.json")
+    if os.path.exists(tfile):
+        try:
+            with open(tfile) as f:
+                traffic = json.load(f).get("traffic_bytes_per_launch_config2")
+        except Exception:
+            traffic = None
+    rvq_bytes = (hi - lo) * (fr.stages + 4 * fr.dims) if world > 1 else P * (fr.stages + 4 * fr.dims)
+    rvq_gbs = rvq_bytes / (stage_ms["decode"] * 1e-3) / 1e9 if world == 1 else None
+    gather_tbs = samples * 16 * 8 * 4 / (blend_ms * 1e-3) / 1e12
+
+    line = {
+        "metric": METRIC, "value": round(value, 3), "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": max(args.warmup, 3), "ms_per_step": round(ms_per_step, 4), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32 (fp16 hash table, fp16 MLP operands)",
+        "data": "synthetic (seeded config-2 scene; RVQ stream decoded every frame)",
+        "config": {"workload": WORKLOAD, "surfels": P, "width": W, "height": H, "frames_per_step": world,
+                   "parallelism": f"camera-sharded x{world}, RVQ decode surfel-sharded + NCCL all-gather"
+                   if world > 1 else "single GPU",
+                   "l2": "flushed between timed steps (256 MB write)"},
+        "frames_per_s": round(world * 1000.0 / ms_per_step, 3),
+        "stage_ms": {k: round(v, 4) for k, v in stage_ms.items()},
+        "work": {"instances": num_rendered, "blended_samples": int(samples)},
+        "rvq_decode": {"gbs": round(rvq_gbs, 1) if rvq_gbs else None,
+                       "frac_of_hbm": round(rvq_gbs / hbm_peak, 4) if rvq_gbs else None,
+                       "bytes_per_surfel": fr.stages + 4 * fr.dims},
+        "roofline": {"kernel": "blend (render_kernel<__half,32>)", "bound": "hbm",
+                     "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s",
+                     "frac": round(achieved / hbm_peak, 4), "traffic": traffic,
+                     "peak_kind": peak_kind, "algorithmic_bytes": int(blend_bytes),
+                     "hash_gather_tbs": round(gather_tbs, 3)},
+        "e2e": {"value": round(world * mpix * 1000.0 / e2e_ms_step, 3), "unit": UNIT,
+                "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h),
+                "ms_per_step": round(e2e_ms_step, 4)},
+        "gpu_launches": int(launches),
+        "clocks": clk.summary(),
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline(sc, budget_s=args.cpu_budget)
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def oracle_frame(sc, row_stride, threads=None):
+    """One frame of the CPU oracle on a bounded sample (tile rows ty % row_stride == 0).
+    Returns (seconds, sampled pixels)."""
+    import numpy as np
+    import torch
+
+    sys.path.insert(0, os.path.join(ROOT, "tests"))
+    from helpers import api_inputs, raw_attributes
+    from oracle import oracle
+
+    t0 = time.perf_counter()
+    dec = torch.from_numpy(oracle.rvq_decode_c(sc.rvq_idx.numpy(), sc.codebooks.numpy()))
+    inp = api_inputs(sc, raw_attributes(sc, dec))
+    g, cam = sc.grid, sc.camera
+    pre = oracle.preprocess(inp["means3D"].numpy(), inp["scales"].numpy(), inp["rotations"].numpy(),
+                            inp["opacities"].numpy(), cam.world_view_transform.numpy(),
+                            cam.full_proj_transform.numpy(), cam.width, cam.height)
+    keys, vals, ranges = oracle.bin_surfels(pre, cam.width, cam.height)
+    out = oracle.render(pre, vals, ranges, inp["homotrans"].numpy(), inp["ap_level"].numpy(), g.table.float().numpy(),
+                        g.offsets.numpy(), g.gridrange.numpy(), cam.width, cam.height, g.channels, g.level_dim,
+                        g.levels, g.S, g.base_resolution, row_stride=row_stride)
+    rows = [ty for ty in range((cam.height + 15) // 16) if ty % row_stride == 0]
+    ys = np.concatenate([np.arange(ty * 16, min(cam.height, ty * 16 + 16)) for ty in rows])
+    oracle.mlp_oracle(out["out_color"][:, ys, :], sc.mlp, out["out_others"][1][ys, :])
+    dt = time.perf_counter() - t0
+    return dt, len(ys) * cam.width
+
+
+def cpu_baseline(sc, budget_s=30.0, row_stride=4):
+    from oracle import oracle
+    threads = oracle.num_threads()
+    dt, px = oracle_frame(sc, row_stride)
+    return {"value": round(px / dt / 1e6, 4), "unit": UNIT, "cores": threads, "kind": "port",
+            "sample": f"one config-2 frame on the CPU oracle (C++/OpenMP restatement): full RVQ decode, "
+                      f"preprocess, binning and sort of all 1M surfels, blend + MLP of every "
+                      f"{row_stride}th tile row ({px} px); value = sampled px / wall time",
+            "seconds": round(dt, 2)}
+
+
+def run_reference(args):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    from nest_b200 import synth
+    from oracle import oracle
+    sc = synth.config2()
+    threads = oracle.num_threads()
+    # Bounded sample: choose the tile-row stride so that warmup + steps fit ~3 minutes.
+    stride = 4
+    dt, px = oracle_frame(sc, stride)
+    total = dt * (args.steps + max(args.warmup, 1))
+    while total > 180 and stride < 64:
+        stride *= 2
+        dt, px = oracle_frame(sc, stride)
+        total = dt * (args.steps + max(args.warmup, 1))
+    for _ in range(max(args.warmup - 1, 0)):
+        oracle_frame(sc, stride)
+    times = []
+    for _ in range(args.steps):
+        dt, px = oracle_frame(sc, stride)
+        times.append(dt)
+    ms = 1000.0 * sum(times) / len(times)
+    value = px / (ms * 1e-3) / 1e6
+    sample = (f"CPU oracle (C++/OpenMP restatement of the reference path; the reference CUDA rasterizer "
+              f"is unbuildable here: glm absent) per step: full RVQ decode + preprocess + sort of 1M "
+              f"surfels, blend + MLP of every {stride}th tile row ({px} px)")
+    line = {"impl": "reference", "metric": METRIC, "value": round(value, 4), "unit": UNIT, "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 2),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (seeded config-2 scene)",
+            "config": {"workload": WORKLOAD, "sample_row_stride": stride},
+            "cpu_baseline": {"value": round(value, 4), "unit": UNIT, "cores": threads, "kind": "port",
+                             "sample": sample},
+            "e2e": {"value": round(value, 4), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-budget", type=float, default=30.0)
+    args = ap.parse_args()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

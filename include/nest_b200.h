@@ -1,0 +1,216 @@
+/*
+ * nest_b200.h -- C-ABI of the B200-native (sm_100a) nest-splatting render path.
+ *
+ * Plain pointers and sizes only: every buffer is caller-owned device memory
+ * unless a parameter says "host". No entry point allocates device memory, none
+ * throws, none traps: each returns an ns_status code. Kernels are enqueued on
+ * the caller's stream (a cudaStream_t passed as void*; NULL = legacy default).
+ *
+ * Reference interfaces replaced (paths inside NilKel/nest-splatting):
+ *   ns_rasterize_forward  <- RasterizeGaussiansCUDA
+ *                            submodules/diff-surfel-rasterization/rasterize_points.cu:39-242
+ *                            and CudaRasterizer::Rasterizer::forward
+ *                            .../cuda_rasterizer/rasterizer_impl.cu:255-440 (render_mode 0)
+ *   ns_mark_visible       <- markVisible, rasterize_points.cu:452-471 and
+ *                            rasterizer_impl.cu:54-66,198-210
+ *   ns_mlp_forward        <- INGP.rgb_decode / get_color, hash_encoder/modules.py:587-602
+ *                            (tiny-cuda-nn "MLP", no biases, sigmoid on the output)
+ *   ns_rvq_decode         <- no reference counterpart: the RVQ attribute decode of
+ *                            the BASELINE config-0 definition (new scope)
+ *   ns_render_frame       <- gaussian_renderer/__init__.py:render() baseline branch
+ *                            (:178-213, 694-797, 905-1021) fused with an RVQ attribute
+ *                            decode: decode -> activate -> rasterize -> MLP -> mask/bg
+ *   ns_radix_sort_pairs   <- cub::DeviceRadixSort::SortPairs as called at
+ *                            rasterizer_impl.cu:381-386 (stable, bits [0, end_bit))
+ */
+#ifndef NEST_B200_H_
+#define NEST_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum ns_status {
+  NS_OK = 0,
+  NS_ERR_INVALID = 1,      /* a pointer, size or shape argument is invalid */
+  NS_ERR_UNSUPPORTED = 2,  /* channel / level-dim combination or mode not built */
+  NS_ERR_CAPACITY = 3,     /* binning scratch too small: *num_rendered holds the need */
+  NS_ERR_CUDA = 4,         /* a CUDA runtime call failed (see ns_last_cuda_error) */
+  NS_ERR_SCRATCH = 5,      /* a scratch buffer is smaller than ns_*_scratch_bytes() */
+  NS_ERR_DEVICE = 6        /* a kernel recorded an error word (bounded wait ran out,
+                              instance count above capacity in device-count mode) */
+} ns_status;
+
+const char* ns_status_string(int status);
+/* Number of kernels this library has launched in the calling process. */
+uint64_t ns_kernel_launches(void);
+/* cudaError_t of the last failing CUDA call made by this library (0 if none). */
+int ns_last_cuda_error(void);
+int ns_version(void);
+
+/* ------------------------------------------------------------------ settings */
+
+/* Mirrors GaussianRasterizationSettings + HashGridSettings
+ * (diff_surfel_rasterization/__init__.py:277-302). */
+typedef struct ns_raster_settings {
+  int32_t image_height;
+  int32_t image_width;
+  float tanfovx;
+  float tanfovy;
+  float scale_modifier;
+  const float* viewmatrix; /* device [16], world_view_transform (row-vector layout) */
+  const float* projmatrix; /* device [16], full_proj_transform */
+  float beta;              /* kernel sharpening; 0 = plain Gaussian */
+  int32_t if_contract;     /* scene contraction in the hash lookup */
+  int32_t record_transmittance;
+  uint32_t max_intersections; /* 0 = no limit */
+  int32_t prefiltered;
+  /* HashGridSettings */
+  uint32_t levels;            /* L (active levels) */
+  float level_scale_log2;     /* S = log2(per_level_scale) */
+  uint32_t base_resolution;   /* H */
+  int32_t align_corners;
+  uint32_t interpolation;     /* 0 linear, 1 smoothstep */
+  uint32_t channels;          /* C = shape_dims[2], output feature channels */
+  uint32_t level_dim;         /* LD = features.size(1) */
+  int32_t table_fp16;         /* 1: features are fp16, 0: fp32 */
+} ns_raster_settings;
+
+/* Per-surfel inputs of the rasterizer (render_mode 0). */
+typedef struct ns_surfels {
+  int32_t P;
+  const float* means3D;   /* [P,3] */
+  const float* scales;    /* [P,2] activated (exp) scales */
+  const float* rotations; /* [P,4] unit quaternions (w,x,y,z) */
+  const float* opacities; /* [P] activated opacity */
+  const float* homotrans; /* [P,16] build_H output, or NULL: computed from the above */
+  const float* ap_level;  /* [P] appearance level, or NULL: all levels */
+  const void* features;   /* hash table [sum_l T_l, LD], fp32 or fp16 */
+  const int32_t* offsets; /* [L+1] int32 level offsets (rows) */
+  const float* gridrange; /* [2] = (vmin, vmax) */
+} ns_surfels;
+
+/* Outputs (caller-owned, device). cover_pixels / trans_avg may be NULL when
+ * record_transmittance is 0; they are accumulated into (zero them first). */
+typedef struct ns_raster_outputs {
+  float* out_color;   /* [C,H,W] composited features */
+  float* out_others;  /* [14,H,W] depth, alpha, normal(3), median depth, distortion,
+                         count, position(3), level colour(3) */
+  int32_t* radii;     /* [P] */
+  float* cover_pixels;/* [P] or NULL */
+  float* trans_avg;   /* [P] or NULL */
+} ns_raster_outputs;
+
+/* ----------------------------------------------------------- scratch sizes */
+
+/* Per-surfel state kept between forward and backward (the reference geomBuffer). */
+size_t ns_geometry_scratch_bytes(int32_t P);
+/* Per-image state (the reference imgBuffer): tile ranges, final T, contributor counts. */
+size_t ns_image_scratch_bytes(int32_t width, int32_t height);
+/* Key/value sort state for up to max_instances surfel/tile pairs (the binningBuffer). */
+size_t ns_binning_scratch_bytes(int64_t max_instances);
+
+/* ------------------------------------------------------------- rasterizer */
+
+#define NS_FLAG_DEVICE_COUNT 1 /* do not read the instance count back to the host;
+                                  size the sort by the binning capacity instead.
+                                  Overflow is reported as NS_ERR_DEVICE by
+                                  ns_read_device_status. */
+
+/* Forward rasterization, render_mode 0 (baseline hash grid).
+ * geom/image/binning are scratch buffers of at least the ns_*_scratch_bytes size.
+ * num_rendered (host, may be NULL): number of surfel/tile instances. Without
+ * NS_FLAG_DEVICE_COUNT the call synchronises the stream once to read it and
+ * returns NS_ERR_CAPACITY (nothing rendered) when binning is too small. */
+int ns_rasterize_forward(const ns_raster_settings* settings, const ns_surfels* surfels,
+                         const ns_raster_outputs* outputs, void* geom, size_t geom_bytes,
+                         void* binning, size_t binning_bytes, void* image, size_t image_bytes,
+                         int64_t* num_rendered, int flags, void* stream);
+
+/* Reads (and clears) the device error word of a geometry scratch buffer; syncs. */
+int ns_read_device_status(void* geom, int32_t P, void* stream);
+
+/* Frustum visibility (view-space z > 0.2) per point: present[P] (bytes, 0/1). */
+int ns_mark_visible(int32_t P, const float* means3D, const float* viewmatrix,
+                    const float* projmatrix, uint8_t* present, void* stream);
+
+/* ------------------------------------------------------------------ MLP */
+
+/* Bias-free MLP in fp16 with fp32 accumulation: feat [in_dims, npix] (channel-major,
+ * fp32) -> rgb [3, npix] = sigmoid(W3 relu(W2 relu(W1 x))) [:3]. weights: fp16
+ * row-major [out,in] matrices packed back to back (W1 [hidden,in], W2 [hidden,hidden],
+ * W3 [out_dims,hidden]). alpha (optional, [npix]): rgb is zeroed where alpha <= 0;
+ * bg (optional, host [3]): rgb += (1-alpha) bg when bg sums > 0.
+ * Supported: in_dims 32, hidden 64, two hidden layers, out_dims 3. */
+int ns_mlp_forward(const float* feat, int32_t in_dims, int64_t npix, const uint16_t* weights,
+                   int32_t hidden, int32_t out_dims, const float* alpha, const float* bg_host,
+                   float* rgb, void* stream);
+
+/* ------------------------------------------------------------------ RVQ */
+
+/* out[n, d] = sum_{k=0..stages-1} codebooks[k, idx[n,k], d], fp32, stage order.
+ * idx u8 [n, stages]; codebooks fp32 [stages, entries, dims]; out fp32 [n, dims].
+ * Supported: entries <= 256, dims <= 64, stages <= 8. Bit-exact. */
+int ns_rvq_decode(const uint8_t* idx, const float* codebooks, float* out, int64_t n,
+                  int32_t stages, int32_t entries, int32_t dims, void* stream);
+
+/* ------------------------------------------------------------------ sort */
+
+/* Stable LSD radix sort of (key u64, value u32) pairs on bits [0, end_bit).
+ * keys_alt / vals_alt are ping-pong buffers of n elements; the sorted result is
+ * written to keys_out / vals_out. temp: ns_radix_sort_temp_bytes(n) bytes. */
+size_t ns_radix_sort_temp_bytes(int64_t n);
+int ns_radix_sort_pairs(const uint64_t* keys_in, const uint32_t* vals_in, uint64_t* keys_out,
+                        uint32_t* vals_out, uint64_t* keys_alt, uint32_t* vals_alt, int64_t n,
+                        int32_t end_bit, void* temp, size_t temp_bytes, void* stream);
+
+/* ------------------------------------------------------------ fused frame */
+
+/* One frame of the RVQ-driven render: decode -> attribute mix + activation ->
+ * preprocess -> bin/sort -> blend + hash -> MLP (fused) -> mask/background.
+ * Attributes: raw[n] = base[n, 0:10] + mix * decoded[n, 0:10] with the decoded
+ * row layout mean(3) log-scale(2) quaternion(4) opacity-logit(1) SH(48) tex(1);
+ * scale = exp(raw), rotation = normalize(raw), opacity = sigmoid(raw). */
+#define NS_FLAG_SKIP_DECODE 2  /* ns_render_frame: `decoded` already holds the decoded
+                                  attributes (e.g. all-gathered from other ranks) */
+#define NS_FRAME_STAGES 5      /* decode, preprocess, binning, blend, mlp */
+
+typedef struct ns_frame_inputs {
+  int32_t P;
+  const uint8_t* rvq_idx;     /* [P, stages] */
+  const float* codebooks;     /* [stages, entries, dims] */
+  int32_t stages, entries, dims;
+  const float* base;          /* [P, 10] raw base attributes */
+  float mix;                  /* weight of the decoded attributes */
+  float* decoded;             /* [P, dims] output of the decode stage (caller-owned) */
+  const float* ap_level;      /* [P] or NULL */
+  const void* features;       /* hash table */
+  const int32_t* offsets;
+  const float* gridrange;
+  const uint16_t* mlp_weights;/* fp16, as ns_mlp_forward */
+  int32_t mlp_hidden;
+  const float* bg_host;       /* host [3] */
+  void* const* stage_events;  /* NULL, or 2*NS_FRAME_STAGES cudaEvent_t recorded on the
+                                 stream before/after each stage (for stage timing) */
+} ns_frame_inputs;
+
+typedef struct ns_frame_outputs {
+  float* rgb;        /* [3,H,W] */
+  float* out_color;  /* [C,H,W] features */
+  float* out_others; /* [14,H,W] */
+  int32_t* radii;    /* [P] */
+} ns_frame_outputs;
+
+int ns_render_frame(const ns_raster_settings* settings, const ns_frame_inputs* inputs,
+                    const ns_frame_outputs* outputs, void* geom, size_t geom_bytes,
+                    void* binning, size_t binning_bytes, void* image, size_t image_bytes,
+                    int64_t* num_rendered, int flags, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* NEST_B200_H_ */

@@ -1,0 +1,402 @@
+// capi.cu -- the extern "C" entry points of libnest_b200.so (declared in
+// include/nest_b200.h), scratch-buffer carving and the frame pipeline.
+//
+// The pipeline mirrors CudaRasterizer::Rasterizer::forward
+// (rasterizer_impl.cu:255-440): preprocess -> prefix sum -> instance count ->
+// duplicate keys -> radix sort -> tile ranges -> blend. Differences by design:
+// buffers are caller-owned (no resize functors), the prefix sum reuses the
+// per-CTA totals computed by preprocess, the sort is the in-house onesweep sort
+// and, in NS_FLAG_DEVICE_COUNT mode, the instance count never returns to the host.
+#include <atomic>
+#include <cstdio>
+#include <cstring>
+
+#include "kernels.cuh"
+
+
+namespace ns_host {
+static thread_local int g_last_cuda_error = 0;
+static std::atomic<uint64_t> g_launches{0};
+int record_cuda(cudaError_t e) {
+  g_last_cuda_error = (int)e;
+  return NS_ERR_CUDA;
+}
+void count_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
+}  // namespace ns_host
+
+namespace {
+
+using namespace ns;
+
+constexpr size_t kAlign = 256;
+inline size_t align_up(size_t x) { return (x + kAlign - 1) & ~(kAlign - 1); }
+
+// Bump allocator over a caller buffer (a null base only measures).
+struct Carver {
+  char* base;
+  size_t off = 0;
+  template <typename T>
+  T* take(size_t count) {
+    off = align_up(off);
+    T* p = base ? reinterpret_cast<T*>(base + off) : nullptr;
+    off += sizeof(T) * count;
+    return p;
+  }
+};
+
+struct GeomState {
+  SurfelRecord* records;
+  BinInfo* bin;
+  uint32_t* tiles;
+  uint32_t* excl_local;
+  uint32_t* block_sums;
+  uint32_t* block_prefix;
+  int64_t* count;
+  uint32_t* err;
+};
+
+GeomState carve_geom(void* base, int P, size_t* used) {
+  Carver c{reinterpret_cast<char*>(base)};
+  GeomState g;
+  const int nb = preprocess_blocks(P);
+  g.records = c.take<SurfelRecord>((size_t)max(P, 1));
+  g.bin = c.take<BinInfo>((size_t)max(P, 1));
+  g.tiles = c.take<uint32_t>((size_t)max(P, 1));
+  g.excl_local = c.take<uint32_t>((size_t)max(P, 1));
+  g.block_sums = c.take<uint32_t>((size_t)nb);
+  g.block_prefix = c.take<uint32_t>((size_t)nb);
+  g.count = c.take<int64_t>(1);
+  g.err = c.take<uint32_t>(4);
+  if (used) *used = align_up(c.off);
+  return g;
+}
+
+struct ImageState {
+  uint2* ranges;
+  float* final_T;
+  uint32_t* n_contrib;
+};
+
+ImageState carve_image(void* base, int W, int H, size_t* used) {
+  Carver c{reinterpret_cast<char*>(base)};
+  ImageState s;
+  const size_t tiles = (size_t)div_up(W, kTile) * div_up(H, kTile);
+  const size_t HW = (size_t)W * H;
+  s.ranges = c.take<uint2>((size_t)max64(tiles, 1));
+  s.final_T = c.take<float>((size_t)max64(3 * HW, 1));
+  s.n_contrib = c.take<uint32_t>((size_t)max64(2 * HW, 1));
+  if (used) *used = align_up(c.off);
+  return s;
+}
+
+struct BinState {
+  uint64_t* keys_unsorted;
+  uint64_t* keys_alt;
+  uint64_t* keys_sorted;
+  uint32_t* vals_unsorted;
+  uint32_t* vals_alt;
+  uint32_t* vals_sorted;
+  void* sort_temp;
+  size_t sort_temp_bytes;
+};
+
+BinState carve_bin(void* base, int64_t cap, size_t* used) {
+  Carver c{reinterpret_cast<char*>(base)};
+  BinState b;
+  const size_t n = (size_t)max64(cap, 1);
+  b.keys_unsorted = c.take<uint64_t>(n);
+  b.keys_alt = c.take<uint64_t>(n);
+  b.keys_sorted = c.take<uint64_t>(n);
+  b.vals_unsorted = c.take<uint32_t>(n);
+  b.vals_alt = c.take<uint32_t>(n);
+  b.vals_sorted = c.take<uint32_t>(n);
+  b.sort_temp_bytes = radix_sort_temp_bytes(cap);
+  b.sort_temp = c.take<char>(b.sort_temp_bytes);
+  if (used) *used = align_up(c.off);
+  return b;
+}
+
+size_t bin_bytes(int64_t cap) {
+  size_t u = 0;
+  carve_bin(nullptr, cap, &u);
+  return u;
+}
+
+// Largest instance capacity whose binning layout fits in `bytes`.
+int64_t bin_capacity(size_t bytes) {
+  if (bytes < bin_bytes(0)) return -1;
+  int64_t lo = 0, hi = 1;
+  while (bin_bytes(hi) <= bytes && hi < ((int64_t)1 << 40)) hi <<= 1;
+  while (hi - lo > 1) {
+    const int64_t mid = lo + (hi - lo) / 2;
+    if (bin_bytes(mid) <= bytes) lo = mid;
+    else hi = mid;
+  }
+  return lo;
+}
+
+// Next-highest bit of the MSB (rasterizer_impl.cu:35-50).
+uint32_t higher_msb(uint32_t n) {
+  uint32_t msb = sizeof(n) * 4;
+  uint32_t step = msb;
+  while (step > 1) {
+    step /= 2;
+    if (n >> msb) msb += step;
+    else msb -= step;
+  }
+  if (n >> msb) msb++;
+  return msb;
+}
+
+int num_sms() {
+  int dev = 0, sms = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 148;
+  if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return 148;
+  return sms;
+}
+
+int validate_settings(const ns_raster_settings* s) {
+  if (!s) return NS_ERR_INVALID;
+  if (s->image_width <= 0 || s->image_height <= 0) return NS_ERR_INVALID;
+  if (!s->viewmatrix || !s->projmatrix) return NS_ERR_INVALID;
+  if (s->levels == 0) return NS_ERR_UNSUPPORTED;  // level == 0 (per-surfel colours) not built
+  if (s->level_dim == 0 || s->channels == 0) return NS_ERR_INVALID;
+  if (s->levels * s->level_dim > s->channels) return NS_ERR_INVALID;
+  return NS_OK;
+}
+
+// Binning + blend shared by the API forward and the fused frame.
+int bin_and_render(const ns_raster_settings* st, int P, const GeomState& g, const ImageState& im,
+                   void* binning, size_t binning_bytes, const void* features,
+                   const int32_t* offsets, const float* gridrange, float* out_color,
+                   float* out_others, float* cover_pixels, float* trans_avg,
+                   int64_t* num_rendered, int flags, cudaStream_t stream,
+                   void* const* ev = nullptr) {
+  const int W = st->image_width, H = st->image_height;
+  const int gx = div_up(W, kTile), gy = div_up(H, kTile);
+  const int tiles = gx * gy;
+  const int nb = preprocess_blocks(P);
+  int rc = scan_block_sums_launch(g.block_sums, g.block_prefix, nb, g.count, stream);
+  if (rc) return rc;
+  const int64_t cap = bin_capacity(binning_bytes);
+  if (cap < 0) return NS_ERR_SCRATCH;
+  if (flags & NS_FLAG_DEVICE_COUNT) return NS_ERR_UNSUPPORTED;
+  int64_t count = 0;
+  NS_CUDA_TRY(cudaMemcpyAsync(&count, g.count, sizeof(int64_t), cudaMemcpyDeviceToHost, stream));
+  NS_CUDA_TRY(cudaStreamSynchronize(stream));
+  if (num_rendered) *num_rendered = count;
+  if (count > cap) return NS_ERR_CAPACITY;
+  BinState b = carve_bin(binning, cap, nullptr);
+  rc = duplicate_keys_launch(P, preprocess_block_size(), g.bin, g.excl_local, g.block_prefix, gx,
+                             gy, b.keys_unsorted, b.vals_unsorted, cap, g.err, stream);
+  if (rc) return rc;
+  const int end_bit = 32 + (int)higher_msb((uint32_t)tiles);
+  rc = radix_sort_launch(b.keys_unsorted, b.vals_unsorted, b.keys_sorted, b.vals_sorted, b.keys_alt,
+                         b.vals_alt, count, end_bit, b.sort_temp, b.sort_temp_bytes, stream);
+  if (rc) return rc;
+  rc = identify_ranges_launch(b.keys_sorted, nullptr, count, cap, im.ranges, tiles, num_sms(),
+                              stream);
+  if (rc) return rc;
+  if (ev) NS_CUDA_TRY(cudaEventRecord((cudaEvent_t)ev[5], stream));
+  RenderParams rp;
+  rp.W = W;
+  rp.H = H;
+  rp.C = (int)st->channels;
+  rp.LD = (int)st->level_dim;
+  rp.L = st->levels;
+  rp.S = st->level_scale_log2;
+  rp.Hres = st->base_resolution;
+  rp.align_corners = st->align_corners;
+  rp.interp = st->interpolation;
+  rp.contract = st->if_contract;
+  rp.beta = st->beta;
+  rp.max_intersections = st->max_intersections;
+  rp.record_transmittance = st->record_transmittance;
+  rp.ranges = im.ranges;
+  rp.point_list = b.vals_sorted;
+  rp.records = g.records;
+  rp.table = features;
+  rp.offsets = offsets;
+  rp.gridrange = gridrange;
+  rp.out_color = out_color;
+  rp.out_others = out_others;
+  rp.final_T = im.final_T;
+  rp.n_contrib = im.n_contrib;
+  rp.cover_pixels = cover_pixels;
+  rp.trans_avg = trans_avg;
+  if (ev) NS_CUDA_TRY(cudaEventRecord((cudaEvent_t)ev[6], stream));
+  rc = render_launch(rp, st->table_fp16, stream);
+  if (rc) return rc;
+  if (ev) NS_CUDA_TRY(cudaEventRecord((cudaEvent_t)ev[7], stream));
+  return NS_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* ns_status_string(int status) {
+  switch (status) {
+    case NS_OK: return "ok";
+    case NS_ERR_INVALID: return "invalid argument";
+    case NS_ERR_UNSUPPORTED: return "unsupported shape or mode";
+    case NS_ERR_CAPACITY: return "binning scratch too small for the instance count";
+    case NS_ERR_CUDA: return "CUDA runtime error";
+    case NS_ERR_SCRATCH: return "scratch buffer too small";
+    case NS_ERR_DEVICE: return "a kernel recorded an error";
+    default: return "unknown status";
+  }
+}
+
+int ns_last_cuda_error(void) { return ns_host::g_last_cuda_error; }
+uint64_t ns_kernel_launches(void) { return ns_host::g_launches.load(); }
+int ns_version(void) { return 1; }
+
+size_t ns_geometry_scratch_bytes(int32_t P) {
+  size_t u = 0;
+  carve_geom(nullptr, P, &u);
+  return u;
+}
+size_t ns_image_scratch_bytes(int32_t width, int32_t height) {
+  size_t u = 0;
+  carve_image(nullptr, width, height, &u);
+  return u;
+}
+size_t ns_binning_scratch_bytes(int64_t max_instances) { return bin_bytes(max_instances); }
+
+int ns_rasterize_forward(const ns_raster_settings* settings, const ns_surfels* surfels,
+                         const ns_raster_outputs* outputs, void* geom, size_t geom_bytes,
+                         void* binning, size_t binning_bytes, void* image, size_t image_bytes,
+                         int64_t* num_rendered, int flags, void* stream_) {
+  cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_);
+  int rc = validate_settings(settings);
+  if (rc) return rc;
+  if (!surfels || !outputs) return NS_ERR_INVALID;
+  const int P = surfels->P;
+  if (P < 0) return NS_ERR_INVALID;
+  if (num_rendered) *num_rendered = 0;
+  if (P == 0) return NS_OK;
+  if (!surfels->means3D || !surfels->scales || !surfels->rotations || !surfels->opacities ||
+      !surfels->features || !surfels->offsets || !surfels->gridrange)
+    return NS_ERR_INVALID;
+  if (!outputs->out_color || !outputs->out_others || !outputs->radii) return NS_ERR_INVALID;
+  if (settings->record_transmittance && (!outputs->cover_pixels || !outputs->trans_avg))
+    return NS_ERR_INVALID;
+  if (settings->level_dim != 2) return NS_ERR_UNSUPPORTED;
+  if (geom_bytes < ns_geometry_scratch_bytes(P)) return NS_ERR_SCRATCH;
+  if (image_bytes < ns_image_scratch_bytes(settings->image_width, settings->image_height))
+    return NS_ERR_SCRATCH;
+  GeomState g = carve_geom(geom, P, nullptr);
+  ImageState im = carve_image(image, settings->image_width, settings->image_height, nullptr);
+  NS_CUDA_TRY(cudaMemsetAsync(g.err, 0, sizeof(uint32_t), stream));
+  rc = preprocess_api_launch(P, *surfels, settings->scale_modifier, settings->viewmatrix,
+                             settings->projmatrix, settings->image_width, settings->image_height,
+                             g.records, g.bin, outputs->radii, g.tiles, g.excl_local, g.block_sums,
+                             stream);
+  if (rc) return rc;
+  return bin_and_render(settings, P, g, im, binning, binning_bytes, surfels->features,
+                        surfels->offsets, surfels->gridrange, outputs->out_color,
+                        outputs->out_others, outputs->cover_pixels, outputs->trans_avg,
+                        num_rendered, flags, stream);
+}
+
+int ns_read_device_status(void* geom, int32_t P, void* stream_) {
+  cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_);
+  if (!geom || P < 0) return NS_ERR_INVALID;
+  GeomState g = carve_geom(geom, P, nullptr);
+  uint32_t err = 0;
+  NS_CUDA_TRY(cudaMemcpyAsync(&err, g.err, sizeof(uint32_t), cudaMemcpyDeviceToHost, stream));
+  NS_CUDA_TRY(cudaMemsetAsync(g.err, 0, sizeof(uint32_t), stream));
+  NS_CUDA_TRY(cudaStreamSynchronize(stream));
+  return err ? NS_ERR_DEVICE : NS_OK;
+}
+
+int ns_mark_visible(int32_t P, const float* means3D, const float* viewmatrix,
+                    const float* projmatrix, uint8_t* present, void* stream) {
+  if (P < 0) return NS_ERR_INVALID;
+  if (P == 0) return NS_OK;
+  if (!means3D || !viewmatrix || !projmatrix || !present) return NS_ERR_INVALID;
+  return mark_visible_launch(P, means3D, viewmatrix, present,
+                             reinterpret_cast<cudaStream_t>(stream));
+}
+
+int ns_mlp_forward(const float* feat, int32_t in_dims, int64_t npix, const uint16_t* weights,
+                   int32_t hidden, int32_t out_dims, const float* alpha, const float* bg_host,
+                   float* rgb, void* stream) {
+  return mlp_launch(feat, in_dims, npix, weights, hidden, out_dims, alpha, bg_host, rgb,
+                    reinterpret_cast<cudaStream_t>(stream));
+}
+
+int ns_rvq_decode(const uint8_t* idx, const float* codebooks, float* out, int64_t n,
+                  int32_t stages, int32_t entries, int32_t dims, void* stream) {
+  return rvq_decode_launch(idx, codebooks, out, n, stages, entries, dims,
+                           reinterpret_cast<cudaStream_t>(stream));
+}
+
+size_t ns_radix_sort_temp_bytes(int64_t n) { return radix_sort_temp_bytes(n); }
+
+int ns_radix_sort_pairs(const uint64_t* keys_in, const uint32_t* vals_in, uint64_t* keys_out,
+                        uint32_t* vals_out, uint64_t* keys_alt, uint32_t* vals_alt, int64_t n,
+                        int32_t end_bit, void* temp, size_t temp_bytes, void* stream) {
+  if (n > 0 && (!keys_in || !vals_in || !keys_out || !vals_out || !keys_alt || !vals_alt || !temp))
+    return NS_ERR_INVALID;
+  if (keys_in == keys_alt || vals_in == vals_alt) return NS_ERR_INVALID;
+  return radix_sort_launch(keys_in, vals_in, keys_out, vals_out, keys_alt, vals_alt, n, end_bit,
+                           temp, temp_bytes, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int ns_render_frame(const ns_raster_settings* settings, const ns_frame_inputs* in,
+                    const ns_frame_outputs* out, void* geom, size_t geom_bytes, void* binning,
+                    size_t binning_bytes, void* image, size_t image_bytes,
+                    int64_t* num_rendered, int flags, void* stream_) {
+  cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_);
+  int rc = validate_settings(settings);
+  if (rc) return rc;
+  if (!in || !out) return NS_ERR_INVALID;
+  const int P = in->P;
+  if (P < 0) return NS_ERR_INVALID;
+  if (num_rendered) *num_rendered = 0;
+  if (!in->rvq_idx || !in->codebooks || !in->base || !in->decoded || !in->features ||
+      !in->offsets || !in->gridrange || !in->mlp_weights)
+    return NS_ERR_INVALID;
+  if (!out->rgb || !out->out_color || !out->out_others || !out->radii) return NS_ERR_INVALID;
+  if (in->dims < 10) return NS_ERR_INVALID;
+  if (settings->level_dim != 2 || settings->channels != 32) return NS_ERR_UNSUPPORTED;
+  if (settings->record_transmittance) return NS_ERR_UNSUPPORTED;
+  if (geom_bytes < ns_geometry_scratch_bytes(P)) return NS_ERR_SCRATCH;
+  if (image_bytes < ns_image_scratch_bytes(settings->image_width, settings->image_height))
+    return NS_ERR_SCRATCH;
+  const int W = settings->image_width, H = settings->image_height;
+  GeomState g = carve_geom(geom, P, nullptr);
+  ImageState im = carve_image(image, W, H, nullptr);
+  void* const* ev = in->stage_events;
+  NS_CUDA_TRY(cudaMemsetAsync(g.err, 0, sizeof(uint32_t), stream));
+  if (ev) NS_CUDA_TRY(cudaEventRecord((cudaEvent_t)ev[0], stream));
+  if (!(flags & NS_FLAG_SKIP_DECODE)) {
+    rc = rvq_decode_launch(in->rvq_idx, in->codebooks, in->decoded, P, in->stages, in->entries,
+                           in->dims, stream);
+    if (rc) return rc;
+  }
+  if (ev) NS_CUDA_TRY(cudaEventRecord((cudaEvent_t)ev[1], stream));
+  if (ev) NS_CUDA_TRY(cudaEventRecord((cudaEvent_t)ev[2], stream));
+  rc = preprocess_mix_launch(P, in->base, in->decoded, in->dims, in->mix, in->ap_level,
+                             settings->scale_modifier, settings->viewmatrix, settings->projmatrix,
+                             W, H, g.records, g.bin, out->radii, g.tiles, g.excl_local,
+                             g.block_sums, stream);
+  if (rc) return rc;
+  if (ev) NS_CUDA_TRY(cudaEventRecord((cudaEvent_t)ev[3], stream));
+  if (ev) NS_CUDA_TRY(cudaEventRecord((cudaEvent_t)ev[4], stream));
+  rc = bin_and_render(settings, P, g, im, binning, binning_bytes, in->features, in->offsets,
+                      in->gridrange, out->out_color, out->out_others, nullptr, nullptr,
+                      num_rendered, flags & ~NS_FLAG_SKIP_DECODE, stream, ev);
+  if (rc) return rc;
+  const size_t HW = (size_t)W * H;
+  if (ev) NS_CUDA_TRY(cudaEventRecord((cudaEvent_t)ev[8], stream));
+  rc = mlp_launch(out->out_color, (int)settings->channels, (int64_t)HW, in->mlp_weights,
+                  in->mlp_hidden, 3, out->out_others + HW, in->bg_host, out->rgb, stream);
+  if (rc) return rc;
+  if (ev) NS_CUDA_TRY(cudaEventRecord((cudaEvent_t)ev[9], stream));
+  return NS_OK;
+}
+
+}  // extern "C"

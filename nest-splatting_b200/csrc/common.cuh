@@ -1,0 +1,98 @@
+// common.cuh -- shared constants, small vector math and error plumbing for the
+// sm_100a kernels of the nest-splatting render path.
+#pragma once
+
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "nest_b200.h"
+
+namespace ns {
+
+// Tile geometry and rasterizer constants (cuda_rasterizer/config.h:17-18,
+// auxiliary.h:42-45 of the reference).
+constexpr int kTile = 16;
+constexpr int kTilePixels = kTile * kTile;
+constexpr float kNear = 0.2f;
+constexpr float kFar = 100.0f;
+constexpr float kFilterSize = 0.707106f;
+constexpr float kFilterInvSquare = 2.0f;
+constexpr int kOtherChannels = 14;
+
+// Device error word bits (written by kernels, read by ns_read_device_status).
+constexpr uint32_t kErrLookbackTimeout = 1u;
+constexpr uint32_t kErrCapacity = 2u;
+constexpr uint32_t kErrSpinTimeout = 4u;
+
+// Upper bound on spin iterations of any wait in these kernels. A wait that runs
+// out records an error bit and continues, so no kernel can hang the GPU.
+constexpr uint32_t kSpinLimit = 1u << 22;
+
+// Per-surfel render record: 8 float4 = 128 bytes, one L2 line, written by the
+// preprocess kernel and gathered by the blend kernel.
+//   q0 = (Tu.x, Tu.y, Tu.z, Tv.x)      q1 = (Tv.y, Tv.z, Tw.x, Tw.y)
+//   q2 = (Tw.z, xy.x, xy.y, opacity)    q3 = (n.x, n.y, n.z, ap_level bits)
+//   q4 = (SuTu.x, SuTu.y, SuTu.z, SvTv.x)  q5 = (SvTv.y, SvTv.z, pk.x, pk.y)
+//   q6 = (pk.z, 0, 0, 0)                 q7 = unused
+struct alignas(16) SurfelRecord {
+  float4 q[8];
+};
+constexpr int kRecordFloat4 = 7;  // float4 words the blend kernel reads
+
+// Binning info per surfel: (x, y, radius, depth) as float4, radius as int bits.
+struct alignas(16) BinInfo {
+  float x, y;
+  int radius;
+  float depth;
+};
+
+__host__ __device__ inline int div_up(int a, int b) { return (a + b - 1) / b; }
+__host__ __device__ inline int64_t div_up64(int64_t a, int64_t b) { return (a + b - 1) / b; }
+__host__ __device__ inline int64_t min64(int64_t a, int64_t b) { return a < b ? a : b; }
+__host__ __device__ inline int64_t max64(int64_t a, int64_t b) { return a > b ? a : b; }
+
+__device__ __forceinline__ float3 f3(float x, float y, float z) { return make_float3(x, y, z); }
+__device__ __forceinline__ float3 operator-(float3 a, float3 b) {
+  return make_float3(a.x - b.x, a.y - b.y, a.z - b.z);
+}
+__device__ __forceinline__ float3 operator*(float f, float3 a) {
+  return make_float3(f * a.x, f * a.y, f * a.z);
+}
+__device__ __forceinline__ float3 cross3(float3 a, float3 b) {
+  return make_float3(a.y * b.z - a.z * b.y, a.z * b.x - a.x * b.z, a.x * b.y - a.y * b.x);
+}
+
+// Tile rectangle of a screen-space disc (auxiliary.h:72-82).
+__device__ __forceinline__ void tile_rect(float px, float py, int r, int gx, int gy, int& x0,
+                                          int& y0, int& x1, int& y1) {
+  x0 = min(gx, max(0, (int)((px - r) / kTile)));
+  y0 = min(gy, max(0, (int)((py - r) / kTile)));
+  x1 = min(gx, max(0, (int)((px + r + kTile - 1) / kTile)));
+  y1 = min(gy, max(0, (int)((py + r + kTile - 1) / kTile)));
+}
+
+__device__ __forceinline__ void set_error(uint32_t* err, uint32_t bit) {
+  if (err) atomicOr(err, bit);
+}
+
+}  // namespace ns
+
+// Host-side helpers shared by the .cu files (defined in capi.cu).
+namespace ns_host {
+int record_cuda(cudaError_t e);  // stores e as the last CUDA error, returns NS_ERR_CUDA
+void count_launch();             // one more kernel launched by this library
+}
+
+#define NS_CUDA_TRY(expr)                                       \
+  do {                                                          \
+    cudaError_t _e = (expr);                                    \
+    if (_e != cudaSuccess) return ns_host::record_cuda(_e);     \
+  } while (0)
+
+#define NS_LAUNCH_CHECK()                                       \
+  do {                                                          \
+    ns_host::count_launch();                                    \
+    cudaError_t _e = cudaGetLastError();                        \
+    if (_e != cudaSuccess) return ns_host::record_cuda(_e);     \
+  } while (0)

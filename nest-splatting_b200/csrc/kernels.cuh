@@ -1,0 +1,64 @@
+// kernels.cuh -- internal launch interfaces shared by the .cu files of
+// libnest_b200.so (not part of the public C-ABI).
+#pragma once
+
+#include "common.cuh"
+
+namespace ns {
+struct RenderParams {
+  int W, H;
+  int C, LD;
+  uint32_t L;
+  float S;
+  uint32_t Hres;
+  int align_corners;
+  uint32_t interp;
+  int contract;
+  float beta;
+  uint32_t max_intersections;
+  int record_transmittance;
+  const uint2* ranges;
+  const uint32_t* point_list;
+  const SurfelRecord* records;
+  const void* table;
+  const int32_t* offsets;
+  const float* gridrange;
+  float* out_color;
+  float* out_others;
+  float* final_T;
+  uint32_t* n_contrib;
+  float* cover_pixels;
+  float* trans_avg;
+};
+int rvq_decode_launch(const uint8_t*, const float*, float*, int64_t, int, int, int, cudaStream_t);
+int preprocess_blocks(int P);
+int preprocess_block_size();
+int preprocess_api_launch(int P, const ns_surfels& s, float mod, const float* vm, const float* pm,
+                          int W, int H, SurfelRecord* records, BinInfo* bin, int32_t* radii,
+                          uint32_t* tiles, uint32_t* excl_local, uint32_t* block_sums,
+                          cudaStream_t stream);
+int preprocess_mix_launch(int P, const float* base, const float* decoded, int dims, float mix,
+                          const float* ap_level, float mod, const float* vm, const float* pm, int W,
+                          int H, SurfelRecord* records, BinInfo* bin, int32_t* radii,
+                          uint32_t* tiles, uint32_t* excl_local, uint32_t* block_sums,
+                          cudaStream_t stream);
+int mark_visible_launch(int P, const float* means3D, const float* vm, uint8_t* present,
+                        cudaStream_t stream);
+int scan_block_sums_launch(const uint32_t* sums, uint32_t* prefix, int nb, int64_t* total,
+                           cudaStream_t stream);
+int duplicate_keys_launch(int P, int block_size, const BinInfo* bin, const uint32_t* excl_local,
+                          const uint32_t* block_prefix, int gx, int gy, uint64_t* keys,
+                          uint32_t* vals, int64_t capacity, uint32_t* err, cudaStream_t stream);
+int identify_ranges_launch(const uint64_t* keys, const int64_t* count_dev, int64_t count_host,
+                           int64_t capacity, uint2* ranges, int tiles, int sms,
+                           cudaStream_t stream);
+size_t radix_sort_temp_bytes(int64_t n);
+int radix_sort_launch(const uint64_t* keys_in, const uint32_t* vals_in, uint64_t* keys_out,
+                      uint32_t* vals_out, uint64_t* keys_alt, uint32_t* vals_alt, int64_t n,
+                      int end_bit, void* temp, size_t temp_bytes, cudaStream_t stream);
+uint32_t* radix_sort_error_word(void* temp);
+int render_launch(const RenderParams& p, int fp16, cudaStream_t stream);
+int mlp_launch(const float* feat, int in_dims, int64_t npix, const uint16_t* weights, int hidden,
+               int out_dims, const float* alpha, const float* bg_host, float* rgb,
+               cudaStream_t stream);
+}  // namespace ns

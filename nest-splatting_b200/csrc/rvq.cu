@@ -1,0 +1,142 @@
+// rvq.cu -- residual-vector-quantised attribute decode.
+//
+// out[n, d] = sum_{k=0..K-1} codebooks[k, idx[n,k], d], accumulated in fp32 from
+// +0.0 in stage order k = 0, 1, ... (the reference repository
+// has no RVQ code, so this is new scope with a bit-exact contract).
+//
+// Shared-memory kernel (the fast path). The whole codebook of the benchmark
+// shape (6 x 256 x 59 fp32 = 354 KB) does not fit one SM's 227 KB of shared
+// memory, so the dimension axis is split in two halves of 32 columns and each
+// CTA holds all stages of one half (6 x 256 x 32 x 4 = 192 KB). CTAs are
+// persistent (one per SM) and walk 512-surfel chunks. Inside a chunk a
+// half-warp owns one surfel: lane j reads a float2 of columns (2j, 2j+1) of the
+// selected codeword of each stage (conflict-free: the half-warp reads one
+// contiguous 128-byte half row), so a warp decodes two surfels per step. Index
+// bytes are packed to one u64 per surfel in shared memory so the six stage
+// indices cost one broadcast read. The next chunk's indices are fetched into
+// registers while the current chunk is decoded.
+//
+// Bound: HBM (6 B of indices read + 4*dims B written per surfel); the shared
+// memory gather (6 x 128 B per surfel-half) runs at about the same time, so
+// the two overlap.
+#include "common.cuh"
+
+namespace ns {
+namespace {
+
+constexpr int kRvqThreads = 512;
+constexpr int kRvqChunk = 512;   // surfels per chunk (one per thread for index loads)
+constexpr int kHalfCols = 32;
+
+__global__ void __launch_bounds__(kRvqThreads, 1)
+rvq_decode_smem_kernel(const uint8_t* __restrict__ idx, const float* __restrict__ cb,
+                       float* __restrict__ out, int64_t n, int K, int E, int D) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  float* cb_s = reinterpret_cast<float*>(smem_raw);                    // [K*E][32]
+  uint64_t* idx_s = reinterpret_cast<uint64_t*>(cb_s + (size_t)K * E * kHalfCols);  // [chunk]
+
+  const int half = blockIdx.y;
+  const int col0 = half * kHalfCols;
+  const int tid = threadIdx.x;
+  const int lane = tid & 31, warp = tid >> 5;
+
+  // Stage this half of every codeword into shared memory (zero-padded columns).
+  const int rows = K * E;
+  for (int i = tid; i < rows * kHalfCols; i += kRvqThreads) {
+    int r = i >> 5, j = i & 31;
+    int c = col0 + j;
+    cb_s[i] = (c < D) ? __ldg(cb + (size_t)r * D + c) : 0.0f;
+  }
+
+  const int64_t nchunks = div_up64(n, kRvqChunk);
+  int64_t chunk = blockIdx.x;
+
+  // Prefetch the indices of the first chunk into registers.
+  auto load_idx = [&](int64_t ch) -> uint64_t {
+    int64_t s = ch * kRvqChunk + tid;
+    uint64_t v = 0;
+    if (ch < nchunks && s < n) {
+      const uint8_t* p = idx + s * K;
+      for (int k = 0; k < K; k++) v |= (uint64_t)__ldg(p + k) << (8 * k);
+    }
+    return v;
+  };
+  uint64_t next = load_idx(chunk);
+
+  const int sub = lane >> 4;        // which surfel of the pair
+  const int l16 = lane & 15;        // float2 column within the half row
+  const int c2 = col0 + 2 * l16;    // first output column of this lane
+  const float2* cb2 = reinterpret_cast<const float2*>(cb_s);
+
+  for (; chunk < nchunks; chunk += gridDim.x) {
+    __syncthreads();  // previous chunk fully consumed (and the codebook staged)
+    idx_s[tid] = next;
+    __syncthreads();
+    next = load_idx(chunk + gridDim.x);
+
+    const int64_t base = chunk * kRvqChunk;
+    const int cnt = (int)min64(kRvqChunk, n - base);
+#pragma unroll 4
+    for (int it = 0; it < 16; it++) {
+      const int s = warp * 32 + 2 * it + sub;
+      if (s >= cnt) break;
+      const uint64_t packed = idx_s[s];
+      float ax = 0.0f, ay = 0.0f;
+      for (int k = 0; k < K; k++) {
+        const int e = (int)((packed >> (8 * k)) & 0xff);
+        const float2 v = cb2[(k * E + e) * (kHalfCols / 2) + l16];
+        ax += v.x;
+        ay += v.y;
+      }
+      float* o = out + (base + s) * D;
+      if (c2 < D) o[c2] = ax;
+      if (c2 + 1 < D) o[c2 + 1] = ay;
+    }
+  }
+}
+
+// General shape: one thread per output value, codebook rows read through L1/L2.
+__global__ void rvq_decode_gather_kernel(const uint8_t* __restrict__ idx,
+                                         const float* __restrict__ cb, float* __restrict__ out,
+                                         int64_t n, int K, int E, int D) {
+  int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  int64_t total = n * D;
+  for (; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    int64_t s = i / D;
+    int d = (int)(i - s * D);
+    float acc = 0.0f;
+    for (int k = 0; k < K; k++) acc += __ldg(cb + ((size_t)k * E + idx[s * K + k]) * D + d);
+    out[i] = acc;
+  }
+}
+
+}  // namespace
+
+int rvq_decode_launch(const uint8_t* idx, const float* cb, float* out, int64_t n, int K, int E,
+                      int D, cudaStream_t stream) {
+  if (n < 0 || K <= 0 || K > 8 || E <= 0 || E > 256 || D <= 0 || D > 64) return NS_ERR_UNSUPPORTED;
+  if (n == 0) return NS_OK;
+  if (!idx || !cb || !out) return NS_ERR_INVALID;
+  const size_t smem = (size_t)K * E * kHalfCols * sizeof(float) + kRvqChunk * sizeof(uint64_t);
+  int dev = 0, sms = 0, max_smem = 0;
+  NS_CUDA_TRY(cudaGetDevice(&dev));
+  NS_CUDA_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+  NS_CUDA_TRY(cudaDeviceGetAttribute(&max_smem, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev));
+  if (smem <= (size_t)max_smem) {
+    NS_CUDA_TRY(cudaFuncSetAttribute(rvq_decode_smem_kernel,
+                                     cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    const int halves = D > kHalfCols ? 2 : 1;
+    const int64_t nchunks = div_up64(n, kRvqChunk);
+    int gx = (int)min64(nchunks, (int64_t)max(1, sms / halves));
+    rvq_decode_smem_kernel<<<dim3(gx, halves), kRvqThreads, smem, stream>>>(idx, cb, out, n, K, E,
+                                                                             D);
+  } else {
+    int64_t total = n * D;
+    int blocks = (int)min64(div_up64(total, 256), (int64_t)sms * 16);
+    rvq_decode_gather_kernel<<<blocks, 256, 0, stream>>>(idx, cb, out, n, K, E, D);
+  }
+  NS_LAUNCH_CHECK();
+  return NS_OK;
+}
+
+}  // namespace ns

@@ -1,0 +1,198 @@
+"""Drop-in replacement of the reference's `diff_surfel_rasterization` module.
+
+Same names, fields and call signatures as
+submodules/diff-surfel-rasterization/diff_surfel_rasterization/__init__.py of
+NilKel/nest-splatting (GaussianRasterizationSettings :277-293,
+HashGridSettings :295-302, GaussianRasterizer :304-396, rasterize_gaussians
+:21-66, _RasterizeGaussians :68-275, compute_relocation :398-414). The forward
+pass runs the sm_100a kernels of libnest_b200.so through its C-ABI; there is
+no CPU fallback. Built: render_mode 0 (baseline hash grid) with the Gaussian
+kernel (kernel_type 0) and level_dim 2. Other modes raise NotImplementedError
+instead of silently rendering nothing as the reference does for shapes it was
+not compiled for.
+
+`features` may be fp32 (as the reference stores the table) or fp16 (read as
+fp16 pairs by the kernels, half the L2 traffic).
+"""
+from __future__ import annotations
+
+import math
+import os
+import sys
+from typing import NamedTuple
+
+import torch
+import torch.nn as nn
+
+_PKG_ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+if _PKG_ROOT not in sys.path:
+    sys.path.insert(0, _PKG_ROOT)
+
+from nest_b200 import raster as _raster  # noqa: E402
+
+
+def cpu_deep_copy_tuple(input_tuple):
+    return tuple(item.cpu().clone() if isinstance(item, torch.Tensor) else item for item in input_tuple)
+
+
+def rasterize_gaussians(means3D, means2D, sh, colors_precomp, opacities, scales, rotations,
+                        cov3Ds_precomp, homotrans, ap_level, features, offsets, gridrange,
+                        features_diffuse, offsets_diffuse, gridrange_diffuse, raster_settings,
+                        hashgrid_settings, render_mode, shapes, kernel_type):
+    return _RasterizeGaussians.apply(means3D, means2D, sh, colors_precomp, opacities, scales, rotations,
+                                     cov3Ds_precomp, homotrans, ap_level, features, offsets, gridrange,
+                                     features_diffuse, offsets_diffuse, gridrange_diffuse, raster_settings,
+                                     hashgrid_settings, render_mode, shapes, kernel_type)
+
+
+def _nonempty(t):
+    return t if (t is not None and t.numel() > 0) else None
+
+
+def _shape_dims(hashgrid_settings):
+    sd = hashgrid_settings.shape_dims
+    if sd is not None and torch.is_tensor(sd) and sd.numel() == 3:
+        return [int(x) for x in sd.tolist()]
+    return [0, 0, 3]
+
+
+class _RasterizeGaussians(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, means3D, means2D, sh, colors_precomp, opacities, scales, rotations, cov3Ds_precomp,
+                homotrans, ap_level, features, offsets, gridrange, features_diffuse, offsets_diffuse,
+                gridrange_diffuse, raster_settings, hashgrid_settings, render_mode, shapes, kernel_type):
+        if int(render_mode) != 0:
+            raise NotImplementedError(f"render_mode {render_mode}: only 0 (baseline hash grid) is built")
+        if int(kernel_type) != 0:
+            raise NotImplementedError(f"kernel_type {kernel_type}: only 0 (Gaussian) is built")
+        if _nonempty(cov3Ds_precomp) is not None:
+            raise NotImplementedError("precomputed transforms (cov3D_precomp) are not built")
+        if means3D.ndim != 2 or means3D.shape[1] != 3:
+            raise RuntimeError("means3D must have dimensions (num_points, 3)")
+        L = int(hashgrid_settings.L)
+        if L <= 0 or _nonempty(features) is None:
+            raise NotImplementedError("level == 0 (per-surfel colours) is not built")
+        _, _, OS = _shape_dims(hashgrid_settings)
+        feats = features.contiguous()
+        if feats.dtype not in (torch.float16, torch.float32):
+            feats = feats.float()
+        cfg = _raster.RasterConfig(
+            image_height=int(raster_settings.image_height), image_width=int(raster_settings.image_width),
+            tanfovx=float(raster_settings.tanfovx), tanfovy=float(raster_settings.tanfovy),
+            viewmatrix=raster_settings.viewmatrix.contiguous().float(),
+            projmatrix=raster_settings.projmatrix.contiguous().float(),
+            scale_modifier=float(raster_settings.scale_modifier), beta=float(raster_settings.beta),
+            if_contract=bool(raster_settings.if_contract),
+            record_transmittance=bool(raster_settings.record_transmittance),
+            max_intersections=int(raster_settings.max_intersections),
+            prefiltered=bool(raster_settings.prefiltered), levels=L, S=float(hashgrid_settings.S),
+            base_resolution=int(hashgrid_settings.H), align_corners=bool(hashgrid_settings.align_corners),
+            interpolation=int(hashgrid_settings.interpolation), channels=int(OS),
+            level_dim=int(feats.shape[1]), table_fp16=feats.dtype == torch.float16)
+        ap = _nonempty(ap_level)
+        num_rendered, color, others, radii, cover, trans, scratch = _raster.rasterize_forward(
+            cfg, means3D.contiguous().float(), scales.contiguous().float(), rotations.contiguous().float(),
+            opacities.contiguous().float().reshape(-1),
+            None if _nonempty(homotrans) is None else homotrans.contiguous().float().reshape(-1, 16),
+            None if ap is None else ap.contiguous().float().reshape(-1), feats,
+            offsets.contiguous().to(torch.int32), gridrange.contiguous().float())
+        ctx.raster_settings = raster_settings
+        ctx.hashgrid_settings = hashgrid_settings
+        ctx.num_rendered = num_rendered
+        ctx.scratch = scratch
+        return color, radii, others, trans, cover
+
+    @staticmethod
+    def backward(ctx, grad_out_color, grad_radii, grad_depth, grad_0, grad_1):
+        raise NotImplementedError("the rasterizer backward pass is not built yet")
+
+
+class GaussianRasterizationSettings(NamedTuple):
+    image_height: int
+    image_width: int
+    tanfovx: float
+    tanfovy: float
+    bg: torch.Tensor
+    scale_modifier: float
+    viewmatrix: torch.Tensor
+    projmatrix: torch.Tensor
+    sh_degree: int
+    campos: torch.Tensor
+    prefiltered: bool
+    debug: bool
+    beta: float
+    if_contract: bool
+    record_transmittance: bool
+    max_intersections: int = 0  # 0 means no limit
+
+
+class HashGridSettings(NamedTuple):
+    L: int
+    S: float
+    H: int
+    align_corners: bool
+    interpolation: int
+    shape_dims: torch.Tensor  # [GS, HS, OS]
+
+
+class GaussianRasterizer(nn.Module):
+    def __init__(self, raster_settings, hashgrid_settings):
+        super().__init__()
+        self.raster_settings = raster_settings
+        self.hashgrid_settings = hashgrid_settings
+
+    def markVisible(self, positions):
+        with torch.no_grad():
+            rs = self.raster_settings
+            return _raster.mark_visible(positions.contiguous().float(), rs.viewmatrix.contiguous().float(),
+                                        rs.projmatrix.contiguous().float())
+
+    def forward(self, means3D, means2D, opacities, shs=None, colors_precomp=None, scales=None, rotations=None,
+                cov3D_precomp=None, homotrans=None, ap_level=None, features=None, offsets=None, gridrange=None,
+                features_diffuse=None, offsets_diffuse=None, gridrange_diffuse=None, render_mode=0, shapes=None,
+                kernel_type=0):
+        if (shs is None and colors_precomp is None) or (shs is not None and colors_precomp is not None):
+            raise Exception('Please provide excatly one of either SHs or precomputed colors!')
+        if ((scales is None or rotations is None) and cov3D_precomp is None) or \
+                ((scales is not None or rotations is not None) and cov3D_precomp is not None):
+            raise Exception('Please provide exactly one of either scale/rotation pair or precomputed 3D covariance!')
+        dev = means3D.device
+        empty = lambda dtype=torch.float32: torch.empty(0, dtype=dtype, device=dev)  # noqa: E731
+        shs = empty() if shs is None else shs
+        colors_precomp = empty() if colors_precomp is None else colors_precomp
+        scales = empty() if scales is None else scales
+        rotations = empty() if rotations is None else rotations
+        cov3D_precomp = empty() if cov3D_precomp is None else cov3D_precomp
+        homotrans = empty() if homotrans is None else homotrans
+        ap_level = empty() if ap_level is None else ap_level
+        features = empty() if features is None else features
+        offsets = empty(torch.int32) if offsets is None else offsets
+        gridrange = empty() if gridrange is None else gridrange
+        features_diffuse = empty() if features_diffuse is None else features_diffuse
+        offsets_diffuse = empty(torch.int32) if offsets_diffuse is None else offsets_diffuse
+        gridrange_diffuse = empty() if gridrange_diffuse is None else gridrange_diffuse
+        shapes = empty() if shapes is None else shapes
+        return rasterize_gaussians(means3D, means2D, shs, colors_precomp, opacities, scales, rotations,
+                                   cov3D_precomp, homotrans, ap_level, features, offsets, gridrange,
+                                   features_diffuse, offsets_diffuse, gridrange_diffuse, self.raster_settings,
+                                   self.hashgrid_settings, render_mode, shapes, kernel_type)
+
+
+def compute_relocation(opacity_old, scale_old, N, binoms, n_max):
+    """3DGS-MCMC relocation (cuda_rasterizer/utils.cu:4-32), a torch restatement.
+
+    Outside the render hot path; kept so that callers of the reference module
+    find the same function.
+    """
+    N = N.int()
+    new_opacity = 1.0 - torch.pow(1.0 - opacity_old, 1.0 / N.float())
+    denom = torch.zeros_like(opacity_old)
+    for i in range(1, int(n_max) + 1):
+        active = (N >= i).float()
+        for k in range(i):
+            coeff = binoms[i - 1, k]
+            term = ((-1.0) ** k / math.sqrt(k + 1)) * torch.pow(new_opacity, k + 1)
+            denom = denom + active * coeff * term
+    coeff = opacity_old / denom
+    new_scale = coeff.reshape(-1, 1) * scale_old
+    return new_opacity, new_scale

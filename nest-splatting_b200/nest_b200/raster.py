@@ -1,0 +1,219 @@
+"""Torch-facing wrappers of the C-ABI (device memory and streams come from torch).
+
+Every function here enqueues the library's kernels on torch's current CUDA
+stream. Tensors must be contiguous CUDA tensors of the stated dtypes.
+"""
+from __future__ import annotations
+
+import ctypes as C
+from dataclasses import dataclass
+
+import torch
+
+from . import _lib
+from ._lib import check, ptr
+
+OTHER_CHANNELS = 14
+
+
+def _require_cuda(*ts):
+    for t in ts:
+        if t is not None and (not t.is_cuda or not t.is_contiguous()):
+            raise ValueError("expected contiguous CUDA tensors")
+
+
+@dataclass
+class RasterConfig:
+    """Plain mirror of GaussianRasterizationSettings + HashGridSettings."""
+    image_height: int
+    image_width: int
+    tanfovx: float
+    tanfovy: float
+    viewmatrix: torch.Tensor
+    projmatrix: torch.Tensor
+    scale_modifier: float = 1.0
+    beta: float = 0.0
+    if_contract: bool = False
+    record_transmittance: bool = False
+    max_intersections: int = 0
+    prefiltered: bool = False
+    levels: int = 16
+    S: float = 0.0
+    base_resolution: int = 16
+    align_corners: bool = False
+    interpolation: int = 0
+    channels: int = 32
+    level_dim: int = 2
+    table_fp16: bool = True
+
+    def to_c(self) -> _lib.RasterSettings:
+        s = _lib.RasterSettings()
+        s.image_height = int(self.image_height)
+        s.image_width = int(self.image_width)
+        s.tanfovx = float(self.tanfovx)
+        s.tanfovy = float(self.tanfovy)
+        s.scale_modifier = float(self.scale_modifier)
+        s.viewmatrix = self.viewmatrix.data_ptr()
+        s.projmatrix = self.projmatrix.data_ptr()
+        s.beta = float(self.beta)
+        s.if_contract = int(bool(self.if_contract))
+        s.record_transmittance = int(bool(self.record_transmittance))
+        s.max_intersections = int(self.max_intersections)
+        s.prefiltered = int(bool(self.prefiltered))
+        s.levels = int(self.levels)
+        s.level_scale_log2 = float(self.S)
+        s.base_resolution = int(self.base_resolution)
+        s.align_corners = int(bool(self.align_corners))
+        s.interpolation = int(self.interpolation)
+        s.channels = int(self.channels)
+        s.level_dim = int(self.level_dim)
+        s.table_fp16 = int(bool(self.table_fp16))
+        return s
+
+
+class Scratch:
+    """Per-device scratch buffers reused across calls (grown on demand)."""
+
+    def __init__(self):
+        self.geom = None
+        self.image = None
+        self.binning = None
+        self.capacity = 0
+
+    @staticmethod
+    def _ensure(buf, nbytes, device):
+        if buf is None or buf.numel() < nbytes or buf.device != device:
+            return torch.empty(max(int(nbytes), 1), dtype=torch.uint8, device=device)
+        return buf
+
+    def geometry(self, P, device):
+        lib = _lib.load()
+        self.geom = self._ensure(self.geom, lib.ns_geometry_scratch_bytes(P), device)
+        return self.geom
+
+    def image_buf(self, W, H, device):
+        lib = _lib.load()
+        self.image = self._ensure(self.image, lib.ns_image_scratch_bytes(W, H), device)
+        return self.image
+
+    def bins(self, capacity, device):
+        lib = _lib.load()
+        if self.binning is None or capacity > self.capacity or self.binning.device != device:
+            self.capacity = int(capacity)
+            self.binning = torch.empty(lib.ns_binning_scratch_bytes(self.capacity), dtype=torch.uint8,
+                                       device=device)
+        return self.binning
+
+
+def rasterize_forward(cfg: RasterConfig, means3D, scales, rotations, opacities, homotrans, ap_level,
+                      features, offsets, gridrange, scratch: Scratch | None = None,
+                      capacity_hint: int | None = None):
+    """Forward rasterization (render_mode 0) through ns_rasterize_forward.
+
+    Returns (num_rendered, out_color [C,H,W], out_others [14,H,W], radii [P] int32,
+    cover_pixels [P,1], trans_avg [P,1], scratch).
+    """
+    lib = _lib.load()
+    dev = means3D.device
+    P = means3D.shape[0]
+    H, W = int(cfg.image_height), int(cfg.image_width)
+    Cc = int(cfg.channels)
+    _require_cuda(means3D, scales, rotations, opacities, homotrans, ap_level, features, offsets,
+                  gridrange, cfg.viewmatrix, cfg.projmatrix)
+    out_color = torch.zeros((Cc, H, W), dtype=torch.float32, device=dev)
+    out_others = torch.zeros((OTHER_CHANNELS, H, W), dtype=torch.float32, device=dev)
+    radii = torch.zeros((P,), dtype=torch.int32, device=dev)
+    rec_P = P if cfg.record_transmittance else 0
+    cover = torch.zeros((rec_P, 1), dtype=torch.float32, device=dev)
+    trans = torch.zeros((rec_P, 1), dtype=torch.float32, device=dev)
+    if P == 0:
+        return 0, out_color, out_others, radii, cover, trans, scratch
+    scratch = scratch or Scratch()
+    settings = cfg.to_c()
+    surf = _lib.Surfels()
+    surf.P = P
+    surf.means3D, surf.scales, surf.rotations = ptr(means3D), ptr(scales), ptr(rotations)
+    surf.opacities, surf.homotrans, surf.ap_level = ptr(opacities), ptr(homotrans), ptr(ap_level)
+    surf.features, surf.offsets, surf.gridrange = ptr(features), ptr(offsets), ptr(gridrange)
+    outs = _lib.RasterOutputs()
+    outs.out_color, outs.out_others, outs.radii = ptr(out_color), ptr(out_others), ptr(radii)
+    outs.cover_pixels = ptr(cover) if rec_P else None
+    outs.trans_avg = ptr(trans) if rec_P else None
+    geom = scratch.geometry(P, dev)
+    image = scratch.image_buf(W, H, dev)
+    cap = max(scratch.capacity, capacity_hint or 4 * P, 1024)
+    stream = _lib.stream_handle(dev)
+    n = C.c_int64(0)
+    for _ in range(2):
+        binning = scratch.bins(cap, dev)
+        rc = lib.ns_rasterize_forward(C.byref(settings), C.byref(surf), C.byref(outs),
+                                      geom.data_ptr(), geom.numel(), binning.data_ptr(),
+                                      binning.numel(), image.data_ptr(), image.numel(), C.byref(n),
+                                      0, stream)
+        if rc == _lib.NS_ERR_CAPACITY:
+            cap = int(n.value * 1.25) + 1024
+            continue
+        check("ns_rasterize_forward", rc)
+        break
+    return int(n.value), out_color, out_others, radii, cover, trans, scratch
+
+
+def mark_visible(means3D, viewmatrix, projmatrix) -> torch.Tensor:
+    lib = _lib.load()
+    _require_cuda(means3D, viewmatrix, projmatrix)
+    P = means3D.shape[0]
+    present = torch.zeros((P,), dtype=torch.bool, device=means3D.device)
+    check("ns_mark_visible", lib.ns_mark_visible(P, ptr(means3D), ptr(viewmatrix), ptr(projmatrix),
+                                                 ptr(present), _lib.stream_handle(means3D.device)))
+    return present
+
+
+def pack_mlp(weights) -> torch.Tensor:
+    """Packs fp16 [out,in] matrices back to back (the ns_mlp_forward layout)."""
+    return torch.cat([w.reshape(-1) for w in weights]).to(torch.float16).contiguous()
+
+
+def mlp_forward(feat_chw: torch.Tensor, packed_weights: torch.Tensor, alpha=None, bg=None,
+                hidden: int = 64) -> torch.Tensor:
+    """RGB [3, ...] = sigmoid(MLP(features)) * (alpha > 0) (+ (1-alpha) bg)."""
+    lib = _lib.load()
+    Cin = feat_chw.shape[0]
+    npix = feat_chw[0].numel()
+    _require_cuda(feat_chw, packed_weights, alpha)
+    rgb = torch.empty((3,) + tuple(feat_chw.shape[1:]), dtype=torch.float32, device=feat_chw.device)
+    bg_arr = None
+    if bg is not None:
+        b = [float(x) for x in (bg.tolist() if torch.is_tensor(bg) else bg)]
+        bg_arr = (C.c_float * 3)(*b)
+    check("ns_mlp_forward", lib.ns_mlp_forward(ptr(feat_chw), Cin, npix, ptr(packed_weights), hidden, 3,
+                                               ptr(alpha), C.cast(bg_arr, C.c_void_p) if bg_arr else None,
+                                               ptr(rgb), _lib.stream_handle(feat_chw.device)))
+    return rgb
+
+
+def rvq_decode(idx: torch.Tensor, codebooks: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    lib = _lib.load()
+    _require_cuda(idx, codebooks)
+    assert idx.dtype == torch.uint8 and codebooks.dtype == torch.float32
+    n, K = idx.shape
+    Kc, E, D = codebooks.shape
+    assert Kc == K
+    if out is None:
+        out = torch.empty((n, D), dtype=torch.float32, device=idx.device)
+    check("ns_rvq_decode", lib.ns_rvq_decode(ptr(idx), ptr(codebooks), ptr(out), n, K, E, D,
+                                             _lib.stream_handle(idx.device)))
+    return out
+
+
+def radix_sort_pairs(keys: torch.Tensor, vals: torch.Tensor, end_bit: int = 64):
+    """Stable sort of (int64 key viewed as u64, int32 value viewed as u32) pairs."""
+    lib = _lib.load()
+    _require_cuda(keys, vals)
+    n = keys.numel()
+    ko, vo = torch.empty_like(keys), torch.empty_like(vals)
+    ka, va = torch.empty_like(keys), torch.empty_like(vals)
+    temp = torch.empty(max(1, lib.ns_radix_sort_temp_bytes(n)), dtype=torch.uint8, device=keys.device)
+    check("ns_radix_sort_pairs", lib.ns_radix_sort_pairs(ptr(keys), ptr(vals), ptr(ko), ptr(vo), ptr(ka),
+                                                         ptr(va), n, end_bit, ptr(temp), temp.numel(),
+                                                         _lib.stream_handle(keys.device)))
+    return ko, vo

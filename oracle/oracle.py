@@ -1,0 +1,219 @@
+"""CPU oracle for the nest-splatting render path -- TEST INFRASTRUCTURE ONLY.
+
+Only tests/, __graft_entry__.smoke() and bench.py's cpu_baseline / reference
+arm may import this module, and only as the checker (or the CPU baseline):
+the product path (nest-splatting_b200) never calls it.
+
+Contents:
+  * ctypes wrapper of oracle/_build/libnest_oracle.so (nest_oracle.cpp, the C++
+    restatement of preprocess / binning / mode-0 blend / hash query);
+  * rvq_decode_np: numpy restatement of the RVQ decode;
+  * rvq_decode_torch: the "reference PyTorch CPU path" timed as the RVQ baseline;
+  * mlp_oracle: fp16 MLP restatement (tiny-cuda-nn is not vendored: parity of
+    the MLP is unpinned, this fixes one definition);
+  * forward / frame helpers chaining the above.
+
+Parity status: pinned by the known-answer tests in tests/test_oracle.py and, for
+the camera and homotrans inputs, by tests/golden (made by importing the
+reference's own Python utilities). The reference CUDA rasterizer cannot be
+built here (its glm dependency is absent), so the blend restatement itself is
+"parity unpinned" against reference outputs.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+import subprocess
+from pathlib import Path
+
+import numpy as np
+
+HERE = Path(__file__).resolve().parent
+LIB_PATH = HERE / "_build" / "libnest_oracle.so"
+KBLOCK = 16
+
+_lib = None
+
+
+def build() -> Path:
+    subprocess.run(["make", "-s", "-C", str(HERE)], check=True)
+    return LIB_PATH
+
+
+def load() -> C.CDLL:
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not LIB_PATH.exists():
+        build()
+    lib = C.CDLL(str(LIB_PATH))
+    vp, i32, u32, i64, f32 = C.c_void_p, C.c_int, C.c_uint32, C.c_int64, C.c_float
+    lib.oracle_preprocess.argtypes = [i32, vp, vp, f32, vp, vp, vp, vp, i32, i32, vp, vp, vp, vp, vp, vp]
+    lib.oracle_bin.restype = i64
+    lib.oracle_bin.argtypes = [i32, vp, vp, vp, i32, i32, vp, vp, i64, vp]
+    lib.oracle_render.argtypes = [i32, i32, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, i32, i32, u32, f32, u32,
+                                  i32, u32, i32, f32, u32, i32, vp, vp, vp, vp, vp, vp, i32]
+    lib.oracle_query.argtypes = [i32, vp, vp, vp, vp, f32, f32, i32, i32, u32, f32, u32, i32, u32, i32, vp]
+    lib.oracle_grid_index.restype = u32
+    lib.oracle_grid_index.argtypes = [i32, u32, u32, u32, u32, u32]
+    lib.oracle_rvq_decode.argtypes = [i64, i32, i32, i32, vp, vp, vp]
+    lib.oracle_num_threads.restype = i32
+    _lib = lib
+    return lib
+
+
+def _p(a: np.ndarray):
+    return a.ctypes.data_as(C.c_void_p) if a is not None else None
+
+
+def _f32(a) -> np.ndarray:
+    return np.ascontiguousarray(np.asarray(a, dtype=np.float32))
+
+
+def preprocess(means3D, scales, rotations, opacities, viewmatrix, projmatrix, W, H, scale_modifier=1.0):
+    """forward.cu:323-441 restated. Returns dict of per-surfel arrays."""
+    lib = load()
+    means3D, scales, rotations = _f32(means3D), _f32(scales), _f32(rotations)
+    opacities = _f32(opacities).reshape(-1)
+    vm, pm = _f32(viewmatrix).reshape(16), _f32(projmatrix).reshape(16)
+    P = means3D.shape[0]
+    out = dict(radii=np.zeros(P, np.int32), means2D=np.zeros((P, 2), np.float32), depths=np.zeros(P, np.float32),
+               transMat=np.zeros((P, 9), np.float32), normal_opacity=np.zeros((P, 4), np.float32),
+               tiles_touched=np.zeros(P, np.uint32))
+    lib.oracle_preprocess(P, _p(means3D), _p(scales), float(scale_modifier), _p(rotations), _p(opacities), _p(vm),
+                          _p(pm), int(W), int(H), _p(out["radii"]), _p(out["means2D"]), _p(out["depths"]),
+                          _p(out["transMat"]), _p(out["normal_opacity"]), _p(out["tiles_touched"]))
+    return out
+
+
+def bin_surfels(pre, W, H):
+    """duplicateWithKeys + stable sort + identifyTileRanges. Returns (keys, vals, ranges [tiles,2])."""
+    lib = load()
+    P = pre["radii"].shape[0]
+    tiles = ((W + KBLOCK - 1) // KBLOCK) * ((H + KBLOCK - 1) // KBLOCK)
+    cap = int(pre["tiles_touched"].astype(np.int64).sum())
+    keys = np.zeros(max(cap, 1), np.uint64)
+    vals = np.zeros(max(cap, 1), np.uint32)
+    ranges = np.zeros((tiles, 2), np.uint32)
+    n = lib.oracle_bin(P, _p(pre["means2D"]), _p(pre["depths"]), _p(pre["radii"]), int(W), int(H), _p(keys),
+                       _p(vals), cap, _p(ranges))
+    assert n == cap, (n, cap)
+    return keys[:n], vals[:n], ranges
+
+
+def render(pre, vals, ranges, homotrans, ap_level, table_f32, offsets, gridrange, W, H, C_out, LD, L, S, Hres,
+           align_corners=False, interp=0, contract=False, beta=0.0, max_intersections=0,
+           record_transmittance=False, row_stride=1):
+    """renderCUDAsurfelForward<C> mode 0 restated. Returns dict of output images.
+
+    row_stride > 1 renders only tile rows ty with ty % row_stride == 0 (a bounded
+    sample for CPU timing); other pixels stay zero."""
+    lib = load()
+    HW = W * H
+    P = pre["radii"].shape[0]
+    out = dict(out_color=np.zeros((C_out, H, W), np.float32), out_others=np.zeros((14, H, W), np.float32),
+               final_T=np.zeros((3, H, W), np.float32), n_contrib=np.zeros((2, H, W), np.uint32),
+               cover_pixels=np.zeros(P, np.float32), trans_avg=np.zeros(P, np.float32))
+    homotrans = _f32(homotrans).reshape(-1, 16)
+    ap = _f32(ap_level).reshape(-1) if ap_level is not None else np.full(P, 1e9, np.float32)
+    table = _f32(table_f32)
+    offs = np.ascontiguousarray(np.asarray(offsets, dtype=np.int32))
+    gr = _f32(gridrange).reshape(2)
+    lib.oracle_render(int(W), int(H), _p(np.ascontiguousarray(ranges, np.uint32)),
+                      _p(np.ascontiguousarray(vals, np.uint32)), _p(pre["means2D"]), _p(pre["transMat"]),
+                      _p(pre["normal_opacity"]), _p(homotrans), _p(ap), _p(table), _p(offs), _p(gr), int(C_out),
+                      int(LD), int(L), float(S), int(Hres), int(bool(align_corners)), int(interp),
+                      int(bool(contract)), float(beta), int(max_intersections), int(bool(record_transmittance)),
+                      _p(out["out_color"]), _p(out["out_others"]), _p(out["final_T"]), _p(out["n_contrib"]),
+                      _p(out["cover_pixels"]), _p(out["trans_avg"]), int(row_stride))
+    assert HW == W * H
+    return out
+
+
+def query(xyz, ap_level, table_f32, offsets, vmin, vmax, C_out, LD, L, S, Hres, align_corners=False, interp=0,
+          contract=False):
+    lib = load()
+    xyz = _f32(xyz).reshape(-1, 3)
+    n = xyz.shape[0]
+    ap = np.ascontiguousarray(np.asarray(ap_level, dtype=np.uint32).reshape(-1))
+    out = np.zeros((n, C_out), np.float32)
+    lib.oracle_query(n, _p(xyz), _p(ap), _p(_f32(table_f32)), _p(np.ascontiguousarray(offsets, np.int32)),
+                     float(vmin), float(vmax), int(C_out), int(LD), int(L), float(S), int(Hres),
+                     int(bool(align_corners)), int(interp), int(bool(contract)), _p(out))
+    return out
+
+
+def grid_index(align_corners, hashmap_size, res, x, y, z) -> int:
+    return int(load().oracle_grid_index(int(bool(align_corners)), hashmap_size, res, x, y, z))
+
+
+def rvq_decode_np(idx: np.ndarray, codebooks: np.ndarray) -> np.ndarray:
+    """out[n] = (((0 + CB0[i0]) + CB1[i1]) + ...) in fp32, stage order."""
+    idx = np.asarray(idx)
+    cb = np.asarray(codebooks, dtype=np.float32)
+    out = np.zeros((idx.shape[0], cb.shape[2]), np.float32)
+    for k in range(cb.shape[0]):
+        out += cb[k][idx[:, k].astype(np.int64)]
+    return out
+
+
+def rvq_decode_c(idx: np.ndarray, codebooks: np.ndarray) -> np.ndarray:
+    """The same decode through the C++ oracle (OpenMP over surfels)."""
+    lib = load()
+    idx = np.ascontiguousarray(idx, dtype=np.uint8)
+    cb = _f32(codebooks)
+    K, E, D = cb.shape
+    out = np.empty((idx.shape[0], D), np.float32)
+    lib.oracle_rvq_decode(idx.shape[0], K, E, D, _p(idx), _p(cb), _p(out))
+    return out
+
+
+def rvq_decode_torch(idx, codebooks):
+    """PyTorch CPU restatement (index_select + in-order adds): the timed CPU baseline."""
+    import torch
+    idx = idx.long()
+    out = torch.zeros((idx.shape[0], codebooks.shape[2]), dtype=torch.float32)
+    for k in range(codebooks.shape[0]):
+        out += codebooks[k].index_select(0, idx[:, k])
+    return out
+
+
+def mlp_oracle(feat_np: np.ndarray, weights, alpha=None, bg=None) -> np.ndarray:
+    """feat [C, ...] fp32 -> rgb [3, ...]: fp16 operands, fp32 accumulation, each layer
+    (and the network output) rounded to fp16, sigmoid in fp32, x (alpha > 0), + (1-alpha) bg."""
+    import torch
+    shape = feat_np.shape[1:]
+    x = torch.as_tensor(np.asarray(feat_np, np.float32)).reshape(feat_np.shape[0], -1).T
+    h = x.half().float()
+    ws = [torch.as_tensor(np.asarray(w)).half().float() for w in weights]
+    for i, w in enumerate(ws):
+        h = h @ w.T
+        if i < len(ws) - 1:
+            h = torch.clamp_min(h, 0.0)
+        h = h.half().float()
+    rgb = torch.sigmoid(h[:, :3]).T.reshape((3,) + tuple(shape)).numpy().astype(np.float32)
+    if alpha is not None:
+        a = np.asarray(alpha, np.float32).reshape(shape)
+        rgb = rgb * (a > 0)
+        if bg is not None and float(np.sum(bg)) > 0:
+            rgb = rgb + (1.0 - a)[None] * np.asarray(bg, np.float32).reshape(3, *([1] * len(shape)))
+    return rgb.astype(np.float32)
+
+
+def forward(means3D, scales, rotations, opacities, homotrans, ap_level, table_f32, offsets, gridrange,
+            viewmatrix, projmatrix, W, H, C_out, LD, L, S, Hres, **kw):
+    """Full oracle forward: preprocess -> bin -> render. Returns (render dict, pre, num_rendered)."""
+    pre = preprocess(means3D, scales, rotations, opacities, viewmatrix, projmatrix, W, H,
+                     kw.pop("scale_modifier", 1.0))
+    keys, vals, ranges = bin_surfels(pre, W, H)
+    out = render(pre, vals, ranges, homotrans, ap_level, table_f32, offsets, gridrange, W, H, C_out, LD, L, S,
+                 Hres, **kw)
+    return out, pre, len(vals)
+
+
+def num_threads() -> int:
+    return int(load().oracle_num_threads())
+
+
+if __name__ == "__main__":
+    print(build(), os.cpu_count())

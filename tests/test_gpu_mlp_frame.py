@@ -1,0 +1,76 @@
+"""GPU parity of the tensor-core MLP and of the fused RVQ frame
+(decode -> activate -> rasterize -> MLP -> mask) against the CPU oracle chain."""
+import numpy as np
+import pytest
+import torch
+
+from helpers import api_inputs, oracle_render, psnr, raw_attributes, small_scene
+from nest_b200 import raster, synth
+from nest_b200.frame import FrameRenderer
+from oracle import oracle
+
+pytestmark = pytest.mark.gpu
+TOL = 2e-3
+
+
+@pytest.mark.parametrize("npix", [1, 15, 16, 1000, 77_777])
+def test_mlp_matches_oracle(npix):
+    g = torch.Generator().manual_seed(npix)
+    ws = synth.xavier_mlp(g)
+    feat = torch.randn(32, npix, generator=g) * 2.0
+    alpha = torch.rand(npix, generator=g)
+    alpha[::5] = 0.0
+    rgb = raster.mlp_forward(feat.cuda(), raster.pack_mlp(ws).cuda(), alpha.cuda()).cpu().numpy()
+    ref = oracle.mlp_oracle(feat.numpy(), ws, alpha.numpy())
+    assert np.abs(rgb - ref).max() <= TOL
+    assert np.all(rgb[:, ::5] == 0)
+
+
+def test_mlp_background():
+    g = torch.Generator().manual_seed(7)
+    ws = synth.xavier_mlp(g)
+    feat = torch.randn(32, 40, 30, generator=g)
+    alpha = torch.rand(40, 30, generator=g)
+    bg = np.array([0.2, 0.5, 1.0], np.float32)
+    rgb = raster.mlp_forward(feat.cuda(), raster.pack_mlp(ws).cuda(), alpha.cuda(), bg=bg).cpu().numpy()
+    ref = oracle.mlp_oracle(feat.numpy(), ws, alpha.numpy(), bg=bg)
+    assert np.abs(rgb - ref).max() <= TOL
+
+
+def frame_oracle(sc):
+    decoded = torch.from_numpy(oracle.rvq_decode_np(sc.rvq_idx.numpy(), sc.codebooks.numpy()))
+    raw = raw_attributes(sc, decoded)
+    inp = api_inputs(sc, raw)
+    out, pre, n = oracle_render(sc, inp)
+    rgb = oracle.mlp_oracle(out["out_color"], sc.mlp, out["out_others"][1])
+    return decoded.numpy(), out, pre, n, rgb
+
+
+@pytest.mark.parametrize("table_range", [1e-4, 1.0])
+def test_fused_frame_matches_oracle(table_range):
+    sc = small_scene(n=2500, seed=21, rvq=True, table_range=table_range)
+    decoded, out, pre, n, rgb_ref = frame_oracle(sc)
+    fr = FrameRenderer(sc)
+    rgb = fr.render(sc.camera)
+    torch.cuda.synchronize()
+    assert np.array_equal(fr.decoded.cpu().numpy().view(np.uint32), decoded.view(np.uint32))
+    assert abs(fr.num_rendered - n) <= max(2, n // 1000)
+    feats = fr.features.cpu().numpy()
+    assert np.abs(feats - out["out_color"]).max() <= TOL
+    others = fr.others.cpu().numpy()
+    for ch in (0, 1, 2, 3, 4, 5):
+        assert np.abs(others[ch] - out["out_others"][ch]).max() <= TOL * max(1.0, np.abs(out["out_others"][ch]).max())
+    rgb = rgb.cpu().numpy()
+    assert np.abs(rgb - rgb_ref).max() <= TOL
+    assert psnr(rgb, rgb_ref) >= 60
+
+
+def test_fused_frame_repeatable_and_index_upload():
+    sc = small_scene(n=2000, seed=22, rvq=True)
+    fr = FrameRenderer(sc)
+    a = fr.render(sc.camera).clone()
+    host = sc.rvq_idx.clone().pin_memory()
+    fr.upload_indices(host)
+    b = fr.render(sc.camera).clone()
+    torch.cuda.synchronize()
+    assert torch.equal(a, b)

@@ -1,0 +1,152 @@
+"""GPU parity of the rasterizer forward through the drop-in Python API
+(diff_surfel_rasterization -> libnest_b200.so C-ABI) against the CPU oracle.
+
+Tolerance: max-abs 2e-3 per channel for features, depth,
+normal and alpha, plus PSNR >= 60 dB. The table is drawn U(-1, 1) (the
+parity-stress range) so hash-gather mistakes cannot hide under tiny values.
+"""
+import math
+
+import numpy as np
+import pytest
+import torch
+
+import diff_surfel_rasterization as dsr
+from helpers import api_inputs, oracle_render, psnr, small_scene
+from nest_b200 import synth
+
+pytestmark = pytest.mark.gpu
+TOL = 2e-3
+
+
+def run_api(scene, inputs, fp16=True, record=False, max_int=0, beta=0.0, contract=False, scale_mod=1.0,
+            homotrans=True):
+    cam = scene.camera
+    g = scene.grid
+    dev = "cuda"
+    rs = dsr.GaussianRasterizationSettings(
+        image_height=cam.height, image_width=cam.width, tanfovx=cam.tanfovx, tanfovy=cam.tanfovy,
+        bg=torch.zeros(3, device=dev), scale_modifier=scale_mod, viewmatrix=cam.world_view_transform.to(dev),
+        projmatrix=cam.full_proj_transform.to(dev), sh_degree=0, campos=cam.camera_center.to(dev),
+        prefiltered=False, debug=False, beta=beta, if_contract=contract, record_transmittance=record,
+        max_intersections=max_int)
+    hs = dsr.HashGridSettings(L=g.levels, S=g.S, H=g.base_resolution, align_corners=g.align_corners,
+                              interpolation=g.interpolation,
+                              shape_dims=torch.tensor([0, g.channels, g.channels], dtype=torch.int32, device=dev))
+    r = dsr.GaussianRasterizer(rs, hs)
+    P = inputs["means3D"].shape[0]
+    table = g.table.to(dev) if fp16 else g.table.float().to(dev)
+    with torch.no_grad():
+        color, radii, allmap, trans, cover = r(
+            means3D=inputs["means3D"].to(dev), means2D=torch.zeros(P, 3, device=dev),
+            shs=torch.zeros(P, 1, 3, device=dev), colors_precomp=None, opacities=inputs["opacities"].to(dev),
+            scales=inputs["scales"].to(dev), rotations=inputs["rotations"].to(dev),
+            homotrans=inputs["homotrans"].to(dev) if homotrans else None, ap_level=inputs["ap_level"].to(dev),
+            cov3D_precomp=None, features=table, offsets=g.offsets.to(dev), gridrange=g.gridrange.to(dev),
+            render_mode=0)
+    torch.cuda.synchronize()
+    return color.cpu().numpy(), radii.cpu().numpy(), allmap.cpu().numpy(), trans.cpu().numpy(), cover.cpu().numpy()
+
+
+def compare(out, got_color, got_allmap, tol=TOL):
+    ref_c, ref_o = out["out_color"], out["out_others"]
+    assert np.abs(got_color - ref_c).max() <= tol, np.abs(got_color - ref_c).max()
+    for ch in range(14):
+        err = np.abs(got_allmap[ch] - ref_o[ch]).max()
+        scale = max(1.0, np.abs(ref_o[ch]).max())
+        assert err <= tol * scale, (ch, err)
+    assert psnr(got_color, ref_c, peak=max(1.0, np.abs(ref_c).max())) >= 60
+
+
+@pytest.mark.parametrize("fp16", [True, False])
+def test_raster_small_scene_matches_oracle(fp16):
+    sc = small_scene()
+    inp = api_inputs(sc)
+    out, pre, n = oracle_render(sc, inp)
+    color, radii, allmap, _, _ = run_api(sc, inp, fp16=fp16)
+    assert (radii == pre["radii"]).mean() > 0.999 and np.abs(radii - pre["radii"]).max() <= 1
+    compare(out, color, allmap)
+    assert allmap[7].sum() > 1000  # the scene really blends samples
+
+
+def test_raster_partial_levels_and_transmittance():
+    sc = small_scene(n=1500, seed=12)
+    inp = api_inputs(sc)
+    ap = inp["ap_level"].clone()
+    ap[::3] = 5.7   # floor -> 5 levels
+    ap[1::7] = 1.0  # level-visualisation colour of the reference's unsigned wrap (ap < 2)
+    ap[2::11] = 0.0
+    inp["ap_level"] = ap
+    out, pre, n = oracle_render(sc, inp, record_transmittance=True)
+    color, radii, allmap, trans, cover = run_api(sc, inp, record=True)
+    compare(out, color, allmap)
+    assert np.abs(cover.reshape(-1) - out["cover_pixels"]).max() <= 1.0
+    assert np.abs(trans.reshape(-1) - out["trans_avg"]).max() <= 1e-2 * max(1.0, out["trans_avg"].max())
+
+
+@pytest.mark.parametrize("opt", [dict(max_int=3), dict(beta=0.5), dict(contract=True), dict(scale_mod=0.8)])
+def test_raster_settings_variants(opt):
+    sc = small_scene(n=1200, seed=13)
+    inp = api_inputs(sc)
+    kw = {}
+    if "max_int" in opt:
+        kw["max_intersections"] = opt["max_int"]
+    if "beta" in opt:
+        kw["beta"] = opt["beta"]
+    if "contract" in opt:
+        kw["contract"] = opt["contract"]
+    if "scale_mod" in opt:
+        kw["scale_modifier"] = opt["scale_mod"]
+    out, pre, n = oracle_render(sc, inp, **kw)
+    color, radii, allmap, _, _ = run_api(sc, inp, **opt)
+    compare(out, color, allmap)
+
+
+def test_raster_homotrans_computed_when_absent():
+    sc = small_scene(n=1000, seed=14)
+    inp = api_inputs(sc)
+    out, pre, n = oracle_render(sc, inp)
+    color, radii, allmap, _, _ = run_api(sc, inp, homotrans=False)
+    compare(out, color, allmap, tol=5e-3)
+
+
+def test_raster_empty_and_culled():
+    sc = small_scene(n=64, seed=15)
+    inp = api_inputs(sc)
+    inp_empty = {k: v[:0] for k, v in inp.items()}
+    color, radii, allmap, _, _ = run_api(sc, inp_empty)
+    assert color.shape[0] == sc.grid.channels and np.all(color == 0) and np.all(allmap == 0)
+    behind = dict(inp)
+    m = inp["means3D"].clone()
+    m[:, 1] = -10.0  # every surfel behind the camera at y = -4 -> culled
+    behind["means3D"] = m
+    color, radii, allmap, _, _ = run_api(sc, behind)
+    assert np.all(radii == 0) and np.all(color == 0) and np.all(allmap[1] == 0)
+
+
+def test_mark_visible():
+    sc = small_scene(n=500, seed=16)
+    cam = sc.camera
+    rs = dsr.GaussianRasterizationSettings(cam.height, cam.width, cam.tanfovx, cam.tanfovy, torch.zeros(3).cuda(), 1.0,
+                                           cam.world_view_transform.cuda(), cam.full_proj_transform.cuda(), 0,
+                                           cam.camera_center.cuda(), False, False, 0.0, False, False)
+    hs = dsr.HashGridSettings(16, 0.5, 16, False, 0, torch.tensor([0, 32, 32], dtype=torch.int32).cuda())
+    pts = sc.base[:, :3].clone()
+    pts[::2, 1] = -5.0
+    vis = dsr.GaussianRasterizer(rs, hs).markVisible(pts.cuda()).cpu().numpy()
+    vm = cam.world_view_transform.numpy()
+    z = pts.numpy() @ vm[:3, 2] + vm[3, 2]
+    assert np.array_equal(vis, z > 0.2)
+
+
+def test_config1_fullsize_parity():
+    """BASELINE config 1 at full size (200k surfels, 800x800) on the default table."""
+    sc = synth.config1()
+    inp = api_inputs(sc)
+    out, pre, n = oracle_render(sc, inp)
+    color, radii, allmap, _, _ = run_api(sc, inp)
+    assert np.abs(color - out["out_color"]).max() <= TOL
+    for ch in (0, 1, 2, 3, 4, 5):
+        err = np.abs(allmap[ch] - out["out_others"][ch])
+        assert np.quantile(err, 0.9999) <= TOL * max(1.0, np.abs(out["out_others"][ch]).max()), ch
+    assert psnr(allmap[1], out["out_others"][1]) >= 60
