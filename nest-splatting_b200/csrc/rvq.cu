@@ -84,6 +84,7 @@ rvq_decode_smem_kernel(const uint8_t* __restrict__ idx, const float* __restrict_
       float ax = 0.0f, ay = 0.0f;
       for (int k = 0; k < K; k++) {
         const int e = (int)((packed >> (8 * k)) & 0xff);
+        if (e >= E) continue;  // an index outside the codebook contributes nothing
         const float2 v = cb2[(k * E + e) * (kHalfCols / 2) + l16];
         ax += v.x;
         ay += v.y;
@@ -105,7 +106,10 @@ __global__ void rvq_decode_gather_kernel(const uint8_t* __restrict__ idx,
     int64_t s = i / D;
     int d = (int)(i - s * D);
     float acc = 0.0f;
-    for (int k = 0; k < K; k++) acc += __ldg(cb + ((size_t)k * E + idx[s * K + k]) * D + d);
+    for (int k = 0; k < K; k++) {
+      const int e = idx[s * K + k];
+      if (e < E) acc += __ldg(cb + ((size_t)k * E + e) * D + d);
+    }
     out[i] = acc;
   }
 }

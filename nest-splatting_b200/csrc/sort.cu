@@ -235,8 +235,12 @@ onesweep_pass_kernel(const uint64_t* __restrict__ keys_in, const uint32_t* __res
     const uint64_t k = S.keys[i];
     const uint32_t d = (uint32_t)(k >> shift) & (kRadix - 1);
     const uint32_t dst = S.global_base[d] + (uint32_t)i - S.digit_excl[d];
-    keys_out[dst] = k;
-    vals_out[dst] = S.vals[i];
+    // dst < n whenever the look-back completed; the guard keeps a timed-out
+    // look-back (error bit set) from writing out of bounds.
+    if ((int64_t)dst < n) {
+      keys_out[dst] = k;
+      vals_out[dst] = S.vals[i];
+    }
   }
 }
 
