@@ -48,13 +48,27 @@ def run_api(scene, inputs, fp16=True, record=False, max_int=0, beta=0.0, contrac
     return color.cpu().numpy(), radii.cpu().numpy(), allmap.cpu().numpy(), trans.cpu().numpy(), cover.cpu().numpy()
 
 
-def compare(out, got_color, got_allmap, tol=TOL):
+def compare(out, got_color, got_allmap, tol=TOL, max_flip_frac=2e-3):
+    """Per-channel max-abs <= tol and PSNR >= 60 dB, except at pixels where a
+    threshold decision flipped between the CPU and GPU float evaluation: a
+    sample whose alpha sits at 1/255 (or whose transmittance sits at 1e-4) can be
+    kept on one side and dropped on the other (FMA contraction and expf ulps
+    differ). Such pixels show a different blended-sample count (channel 7); they
+    must be rare, and each flip moves a feature channel by at most alpha*T*|f|
+    < |f|/255 (|f| <= 1 for the U(-1, 1) stress table)."""
     ref_c, ref_o = out["out_color"], out["out_others"]
-    assert np.abs(got_color - ref_c).max() <= tol, np.abs(got_color - ref_c).max()
+    flips = got_allmap[7] != ref_o[7]
+    assert flips.mean() <= max_flip_frac, flips.mean()
+    keep = ~flips
+    err_c = np.abs(got_color - ref_c).max(axis=0)
+    assert err_c[keep].max(initial=0.0) <= tol, err_c[keep].max()
+    assert err_c.max() <= 2.0 / 255.0, err_c.max()
     for ch in range(14):
-        err = np.abs(got_allmap[ch] - ref_o[ch]).max()
+        if ch == 7:
+            continue
+        err = np.abs(got_allmap[ch] - ref_o[ch])
         scale = max(1.0, np.abs(ref_o[ch]).max())
-        assert err <= tol * scale, (ch, err)
+        assert err[keep].max(initial=0.0) <= tol * scale, (ch, err[keep].max())
     assert psnr(got_color, ref_c, peak=max(1.0, np.abs(ref_c).max())) >= 60
 
 
