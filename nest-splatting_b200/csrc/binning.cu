@@ -5,6 +5,10 @@
 // already produced), duplicateWithKeys (:70-111) emitting
 // key = (tile << 32) | float bits of view depth, value = surfel index, and
 // identifyTileRanges (:173-195). Sorting is in sort.cu.
+//
+// The tile rectangle of a surfel is the one preprocess computed from its
+// alpha >= 1/255 footprint, a subset of the reference's 4-sigma rectangle that
+// holds every pixel the surfel can be blended into (see preprocess.cu).
 #include "common.cuh"
 
 namespace ns {
@@ -52,9 +56,8 @@ duplicate_keys_kernel(int P, int block_size, const BinInfo* __restrict__ bin,
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= P) return;
   const BinInfo b = bin[i];
-  if (b.radius <= 0) return;
-  int x0, y0, x1, y1;
-  tile_rect(b.x, b.y, b.radius, gx, gy, x0, y0, x1, y1);
+  const int x0 = b.x0, y0 = b.y0, x1 = b.x1, y1 = b.y1;
+  if (x1 <= x0 || y1 <= y0) return;
   int64_t off = (int64_t)block_prefix[i / block_size] + excl_local[i];
   const int64_t cnt = (int64_t)(x1 - x0) * (y1 - y0);
   if (off + cnt > capacity) {

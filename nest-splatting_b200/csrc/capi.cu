@@ -289,7 +289,8 @@ int ns_rasterize_forward(const ns_raster_settings* settings, const ns_surfels* s
   GeomState g = carve_geom(geom, P, nullptr);
   ImageState im = carve_image(image, settings->image_width, settings->image_height, nullptr);
   NS_CUDA_TRY(cudaMemsetAsync(g.err, 0, sizeof(uint32_t), stream));
-  rc = preprocess_api_launch(P, *surfels, settings->scale_modifier, settings->viewmatrix,
+  rc = preprocess_api_launch(P, *surfels, settings->scale_modifier, settings->beta,
+                             settings->viewmatrix,
                              settings->projmatrix, settings->image_width, settings->image_height,
                              g.records, g.bin, outputs->radii, g.tiles, g.excl_local, g.block_sums,
                              stream);
@@ -380,7 +381,8 @@ int ns_render_frame(const ns_raster_settings* settings, const ns_frame_inputs* i
   if (ev) NS_CUDA_TRY(cudaEventRecord((cudaEvent_t)ev[1], stream));
   if (ev) NS_CUDA_TRY(cudaEventRecord((cudaEvent_t)ev[2], stream));
   rc = preprocess_mix_launch(P, in->base, in->decoded, in->dims, in->mix, in->ap_level,
-                             settings->scale_modifier, settings->viewmatrix, settings->projmatrix,
+                             settings->scale_modifier, settings->beta, settings->viewmatrix,
+                             settings->projmatrix,
                              W, H, g.records, g.bin, out->radii, g.tiles, g.excl_local,
                              g.block_sums, stream);
   if (rc) return rc;

@@ -31,20 +31,22 @@ constexpr uint32_t kSpinLimit = 1u << 22;
 
 // Per-surfel render record: 8 float4 = 128 bytes, one L2 line, written by the
 // preprocess kernel and gathered by the blend kernel.
-//   q0 = (Tu.x, Tu.y, Tu.z, Tv.x)      q1 = (Tv.y, Tv.z, Tw.x, Tw.y)
-//   q2 = (Tw.z, xy.x, xy.y, opacity)    q3 = (n.x, n.y, n.z, ap_level bits)
-//   q4 = (SuTu.x, SuTu.y, SuTu.z, SvTv.x)  q5 = (SvTv.y, SvTv.z, pk.x, pk.y)
-//   q6 = (pk.z, 0, 0, 0)                 q7 = unused
+//   q0 = (x0, x1, y0, y1): pixel box outside which the surfel's alpha < 1/255
+//   q1 = (Tu.x, Tu.y, Tu.z, Tv.x)      q2 = (Tv.y, Tv.z, Tw.x, Tw.y)
+//   q3 = (Tw.z, xy.x, xy.y, opacity)    q4 = (n.x, n.y, n.z, ap_level bits)
+//   q5 = (SuTu.x, SuTu.y, SuTu.z, SvTv.x)  q6 = (SvTv.y, SvTv.z, pk.x, pk.y)
+//   q7 = (pk.z, 0, 0, 0)
 struct alignas(16) SurfelRecord {
   float4 q[8];
 };
-constexpr int kRecordFloat4 = 7;  // float4 words the blend kernel reads
+constexpr int kRecordFloat4 = 8;  // float4 words the blend kernel reads
 
-// Binning info per surfel: (x, y, radius, depth) as float4, radius as int bits.
+// Binning info per surfel: the tile rectangle [x0, x1) x [y0, y1) that receives
+// instances (empty for culled surfels) and the view depth of the sort key.
 struct alignas(16) BinInfo {
-  float x, y;
-  int radius;
+  int16_t x0, y0, x1, y1;
   float depth;
+  uint32_t pad;
 };
 
 __host__ __device__ inline int div_up(int a, int b) { return (a + b - 1) / b; }

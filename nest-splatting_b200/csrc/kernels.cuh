@@ -33,15 +33,15 @@ struct RenderParams {
 int rvq_decode_launch(const uint8_t*, const float*, float*, int64_t, int, int, int, cudaStream_t);
 int preprocess_blocks(int P);
 int preprocess_block_size();
-int preprocess_api_launch(int P, const ns_surfels& s, float mod, const float* vm, const float* pm,
-                          int W, int H, SurfelRecord* records, BinInfo* bin, int32_t* radii,
-                          uint32_t* tiles, uint32_t* excl_local, uint32_t* block_sums,
-                          cudaStream_t stream);
+int preprocess_api_launch(int P, const ns_surfels& s, float mod, float beta, const float* vm,
+                          const float* pm, int W, int H, SurfelRecord* records, BinInfo* bin,
+                          int32_t* radii, uint32_t* tiles, uint32_t* excl_local,
+                          uint32_t* block_sums, cudaStream_t stream);
 int preprocess_mix_launch(int P, const float* base, const float* decoded, int dims, float mix,
-                          const float* ap_level, float mod, const float* vm, const float* pm, int W,
-                          int H, SurfelRecord* records, BinInfo* bin, int32_t* radii,
-                          uint32_t* tiles, uint32_t* excl_local, uint32_t* block_sums,
-                          cudaStream_t stream);
+                          const float* ap_level, float mod, float beta, const float* vm,
+                          const float* pm, int W, int H, SurfelRecord* records, BinInfo* bin,
+                          int32_t* radii, uint32_t* tiles, uint32_t* excl_local,
+                          uint32_t* block_sums, cudaStream_t stream);
 int mark_visible_launch(int P, const float* means3D, const float* vm, uint8_t* present,
                         cudaStream_t stream);
 int scan_block_sums_launch(const uint32_t* sums, uint32_t* prefix, int nb, int64_t* total,

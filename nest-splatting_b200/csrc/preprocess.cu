@@ -107,10 +107,26 @@ struct PreOut {
   uint32_t* block_sums;  // per-CTA total
 };
 
-// Returns the tile count (0 when culled) and fills the record.
-__device__ __forceinline__ uint32_t preprocess_one(const SurfelIn& a, float mod, const float* vm,
-                                                   const float* pm, int W, int H, int gx, int gy,
-                                                   SurfelRecord& rec, BinInfo& bi) {
+// Squared radius rho (in the units of the blend kernel's rho = min(rho3d, rho2d))
+// beyond which alpha = min(0.99, o * G(rho)) < 1/255, G(rho) = exp(-rho/2) or, for
+// beta > 0, (1+beta) G / (1 + beta G). Returns false when no rho reaches 1/255.
+// A relative margin keeps the bound conservative under float rounding.
+__device__ __forceinline__ bool alpha_cutoff(float o, float beta, float& rho_cut) {
+  const double a = 1.0 / (255.0 * (double)o);  // G' needed
+  if (!(o > 0.0f) || a > 1.001) return false;
+  double g = a;
+  if (beta > 0.0f) g = a / (1.0 + beta - beta * a);  // invert G' = (1+b) G / (1 + b G)
+  const double rc = g >= 1.0 ? 0.0 : -2.0 * log(g);
+  rho_cut = (float)(rc * 1.002 + 1e-3);
+  return true;
+}
+
+// Returns the number of tiles that receive instances (0 when culled) and fills
+// the record, the binning info and the reference's radius.
+__device__ __forceinline__ uint32_t preprocess_one(const SurfelIn& a, float mod, float beta,
+                                                   const float* vm, const float* pm, int W, int H,
+                                                   int gx, int gy, SurfelRecord& rec, BinInfo& bi,
+                                                   int& radius_out) {
   // in_frustum: view-space depth must exceed 0.2 (auxiliary.h:190-215).
   const float3 pv = f3(vm[0] * a.p.x + vm[4] * a.p.y + vm[8] * a.p.z + vm[12],
                        vm[1] * a.p.x + vm[5] * a.p.y + vm[9] * a.p.z + vm[13],
@@ -171,28 +187,81 @@ __device__ __forceinline__ uint32_t preprocess_one(const SurfelIn& a, float mod,
   const float radius = ceilf(fmaxf(fmaxf(ex, ey), cutoff * kFilterSize));
   int x0, y0, x1, y1;
   tile_rect(ppx, ppy, (int)radius, gx, gy, x0, y0, x1, y1);
-  const uint32_t tiles = (uint32_t)((x1 - x0) * (y1 - y0));
-  if (tiles == 0) return 0;
+  if ((x1 - x0) * (y1 - y0) == 0) return 0;
+  radius_out = (int)radius;
+
+  // Tight footprint: a pixel can only blend this surfel where
+  // min(rho3d, rho2d) <= rho_cut, i.e. inside the ellipse rho3d <= rho_cut (its
+  // screen box is compute_aabb's formula at cutoff sqrt(rho_cut)) or inside the
+  // disc rho2d = 2 |xy - pixel|^2 <= rho_cut. Tiles outside that box would only
+  // ever see alpha < 1/255 and are not emitted; the pixel box is also kept in
+  // the record so the blend kernel skips pixels outside it.
+  float rho_cut = 0.f;
+  float bx0 = 1.f, bx1 = 0.f, by0 = 1.f, by1 = 0.f;  // empty
+  uint32_t tiles = 0;
+  int tx0 = x0, tx1 = x0, ty0 = y0, ty1 = y0;
+  if (alpha_cutoff(a.opacity, beta, rho_cut)) {
+    const float dc = rho_cut * (Tw.x * Tw.x) + rho_cut * (Tw.y * Tw.y) - (Tw.z * Tw.z);
+    float ex0, ex1, ey0, ey1;
+    bool ok = dc > 0.0f;
+    if (ok) {
+      const float idc = 1.0f / dc;
+      const float3 fc = f3(idc * rho_cut, idc * rho_cut, -idc);
+      const float cx = fc.x * (Tu.x * Tw.x) + fc.y * (Tu.y * Tw.y) + fc.z * (Tu.z * Tw.z);
+      const float cy = fc.x * (Tv.x * Tw.x) + fc.y * (Tv.y * Tw.y) + fc.z * (Tv.z * Tw.z);
+      const float hx2 = cx * cx - (fc.x * (Tu.x * Tu.x) + fc.y * (Tu.y * Tu.y) + fc.z * (Tu.z * Tu.z));
+      const float hy2 = cy * cy - (fc.x * (Tv.x * Tv.x) + fc.y * (Tv.y * Tv.y) + fc.z * (Tv.z * Tv.z));
+      ok = hx2 >= 0.0f && hy2 >= 0.0f && isfinite(cx) && isfinite(cy);
+      if (ok) {
+        const float hx = sqrtf(hx2) * 1.01f + 1.0f, hy = sqrtf(hy2) * 1.01f + 1.0f;
+        ex0 = cx - hx;
+        ex1 = cx + hx;
+        ey0 = cy - hy;
+        ey1 = cy + hy;
+      }
+    }
+    if (!ok) {  // not an ellipse at this cutoff: keep the reference rectangle
+      ex0 = (float)(x0 * kTile);
+      ex1 = (float)(x1 * kTile - 1);
+      ey0 = (float)(y0 * kTile);
+      ey1 = (float)(y1 * kTile - 1);
+    }
+    const float r2 = sqrtf(0.5f * rho_cut) * 1.01f + 1.0f;
+    bx0 = fmaxf(fminf(ex0, ppx - r2), -1.0f);
+    bx1 = fminf(fmaxf(ex1, ppx + r2), (float)W);
+    by0 = fmaxf(fminf(ey0, ppy - r2), -1.0f);
+    by1 = fminf(fmaxf(ey1, ppy + r2), (float)H);
+    if (bx0 <= bx1 && by0 <= by1) {
+      tx0 = max(x0, (int)floorf(fmaxf(bx0, 0.f) / kTile));
+      tx1 = min(x1, (int)floorf(bx1 / kTile) + 1);
+      ty0 = max(y0, (int)floorf(fmaxf(by0, 0.f) / kTile));
+      ty1 = min(y1, (int)floorf(by1 / kTile) + 1);
+      if (tx1 > tx0 && ty1 > ty0) tiles = (uint32_t)((tx1 - tx0) * (ty1 - ty0));
+    }
+  }
+  if (tiles == 0) tx1 = tx0, ty1 = ty0;
 
   const uint32_t ap_bits = (uint32_t)floorf(fminf(a.ap, 4.0e9f));
-  rec.q[0] = make_float4(Tu.x, Tu.y, Tu.z, Tv.x);
-  rec.q[1] = make_float4(Tv.y, Tv.z, Tw.x, Tw.y);
-  rec.q[2] = make_float4(Tw.z, ppx, ppy, a.opacity);
-  rec.q[3] = make_float4(n.x, n.y, n.z, __uint_as_float(ap_bits));
-  rec.q[4] = make_float4(a.su.x, a.su.y, a.su.z, a.sv.x);
-  rec.q[5] = make_float4(a.sv.y, a.sv.z, a.pk.x, a.pk.y);
-  rec.q[6] = make_float4(a.pk.z, 0.f, 0.f, 0.f);
-  rec.q[7] = make_float4(0.f, 0.f, 0.f, 0.f);
-  bi.x = ppx;
-  bi.y = ppy;
-  bi.radius = (int)radius;
+  rec.q[0] = make_float4(bx0, bx1, by0, by1);
+  rec.q[1] = make_float4(Tu.x, Tu.y, Tu.z, Tv.x);
+  rec.q[2] = make_float4(Tv.y, Tv.z, Tw.x, Tw.y);
+  rec.q[3] = make_float4(Tw.z, ppx, ppy, a.opacity);
+  rec.q[4] = make_float4(n.x, n.y, n.z, __uint_as_float(ap_bits));
+  rec.q[5] = make_float4(a.su.x, a.su.y, a.su.z, a.sv.x);
+  rec.q[6] = make_float4(a.sv.y, a.sv.z, a.pk.x, a.pk.y);
+  rec.q[7] = make_float4(a.pk.z, 0.f, 0.f, 0.f);
+  bi.x0 = (int16_t)tx0;
+  bi.x1 = (int16_t)tx1;
+  bi.y0 = (int16_t)ty0;
+  bi.y1 = (int16_t)ty1;
   bi.depth = pv.z;
+  bi.pad = 0;
   return tiles;
 }
 
 template <class Attrs>
 __global__ void __launch_bounds__(kPreThreads)
-preprocess_kernel(int P, Attrs attrs, float mod, const float* __restrict__ viewmatrix,
+preprocess_kernel(int P, Attrs attrs, float mod, float beta, const float* __restrict__ viewmatrix,
                   const float* __restrict__ projmatrix, int W, int H, PreOut out) {
   __shared__ float vm[16], pm[16];
   __shared__ uint32_t warp_sums[kPreThreads / 32];
@@ -205,21 +274,19 @@ preprocess_kernel(int P, Attrs attrs, float mod, const float* __restrict__ viewm
   if (i < P) {
     SurfelRecord rec;
     BinInfo bi;
+    bi.x0 = bi.x1 = bi.y0 = bi.y1 = 0;
+    bi.depth = 0.f;
+    bi.pad = 0;
+    int radius = 0;
     const SurfelIn a = attrs.load(i);
-    tiles = preprocess_one(a, mod, vm, pm, W, H, gx, gy, rec, bi);
+    tiles = preprocess_one(a, mod, beta, vm, pm, W, H, gx, gy, rec, bi, radius);
     if (tiles) {
       float4* dst = reinterpret_cast<float4*>(out.records + i);
 #pragma unroll
       for (int k = 0; k < 8; k++) dst[k] = rec.q[k];
-      out.bin[i] = bi;
-      out.radii[i] = bi.radius;
-    } else {
-      BinInfo z;
-      z.x = z.y = z.depth = 0.f;
-      z.radius = 0;
-      out.bin[i] = z;
-      out.radii[i] = 0;
     }
+    out.bin[i] = bi;
+    out.radii[i] = radius;
     out.tiles[i] = tiles;
   }
   // CTA-local exclusive scan of the tile counts.
@@ -252,27 +319,27 @@ __global__ void mark_visible_kernel(int P, const float* __restrict__ means3D,
 int preprocess_blocks(int P) { return div_up(max(P, 1), kPreThreads); }
 int preprocess_block_size() { return kPreThreads; }
 
-int preprocess_api_launch(int P, const ns_surfels& s, float mod, const float* vm, const float* pm,
-                          int W, int H, SurfelRecord* records, BinInfo* bin, int32_t* radii,
-                          uint32_t* tiles, uint32_t* excl_local, uint32_t* block_sums,
-                          cudaStream_t stream) {
+int preprocess_api_launch(int P, const ns_surfels& s, float mod, float beta, const float* vm,
+                          const float* pm, int W, int H, SurfelRecord* records, BinInfo* bin,
+                          int32_t* radii, uint32_t* tiles, uint32_t* excl_local,
+                          uint32_t* block_sums, cudaStream_t stream) {
   ApiAttrs a{s.means3D, s.scales, s.rotations, s.opacities, s.homotrans, s.ap_level};
   PreOut o{records, bin, radii, tiles, excl_local, block_sums};
-  preprocess_kernel<ApiAttrs><<<preprocess_blocks(P), kPreThreads, 0, stream>>>(P, a, mod, vm, pm,
-                                                                                W, H, o);
+  preprocess_kernel<ApiAttrs><<<preprocess_blocks(P), kPreThreads, 0, stream>>>(P, a, mod, beta, vm,
+                                                                                pm, W, H, o);
   NS_LAUNCH_CHECK();
   return NS_OK;
 }
 
 int preprocess_mix_launch(int P, const float* base, const float* decoded, int dims, float mix,
-                          const float* ap_level, float mod, const float* vm, const float* pm, int W,
-                          int H, SurfelRecord* records, BinInfo* bin, int32_t* radii,
-                          uint32_t* tiles, uint32_t* excl_local, uint32_t* block_sums,
-                          cudaStream_t stream) {
+                          const float* ap_level, float mod, float beta, const float* vm,
+                          const float* pm, int W, int H, SurfelRecord* records, BinInfo* bin,
+                          int32_t* radii, uint32_t* tiles, uint32_t* excl_local,
+                          uint32_t* block_sums, cudaStream_t stream) {
   MixAttrs a{base, decoded, dims, mix, ap_level};
   PreOut o{records, bin, radii, tiles, excl_local, block_sums};
-  preprocess_kernel<MixAttrs><<<preprocess_blocks(P), kPreThreads, 0, stream>>>(P, a, mod, vm, pm,
-                                                                                W, H, o);
+  preprocess_kernel<MixAttrs><<<preprocess_blocks(P), kPreThreads, 0, stream>>>(P, a, mod, beta, vm,
+                                                                                pm, W, H, o);
   NS_LAUNCH_CHECK();
   return NS_OK;
 }

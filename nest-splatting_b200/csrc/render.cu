@@ -212,7 +212,11 @@ __global__ void __launch_bounds__(kThreads, 2) blend_kernel(const RenderParams p
       while (!done && j < todo && cnt < kQueue) {
         const int jj = j++;
         contributor++;
-        const float4 q0 = S.rec[jj][0], q1 = S.rec[jj][1], q2 = S.rec[jj][2];
+        // Outside the surfel's alpha >= 1/255 box the reference would reach
+        // `alpha < 1/255 -> continue` (or an earlier continue): skip the math.
+        const float4 box = S.rec[jj][0];
+        if (pxf < box.x || pxf > box.y || pyf < box.z || pyf > box.w) continue;
+        const float4 q0 = S.rec[jj][1], q1 = S.rec[jj][2], q2 = S.rec[jj][3];
         const float3 Tu = f3(q0.x, q0.y, q0.z), Tv = f3(q0.w, q1.x, q1.y), Tw = f3(q1.z, q1.w, q2.x);
         const float3 kk = pxf * Tw - Tu;
         const float3 ll = pyf * Tw - Tv;
@@ -251,12 +255,12 @@ __global__ void __launch_bounds__(kThreads, 2) blend_kernel(const RenderParams p
           median_depth = depth;
           median_contributor = (float)contributor;
         }
-        const float4 q3 = S.rec[jj][3];
+        const float4 q3 = S.rec[jj][4];
         N0 += q3.x * w;
         N1 += q3.y * w;
         N2 += q3.z * w;
 
-        const float4 q4 = S.rec[jj][4], q5 = S.rec[jj][5], q6 = S.rec[jj][6];
+        const float4 q4 = S.rec[jj][5], q5 = S.rec[jj][6], q6 = S.rec[jj][7];
         float3 xyz;
         if (on_plane) {
           xyz = f3(sx * q4.x + sy * q4.w + q5.z, sx * q4.y + sy * q5.x + q5.w,
