@@ -35,7 +35,7 @@ constexpr uint32_t kSpinLimit = 1u << 22;
 //   q1 = (Tu.x, Tu.y, Tu.z, Tv.x)      q2 = (Tv.y, Tv.z, Tw.x, Tw.y)
 //   q3 = (Tw.z, xy.x, xy.y, opacity)    q4 = (n.x, n.y, n.z, ap_level bits)
 //   q5 = (SuTu.x, SuTu.y, SuTu.z, SvTv.x)  q6 = (SvTv.y, SvTv.z, pk.x, pk.y)
-//   q7 = (pk.z, 0, 0, 0)
+//   q7 = (pk.z, rho_cut, 0, 0): rho_cut bounds min(rho3d, rho2d) where alpha >= 1/255
 struct alignas(16) SurfelRecord {
   float4 q[8];
 };

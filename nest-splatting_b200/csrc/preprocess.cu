@@ -249,7 +249,7 @@ __device__ __forceinline__ uint32_t preprocess_one(const SurfelIn& a, float mod,
   rec.q[4] = make_float4(n.x, n.y, n.z, __uint_as_float(ap_bits));
   rec.q[5] = make_float4(a.su.x, a.su.y, a.su.z, a.sv.x);
   rec.q[6] = make_float4(a.sv.y, a.sv.z, a.pk.x, a.pk.y);
-  rec.q[7] = make_float4(a.pk.z, 0.f, 0.f, 0.f);
+  rec.q[7] = make_float4(a.pk.z, rho_cut, 0.f, 0.f);
   bi.x0 = (int16_t)tx0;
   bi.x1 = (int16_t)tx1;
   bi.y0 = (int16_t)ty0;

@@ -208,24 +208,37 @@ __global__ void __launch_bounds__(kThreads, 2) blend_kernel(const RenderParams p
     int j = 0;
     while (true) {
       // ---------------- phase A: intersect, composite aux maps, queue samples
+      // The walk is warp-synchronous: all lanes of a warp share `j`, and a warp
+      // pauses for a drain as soon as one of its lanes has a full queue. Votes
+      // are taken at the loop head only, by all 32 lanes.
       int cnt = 0;
-      while (!done && j < todo && cnt < kQueue) {
+      while (j < todo) {
+        const bool active = !done;
+        if (!__any_sync(0xffffffffu, active)) break;
+        if (__any_sync(0xffffffffu, cnt == kQueue)) break;
         const int jj = j++;
-        contributor++;
+        if (active) contributor++;
         // Outside the surfel's alpha >= 1/255 box the reference would reach
-        // `alpha < 1/255 -> continue` (or an earlier continue): skip the math.
+        // `alpha < 1/255 -> continue` (or an earlier continue): skip the math,
+        // for the whole warp when no lane is inside.
         const float4 box = S.rec[jj][0];
-        if (pxf < box.x || pxf > box.y || pyf < box.z || pyf > box.w) continue;
+        const bool cand = active && !(pxf < box.x || pxf > box.y || pyf < box.z || pyf > box.w);
+        if (!__any_sync(0xffffffffu, cand)) continue;
+        if (!cand) continue;
         const float4 q0 = S.rec[jj][1], q1 = S.rec[jj][2], q2 = S.rec[jj][3];
         const float3 Tu = f3(q0.x, q0.y, q0.z), Tv = f3(q0.w, q1.x, q1.y), Tw = f3(q1.z, q1.w, q2.x);
         const float3 kk = pxf * Tw - Tu;
         const float3 ll = pyf * Tw - Tv;
         const float3 pp = cross3(kk, ll);
+        const float dx = q2.y - pxf, dy = q2.z - pyf;
+        const float rho2d = kFilterInvSquare * (dx * dx + dy * dy);
+        // Division-free pre-test: rho3d = |p.xy|^2 / p.z^2 and rho2d both above the
+        // surfel's (margined) alpha cutoff means alpha < 1/255 on the reference path.
+        const float rho_cut = S.rec[jj][7].y;
+        if (pp.x * pp.x + pp.y * pp.y > rho_cut * (pp.z * pp.z) && rho2d > rho_cut) continue;
         if (pp.z == 0.0f) continue;
         const float sx = pp.x / pp.z, sy = pp.y / pp.z;
         const float rho3d = sx * sx + sy * sy;
-        const float dx = q2.y - pxf, dy = q2.z - pyf;
-        const float rho2d = kFilterInvSquare * (dx * dx + dy * dy);
         const float rho = fminf(rho3d, rho2d);
         const bool on_plane = rho3d <= rho2d;
         const float depth = on_plane ? (sx * Tw.x + sy * Tw.y) + Tw.z : Tw.z;
