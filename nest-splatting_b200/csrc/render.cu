@@ -46,26 +46,11 @@ struct BlendSmem {
   float acc[kThreads * kAccStride];     // feature accumulators [pixel][channel]
 };
 
-template <typename TableT>
-struct TableLoad;
-template <>
-struct TableLoad<__half> {
-  __device__ static float2 get(const void* t, uint32_t row) {
-    return __half22float2(__ldg(reinterpret_cast<const __half2*>(t) + row));
-  }
-};
-template <>
-struct TableLoad<float> {
-  __device__ static float2 get(const void* t, uint32_t row) {
-    return __ldg(reinterpret_cast<const float2*>(t) + row);
-  }
-};
-
 // Constants of one hash level (hashgrid.h:128-131 and the dense/hash choice of
 // get_grid_index, :22-40), computed with the device's exp2f as the reference does.
 struct Level {
   float scale;
-  uint32_t row0;   // first table row of the level
+  const void* base;  // the level's first table row
   uint32_t hsize;  // rows in the level
   uint32_t mask;   // hsize-1 for a power-of-two level size, ~0 otherwise
   uint32_t s1, s2; // dense strides of y and z
@@ -73,8 +58,11 @@ struct Level {
   bool modulo;     // level size is not a power of two: use %
 };
 
+template <typename TableT>
 __device__ Level make_level(const RenderParams& p, int l) {
   Level lv{};
+  lv.base = p.table;
+  lv.mask = 0;
   if (l >= (int)p.L) return lv;
   const uint32_t hsize = (uint32_t)(p.offsets[l + 1] - p.offsets[l]);
   const float scale = exp2f(l * p.S) * p.Hres - 1.0f;
@@ -89,7 +77,7 @@ __device__ Level make_level(const RenderParams& p, int l) {
     used++;
   }
   lv.scale = scale;
-  lv.row0 = (uint32_t)p.offsets[l];
+  lv.base = reinterpret_cast<const TableT*>(p.table) + 2 * (size_t)(uint32_t)p.offsets[l];
   lv.hsize = hsize;
   lv.dense = stride <= hsize && used == 3;
   lv.s1 = s1;
@@ -102,49 +90,113 @@ __device__ Level make_level(const RenderParams& p, int l) {
   return lv;
 }
 
-// Trilinear lookup of one level at a point of [0,1]^3 (hashgrid.h:140-193):
-// corner c has offsets (c&1, c>>1&1, c>>2&1) and weight ((wx * wy) * wz); the
-// corners are accumulated in order c = 0..7.
+// Trilinear lookup of one level at a point of [0,1]^3 (hashgrid.h:140-193),
+// split in two so that the loads of several lookups are in flight together:
+// lookup_issue() computes the cell, the 8 corner rows and issues their loads;
+// lookup_finish() weights corner c by ((wx * wy) * wz) and accumulates corners
+// in order c = 0..7, as the reference does.
 template <typename TableT>
-__device__ __forceinline__ float2 lookup(const Level& lv, float in0, float in1, float in2,
-                                         const void* __restrict__ table, float half_shift,
-                                         uint32_t interp) {
-  float f[3];
+struct Corner8;
+template <>
+struct Corner8<__half> {
+  __half2 v[8];
+  __device__ float2 get(int c) const { return __half22float2(v[c]); }
+  __device__ void load(const void* t, int c, uint32_t row) {
+    v[c] = __ldg(reinterpret_cast<const __half2*>(t) + row);
+  }
+};
+template <>
+struct Corner8<float> {
+  float2 v[8];
+  __device__ float2 get(int c) const { return v[c]; }
+  __device__ void load(const void* t, int c, uint32_t row) {
+    v[c] = __ldg(reinterpret_cast<const float2*>(t) + row);
+  }
+};
+
+template <typename TableT, bool kModulo>
+__device__ __forceinline__ void lookup_issue(const Level& lv, float4 in, float half_shift,
+                                             uint32_t interp, float (&f)[3],
+                                             Corner8<TableT>& cv) {
   uint32_t g[3];
-  const float in[3] = {in0, in1, in2};
+  const float pin[3] = {in.x, in.y, in.z};
 #pragma unroll
   for (int d = 0; d < 3; d++) {
-    const float pos = in[d] * lv.scale + half_shift;
+    const float pos = pin[d] * lv.scale + half_shift;
     g[d] = (uint32_t)floorf(pos);
     f[d] = pos - (float)g[d];
     if (interp == 1) f[d] = f[d] * f[d] * (3.0f - 2.0f * f[d]);
   }
-  // Hashed index terms for y, y+1, z, z+1 and the dense base.
+  // Hashed rows: (x ^ y*P1 ^ z*P2) with the four (y, z) terms formed once.
   const uint32_t hy0 = g[1] * 2654435761u, hy1 = (g[1] + 1) * 2654435761u;
   const uint32_t hz0 = g[2] * 805459861u, hz1 = (g[2] + 1) * 805459861u;
+  const uint32_t hyz[4] = {hy0 ^ hz0, hy1 ^ hz0, hy0 ^ hz1, hy1 ^ hz1};
   const uint32_t dbase = g[0] + g[1] * lv.s1 + g[2] * lv.s2;
-  uint32_t idx[8];
 #pragma unroll
   for (int c = 0; c < 8; c++) {
     const uint32_t bx = c & 1, by = (c >> 1) & 1, bz = (c >> 2) & 1;
-    const uint32_t hashed = (g[0] + bx) ^ (by ? hy1 : hy0) ^ (bz ? hz1 : hz0);
-    const uint32_t dense = dbase + bx + (by ? lv.s1 : 0u) + (bz ? lv.s2 : 0u);
-    uint32_t i = lv.dense ? dense : hashed;
-    i = lv.modulo ? (i % lv.hsize) : (i & lv.mask);
-    idx[c] = lv.row0 + i;
+    uint32_t i = lv.dense ? dbase + bx + (by ? lv.s1 : 0u) + (bz ? lv.s2 : 0u)
+                          : (g[0] + bx) ^ hyz[c >> 1];
+    i = kModulo ? (i % lv.hsize) : (i & lv.mask);
+    cv.load(lv.base, c, i);
   }
-  float2 v[8];
-#pragma unroll
-  for (int c = 0; c < 8; c++) v[c] = TableLoad<TableT>::get(table, idx[c]);
+}
+
+template <typename TableT>
+__device__ __forceinline__ float2 lookup_finish(const float (&f)[3], const Corner8<TableT>& cv) {
   float rx = 0.f, ry = 0.f;
 #pragma unroll
   for (int c = 0; c < 8; c++) {
     const float w = ((c & 1 ? f[0] : 1 - f[0]) * ((c >> 1) & 1 ? f[1] : 1 - f[1])) *
                     ((c >> 2) & 1 ? f[2] : 1 - f[2]);
-    rx += w * v[c].x;
-    ry += w * v[c].y;
+    const float2 v = cv.get(c);
+    rx += w * v.x;
+    ry += w * v.y;
   }
   return make_float2(rx, ry);
+}
+
+// Drains the queued samples of the 16 pixels of tile column `col` for hash
+// level `lv.level`: two samples' lookups are issued before either is used.
+template <typename TableT, bool kModulo>
+__device__ __forceinline__ void drain_column(BlendSmem& S, const Level& lv, int my_level, int col,
+                                             float half_shift, uint32_t interp) {
+  for (int i = 0; i < kTile; i++) {
+    const int pix = col + kTile * i;
+    const int n = S.cnt[pix];
+    if (n == 0) continue;
+    float2* a = reinterpret_cast<float2*>(&S.acc[pix * kAccStride + 2 * my_level]);
+    float2 c = *a;
+    int k = 0;
+    for (; k + 1 < n; k += 2) {
+      const float4 s0 = S.samp[k][pix], s1 = S.samp[k + 1][pix];
+      const bool u0 = my_level < (int)S.lvl[k][pix], u1 = my_level < (int)S.lvl[k + 1][pix];
+      float f0[3], f1[3];
+      Corner8<TableT> v0, v1;
+      if (u0) lookup_issue<TableT, kModulo>(lv, s0, half_shift, interp, f0, v0);
+      if (u1) lookup_issue<TableT, kModulo>(lv, s1, half_shift, interp, f1, v1);
+      if (u0) {
+        const float2 r = lookup_finish<TableT>(f0, v0);
+        c.x += r.x * s0.w;
+        c.y += r.y * s0.w;
+      }
+      if (u1) {
+        const float2 r = lookup_finish<TableT>(f1, v1);
+        c.x += r.x * s1.w;
+        c.y += r.y * s1.w;
+      }
+    }
+    if (k < n && my_level < (int)S.lvl[k][pix]) {
+      const float4 s0 = S.samp[k][pix];
+      float f0[3];
+      Corner8<TableT> v0;
+      lookup_issue<TableT, kModulo>(lv, s0, half_shift, interp, f0, v0);
+      const float2 r = lookup_finish<TableT>(f0, v0);
+      c.x += r.x * s0.w;
+      c.y += r.y * s0.w;
+    }
+    *a = c;
+  }
 }
 
 template <typename TableT>
@@ -167,7 +219,10 @@ __global__ void __launch_bounds__(kThreads, 2) blend_kernel(const RenderParams p
   // Phase B identity: one hash level of the 16 pixels of tile column `col`.
   const int my_level = t & (kLevelLanes - 1);
   const int col = t >> 4;
-  const Level lv = make_level(p, my_level);
+  const Level lv = make_level<TableT>(p, my_level);
+  // Level sizes are powers of two in the reference's table layout
+  // (gridencoder/grid.py:120-130); any other size takes the modulo variant.
+  const bool all_pow2 = __syncthreads_and(!lv.modulo) != 0;
   const float half_shift = p.align_corners ? 0.0f : 0.5f;
 
   for (int i = t; i < kThreads * kAccStride; i += kThreads) S.acc[i] = 0.f;
@@ -337,22 +392,8 @@ __global__ void __launch_bounds__(kThreads, 2) blend_kernel(const RenderParams p
       if (!any_pending && r + 1 < rounds) fetch(r + 1);
 
       // ---------------- phase B: hash lookups of the queued samples
-      for (int i = 0; i < kTile; i++) {
-        const int pix = col + kTile * i;
-        const int n = S.cnt[pix];
-        if (n == 0) continue;
-        float2* a = reinterpret_cast<float2*>(&S.acc[pix * kAccStride + 2 * my_level]);
-        float2 c = *a;
-        for (int k = 0; k < n; k++) {
-          if (my_level < (int)S.lvl[k][pix]) {
-            const float4 s = S.samp[k][pix];
-            const float2 f = lookup<TableT>(lv, s.x, s.y, s.z, p.table, half_shift, p.interp);
-            c.x += f.x * s.w;
-            c.y += f.y * s.w;
-          }
-        }
-        *a = c;
-      }
+      if (all_pow2) drain_column<TableT, false>(S, lv, my_level, col, half_shift, p.interp);
+      else drain_column<TableT, true>(S, lv, my_level, col, half_shift, p.interp);
       __syncthreads();
       if (!any_pending) break;
     }
