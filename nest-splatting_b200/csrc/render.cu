@@ -8,22 +8,27 @@
 //   hashgrid.h:53-212), feature compositing (:1914-1916), level colour
 //   (:1945-1957), transmittance record (:1961-1964), outputs (:2008-2048).
 //
-// Structure (one CTA of 256 threads per 16x16 tile), two alternating phases:
+// One CTA of 256 threads per 16x16 tile, one thread per pixel; warp w owns tile
+// rows 2w and 2w+1. Batches of up to 256 surfel records are gathered into shared
+// memory with cp.async. Each warp then alternates, on its own 32 pixels and
+// without CTA-wide barriers, between two phases:
 //
-//   Phase A, thread = pixel. Walks the current batch of (up to 256) surfel
-//   records, gathered into shared memory with cp.async, in the reference's
-//   front-to-back order and with its exact decision rules (alpha >= 1/255,
-//   T * (1 - alpha) >= 1e-4, depth >= near, max_intersections). It keeps the
-//   per-pixel auxiliary maps in registers and appends every blended sample
-//   (normalised hit point, weight, number of levels to query) to a short
-//   per-pixel queue in shared memory. A pixel pauses when its queue is full.
+//   Phase A (intersect). The warp walks the batch in the reference's
+//   front-to-back order, all lanes at the same position (a warp-uniform skip
+//   when no lane is inside the surfel's alpha >= 1/255 box; a division-free
+//   pre-test per lane before the reference arithmetic). It applies the
+//   reference's decision rules exactly (alpha >= 1/255, T * (1 - alpha) >=
+//   1e-4, depth >= near, max_intersections), keeps the auxiliary maps in
+//   registers and appends each blended sample (hit point mapped to [0,1]^3,
+//   weight, number of levels to query) to its pixel's queue in shared memory.
+//   The warp stops when one of its queues is full or the batch is done.
 //
-//   Phase B, thread = (hash level, tile column). Lane l of a half-warp owns
-//   level l of one pixel, so the 16 lanes of a half-warp query the 16 levels
-//   of the same sample together: no divergence on which pixels were hit, no
-//   unrolled level loop (the per-level trilinear lookup is the only code), and
-//   each level's constants live in registers. Each (pixel, level) accumulator
-//   adds its samples in queue order, i.e. the reference's per-pixel order.
+//   Phase B (hash lookups). Levels in a warp-uniform outer loop (so the
+//   dense/hashed choice is a uniform branch), the pixel's queued samples in the
+//   inner loop, two lookups in flight per lane. The 32 lanes are 32 neighbouring
+//   pixels whose k-th samples usually hit nearby points, so at the coarse
+//   levels their corner loads coalesce. Each (pixel, level) accumulator adds
+//   its samples in queue order, the reference's per-pixel order.
 //
 // The hash table is read as fp16 (or fp32) pairs through the read-only path;
 // at 16 levels x 2^19 x 2 fp16 it is 32 MB and stays resident in the 126 MB L2.
@@ -32,38 +37,34 @@
 namespace ns {
 namespace {
 
-constexpr int kThreads = kTilePixels;  // 256: one pixel per thread in phase A
-constexpr int kLevelLanes = 16;        // hash levels queried per pixel in phase B
+constexpr int kThreads = kTilePixels;  // 256: one pixel per thread
 constexpr int kQueue = 8;              // queued samples per pixel between drains
 constexpr int kAccStride = 34;         // floats per pixel row of the accumulators
 constexpr int kMaxChannels = 32;
+constexpr int kMaxLevels = 16;
+
+// Constants of one hash level (hashgrid.h:128-131 and the dense/hash choice of
+// get_grid_index, :22-40), computed with the device's exp2f as the reference does.
+struct LevelConst {
+  float scale;
+  uint32_t row0;    // first table row of the level
+  uint32_t mask;    // hsize-1 for a power-of-two size, ~0 otherwise
+  uint32_t hsize;   // rows in the level
+  uint32_t s1, s2;  // dense strides of y and z
+  uint32_t dense;   // 1: dense index, 0: hashed
+  uint32_t modulo;  // 1: size not a power of two, use %
+};
 
 struct BlendSmem {
   float4 rec[kThreads][kRecordFloat4];  // surfel records of the current batch
   float4 samp[kQueue][kThreads];        // (hit point in [0,1]^3, weight)
   uint8_t lvl[kQueue][kThreads];        // levels to query for the sample (0: none)
-  int cnt[kThreads];                    // queued samples per pixel
   float acc[kThreads * kAccStride];     // feature accumulators [pixel][channel]
+  LevelConst lv[kMaxLevels];
 };
 
-// Constants of one hash level (hashgrid.h:128-131 and the dense/hash choice of
-// get_grid_index, :22-40), computed with the device's exp2f as the reference does.
-struct Level {
-  float scale;
-  const void* base;  // the level's first table row
-  uint32_t hsize;  // rows in the level
-  uint32_t mask;   // hsize-1 for a power-of-two level size, ~0 otherwise
-  uint32_t s1, s2; // dense strides of y and z
-  bool dense;
-  bool modulo;     // level size is not a power of two: use %
-};
-
-template <typename TableT>
-__device__ Level make_level(const RenderParams& p, int l) {
-  Level lv{};
-  lv.base = p.table;
-  lv.mask = 0;
-  if (l >= (int)p.L) return lv;
+__device__ LevelConst make_level(const RenderParams& p, int l) {
+  LevelConst lc{};
   const uint32_t hsize = (uint32_t)(p.offsets[l + 1] - p.offsets[l]);
   const float scale = exp2f(l * p.S) * p.Hres - 1.0f;
   const uint32_t res = (uint32_t)ceilf(scale) + 1;
@@ -76,25 +77,20 @@ __device__ Level make_level(const RenderParams& p, int l) {
     stride *= R;
     used++;
   }
-  lv.scale = scale;
-  lv.base = reinterpret_cast<const TableT*>(p.table) + 2 * (size_t)(uint32_t)p.offsets[l];
-  lv.hsize = hsize;
-  lv.dense = stride <= hsize && used == 3;
-  lv.s1 = s1;
-  lv.s2 = s2;
+  lc.scale = scale;
+  lc.row0 = (uint32_t)p.offsets[l];
+  lc.hsize = hsize;
+  lc.dense = (stride <= hsize && used == 3) ? 1u : 0u;
+  lc.s1 = s1;
+  lc.s2 = s2;
   // index % hashmap_size applies to dense levels too (with align_corners the
   // top corner of a dense level can pass R^3 - 1).
-  const bool pow2 = (hsize & (hsize - 1)) == 0;
-  lv.mask = pow2 ? hsize - 1 : 0xffffffffu;
-  lv.modulo = !pow2;
-  return lv;
+  const bool pow2 = hsize != 0 && (hsize & (hsize - 1)) == 0;
+  lc.mask = pow2 ? hsize - 1 : 0xffffffffu;
+  lc.modulo = pow2 ? 0u : 1u;
+  return lc;
 }
 
-// Trilinear lookup of one level at a point of [0,1]^3 (hashgrid.h:140-193),
-// split in two so that the loads of several lookups are in flight together:
-// lookup_issue() computes the cell, the 8 corner rows and issues their loads;
-// lookup_finish() weights corner c by ((wx * wy) * wz) and accumulates corners
-// in order c = 0..7, as the reference does.
 template <typename TableT>
 struct Corner8;
 template <>
@@ -114,31 +110,43 @@ struct Corner8<float> {
   }
 };
 
-template <typename TableT, bool kModulo>
-__device__ __forceinline__ void lookup_issue(const Level& lv, float4 in, float half_shift,
-                                             uint32_t interp, float (&f)[3],
+// Trilinear lookup of one level at a point of [0,1]^3 (hashgrid.h:140-193),
+// split so that two lookups' loads are in flight together: lookup_issue()
+// finds the cell and issues the 8 corner loads; lookup_finish() weights corner
+// c by ((wx * wy) * wz) and accumulates corners in order c = 0..7.
+template <typename TableT>
+__device__ __forceinline__ void lookup_issue(const LevelConst& lc, const void* table, float4 in,
+                                             float half_shift, uint32_t interp, float (&f)[3],
                                              Corner8<TableT>& cv) {
   uint32_t g[3];
   const float pin[3] = {in.x, in.y, in.z};
 #pragma unroll
   for (int d = 0; d < 3; d++) {
-    const float pos = pin[d] * lv.scale + half_shift;
+    const float pos = pin[d] * lc.scale + half_shift;
     g[d] = (uint32_t)floorf(pos);
     f[d] = pos - (float)g[d];
     if (interp == 1) f[d] = f[d] * f[d] * (3.0f - 2.0f * f[d]);
   }
-  // Hashed rows: (x ^ y*P1 ^ z*P2) with the four (y, z) terms formed once.
-  const uint32_t hy0 = g[1] * 2654435761u, hy1 = (g[1] + 1) * 2654435761u;
-  const uint32_t hz0 = g[2] * 805459861u, hz1 = (g[2] + 1) * 805459861u;
-  const uint32_t hyz[4] = {hy0 ^ hz0, hy1 ^ hz0, hy0 ^ hz1, hy1 ^ hz1};
-  const uint32_t dbase = g[0] + g[1] * lv.s1 + g[2] * lv.s2;
+  uint32_t idx[8];
+  if (lc.dense) {
+    const uint32_t base = g[0] + g[1] * lc.s1 + g[2] * lc.s2;
 #pragma unroll
-  for (int c = 0; c < 8; c++) {
-    const uint32_t bx = c & 1, by = (c >> 1) & 1, bz = (c >> 2) & 1;
-    uint32_t i = lv.dense ? dbase + bx + (by ? lv.s1 : 0u) + (bz ? lv.s2 : 0u)
-                          : (g[0] + bx) ^ hyz[c >> 1];
-    i = kModulo ? (i % lv.hsize) : (i & lv.mask);
-    cv.load(lv.base, c, i);
+    for (int c = 0; c < 8; c++)
+      idx[c] = base + (c & 1) + ((c >> 1) & 1 ? lc.s1 : 0u) + ((c >> 2) & 1 ? lc.s2 : 0u);
+  } else {
+    // (x * 1) ^ (y * 2654435761) ^ (z * 805459861) with the (y, z) terms formed once.
+    const uint32_t hy0 = g[1] * 2654435761u, hy1 = (g[1] + 1) * 2654435761u;
+    const uint32_t hz0 = g[2] * 805459861u, hz1 = (g[2] + 1) * 805459861u;
+    const uint32_t hyz[4] = {hy0 ^ hz0, hy1 ^ hz0, hy0 ^ hz1, hy1 ^ hz1};
+#pragma unroll
+    for (int c = 0; c < 8; c++) idx[c] = (g[0] + (c & 1)) ^ hyz[c >> 1];
+  }
+  if (lc.modulo) {
+#pragma unroll
+    for (int c = 0; c < 8; c++) cv.load(table, c, lc.row0 + idx[c] % lc.hsize);
+  } else {
+#pragma unroll
+    for (int c = 0; c < 8; c++) cv.load(table, c, lc.row0 + (idx[c] & lc.mask));
   }
 }
 
@@ -156,49 +164,6 @@ __device__ __forceinline__ float2 lookup_finish(const float (&f)[3], const Corne
   return make_float2(rx, ry);
 }
 
-// Drains the queued samples of the 16 pixels of tile column `col` for hash
-// level `lv.level`: two samples' lookups are issued before either is used.
-template <typename TableT, bool kModulo>
-__device__ __forceinline__ void drain_column(BlendSmem& S, const Level& lv, int my_level, int col,
-                                             float half_shift, uint32_t interp) {
-  for (int i = 0; i < kTile; i++) {
-    const int pix = col + kTile * i;
-    const int n = S.cnt[pix];
-    if (n == 0) continue;
-    float2* a = reinterpret_cast<float2*>(&S.acc[pix * kAccStride + 2 * my_level]);
-    float2 c = *a;
-    int k = 0;
-    for (; k + 1 < n; k += 2) {
-      const float4 s0 = S.samp[k][pix], s1 = S.samp[k + 1][pix];
-      const bool u0 = my_level < (int)S.lvl[k][pix], u1 = my_level < (int)S.lvl[k + 1][pix];
-      float f0[3], f1[3];
-      Corner8<TableT> v0, v1;
-      if (u0) lookup_issue<TableT, kModulo>(lv, s0, half_shift, interp, f0, v0);
-      if (u1) lookup_issue<TableT, kModulo>(lv, s1, half_shift, interp, f1, v1);
-      if (u0) {
-        const float2 r = lookup_finish<TableT>(f0, v0);
-        c.x += r.x * s0.w;
-        c.y += r.y * s0.w;
-      }
-      if (u1) {
-        const float2 r = lookup_finish<TableT>(f1, v1);
-        c.x += r.x * s1.w;
-        c.y += r.y * s1.w;
-      }
-    }
-    if (k < n && my_level < (int)S.lvl[k][pix]) {
-      const float4 s0 = S.samp[k][pix];
-      float f0[3];
-      Corner8<TableT> v0;
-      lookup_issue<TableT, kModulo>(lv, s0, half_shift, interp, f0, v0);
-      const float2 r = lookup_finish<TableT>(f0, v0);
-      c.x += r.x * s0.w;
-      c.y += r.y * s0.w;
-    }
-    *a = c;
-  }
-}
-
 template <typename TableT>
 __global__ void __launch_bounds__(kThreads, 2) blend_kernel(const RenderParams p) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
@@ -208,24 +173,17 @@ __global__ void __launch_bounds__(kThreads, 2) blend_kernel(const RenderParams p
   const int gx = div_up(p.W, kTile);
   const int tile = blockIdx.x;
   const int tx = tile % gx, ty = tile / gx;
-
-  // Phase A identity: one pixel.
   const uint32_t px = tx * kTile + (t & (kTile - 1));
   const uint32_t py = ty * kTile + (t >> 4);
   const bool inside = px < (uint32_t)p.W && py < (uint32_t)p.H;
   const uint32_t pid = py * p.W + px;
   const float pxf = (float)px, pyf = (float)py;
-
-  // Phase B identity: one hash level of the 16 pixels of tile column `col`.
-  const int my_level = t & (kLevelLanes - 1);
-  const int col = t >> 4;
-  const Level lv = make_level<TableT>(p, my_level);
-  // Level sizes are powers of two in the reference's table layout
-  // (gridencoder/grid.py:120-130); any other size takes the modulo variant.
-  const bool all_pow2 = __syncthreads_and(!lv.modulo) != 0;
   const float half_shift = p.align_corners ? 0.0f : 0.5f;
+  const uint32_t L = p.L;
 
-  for (int i = t; i < kThreads * kAccStride; i += kThreads) S.acc[i] = 0.f;
+  if (t < (int)L) S.lv[t] = make_level(p, t);
+  float* my_acc = &S.acc[t * kAccStride];
+  for (int c = 0; c < kAccStride; c++) my_acc[c] = 0.f;  // only this thread touches its row
 
   const uint2 range = p.ranges[tile];
   const int total = (int)(range.y - range.x);
@@ -257,15 +215,13 @@ __global__ void __launch_bounds__(kThreads, 2) blend_kernel(const RenderParams p
   for (int r = 0; r < rounds; r++) {
     asm volatile("cp.async.wait_group 0;");
     // End when the whole tile is done (forward.cu:791-796); the barrier also
-    // publishes the batch copied into S.rec.
+    // publishes the batch copied into S.rec (and, first time, the level table).
     if (__syncthreads_count(done) == kThreads) break;
     const int todo = min(kThreads, total - r * kThreads);
     int j = 0;
     while (true) {
-      // ---------------- phase A: intersect, composite aux maps, queue samples
-      // The walk is warp-synchronous: all lanes of a warp share `j`, and a warp
-      // pauses for a drain as soon as one of its lanes has a full queue. Votes
-      // are taken at the loop head only, by all 32 lanes.
+      // ---------------- phase A: intersect, composite aux maps, queue samples.
+      // Warp-synchronous walk: all lanes share `j`; votes only at the loop head.
       int cnt = 0;
       while (j < todo) {
         const bool active = !done;
@@ -364,7 +320,7 @@ __global__ void __launch_bounds__(kThreads, 2) blend_kernel(const RenderParams p
           in2 = (st * in2 + 2.0f) * 0.25f;
         }
         S.samp[cnt][t] = make_float4(in0, in1, in2, w);
-        S.lvl[cnt][t] = (uint8_t)(oob ? 0u : min(apl, p.L));
+        S.lvl[cnt][t] = (uint8_t)(oob ? 0u : min(apl, L));
         cnt++;
 
         float ac0, ac1;
@@ -385,21 +341,52 @@ __global__ void __launch_bounds__(kThreads, 2) blend_kernel(const RenderParams p
         T = test_T;
         last_contributor = contributor;
       }
-      S.cnt[t] = cnt;
-      const bool pending = !done && j < todo;
-      const int any_pending = __syncthreads_or(pending);
-      // The batch is finished by every pixel: stream the next one in under phase B.
-      if (!any_pending && r + 1 < rounds) fetch(r + 1);
 
-      // ---------------- phase B: hash lookups of the queued samples
-      if (all_pow2) drain_column<TableT, false>(S, lv, my_level, col, half_shift, p.interp);
-      else drain_column<TableT, true>(S, lv, my_level, col, half_shift, p.interp);
-      __syncthreads();
-      if (!any_pending) break;
+      // ---------------- phase B: this warp's hash lookups. Each lane reads
+      // only its own queue and accumulator row, so no synchronisation is needed.
+      const int kmax = __reduce_max_sync(0xffffffffu, cnt);
+      if (kmax > 0) {
+        for (uint32_t l = 0; l < L; l++) {
+          const LevelConst lc = S.lv[l];
+          float2* ap = reinterpret_cast<float2*>(my_acc + 2 * l);
+          float2 c = *ap;
+          for (int k = 0; k < kmax; k += 2) {
+            const bool u0 = k < cnt && l < (uint32_t)S.lvl[k][t];
+            const bool u1 = k + 1 < cnt && l < (uint32_t)S.lvl[k + 1][t];
+            float4 s0, s1;
+            float f0[3], f1[3];
+            Corner8<TableT> v0, v1;
+            if (u0) {
+              s0 = S.samp[k][t];
+              lookup_issue<TableT>(lc, p.table, s0, half_shift, p.interp, f0, v0);
+            }
+            if (u1) {
+              s1 = S.samp[k + 1][t];
+              lookup_issue<TableT>(lc, p.table, s1, half_shift, p.interp, f1, v1);
+            }
+            if (u0) {
+              const float2 rr = lookup_finish<TableT>(f0, v0);
+              c.x += rr.x * s0.w;
+              c.y += rr.y * s0.w;
+            }
+            if (u1) {
+              const float2 rr = lookup_finish<TableT>(f1, v1);
+              c.x += rr.x * s1.w;
+              c.y += rr.y * s1.w;
+            }
+          }
+          *ap = c;
+        }
+      }
+      // Warp-uniform: the batch is finished for this warp when the walk reached
+      // its end or every lane is done.
+      if (j >= todo || !__any_sync(0xffffffffu, !done)) break;
     }
+    // Every warp is past this batch before the next one overwrites S.rec.
+    __syncthreads();
+    if (r + 1 < rounds) fetch(r + 1);
   }
   asm volatile("cp.async.wait_group 0;");
-  __syncthreads();
 
   if (inside) {
     const size_t HW = (size_t)p.H * p.W;
@@ -408,8 +395,7 @@ __global__ void __launch_bounds__(kThreads, 2) blend_kernel(const RenderParams p
     p.final_T[pid + 2 * HW] = M2;
     p.n_contrib[pid] = last_contributor;
     p.n_contrib[pid + HW] = (uint32_t)median_contributor;  // -1 saturates to 0
-    const float* a = &S.acc[t * kAccStride];
-    for (int c = 0; c < p.C; c++) p.out_color[c * HW + pid] = a[c];
+    for (int c = 0; c < p.C; c++) p.out_color[c * HW + pid] = my_acc[c];
     float* o = p.out_others + pid;
     o[0 * HW] = D;
     o[1 * HW] = 1 - T;
@@ -445,7 +431,7 @@ int launch_blend(const RenderParams& p, int tiles, cudaStream_t stream) {
 // renders nothing for shapes it was not compiled for).
 int render_launch(const RenderParams& p, int fp16, cudaStream_t stream) {
   if (p.LD != 2 || p.C > kMaxChannels || p.C <= 0) return NS_ERR_UNSUPPORTED;
-  if (p.L > (uint32_t)(p.C / p.LD) || p.L > (uint32_t)kLevelLanes) return NS_ERR_UNSUPPORTED;
+  if (p.L > (uint32_t)(p.C / p.LD) || p.L > (uint32_t)kMaxLevels) return NS_ERR_UNSUPPORTED;
   const int tiles = div_up(p.W, kTile) * div_up(p.H, kTile);
   if (tiles == 0) return NS_OK;
   return fp16 ? launch_blend<__half>(p, tiles, stream) : launch_blend<float>(p, tiles, stream);
