@@ -21,8 +21,7 @@
 //   1e-4, depth >= near, max_intersections), keeps the auxiliary maps in
 //   registers and appends each blended sample (hit point mapped to [0,1]^3,
 //   weight, number of levels to query) to its pixel's queue in shared memory.
-//   A lane with a full queue stops taking surfels and resumes after the drain;
-//   the warp drains when no lane can take more or the batch is done.
+//   The warp stops when one of its queues is full or the batch is done.
 //
 //   Phase B (hash lookups). Levels in a warp-uniform outer loop (so the
 //   dense/hashed choice is a uniform branch), the pixel's queued samples in the
@@ -219,32 +218,22 @@ __global__ void __launch_bounds__(kThreads, 2) blend_kernel(const RenderParams p
     // publishes the batch copied into S.rec (and, first time, the level table).
     if (__syncthreads_count(done) == kThreads) break;
     const int todo = min(kThreads, total - r * kThreads);
-    int jn = 0;  // this lane's next unprocessed surfel of the batch
+    int j = 0;
     while (true) {
       // ---------------- phase A: intersect, composite aux maps, queue samples.
-      // The warp walks the batch from the smallest resume position of its
-      // lanes; a lane takes surfel j only if it has not processed it yet, is
-      // not done and has queue room, so every pixel still visits each list
-      // entry exactly once and in order. A lane whose queue is full just stops
-      // taking surfels; the warp walks on for the others and drains when no
-      // lane can take more (or at the end of the batch). Votes are taken by all
-      // 32 lanes at the loop head only.
+      // Warp-synchronous walk: all lanes share `j`; votes only at the loop head.
       int cnt = 0;
-      int j = __reduce_min_sync(0xffffffffu, done ? todo : jn);
       while (j < todo) {
-        const bool open = !done && cnt < kQueue;
-        if (!__any_sync(0xffffffffu, open)) break;
+        const bool active = !done;
+        if (!__any_sync(0xffffffffu, active)) break;
+        if (__any_sync(0xffffffffu, cnt == kQueue)) break;
         const int jj = j++;
-        const bool take = open && jj >= jn;
-        if (take) {
-          contributor++;
-          jn = jj + 1;
-        }
+        if (active) contributor++;
         // Outside the surfel's alpha >= 1/255 box the reference would reach
         // `alpha < 1/255 -> continue` (or an earlier continue): skip the math,
         // for the whole warp when no lane is inside.
         const float4 box = S.rec[jj][0];
-        const bool cand = take && !(pxf < box.x || pxf > box.y || pyf < box.z || pyf > box.w);
+        const bool cand = active && !(pxf < box.x || pxf > box.y || pyf < box.z || pyf > box.w);
         if (!__any_sync(0xffffffffu, cand)) continue;
         if (!cand) continue;
         const float4 q0 = S.rec[jj][1], q1 = S.rec[jj][2], q2 = S.rec[jj][3];
@@ -389,9 +378,9 @@ __global__ void __launch_bounds__(kThreads, 2) blend_kernel(const RenderParams p
           *ap = c;
         }
       }
-      // Warp-uniform: the batch is finished for this warp when every lane is
-      // done or has processed the whole batch.
-      if (!__any_sync(0xffffffffu, !done && jn < todo)) break;
+      // Warp-uniform: the batch is finished for this warp when the walk reached
+      // its end or every lane is done.
+      if (j >= todo || !__any_sync(0xffffffffu, !done)) break;
     }
     // Every warp is past this batch before the next one overwrites S.rec.
     __syncthreads();
