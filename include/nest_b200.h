@@ -167,6 +167,21 @@ int ns_radix_sort_pairs(const uint64_t* keys_in, const uint32_t* vals_in, uint64
                         uint32_t* vals_out, uint64_t* keys_alt, uint32_t* vals_alt, int64_t n,
                         int32_t end_bit, void* temp, size_t temp_bytes, void* stream);
 
+/* Allocation-free variant of ns_radix_sort_pairs, for callers that cannot
+ * allocate device memory (a plugin inside a host renderer with a fixed memory
+ * budget, a runtime that hands out slices of its own arena, a language binding
+ * without a CUDA allocator). It has no counterpart in the reference. The
+ * ping-pong buffers and look-back state live in a file-scope device array sized
+ * for at most 1,048,576 pairs (about 14 MB, held on every GPU that loads the
+ * library until process exit); larger n returns NS_ERR_CAPACITY. All calls share
+ * that array: calls whose kernels overlap on the GPU (other streams or host
+ * threads) race, so serialise them. The first call on a device looks up the
+ * array's address for that device (cudaGetSymbolAddress); make it before any
+ * stream capture. Same result as ns_radix_sort_pairs. */
+int ns_radix_sort_pairs_noalloc(const uint64_t* keys_in, const uint32_t* vals_in,
+                                uint64_t* keys_out, uint32_t* vals_out, int64_t n,
+                                int32_t end_bit, void* stream);
+
 /* ------------------------------------------------------------ fused frame */
 
 /* One frame of the RVQ-driven render: decode -> attribute mix + activation ->

@@ -23,6 +23,7 @@ EXPORTED = [
     "ns_geometry_scratch_bytes", "ns_image_scratch_bytes", "ns_binning_scratch_bytes",
     "ns_rasterize_forward", "ns_read_device_status", "ns_mark_visible", "ns_mlp_forward",
     "ns_rvq_decode", "ns_radix_sort_temp_bytes", "ns_radix_sort_pairs", "ns_render_frame",
+    "ns_radix_sort_pairs_noalloc",
 ]
 
 
@@ -123,6 +124,8 @@ def load() -> C.CDLL:
     lib.ns_radix_sort_temp_bytes.argtypes = [i64]
     lib.ns_radix_sort_pairs.restype = C.c_int
     lib.ns_radix_sort_pairs.argtypes = [vp, vp, vp, vp, vp, vp, i64, i32, vp, sz, vp]
+    lib.ns_radix_sort_pairs_noalloc.restype = C.c_int
+    lib.ns_radix_sort_pairs_noalloc.argtypes = [vp, vp, vp, vp, i64, i32, vp]
     lib.ns_render_frame.restype = C.c_int
     lib.ns_render_frame.argtypes = [C.POINTER(RasterSettings), C.POINTER(FrameInputs),
                                     C.POINTER(FrameOutputs), vp, sz, vp, sz, vp, sz,
