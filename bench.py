@@ -25,7 +25,6 @@ import os
 import statistics
 import subprocess
 import sys
-import threading
 import time
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
@@ -47,49 +46,49 @@ def peaks():
 
 
 class ClockSampler:
-    """Samples SM clocks and throttle reasons with nvidia-smi during the timed region."""
+    """Samples SM clocks and throttle reasons with `nvidia-smi -lms` during the timed region."""
 
     QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
-    def __init__(self, gpu_index: int):
+    def __init__(self, gpu_index: int, period_ms: int = 50):
         self.gpu = gpu_index
-        self.samples = []
-        self._stop = threading.Event()
-        self._t = None
-
-    def _run(self):
-        while not self._stop.is_set():
-            try:
-                out = subprocess.run(["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.QUERY}",
-                                      "--format=csv,noheader,nounits"], capture_output=True, text=True,
-                                     timeout=5).stdout.strip()
-                if out:
-                    self.samples.append([x.strip() for x in out.split(",")])
-            except Exception:
-                pass
-            self._stop.wait(0.2)
+        self.period = period_ms
+        self.proc = None
+        self.out = ""
 
     def __enter__(self):
-        self._t = threading.Thread(target=self._run, daemon=True)
-        self._t.start()
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.QUERY}",
+                                          "--format=csv,noheader,nounits", f"-lms={self.period}"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            time.sleep(0.3)  # first sample before the timed work starts
+        except Exception:
+            self.proc = None
         return self
 
     def __exit__(self, *a):
-        self._stop.set()
-        self._t.join(timeout=10)
+        if self.proc is not None:
+            time.sleep(0.1)
+            self.proc.terminate()
+            try:
+                self.out, _ = self.proc.communicate(timeout=10)
+            except Exception:
+                self.proc.kill()
+                self.out = ""
 
     def summary(self):
-        if not self.samples:
+        rows = [[x.strip() for x in l.split(",")] for l in self.out.splitlines() if l.count(",") >= 8]
+        if not rows:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
-        sm = [float(s[1]) for s in self.samples if s[1].replace(".", "").isdigit()]
-        mx = [float(s[2]) for s in self.samples if s[2].replace(".", "").isdigit()]
+        num = lambda v: float(v) if v.replace(".", "", 1).isdigit() else None  # noqa: E731
+        sm = [num(r[1]) for r in rows if num(r[1]) is not None]
+        mx = [num(r[2]) for r in rows if num(r[2]) is not None]
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({names[i] for s in self.samples for i in range(4) if len(s) > 5 + i and
-                          s[5 + i].lower() == "active"})
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower() == "active"})
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
-                "reasons": reasons, "samples": len(self.samples)}
+                "reasons": reasons, "samples": len(rows)}
 
 
 def dist_setup(n_gpus):
@@ -111,12 +110,26 @@ def flush_l2(buf):
     buf.add_(1)  # 256 MB read+write evicts the 126 MB L2
 
 
-def blend_algorithmic_bytes(num_rendered, width, height, channels, table_bytes):
-    """Per blend launch: gathered records (112 B) + point list (4 B) per instance, tile
-    ranges, the per-pixel outputs (C features + 14 aux + 3 final T + 2 counts, fp32)
-    and one pass over the hash table."""
+def blend_algorithmic_bytes(num_rendered, surfels, width, height, channels, table_bytes):
+    """Unique DRAM bytes one blend launch must move: every surfel record once
+    (128 B), the sorted point list (4 B per instance), the tile ranges, the
+    per-pixel outputs (C features + 14 aux + 3 final T + 2 counts, fp32) and one
+    pass over the hash table. Re-gathers of records and table rows are served
+    by L2 and are not counted."""
     tiles = ((width + 15) // 16) * ((height + 15) // 16)
-    return num_rendered * (112 + 4) + tiles * 8 + width * height * (channels + 14 + 5) * 4 + table_bytes
+    return surfels * 128 + num_rendered * 4 + tiles * 8 + width * height * (channels + 14 + 5) * 4 + table_bytes
+
+
+def profiled_traffic():
+    """dram read+write bytes per blend launch from the committed ncu summary."""
+    path = os.path.join(ROOT, "profiles", "blend_kernel_config2_ncu.md")
+    try:
+        for line in open(path):
+            if line.startswith("traffic_bytes_per_launch:"):
+                return int(line.split(":")[1])
+    except OSError:
+        pass
+    return None
 
 
 def run_ours(args):
@@ -137,22 +150,16 @@ def run_ours(args):
     view = cam.world_view_transform.to(dev).contiguous()
     proj = cam.full_proj_transform.to(dev).contiguous()
     P = sc.P
-    shard = (P + world - 1) // world
-    lo, hi = rank * shard, min(P, (rank + 1) * shard)
-    dec_full = fr.decoded
-    if world > 1:
-        dec_full = torch.empty((shard * world, fr.dims), dtype=torch.float32, device=dev)
-        fr.decoded = dec_full[:P]
-        dec_shard = torch.empty((shard, fr.dims), dtype=torch.float32, device=dev)
-        idx_shard = torch.zeros((shard, fr.stages), dtype=torch.uint8, device=dev)
-        idx_shard[: hi - lo].copy_(fr.rvq_idx[lo:hi])
-
     from nest_b200 import raster
+    from nest_b200.views import DecodeShard, shard_range
+    lo, hi = shard_range(P, world, rank)
+    if world > 1:
+        shard = DecodeShard.create(fr.rvq_idx, fr.dims, world, rank)
+        fr.decoded = shard.decoded  # the frame reads the gathered rows
 
     def step(events=None):
         if world > 1:
-            raster.rvq_decode(idx_shard, fr.codebooks, out=dec_shard)
-            dist.all_gather_into_tensor(dec_full, dec_shard)
+            shard.decode_and_gather(fr.codebooks, raster.rvq_decode)
             return fr.render(cam, view, proj, events=events, skip_decode=True)
         return fr.render(cam, view, proj, events=events)
 
@@ -204,13 +211,12 @@ def run_ours(args):
 
     def e2e_step():
         if world > 1:
-            idx_shard[: hi - lo].copy_(host_idx[lo:hi], non_blocking=True)
+            shard.upload(host_idx)
         else:
             fr.upload_indices(host_idx)
         dev_cam.copy_(host_cam, non_blocking=True)
         if world > 1:
-            raster.rvq_decode(idx_shard, fr.codebooks, out=dec_shard)
-            dist.all_gather_into_tensor(dec_full, dec_shard)
+            shard.decode_and_gather(fr.codebooks, raster.rvq_decode)
             rgb = fr.render(cam, dev_cam[0], dev_cam[1], skip_decode=True)
         else:
             rgb = fr.render(cam, dev_cam[0], dev_cam[1])
@@ -241,17 +247,10 @@ def run_ours(args):
     num_rendered = fr.num_rendered
     hbm_peak, _, peak_kind = peaks()
     table_bytes = fr.table.numel() * fr.table.element_size()
-    blend_bytes = blend_algorithmic_bytes(num_rendered, W, H, fr.grid.channels, table_bytes)
+    blend_bytes = blend_algorithmic_bytes(num_rendered, P, W, H, fr.grid.channels, table_bytes)
     blend_ms = stage_ms["blend"]
     achieved = blend_bytes / (blend_ms * 1e-3) / 1e9
-    traffic = None
-    tfile = os.path.join(ROOT, "profiles", "blend_traffic.json")
-    if os.path.exists(tfile):
-        try:
-            with open(tfile) as f:
-                traffic = json.load(f).get("traffic_bytes_per_launch_config2")
-        except Exception:
-            traffic = None
+    traffic = profiled_traffic()
     rvq_bytes = (hi - lo) * (fr.stages + 4 * fr.dims) if world > 1 else P * (fr.stages + 4 * fr.dims)
     rvq_gbs = rvq_bytes / (stage_ms["decode"] * 1e-3) / 1e9 if world == 1 else None
     gather_tbs = samples * 16 * 8 * 4 / (blend_ms * 1e-3) / 1e12
@@ -271,7 +270,7 @@ def run_ours(args):
         "rvq_decode": {"gbs": round(rvq_gbs, 1) if rvq_gbs else None,
                        "frac_of_hbm": round(rvq_gbs / hbm_peak, 4) if rvq_gbs else None,
                        "bytes_per_surfel": fr.stages + 4 * fr.dims},
-        "roofline": {"kernel": "blend (render_kernel<__half,32>)", "bound": "hbm",
+        "roofline": {"kernel": "blend_kernel<__half>", "bound": "hbm",
                      "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s",
                      "frac": round(achieved / hbm_peak, 4), "traffic": traffic,
                      "peak_kind": peak_kind, "algorithmic_bytes": int(blend_bytes),
@@ -372,7 +371,7 @@ def run_reference(args):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")

@@ -1,0 +1,81 @@
+"""Multi-view batches sharded by camera over torch.distributed ranks.
+
+One process per GPU. Cameras are independent, so rank r renders its own share
+of a view batch; the RVQ attribute decode is sharded by surfel range and the
+decoded rows are exchanged with one all-gather (NCCL over NVLink on B200,
+gloo on CPU in the tests) -- the only collective of the path.
+
+Shard layout: the surfel axis is padded to world * ceil(P / world) rows so that
+every rank decodes the same number of rows; rank r owns rows
+[r * shard, (r + 1) * shard) and rows >= P are padding (never read).
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import torch
+import torch.distributed as dist
+
+
+def shard_size(P: int, world: int) -> int:
+    return (P + world - 1) // world
+
+
+def shard_range(P: int, world: int, rank: int) -> tuple[int, int]:
+    """[lo, hi) surfel rows decoded by `rank` (hi - lo may be < shard_size on the last ranks)."""
+    s = shard_size(P, world)
+    lo = min(P, rank * s)
+    return lo, min(P, lo + s)
+
+
+def camera_share(n_views: int, world: int, rank: int) -> list[int]:
+    """View indices rendered by `rank`: contiguous blocks, sizes differing by at most one."""
+    base, extra = divmod(n_views, world)
+    start = rank * base + min(rank, extra)
+    count = base + (1 if rank < extra else 0)
+    return list(range(start, start + count))
+
+
+@dataclass
+class DecodeShard:
+    """Device buffers of one rank's decode shard and of the gathered rows."""
+    P: int
+    world: int
+    rank: int
+    idx_shard: torch.Tensor   # [shard, K] uint8 (padding rows are zero)
+    dec_shard: torch.Tensor   # [shard, D] fp32
+    dec_full: torch.Tensor    # [world * shard, D] fp32; rows [:P] are the decoded attributes
+
+    @classmethod
+    def create(cls, rvq_idx: torch.Tensor, dims: int, world: int, rank: int) -> "DecodeShard":
+        P, K = rvq_idx.shape
+        s = shard_size(P, world)
+        lo, hi = shard_range(P, world, rank)
+        dev = rvq_idx.device
+        idx_shard = torch.zeros((s, K), dtype=torch.uint8, device=dev)
+        idx_shard[: hi - lo].copy_(rvq_idx[lo:hi])
+        dec_shard = torch.empty((s, dims), dtype=torch.float32, device=dev)
+        dec_full = torch.empty((s * world, dims), dtype=torch.float32, device=dev)
+        return cls(P, world, rank, idx_shard, dec_shard, dec_full)
+
+    @property
+    def decoded(self) -> torch.Tensor:
+        return self.dec_full[: self.P]
+
+    def upload(self, host_idx: torch.Tensor) -> None:
+        """Copies this rank's rows of a host index stream (non-blocking from pinned memory)."""
+        lo, hi = shard_range(self.P, self.world, self.rank)
+        self.idx_shard[: hi - lo].copy_(host_idx[lo:hi], non_blocking=True)
+
+    def gather(self, group=None) -> torch.Tensor:
+        """All-gather of the decoded shards into dec_full (every rank gets every row)."""
+        if self.world > 1:
+            dist.all_gather_into_tensor(self.dec_full, self.dec_shard, group=group)
+        else:
+            self.dec_full.copy_(self.dec_shard)
+        return self.decoded
+
+    def decode_and_gather(self, codebooks: torch.Tensor, decode_fn, group=None) -> torch.Tensor:
+        """decode_fn(idx, codebooks, out=...) on this rank's rows, then the all-gather."""
+        decode_fn(self.idx_shard, codebooks, out=self.dec_shard)
+        return self.gather(group)
