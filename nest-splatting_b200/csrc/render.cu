@@ -25,7 +25,7 @@
 //
 //   Phase B (hash lookups). Levels in a warp-uniform outer loop (so the
 //   dense/hashed choice is a uniform branch), the pixel's queued samples in the
-//   inner loop, two lookups in flight per lane. The 32 lanes are 32 neighbouring
+//   inner loop, two levels x two samples (four lookups) in flight per lane. The 32 lanes are 32 neighbouring
 //   pixels whose k-th samples usually hit nearby points, so at the coarse
 //   levels their corner loads coalesce. Each (pixel, level) accumulator adds
 //   its samples in queue order, the reference's per-pixel order.
@@ -46,6 +46,7 @@ constexpr int kMaxLevels = 16;
 // Constants of one hash level (hashgrid.h:128-131 and the dense/hash choice of
 // get_grid_index, :22-40), computed with the device's exp2f as the reference does.
 struct LevelConst {
+  const void* base; // the level's first table row
   float scale;
   uint32_t row0;    // first table row of the level
   uint32_t mask;    // hsize-1 for a power-of-two size, ~0 otherwise
@@ -63,6 +64,7 @@ struct BlendSmem {
   LevelConst lv[kMaxLevels];
 };
 
+template <typename TableT>
 __device__ LevelConst make_level(const RenderParams& p, int l) {
   LevelConst lc{};
   const uint32_t hsize = (uint32_t)(p.offsets[l + 1] - p.offsets[l]);
@@ -79,6 +81,7 @@ __device__ LevelConst make_level(const RenderParams& p, int l) {
   }
   lc.scale = scale;
   lc.row0 = (uint32_t)p.offsets[l];
+  lc.base = static_cast<const TableT*>(p.table) + 2 * (size_t)lc.row0;  // LD = 2 per row
   lc.hsize = hsize;
   lc.dense = (stride <= hsize && used == 3) ? 1u : 0u;
   lc.s1 = s1;
@@ -143,25 +146,28 @@ __device__ __forceinline__ void lookup_issue(const LevelConst& lc, const void* t
   }
   if (lc.modulo) {
 #pragma unroll
-    for (int c = 0; c < 8; c++) cv.load(table, c, lc.row0 + idx[c] % lc.hsize);
+    for (int c = 0; c < 8; c++) cv.load(lc.base, c, idx[c] % lc.hsize);
   } else {
 #pragma unroll
-    for (int c = 0; c < 8; c++) cv.load(table, c, lc.row0 + (idx[c] & lc.mask));
+    for (int c = 0; c < 8; c++) cv.load(lc.base, c, idx[c] & lc.mask);
   }
 }
 
+// Corner weights ((wx * wy) * wz) and the weighted sum in packed fp32
+// (__fmul2_rn / __ffma2_rn round each lane like the scalar operations).
 template <typename TableT>
 __device__ __forceinline__ float2 lookup_finish(const float (&f)[3], const Corner8<TableT>& cv) {
-  float rx = 0.f, ry = 0.f;
+  const float2 wx = make_float2(1 - f[0], f[0]);
+  const float2 wxy0 = __fmul2_rn(wx, make_float2(1 - f[1], 1 - f[1]));  // corners 0, 1
+  const float2 wxy1 = __fmul2_rn(wx, make_float2(f[1], f[1]));          // corners 2, 3
+  const float2 z0 = make_float2(1 - f[2], 1 - f[2]), z1 = make_float2(f[2], f[2]);
+  const float2 w01 = __fmul2_rn(wxy0, z0), w23 = __fmul2_rn(wxy1, z0);
+  const float2 w45 = __fmul2_rn(wxy0, z1), w67 = __fmul2_rn(wxy1, z1);
+  const float w[8] = {w01.x, w01.y, w23.x, w23.y, w45.x, w45.y, w67.x, w67.y};
+  float2 r = make_float2(0.f, 0.f);
 #pragma unroll
-  for (int c = 0; c < 8; c++) {
-    const float w = ((c & 1 ? f[0] : 1 - f[0]) * ((c >> 1) & 1 ? f[1] : 1 - f[1])) *
-                    ((c >> 2) & 1 ? f[2] : 1 - f[2]);
-    const float2 v = cv.get(c);
-    rx += w * v.x;
-    ry += w * v.y;
-  }
-  return make_float2(rx, ry);
+  for (int c = 0; c < 8; c++) r = __ffma2_rn(make_float2(w[c], w[c]), cv.get(c), r);
+  return r;
 }
 
 template <typename TableT>
@@ -181,7 +187,7 @@ __global__ void __launch_bounds__(kThreads, 2) blend_kernel(const RenderParams p
   const float half_shift = p.align_corners ? 0.0f : 0.5f;
   const uint32_t L = p.L;
 
-  if (t < (int)L) S.lv[t] = make_level(p, t);
+  if (t < (int)L) S.lv[t] = make_level<TableT>(p, t);
   float* my_acc = &S.acc[t * kAccStride];
   for (int c = 0; c < kAccStride; c++) my_acc[c] = 0.f;  // only this thread touches its row
 
@@ -346,36 +352,36 @@ __global__ void __launch_bounds__(kThreads, 2) blend_kernel(const RenderParams p
       // only its own queue and accumulator row, so no synchronisation is needed.
       const int kmax = __reduce_max_sync(0xffffffffu, cnt);
       if (kmax > 0) {
-        for (uint32_t l = 0; l < L; l++) {
-          const LevelConst lc = S.lv[l];
+        // Two levels x two samples per step: four independent lookups in
+        // flight per lane. Per (pixel, level) the samples still add in order.
+        for (uint32_t l = 0; l < L; l += 2) {
+          const bool has1 = l + 1 < L;
+          const LevelConst lc0 = S.lv[l];
+          const LevelConst lc1 = S.lv[has1 ? l + 1 : l];
           float2* ap = reinterpret_cast<float2*>(my_acc + 2 * l);
-          float2 c = *ap;
+          float2 c0 = ap[0];
+          float2 c1 = has1 ? ap[1] : make_float2(0.f, 0.f);
           for (int k = 0; k < kmax; k += 2) {
-            const bool u0 = k < cnt && l < (uint32_t)S.lvl[k][t];
-            const bool u1 = k + 1 < cnt && l < (uint32_t)S.lvl[k + 1][t];
-            float4 s0, s1;
-            float f0[3], f1[3];
-            Corner8<TableT> v0, v1;
-            if (u0) {
-              s0 = S.samp[k][t];
-              lookup_issue<TableT>(lc, p.table, s0, half_shift, p.interp, f0, v0);
-            }
-            if (u1) {
-              s1 = S.samp[k + 1][t];
-              lookup_issue<TableT>(lc, p.table, s1, half_shift, p.interp, f1, v1);
-            }
-            if (u0) {
-              const float2 rr = lookup_finish<TableT>(f0, v0);
-              c.x += rr.x * s0.w;
-              c.y += rr.y * s0.w;
-            }
-            if (u1) {
-              const float2 rr = lookup_finish<TableT>(f1, v1);
-              c.x += rr.x * s1.w;
-              c.y += rr.y * s1.w;
-            }
+            const uint32_t m0 = k < cnt ? (uint32_t)S.lvl[k][t] : 0u;
+            const uint32_t m1 = k + 1 < cnt ? (uint32_t)S.lvl[k + 1][t] : 0u;
+            const bool u00 = l < m0, u10 = l < m1;                       // level l
+            const bool u01 = has1 && l + 1 < m0, u11 = has1 && l + 1 < m1;  // level l+1
+            const float4 s0 = S.samp[k][t];
+            const float4 s1 = S.samp[k + 1 < kQueue ? k + 1 : k][t];
+            float f00[3], f10[3], f01[3], f11[3];
+            Corner8<TableT> v00, v10, v01, v11;
+            if (u00) lookup_issue<TableT>(lc0, p.table, s0, half_shift, p.interp, f00, v00);
+            if (u10) lookup_issue<TableT>(lc0, p.table, s1, half_shift, p.interp, f10, v10);
+            if (u01) lookup_issue<TableT>(lc1, p.table, s0, half_shift, p.interp, f01, v01);
+            if (u11) lookup_issue<TableT>(lc1, p.table, s1, half_shift, p.interp, f11, v11);
+            const float2 sw0 = make_float2(s0.w, s0.w), sw1 = make_float2(s1.w, s1.w);
+            if (u00) c0 = __ffma2_rn(lookup_finish<TableT>(f00, v00), sw0, c0);
+            if (u10) c0 = __ffma2_rn(lookup_finish<TableT>(f10, v10), sw1, c0);
+            if (u01) c1 = __ffma2_rn(lookup_finish<TableT>(f01, v01), sw0, c1);
+            if (u11) c1 = __ffma2_rn(lookup_finish<TableT>(f11, v11), sw1, c1);
           }
-          *ap = c;
+          ap[0] = c0;
+          if (has1) ap[1] = c1;
         }
       }
       // Warp-uniform: the batch is finished for this warp when the walk reached
