@@ -8,13 +8,14 @@
 // shape (6 x 256 x 59 fp32 = 354 KB) does not fit one SM's 227 KB of shared
 // memory, so the dimension axis is split in two halves of 32 columns and each
 // CTA holds all stages of one half (6 x 256 x 32 x 4 = 192 KB). CTAs are
-// persistent (one per SM) and walk 512-surfel chunks. Inside a chunk a
-// half-warp owns one surfel: lane j reads a float2 of columns (2j, 2j+1) of the
-// selected codeword of each stage (conflict-free: the half-warp reads one
-// contiguous 128-byte half row), so a warp decodes two surfels per step. Index
-// bytes are packed to one u64 per surfel in shared memory so the six stage
-// indices cost one broadcast read. The next chunk's indices are fetched into
-// registers while the current chunk is decoded.
+// persistent (one per SM) and walk 512-surfel chunks. The codebook half and
+// each chunk's index bytes arrive by cp.async (the next chunk's bytes stream in
+// while the current chunk is decoded). Inside a chunk a half-warp owns one
+// surfel: lane j reads a float2 of columns (2j, 2j+1) of the selected codeword
+// of each stage (conflict-free: the half-warp reads one contiguous 128-byte half
+// row), so a warp decodes two surfels per step, 16 independent steps per chunk.
+// Index bytes are packed to one u64 per surfel in shared memory so the stage
+// indices of a surfel cost one broadcast read.
 //
 // Bound: HBM (6 B of indices read + 4*dims B written per surfel); the shared
 // memory gather (6 x 128 B per surfel-half) runs at about the same time, so
@@ -25,75 +26,99 @@ namespace ns {
 namespace {
 
 constexpr int kRvqThreads = 512;
-constexpr int kRvqChunk = 512;   // surfels per chunk (one per thread for index loads)
+constexpr int kRvqChunk = 512;   // surfels per chunk (one per thread for index packing)
 constexpr int kHalfCols = 32;
+constexpr int kIdxWords = kRvqChunk * 8 / 4;  // raw index bytes of a chunk, as 4-byte words
+
+__device__ __forceinline__ void cp_async4(void* smem_dst, const void* gmem_src, int src_bytes) {
+  const unsigned dst = (unsigned)__cvta_generic_to_shared(smem_dst);
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(dst), "l"(gmem_src),
+               "r"(src_bytes));
+}
+
+// Streams the raw index bytes of chunk `ch` (cnt surfels x K bytes, contiguous
+// in global memory at a 4-byte aligned offset) into `raw` with 4-byte cp.async;
+// the tail word is zero-filled past the end of the array.
+__device__ __forceinline__ void fetch_indices(const uint8_t* __restrict__ idx, int64_t n, int K,
+                                              int64_t ch, int64_t nchunks, uint32_t* raw) {
+  if (ch < nchunks) {
+    const int64_t first = ch * kRvqChunk;
+    const int cnt = (int)min64(kRvqChunk, n - first);
+    const int bytes = cnt * K;
+    const uint8_t* src = idx + first * K;
+    for (int w = threadIdx.x; w * 4 < bytes; w += kRvqThreads)
+      cp_async4(raw + w, src + 4 * w, min(4, bytes - 4 * w));
+  }
+  asm volatile("cp.async.commit_group;");
+}
 
 __global__ void __launch_bounds__(kRvqThreads, 1)
 rvq_decode_smem_kernel(const uint8_t* __restrict__ idx, const float* __restrict__ cb,
                        float* __restrict__ out, int64_t n, int K, int E, int D) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
-  float* cb_s = reinterpret_cast<float*>(smem_raw);                    // [K*E][32]
-  uint64_t* idx_s = reinterpret_cast<uint64_t*>(cb_s + (size_t)K * E * kHalfCols);  // [chunk]
+  float* cb_s = reinterpret_cast<float*>(smem_raw);                                  // [K*E][32]
+  uint32_t* raw = reinterpret_cast<uint32_t*>(cb_s + (size_t)K * E * kHalfCols);     // [2][kIdxWords]
+  uint64_t* idx_s = reinterpret_cast<uint64_t*>(raw + 2 * kIdxWords);                // [chunk]
 
   const int half = blockIdx.y;
   const int col0 = half * kHalfCols;
   const int tid = threadIdx.x;
   const int lane = tid & 31, warp = tid >> 5;
 
-  // Stage this half of every codeword into shared memory (zero-padded columns).
+  // Stage this half of every codeword with 4-byte cp.async (columns past D zero-filled).
   const int rows = K * E;
   for (int i = tid; i < rows * kHalfCols; i += kRvqThreads) {
-    int r = i >> 5, j = i & 31;
-    int c = col0 + j;
-    cb_s[i] = (c < D) ? __ldg(cb + (size_t)r * D + c) : 0.0f;
+    const int r = i >> 5, c = col0 + (i & 31);
+    const float* src = cb + (size_t)r * D + (c < D ? c : 0);
+    cp_async4(cb_s + i, src, c < D ? 4 : 0);
   }
+  asm volatile("cp.async.commit_group;");
 
   const int64_t nchunks = div_up64(n, kRvqChunk);
   int64_t chunk = blockIdx.x;
-
-  // Prefetch the indices of the first chunk into registers.
-  auto load_idx = [&](int64_t ch) -> uint64_t {
-    int64_t s = ch * kRvqChunk + tid;
-    uint64_t v = 0;
-    if (ch < nchunks && s < n) {
-      const uint8_t* p = idx + s * K;
-      for (int k = 0; k < K; k++) v |= (uint64_t)__ldg(p + k) << (8 * k);
-    }
-    return v;
-  };
-  uint64_t next = load_idx(chunk);
+  int buf = 0;
+  fetch_indices(idx, n, K, chunk, nchunks, raw);
 
   const int sub = lane >> 4;        // which surfel of the pair
   const int l16 = lane & 15;        // float2 column within the half row
   const int c2 = col0 + 2 * l16;    // first output column of this lane
   const float2* cb2 = reinterpret_cast<const float2*>(cb_s);
 
-  for (; chunk < nchunks; chunk += gridDim.x) {
-    __syncthreads();  // previous chunk fully consumed (and the codebook staged)
-    idx_s[tid] = next;
-    __syncthreads();
-    next = load_idx(chunk + gridDim.x);
-
+  for (; chunk < nchunks; chunk += gridDim.x, buf ^= 1) {
+    asm volatile("cp.async.wait_group 0;");
+    __syncthreads();  // codebook and this chunk's index bytes are in; last chunk consumed
+    // Prefetch the next chunk's index bytes under this chunk's work.
+    fetch_indices(idx, n, K, chunk + gridDim.x, nchunks, raw + (buf ^ 1) * kIdxWords);
     const int64_t base = chunk * kRvqChunk;
     const int cnt = (int)min64(kRvqChunk, n - base);
-#pragma unroll 4
+    {  // pack surfel tid's K index bytes into one u64
+      const uint8_t* b = reinterpret_cast<const uint8_t*>(raw + buf * kIdxWords) + tid * K;
+      uint64_t v = 0;
+      if (tid < cnt)
+        for (int k = 0; k < K; k++) v |= (uint64_t)b[k] << (8 * k);
+      idx_s[tid] = v;
+    }
+    __syncthreads();
+#pragma unroll
     for (int it = 0; it < 16; it++) {
       const int s = warp * 32 + 2 * it + sub;
-      if (s >= cnt) break;
-      const uint64_t packed = idx_s[s];
-      float ax = 0.0f, ay = 0.0f;
-      for (int k = 0; k < K; k++) {
-        const int e = (int)((packed >> (8 * k)) & 0xff);
-        if (e >= E) continue;  // an index outside the codebook contributes nothing
-        const float2 v = cb2[(k * E + e) * (kHalfCols / 2) + l16];
-        ax += v.x;
-        ay += v.y;
+      if (s < cnt) {
+        const uint64_t packed = idx_s[s];
+        float ax = 0.0f, ay = 0.0f;
+        for (int k = 0; k < K; k++) {
+          const int e = (int)((packed >> (8 * k)) & 0xff);
+          if (e >= E) continue;  // an index outside the codebook contributes nothing
+          const float2 v = cb2[(k * E + e) * (kHalfCols / 2) + l16];
+          ax += v.x;
+          ay += v.y;
+        }
+        float* o = out + (base + s) * D;
+        if (c2 < D) o[c2] = ax;
+        if (c2 + 1 < D) o[c2 + 1] = ay;
       }
-      float* o = out + (base + s) * D;
-      if (c2 < D) o[c2] = ax;
-      if (c2 + 1 < D) o[c2 + 1] = ay;
     }
   }
+  asm volatile("cp.async.wait_group 0;");
 }
 
 // General shape: one thread per output value, codebook rows read through L1/L2.
@@ -121,12 +146,16 @@ int rvq_decode_launch(const uint8_t* idx, const float* cb, float* out, int64_t n
   if (n < 0 || K <= 0 || K > 8 || E <= 0 || E > 256 || D <= 0 || D > 64) return NS_ERR_UNSUPPORTED;
   if (n == 0) return NS_OK;
   if (!idx || !cb || !out) return NS_ERR_INVALID;
-  const size_t smem = (size_t)K * E * kHalfCols * sizeof(float) + kRvqChunk * sizeof(uint64_t);
+  const size_t smem = (size_t)K * E * kHalfCols * sizeof(float) + 2 * kIdxWords * sizeof(uint32_t) +
+                      kRvqChunk * sizeof(uint64_t);
   int dev = 0, sms = 0, max_smem = 0;
   NS_CUDA_TRY(cudaGetDevice(&dev));
   NS_CUDA_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
   NS_CUDA_TRY(cudaDeviceGetAttribute(&max_smem, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev));
-  if (smem <= (size_t)max_smem) {
+  // The shared-memory kernel copies index bytes in 4-byte words and codebook
+  // entries as floats: both arrays must be 4-byte aligned.
+  const bool aligned = ((uintptr_t)idx % 4 == 0) && ((uintptr_t)cb % 4 == 0);
+  if (smem <= (size_t)max_smem && aligned) {
     NS_CUDA_TRY(cudaFuncSetAttribute(rvq_decode_smem_kernel,
                                      cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     const int halves = D > kHalfCols ? 2 : 1;

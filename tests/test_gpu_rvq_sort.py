@@ -30,6 +30,18 @@ def test_rvq_shapes_bit_exact(n, K, E, D):
     assert np.array_equal(out.view(np.uint32), ref.view(np.uint32))
 
 
+def test_rvq_unaligned_index_view():
+    # a view starting one row in: index bytes at an odd offset take the gather path
+    g = torch.Generator().manual_seed(9)
+    cb = torch.randn(6, 256, 59, generator=g)
+    idx = torch.randint(0, 256, (5001, 6), generator=g).to(torch.uint8)
+    dev_idx = idx.cuda()
+    view = dev_idx.view(-1)[3:3 + 5000 * 6].view(5000, 6)  # 3-byte offset
+    out = raster.rvq_decode(view.contiguous() if not view.is_contiguous() else view, cb.cuda()).cpu().numpy()
+    ref = oracle.rvq_decode_np(idx.view(-1)[3:3 + 5000 * 6].view(5000, 6).numpy(), cb.numpy())
+    assert np.array_equal(out.view(np.uint32), ref.view(np.uint32))
+
+
 def test_rvq_negative_zero_and_specials():
     cb = torch.zeros(6, 256, 59)
     cb[0, 0, 0] = -0.0
