@@ -52,23 +52,31 @@ __device__ __forceinline__ void fetch_indices(const uint8_t* __restrict__ idx, i
   asm volatile("cp.async.commit_group;");
 }
 
+// Shared-memory decode. Template on the stage count K (fully unrolled).
+// Codebook half layout in shared memory, permuted per lane: entry (k, e) is 32
+// floats where lane j of an 8-lane group finds its columns col0 + j + 8q
+// (q = 0..3) at [j*4 + q], so one 128-bit load gives a lane its four columns.
+// A warp decodes four surfels per step (one 8-lane group each); stores of a
+// step are 8 consecutive floats per surfel and column block (full sectors).
+template <int K>
 __global__ void __launch_bounds__(kRvqThreads, 1)
 rvq_decode_smem_kernel(const uint8_t* __restrict__ idx, const float* __restrict__ cb,
-                       float* __restrict__ out, int64_t n, int K, int E, int D) {
+                       float* __restrict__ out, int64_t n, int E, int D) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   float* cb_s = reinterpret_cast<float*>(smem_raw);                                  // [K*E][32]
   uint32_t* raw = reinterpret_cast<uint32_t*>(cb_s + (size_t)K * E * kHalfCols);     // [2][kIdxWords]
-  uint64_t* idx_s = reinterpret_cast<uint64_t*>(raw + 2 * kIdxWords);                // [chunk]
+  uint2* idx_s = reinterpret_cast<uint2*>(raw + 2 * kIdxWords);                      // [chunk]
 
   const int half = blockIdx.y;
   const int col0 = half * kHalfCols;
   const int tid = threadIdx.x;
   const int lane = tid & 31, warp = tid >> 5;
 
-  // Stage this half of every codeword with 4-byte cp.async (columns past D zero-filled).
+  // Stage this half of every codeword, permuted (columns past D zero-filled).
   const int rows = K * E;
   for (int i = tid; i < rows * kHalfCols; i += kRvqThreads) {
-    const int r = i >> 5, c = col0 + (i & 31);
+    const int r = i >> 5, jq = i & 31;           // destination slot j*4 + q
+    const int c = col0 + (jq >> 2) + 8 * (jq & 3);
     const float* src = cb + (size_t)r * D + (c < D ? c : 0);
     cp_async4(cb_s + i, src, c < D ? 4 : 0);
   }
@@ -79,46 +87,66 @@ rvq_decode_smem_kernel(const uint8_t* __restrict__ idx, const float* __restrict_
   int buf = 0;
   fetch_indices(idx, n, K, chunk, nchunks, raw);
 
-  const int sub = lane >> 4;        // which surfel of the pair
-  const int l16 = lane & 15;        // float2 column within the half row
-  const int c2 = col0 + 2 * l16;    // first output column of this lane
-  const float2* cb2 = reinterpret_cast<const float2*>(cb_s);
+  const int grp = lane >> 3;  // surfel of the step
+  const int j = lane & 7;     // column block of the lane
+  const float4* cb4 = reinterpret_cast<const float4*>(cb_s);
+  const bool check_e = E < 256;
 
   for (; chunk < nchunks; chunk += gridDim.x, buf ^= 1) {
     asm volatile("cp.async.wait_group 0;");
     __syncthreads();  // codebook and this chunk's index bytes are in; last chunk consumed
-    // Prefetch the next chunk's index bytes under this chunk's work.
     fetch_indices(idx, n, K, chunk + gridDim.x, nchunks, raw + (buf ^ 1) * kIdxWords);
     const int64_t base = chunk * kRvqChunk;
     const int cnt = (int)min64(kRvqChunk, n - base);
-    {  // pack surfel tid's K index bytes into one u64
+    {  // surfel tid's K index bytes as two words (bytes 0-3, 4-7)
       const uint8_t* b = reinterpret_cast<const uint8_t*>(raw + buf * kIdxWords) + tid * K;
-      uint64_t v = 0;
-      if (tid < cnt)
-        for (int k = 0; k < K; k++) v |= (uint64_t)b[k] << (8 * k);
-      idx_s[tid] = v;
+      uint32_t lo = 0, hi = 0;
+      if (tid < cnt) {
+#pragma unroll
+        for (int k = 0; k < K; k++) {
+          if (k < 4) lo |= (uint32_t)b[k] << (8 * k);
+          else hi |= (uint32_t)b[k] << (8 * (k - 4));
+        }
+      }
+      idx_s[tid] = make_uint2(lo, hi);
     }
     __syncthreads();
-#pragma unroll
-    for (int it = 0; it < 16; it++) {
-      const int s = warp * 32 + 2 * it + sub;
+#pragma unroll 2
+    for (int step = 0; step < 8; step++) {
+      const int s = warp * 32 + step * 4 + grp;
       if (s < cnt) {
-        const uint64_t packed = idx_s[s];
-        float ax = 0.0f, ay = 0.0f;
+        const uint2 ix = idx_s[s];
+        float2 a01 = make_float2(0.0f, 0.0f), a23 = make_float2(0.0f, 0.0f);
+#pragma unroll
         for (int k = 0; k < K; k++) {
-          const int e = (int)((packed >> (8 * k)) & 0xff);
-          if (e >= E) continue;  // an index outside the codebook contributes nothing
-          const float2 v = cb2[(k * E + e) * (kHalfCols / 2) + l16];
-          ax += v.x;
-          ay += v.y;
+          const uint32_t e = ((k < 4 ? ix.x : ix.y) >> (8 * (k & 3))) & 0xffu;
+          if (check_e && e >= (uint32_t)E) continue;  // outside the codebook: contributes nothing
+          const float4 v = cb4[(k * E + (int)e) * 8 + j];
+          a01 = __fadd2_rn(a01, make_float2(v.x, v.y));
+          a23 = __fadd2_rn(a23, make_float2(v.z, v.w));
         }
-        float* o = out + (base + s) * D;
-        if (c2 < D) o[c2] = ax;
-        if (c2 + 1 < D) o[c2 + 1] = ay;
+        float* o = out + (base + s) * D + col0 + j;
+        const float a[4] = {a01.x, a01.y, a23.x, a23.y};
+#pragma unroll
+        for (int q = 0; q < 4; q++)
+          if (col0 + j + 8 * q < D) o[8 * q] = a[q];
       }
     }
   }
   asm volatile("cp.async.wait_group 0;");
+}
+
+template <int K>
+int launch_rvq_smem(const uint8_t* idx, const float* cb, float* out, int64_t n, int E, int D,
+                    size_t smem, int sms, cudaStream_t stream) {
+  NS_CUDA_TRY(cudaFuncSetAttribute(rvq_decode_smem_kernel<K>,
+                                   cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  const int halves = D > kHalfCols ? 2 : 1;
+  const int64_t nchunks = div_up64(n, kRvqChunk);
+  const int gx = (int)min64(nchunks, (int64_t)max(1, sms / halves));
+  rvq_decode_smem_kernel<K><<<dim3(gx, halves), kRvqThreads, smem, stream>>>(idx, cb, out, n, E, D);
+  NS_LAUNCH_CHECK();
+  return NS_OK;
 }
 
 // General shape: one thread per output value, codebook rows read through L1/L2.
@@ -147,7 +175,7 @@ int rvq_decode_launch(const uint8_t* idx, const float* cb, float* out, int64_t n
   if (n == 0) return NS_OK;
   if (!idx || !cb || !out) return NS_ERR_INVALID;
   const size_t smem = (size_t)K * E * kHalfCols * sizeof(float) + 2 * kIdxWords * sizeof(uint32_t) +
-                      kRvqChunk * sizeof(uint64_t);
+                      kRvqChunk * sizeof(uint2);
   int dev = 0, sms = 0, max_smem = 0;
   NS_CUDA_TRY(cudaGetDevice(&dev));
   NS_CUDA_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
@@ -156,13 +184,16 @@ int rvq_decode_launch(const uint8_t* idx, const float* cb, float* out, int64_t n
   // entries as floats: both arrays must be 4-byte aligned.
   const bool aligned = ((uintptr_t)idx % 4 == 0) && ((uintptr_t)cb % 4 == 0);
   if (smem <= (size_t)max_smem && aligned) {
-    NS_CUDA_TRY(cudaFuncSetAttribute(rvq_decode_smem_kernel,
-                                     cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    const int halves = D > kHalfCols ? 2 : 1;
-    const int64_t nchunks = div_up64(n, kRvqChunk);
-    int gx = (int)min64(nchunks, (int64_t)max(1, sms / halves));
-    rvq_decode_smem_kernel<<<dim3(gx, halves), kRvqThreads, smem, stream>>>(idx, cb, out, n, K, E,
-                                                                             D);
+    switch (K) {
+      case 1: return launch_rvq_smem<1>(idx, cb, out, n, E, D, smem, sms, stream);
+      case 2: return launch_rvq_smem<2>(idx, cb, out, n, E, D, smem, sms, stream);
+      case 3: return launch_rvq_smem<3>(idx, cb, out, n, E, D, smem, sms, stream);
+      case 4: return launch_rvq_smem<4>(idx, cb, out, n, E, D, smem, sms, stream);
+      case 5: return launch_rvq_smem<5>(idx, cb, out, n, E, D, smem, sms, stream);
+      case 6: return launch_rvq_smem<6>(idx, cb, out, n, E, D, smem, sms, stream);
+      case 7: return launch_rvq_smem<7>(idx, cb, out, n, E, D, smem, sms, stream);
+      default: return launch_rvq_smem<8>(idx, cb, out, n, E, D, smem, sms, stream);
+    }
   } else {
     int64_t total = n * D;
     int blocks = (int)min64(div_up64(total, 256), (int64_t)sms * 16);
