@@ -23,12 +23,13 @@
 //   weight, number of levels to query) to its pixel's queue in shared memory.
 //   The warp stops when one of its queues is full or the batch is done.
 //
-//   Phase B (hash lookups). Levels in a warp-uniform outer loop (so the
-//   dense/hashed choice is a uniform branch), the pixel's queued samples in the
-//   inner loop, two levels x two samples (four lookups) in flight per lane. The 32 lanes are 32 neighbouring
-//   pixels whose k-th samples usually hit nearby points, so at the coarse
-//   levels their corner loads coalesce. Each (pixel, level) accumulator adds
-//   its samples in queue order, the reference's per-pixel order.
+//   Phase B (hash lookups). The warp's queued samples are compacted into one
+//   k-major list (every pixel's sample k, then k+1, ...) so all 32 lanes look up
+//   real samples; neighbouring pixels' k-th samples usually hit nearby points,
+//   so their corner loads coalesce at the coarse levels. Levels run in a
+//   warp-uniform outer loop (the dense/hashed choice is a uniform branch), two
+//   levels x two list entries (four lookups) in flight per lane. Each pixel's
+//   owner lane adds its results in queue order, the reference's per-pixel order.
 //
 // The hash table is read as fp16 (or fp32) pairs through the read-only path;
 // at 16 levels x 2^19 x 2 fp16 it is 32 MB and stays resident in the 126 MB L2.
@@ -39,7 +40,9 @@ namespace {
 
 constexpr int kThreads = kTilePixels;  // 256: one pixel per thread
 constexpr int kQueue = 8;              // queued samples per pixel between drains
-constexpr int kAccStride = 34;         // floats per pixel row of the accumulators
+constexpr int kWarps = kThreads / 32;
+constexpr int kChunk = 64;             // compacted samples looked up per warp step (2 per lane)
+constexpr int kAccStride = 32;         // floats per pixel row of the accumulators
 constexpr int kMaxChannels = 32;
 constexpr int kMaxLevels = 16;
 
@@ -60,9 +63,24 @@ struct BlendSmem {
   float4 rec[kThreads][kRecordFloat4];  // surfel records of the current batch
   float4 samp[kQueue][kThreads];        // (hit point in [0,1]^3, weight)
   uint8_t lvl[kQueue][kThreads];        // levels to query for the sample (0: none)
-  float acc[kThreads * kAccStride];     // feature accumulators [pixel][channel]
+  uint8_t item[kWarps][kThreads];       // per warp: queued samples in k-major order, (k << 5) | lane
+  uint8_t pos[kQueue][kThreads];        // position of a pixel's k-th sample in its warp's list
+  float4 res[kWarps][kChunk];           // lookups of the current chunk: level l (xy), l+1 (zw)
+  float acc[kThreads * kAccStride];     // feature accumulators, see acc_pair()
   LevelConst lv[kMaxLevels];
 };
+
+// Channels (2l, 2l+1) of pixel p: float2 pair (l ^ (p & 15)) of the pixel's row,
+// so that threads reading one channel of consecutive pixels hit distinct banks.
+__device__ __forceinline__ float2* acc_pair(float* acc, int p, int l) {
+  return reinterpret_cast<float2*>(acc + p * kAccStride + 2 * (l ^ (p & 15)));
+}
+
+__device__ __forceinline__ uint32_t lane_mask_lt() {
+  uint32_t m;
+  asm("mov.u32 %0, %%lanemask_lt;" : "=r"(m));
+  return m;
+}
 
 template <typename TableT>
 __device__ LevelConst make_level(const RenderParams& p, int l) {
@@ -188,8 +206,7 @@ __global__ void __launch_bounds__(kThreads, 2) blend_kernel(const RenderParams p
   const uint32_t L = p.L;
 
   if (t < (int)L) S.lv[t] = make_level<TableT>(p, t);
-  float* my_acc = &S.acc[t * kAccStride];
-  for (int c = 0; c < kAccStride; c++) my_acc[c] = 0.f;  // only this thread touches its row
+  for (int c = 0; c < kAccStride; c++) S.acc[t * kAccStride + c] = 0.f;  // only this thread's row
 
   const uint2 range = p.ranges[tile];
   const int total = (int)(range.y - range.x);
@@ -352,36 +369,81 @@ __global__ void __launch_bounds__(kThreads, 2) blend_kernel(const RenderParams p
       // only its own queue and accumulator row, so no synchronisation is needed.
       const int kmax = __reduce_max_sync(0xffffffffu, cnt);
       if (kmax > 0) {
-        // Two levels x two samples per step: four independent lookups in
-        // flight per lane. Per (pixel, level) the samples still add in order.
+        // Compact the warp's queued samples into one k-major list (sample k of
+        // every pixel that has one, then k+1, ...), so all 32 lanes look up real
+        // samples; neighbouring pixels' k-th samples stay adjacent (coalescing).
+        const int lane = t & 31, wid = t >> 5, pbase = wid * 32;
+        const uint32_t lt = lane_mask_lt();
+        int nitems = 0;
+#pragma unroll
+        for (int k = 0; k < kQueue; k++) {
+          const uint32_t m = __ballot_sync(0xffffffffu, cnt > k);
+          if (cnt > k) {
+            const int ps = nitems + __popc(m & lt);
+            S.item[wid][ps] = (uint8_t)((k << 5) | lane);
+            S.pos[k][t] = (uint8_t)ps;
+          }
+          nitems += __popc(m);
+        }
+        __syncwarp();
+        // Two levels per pass, 64 list entries (two per lane) per step: four
+        // lookups in flight per lane. Each pixel's owner lane then adds its own
+        // results from the step, in sample order.
         for (uint32_t l = 0; l < L; l += 2) {
           const bool has1 = l + 1 < L;
           const LevelConst lc0 = S.lv[l];
           const LevelConst lc1 = S.lv[has1 ? l + 1 : l];
-          float2* ap = reinterpret_cast<float2*>(my_acc + 2 * l);
-          float2 c0 = ap[0];
-          float2 c1 = has1 ? ap[1] : make_float2(0.f, 0.f);
-          for (int k = 0; k < kmax; k += 2) {
-            const uint32_t m0 = k < cnt ? (uint32_t)S.lvl[k][t] : 0u;
-            const uint32_t m1 = k + 1 < cnt ? (uint32_t)S.lvl[k + 1][t] : 0u;
-            const bool u00 = l < m0, u10 = l < m1;                       // level l
-            const bool u01 = has1 && l + 1 < m0, u11 = has1 && l + 1 < m1;  // level l+1
-            const float4 s0 = S.samp[k][t];
-            const float4 s1 = S.samp[k + 1 < kQueue ? k + 1 : k][t];
-            float f00[3], f10[3], f01[3], f11[3];
-            Corner8<TableT> v00, v10, v01, v11;
-            if (u00) lookup_issue<TableT>(lc0, p.table, s0, half_shift, p.interp, f00, v00);
-            if (u10) lookup_issue<TableT>(lc0, p.table, s1, half_shift, p.interp, f10, v10);
-            if (u01) lookup_issue<TableT>(lc1, p.table, s0, half_shift, p.interp, f01, v01);
-            if (u11) lookup_issue<TableT>(lc1, p.table, s1, half_shift, p.interp, f11, v11);
-            const float2 sw0 = make_float2(s0.w, s0.w), sw1 = make_float2(s1.w, s1.w);
-            if (u00) c0 = __ffma2_rn(lookup_finish<TableT>(f00, v00), sw0, c0);
-            if (u10) c0 = __ffma2_rn(lookup_finish<TableT>(f10, v10), sw1, c0);
-            if (u01) c1 = __ffma2_rn(lookup_finish<TableT>(f01, v01), sw0, c1);
-            if (u11) c1 = __ffma2_rn(lookup_finish<TableT>(f11, v11), sw1, c1);
+          float2* ap0 = acc_pair(S.acc, t, l);
+          float2* ap1 = acc_pair(S.acc, t, has1 ? l + 1 : l);
+          float2 c0 = *ap0;
+          float2 c1 = has1 ? *ap1 : make_float2(0.f, 0.f);
+          int nk = 0;
+          for (int ch = 0; ch < nitems; ch += kChunk) {
+            float4 sa = make_float4(0.f, 0.f, 0.f, 0.f), sb = sa;
+            uint32_t ma = 0, mb = 0;
+            const int ia = ch + lane, ib = ch + 32 + lane;
+            if (ia < nitems) {
+              const uint32_t tb = S.item[wid][ia];
+              const int pp = pbase + (int)(tb & 31u), k = (int)(tb >> 5);
+              sa = S.samp[k][pp];
+              ma = S.lvl[k][pp];
+            }
+            if (ib < nitems) {
+              const uint32_t tb = S.item[wid][ib];
+              const int pp = pbase + (int)(tb & 31u), k = (int)(tb >> 5);
+              sb = S.samp[k][pp];
+              mb = S.lvl[k][pp];
+            }
+            const bool ua0 = l < ma, ub0 = l < mb, ua1 = has1 && l + 1 < ma, ub1 = has1 && l + 1 < mb;
+            float fa0[3], fb0[3], fa1[3], fb1[3];
+            Corner8<TableT> va0, vb0, va1, vb1;
+            if (ua0) lookup_issue<TableT>(lc0, p.table, sa, half_shift, p.interp, fa0, va0);
+            if (ub0) lookup_issue<TableT>(lc0, p.table, sb, half_shift, p.interp, fb0, vb0);
+            if (ua1) lookup_issue<TableT>(lc1, p.table, sa, half_shift, p.interp, fa1, va1);
+            if (ub1) lookup_issue<TableT>(lc1, p.table, sb, half_shift, p.interp, fb1, vb1);
+            const float2 z = make_float2(0.f, 0.f);
+            const float2 ra0 = ua0 ? lookup_finish<TableT>(fa0, va0) : z;
+            const float2 rb0 = ub0 ? lookup_finish<TableT>(fb0, vb0) : z;
+            const float2 ra1 = ua1 ? lookup_finish<TableT>(fa1, va1) : z;
+            const float2 rb1 = ub1 ? lookup_finish<TableT>(fb1, vb1) : z;
+            S.res[wid][lane] = make_float4(ra0.x, ra0.y, ra1.x, ra1.y);
+            S.res[wid][32 + lane] = make_float4(rb0.x, rb0.y, rb1.x, rb1.y);
+            __syncwarp();
+            while (nk < cnt) {
+              const int ps = S.pos[nk][t];
+              if (ps >= ch + kChunk) break;
+              const float4 rv = S.res[wid][ps - ch];
+              const uint32_t mk = S.lvl[nk][t];
+              const float w = S.samp[nk][t].w;
+              const float2 ww = make_float2(w, w);
+              if (l < mk) c0 = __ffma2_rn(make_float2(rv.x, rv.y), ww, c0);
+              if (has1 && l + 1 < mk) c1 = __ffma2_rn(make_float2(rv.z, rv.w), ww, c1);
+              nk++;
+            }
+            __syncwarp();
           }
-          ap[0] = c0;
-          if (has1) ap[1] = c1;
+          *ap0 = c0;
+          if (has1) *ap1 = c1;
         }
       }
       // Warp-uniform: the batch is finished for this warp when the walk reached
@@ -401,7 +463,10 @@ __global__ void __launch_bounds__(kThreads, 2) blend_kernel(const RenderParams p
     p.final_T[pid + 2 * HW] = M2;
     p.n_contrib[pid] = last_contributor;
     p.n_contrib[pid + HW] = (uint32_t)median_contributor;  // -1 saturates to 0
-    for (int c = 0; c < p.C; c++) p.out_color[c * HW + pid] = my_acc[c];
+    for (int c = 0; c < p.C; c++) {
+      const float2 pr = *acc_pair(S.acc, t, c >> 1);
+      p.out_color[c * HW + pid] = (c & 1) ? pr.y : pr.x;
+    }
     float* o = p.out_others + pid;
     o[0 * HW] = D;
     o[1 * HW] = 1 - T;
