@@ -58,6 +58,10 @@ def load() -> C.CDLL:
     lib.oracle_grid_index.argtypes = [i32, u32, u32, u32, u32, u32]
     lib.oracle_rvq_decode.argtypes = [i64, i32, i32, i32, vp, vp, vp]
     lib.oracle_num_threads.restype = i32
+    lib.oracle_render_backward.argtypes = [i32, i32, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, i32, i32, u32, f32,
+                                           u32, i32, u32, i32, f32, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp]
+    lib.oracle_preprocess_backward.argtypes = [i32, vp, vp, vp, vp, vp, vp, vp, i32, i32, f32, f32, vp, vp, vp,
+                                               vp, vp, vp, vp]
     _lib = lib
     return lib
 
@@ -209,6 +213,52 @@ def forward(means3D, scales, rotations, opacities, homotrans, ap_level, table_f3
     out = render(pre, vals, ranges, homotrans, ap_level, table_f32, offsets, gridrange, W, H, C_out, LD, L, S,
                  Hres, **kw)
     return out, pre, len(vals)
+
+
+def render_backward(pre, vals, ranges, fwd, homotrans, ap_level, table_f32, offsets, gridrange, W, H, C_out, LD,
+                    L, S, Hres, dL_dcolor, dL_dothers, align_corners=False, interp=0, contract=False, beta=0.0):
+    """renderCUDAsurfelBackward<C> mode 0 restated (nest_oracle_bw.cpp). `fwd` is the
+    dict returned by render(). Returns the render-pass gradients (reference layouts)."""
+    lib = load()
+    P = pre["radii"].shape[0]
+    table = _f32(table_f32)
+    g = dict(dL_dtable=np.zeros_like(table), dL_dtransMat=np.zeros((P, 9), np.float32),
+             dL_dhomoMat=np.zeros((P, 9), np.float32), dL_dmean2D=np.zeros((P, 3), np.float32),
+             dL_dnormal=np.zeros((P, 3), np.float32), dL_dopacity=np.zeros(P, np.float32),
+             dL_gradsum=np.zeros(P, np.float32))
+    homotrans = _f32(homotrans).reshape(-1, 16)
+    ap = _f32(ap_level).reshape(-1) if ap_level is not None else np.full(P, 1e9, np.float32)
+    offs = np.ascontiguousarray(np.asarray(offsets, dtype=np.int32))
+    gc, go = _f32(dL_dcolor), _f32(dL_dothers)
+    assert gc.shape == (C_out, H, W) and go.shape == (14, H, W)
+    lib.oracle_render_backward(int(W), int(H), _p(np.ascontiguousarray(ranges, np.uint32)),
+                               _p(np.ascontiguousarray(vals, np.uint32)), _p(pre["means2D"]), _p(pre["transMat"]),
+                               _p(pre["normal_opacity"]), _p(homotrans), _p(ap), _p(table), _p(offs),
+                               _p(_f32(gridrange).reshape(2)), int(C_out), int(LD), int(L), float(S), int(Hres),
+                               int(bool(align_corners)), int(interp), int(bool(contract)), float(beta),
+                               _p(fwd["final_T"]), _p(fwd["n_contrib"]), _p(gc), _p(go), _p(g["dL_dtable"]),
+                               _p(g["dL_dtransMat"]), _p(g["dL_dhomoMat"]), _p(g["dL_dmean2D"]),
+                               _p(g["dL_dnormal"]), _p(g["dL_dopacity"]), _p(g["dL_gradsum"]))
+    return g
+
+
+def preprocess_backward(means3D, scales, rotations, pre, g, viewmatrix, projmatrix, W, H, tanfovx, tanfovy):
+    """preprocessCUDA backward + compute_transmat_aabb restated. Consumes the
+    render-pass gradients `g` (from render_backward) and returns
+    dL_dmeans3D [P,3], dL_dscales [P,2], dL_drots [P,4] and the densification
+    statistic dL_dmean2D [P,3] (the rasterizer's means2D gradient)."""
+    lib = load()
+    means3D, scales, rotations = _f32(means3D), _f32(scales), _f32(rotations)
+    P = means3D.shape[0]
+    out = dict(dL_dmeans3D=np.zeros((P, 3), np.float32), dL_dscales=np.zeros((P, 2), np.float32),
+               dL_drots=np.zeros((P, 4), np.float32), dL_dmean2D=np.array(g["dL_dmean2D"], np.float32, copy=True))
+    lib.oracle_preprocess_backward(P, _p(means3D), _p(scales), _p(rotations), _p(pre["radii"]),
+                                   _p(pre["transMat"]), _p(_f32(viewmatrix).reshape(16)),
+                                   _p(_f32(projmatrix).reshape(16)), int(W), int(H), float(tanfovx),
+                                   float(tanfovy), _p(out["dL_dmean2D"]), _p(_f32(g["dL_dnormal"])),
+                                   _p(_f32(g["dL_dtransMat"])), _p(_f32(g["dL_dhomoMat"])), _p(out["dL_dmeans3D"]),
+                                   _p(out["dL_dscales"]), _p(out["dL_drots"]))
+    return out
 
 
 def num_threads() -> int:

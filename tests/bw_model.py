@@ -1,0 +1,183 @@
+"""Float64 torch model of the mode-0 forward pass, differentiated by autograd.
+
+Test infrastructure: it pins the CPU oracle's backward (oracle/nest_oracle_bw.cpp)
+to true gradients. It is written independently of the oracle -- tensors over
+the pixels of a tile, one step per list entry -- and reuses only the oracle's
+discrete structure (per-tile lists from binning), so that both walk the same
+surfels in the same order.
+
+The reference's backward differs from the derivative of its forward in known
+places; the model states them explicitly so the comparison covers the rest:
+  * means2D: the forward centre uses compute_aabb's cutoff 4 (forward.cu:294-320,
+    t = (16, 16, -1)); the backward pushes dL/dmeans2D into T with cutoff 3
+    (backward.cu:2143, t = (9, 9, -1)). The model's centre has the cutoff-4 value
+    and the cutoff-3 derivative.
+  * rotations: quat_to_rotmat_vjp (auxiliary.h:243-287) is the derivative of the
+    rotation formula on the quaternion as given, without the normalisation; the
+    model feeds unit quaternions to that formula directly.
+  * beta > 0 and the 0.99 alpha clamp are not modelled (the pin uses beta = 0 and
+    opacities below 0.99).
+"""
+from __future__ import annotations
+
+import numpy as np
+import torch
+
+NEAR, FAR = 0.2, 100.0
+TILE = 16
+
+
+def rotation_columns(q: torch.Tensor):
+    w, x, y, z = q.unbind(1)
+    r0 = torch.stack([1 - 2 * (y * y + z * z), 2 * (x * y + w * z), 2 * (x * z - w * y)], 1)
+    r1 = torch.stack([2 * (x * y - w * z), 1 - 2 * (x * x + z * z), 2 * (y * z + w * x)], 1)
+    r2 = torch.stack([2 * (x * z + w * y), 2 * (y * z - w * x), 1 - 2 * (x * x + y * y)], 1)
+    return r0, r1, r2
+
+
+def ndc_to_pixel(pm: np.ndarray, W: int, H: int) -> torch.Tensor:
+    """P[c, r] = sum_k pm[4r + k] n[c][k]: world -> homogeneous pixel coordinates."""
+    n = np.array([[W / 2, 0, 0, (W - 1) / 2], [0, H / 2, 0, (H - 1) / 2], [0, 0, 0, 1]], np.float64)
+    M = np.asarray(pm, np.float64).reshape(4, 4)  # M[r, k] = pm[4r + k]
+    return torch.tensor(n @ M.T)  # [3, 4]
+
+
+def centre(Tu, Tv, Tw, cutoff: float):
+    t0 = cutoff * cutoff
+    d = t0 * Tw[:, 0] ** 2 + t0 * Tw[:, 1] ** 2 - Tw[:, 2] ** 2
+    px = (t0 * Tu[:, 0] * Tw[:, 0] + t0 * Tu[:, 1] * Tw[:, 1] - Tu[:, 2] * Tw[:, 2]) / d
+    py = (t0 * Tv[:, 0] * Tw[:, 0] + t0 * Tv[:, 1] * Tw[:, 1] - Tv[:, 2] * Tw[:, 2]) / d
+    return torch.stack([px, py], 1)
+
+
+def grid_index(g: torch.Tensor, hsize: int, res: int, align_corners: bool) -> torch.Tensor:
+    stride, index = 1, torch.zeros_like(g[:, 0])
+    for d in range(3):
+        if stride > hsize:
+            break
+        index = index + g[:, d] * stride
+        stride *= res if align_corners else res + 1
+    if stride > hsize:
+        m = 0xFFFFFFFF
+        index = (g[:, 0] & m) ^ ((g[:, 1] * 2654435761) & m) ^ ((g[:, 2] * 805459861) & m)
+    return index % hsize
+
+
+def query(xyz, apl, table, offsets, L, LD, S, Hres, vmin, vmax, align_corners=False, interp=0):
+    """Trilinear hash-grid features [n, L*LD] at xyz [n,3]; levels >= apl are zero."""
+    inp = (xyz - vmin) / (vmax - vmin)
+    oob = ((inp < 0) | (inp > 1)).any(1)
+    feats = []
+    for lv in range(L):
+        hs = int(offsets[lv + 1] - offsets[lv])
+        scale = float(np.float32(np.exp2(np.float32(lv * np.float32(S)))) * np.float32(Hres) - np.float32(1.0))
+        res = int(np.ceil(np.float32(scale))) + 1
+        pos = inp * scale + (0.0 if align_corners else 0.5)
+        pg = torch.floor(pos.detach())
+        frac = pos - pg
+        if interp == 1:
+            frac = frac * frac * (3.0 - 2.0 * frac)
+        acc = 0
+        for c in range(8):
+            bits = [(c >> d) & 1 for d in range(3)]
+            w = 1
+            for d in range(3):
+                w = w * (frac[:, d] if bits[d] else 1 - frac[:, d])
+            g = pg.long() + torch.tensor(bits, dtype=torch.long)
+            rows = int(offsets[lv]) + grid_index(g, hs, res, align_corners)
+            acc = acc + w[:, None] * table[rows]
+        on = torch.as_tensor(lv < apl, dtype=table.dtype)[:, None] * (~oob)[:, None].to(table.dtype)
+        feats.append(acc * on)
+    return torch.cat(feats, 1)
+
+
+def render(means, scales, rots, opac, table, cam, lists, grid, apl_int, W, H):
+    """Forward pass over the oracle's tile lists. Returns (color [C,H,W], others [7,H,W], margins).
+
+    margins: the smallest relative distance of any decision (alpha >= 1/255, the
+    rho3d/rho2d branch, near plane, termination) from its threshold, so a test can
+    check that float32 and float64 take the same branches."""
+    vm = np.asarray(cam["viewmatrix"], np.float64).reshape(4, 4)
+    P = ndc_to_pixel(cam["projmatrix"], W, H)
+    r0, r1, r2 = rotation_columns(rots)
+    L0, L1 = r0 * scales[:, 0:1], r1 * scales[:, 1:2]
+    Tu = torch.stack([L0 @ P[0, :3], L1 @ P[0, :3], means @ P[0, :3] + P[0, 3]], 1)
+    Tv = torch.stack([L0 @ P[1, :3], L1 @ P[1, :3], means @ P[1, :3] + P[1, 3]], 1)
+    Tw = torch.stack([L0 @ P[2, :3], L1 @ P[2, :3], means @ P[2, :3] + P[2, 3]], 1)
+    vmt = torch.tensor(vm)
+    n = r2 @ vmt[:3, :3]
+    n = n / n.norm(dim=1, keepdim=True)
+    pv = means @ vmt[:3, :3] + vmt[3, :3]
+    flip = torch.where(-(pv * n).sum(1) > 0, 1.0, -1.0).detach()
+    n = n * flip[:, None]
+    xy3 = centre(Tu, Tv, Tw, 3.0)
+    xy = xy3 + (centre(Tu, Tv, Tw, 4.0) - xy3).detach()
+
+    ranges, point_list = lists
+    C = grid["L"] * grid["LD"]
+    color = torch.zeros(C, H * W, dtype=torch.float64)
+    others = torch.zeros(7, H * W, dtype=torch.float64)
+    gx = (W + TILE - 1) // TILE
+    margin = np.inf
+    for t in range(ranges.shape[0]):
+        tx, ty = t % gx, t // gx
+        ys, xs = np.meshgrid(np.arange(ty * TILE, min(H, ty * TILE + TILE)),
+                             np.arange(tx * TILE, min(W, tx * TILE + TILE)), indexing="ij")
+        ys, xs = ys.reshape(-1), xs.reshape(-1)
+        pid = torch.as_tensor(ys * W + xs)
+        pxf = torch.as_tensor(xs, dtype=torch.float64)
+        pyf = torch.as_tensor(ys, dtype=torch.float64)
+        npx = len(xs)
+        T = torch.ones(npx, dtype=torch.float64)
+        done = torch.zeros(npx, dtype=torch.bool)
+        D = torch.zeros(npx, dtype=torch.float64)
+        M1, M2, dist, med = D.clone(), D.clone(), D.clone(), D.clone()
+        N = torch.zeros(npx, 3, dtype=torch.float64)
+        Cacc = torch.zeros(npx, C, dtype=torch.float64)
+        for k in range(int(ranges[t, 0]), int(ranges[t, 1])):
+            i = int(point_list[k])
+            kk = pxf[:, None] * Tw[i] - Tu[i]
+            ll = pyf[:, None] * Tw[i] - Tv[i]
+            p = torch.linalg.cross(kk, ll, dim=1)
+            sx, sy = p[:, 0] / p[:, 2], p[:, 1] / p[:, 2]
+            rho3d = sx * sx + sy * sy
+            dx, dy = xy[i, 0] - pxf, xy[i, 1] - pyf
+            rho2d = 2.0 * (dx * dx + dy * dy)
+            b3 = (rho3d <= rho2d).detach()
+            rho = torch.where(b3, rho3d, rho2d)
+            c_d = torch.where(b3, sx * Tw[i, 0] + sy * Tw[i, 1] + Tw[i, 2], Tw[i, 2].expand(npx))
+            G = torch.exp(-0.5 * rho)
+            alpha = opac[i] * G
+            valid = (~done) & (c_d.detach() >= NEAR) & (alpha.detach() >= 1.0 / 255.0)
+            test_T = T * (1 - alpha)
+            stop = valid & (test_T.detach() < 1e-4)
+            live = (~done)
+            if live.any():
+                a = alpha.detach()[live].numpy()
+                gap = (rho3d - rho2d).detach().abs() / torch.maximum(rho3d, rho2d).detach().clamp_min(1e-300)
+                m = [np.abs(a - 1 / 255) / np.maximum(a, 1e-300), gap[live].numpy(),
+                     np.abs(c_d.detach()[live].numpy() - NEAR)]
+                tt = test_T.detach()[live].numpy()
+                m.append(np.abs(tt - 1e-4) / 1e-4)
+                margin = min(margin, *[float(np.min(x)) for x in m])
+            done = done | stop
+            valid = valid & ~stop
+            vf = valid.to(torch.float64)
+            w = alpha * T * vf
+            A = 1 - T
+            md = FAR / (FAR - NEAR) * (1 - NEAR / c_d)
+            dist = dist + (md * md * A + M2 - 2 * md * M1) * w
+            D = D + c_d * w
+            M1 = M1 + md * w
+            M2 = M2 + md * md * w
+            med = torch.where(valid & (T.detach() > 0.5), c_d, med)
+            N = N + n[i][None, :] * w[:, None]
+            hit = torch.where(b3[:, None], sx[:, None] * L0[i] + sy[:, None] * L1[i] + means[i], means[i].expand(npx, 3))
+            f = query(hit, np.full(npx, apl_int[i]), table, grid["offsets"], grid["L"], grid["LD"], grid["S"],
+                      grid["H"], grid["vmin"], grid["vmax"], grid.get("align_corners", False),
+                      grid.get("interp", 0))
+            Cacc = Cacc + f * w[:, None]
+            T = torch.where(valid, test_T, T)
+        color = color.index_copy(1, pid, Cacc.T)
+        others = others.index_copy(1, pid, torch.stack([D, 1 - T, N[:, 0], N[:, 1], N[:, 2], med, dist], 0))
+    return color.reshape(C, H, W), others.reshape(7, H, W), margin, xy
