@@ -22,6 +22,10 @@
  *                            decode: decode -> activate -> rasterize -> MLP -> mask/bg
  *   ns_radix_sort_pairs   <- cub::DeviceRadixSort::SortPairs as called at
  *                            rasterizer_impl.cu:381-386 (stable, bits [0, end_bit))
+ *   ns_rasterize_backward <- RasterizeGaussiansBackwardCUDA, rasterize_points.cu:244-450,
+ *                            and CudaRasterizer::Rasterizer::backward,
+ *                            rasterizer_impl.cu:444-592 (BACKWARD::render,
+ *                            backward.cu:445-2052; BACKWARD::preprocess, :2216-2273)
  */
 #ifndef NEST_B200_H_
 #define NEST_B200_H_
@@ -129,6 +133,46 @@ int ns_rasterize_forward(const ns_raster_settings* settings, const ns_surfels* s
                          const ns_raster_outputs* outputs, void* geom, size_t geom_bytes,
                          void* binning, size_t binning_bytes, void* image, size_t image_bytes,
                          int64_t* num_rendered, int flags, void* stream);
+
+/* Gradients arriving at the forward outputs. */
+typedef struct ns_raster_grads_in {
+  const float* dL_dout_color;   /* [channels, H, W] */
+  const float* dL_dout_others;  /* [14, H, W]; channels 0-6 carry gradient (depth,
+                                   alpha, normal x3, median depth, distortion) */
+  const int32_t* radii;         /* [P] as written by the forward call */
+} ns_raster_grads_in;
+
+/* Gradients produced by the backward pass (every pointer required). Per-surfel
+ * arrays are written for all P surfels (zero where radii <= 0); dL_dtable is
+ * zeroed by the call and then accumulated. */
+typedef struct ns_raster_grads_out {
+  float* dL_dmeans3D;   /* [P,3] */
+  float* dL_dmean2D;    /* [P,3] screen-space densification statistic (the
+                           reference's means2D gradient, backward.cu:2268-2272) */
+  float* dL_dopacity;   /* [P] */
+  float* dL_dscales;    /* [P,2] */
+  float* dL_drots;      /* [P,4] */
+  float* dL_dtable;     /* [table_rows, level_dim] fp32, for an fp16 or fp32 table */
+  int64_t table_rows;   /* rows of dL_dtable (offsets[levels]) */
+  float* dL_gradsum;    /* [P] sum over samples of alpha*T*|dL/dcolor|_1 (the
+                           reference's dL_gradsum, returned in ap_level's slot) */
+} ns_raster_grads_out;
+
+/* Scratch of the backward pass: per-surfel gradient accumulators. */
+size_t ns_backward_scratch_bytes(int32_t P);
+
+/* Backward rasterization, render_mode 0. settings, surfels, geom, binning and
+ * image must be those of the forward call whose outputs the gradients refer to
+ * (the scratch buffers unchanged since). homotrans, when given to the forward,
+ * is treated as build_H(rotations, scales, means3D): its gradient is folded into
+ * the mean, scale and rotation gradients, as the reference does. The transform
+ * is rebuilt with scale_modifier 1 and rotations are differentiated as given
+ * (no normalisation), also as in the reference. */
+int ns_rasterize_backward(const ns_raster_settings* settings, const ns_surfels* surfels,
+                          const ns_raster_grads_in* grads_in, const ns_raster_grads_out* grads_out,
+                          const void* geom, size_t geom_bytes, const void* binning,
+                          size_t binning_bytes, const void* image, size_t image_bytes,
+                          int64_t num_rendered, void* scratch, size_t scratch_bytes, void* stream);
 
 /* Reads (and clears) the device error word of a geometry scratch buffer; syncs. */
 int ns_read_device_status(void* geom, int32_t P, void* stream);

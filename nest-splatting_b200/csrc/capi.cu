@@ -301,6 +301,90 @@ int ns_rasterize_forward(const ns_raster_settings* settings, const ns_surfels* s
                         num_rendered, flags, stream);
 }
 
+size_t ns_backward_scratch_bytes(int32_t P) { return align_up(backward_accum_bytes(P)); }
+
+int ns_rasterize_backward(const ns_raster_settings* settings, const ns_surfels* surfels,
+                          const ns_raster_grads_in* gi, const ns_raster_grads_out* go,
+                          const void* geom, size_t geom_bytes, const void* binning,
+                          size_t binning_bytes, const void* image, size_t image_bytes,
+                          int64_t num_rendered, void* scratch, size_t scratch_bytes,
+                          void* stream_) {
+  cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_);
+  int rc = validate_settings(settings);
+  if (rc) return rc;
+  if (!surfels || !gi || !go) return NS_ERR_INVALID;
+  const int P = surfels->P;
+  if (P < 0 || num_rendered < 0) return NS_ERR_INVALID;
+  if (settings->level_dim != 2) return NS_ERR_UNSUPPORTED;
+  if (!go->dL_dmeans3D || !go->dL_dmean2D || !go->dL_dopacity || !go->dL_dscales ||
+      !go->dL_drots || !go->dL_dtable || !go->dL_gradsum || go->table_rows < 0)
+    return NS_ERR_INVALID;
+  if (go->table_rows > 0)
+    NS_CUDA_TRY(cudaMemsetAsync(go->dL_dtable, 0,
+                                (size_t)go->table_rows * settings->level_dim * sizeof(float), stream));
+  if (P == 0) return NS_OK;
+  if (!surfels->means3D || !surfels->scales || !surfels->rotations || !surfels->features ||
+      !surfels->offsets || !surfels->gridrange)
+    return NS_ERR_INVALID;
+  if (!gi->dL_dout_color || !gi->dL_dout_others || !gi->radii) return NS_ERR_INVALID;
+  if (!geom || !binning || !image || !scratch) return NS_ERR_INVALID;
+  if (geom_bytes < ns_geometry_scratch_bytes(P)) return NS_ERR_SCRATCH;
+  if (image_bytes < ns_image_scratch_bytes(settings->image_width, settings->image_height))
+    return NS_ERR_SCRATCH;
+  if (scratch_bytes < ns_backward_scratch_bytes(P)) return NS_ERR_SCRATCH;
+  const int64_t cap = bin_capacity(binning_bytes);
+  if (cap < 0 || num_rendered > cap) return NS_ERR_SCRATCH;
+  const int W = settings->image_width, H = settings->image_height;
+  GeomState g = carve_geom(const_cast<void*>(geom), P, nullptr);
+  ImageState im = carve_image(const_cast<void*>(image), W, H, nullptr);
+  BinState b = carve_bin(const_cast<void*>(binning), cap, nullptr);
+  float* accum = static_cast<float*>(scratch);
+  NS_CUDA_TRY(cudaMemsetAsync(accum, 0, backward_accum_bytes(P), stream));
+  // W and H as preprocessCUDA's backward recomputes them from the focal length
+  // (backward.cu:2247-2248, focal from rasterizer_impl.cu:508-509), in float.
+  const float focal_x = (float)W / (2.0f * settings->tanfovx);
+  const float focal_y = (float)H / (2.0f * settings->tanfovy);
+  volatile float wx = focal_x * settings->tanfovx, wy = focal_y * settings->tanfovy;
+  const int Wq = (int)(wx * 2.0f), Hq = (int)(wy * 2.0f);
+  BackwardParams bp;
+  bp.W = W;
+  bp.H = H;
+  bp.C = (int)settings->channels;
+  bp.LD = (int)settings->level_dim;
+  bp.L = settings->levels;
+  bp.S = settings->level_scale_log2;
+  bp.Hres = settings->base_resolution;
+  bp.align_corners = settings->align_corners;
+  bp.interp = settings->interpolation;
+  bp.contract = settings->if_contract;
+  bp.beta = settings->beta;
+  bp.Wq = Wq;
+  bp.Hq = Hq;
+  bp.projmatrix = settings->projmatrix;
+  bp.viewmatrix = settings->viewmatrix;
+  // The ray/plane form of the hit-point gradient equals the reference's form
+  // when the blended transform and the preprocess backward's rebuilt transform
+  // are the same matrix: scale_modifier 1 and the same image size.
+  bp.ray_hit = (settings->scale_modifier == 1.0f && Wq == W && Hq == H) ? 1 : 0;
+  bp.ranges = im.ranges;
+  bp.point_list = b.vals_sorted;
+  bp.records = g.records;
+  bp.table = surfels->features;
+  bp.offsets = surfels->offsets;
+  bp.gridrange = surfels->gridrange;
+  bp.final_T = im.final_T;
+  bp.n_contrib = im.n_contrib;
+  bp.dL_dcolor = gi->dL_dout_color;
+  bp.dL_dothers = gi->dL_dout_others;
+  bp.dL_dtable = go->dL_dtable;
+  bp.accum = accum;
+  rc = blend_backward_launch(bp, settings->table_fp16, stream);
+  if (rc) return rc;
+  return preprocess_backward_launch(P, surfels->means3D, surfels->scales, surfels->rotations,
+                                    gi->radii, settings->viewmatrix, settings->projmatrix, Wq, Hq,
+                                    accum, *go, stream);
+}
+
 int ns_read_device_status(void* geom, int32_t P, void* stream_) {
   cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_);
   if (!geom || P < 0) return NS_ERR_INVALID;

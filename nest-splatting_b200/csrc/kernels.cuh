@@ -30,6 +30,39 @@ struct RenderParams {
   float* cover_pixels;
   float* trans_avg;
 };
+struct BackwardParams {
+  int W, H;
+  int C, LD;
+  uint32_t L;
+  float S;
+  uint32_t Hres;
+  int align_corners;
+  uint32_t interp;
+  int contract;
+  float beta;
+  int Wq, Hq;                 // image size as the reference's preprocess backward recomputes it
+  const float* projmatrix;
+  const float* viewmatrix;
+  int ray_hit;                // 1: hit-point gradient in the ray/plane form (see backward.cu)
+  const uint2* ranges;
+  const uint32_t* point_list;
+  const SurfelRecord* records;
+  const void* table;
+  const int32_t* offsets;
+  const float* gridrange;
+  const float* final_T;
+  const uint32_t* n_contrib;
+  const float* dL_dcolor;
+  const float* dL_dothers;
+  float* dL_dtable;
+  float* accum;
+};
+size_t backward_accum_bytes(int64_t P);
+int blend_backward_launch(const BackwardParams& p, int fp16, cudaStream_t stream);
+int preprocess_backward_launch(int P, const float* means3D, const float* scales,
+                               const float* rotations, const int32_t* radii, const float* vm,
+                               const float* pm, int Wq, int Hq, const float* accum,
+                               const ns_raster_grads_out& o, cudaStream_t stream);
 int rvq_decode_launch(const uint8_t*, const float*, float*, int64_t, int, int, int, cudaStream_t);
 int preprocess_blocks(int P);
 int preprocess_block_size();

@@ -33,6 +33,7 @@
 //
 // The hash table is read as fp16 (or fp32) pairs through the read-only path;
 // at 16 levels x 2^19 x 2 fp16 it is 32 MB and stays resident in the 126 MB L2.
+#include "hashgrid.cuh"
 #include "kernels.cuh"
 
 namespace ns {
@@ -42,22 +43,7 @@ constexpr int kThreads = kTilePixels;  // 256: one pixel per thread
 constexpr int kQueue = 8;              // queued samples per pixel between drains
 constexpr int kWarps = kThreads / 32;
 constexpr int kChunk = 64;             // compacted samples looked up per warp step (2 per lane)
-constexpr int kAccStride = 32;         // floats per pixel row of the accumulators
 constexpr int kMaxChannels = 32;
-constexpr int kMaxLevels = 16;
-
-// Constants of one hash level (hashgrid.h:128-131 and the dense/hash choice of
-// get_grid_index, :22-40), computed with the device's exp2f as the reference does.
-struct LevelConst {
-  const void* base; // the level's first table row
-  float scale;
-  uint32_t row0;    // first table row of the level
-  uint32_t mask;    // hsize-1 for a power-of-two size, ~0 otherwise
-  uint32_t hsize;   // rows in the level
-  uint32_t s1, s2;  // dense strides of y and z
-  uint32_t dense;   // 1: dense index, 0: hashed
-  uint32_t modulo;  // 1: size not a power of two, use %
-};
 
 struct BlendSmem {
   float4 rec[kThreads][kRecordFloat4];  // surfel records of the current batch
@@ -68,67 +54,6 @@ struct BlendSmem {
   float4 res[kWarps][kChunk];           // lookups of the current chunk: level l (xy), l+1 (zw)
   float acc[kThreads * kAccStride];     // feature accumulators, see acc_pair()
   LevelConst lv[kMaxLevels];
-};
-
-// Channels (2l, 2l+1) of pixel p: float2 pair (l ^ (p & 15)) of the pixel's row,
-// so that threads reading one channel of consecutive pixels hit distinct banks.
-__device__ __forceinline__ float2* acc_pair(float* acc, int p, int l) {
-  return reinterpret_cast<float2*>(acc + p * kAccStride + 2 * (l ^ (p & 15)));
-}
-
-__device__ __forceinline__ uint32_t lane_mask_lt() {
-  uint32_t m;
-  asm("mov.u32 %0, %%lanemask_lt;" : "=r"(m));
-  return m;
-}
-
-template <typename TableT>
-__device__ LevelConst make_level(const RenderParams& p, int l) {
-  LevelConst lc{};
-  const uint32_t hsize = (uint32_t)(p.offsets[l + 1] - p.offsets[l]);
-  const float scale = exp2f(l * p.S) * p.Hres - 1.0f;
-  const uint32_t res = (uint32_t)ceilf(scale) + 1;
-  const uint32_t R = p.align_corners ? res : res + 1;
-  uint32_t stride = 1, s1 = 0, s2 = 0;
-  int used = 0;
-  for (int d = 0; d < 3 && stride <= hsize; d++) {
-    if (d == 1) s1 = stride;
-    if (d == 2) s2 = stride;
-    stride *= R;
-    used++;
-  }
-  lc.scale = scale;
-  lc.row0 = (uint32_t)p.offsets[l];
-  lc.base = static_cast<const TableT*>(p.table) + 2 * (size_t)lc.row0;  // LD = 2 per row
-  lc.hsize = hsize;
-  lc.dense = (stride <= hsize && used == 3) ? 1u : 0u;
-  lc.s1 = s1;
-  lc.s2 = s2;
-  // index % hashmap_size applies to dense levels too (with align_corners the
-  // top corner of a dense level can pass R^3 - 1).
-  const bool pow2 = hsize != 0 && (hsize & (hsize - 1)) == 0;
-  lc.mask = pow2 ? hsize - 1 : 0xffffffffu;
-  lc.modulo = pow2 ? 0u : 1u;
-  return lc;
-}
-
-template <typename TableT>
-struct Corner8;
-template <>
-struct Corner8<__half> {
-  __half2 v[8];
-  __device__ float2 get(int c) const { return __half22float2(v[c]); }
-  __device__ void load(const void* t, int c, uint32_t row) {
-    v[c] = __ldg(reinterpret_cast<const __half2*>(t) + row);
-  }
-};
-template <>
-struct Corner8<float> {
-  float2 v[8];
-  __device__ float2 get(int c) const { return v[c]; }
-  __device__ void load(const void* t, int c, uint32_t row) {
-    v[c] = __ldg(reinterpret_cast<const float2*>(t) + row);
-  }
 };
 
 // Trilinear lookup of one level at a point of [0,1]^3 (hashgrid.h:140-193),
@@ -149,26 +74,9 @@ __device__ __forceinline__ void lookup_issue(const LevelConst& lc, const void* t
     if (interp == 1) f[d] = f[d] * f[d] * (3.0f - 2.0f * f[d]);
   }
   uint32_t idx[8];
-  if (lc.dense) {
-    const uint32_t base = g[0] + g[1] * lc.s1 + g[2] * lc.s2;
+  corner_rows(lc, g, idx);
 #pragma unroll
-    for (int c = 0; c < 8; c++)
-      idx[c] = base + (c & 1) + ((c >> 1) & 1 ? lc.s1 : 0u) + ((c >> 2) & 1 ? lc.s2 : 0u);
-  } else {
-    // (x * 1) ^ (y * 2654435761) ^ (z * 805459861) with the (y, z) terms formed once.
-    const uint32_t hy0 = g[1] * 2654435761u, hy1 = (g[1] + 1) * 2654435761u;
-    const uint32_t hz0 = g[2] * 805459861u, hz1 = (g[2] + 1) * 805459861u;
-    const uint32_t hyz[4] = {hy0 ^ hz0, hy1 ^ hz0, hy0 ^ hz1, hy1 ^ hz1};
-#pragma unroll
-    for (int c = 0; c < 8; c++) idx[c] = (g[0] + (c & 1)) ^ hyz[c >> 1];
-  }
-  if (lc.modulo) {
-#pragma unroll
-    for (int c = 0; c < 8; c++) cv.load(lc.base, c, idx[c] % lc.hsize);
-  } else {
-#pragma unroll
-    for (int c = 0; c < 8; c++) cv.load(lc.base, c, idx[c] & lc.mask);
-  }
+  for (int c = 0; c < 8; c++) cv.load(lc.base, c, idx[c]);
 }
 
 // Corner weights ((wx * wy) * wz) and the weighted sum in packed fp32
@@ -205,7 +113,7 @@ __global__ void __launch_bounds__(kThreads, 2) blend_kernel(const RenderParams p
   const float half_shift = p.align_corners ? 0.0f : 0.5f;
   const uint32_t L = p.L;
 
-  if (t < (int)L) S.lv[t] = make_level<TableT>(p, t);
+  if (t < (int)L) S.lv[t] = make_level<TableT>(p.table, p.offsets, p.S, p.Hres, p.align_corners, t);
   for (int c = 0; c < kAccStride; c++) S.acc[t * kAccStride + c] = 0.f;  // only this thread's row
 
   const uint2 range = p.ranges[tile];

@@ -5,11 +5,17 @@ submodules/diff-surfel-rasterization/diff_surfel_rasterization/__init__.py of
 NilKel/nest-splatting (GaussianRasterizationSettings :277-293,
 HashGridSettings :295-302, GaussianRasterizer :304-396, rasterize_gaussians
 :21-66, _RasterizeGaussians :68-275, compute_relocation :398-414). The forward
-pass runs the sm_100a kernels of libnest_b200.so through its C-ABI; there is
-no CPU fallback. Built: render_mode 0 (baseline hash grid) with the Gaussian
-kernel (kernel_type 0) and level_dim 2. Other modes raise NotImplementedError
-instead of silently rendering nothing as the reference does for shapes it was
-not compiled for.
+and backward passes run the sm_100a kernels of libnest_b200.so through its
+C-ABI; there is no CPU fallback. Built: render_mode 0 (baseline hash grid) with
+the Gaussian kernel (kernel_type 0) and level_dim 2. Other modes raise
+NotImplementedError instead of silently rendering nothing as the reference does
+for shapes it was not compiled for.
+
+Backward (__init__.py:174-275 of the reference): the 21 gradients come back in
+argument order; means2D's slot carries the densification statistic and
+ap_level's slot dL_gradsum, homotrans gets None (its gradient is folded into
+means, scales and rotations), sh / colors_precomp get zeros (mode 0 never reads
+them).
 
 `features` may be fp32 (as the reference stores the table) or fp16 (read as
 fp16 pairs by the kernels, half the L2 traffic).
@@ -90,21 +96,53 @@ class _RasterizeGaussians(torch.autograd.Function):
             interpolation=int(hashgrid_settings.interpolation), channels=int(OS),
             level_dim=int(feats.shape[1]), table_fp16=feats.dtype == torch.float16)
         ap = _nonempty(ap_level)
-        num_rendered, color, others, radii, cover, trans, scratch = _raster.rasterize_forward(
-            cfg, means3D.contiguous().float(), scales.contiguous().float(), rotations.contiguous().float(),
-            opacities.contiguous().float().reshape(-1),
-            None if _nonempty(homotrans) is None else homotrans.contiguous().float().reshape(-1, 16),
-            None if ap is None else ap.contiguous().float().reshape(-1), feats,
-            offsets.contiguous().to(torch.int32), gridrange.contiguous().float())
-        ctx.raster_settings = raster_settings
-        ctx.hashgrid_settings = hashgrid_settings
+        args = (means3D.detach().contiguous().float(), scales.detach().contiguous().float(),
+                rotations.detach().contiguous().float(), opacities.detach().contiguous().float().reshape(-1),
+                None if _nonempty(homotrans) is None else homotrans.detach().contiguous().float().reshape(-1, 16),
+                None if ap is None else ap.detach().contiguous().float().reshape(-1), feats.detach(),
+                offsets.contiguous().to(torch.int32), gridrange.contiguous().float())
+        num_rendered, color, others, radii, cover, trans, scratch = _raster.rasterize_forward(cfg, *args)
+        ctx.cfg = cfg
+        ctx.args = args
+        ctx.radii = radii
         ctx.num_rendered = num_rendered
         ctx.scratch = scratch
+        ctx.shapes = dict(opacities=opacities.shape, ap_level=ap_level.shape, features=features.dtype,
+                          sh=sh.shape, colors_precomp=colors_precomp.shape)
+        ctx.mark_non_differentiable(radii)
         return color, radii, others, trans, cover
 
     @staticmethod
     def backward(ctx, grad_out_color, grad_radii, grad_depth, grad_0, grad_1):
-        raise NotImplementedError("the rasterizer backward pass is not built yet")
+        dev = ctx.radii.device
+        H, W = ctx.cfg.image_height, ctx.cfg.image_width
+        if grad_out_color is None:
+            grad_out_color = torch.zeros((ctx.cfg.channels, H, W), dtype=torch.float32, device=dev)
+        if grad_depth is None:
+            grad_depth = torch.zeros((_raster.OTHER_CHANNELS, H, W), dtype=torch.float32, device=dev)
+        g = _raster.rasterize_backward(ctx.cfg, *ctx.args, ctx.radii, ctx.num_rendered, ctx.scratch,
+                                       grad_out_color, grad_depth)
+        ctx.scratch = None
+        need = ctx.needs_input_grad
+        sh = ctx.shapes
+
+        def zeros_if(i, shape):
+            return torch.zeros(shape, dtype=torch.float32, device=dev) if need[i] else None
+
+        gradsum = g["gradsum"].reshape(sh["ap_level"]) if (need[9] and len(sh["ap_level"]) and
+                                                          sh["ap_level"][0] == g["gradsum"].shape[0]) else None
+        return (g["means3D"] if need[0] else None,
+                g["means2D"] if need[1] else None,
+                zeros_if(2, sh["sh"]),
+                zeros_if(3, sh["colors_precomp"]),
+                g["opacity"].reshape(sh["opacities"]) if need[4] else None,
+                g["scales"] if need[5] else None,
+                g["rotations"] if need[6] else None,
+                None,  # cov3Ds_precomp (not built)
+                None,  # homotrans: folded into means / scales / rotations
+                gradsum,
+                g["table"].to(sh["features"]) if need[10] else None,
+                None, None, None, None, None, None, None, None, None, None)
 
 
 class GaussianRasterizationSettings(NamedTuple):

@@ -23,7 +23,7 @@ EXPORTED = [
     "ns_geometry_scratch_bytes", "ns_image_scratch_bytes", "ns_binning_scratch_bytes",
     "ns_rasterize_forward", "ns_read_device_status", "ns_mark_visible", "ns_mlp_forward",
     "ns_rvq_decode", "ns_radix_sort_temp_bytes", "ns_radix_sort_pairs", "ns_render_frame",
-    "ns_radix_sort_pairs_noalloc",
+    "ns_radix_sort_pairs_noalloc", "ns_backward_scratch_bytes", "ns_rasterize_backward",
 ]
 
 
@@ -71,6 +71,18 @@ class FrameOutputs(C.Structure):
     _fields_ = [
         ("rgb", C.c_void_p), ("out_color", C.c_void_p), ("out_others", C.c_void_p),
         ("radii", C.c_void_p),
+    ]
+
+
+class GradsIn(C.Structure):
+    _fields_ = [("dL_dout_color", C.c_void_p), ("dL_dout_others", C.c_void_p), ("radii", C.c_void_p)]
+
+
+class GradsOut(C.Structure):
+    _fields_ = [
+        ("dL_dmeans3D", C.c_void_p), ("dL_dmean2D", C.c_void_p), ("dL_dopacity", C.c_void_p),
+        ("dL_dscales", C.c_void_p), ("dL_drots", C.c_void_p), ("dL_dtable", C.c_void_p),
+        ("table_rows", C.c_int64), ("dL_gradsum", C.c_void_p),
     ]
 
 
@@ -130,6 +142,11 @@ def load() -> C.CDLL:
     lib.ns_render_frame.argtypes = [C.POINTER(RasterSettings), C.POINTER(FrameInputs),
                                     C.POINTER(FrameOutputs), vp, sz, vp, sz, vp, sz,
                                     C.POINTER(C.c_int64), C.c_int, vp]
+    lib.ns_backward_scratch_bytes.restype = sz
+    lib.ns_backward_scratch_bytes.argtypes = [i32]
+    lib.ns_rasterize_backward.restype = C.c_int
+    lib.ns_rasterize_backward.argtypes = [C.POINTER(RasterSettings), C.POINTER(Surfels), C.POINTER(GradsIn),
+                                          C.POINTER(GradsOut), vp, sz, vp, sz, vp, sz, i64, vp, sz, vp]
     _lib = lib
     return lib
 

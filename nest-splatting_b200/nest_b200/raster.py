@@ -158,6 +158,56 @@ def rasterize_forward(cfg: RasterConfig, means3D, scales, rotations, opacities, 
     return int(n.value), out_color, out_others, radii, cover, trans, scratch
 
 
+def rasterize_backward(cfg: RasterConfig, means3D, scales, rotations, opacities, homotrans, ap_level, features,
+                       offsets, gridrange, radii, num_rendered: int, scratch: Scratch, dL_dcolor, dL_dothers,
+                       return_accumulators: bool = False):
+    """Backward rasterization (render_mode 0) through ns_rasterize_backward.
+
+    `scratch` and every input must be the ones of the forward call. Returns a dict
+    of fp32 gradients: means3D [P,3], means2D [P,3] (densification statistic),
+    opacity [P,1], scales [P,2], rotations [P,4], table [rows, level_dim],
+    gradsum [P,1]. With return_accumulators, also "accum": the render pass's
+    per-surfel accumulators [P,20] (dL/dM 9, dL/dT[0].z, dL/dT[1].z, dL/dmean2D 2,
+    dL/dnormal 3, opacity, gradsum, 2 unused), for tests.
+    """
+    lib = _lib.load()
+    dev = means3D.device
+    P = means3D.shape[0]
+    dL_dcolor = dL_dcolor.contiguous().float()
+    dL_dothers = dL_dothers.contiguous().float()
+    _require_cuda(means3D, scales, rotations, opacities, homotrans, ap_level, features, offsets, gridrange, radii,
+                  dL_dcolor, dL_dothers)
+    rows = int(features.shape[0])
+    g = dict(means3D=torch.empty((P, 3), dtype=torch.float32, device=dev),
+             means2D=torch.empty((P, 3), dtype=torch.float32, device=dev),
+             opacity=torch.empty((P, 1), dtype=torch.float32, device=dev),
+             scales=torch.empty((P, 2), dtype=torch.float32, device=dev),
+             rotations=torch.empty((P, 4), dtype=torch.float32, device=dev),
+             table=torch.empty((rows, int(cfg.level_dim)), dtype=torch.float32, device=dev),
+             gradsum=torch.empty((P, 1), dtype=torch.float32, device=dev))
+    if P == 0:
+        g["table"].zero_()
+        return g
+    settings = cfg.to_c()
+    surf = _lib.Surfels()
+    surf.P = P
+    surf.means3D, surf.scales, surf.rotations = ptr(means3D), ptr(scales), ptr(rotations)
+    surf.opacities, surf.homotrans, surf.ap_level = ptr(opacities), ptr(homotrans), ptr(ap_level)
+    surf.features, surf.offsets, surf.gridrange = ptr(features), ptr(offsets), ptr(gridrange)
+    gi = _lib.GradsIn(ptr(dL_dcolor), ptr(dL_dothers), ptr(radii))
+    go = _lib.GradsOut(ptr(g["means3D"]), ptr(g["means2D"]), ptr(g["opacity"]), ptr(g["scales"]),
+                       ptr(g["rotations"]), ptr(g["table"]), rows, ptr(g["gradsum"]))
+    acc = torch.empty(lib.ns_backward_scratch_bytes(P), dtype=torch.uint8, device=dev)
+    check("ns_rasterize_backward",
+          lib.ns_rasterize_backward(C.byref(settings), C.byref(surf), C.byref(gi), C.byref(go),
+                                    scratch.geom.data_ptr(), scratch.geom.numel(), scratch.binning.data_ptr(),
+                                    scratch.binning.numel(), scratch.image.data_ptr(), scratch.image.numel(),
+                                    int(num_rendered), acc.data_ptr(), acc.numel(), _lib.stream_handle(dev)))
+    if return_accumulators:
+        g["accum"] = acc[: P * 80].view(torch.float32).reshape(P, 20)
+    return g
+
+
 def mark_visible(means3D, viewmatrix, projmatrix) -> torch.Tensor:
     lib = _lib.load()
     _require_cuda(means3D, viewmatrix, projmatrix)

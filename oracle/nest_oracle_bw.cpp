@@ -19,9 +19,25 @@ using namespace oracle;
 
 namespace {
 
-inline void atomic_add(float* p, float v) {
+template <typename R>
+inline void atomic_add(R* p, R v) {
 #pragma omp atomic
   *p += v;
+}
+
+// 3-vector in the working precision R (float: the reference's arithmetic;
+// double: the same formulas without float cancellation, for conditioning checks).
+template <typename R>
+struct V3 {
+  R x, y, z;
+};
+template <typename R>
+inline V3<R> vsub(V3<R> a, V3<R> b) { return {a.x - b.x, a.y - b.y, a.z - b.z}; }
+template <typename R>
+inline V3<R> vscl(R f, V3<R> a) { return {f * a.x, f * a.y, f * a.z}; }
+template <typename R>
+inline V3<R> vcrs(V3<R> a, V3<R> b) {
+  return {a.y * b.z - a.z * b.y, a.z * b.x - a.x * b.z, a.x * b.y - a.y * b.x};
 }
 
 // hashgrid.h:53-299 with BW = true, D = 3: the forward lookup, the table
@@ -30,75 +46,77 @@ inline void atomic_add(float* p, float v) {
 // (:212-299). grad_scale is the box-map slope, or for contract the slope of the
 // inner region times the radial scale (the reference's approximation of the
 // contraction Jacobian, :66-97).
-void query_feature_bw(float* feat, int C, int LD, F3 xyz, float vmin, float vmax,
-                      const int* offsets, uint32_t ap_level, const float* table, uint32_t L,
-                      float S, uint32_t Hres, bool align_corners, uint32_t interp, bool contract,
-                      const float* grad_feat, float* dL_dtable, float dL_dxyz[3]) {
-  float in[3];
+template <typename R>
+void query_feature_bw(R* feat, int C, int LD, V3<R> xyz, R vmin, R vmax, const int* offsets,
+                      uint32_t ap_level, const float* table, uint32_t L, float S, uint32_t Hres,
+                      bool align_corners, uint32_t interp, bool contract, const R* grad_feat,
+                      R* dL_dtable, R dL_dxyz[3]) {
+  R in[3];
   bool oob = false;
-  float grad_scale = 0.0f;
+  R grad_scale = 0;
   if (!contract) {
-    float inv = 1.0f / (vmax - vmin);
+    R inv = R(1) / (vmax - vmin);
     in[0] = (xyz.x - vmin) * inv;
     in[1] = (xyz.y - vmin) * inv;
     in[2] = (xyz.z - vmin) * inv;
     grad_scale = inv;
     oob = in[0] < 0 || in[0] > 1 || in[1] < 0 || in[1] > 1 || in[2] < 0 || in[2] > 1;
   } else {
-    float vmid = (vmax + vmin) * 0.5f;
-    float inv = 1.0f / ((vmax - vmin) * 0.5f);
+    R vmid = (vmax + vmin) * R(0.5);
+    R inv = R(1) / ((vmax - vmin) * R(0.5));
     in[0] = (xyz.x - vmid) * inv;
     in[1] = (xyz.y - vmid) * inv;
     in[2] = (xyz.z - vmid) * inv;
-    float norm = std::sqrt(in[0] * in[0] + in[1] * in[1] + in[2] * in[2]);
-    float inv_norm = 1.0f / norm;
-    float st = (norm <= 1.0f) ? 1.0f : (2.0f - inv_norm) * inv_norm;
-    for (int d = 0; d < 3; d++) in[d] = (st * in[d] + 2.0f) * 0.25f;
-    grad_scale = inv * st * 0.25f;
+    R norm = std::sqrt(in[0] * in[0] + in[1] * in[1] + in[2] * in[2]);
+    R inv_norm = R(1) / norm;
+    R st = (norm <= R(1)) ? R(1) : (R(2) - inv_norm) * inv_norm;
+    for (int d = 0; d < 3; d++) in[d] = (st * in[d] + R(2)) * R(0.25);
+    grad_scale = inv * st * R(0.25);
   }
   const uint32_t max_level = std::min(ap_level, L);
-  for (int c = 0; c < C; c++) feat[c] = 0.f;
-  for (int d = 0; d < 3; d++) dL_dxyz[d] = 0.f;
+  for (int c = 0; c < C; c++) feat[c] = 0;
+  for (int d = 0; d < 3; d++) dL_dxyz[d] = 0;
   if (oob) return;
-  std::vector<float> dy_dx((size_t)3 * C, 0.f);
+  std::vector<R> dy_dx((size_t)3 * C, R(0));
   for (uint32_t lv = 0; lv < max_level; lv++) {
     const uint32_t hsize = (uint32_t)(offsets[lv + 1] - offsets[lv]);
-    const float scale = std::exp2(lv * S) * Hres - 1.0f;
-    const uint32_t res = (uint32_t)std::ceil(scale) + 1;
+    const float scale_f = std::exp2(lv * S) * Hres - 1.0f;  // the level scale as the reference forms it
+    const R scale = scale_f;
+    const uint32_t res = (uint32_t)std::ceil(scale_f) + 1;
     const float* grid = table + (size_t)(uint32_t)offsets[lv] * LD;
-    float* dgrid = dL_dtable + (size_t)(uint32_t)offsets[lv] * LD;
-    const float* gl = grad_feat + lv * LD;
-    float pos[3], deriv[3];
+    R* dgrid = dL_dtable + (size_t)(uint32_t)offsets[lv] * LD;
+    const R* gl = grad_feat + lv * LD;
+    R pos[3], deriv[3];
     uint32_t pg[3];
     for (int d = 0; d < 3; d++) {
-      pos[d] = in[d] * scale + (align_corners ? 0.0f : 0.5f);
+      pos[d] = in[d] * scale + (align_corners ? R(0) : R(0.5));
       pg[d] = (uint32_t)std::floor(pos[d]);
-      pos[d] -= (float)pg[d];
+      pos[d] -= (R)pg[d];
       if (interp == 1) {
-        deriv[d] = 6 * pos[d] * (1.0f - pos[d]);
-        pos[d] = pos[d] * pos[d] * (3.0f - 2.0f * pos[d]);
+        deriv[d] = 6 * pos[d] * (R(1) - pos[d]);
+        pos[d] = pos[d] * pos[d] * (R(3) - R(2) * pos[d]);
       } else {
-        deriv[d] = 1.0f;
+        deriv[d] = R(1);
       }
     }
-    float r[16] = {0};
+    R r[16] = {0};
     for (uint32_t c = 0; c < 8; c++) {
-      float w = 1;
+      R w = 1;
       uint32_t g[3];
       for (int d = 0; d < 3; d++) {
         if ((c & (1u << d)) == 0) { w *= 1 - pos[d]; g[d] = pg[d]; }
         else { w *= pos[d]; g[d] = pg[d] + 1; }
       }
       const uint32_t idx = grid_index(align_corners, hsize, res, g) * LD;
-      for (int ch = 0; ch < LD; ch++) r[ch] += w * grid[idx + ch];
-      for (int ch = 0; ch < LD; ch++) atomic_add(&dgrid[idx + ch], w * gl[ch]);
+      for (int ch = 0; ch < LD; ch++) r[ch] += w * (R)grid[idx + ch];
+      for (int ch = 0; ch < LD; ch++) atomic_add<R>(&dgrid[idx + ch], w * gl[ch]);
     }
     for (int ch = 0; ch < LD; ch++) feat[lv * LD + ch] = r[ch];
     // hashgrid.h:231-283: d feat / d in_gd from the 4 edges along axis gd.
     for (int gd = 0; gd < 3; gd++) {
-      float rg[16] = {0};
+      R rg[16] = {0};
       for (uint32_t e = 0; e < 4; e++) {
-        float w = scale * grad_scale;
+        R w = scale * grad_scale;
         uint32_t g[3];
         for (int nd = 0; nd < 2; nd++) {
           const int d = (nd >= gd) ? nd + 1 : nd;
@@ -109,14 +127,14 @@ void query_feature_bw(float* feat, int C, int LD, F3 xyz, float vmin, float vmax
         const uint32_t il = grid_index(align_corners, hsize, res, g) * LD;
         g[gd] = pg[gd] + 1;
         const uint32_t ir = grid_index(align_corners, hsize, res, g) * LD;
-        for (int ch = 0; ch < LD; ch++) rg[ch] += w * (grid[ir + ch] - grid[il + ch]) * deriv[gd];
+        for (int ch = 0; ch < LD; ch++) rg[ch] += w * ((R)grid[ir + ch] - (R)grid[il + ch]) * deriv[gd];
       }
       for (int ch = 0; ch < LD; ch++) dy_dx[(size_t)gd * C + lv * LD + ch] = rg[ch];
     }
   }
   // hashgrid.h:285-297
   for (int d = 0; d < 3; d++) {
-    float acc = 0;
+    R acc = 0;
     for (uint32_t lv = 0; lv < max_level; lv++)
       for (int ch = 0; ch < LD; ch++)
         acc += grad_feat[lv * LD + ch] * dy_dx[(size_t)d * C + lv * LD + ch];
@@ -125,13 +143,14 @@ void query_feature_bw(float* feat, int C, int LD, F3 xyz, float vmin, float vmax
 }
 
 // glm::dot of two 3-vectors: the products summed left to right.
-inline float dot3(F3 a, F3 b) { return a.x * b.x + a.y * b.y + a.z * b.z; }
-inline F3 add3(F3 a, F3 b) { return {a.x + b.x, a.y + b.y, a.z + b.z}; }
-inline F3 mul3(F3 a, F3 b) { return {a.x * b.x, a.y * b.y, a.z * b.z}; }
+template <typename R>
+inline R dot3(V3<R> a, V3<R> b) { return a.x * b.x + a.y * b.y + a.z * b.z; }
+template <typename R>
+inline V3<R> add3(V3<R> a, V3<R> b) { return {a.x + b.x, a.y + b.y, a.z + b.z}; }
+template <typename R>
+inline V3<R> mul3(V3<R> a, V3<R> b) { return {a.x * b.x, a.y * b.y, a.z * b.z}; }
 
-}  // namespace
 
-extern "C" {
 
 // backward.cu:445-2052, renderCUDAsurfelBackward<C> for render_mode 0,
 // kernel_type 0, level > 0, homotrans given. Per pixel, the tile list is walked
@@ -149,200 +168,200 @@ extern "C" {
 // Gradient outputs are accumulated (+=), as with the reference's zeroed
 // buffers: dL_dtable [rows, LD], dL_dtransMat [P,9], dL_dhomoMat [P,9],
 // dL_dmean2D [P,3], dL_dnormal [P,3], dL_dopacity [P], dL_gradsum [P].
-void oracle_render_backward(int W, int H, const uint32_t* ranges, const uint32_t* point_list,
-                            const float* means2D, const float* transMat,
-                            const float* normal_opacity, const float* homotrans,
-                            const float* ap_level, const float* table, const int* offsets,
-                            const float* gridrange, int C, int LD, uint32_t L, float S,
-                            uint32_t Hres, int align_corners, uint32_t interp, int contract,
-                            float beta, const float* final_T, const uint32_t* n_contrib,
-                            const float* dL_dout_color, const float* dL_dout_others,
-                            float* dL_dtable, float* dL_dtransMat, float* dL_dhomoMat,
-                            float* dL_dmean2D, float* dL_dnormal, float* dL_dopacity,
-                            float* dL_gradsum) {
+template <typename R>
+void render_backward(int W, int H, const uint32_t* ranges, const uint32_t* point_list,
+                     const float* means2D, const float* transMat, const float* normal_opacity,
+                     const float* homotrans, const float* ap_level, const float* table,
+                     const int* offsets, const float* gridrange, int C, int LD, uint32_t L, float S,
+                     uint32_t Hres, int align_corners, uint32_t interp, int contract, float beta,
+                     const float* final_T, const uint32_t* n_contrib, const float* dL_dout_color,
+                     const float* dL_dout_others, R* dL_dtable, R* dL_dtransMat, R* dL_dhomoMat,
+                     R* dL_dmean2D, R* dL_dnormal, R* dL_dopacity, R* dL_gradsum) {
+  using V = V3<R>;
   const int gx = (W + kBlock - 1) / kBlock, gy = (H + kBlock - 1) / kBlock;
   const size_t HW = (size_t)H * W;
-  const float vmin = gridrange[0], vmax = gridrange[1];
+  const R vmin = gridrange[0], vmax = gridrange[1];
 #pragma omp parallel for schedule(dynamic, 1)
   for (int tile = 0; tile < gx * gy; tile++) {
-    std::vector<float> dL_dpixel(C), accum_rec(C), last_color(C), grad_feat(C), feat(C);
+    std::vector<R> dL_dpixel(C), accum_rec(C), last_color(C), grad_feat(C), feat(C);
     const int tx = tile % gx, ty = tile / gx;
     const uint32_t r0 = ranges[2 * tile], r1 = ranges[2 * tile + 1];
     for (int py = ty * kBlock; py < std::min(H, (ty + 1) * kBlock); py++) {
       for (int px = tx * kBlock; px < std::min(W, (tx + 1) * kBlock); px++) {
         const size_t pid = (size_t)py * W + px;
-        const float pxf = (float)px, pyf = (float)py;
-        const float T_final = final_T[pid];
-        float T = T_final;
+        const R pxf = (R)px, pyf = (R)py;
+        const R T_final = final_T[pid];
+        R T = T_final;
         uint32_t contributor = r1 - r0;
         const uint32_t last_contributor = n_contrib[pid];
         const int median_contributor = (int)n_contrib[pid + HW];
-        const float dL_ddepth = dL_dout_others[0 * HW + pid];
-        const float dL_daccum = dL_dout_others[1 * HW + pid];
-        const float dL_dreg = dL_dout_others[6 * HW + pid];
-        float dL_dnormal2D[3];
+        const R dL_ddepth = dL_dout_others[0 * HW + pid];
+        const R dL_daccum = dL_dout_others[1 * HW + pid];
+        const R dL_dreg = dL_dout_others[6 * HW + pid];
+        R dL_dnormal2D[3];
         for (int i = 0; i < 3; i++) dL_dnormal2D[i] = dL_dout_others[(2 + i) * HW + pid];
-        const float dL_dmedian_depth = dL_dout_others[5 * HW + pid];
-        float last_depth = 0, last_normal[3] = {0, 0, 0};
-        float accum_depth_rec = 0, accum_alpha_rec = 0, accum_normal_rec[3] = {0, 0, 0};
-        const float final_D = final_T[pid + HW];
-        const float final_D2 = final_T[pid + 2 * HW];
-        const float final_A = 1 - T_final;
-        float last_dL_dT = 0;
+        const R dL_dmedian_depth = dL_dout_others[5 * HW + pid];
+        R last_depth = 0, last_normal[3] = {0, 0, 0};
+        R accum_depth_rec = 0, accum_alpha_rec = 0, accum_normal_rec[3] = {0, 0, 0};
+        const R final_D = final_T[pid + HW];
+        const R final_D2 = final_T[pid + 2 * HW];
+        const R final_A = 1 - T_final;
+        R last_dL_dT = 0;
         for (int c = 0; c < C; c++) {
           dL_dpixel[c] = dL_dout_color[c * HW + pid];
-          accum_rec[c] = 0.f;
-          last_color[c] = 0.f;
+          accum_rec[c] = 0;
+          last_color[c] = 0;
         }
-        float last_alpha = 0;
+        R last_alpha = 0;
         for (uint32_t k = r1; k-- > r0;) {
           contributor--;
           if (contributor >= last_contributor) continue;
           const uint32_t id = point_list[k];
           const float* Tm = transMat + 9 * (size_t)id;
-          const F3 Tu = {Tm[0], Tm[1], Tm[2]}, Tv = {Tm[3], Tm[4], Tm[5]}, Tw = {Tm[6], Tm[7], Tm[8]};
-          const F3 kk = sub(scl(pxf, Tw), Tu);
-          const F3 ll = sub(scl(pyf, Tw), Tv);
-          const F3 p = crs(kk, ll);
-          if (p.z == 0.0f) continue;
-          const float sx = p.x / p.z, sy = p.y / p.z;
-          const float rho3d = sx * sx + sy * sy;
-          const float dx = means2D[2 * id] - pxf, dy = means2D[2 * id + 1] - pyf;
-          const float rho2d = kFilterInvSquare * (dx * dx + dy * dy);
-          const float rho = std::min(rho3d, rho2d);
-          const float c_d = (rho3d <= rho2d) ? (sx * Tw.x + sy * Tw.y) + Tw.z : Tw.z;
-          if (c_d < kNear) continue;
+          const V Tu = {Tm[0], Tm[1], Tm[2]}, Tv = {Tm[3], Tm[4], Tm[5]}, Tw = {Tm[6], Tm[7], Tm[8]};
+          const V kk = vsub(vscl(pxf, Tw), Tu);
+          const V ll = vsub(vscl(pyf, Tw), Tv);
+          const V p = vcrs(kk, ll);
+          if (p.z == 0) continue;
+          const R sx = p.x / p.z, sy = p.y / p.z;
+          const R rho3d = sx * sx + sy * sy;
+          const R dx = (R)means2D[2 * id] - pxf, dy = (R)means2D[2 * id + 1] - pyf;
+          const R rho2d = R(kFilterInvSquare) * (dx * dx + dy * dy);
+          const R rho = std::min(rho3d, rho2d);
+          const R c_d = (rho3d <= rho2d) ? (sx * Tw.x + sy * Tw.y) + Tw.z : Tw.z;
+          if (c_d < R(kNear)) continue;
           const float* no = normal_opacity + 4 * (size_t)id;
-          const float normal[3] = {no[0], no[1], no[2]};
-          const float opa = no[3];
-          const float power = -0.5f * rho;
-          if (power > 0.0f) continue;
-          float G = std::exp(power);
-          float demon = 1.0f;
+          const R normal[3] = {no[0], no[1], no[2]};
+          const R opa = no[3];
+          const R power = R(-0.5) * rho;
+          if (power > 0) continue;
+          R G = std::exp(power);
+          R demon = 1;
           if (beta > 0.0) {
-            demon = (float)(1.0 + beta * G);
-            G = (float)((1.0 + beta) * G / demon);
+            demon = (R)(1.0 + beta * G);
+            G = (R)((1.0 + beta) * G / demon);
           }
-          const float alpha = std::min(0.99f, opa * G);
-          if (alpha < 1.0f / 255.0f) continue;
+          const R alpha = std::min(R(0.99f), opa * G);
+          if (alpha < R(1.0f / 255.0f)) continue;
 
-          T = T / (1.f - alpha);
-          const float dchannel_dcolor = alpha * T;
-          float dL_dalpha = 0.0f;
+          T = T / (R(1) - alpha);
+          const R dchannel_dcolor = alpha * T;
+          R dL_dalpha = 0;
 
           // Hit point and hash features (:934-980).
           const float* h = homotrans + 16 * (size_t)id;
-          const F3 sutu = {h[0], h[4], h[8]}, svtv = {h[1], h[5], h[9]}, pk = {h[3], h[7], h[11]};
-          F3 xyz;
+          const V sutu = {h[0], h[4], h[8]}, svtv = {h[1], h[5], h[9]}, pk = {h[3], h[7], h[11]};
+          V xyz;
           if (rho3d <= rho2d) {
             xyz = {sx * sutu.x + sy * svtv.x + pk.x, sx * sutu.y + sy * svtv.y + pk.y,
                    sx * sutu.z + sy * svtv.z + pk.z};
           } else {
             xyz = pk;
           }
-          float sum_grad = 0.0f;
+          R sum_grad = 0;
           for (int c = 0; c < C; c++) {
             grad_feat[c] = dchannel_dcolor * dL_dpixel[c];
             sum_grad += std::fabs(grad_feat[c]);
           }
-          atomic_add(&dL_gradsum[id], sum_grad);
+          atomic_add<R>(&dL_gradsum[id], sum_grad);
           const uint32_t apl = (uint32_t)std::floor(ap_level[id]);
-          float dL_dxyz[3];
-          query_feature_bw(feat.data(), C, LD, xyz, vmin, vmax, offsets, apl, table, L, S, Hres,
+          R dL_dxyz[3];
+          query_feature_bw<R>(feat.data(), C, LD, xyz, vmin, vmax, offsets, apl, table, L, S, Hres,
                            align_corners != 0, interp, contract != 0, grad_feat.data(), dL_dtable,
                            dL_dxyz);
           for (int c = 0; c < C; c++) {
-            accum_rec[c] = last_alpha * last_color[c] + (1.f - last_alpha) * accum_rec[c];
+            accum_rec[c] = last_alpha * last_color[c] + (R(1) - last_alpha) * accum_rec[c];
             last_color[c] = feat[c];
             dL_dalpha += (feat[c] - accum_rec[c]) * dL_dpixel[c];
           }
 
           // Auxiliary maps (:1799-1852).
-          float dL_dz = 0.0f;
-          float dL_dweight = 0;
-          const float m_d = kFar / (kFar - kNear) * (1 - kNear / c_d);
-          const float dmd_dd = (kFar * kNear) / ((kFar - kNear) * c_d * c_d);
+          R dL_dz = 0;
+          R dL_dweight = 0;
+          const R m_d = R(kFar) / (R(kFar) - R(kNear)) * (1 - R(kNear) / c_d);
+          const R dmd_dd = (R(kFar) * R(kNear)) / ((R(kFar) - R(kNear)) * c_d * c_d);
           if ((int)contributor == median_contributor - 1) dL_dz += dL_dmedian_depth;
           dL_dweight += (final_D2 + m_d * m_d * final_A - 2 * m_d * final_D) * dL_dreg;
           dL_dalpha += dL_dweight - last_dL_dT;
           last_dL_dT = dL_dweight * alpha + (1 - alpha) * last_dL_dT;
-          const float dL_dmd = 2.0f * (T * alpha) * (m_d * final_A - final_D) * dL_dreg;
+          const R dL_dmd = R(2) * (T * alpha) * (m_d * final_A - final_D) * dL_dreg;
           dL_dz += dL_dmd * dmd_dd;
-          accum_depth_rec = last_alpha * last_depth + (1.f - last_alpha) * accum_depth_rec;
+          accum_depth_rec = last_alpha * last_depth + (R(1) - last_alpha) * accum_depth_rec;
           last_depth = c_d;
           dL_dalpha += (c_d - accum_depth_rec) * dL_ddepth;
-          accum_alpha_rec = (float)(last_alpha * 1.0 + (1.f - last_alpha) * accum_alpha_rec);
+          accum_alpha_rec = (R)(last_alpha * 1.0 + (R(1) - last_alpha) * accum_alpha_rec);
           dL_dalpha += (1 - accum_alpha_rec) * dL_daccum;
           for (int c = 0; c < 3; c++) {
-            accum_normal_rec[c] = last_alpha * last_normal[c] + (1.f - last_alpha) * accum_normal_rec[c];
+            accum_normal_rec[c] = last_alpha * last_normal[c] + (R(1) - last_alpha) * accum_normal_rec[c];
             last_normal[c] = normal[c];
             dL_dalpha += (normal[c] - accum_normal_rec[c]) * dL_dnormal2D[c];
-            atomic_add(&dL_dnormal[id * 3 + c], alpha * T * dL_dnormal2D[c]);
+            atomic_add<R>(&dL_dnormal[id * 3 + c], alpha * T * dL_dnormal2D[c]);
           }
           dL_dalpha *= T;
           last_alpha = alpha;
 
-          float dL_dG = opa * dL_dalpha;
+          R dL_dG = opa * dL_dalpha;
           if (beta > 0.0) {
-            const float dG_dg = (float)((1.0 + beta) / (demon * demon));
+            const R dG_dg = (R)((1.0 + beta) / (demon * demon));
             dL_dG *= dG_dg;
           }
           dL_dz += alpha * T * dL_ddepth;
 
           // homotrans grads (:1921-1953).
-          float dL_du = 0.0f, dL_dv = 0.0f;
-          float* hm = dL_dhomoMat + (size_t)id * 9;
+          R dL_du = 0, dL_dv = 0;
+          R* hm = dL_dhomoMat + (size_t)id * 9;
           if (rho3d <= rho2d) {
             dL_du = dL_dxyz[0] * sutu.x + dL_dxyz[1] * sutu.y + dL_dxyz[2] * sutu.z;
             dL_dv = dL_dxyz[0] * svtv.x + dL_dxyz[1] * svtv.y + dL_dxyz[2] * svtv.z;
-            atomic_add(&hm[0], dL_dxyz[0] * sx);
-            atomic_add(&hm[1], dL_dxyz[1] * sx);
-            atomic_add(&hm[2], dL_dxyz[2] * sx);
-            atomic_add(&hm[3], dL_dxyz[0] * sy);
-            atomic_add(&hm[4], dL_dxyz[1] * sy);
-            atomic_add(&hm[5], dL_dxyz[2] * sy);
+            atomic_add<R>(&hm[0], dL_dxyz[0] * sx);
+            atomic_add<R>(&hm[1], dL_dxyz[1] * sx);
+            atomic_add<R>(&hm[2], dL_dxyz[2] * sx);
+            atomic_add<R>(&hm[3], dL_dxyz[0] * sy);
+            atomic_add<R>(&hm[4], dL_dxyz[1] * sy);
+            atomic_add<R>(&hm[5], dL_dxyz[2] * sy);
           }
-          atomic_add(&hm[6], dL_dxyz[0]);
-          atomic_add(&hm[7], dL_dxyz[1]);
-          atomic_add(&hm[8], dL_dxyz[2]);
+          atomic_add<R>(&hm[6], dL_dxyz[0]);
+          atomic_add<R>(&hm[7], dL_dxyz[1]);
+          atomic_add<R>(&hm[8], dL_dxyz[2]);
 
-          float* tm = dL_dtransMat + (size_t)id * 9;
+          R* tm = dL_dtransMat + (size_t)id * 9;
           if (rho3d <= rho2d) {
             // :1956-2017, Gaussian kernel: dG_factor = -G.
-            const float dG_factor = -G;
-            float dsx = dL_dG * dG_factor * sx + dL_dz * Tw.x;
-            float dsy = dL_dG * dG_factor * sy + dL_dz * Tw.y;
+            const R dG_factor = -G;
+            R dsx = dL_dG * dG_factor * sx + dL_dz * Tw.x;
+            R dsy = dL_dG * dG_factor * sy + dL_dz * Tw.y;
             dsx += dL_du;
             dsy += dL_dv;
-            const float dsx_pz = dsx / p.z;
-            const float dsy_pz = dsy / p.z;
-            const F3 dL_dp = {dsx_pz, dsy_pz, -(dsx_pz * sx + dsy_pz * sy)};
-            const F3 dL_dk = crs(ll, dL_dp);
-            const F3 dL_dl = crs(dL_dp, kk);
-            atomic_add(&tm[0], -dL_dk.x);
-            atomic_add(&tm[1], -dL_dk.y);
-            atomic_add(&tm[2], -dL_dk.z);
-            atomic_add(&tm[3], -dL_dl.x);
-            atomic_add(&tm[4], -dL_dl.y);
-            atomic_add(&tm[5], -dL_dl.z);
-            atomic_add(&tm[6], pxf * dL_dk.x + pyf * dL_dl.x + dL_dz * sx);
-            atomic_add(&tm[7], pxf * dL_dk.y + pyf * dL_dl.y + dL_dz * sy);
-            atomic_add(&tm[8], pxf * dL_dk.z + pyf * dL_dl.z + dL_dz * 1.0f);
+            const R dsx_pz = dsx / p.z;
+            const R dsy_pz = dsy / p.z;
+            const V dL_dp = {dsx_pz, dsy_pz, -(dsx_pz * sx + dsy_pz * sy)};
+            const V dL_dk = vcrs(ll, dL_dp);
+            const V dL_dl = vcrs(dL_dp, kk);
+            atomic_add<R>(&tm[0], -dL_dk.x);
+            atomic_add<R>(&tm[1], -dL_dk.y);
+            atomic_add<R>(&tm[2], -dL_dk.z);
+            atomic_add<R>(&tm[3], -dL_dl.x);
+            atomic_add<R>(&tm[4], -dL_dl.y);
+            atomic_add<R>(&tm[5], -dL_dl.z);
+            atomic_add<R>(&tm[6], pxf * dL_dk.x + pyf * dL_dl.x + dL_dz * sx);
+            atomic_add<R>(&tm[7], pxf * dL_dk.y + pyf * dL_dl.y + dL_dz * sy);
+            atomic_add<R>(&tm[8], pxf * dL_dk.z + pyf * dL_dl.z + dL_dz * R(1));
           } else {
             // :2018-2045
-            const float dG_factor_2d = -G * kFilterInvSquare;
-            const float dG_ddelx = dG_factor_2d * dx;
-            const float dG_ddely = dG_factor_2d * dy;
-            atomic_add(&dL_dmean2D[(size_t)id * 3 + 0], dL_dG * dG_ddelx);
-            atomic_add(&dL_dmean2D[(size_t)id * 3 + 1], dL_dG * dG_ddely);
-            atomic_add(&tm[8], dL_dz);
+            const R dG_factor_2d = -G * R(kFilterInvSquare);
+            const R dG_ddelx = dG_factor_2d * dx;
+            const R dG_ddely = dG_factor_2d * dy;
+            atomic_add<R>(&dL_dmean2D[(size_t)id * 3 + 0], dL_dG * dG_ddelx);
+            atomic_add<R>(&dL_dmean2D[(size_t)id * 3 + 1], dL_dG * dG_ddely);
+            atomic_add<R>(&tm[8], dL_dz);
           }
-          atomic_add(&dL_dopacity[id], G * dL_dalpha);
+          atomic_add<R>(&dL_dopacity[id], G * dL_dalpha);
         }
       }
     }
   }
 }
+
 
 // backward.cu:2216-2273 (preprocessCUDA, backward) and :2056-2214
 // (compute_transmat_aabb) for surfels with radii > 0, scales and rotations given.
@@ -355,13 +374,13 @@ void oracle_render_backward(int W, int H, const uint32_t* ranges, const uint32_t
 // In: dL_dmean2D [P,3] (render pass values; overwritten), dL_dnormal [P,3],
 // dL_dtransMat [P,9], dL_dhomoMat [P,9]. Out: dL_dmeans3D [P,3], dL_dscales
 // [P,2], dL_drots [P,4] (written only for radii > 0).
-void oracle_preprocess_backward(int P, const float* means3D, const float* scales,
-                                const float* rotations, const int* radii,
-                                const float* transMat, const float* viewmatrix, const float* projmatrix, int width,
-                                int height, float tanfovx, float tanfovy, float* dL_dmean2D,
-                                const float* dL_dnormal, const float* dL_dtransMat,
-                                const float* dL_dhomoMat, float* dL_dmeans3D, float* dL_dscales,
-                                float* dL_drots) {
+template <typename R>
+void preprocess_backward(int P, const float* means3D, const float* scales, const float* rotations,
+                         const int* radii, const float* transMat, const float* viewmatrix,
+                         const float* projmatrix, int width, int height, float tanfovx,
+                         float tanfovy, R* dL_dmean2D, const R* dL_dnormal, const R* dL_dtransMat,
+                         const R* dL_dhomoMat, R* dL_dmeans3D, R* dL_dscales, R* dL_drots) {
+  using V = V3<R>;
   const float focal_x = width / (2.0f * tanfovx);
   const float focal_y = height / (2.0f * tanfovy);
   const int W = int(focal_x * tanfovx * 2);
@@ -371,55 +390,63 @@ void oracle_preprocess_backward(int P, const float* means3D, const float* scales
 #pragma omp parallel for schedule(static)
   for (int i = 0; i < P; i++) {
     if (!(radii[i] > 0)) continue;
-    const F3 p = {means3D[3 * i], means3D[3 * i + 1], means3D[3 * i + 2]};
-    const float* q = rotations + 4 * i;
-    const float sx = scales[2 * i], sy = scales[2 * i + 1];
-    F3 R[3];
-    quat_to_cols(q, R);
-    const F3 L0 = scl(sx, R[0]), L1 = scl(sy, R[1]), L2 = R[2];
+    const V p = {means3D[3 * i], means3D[3 * i + 1], means3D[3 * i + 2]};
+    const float* qf = rotations + 4 * i;
+    const R q[4] = {qf[0], qf[1], qf[2], qf[3]};
+    const R sx = scales[2 * i], sy = scales[2 * i + 1];
+    // auxiliary.h:218-240 quat_to_rotmat (normalised), as three columns.
+    const R s = R(1) / std::sqrt(q[3] * q[3] + q[0] * q[0] + q[1] * q[1] + q[2] * q[2]);
+    const R w = q[0] * s, x = q[1] * s, y = q[2] * s, z = q[3] * s;
+    const V Rc[3] = {{R(1) - R(2) * (y * y + z * z), R(2) * (x * y + w * z), R(2) * (x * z - w * y)},
+                     {R(2) * (x * y - w * z), R(1) - R(2) * (x * x + z * z), R(2) * (y * z + w * x)},
+                     {R(2) * (x * z + w * y), R(2) * (y * z - w * x), R(1) - R(2) * (x * x + y * y)}};
+    const V L0 = vscl(sx, Rc[0]), L1 = vscl(sy, Rc[1]), L2 = Rc[2];
     // P = world2ndc * ndc2pix as glm mat3x4: column c, rows 0..3.
-    const float n[3][4] = {{float(W) / 2.0f, 0.f, 0.f, float(W - 1) / 2.0f},
-                           {0.f, float(H) / 2.0f, 0.f, float(H - 1) / 2.0f},
-                           {0.f, 0.f, 0.f, 1.f}};
-    float Pm[3][4];
+    const R n[3][4] = {{R(float(W) / 2.0f), 0, 0, R(float(W - 1) / 2.0f)},
+                       {0, R(float(H) / 2.0f), 0, R(float(H - 1) / 2.0f)},
+                       {0, 0, 0, 1}};
+    R Pm[3][4];
     for (int c = 0; c < 3; c++)
       for (int r = 0; r < 4; r++)
-        Pm[c][r] = ((pm[4 * r + 0] * n[c][0] + pm[4 * r + 1] * n[c][1]) + pm[4 * r + 2] * n[c][2]) +
-                   pm[4 * r + 3] * n[c][3];
+        Pm[c][r] = (((R)pm[4 * r + 0] * n[c][0] + (R)pm[4 * r + 1] * n[c][1]) + (R)pm[4 * r + 2] * n[c][2]) +
+                   (R)pm[4 * r + 3] * n[c][3];
     // T = transpose(M) * P, M columns (L0,0), (L1,0), (p,1); T[c][i] = M[i] . P[c].
-    const float Mc[3][4] = {{L0.x, L0.y, L0.z, 0.f}, {L1.x, L1.y, L1.z, 0.f}, {p.x, p.y, p.z, 1.f}};
-    F3 T[3];
+    const R Mc[3][4] = {{L0.x, L0.y, L0.z, 0}, {L1.x, L1.y, L1.z, 0}, {p.x, p.y, p.z, 1}};
+    V T[3];
     for (int c = 0; c < 3; c++) {
-      float t[3];
+      R t[3];
       for (int r = 0; r < 3; r++)
         t[r] = ((Mc[r][0] * Pm[c][0] + Mc[r][1] * Pm[c][1]) + Mc[r][2] * Pm[c][2]) + Mc[r][3] * Pm[c][3];
       T[c] = {t[0], t[1], t[2]};
     }
-    const F3 normal = xform_vec4x3(L2, vm);
+    // auxiliary.h:105-113 transformVec4x3
+    const V normal = {(R)vm[0] * L2.x + (R)vm[4] * L2.y + (R)vm[8] * L2.z,
+                      (R)vm[1] * L2.x + (R)vm[5] * L2.y + (R)vm[9] * L2.z,
+                      (R)vm[2] * L2.x + (R)vm[6] * L2.y + (R)vm[10] * L2.z};
 
-    F3 dT[3];
+    V dT[3];
     for (int c = 0; c < 3; c++)
       dT[c] = {dL_dtransMat[9 * i + 3 * c], dL_dtransMat[9 * i + 3 * c + 1], dL_dtransMat[9 * i + 3 * c + 2]};
-    const float gmx = dL_dmean2D[3 * i], gmy = dL_dmean2D[3 * i + 1];
+    const R gmx = dL_dmean2D[3 * i], gmy = dL_dmean2D[3 * i + 1];
     if (gmx != 0 || gmy != 0) {
-      const F3 t_vec = {9.0f, 9.0f, -1.0f};
-      const float d = dot3(t_vec, mul3(T[2], T[2]));
-      const F3 f_vec = scl(1.0f / d, t_vec);
-      const F3 dT0 = mul3(scl(gmx, f_vec), T[2]);
-      const F3 dT1 = mul3(scl(gmy, f_vec), T[2]);
-      F3 dT3 = add3(mul3(scl(gmx, f_vec), T[0]), mul3(scl(gmy, f_vec), T[1]));
-      const F3 dL_df = add3(mul3(scl(gmx, T[0]), T[2]), mul3(scl(gmy, T[1]), T[2]));
-      const float dL_dd = (float)(dot3(dL_df, f_vec) * (-1.0 / d));
-      const F3 dd_dT3 = scl(2.0f, mul3(t_vec, T[2]));
-      dT3 = add3(dT3, scl(dL_dd, dd_dT3));
+      const V t_vec = {9, 9, -1};
+      const R d = dot3(t_vec, mul3(T[2], T[2]));
+      const V f_vec = vscl(R(1) / d, t_vec);
+      const V dT0 = mul3(vscl(gmx, f_vec), T[2]);
+      const V dT1 = mul3(vscl(gmy, f_vec), T[2]);
+      V dT3 = add3(mul3(vscl(gmx, f_vec), T[0]), mul3(vscl(gmy, f_vec), T[1]));
+      const V dL_df = add3(mul3(vscl(gmx, T[0]), T[2]), mul3(vscl(gmy, T[1]), T[2]));
+      const R dL_dd = (R)(dot3(dL_df, f_vec) * (-1.0 / d));
+      const V dd_dT3 = vscl(R(2), mul3(t_vec, T[2]));
+      dT3 = add3(dT3, vscl(dL_dd, dd_dT3));
       dT[0] = add3(dT[0], dT0);
       dT[1] = add3(dT[1], dT1);
       dT[2] = add3(dT[2], dT3);
     }
     // dL_dM = P * transpose(dL_dT) + dL_dhomo: column c = sum_k P[k] dL_dT[k][c].
-    float dM[3][4];
+    R dM[3][4];
     for (int c = 0; c < 3; c++) {
-      const float g[3] = {(&dT[0].x)[c], (&dT[1].x)[c], (&dT[2].x)[c]};
+      const R g[3] = {(&dT[0].x)[c], (&dT[1].x)[c], (&dT[2].x)[c]};
       for (int r = 0; r < 4; r++)
         dM[c][r] = (Pm[0][r] * g[0] + Pm[1][r] * g[1]) + Pm[2][r] * g[2];
     }
@@ -428,47 +455,117 @@ void oracle_preprocess_backward(int P, const float* means3D, const float* scales
 
     // Normal: normalisation backprop as written at :2177-2190, view transform
     // transposed, and the camera-facing flip (DUAL_VISIABLE, :2194-2199).
-    const F3 gn = {dL_dnormal[3 * i], dL_dnormal[3 * i + 1], dL_dnormal[3 * i + 2]};
-    const float nlen = std::sqrt(normal.x * normal.x + normal.y * normal.y + normal.z * normal.z);
-    F3 gu = {0.f, 0.f, 0.f};
-    if (nlen > 1e-7f) {
-      const float dgn = gn.x * normal.x + gn.y * normal.y + gn.z * normal.z;
+    const V gn = {dL_dnormal[3 * i], dL_dnormal[3 * i + 1], dL_dnormal[3 * i + 2]};
+    const R nlen = std::sqrt(normal.x * normal.x + normal.y * normal.y + normal.z * normal.z);
+    V gu = {0, 0, 0};
+    if (nlen > R(1e-7f)) {
+      const R dgn = gn.x * normal.x + gn.y * normal.y + gn.z * normal.z;
       gu.x = (gn.x - dgn * normal.x / nlen) / nlen;
       gu.y = (gn.y - dgn * normal.y / nlen) / nlen;
       gu.z = (gn.z - dgn * normal.z / nlen) / nlen;
     }
-    F3 dtn = {vm[0] * gu.x + vm[1] * gu.y + vm[2] * gu.z, vm[4] * gu.x + vm[5] * gu.y + vm[6] * gu.z,
-              vm[8] * gu.x + vm[9] * gu.y + vm[10] * gu.z};
-    const F3 pv = xform_point4x3(p, vm);
-    const float cosv = -((pv.x * normal.x + pv.y * normal.y) + pv.z * normal.z);
-    const float mult = cosv > 0 ? 1.f : -1.f;
-    dtn = scl(mult, dtn);
+    V dtn = {(R)vm[0] * gu.x + (R)vm[1] * gu.y + (R)vm[2] * gu.z,
+             (R)vm[4] * gu.x + (R)vm[5] * gu.y + (R)vm[6] * gu.z,
+             (R)vm[8] * gu.x + (R)vm[9] * gu.y + (R)vm[10] * gu.z};
+    // auxiliary.h:84-92 transformPoint4x3
+    const V pv = {(R)vm[0] * p.x + (R)vm[4] * p.y + (R)vm[8] * p.z + (R)vm[12],
+                  (R)vm[1] * p.x + (R)vm[5] * p.y + (R)vm[9] * p.z + (R)vm[13],
+                  (R)vm[2] * p.x + (R)vm[6] * p.y + (R)vm[10] * p.z + (R)vm[14]};
+    const R cosv = -((pv.x * normal.x + pv.y * normal.y) + pv.z * normal.z);
+    const R mult = cosv > 0 ? R(1) : R(-1);
+    dtn = vscl(mult, dtn);
 
-    const F3 dRS0 = {dM[0][0], dM[0][1], dM[0][2]}, dRS1 = {dM[1][0], dM[1][1], dM[1][2]};
-    const F3 dR0 = scl(sx, dRS0), dR1 = scl(sy, dRS1), dR2 = dtn;
+    const V dRS0 = {dM[0][0], dM[0][1], dM[0][2]}, dRS1 = {dM[1][0], dM[1][1], dM[1][2]};
+    const V dR0 = vscl(sx, dRS0), dR1 = vscl(sy, dRS1), dR2 = dtn;
     // auxiliary.h:243-287 quat_to_rotmat_vjp; v_R[c][r] = column c, row r.
-    const float s = 1.0f / std::sqrt(q[3] * q[3] + q[0] * q[0] + q[1] * q[1] + q[2] * q[2]);
-    const float w = q[0] * s, x = q[1] * s, y = q[2] * s, z = q[3] * s;
-    const float v[3][3] = {{dR0.x, dR0.y, dR0.z}, {dR1.x, dR1.y, dR1.z}, {dR2.x, dR2.y, dR2.z}};
-    float* dq = dL_drots + 4 * i;
-    dq[0] = 2.f * (x * (v[1][2] - v[2][1]) + y * (v[2][0] - v[0][2]) + z * (v[0][1] - v[1][0]));
-    dq[1] = 2.f * (-2.f * x * (v[1][1] + v[2][2]) + y * (v[0][1] + v[1][0]) +
-                   z * (v[0][2] + v[2][0]) + w * (v[1][2] - v[2][1]));
-    dq[2] = 2.f * (x * (v[0][1] + v[1][0]) - 2.f * y * (v[0][0] + v[2][2]) +
-                   z * (v[1][2] + v[2][1]) + w * (v[2][0] - v[0][2]));
-    dq[3] = 2.f * (x * (v[0][2] + v[2][0]) + y * (v[1][2] + v[2][1]) -
-                   2.f * z * (v[0][0] + v[1][1]) + w * (v[0][1] - v[1][0]));
-    dL_dscales[2 * i] = dot3(dRS0, R[0]);
-    dL_dscales[2 * i + 1] = dot3(dRS1, R[1]);
+    const R v[3][3] = {{dR0.x, dR0.y, dR0.z}, {dR1.x, dR1.y, dR1.z}, {dR2.x, dR2.y, dR2.z}};
+    R* dq = dL_drots + 4 * i;
+    dq[0] = R(2) * (x * (v[1][2] - v[2][1]) + y * (v[2][0] - v[0][2]) + z * (v[0][1] - v[1][0]));
+    dq[1] = R(2) * (R(-2) * x * (v[1][1] + v[2][2]) + y * (v[0][1] + v[1][0]) +
+                    z * (v[0][2] + v[2][0]) + w * (v[1][2] - v[2][1]));
+    dq[2] = R(2) * (x * (v[0][1] + v[1][0]) - R(2) * y * (v[0][0] + v[2][2]) +
+                    z * (v[1][2] + v[2][1]) + w * (v[2][0] - v[0][2]));
+    dq[3] = R(2) * (x * (v[0][2] + v[2][0]) + y * (v[1][2] + v[2][1]) -
+                    R(2) * z * (v[0][0] + v[1][1]) + w * (v[0][1] - v[1][0]));
+    dL_dscales[2 * i] = dot3(dRS0, Rc[0]);
+    dL_dscales[2 * i + 1] = dot3(dRS1, Rc[1]);
     dL_dmeans3D[3 * i] = dM[2][0];
     dL_dmeans3D[3 * i + 1] = dM[2][1];
     dL_dmeans3D[3 * i + 2] = dM[2][2];
 
     // Densification statistic (:2268-2272), depth = Tw.z of the forward transform.
-    const float depth = transMat[9 * i + 8];
-    dL_dmean2D[3 * i] = (float)((double)(dL_dtransMat[9 * i + 2] * depth) * 0.5 * (double)(float)W);
-    dL_dmean2D[3 * i + 1] = (float)((double)(dL_dtransMat[9 * i + 5] * depth) * 0.5 * (double)(float)H);
+    const R depth = transMat[9 * i + 8];
+    dL_dmean2D[3 * i] = (R)((double)(dL_dtransMat[9 * i + 2] * depth) * 0.5 * (double)(float)W);
+    dL_dmean2D[3 * i + 1] = (R)((double)(dL_dtransMat[9 * i + 5] * depth) * 0.5 * (double)(float)H);
   }
+}
+
+}  // namespace
+
+extern "C" {
+
+// Working precision float: the reference's arithmetic, the parity checker.
+void oracle_render_backward(int W, int H, const uint32_t* ranges, const uint32_t* point_list,
+                            const float* means2D, const float* transMat,
+                            const float* normal_opacity, const float* homotrans,
+                            const float* ap_level, const float* table, const int* offsets,
+                            const float* gridrange, int C, int LD, uint32_t L, float S,
+                            uint32_t Hres, int align_corners, uint32_t interp, int contract,
+                            float beta, const float* final_T, const uint32_t* n_contrib,
+                            const float* dL_dout_color, const float* dL_dout_others,
+                            float* dL_dtable, float* dL_dtransMat, float* dL_dhomoMat,
+                            float* dL_dmean2D, float* dL_dnormal, float* dL_dopacity,
+                            float* dL_gradsum) {
+  render_backward<float>(W, H, ranges, point_list, means2D, transMat, normal_opacity, homotrans,
+                         ap_level, table, offsets, gridrange, C, LD, L, S, Hres, align_corners,
+                         interp, contract, beta, final_T, n_contrib, dL_dout_color, dL_dout_others,
+                         dL_dtable, dL_dtransMat, dL_dhomoMat, dL_dmean2D, dL_dnormal, dL_dopacity,
+                         dL_gradsum);
+}
+
+// Working precision double: the same formulas and decisions, without float
+// rounding; measures how far any float32 evaluation (the reference's, this
+// file's float instance, the CUDA kernels) sits from its exact value.
+void oracle_render_backward_f64(int W, int H, const uint32_t* ranges, const uint32_t* point_list,
+                                const float* means2D, const float* transMat,
+                                const float* normal_opacity, const float* homotrans,
+                                const float* ap_level, const float* table, const int* offsets,
+                                const float* gridrange, int C, int LD, uint32_t L, float S,
+                                uint32_t Hres, int align_corners, uint32_t interp, int contract,
+                                float beta, const float* final_T, const uint32_t* n_contrib,
+                                const float* dL_dout_color, const float* dL_dout_others,
+                                double* dL_dtable, double* dL_dtransMat, double* dL_dhomoMat,
+                                double* dL_dmean2D, double* dL_dnormal, double* dL_dopacity,
+                                double* dL_gradsum) {
+  render_backward<double>(W, H, ranges, point_list, means2D, transMat, normal_opacity, homotrans,
+                          ap_level, table, offsets, gridrange, C, LD, L, S, Hres, align_corners,
+                          interp, contract, beta, final_T, n_contrib, dL_dout_color,
+                          dL_dout_others, dL_dtable, dL_dtransMat, dL_dhomoMat, dL_dmean2D,
+                          dL_dnormal, dL_dopacity, dL_gradsum);
+}
+
+void oracle_preprocess_backward(int P, const float* means3D, const float* scales,
+                                const float* rotations, const int* radii, const float* transMat,
+                                const float* viewmatrix, const float* projmatrix, int width,
+                                int height, float tanfovx, float tanfovy, float* dL_dmean2D,
+                                const float* dL_dnormal, const float* dL_dtransMat,
+                                const float* dL_dhomoMat, float* dL_dmeans3D, float* dL_dscales,
+                                float* dL_drots) {
+  preprocess_backward<float>(P, means3D, scales, rotations, radii, transMat, viewmatrix, projmatrix,
+                             width, height, tanfovx, tanfovy, dL_dmean2D, dL_dnormal, dL_dtransMat,
+                             dL_dhomoMat, dL_dmeans3D, dL_dscales, dL_drots);
+}
+
+void oracle_preprocess_backward_f64(int P, const float* means3D, const float* scales,
+                                    const float* rotations, const int* radii,
+                                    const float* transMat, const float* viewmatrix,
+                                    const float* projmatrix, int width, int height, float tanfovx,
+                                    float tanfovy, double* dL_dmean2D, const double* dL_dnormal,
+                                    const double* dL_dtransMat, const double* dL_dhomoMat,
+                                    double* dL_dmeans3D, double* dL_dscales, double* dL_drots) {
+  preprocess_backward<double>(P, means3D, scales, rotations, radii, transMat, viewmatrix,
+                              projmatrix, width, height, tanfovx, tanfovy, dL_dmean2D, dL_dnormal,
+                              dL_dtransMat, dL_dhomoMat, dL_dmeans3D, dL_dscales, dL_drots);
 }
 
 }  // extern "C"

@@ -62,6 +62,8 @@ def load() -> C.CDLL:
                                            u32, i32, u32, i32, f32, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp]
     lib.oracle_preprocess_backward.argtypes = [i32, vp, vp, vp, vp, vp, vp, vp, i32, i32, f32, f32, vp, vp, vp,
                                                vp, vp, vp, vp]
+    lib.oracle_render_backward_f64.argtypes = lib.oracle_render_backward.argtypes
+    lib.oracle_preprocess_backward_f64.argtypes = lib.oracle_preprocess_backward.argtypes
     _lib = lib
     return lib
 
@@ -216,22 +218,25 @@ def forward(means3D, scales, rotations, opacities, homotrans, ap_level, table_f3
 
 
 def render_backward(pre, vals, ranges, fwd, homotrans, ap_level, table_f32, offsets, gridrange, W, H, C_out, LD,
-                    L, S, Hres, dL_dcolor, dL_dothers, align_corners=False, interp=0, contract=False, beta=0.0):
+                    L, S, Hres, dL_dcolor, dL_dothers, align_corners=False, interp=0, contract=False, beta=0.0,
+                    f64=False):
     """renderCUDAsurfelBackward<C> mode 0 restated (nest_oracle_bw.cpp). `fwd` is the
-    dict returned by render(). Returns the render-pass gradients (reference layouts)."""
+    dict returned by render(). Returns the render-pass gradients (reference layouts).
+    f64=True evaluates the same formulas in double (float64 outputs)."""
     lib = load()
     P = pre["radii"].shape[0]
     table = _f32(table_f32)
-    g = dict(dL_dtable=np.zeros_like(table), dL_dtransMat=np.zeros((P, 9), np.float32),
-             dL_dhomoMat=np.zeros((P, 9), np.float32), dL_dmean2D=np.zeros((P, 3), np.float32),
-             dL_dnormal=np.zeros((P, 3), np.float32), dL_dopacity=np.zeros(P, np.float32),
-             dL_gradsum=np.zeros(P, np.float32))
+    dt = np.float64 if f64 else np.float32
+    g = dict(dL_dtable=np.zeros(table.shape, dt), dL_dtransMat=np.zeros((P, 9), dt),
+             dL_dhomoMat=np.zeros((P, 9), dt), dL_dmean2D=np.zeros((P, 3), dt),
+             dL_dnormal=np.zeros((P, 3), dt), dL_dopacity=np.zeros(P, dt), dL_gradsum=np.zeros(P, dt))
     homotrans = _f32(homotrans).reshape(-1, 16)
     ap = _f32(ap_level).reshape(-1) if ap_level is not None else np.full(P, 1e9, np.float32)
     offs = np.ascontiguousarray(np.asarray(offsets, dtype=np.int32))
     gc, go = _f32(dL_dcolor), _f32(dL_dothers)
     assert gc.shape == (C_out, H, W) and go.shape == (14, H, W)
-    lib.oracle_render_backward(int(W), int(H), _p(np.ascontiguousarray(ranges, np.uint32)),
+    fn = lib.oracle_render_backward_f64 if f64 else lib.oracle_render_backward
+    fn(int(W), int(H), _p(np.ascontiguousarray(ranges, np.uint32)),
                                _p(np.ascontiguousarray(vals, np.uint32)), _p(pre["means2D"]), _p(pre["transMat"]),
                                _p(pre["normal_opacity"]), _p(homotrans), _p(ap), _p(table), _p(offs),
                                _p(_f32(gridrange).reshape(2)), int(C_out), int(LD), int(L), float(S), int(Hres),
@@ -242,7 +247,8 @@ def render_backward(pre, vals, ranges, fwd, homotrans, ap_level, table_f32, offs
     return g
 
 
-def preprocess_backward(means3D, scales, rotations, pre, g, viewmatrix, projmatrix, W, H, tanfovx, tanfovy):
+def preprocess_backward(means3D, scales, rotations, pre, g, viewmatrix, projmatrix, W, H, tanfovx, tanfovy,
+                        f64=False):
     """preprocessCUDA backward + compute_transmat_aabb restated. Consumes the
     render-pass gradients `g` (from render_backward) and returns
     dL_dmeans3D [P,3], dL_dscales [P,2], dL_drots [P,4] and the densification
@@ -250,14 +256,15 @@ def preprocess_backward(means3D, scales, rotations, pre, g, viewmatrix, projmatr
     lib = load()
     means3D, scales, rotations = _f32(means3D), _f32(scales), _f32(rotations)
     P = means3D.shape[0]
-    out = dict(dL_dmeans3D=np.zeros((P, 3), np.float32), dL_dscales=np.zeros((P, 2), np.float32),
-               dL_drots=np.zeros((P, 4), np.float32), dL_dmean2D=np.array(g["dL_dmean2D"], np.float32, copy=True))
-    lib.oracle_preprocess_backward(P, _p(means3D), _p(scales), _p(rotations), _p(pre["radii"]),
-                                   _p(pre["transMat"]), _p(_f32(viewmatrix).reshape(16)),
-                                   _p(_f32(projmatrix).reshape(16)), int(W), int(H), float(tanfovx),
-                                   float(tanfovy), _p(out["dL_dmean2D"]), _p(_f32(g["dL_dnormal"])),
-                                   _p(_f32(g["dL_dtransMat"])), _p(_f32(g["dL_dhomoMat"])), _p(out["dL_dmeans3D"]),
-                                   _p(out["dL_dscales"]), _p(out["dL_drots"]))
+    dt = np.float64 if f64 else np.float32
+    cast = lambda a: np.ascontiguousarray(np.asarray(a, dtype=dt))  # noqa: E731
+    out = dict(dL_dmeans3D=np.zeros((P, 3), dt), dL_dscales=np.zeros((P, 2), dt),
+               dL_drots=np.zeros((P, 4), dt), dL_dmean2D=np.array(g["dL_dmean2D"], dt, copy=True))
+    fn = lib.oracle_preprocess_backward_f64 if f64 else lib.oracle_preprocess_backward
+    fn(P, _p(means3D), _p(scales), _p(rotations), _p(pre["radii"]), _p(pre["transMat"]),
+       _p(_f32(viewmatrix).reshape(16)), _p(_f32(projmatrix).reshape(16)), int(W), int(H), float(tanfovx),
+       float(tanfovy), _p(out["dL_dmean2D"]), _p(cast(g["dL_dnormal"])), _p(cast(g["dL_dtransMat"])),
+       _p(cast(g["dL_dhomoMat"])), _p(out["dL_dmeans3D"]), _p(out["dL_dscales"]), _p(out["dL_drots"]))
     return out
 
 

@@ -43,7 +43,8 @@ def test_every_declared_symbol_is_exported():
 def test_struct_layout_matches_header():
     structs = {"ns_raster_settings": _lib.RasterSettings, "ns_surfels": _lib.Surfels,
                "ns_raster_outputs": _lib.RasterOutputs, "ns_frame_inputs": _lib.FrameInputs,
-               "ns_frame_outputs": _lib.FrameOutputs}
+               "ns_frame_outputs": _lib.FrameOutputs, "ns_raster_grads_in": _lib.GradsIn,
+               "ns_raster_grads_out": _lib.GradsOut}
     lines = ['#include <stdio.h>', '#include <stddef.h>', '#include "nest_b200.h"', 'int main(void) {']
     for cname, py in structs.items():
         lines.append(f'printf("{cname} %zu\\n", sizeof({cname}));')
@@ -72,6 +73,7 @@ def test_status_strings_and_scratch_sizes():
     a, b = lib.ns_binning_scratch_bytes(1000), lib.ns_binning_scratch_bytes(100000)
     assert b > a >= 1000 * 36
     assert lib.ns_radix_sort_temp_bytes(1 << 20) > 0
+    assert lib.ns_backward_scratch_bytes(1000) >= 1000 * 18 * 4
 
 
 def test_invalid_arguments_return_status_without_launching():
@@ -90,6 +92,14 @@ def test_invalid_arguments_return_status_without_launching():
     s.levels, s.level_dim, s.channels = 16, 2, 16  # 16 levels x 2 > 16 channels
     assert lib.ns_rasterize_forward(C.byref(s), None, None, None, 0, None, 0, None, 0, None, 0, None) == \
         _lib.NS_ERR_INVALID
+    assert lib.ns_rasterize_backward(C.byref(s), None, None, None, None, 0, None, 0, None, 0, 0, None, 0,
+                                     None) == _lib.NS_ERR_INVALID
+    s.channels = 32
+    surf = _lib.Surfels()
+    surf.P = 10
+    gi, go = _lib.GradsIn(), _lib.GradsOut()  # null gradient buffers
+    assert lib.ns_rasterize_backward(C.byref(s), C.byref(surf), C.byref(gi), C.byref(go), None, 0, None, 0,
+                                     None, 0, 0, None, 0, None) == _lib.NS_ERR_INVALID
 
 
 def test_python_api_surface_matches_reference():

@@ -1,0 +1,285 @@
+"""GPU parity of the rasterizer backward (ns_rasterize_backward through the
+torch wrapper and through the drop-in autograd Function) against the CPU
+oracle's restatement of the reference backward (itself pinned to float64
+autograd in test_oracle_backward.py).
+
+Tolerance: every gradient within 1e-3 relative L2 of the
+oracle. Where the reference's formulas are ill-conditioned in float32 that
+bar cannot be met by any float32 evaluation, the reference's included: with a
+hash table of large entries the hit-point term of the mean / rotation
+gradients is the small difference of two large per-sample terms (the
+homotrans term and the same motion through the splat coordinates), and the
+float32 oracle itself sits 3-5% from its own double-precision evaluation
+(measured: table U(-1,1), 16 levels up to resolution 4096). There the test
+asks the CUDA gradient to be as close to the double-precision value of the
+same formulas as the float32 reference arithmetic is (within 2x), and 1e-3
+otherwise. With the benchmark's table (U(-1e-4, 1e-4)) every gradient
+meets 1e-3 against the float32 oracle directly.
+
+Second, the reference's gradient is discontinuous where a hit point crosses a
+hash-cell boundary (the trilinear derivative jumps there) or the rho3d/rho2d
+branch switches. At the fine levels (cells ~1e-3 of the grid) float rounding
+differences of one ulp in the hit point move a few samples across a boundary
+between any two implementations, so a handful of surfels get a different but
+equally valid one-sided gradient. As the forward parity tests allow 0.1% of
+pixels to flip, these tests leave out the 0.5% of surfels that differ most
+(at least one) before measuring the relative L2, and bound the full relative
+L2 (nothing left out) by 1e-1.
+
+Upstream gradients are N(0, 1) on every output channel, including the
+allmap channels the reference's backward ignores (count, position, level
+colour), so a kernel that read them would fail.
+"""
+import numpy as np
+import pytest
+import torch
+
+import diff_surfel_rasterization as dsr
+from helpers import api_inputs, small_scene
+from nest_b200 import raster
+from oracle import oracle
+
+pytestmark = pytest.mark.gpu
+REL_TOL = 1e-3
+GRAD_KEYS = {  # torch wrapper key -> (oracle dict, oracle key)
+    "means3D": ("pg", "dL_dmeans3D"), "scales": ("pg", "dL_dscales"), "rotations": ("pg", "dL_drots"),
+    "opacity": ("g", "dL_dopacity"), "table": ("g", "dL_dtable"), "gradsum": ("g", "dL_gradsum"),
+    "means2D": ("pg", "dL_dmean2D"),
+}
+
+
+def rel_l2(a, b):
+    a = np.asarray(a, np.float64).reshape(-1)
+    b = np.asarray(b, np.float64).reshape(-1)
+    return float(np.linalg.norm(a - b) / max(np.linalg.norm(b), 1e-30))
+
+
+def upstream(scene, seed=3):
+    g = torch.Generator().manual_seed(seed)
+    cam = scene.camera
+    gc = torch.randn(scene.grid.channels, cam.height, cam.width, generator=g)
+    go = torch.randn(14, cam.height, cam.width, generator=g)
+    return gc, go
+
+
+def make_cfg(scene, fp16=True, **kw):
+    cam, g = scene.camera, scene.grid
+    return raster.RasterConfig(
+        image_height=cam.height, image_width=cam.width, tanfovx=cam.tanfovx, tanfovy=cam.tanfovy,
+        viewmatrix=cam.world_view_transform.cuda().contiguous(),
+        projmatrix=cam.full_proj_transform.cuda().contiguous(), levels=g.levels, S=g.S,
+        base_resolution=g.base_resolution, align_corners=g.align_corners, interpolation=g.interpolation,
+        channels=g.channels, level_dim=g.level_dim, table_fp16=fp16, **kw)
+
+
+def gpu_grads(scene, inputs, gc, go, fp16=True, accum=False, **kw):
+    g = scene.grid
+    cfg = make_cfg(scene, fp16, **kw)
+    table = g.table.cuda() if fp16 else g.table.float().cuda()
+    args = (inputs["means3D"].cuda().contiguous(), inputs["scales"].cuda().contiguous(),
+            inputs["rotations"].cuda().contiguous(), inputs["opacities"].cuda().reshape(-1).contiguous(),
+            inputs["homotrans"].cuda().reshape(-1, 16).contiguous(), inputs["ap_level"].cuda().reshape(-1).contiguous(),
+            table.contiguous(), g.offsets.cuda().contiguous(), g.gridrange.cuda().contiguous())
+    n, color, others, radii, _, _, scratch = raster.rasterize_forward(cfg, *args)
+    grads = raster.rasterize_backward(cfg, *args, radii, n, scratch, gc.cuda(), go.cuda(),
+                                      return_accumulators=accum)
+    torch.cuda.synchronize()
+    return {k: v.cpu().numpy() for k, v in grads.items()}, radii.cpu().numpy()
+
+
+def oracle_grads(scene, inputs, gc, go, **kw):
+    cam, g = scene.camera, scene.grid
+    W, H = cam.width, cam.height
+    vm, pm = cam.world_view_transform.numpy(), cam.full_proj_transform.numpy()
+    pre = oracle.preprocess(inputs["means3D"].numpy(), inputs["scales"].numpy(), inputs["rotations"].numpy(),
+                            inputs["opacities"].numpy(), vm, pm, W, H, kw.get("scale_modifier", 1.0))
+    _, vals, ranges = oracle.bin_surfels(pre, W, H)
+    rkw = {k: v for k, v in kw.items() if k in ("interp", "contract", "beta", "align_corners")}
+    f64 = bool(kw.get("f64", False))
+    table = g.table.float().numpy()
+    common = (inputs["homotrans"].numpy(), inputs["ap_level"].numpy(), table, g.offsets.numpy(),
+              g.gridrange.numpy(), W, H, g.channels, g.level_dim, g.levels, g.S, g.base_resolution)
+    fwd = oracle.render(pre, vals, ranges, *common, **rkw)
+    gr = oracle.render_backward(pre, vals, ranges, fwd, *common, gc.numpy(), go.numpy(), f64=f64, **rkw)
+    pg = oracle.preprocess_backward(inputs["means3D"].numpy(), inputs["scales"].numpy(),
+                                    inputs["rotations"].numpy(), pre, gr, vm, pm, W, H, cam.tanfovx, cam.tanfovy,
+                                    f64=f64)
+    return dict(g=gr, pg=pg), pre
+
+
+OUTLIER_FRAC = 5e-3
+FULL_REL_MAX = 1e-1
+REF_FACTOR = 2.0
+REF_FACTOR_STAT = 3.0  # the densification statistic (means2D slot) is not a gradient
+
+
+def robust_rel_l2(a, b, frac=OUTLIER_FRAC):
+    """Relative L2 of a - b over rows (surfels) after leaving out the
+    ceil(frac * rows) rows with the largest difference."""
+    a = np.asarray(a, np.float64).reshape(len(a), -1)
+    b = np.asarray(b, np.float64).reshape(len(b), -1)
+    d = np.sum((a - b) ** 2, axis=1)
+    k = max(1, int(np.ceil(frac * len(d))))
+    keep = np.sort(d)[:-k] if len(d) > k else d[:0]
+    return float(np.sqrt(keep.sum()) / max(np.linalg.norm(b), 1e-30))
+
+
+def check_all(got, ref, exact=None, tol=REL_TOL):
+    """Per gradient: robust relative L2 to the float32 oracle `ref` within tol;
+    where that fails, robust relative L2 to the double-precision oracle `exact`
+    within max(tol, 2 x the float32 oracle's own robust distance to it; 3 x
+    for the densification statistic, a sum of transform-gradient rows).
+    The hash-table gradient is compared whole (rows are table entries)."""
+    report, ok = [], True
+    for k, (src, key) in GRAD_KEYS.items():
+        want = ref[src][key]
+        assert np.isfinite(got[k]).all(), k
+        assert np.linalg.norm(want) > 0, k
+        rel = rel_l2 if k == "table" else robust_rel_l2
+        full = rel_l2(got[k], want)
+        e32 = rel(got[k], want)
+        good = e32 <= tol and full <= FULL_REL_MAX
+        msg = f"{k}: vs f32 oracle {e32:.2e} (full {full:.2e})"
+        if not good and exact is not None:
+            e64 = rel(got[k], exact[src][key])
+            eref = rel(want, exact[src][key])
+            factor = REF_FACTOR_STAT if k == "means2D" else REF_FACTOR
+            good = e64 <= max(tol, factor * eref) and full <= FULL_REL_MAX
+            msg += f", vs f64 {e64:.2e} (f32 oracle vs f64 {eref:.2e})"
+        ok &= good
+        report.append(msg)
+    assert ok, "; ".join(report)
+    return report
+
+
+def run_case(scene, fp16=True, seed=3, contract=False, beta=0.0, strict=False):
+    inputs = api_inputs(scene)
+    gc, go = upstream(scene, seed)
+    got, radii = gpu_grads(scene, inputs, gc, go, fp16=fp16, if_contract=contract, beta=beta)
+    kw = dict(interp=scene.grid.interpolation, contract=contract, beta=beta)
+    ref, pre = oracle_grads(scene, inputs, gc, go, **kw)
+    np.testing.assert_array_equal(radii, pre["radii"])
+    exact = None if strict else oracle_grads(scene, inputs, gc, go, f64=True, **kw)[0]
+    return check_all(got, ref, exact)
+
+
+def folded_oracle_accumulators(scene, g):
+    """The render pass's per-surfel sums in the kernel's folded layout, from the
+    oracle's reference-layout outputs: dL/dM[c][r] = sum_k P[k][r] dL/dT[k][c] +
+    dL/dhomotrans[3c + r], P = world2ndc * ndc2pix (backward.cu:2106-2161)."""
+    cam = scene.camera
+    W, H = cam.width, cam.height
+    pm = cam.full_proj_transform.numpy().reshape(16).astype(np.float64)
+    n = np.array([[W / 2, 0, 0, (W - 1) / 2], [0, H / 2, 0, (H - 1) / 2], [0, 0, 0, 1]])
+    P = np.array([[sum(pm[4 * r + j] * n[k][j] for j in range(4)) for r in range(3)] for k in range(3)])
+    dT = g["dL_dtransMat"].astype(np.float64).reshape(-1, 3, 3)  # [i, k, c]
+    dM = np.einsum("kr,ikc->icr", P, dT).reshape(-1, 9) + g["dL_dhomoMat"]
+    return np.concatenate([dM, g["dL_dtransMat"][:, 2:3], g["dL_dtransMat"][:, 5:6], g["dL_dmean2D"][:, :2],
+                           g["dL_dnormal"], g["dL_dopacity"][:, None], g["dL_gradsum"][:, None]], 1)
+
+
+def test_backward_render_accumulators_match_oracle():
+    sc = small_scene(seed=19, table_range=1e-4)
+    inputs = api_inputs(sc)
+    gc, go = upstream(sc)
+    got, _ = gpu_grads(sc, inputs, gc, go, accum=True)
+    ref, _ = oracle_grads(sc, inputs, gc, go)
+    want = folded_oracle_accumulators(sc, ref["g"])
+    names = ["dM%d" % i for i in range(9)] + ["dTuz", "dTvz", "mean2Dx", "mean2Dy", "nx", "ny", "nz", "opacity",
+                                               "gradsum"]
+    errs = {nm: rel_l2(got["accum"][:, i], want[:, i]) for i, nm in enumerate(names)}
+    assert all(e <= REL_TOL for e in errs.values()), ", ".join(f"{k}={v:.2e}" for k, v in errs.items())
+
+
+def test_backward_matches_oracle_benchmark_table():
+    # The benchmark's table range: 1e-3 against the float32 oracle on every gradient.
+    run_case(small_scene(table_range=1e-4), strict=True)
+
+
+def test_backward_matches_oracle_fp16_table():
+    run_case(small_scene())
+
+
+def test_backward_matches_oracle_fp32_table():
+    run_case(small_scene(), fp16=False)
+
+
+def test_backward_matches_oracle_mixed_ap_levels():
+    sc = small_scene(seed=12)
+    g = torch.Generator().manual_seed(5)
+    sc.ap_level = (torch.randint(0, 19, (sc.P, 1), generator=g).float() + 0.25)
+    run_case(sc, seed=4)
+
+
+def test_backward_matches_oracle_smoothstep():
+    sc = small_scene(seed=13)
+    sc.grid.interpolation = 1
+    run_case(sc)
+
+
+def test_backward_matches_oracle_contract():
+    sc = small_scene(seed=14)
+    sc.grid.gridrange = torch.tensor([-0.8, 0.8])  # |hit| up to 1.2: both contraction branches
+    run_case(sc, contract=True)
+
+
+def test_backward_matches_oracle_beta():
+    run_case(small_scene(seed=15), beta=0.5)
+
+
+def test_backward_is_repeatable():
+    sc = small_scene(seed=16)
+    inputs = api_inputs(sc)
+    gc, go = upstream(sc)
+    a, _ = gpu_grads(sc, inputs, gc, go)
+    b, _ = gpu_grads(sc, inputs, gc, go)
+    for k in GRAD_KEYS:
+        # float atomics add in a run-dependent order: equal up to rounding
+        assert rel_l2(a[k], b[k]) < 1e-4, k
+
+
+def test_backward_empty_and_offscreen():
+    sc = small_scene(n=64, seed=17)
+    inputs = api_inputs(sc)
+    inputs["means3D"] = inputs["means3D"] + torch.tensor([0.0, -50.0, 0.0])  # behind the camera (at y = -4)
+    gc, go = upstream(sc)
+    got, radii = gpu_grads(sc, inputs, gc, go)
+    assert (radii == 0).all()
+    for k in GRAD_KEYS:
+        assert not np.any(got[k]), k
+
+
+def test_dropin_autograd_matches_oracle():
+    sc = small_scene(seed=18)
+    inputs = api_inputs(sc)
+    gc, go = upstream(sc, seed=9)
+    cam, g = sc.camera, sc.grid
+    dev = "cuda"
+    rs = dsr.GaussianRasterizationSettings(
+        image_height=cam.height, image_width=cam.width, tanfovx=cam.tanfovx, tanfovy=cam.tanfovy,
+        bg=torch.zeros(3, device=dev), scale_modifier=1.0, viewmatrix=cam.world_view_transform.to(dev),
+        projmatrix=cam.full_proj_transform.to(dev), sh_degree=0, campos=cam.camera_center.to(dev),
+        prefiltered=False, debug=False, beta=0.0, if_contract=False, record_transmittance=False,
+        max_intersections=0)
+    hs = dsr.HashGridSettings(L=g.levels, S=g.S, H=g.base_resolution, align_corners=g.align_corners,
+                              interpolation=g.interpolation,
+                              shape_dims=torch.tensor([0, g.channels, g.channels], dtype=torch.int32, device=dev))
+    r = dsr.GaussianRasterizer(rs, hs)
+    P = sc.P
+    leaf = lambda t: t.to(dev).clone().requires_grad_(True)  # noqa: E731
+    means, scales, rots = leaf(inputs["means3D"]), leaf(inputs["scales"]), leaf(inputs["rotations"])
+    opac, table = leaf(inputs["opacities"]), leaf(g.table.float())
+    means2D = leaf(torch.zeros(P, 3))
+    ap = leaf(inputs["ap_level"])
+    color, radii, allmap, trans, cover = r(
+        means3D=means, means2D=means2D, shs=torch.zeros(P, 1, 3, device=dev), opacities=opac, scales=scales,
+        rotations=rots, homotrans=inputs["homotrans"].to(dev), ap_level=ap, features=table,
+        offsets=g.offsets.to(dev), gridrange=g.gridrange.to(dev), render_mode=0)
+    loss = (color * gc.to(dev)).sum() + (allmap * go.to(dev)).sum()
+    loss.backward()
+    ref, _ = oracle_grads(sc, inputs, gc, go)
+    exact, _ = oracle_grads(sc, inputs, gc, go, f64=True)
+    got = {"means3D": means.grad, "scales": scales.grad, "rotations": rots.grad, "opacity": opac.grad,
+           "table": table.grad, "gradsum": ap.grad, "means2D": means2D.grad}
+    assert opac.grad.shape == opac.shape and ap.grad.shape == ap.shape and table.grad.dtype == table.dtype
+    check_all({k: v.detach().cpu().numpy() for k, v in got.items()}, ref, exact)
