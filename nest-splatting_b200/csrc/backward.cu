@@ -281,19 +281,29 @@ __global__ void __launch_bounds__(kThreads, 2) blend_backward_kernel(const Backw
         nitems += __popc(m);
       }
       __syncwarp();
+      // One list entry per lane per step; levels in a warp-uniform loop so that
+      // the table-gradient scatter can be aggregated across the warp.
       for (int base = 0; base < nitems; base += 32) {
         const int ii = base + lane;
-        if (ii >= nitems) continue;
-        const uint32_t tb = S.item[wid][ii];
-        const int pp = pbase + (int)(tb & 31u), k = (int)(tb >> 5);
-        const float4 sm = S.samp[k][pp];
-        const uint32_t nl = S.lvl[k][pp];
+        const bool has = ii < nitems;
+        int pp = pbase, k = 0;
+        float4 sm = make_float4(0.f, 0.f, 0.f, 0.f);
+        uint32_t nl = 0;
+        if (has) {
+          const uint32_t tb = S.item[wid][ii];
+          pp = pbase + (int)(tb & 31u);
+          k = (int)(tb >> 5);
+          sm = S.samp[k][pp];
+          nl = S.lvl[k][pp];
+        }
+        const uint32_t nlmax = __reduce_max_sync(0xffffffffu, nl);
         const float aT = sm.w;
         const float pin[3] = {sm.x, sm.y, sm.z};
         float fdot = 0.f, d0 = 0.f, d1 = 0.f, d2 = 0.f;
-        for (uint32_t l = 0; l < nl; l++) {
+        for (uint32_t l = 0; l < nlmax; l++) {
+          const bool on = l < nl;
           const LevelConst lcst = S.lv[l];
-          uint32_t gc[3];
+          uint32_t gc[3] = {0u, 0u, 0u}, idx[8];
           float f[3], dv[3];
 #pragma unroll
           for (int d = 0; d < 3; d++) {
@@ -307,48 +317,89 @@ __global__ void __launch_bounds__(kThreads, 2) blend_backward_kernel(const Backw
               dv[d] = 1.0f;
             }
           }
-          uint32_t idx[8];
-          corner_rows(lcst, gc, idx);
           Corner8<TableT> cv;
+          float2 v[8];
+          float2 gl = make_float2(0.f, 0.f);
+          if (on) {
+            corner_rows(lcst, gc, idx);
 #pragma unroll
-          for (int c = 0; c < 8; c++) cv.load(lcst.base, c, idx[c]);
-          const float2 gl = *acc_pair(S.g, pp, (int)l);
-          const float2 grad = make_float2(aT * gl.x, aT * gl.y);
-          const float wx[2] = {1 - f[0], f[0]}, wy[2] = {1 - f[1], f[1]}, wz[2] = {1 - f[2], f[2]};
-          float2 feat = make_float2(0.f, 0.f);
-          float2* dtab = reinterpret_cast<float2*>(p.dL_dtable) + lcst.row0;
+            for (int c = 0; c < 8; c++) cv.load(lcst.base, c, idx[c]);
+            gl = *acc_pair(S.g, pp, (int)l);
+            const float2 grad = make_float2(aT * gl.x, aT * gl.y);
+            const float wx[2] = {1 - f[0], f[0]}, wy[2] = {1 - f[1], f[1]}, wz[2] = {1 - f[2], f[2]};
+            float2 feat = make_float2(0.f, 0.f);
 #pragma unroll
-          for (int c = 0; c < 8; c++) {
-            const float w = (wx[c & 1] * wy[(c >> 1) & 1]) * wz[c >> 2];
-            const float2 v = cv.get(c);
-            feat.x += w * v.x;
-            feat.y += w * v.y;
-            atomicAdd(dtab + idx[c], make_float2(w * grad.x, w * grad.y));
+            for (int c = 0; c < 8; c++) {
+              const float w = (wx[c & 1] * wy[(c >> 1) & 1]) * wz[c >> 2];
+              const float2 cvv = cv.get(c);
+              feat.x += w * cvv.x;
+              feat.y += w * cvv.y;
+              v[c] = make_float2(w * grad.x, w * grad.y);
+            }
+            fdot += gl.x * feat.x + gl.y * feat.y;
+            // d feat / d hit_d: the 4 edges along axis d weighted by the other two
+            // axes' corner weights (hashgrid.h:231-283), dotted with grad.
+            float ex = 0.f, ey = 0.f, ez = 0.f;
+#pragma unroll
+            for (int e = 0; e < 4; e++) {
+              // x edges: corners (0|1) + 2 by + 4 bz, e = by + 2 bz
+              const int by = e & 1, bz = e >> 1;
+              const float2 a0 = cv.get(2 * by + 4 * bz), a1 = cv.get(1 + 2 * by + 4 * bz);
+              ex += (wy[by] * wz[bz]) * (grad.x * (a1.x - a0.x) + grad.y * (a1.y - a0.y));
+              // y edges: corners bx + (0|2) + 4 bz, e = bx + 2 bz
+              const int bx = e & 1;
+              const float2 b0 = cv.get(bx + 4 * bz), b1 = cv.get(bx + 2 + 4 * bz);
+              ey += (wx[bx] * wz[bz]) * (grad.x * (b1.x - b0.x) + grad.y * (b1.y - b0.y));
+              // z edges: corners bx + 2 by + (0|4), e = bx + 2 by
+              const int by2 = e >> 1;
+              const float2 c0 = cv.get(bx + 2 * by2), c1 = cv.get(bx + 2 * by2 + 4);
+              ez += (wx[bx] * wy[by2]) * (grad.x * (c1.x - c0.x) + grad.y * (c1.y - c0.y));
+            }
+            d0 += ex * lcst.scale * dv[0];
+            d1 += ey * lcst.scale * dv[1];
+            d2 += ez * lcst.scale * dv[2];
+          } else {
+#pragma unroll
+            for (int c = 0; c < 8; c++) v[c] = make_float2(0.f, 0.f);
           }
-          fdot += gl.x * feat.x + gl.y * feat.y;
-          // d feat / d hit_d: the 4 edges along axis d weighted by the other two
-          // axes' corner weights (hashgrid.h:231-283), dotted with grad.
-          float ex = 0.f, ey = 0.f, ez = 0.f;
-#pragma unroll
-          for (int e = 0; e < 4; e++) {
-            // x edges: corners (0|1) + 2 by + 4 bz, e = by + 2 bz
-            const int by = e & 1, bz = e >> 1;
-            const float2 a0 = cv.get(2 * by + 4 * bz), a1 = cv.get(1 + 2 * by + 4 * bz);
-            ex += (wy[by] * wz[bz]) * (grad.x * (a1.x - a0.x) + grad.y * (a1.y - a0.y));
-            // y edges: corners bx + (0|2) + 4 bz, e = bx + 2 bz
-            const int bx = e & 1;
-            const float2 b0 = cv.get(bx + 4 * bz), b1 = cv.get(bx + 2 + 4 * bz);
-            ey += (wx[bx] * wz[bz]) * (grad.x * (b1.x - b0.x) + grad.y * (b1.y - b0.y));
-            // z edges: corners bx + 2 by + (0|4), e = bx + 2 by
-            const int by2 = e >> 1;
-            const float2 c0 = cv.get(bx + 2 * by2), c1 = cv.get(bx + 2 * by2 + 4);
-            ez += (wx[bx] * wy[by2]) * (grad.x * (c1.x - c0.x) + grad.y * (c1.y - c0.y));
+          // Table-gradient scatter (hashgrid.h:184-190), aggregated per cell:
+          // lanes in the same cell of this level form a list (each lane links to
+          // the next lane of its cell), pointer jumping sums every list into its
+          // first lane, which alone issues the cell's 8 float2 atomics. At the
+          // coarse levels a warp's 32 samples share a few cells, and unaggregated
+          // atomics there serialise on a few hundred table rows.
+          const uint32_t act = __ballot_sync(0xffffffffu, on);
+          int nxt = -1;
+          bool head = false;
+          if (on) {
+            const unsigned long long key =
+                (unsigned long long)gc[0] | ((unsigned long long)gc[1] << 21) | ((unsigned long long)gc[2] << 42);
+            const uint32_t grp = __match_any_sync(act, key);
+            const uint32_t after = grp & ~((2u << lane) - 1u);
+            nxt = after ? __ffs(after) - 1 : -1;
+            head = (grp & ((1u << lane) - 1u)) == 0u;
           }
-          d0 += ex * lcst.scale * dv[0];
-          d1 += ey * lcst.scale * dv[1];
-          d2 += ez * lcst.scale * dv[2];
+          while (__any_sync(0xffffffffu, nxt >= 0)) {
+            const int src = nxt >= 0 ? nxt : lane;
+#pragma unroll
+            for (int c = 0; c < 8; c++) {
+              const float vx = __shfl_sync(0xffffffffu, v[c].x, src);
+              const float vy = __shfl_sync(0xffffffffu, v[c].y, src);
+              if (nxt >= 0) {
+                v[c].x += vx;
+                v[c].y += vy;
+              }
+            }
+            const int nn = __shfl_sync(0xffffffffu, nxt, src);
+            nxt = nxt >= 0 ? nn : -1;
+          }
+          if (on && head) {
+            float2* dtab = reinterpret_cast<float2*>(p.dL_dtable) + lcst.row0;
+#pragma unroll
+            for (int c = 0; c < 8; c++) atomicAdd(dtab + idx[c], v[c]);
+          }
         }
-        S.samp[k][pp] = make_float4(fdot, d0, d1, d2);
+        if (has) S.samp[k][pp] = make_float4(fdot, d0, d1, d2);
       }
       __syncwarp();
 
