@@ -132,6 +132,57 @@ def profiled_traffic():
     return None
 
 
+def train_step_timing(sc, cam, dev, steps, warmup=2):
+    """one training step (forward, MLP, L1 + normal loss,
+    backward into the surfels, the hash table and the MLP) on the config-2 scene."""
+    import torch
+
+    import diff_surfel_rasterization as dsr
+    from nest_b200 import train
+
+    g = sc.grid
+    state = train.make_state(sc, device=dev)
+    rs = dsr.GaussianRasterizationSettings(
+        image_height=cam.height, image_width=cam.width, tanfovx=cam.tanfovx, tanfovy=cam.tanfovy,
+        bg=torch.zeros(3, device=dev), scale_modifier=1.0, viewmatrix=cam.world_view_transform.to(dev),
+        projmatrix=cam.full_proj_transform.to(dev), sh_degree=0, campos=cam.camera_center.to(dev),
+        prefiltered=False, debug=False, beta=0.0, if_contract=False, record_transmittance=False,
+        max_intersections=0)
+    hs = dsr.HashGridSettings(L=g.levels, S=g.S, H=g.base_resolution, align_corners=False, interpolation=0,
+                              shape_dims=torch.tensor([0, g.channels, g.channels], dtype=torch.int32, device=dev))
+    rast = dsr.GaussianRasterizer(rs, hs)
+
+    def one(evs=None):
+        for t in state.leaves():
+            t.grad = None
+        if evs:
+            evs[0].record()
+        loss, _, _ = train.forward(state, rast, cam)
+        if evs:
+            evs[1].record()
+        loss.backward()
+        if evs:
+            evs[2].record()
+        return loss
+
+    for _ in range(warmup):
+        one()
+    torch.cuda.synchronize()
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(steps)]
+    losses = []
+    for i in range(steps):
+        losses.append(one(evs[i]))
+    torch.cuda.synchronize()
+    fwd = statistics.mean(e[0].elapsed_time(e[1]) for e in evs)
+    bwd = statistics.mean(e[1].elapsed_time(e[2]) for e in evs)
+    ms = fwd + bwd
+    return {"workload": "config 4: config-2 scene, forward + backward of L1(rgb, target) + 0.05 normal loss; "
+                        "leaves means, scales, rotations, opacities, hash table, MLP weights",
+            "steps": steps, "ms_per_step": round(ms, 3), "forward_ms": round(fwd, 3),
+            "backward_ms": round(bwd, 3), "mpix_per_s": round(cam.width * cam.height / 1e6 * 1000.0 / ms, 3),
+            "loss_first": round(float(losses[0].detach()), 6)}
+
+
 def run_ours(args):
     import torch
     import torch.distributed as dist
@@ -281,6 +332,8 @@ def run_ours(args):
         "gpu_launches": int(launches),
         "clocks": clk.summary(),
     }
+    if not args.no_train:
+        line["train_step"] = train_step_timing(sc, cam, dev, steps=min(args.steps, 10))
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(sc, budget_s=args.cpu_budget)
     if rank == 0:
@@ -375,6 +428,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-train", action="store_true", help="skip the config-4 training-step timing")
     ap.add_argument("--cpu-budget", type=float, default=30.0)
     args = ap.parse_args()
     if args.impl == "reference":
