@@ -8,14 +8,12 @@
 // shape (6 x 256 x 59 fp32 = 354 KB) does not fit one SM's 227 KB of shared
 // memory, so the dimension axis is split in two halves of 32 columns and each
 // CTA holds all stages of one half (6 x 256 x 32 x 4 = 192 KB). CTAs are
-// persistent (one per SM) and walk 512-surfel chunks. The codebook half and
-// each chunk's index bytes arrive by cp.async (the next chunk's bytes stream in
-// while the current chunk is decoded). Inside a chunk a half-warp owns one
-// surfel: lane j reads a float2 of columns (2j, 2j+1) of the selected codeword
-// of each stage (conflict-free: the half-warp reads one contiguous 128-byte half
-// row), so a warp decodes two surfels per step, 16 independent steps per chunk.
-// Index bytes are packed to one u64 per surfel in shared memory so the stage
-// indices of a surfel cost one broadcast read.
+// persistent (one per SM) and walk 1024-surfel chunks. The codebook half and
+// the chunks' index bytes arrive by cp.async; index bytes run three chunks
+// ahead of the decode (a chunk decodes in about a microsecond, less than one
+// DRAM round trip, so a single chunk of look-ahead left the kernel waiting on
+// its index stream). Index bytes are packed to one u64 per surfel in shared
+// memory so the stage indices of a surfel cost one broadcast read.
 //
 // Bound: HBM (6 B of indices read + 4*dims B written per surfel); the shared
 // memory gather (6 x 128 B per surfel-half) runs at about the same time, so
@@ -26,9 +24,13 @@ namespace ns {
 namespace {
 
 constexpr int kRvqThreads = 512;
-constexpr int kRvqChunk = 512;   // surfels per chunk (one per thread for index packing)
+constexpr int kRvqChunk = 1024;  // surfels per chunk (two per thread for index packing)
 constexpr int kHalfCols = 32;
-constexpr int kIdxWords = kRvqChunk * 8 / 4;  // raw index bytes of a chunk, as 4-byte words
+constexpr int kIdxStages = 3;    // index chunks in flight
+
+// Raw index bytes of one chunk as 4-byte words, for K stages.
+template <int K>
+__host__ __device__ constexpr int kIdxWordsK() { return (kRvqChunk * K + 3) / 4; }
 
 __device__ __forceinline__ void cp_async4(void* smem_dst, const void* gmem_src, int src_bytes) {
   const unsigned dst = (unsigned)__cvta_generic_to_shared(smem_dst);
@@ -64,8 +66,8 @@ rvq_decode_smem_kernel(const uint8_t* __restrict__ idx, const float* __restrict_
                        float* __restrict__ out, int64_t n, int E, int D) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   float* cb_s = reinterpret_cast<float*>(smem_raw);                                  // [K*E][32]
-  uint32_t* raw = reinterpret_cast<uint32_t*>(cb_s + (size_t)K * E * kHalfCols);     // [2][kIdxWords]
-  uint2* idx_s = reinterpret_cast<uint2*>(raw + 2 * kIdxWords);                      // [chunk]
+  uint32_t* raw = reinterpret_cast<uint32_t*>(cb_s + (size_t)K * E * kHalfCols);     // [stages][words]
+  uint2* idx_s = reinterpret_cast<uint2*>(raw + kIdxStages * kIdxWordsK<K>());       // [chunk]
 
   const int half = blockIdx.y;
   const int col0 = half * kHalfCols;
@@ -85,35 +87,44 @@ rvq_decode_smem_kernel(const uint8_t* __restrict__ idx, const float* __restrict_
   const int64_t nchunks = div_up64(n, kRvqChunk);
   int64_t chunk = blockIdx.x;
   int buf = 0;
-  fetch_indices(idx, n, K, chunk, nchunks, raw);
+  constexpr int kWords = kIdxWordsK<K>();
+#pragma unroll
+  for (int st = 0; st < kIdxStages; st++)
+    fetch_indices(idx, n, K, chunk + (int64_t)st * gridDim.x, nchunks, raw + st * kWords);
 
   const int grp = lane >> 3;  // surfel of the step
   const int j = lane & 7;     // column block of the lane
   const float4* cb4 = reinterpret_cast<const float4*>(cb_s);
   const bool check_e = E < 256;
 
-  for (; chunk < nchunks; chunk += gridDim.x, buf ^= 1) {
-    asm volatile("cp.async.wait_group 0;");
-    __syncthreads();  // codebook and this chunk's index bytes are in; last chunk consumed
-    fetch_indices(idx, n, K, chunk + gridDim.x, nchunks, raw + (buf ^ 1) * kIdxWords);
+  for (; chunk < nchunks; chunk += gridDim.x, buf = (buf + 1 == kIdxStages) ? 0 : buf + 1) {
+    // The oldest of the kIdxStages groups in flight (this chunk's bytes; the
+    // first time also the codebook) is complete.
+    asm volatile("cp.async.wait_group %0;" ::"n"(kIdxStages - 1));
+    __syncthreads();  // ... for every thread; the previous chunk's decode is done
     const int64_t base = chunk * kRvqChunk;
     const int cnt = (int)min64(kRvqChunk, n - base);
-    {  // surfel tid's K index bytes as two words (bytes 0-3, 4-7)
-      const uint8_t* b = reinterpret_cast<const uint8_t*>(raw + buf * kIdxWords) + tid * K;
+#pragma unroll
+    for (int h = 0; h < (kRvqChunk + kRvqThreads - 1) / kRvqThreads; h++) {  // surfel's K index bytes
+      const int sl = tid + h * kRvqThreads;
+      const uint8_t* b = reinterpret_cast<const uint8_t*>(raw + buf * kWords) + sl * K;
       uint32_t lo = 0, hi = 0;
-      if (tid < cnt) {
+      if (sl < cnt) {
 #pragma unroll
         for (int k = 0; k < K; k++) {
           if (k < 4) lo |= (uint32_t)b[k] << (8 * k);
           else hi |= (uint32_t)b[k] << (8 * (k - 4));
         }
       }
-      idx_s[tid] = make_uint2(lo, hi);
+      idx_s[sl] = make_uint2(lo, hi);
     }
-    __syncthreads();
+    __syncthreads();  // packed indices visible; raw[buf] free for the chunk kIdxStages ahead
+    fetch_indices(idx, n, K, chunk + (int64_t)kIdxStages * gridDim.x, nchunks, raw + buf * kWords);
+    constexpr int kWarpsPerCta = kRvqThreads / 32;
+    constexpr int kPerWarp = kRvqChunk / kWarpsPerCta;  // surfels per warp per chunk
 #pragma unroll 2
-    for (int step = 0; step < 8; step++) {
-      const int s = warp * 32 + step * 4 + grp;
+    for (int step = 0; step < kPerWarp / 4; step++) {
+      const int s = warp * kPerWarp + step * 4 + grp;
       if (s < cnt) {
         const uint2 ix = idx_s[s];
         float2 a01 = make_float2(0.0f, 0.0f), a23 = make_float2(0.0f, 0.0f);
@@ -174,7 +185,8 @@ int rvq_decode_launch(const uint8_t* idx, const float* cb, float* out, int64_t n
   if (n < 0 || K <= 0 || K > 8 || E <= 0 || E > 256 || D <= 0 || D > 64) return NS_ERR_UNSUPPORTED;
   if (n == 0) return NS_OK;
   if (!idx || !cb || !out) return NS_ERR_INVALID;
-  const size_t smem = (size_t)K * E * kHalfCols * sizeof(float) + 2 * kIdxWords * sizeof(uint32_t) +
+  const size_t smem = (size_t)K * E * kHalfCols * sizeof(float) +
+                      kIdxStages * (size_t)((kRvqChunk * K + 3) / 4) * sizeof(uint32_t) +
                       kRvqChunk * sizeof(uint2);
   int dev = 0, sms = 0, max_smem = 0;
   NS_CUDA_TRY(cudaGetDevice(&dev));
