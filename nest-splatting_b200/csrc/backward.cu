@@ -25,9 +25,11 @@
 //     table gradient is scattered with float2 vector atomics and dL/d(hit) is
 //     formed from the corner differences;
 //   * phase C: each lane replays its own samples in order with the reference's
-//     recursions (colour, depth, alpha, normal, distortion) and adds the
-//     per-surfel gradients into per-record shared-memory accumulators, flushed
-//     to global memory with float4 atomics once per batch.
+//     recursions (colour, depth, alpha, normal, distortion) and adds each
+//     sample's per-surfel gradients to the surfel's accumulators in global
+//     memory with four (rho2d branch: five) float4 reductions. Shared-memory
+//     float atomics (a compare-and-swap loop) cost a third of the kernel here;
+//     vector reductions resolve in L2 and a surfel's ~30 samples rarely collide.
 // The transform gradient is folded into dL/dM = P dL/dT^T + dL/dhomotrans per
 // sample (P = world2ndc * ndc2pix is one matrix per camera), so a record carries
 // 18 accumulators instead of 25; the preprocess-backward kernel then turns dL/dM,
@@ -43,15 +45,16 @@ constexpr int kWarps = kThreads / 32;
 constexpr int kQueue = 4;       // queued samples per pixel between drains
 constexpr int kGradWords = 20;  // per-surfel accumulator words (18 used), 80 bytes
 
-// Accumulator words of one surfel.
+// Accumulator words of one surfel (80 bytes, five float4 groups; the last group
+// is non-zero only for samples of the rho2d branch).
 enum : int {
-  kGM = 0,          // dL/dM columns 0..2 (rows 0..2): L0, L1, mean
+  kGM = 0,          // dL/dM columns 0..2 (rows 0..2): L0, L1, mean -> words 0..8
   kGTuz = 9,        // dL/dT[0].z, dL/dT[1].z: the densification statistic
   kGTvz = 10,
-  kGMean2D = 11,    // dL/dmean2D x, y (rho2d branch)
-  kGNormal = 13,    // dL/dnormal (view space) x, y, z
-  kGOpacity = 16,
-  kGGradSum = 17,
+  kGOpacity = 11,
+  kGNormal = 12,    // dL/dnormal (view space) x, y, z
+  kGGradSum = 15,
+  kGMean2D = 16,    // dL/dmean2D x, y (rho2d branch)
 };
 
 // a * b - c * d with one rounding error at most (Kahan's difference of products
@@ -66,7 +69,6 @@ __device__ __forceinline__ float dop(float a, float b, float c, float d) {
 
 struct BwSmem {
   float4 rec[kThreads][kRecordFloat4];  // records of the batch, back to front
-  float gacc[kThreads][kGradWords];     // per-record gradient accumulators
   float g[kThreads * kAccStride];       // dL/dcolor per pixel (acc_pair layout)
   float4 samp[kQueue][kThreads];        // (hit in [0,1]^3, alpha T) -> (f, dL/dhit)
   float Ts[kQueue][kThreads];           // T at the sample
@@ -74,7 +76,6 @@ struct BwSmem {
   uint8_t lvl[kQueue][kThreads];        // levels to query
   uint8_t item[kWarps][kQueue * 32];    // per warp: samples in k-major order, (k << 5) | lane
   uint32_t ids[kThreads];
-  uint32_t touched[kThreads];
   uint32_t wmax[kWarps];
   float Pm[9];                          // P[k][r], k = T column, r = 0..2
   float cam[3];                         // camera centre in world space
@@ -184,9 +185,6 @@ __global__ void __launch_bounds__(kThreads, 2) blend_backward_kernel(const Backw
       }
     }
     asm volatile("cp.async.commit_group;");
-#pragma unroll
-    for (int q = 0; q < kGradWords; q++) S.gacc[t][q] = 0.f;
-    S.touched[t] = 0u;
     asm volatile("cp.async.wait_group 0;");
     __syncthreads();
 
@@ -560,40 +558,23 @@ __global__ void __launch_bounds__(kThreads, 2) blend_backward_kernel(const Backw
           dTw.z = dL_dz;
         }
         // dL/dM column c = sum_k P[k] dL/dT[k][c] + dL/dhomotrans column c.
-        float* ga = S.gacc[jj];
-        atomicAdd(ga + kGM + 0, P00 * dTu.x + P10 * dTv.x + P20 * dTw.x + h0x);
-        atomicAdd(ga + kGM + 1, P01 * dTu.x + P11 * dTv.x + P21 * dTw.x + h0y);
-        atomicAdd(ga + kGM + 2, P02 * dTu.x + P12 * dTv.x + P22 * dTw.x + h0z);
-        atomicAdd(ga + kGM + 3, P00 * dTu.y + P10 * dTv.y + P20 * dTw.y + h1x);
-        atomicAdd(ga + kGM + 4, P01 * dTu.y + P11 * dTv.y + P21 * dTw.y + h1y);
-        atomicAdd(ga + kGM + 5, P02 * dTu.y + P12 * dTv.y + P22 * dTw.y + h1z);
-        atomicAdd(ga + kGM + 6, P00 * dTu.z + P10 * dTv.z + P20 * dTw.z + h2x);
-        atomicAdd(ga + kGM + 7, P01 * dTu.z + P11 * dTv.z + P21 * dTw.z + h2y);
-        atomicAdd(ga + kGM + 8, P02 * dTu.z + P12 * dTv.z + P22 * dTw.z + h2z);
-        atomicAdd(ga + kGTuz, tuz);
-        atomicAdd(ga + kGTvz, tvz);
-        if (!on_plane) {
-          atomicAdd(ga + kGMean2D + 0, dmx);
-          atomicAdd(ga + kGMean2D + 1, dmy);
-        }
-        atomicAdd(ga + kGNormal + 0, aT * dn0);
-        atomicAdd(ga + kGNormal + 1, aT * dn1);
-        atomicAdd(ga + kGNormal + 2, aT * dn2);
-        atomicAdd(ga + kGOpacity, G * dL_dalpha);
-        atomicAdd(ga + kGGradSum, aT * gabs);
-        S.touched[jj] = 1u;
+        float4* ga = reinterpret_cast<float4*>(p.accum + (size_t)S.ids[jj] * kGradWords);
+        atomicAdd(ga + 0, make_float4(P00 * dTu.x + P10 * dTv.x + P20 * dTw.x + h0x,
+                                      P01 * dTu.x + P11 * dTv.x + P21 * dTw.x + h0y,
+                                      P02 * dTu.x + P12 * dTv.x + P22 * dTw.x + h0z,
+                                      P00 * dTu.y + P10 * dTv.y + P20 * dTw.y + h1x));
+        atomicAdd(ga + 1, make_float4(P01 * dTu.y + P11 * dTv.y + P21 * dTw.y + h1y,
+                                      P02 * dTu.y + P12 * dTv.y + P22 * dTw.y + h1z,
+                                      P00 * dTu.z + P10 * dTv.z + P20 * dTw.z + h2x,
+                                      P01 * dTu.z + P11 * dTv.z + P21 * dTw.z + h2y));
+        atomicAdd(ga + 2, make_float4(P02 * dTu.z + P12 * dTv.z + P22 * dTw.z + h2z, tuz, tvz,
+                                      G * dL_dalpha));
+        atomicAdd(ga + 3, make_float4(aT * dn0, aT * dn1, aT * dn2, aT * gabs));
+        if (!on_plane) atomicAdd(ga + 4, make_float4(dmx, dmy, 0.f, 0.f));
       }
       __syncwarp();
     }
-    __syncthreads();
-    if (t < todo && S.touched[t]) {
-      float4* dst = reinterpret_cast<float4*>(p.accum + (size_t)S.ids[t] * kGradWords);
-      const float* src = S.gacc[t];
-#pragma unroll
-      for (int q = 0; q < kGradWords / 4; q++)
-        atomicAdd(dst + q, make_float4(src[4 * q], src[4 * q + 1], src[4 * q + 2], src[4 * q + 3]));
-    }
-    __syncthreads();
+    __syncthreads();  // every warp is done with this batch before S.rec is refilled
   }
 }
 

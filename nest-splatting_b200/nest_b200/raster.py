@@ -167,8 +167,8 @@ def rasterize_backward(cfg: RasterConfig, means3D, scales, rotations, opacities,
     of fp32 gradients: means3D [P,3], means2D [P,3] (densification statistic),
     opacity [P,1], scales [P,2], rotations [P,4], table [rows, level_dim],
     gradsum [P,1]. With return_accumulators, also "accum": the render pass's
-    per-surfel accumulators [P,20] (dL/dM 9, dL/dT[0].z, dL/dT[1].z, dL/dmean2D 2,
-    dL/dnormal 3, opacity, gradsum, 2 unused), for tests.
+    per-surfel accumulators [P,20] (dL/dM 9, dL/dT[0].z, dL/dT[1].z, opacity,
+    dL/dnormal 3, gradsum, dL/dmean2D 2, 2 unused), for tests.
     """
     lib = _lib.load()
     dev = means3D.device

@@ -174,8 +174,8 @@ def folded_oracle_accumulators(scene, g):
     P = np.array([[sum(pm[4 * r + j] * n[k][j] for j in range(4)) for r in range(3)] for k in range(3)])
     dT = g["dL_dtransMat"].astype(np.float64).reshape(-1, 3, 3)  # [i, k, c]
     dM = np.einsum("kr,ikc->icr", P, dT).reshape(-1, 9) + g["dL_dhomoMat"]
-    return np.concatenate([dM, g["dL_dtransMat"][:, 2:3], g["dL_dtransMat"][:, 5:6], g["dL_dmean2D"][:, :2],
-                           g["dL_dnormal"], g["dL_dopacity"][:, None], g["dL_gradsum"][:, None]], 1)
+    return np.concatenate([dM, g["dL_dtransMat"][:, 2:3], g["dL_dtransMat"][:, 5:6], g["dL_dopacity"][:, None],
+                           g["dL_dnormal"], g["dL_gradsum"][:, None], g["dL_dmean2D"][:, :2]], 1)
 
 
 def test_backward_render_accumulators_match_oracle():
@@ -185,8 +185,8 @@ def test_backward_render_accumulators_match_oracle():
     got, _ = gpu_grads(sc, inputs, gc, go, accum=True)
     ref, _ = oracle_grads(sc, inputs, gc, go)
     want = folded_oracle_accumulators(sc, ref["g"])
-    names = ["dM%d" % i for i in range(9)] + ["dTuz", "dTvz", "mean2Dx", "mean2Dy", "nx", "ny", "nz", "opacity",
-                                               "gradsum"]
+    names = ["dM%d" % i for i in range(9)] + ["dTuz", "dTvz", "opacity", "nx", "ny", "nz", "gradsum", "mean2Dx",
+                                               "mean2Dy"]
     errs = {nm: rel_l2(got["accum"][:, i], want[:, i]) for i, nm in enumerate(names)}
     assert all(e <= REL_TOL for e in errs.values()), ", ".join(f"{k}={v:.2e}" for k, v in errs.items())
 
