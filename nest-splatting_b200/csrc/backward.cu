@@ -44,6 +44,7 @@ constexpr int kThreads = kTilePixels;
 constexpr int kWarps = kThreads / 32;
 constexpr int kQueue = 4;       // queued samples per pixel between drains
 constexpr int kGradWords = 20;  // per-surfel accumulator words (18 used), 80 bytes
+constexpr float kAggScale = 128.f;  // table-gradient aggregation below this level resolution
 
 // Accumulator words of one surfel (80 bytes, five float4 groups; the last group
 // is non-zero only for samples of the rho2d branch).
@@ -67,6 +68,14 @@ __device__ __forceinline__ float dop(float a, float b, float c, float d) {
   return f + e;
 }
 
+// Per-pixel constants of phase C, parked in shared memory while phase B runs
+// (they are not needed there, and the registers they would hold go to phase
+// B's loads in flight).
+enum : int {
+  kPxD = 0, kPxD2, kPxA, kPxDepth, kPxAccum, kPxReg, kPxMed, kPxN0, kPxN1, kPxN2, kPxAbs, kPxMedC,
+  kPxWords
+};
+
 struct BwSmem {
   float4 rec[kThreads][kRecordFloat4];  // records of the batch, back to front
   float g[kThreads * kAccStride];       // dL/dcolor per pixel (acc_pair layout)
@@ -77,6 +86,7 @@ struct BwSmem {
   uint8_t item[kWarps][kQueue * 32];    // per warp: samples in k-major order, (k << 5) | lane
   uint32_t ids[kThreads];
   uint32_t wmax[kWarps];
+  float pix[kPxWords][kThreads];        // per-pixel constants of phase C
   float Pm[9];                          // P[k][r], k = T column, r = 0..2
   float cam[3];                         // camera centre in world space
   LevelConst lv[kMaxLevels];
@@ -148,7 +158,21 @@ __global__ void __launch_bounds__(kThreads, 2) blend_backward_kernel(const Backw
     gabs += fabsf(v.x) + fabsf(v.y);
     *acc_pair(S.g, t, l) = v;
   }
-  const float final_A = 1 - T;
+  {
+    float* px = &S.pix[0][t];
+    px[kPxD * kThreads] = final_D;
+    px[kPxD2 * kThreads] = final_D2;
+    px[kPxA * kThreads] = 1 - T;
+    px[kPxDepth * kThreads] = dL_ddepth;
+    px[kPxAccum * kThreads] = dL_daccum;
+    px[kPxReg * kThreads] = dL_dreg;
+    px[kPxMed * kThreads] = dL_dmed;
+    px[kPxN0 * kThreads] = dn0;
+    px[kPxN1 * kThreads] = dn1;
+    px[kPxN2 * kThreads] = dn2;
+    px[kPxAbs * kThreads] = gabs;
+    px[kPxMedC * kThreads] = __int_as_float(median_c);
+  }
   {
     const uint32_t m = __reduce_max_sync(0xffffffffu, lc);
     if (lane == 0) S.wmax[wid] = m;
@@ -160,9 +184,6 @@ __global__ void __launch_bounds__(kThreads, 2) blend_backward_kernel(const Backw
   const uint2 range = p.ranges[tile];
   const int total = (int)maxlc;
   const int rounds = div_up(total, kThreads);
-  const float P00 = S.Pm[0], P01 = S.Pm[1], P02 = S.Pm[2];
-  const float P10 = S.Pm[3], P11 = S.Pm[4], P12 = S.Pm[5];
-  const float P20 = S.Pm[6], P21 = S.Pm[7], P22 = S.Pm[8];
 
   // Back-to-front recursions of the reference (scalar colour term: the
   // feature vector only enters through f = feat . dL/dcolor).
@@ -368,8 +389,12 @@ __global__ void __launch_bounds__(kThreads, 2) blend_backward_kernel(const Backw
           // atomics there serialise on a few hundred table rows.
           const uint32_t act = __ballot_sync(0xffffffffu, on);
           int nxt = -1;
-          bool head = false;
-          if (on) {
+          bool head = true;
+          // Coarse levels only (fewer than kAggScale cells per axis): finer cells
+          // are rarely shared by a warp's samples and their atomics do not
+          // contend, so the grouping would cost more than it saves.
+          if (on && lcst.scale < kAggScale) {
+            head = false;
             const unsigned long long key =
                 (unsigned long long)gc[0] | ((unsigned long long)gc[1] << 21) | ((unsigned long long)gc[2] << 42);
             const uint32_t grp = __match_any_sync(act, key);
@@ -402,6 +427,18 @@ __global__ void __launch_bounds__(kThreads, 2) blend_backward_kernel(const Backw
       __syncwarp();
 
       // ---------------- phase C: this lane's samples, back to front.
+      const volatile float* pxv = &S.pix[0][t];
+      const float final_D = pxv[kPxD * kThreads], final_D2 = pxv[kPxD2 * kThreads];
+      const float final_A = pxv[kPxA * kThreads], dL_ddepth = pxv[kPxDepth * kThreads];
+      const float dL_daccum = pxv[kPxAccum * kThreads], dL_dreg = pxv[kPxReg * kThreads];
+      const float dL_dmed = pxv[kPxMed * kThreads];
+      const float dn0 = pxv[kPxN0 * kThreads], dn1 = pxv[kPxN1 * kThreads], dn2 = pxv[kPxN2 * kThreads];
+      const float gabs = pxv[kPxAbs * kThreads];
+      const int median_c = __float_as_int(pxv[kPxMedC * kThreads]);
+      const volatile float* pmv = S.Pm;
+      const float P00 = pmv[0], P01 = pmv[1], P02 = pmv[2];
+      const float P10 = pmv[3], P11 = pmv[4], P12 = pmv[5];
+      const float P20 = pmv[6], P21 = pmv[7], P22 = pmv[8];
       for (int k = 0; k < cnt; k++) {
         const int jj = S.jj[k][t];
         const float Ti = S.Ts[k][t];
