@@ -28,7 +28,9 @@ class _MLP(torch.autograd.Function):
 
     Forward on the library's tensor-core kernel (fp16 operands, fp32
     accumulation, each layer rounded to fp16). Backward treats the fp16
-    roundings as identity and runs in fp32 on the recomputed fp16 activations.
+    roundings as identity and runs on the recomputed fp16 activations with
+    TF32 tensor-core GEMMs (fp32 range: the per-pixel gradients of a mean
+    loss over megapixels are ~1e-7, below fp16's normal range).
     """
 
     @staticmethod
@@ -42,6 +44,15 @@ class _MLP(torch.autograd.Function):
 
     @staticmethod
     def backward(ctx, grgb):
+        prev = torch.backends.cuda.matmul.allow_tf32
+        torch.backends.cuda.matmul.allow_tf32 = True
+        try:
+            return _MLP._backward(ctx, grgb)
+        finally:
+            torch.backends.cuda.matmul.allow_tf32 = prev
+
+    @staticmethod
+    def _backward(ctx, grgb):
         feat, w1, w2, w3, alpha = ctx.saved_tensors
         C = feat.shape[0]
         x = feat.detach().reshape(C, -1).T.half().float()
@@ -76,9 +87,16 @@ def mlp(feat, w1, w2, w3, alpha, bg=None):
     return _MLP.apply(feat, w1, w2, w3, alpha, bg)
 
 
-def depths_to_points(cam, depthmap):
-    """utils/point_utils.py:10-30: pixel rays scaled by depth (world points [H*W, 3])."""
-    dev = depthmap.device
+_RAYS = {}
+
+
+def _camera_rays(cam, dev):
+    """Per-pixel ray directions and origin of utils/point_utils.py:10-30, computed
+    once per camera (the reference recomputes them, with a 3x3 inverse, per call)."""
+    key = (id(cam), cam.width, cam.height, str(dev))
+    hit = _RAYS.get(key)
+    if hit is not None and hit[0] is cam:
+        return hit[1], hit[2]
     W, H = cam.width, cam.height
     wv = cam.world_view_transform.to(dev)
     c2w = wv.T.inverse()
@@ -90,6 +108,15 @@ def depths_to_points(cam, depthmap):
     pts = torch.stack([gx, gy, torch.ones_like(gx)], dim=-1).reshape(-1, 3)
     rays_d = pts @ intrins.inverse().T @ c2w[:3, :3].T
     rays_o = c2w[:3, 3]
+    if len(_RAYS) > 64:
+        _RAYS.clear()
+    _RAYS[key] = (cam, rays_d, rays_o)
+    return rays_d, rays_o
+
+
+def depths_to_points(cam, depthmap):
+    """utils/point_utils.py:10-30: pixel rays scaled by depth (world points [H*W, 3])."""
+    rays_d, rays_o = _camera_rays(cam, depthmap.device)
     return depthmap.reshape(-1, 1) * rays_d + rays_o
 
 
