@@ -27,8 +27,8 @@
 //   * phase C: each lane replays its own samples in order with the reference's
 //     recursions (colour, depth, alpha, normal, distortion) and adds each
 //     sample's per-surfel gradients to the surfel's accumulators in global
-//     memory with four (rho2d branch: five) float4 reductions. Shared-memory
-//     float atomics (a compare-and-swap loop) cost a third of the kernel here;
+//     memory with four (rho2d branch: five) float4 reductions. Per-record
+//     shared-memory float atomics cost a third of the kernel here (measured);
 //     vector reductions resolve in L2 and a surfel's ~30 samples rarely collide.
 // The transform gradient is folded into dL/dM = P dL/dT^T + dL/dhomotrans per
 // sample (P = world2ndc * ndc2pix is one matrix per camera), so a record carries
