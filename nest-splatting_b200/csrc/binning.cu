@@ -47,30 +47,59 @@ scan_block_sums_kernel(const uint32_t* __restrict__ sums, uint32_t* __restrict__
   if (t == 0) *total = (int64_t)carry_s;
 }
 
-__global__ void __launch_bounds__(256)
-duplicate_keys_kernel(int P, int block_size, const BinInfo* __restrict__ bin,
+constexpr int kDupThreads = 256;  // = the preprocess CTA size (one CTA's surfels per CTA here)
+constexpr int kDupStage = 4096;   // instances staged in shared memory per CTA (48 KB)
+
+// A CTA's surfels emit one contiguous run of instances (their offsets come from
+// the preprocess CTA's scan), so the run is assembled in shared memory and
+// written out with consecutive threads on consecutive instances: per-surfel
+// writes of a few scattered 12-byte records kept the store queue full.
+// Instances past kDupStage (surfels with very large footprints) are written
+// directly.
+__global__ void __launch_bounds__(kDupThreads)
+duplicate_keys_kernel(int P, const BinInfo* __restrict__ bin,
                       const uint32_t* __restrict__ excl_local,
-                      const uint32_t* __restrict__ block_prefix, int gx, int gy,
+                      const uint32_t* __restrict__ block_prefix,
+                      const uint32_t* __restrict__ block_sums, int gx,
                       uint64_t* __restrict__ keys, uint32_t* __restrict__ vals, int64_t capacity,
                       uint32_t* __restrict__ err) {
-  const int i = blockIdx.x * blockDim.x + threadIdx.x;
-  if (i >= P) return;
-  const BinInfo b = bin[i];
-  const int x0 = b.x0, y0 = b.y0, x1 = b.x1, y1 = b.y1;
-  if (x1 <= x0 || y1 <= y0) return;
-  int64_t off = (int64_t)block_prefix[i / block_size] + excl_local[i];
-  const int64_t cnt = (int64_t)(x1 - x0) * (y1 - y0);
-  if (off + cnt > capacity) {
-    set_error(err, kErrCapacity);
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  uint64_t* sk = reinterpret_cast<uint64_t*>(smem_raw);
+  uint32_t* sv = reinterpret_cast<uint32_t*>(sk + kDupStage);
+  const int cta = blockIdx.x;
+  const int i = cta * kDupThreads + threadIdx.x;
+  const int64_t base = (int64_t)block_prefix[cta];
+  const int64_t total = (int64_t)block_sums[cta];
+  if (base + total > capacity) {  // uniform over the CTA
+    if (threadIdx.x == 0) set_error(err, kErrCapacity);
     return;
   }
-  const uint64_t dbits = (uint64_t)__float_as_uint(b.depth);
-  for (int y = y0; y < y1; y++) {
-    for (int x = x0; x < x1; x++) {
-      keys[off] = ((uint64_t)(uint32_t)(y * gx + x) << 32) | dbits;
-      vals[off] = (uint32_t)i;
-      off++;
+  if (i < P) {
+    const BinInfo b = bin[i];
+    const int x0 = b.x0, y0 = b.y0, x1 = b.x1, y1 = b.y1;
+    if (x1 > x0 && y1 > y0) {
+      int64_t off = (int64_t)excl_local[i];
+      const uint64_t dbits = (uint64_t)__float_as_uint(b.depth);
+      for (int y = y0; y < y1; y++) {
+        for (int x = x0; x < x1; x++) {
+          const uint64_t key = ((uint64_t)(uint32_t)(y * gx + x) << 32) | dbits;
+          if (off < kDupStage) {
+            sk[off] = key;
+            sv[off] = (uint32_t)i;
+          } else {
+            keys[base + off] = key;
+            vals[base + off] = (uint32_t)i;
+          }
+          off++;
+        }
+      }
     }
+  }
+  __syncthreads();
+  const int staged = (int)min64(total, kDupStage);
+  for (int j = threadIdx.x; j < staged; j += kDupThreads) {
+    keys[base + j] = sk[j];
+    vals[base + j] = sv[j];
   }
 }
 
@@ -104,12 +133,17 @@ int scan_block_sums_launch(const uint32_t* sums, uint32_t* prefix, int nb, int64
 }
 
 int duplicate_keys_launch(int P, int block_size, const BinInfo* bin, const uint32_t* excl_local,
-                          const uint32_t* block_prefix, int gx, int gy, uint64_t* keys,
-                          uint32_t* vals, int64_t capacity, uint32_t* err, cudaStream_t stream) {
+                          const uint32_t* block_prefix, const uint32_t* block_sums, int gx,
+                          int gy, uint64_t* keys, uint32_t* vals, int64_t capacity, uint32_t* err,
+                          cudaStream_t stream) {
   if (P <= 0) return NS_OK;
-  duplicate_keys_kernel<<<div_up(P, 256), 256, 0, stream>>>(P, block_size, bin, excl_local,
-                                                            block_prefix, gx, gy, keys, vals,
-                                                            capacity, err);
+  if (block_size != kDupThreads) return NS_ERR_UNSUPPORTED;  // offsets are per preprocess CTA
+  (void)gy;
+  const int smem = kDupStage * (int)(sizeof(uint64_t) + sizeof(uint32_t));
+  NS_CUDA_TRY(cudaFuncSetAttribute(duplicate_keys_kernel,
+                                   cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+  duplicate_keys_kernel<<<div_up(P, kDupThreads), kDupThreads, smem, stream>>>(
+      P, bin, excl_local, block_prefix, block_sums, gx, keys, vals, capacity, err);
   NS_LAUNCH_CHECK();
   return NS_OK;
 }

@@ -187,8 +187,9 @@ int bin_and_render(const ns_raster_settings* st, int P, const GeomState& g, cons
   if (num_rendered) *num_rendered = count;
   if (count > cap) return NS_ERR_CAPACITY;
   BinState b = carve_bin(binning, cap, nullptr);
-  rc = duplicate_keys_launch(P, preprocess_block_size(), g.bin, g.excl_local, g.block_prefix, gx,
-                             gy, b.keys_unsorted, b.vals_unsorted, cap, g.err, stream);
+  rc = duplicate_keys_launch(P, preprocess_block_size(), g.bin, g.excl_local, g.block_prefix,
+                             g.block_sums, gx, gy, b.keys_unsorted, b.vals_unsorted, cap, g.err,
+                             stream);
   if (rc) return rc;
   const int end_bit = 32 + (int)higher_msb((uint32_t)tiles);
   rc = radix_sort_launch(b.keys_unsorted, b.vals_unsorted, b.keys_sorted, b.vals_sorted, b.keys_alt,

@@ -80,8 +80,9 @@ int mark_visible_launch(int P, const float* means3D, const float* vm, uint8_t* p
 int scan_block_sums_launch(const uint32_t* sums, uint32_t* prefix, int nb, int64_t* total,
                            cudaStream_t stream);
 int duplicate_keys_launch(int P, int block_size, const BinInfo* bin, const uint32_t* excl_local,
-                          const uint32_t* block_prefix, int gx, int gy, uint64_t* keys,
-                          uint32_t* vals, int64_t capacity, uint32_t* err, cudaStream_t stream);
+                          const uint32_t* block_prefix, const uint32_t* block_sums, int gx,
+                          int gy, uint64_t* keys, uint32_t* vals, int64_t capacity, uint32_t* err,
+                          cudaStream_t stream);
 int identify_ranges_launch(const uint64_t* keys, const int64_t* count_dev, int64_t count_host,
                            int64_t capacity, uint2* ranges, int tiles, int sms,
                            cudaStream_t stream);
