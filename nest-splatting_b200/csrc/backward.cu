@@ -327,8 +327,9 @@ __global__ void __launch_bounds__(kThreads, 2) blend_backward_kernel(const Backw
 #pragma unroll
           for (int d = 0; d < 3; d++) {
             const float pos = pin[d] * lcst.scale + half_shift;
-            gc[d] = (uint32_t)floorf(pos);
-            f[d] = pos - (float)gc[d];
+            const float fl = floorf(pos);
+            gc[d] = (uint32_t)fl;
+            f[d] = pos - fl;
             if (p.interp == 1) {
               dv[d] = 6 * f[d] * (1.0f - f[d]);
               f[d] = f[d] * f[d] * (3.0f - 2.0f * f[d]);

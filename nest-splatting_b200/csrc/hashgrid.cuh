@@ -99,19 +99,28 @@ __device__ __forceinline__ void corner_rows(const LevelConst& lc, const uint32_t
 #pragma unroll
     for (int c = 0; c < 8; c++)
       idx[c] = base + (c & 1) + ((c >> 1) & 1 ? lc.s1 : 0u) + ((c >> 2) & 1 ? lc.s2 : 0u);
-  } else {
-    const uint32_t hy0 = g[1] * 2654435761u, hy1 = (g[1] + 1) * 2654435761u;
-    const uint32_t hz0 = g[2] * 805459861u, hz1 = (g[2] + 1) * 805459861u;
-    const uint32_t hyz[4] = {hy0 ^ hz0, hy1 ^ hz0, hy0 ^ hz1, hy1 ^ hz1};
+    if (lc.modulo) {
 #pragma unroll
-    for (int c = 0; c < 8; c++) idx[c] = (g[0] + (c & 1)) ^ hyz[c >> 1];
+      for (int c = 0; c < 8; c++) idx[c] %= lc.hsize;
+    } else {
+#pragma unroll
+      for (int c = 0; c < 8; c++) idx[c] &= lc.mask;
+    }
+    return;
   }
+  const uint32_t hy0 = g[1] * 2654435761u, hy1 = (g[1] + 1) * 2654435761u;
+  const uint32_t hz0 = g[2] * 805459861u, hz1 = (g[2] + 1) * 805459861u;
+  uint32_t hyz[4] = {hy0 ^ hz0, hy1 ^ hz0, hy0 ^ hz1, hy1 ^ hz1};
   if (lc.modulo) {
 #pragma unroll
-    for (int c = 0; c < 8; c++) idx[c] %= lc.hsize;
+    for (int c = 0; c < 8; c++) idx[c] = ((g[0] + (c & 1)) ^ hyz[c >> 1]) % lc.hsize;
   } else {
+    // (x ^ h) & m == (x & m) ^ (h & m): six masks instead of eight.
 #pragma unroll
-    for (int c = 0; c < 8; c++) idx[c] &= lc.mask;
+    for (int e = 0; e < 4; e++) hyz[e] &= lc.mask;
+    const uint32_t x0 = g[0] & lc.mask, x1 = (g[0] + 1) & lc.mask;
+#pragma unroll
+    for (int c = 0; c < 8; c++) idx[c] = ((c & 1) ? x1 : x0) ^ hyz[c >> 1];
   }
 }
 

@@ -69,8 +69,9 @@ __device__ __forceinline__ void lookup_issue(const LevelConst& lc, const void* t
 #pragma unroll
   for (int d = 0; d < 3; d++) {
     const float pos = pin[d] * lc.scale + half_shift;
-    g[d] = (uint32_t)floorf(pos);
-    f[d] = pos - (float)g[d];
+    const float fl = floorf(pos);  // pos in (0, 2^24): the integer converts exactly
+    g[d] = (uint32_t)fl;
+    f[d] = pos - fl;
     if (interp == 1) f[d] = f[d] * f[d] * (3.0f - 2.0f * f[d]);
   }
   uint32_t idx[8];
