@@ -334,6 +334,10 @@ def run_ours(args):
     }
     if not args.no_train:
         line["train_step"] = train_step_timing(sc, cam, dev, steps=min(args.steps, 10))
+    if not args.no_multiview:
+        del fr
+        torch.cuda.empty_cache()
+        line["multiview"] = multiview_timing(world, rank, dev)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(sc, budget_s=args.cpu_budget)
     if rank == 0:
@@ -421,6 +425,63 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
+def multiview_timing(world, rank, dev, batches=2):
+    """a 64-view batch (1920x1080, 3M RVQ surfels, elevation
+    20 deg, azimuth 360 i / 64) split over the ranks by camera. Per batch: the
+    surfel-sharded RVQ decode and its all-gather once, then this rank's views.
+    Time per batch = max over ranks (CUDA events), strong scaling in the ranks."""
+    import torch
+    import torch.distributed as dist
+
+    from nest_b200 import raster, synth
+    from nest_b200.frame import FrameRenderer
+    from nest_b200.views import DecodeShard, camera_share
+
+    sc = synth.config3()
+    cams = synth.config3_cameras()
+    mine = camera_share(len(cams), world, rank)
+    fr = FrameRenderer(sc, device=dev, capacity=24_000_000)
+    if world > 1:
+        shard = DecodeShard.create(fr.rvq_idx, fr.dims, world, rank)
+        fr.decoded = shard.decoded
+    views = [(cams[i], cams[i].world_view_transform.to(dev).contiguous(),
+              cams[i].full_proj_transform.to(dev).contiguous()) for i in mine]
+
+    def batch():
+        if world > 1:
+            shard.decode_and_gather(fr.codebooks, raster.rvq_decode)
+        for k, (cam, v, pr) in enumerate(views):
+            fr.render(cam, v, pr, skip_decode=world > 1 or k > 0)
+
+    batch()  # warm-up; sizes the binning capacity
+    torch.cuda.synchronize()
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(batches)]
+    for s, e in evs:
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        s.record()
+        batch()
+        e.record()
+        torch.cuda.synchronize()
+    ms = [s.elapsed_time(e) for s, e in evs]
+    t = torch.tensor(ms, dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = t.tolist()
+    batch_ms = statistics.median(ms)
+    W, H = cams[0].width, cams[0].height
+    out = {"workload": "config 3: 3M RVQ surfels, 64 views 1920x1080 per batch, decode + all-gather once "
+                       "per batch, views split over the ranks",
+           "views": len(cams), "views_per_rank_max": -(-len(cams) // world), "batches": batches,
+           "ms_per_batch": round(batch_ms, 3), "views_per_s": round(len(cams) * 1000.0 / batch_ms, 3),
+           "mpix_per_s": round(len(cams) * W * H / 1e6 * 1000.0 / batch_ms, 3),
+           "instances_last_view": fr.num_rendered}
+    del fr
+    torch.cuda.empty_cache()
+    return out
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -429,6 +490,7 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-train", action="store_true", help="skip the config-4 training-step timing")
+    ap.add_argument("--no-multiview", action="store_true", help="skip the config-3 64-view batch timing")
     ap.add_argument("--cpu-budget", type=float, default=30.0)
     args = ap.parse_args()
     if args.impl == "reference":

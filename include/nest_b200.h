@@ -26,6 +26,11 @@
  *                            and CudaRasterizer::Rasterizer::backward,
  *                            rasterizer_impl.cu:444-592 (BACKWARD::render,
  *                            backward.cu:445-2052; BACKWARD::preprocess, :2216-2273)
+ *   ns_normal_error       <- the depth-normal term of the 2DGS training loss:
+ *                            gaussian_renderer/__init__.py:763-792 (allmap decode,
+ *                            depth_ratio 0), utils/point_utils.py:10-30,48-60
+ *                            (depths_to_points, depth_to_normal), train.py:674-675
+ *   ns_normal_error_backward <- torch autograd of the same expressions
  */
 #ifndef NEST_B200_H_
 #define NEST_B200_H_
@@ -267,6 +272,37 @@ int ns_render_frame(const ns_raster_settings* settings, const ns_frame_inputs* i
                     const ns_frame_outputs* outputs, void* geom, size_t geom_bytes,
                     void* binning, size_t binning_bytes, void* image, size_t image_bytes,
                     int64_t* num_rendered, int flags, void* stream);
+
+/* --------------------------------------------------------- normal error */
+
+/* Per-pixel depth-normal consistency error of the training loss, with the
+ * allmap decode fused in (allmap = out_others of the rasterizer, channels
+ * 0 = accumulated depth D, 1 = alpha, 2-4 = view-space normal):
+ *   depth(q)  = D(q) / alpha(q), non-finite -> 0 (+inf, NaN) or -FLT_MAX (-inf)
+ *   P(q)      = depth(q) * rays_d[q] + ray_o                        (world point)
+ *   surf(p)   = normalize(cross(P(x, y+1) - P(x, y-1), P(x+1, y) - P(x-1, y))) * alpha(p)
+ *               (eps 1e-12; zero on the one-pixel image border)
+ *   rend(p)   = R^T n_view(p), R = viewmatrix[:3,:3] (world-to-view rotation)
+ *   err[p]    = 1 - <rend(p), surf(p)>
+ * allmap fp32 [>=5, H, W]; viewmatrix fp32 [16] (device, the rasterizer's
+ * layout); rays_d fp32 [H*W, 3] (device: per-pixel ray direction, pixel y*W + x,
+ * as utils/point_utils.py:10-30 builds it); ray_o fp32 [3] (device); err fp32
+ * [H, W]. */
+int ns_normal_error(const float* allmap, const float* viewmatrix, const float* rays_d,
+                    const float* ray_o, int32_t width, int32_t height, float* err, void* stream);
+
+/* Scratch of ns_normal_error_backward: 6 floats per pixel. */
+size_t ns_normal_error_scratch_bytes(int32_t width, int32_t height);
+
+/* dL_dallmap[0:5] = d L / d allmap[0:5] given dL_derr (fp32, pixel p at
+ * dL_derr[p * derr_stride]; stride 0 broadcasts one value, e.g. the gradient
+ * of a mean). Channels 5 and up of dL_dallmap are not written. alpha enters
+ * through the depth only (surf uses alpha detached, as the reference does);
+ * pixels whose depth is not finite pass no gradient to D or alpha. */
+int ns_normal_error_backward(const float* allmap, const float* viewmatrix, const float* rays_d,
+                             const float* ray_o, int32_t width, int32_t height,
+                             const float* dL_derr, int64_t derr_stride, float* dL_dallmap,
+                             void* scratch, size_t scratch_bytes, void* stream);
 
 #ifdef __cplusplus
 }

@@ -413,6 +413,34 @@ int ns_mlp_forward(const float* feat, int32_t in_dims, int64_t npix, const uint1
                     reinterpret_cast<cudaStream_t>(stream));
 }
 
+int ns_normal_error(const float* allmap, const float* viewmatrix, const float* rays_d,
+                    const float* ray_o, int32_t width, int32_t height, float* err, void* stream) {
+  if (width < 0 || height < 0) return NS_ERR_INVALID;
+  if ((int64_t)width * height == 0) return NS_OK;
+  if (!allmap || !viewmatrix || !rays_d || !ray_o || !err) return NS_ERR_INVALID;
+  return normal_error_launch(allmap, viewmatrix, rays_d, ray_o, width, height, err,
+                             reinterpret_cast<cudaStream_t>(stream));
+}
+
+size_t ns_normal_error_scratch_bytes(int32_t width, int32_t height) {
+  if (width <= 0 || height <= 0) return 0;
+  return align_up((size_t)width * (size_t)height * 6 * sizeof(float));
+}
+
+int ns_normal_error_backward(const float* allmap, const float* viewmatrix, const float* rays_d,
+                             const float* ray_o, int32_t width, int32_t height,
+                             const float* dL_derr, int64_t derr_stride, float* dL_dallmap,
+                             void* scratch, size_t scratch_bytes, void* stream) {
+  if (width < 0 || height < 0 || derr_stride < 0) return NS_ERR_INVALID;
+  if ((int64_t)width * height == 0) return NS_OK;
+  if (!allmap || !viewmatrix || !rays_d || !ray_o || !dL_derr || !dL_dallmap || !scratch)
+    return NS_ERR_INVALID;
+  if (scratch_bytes < ns_normal_error_scratch_bytes(width, height)) return NS_ERR_SCRATCH;
+  return normal_error_backward_launch(allmap, viewmatrix, rays_d, ray_o, width, height, dL_derr,
+                                      derr_stride, dL_dallmap, static_cast<float*>(scratch),
+                                      reinterpret_cast<cudaStream_t>(stream));
+}
+
 int ns_rvq_decode(const uint8_t* idx, const float* codebooks, float* out, int64_t n,
                   int32_t stages, int32_t entries, int32_t dims, void* stream) {
   return rvq_decode_launch(idx, codebooks, out, n, stages, entries, dims,

@@ -241,6 +241,39 @@ def mlp_forward(feat_chw: torch.Tensor, packed_weights: torch.Tensor, alpha=None
     return rgb
 
 
+def normal_error(allmap: torch.Tensor, viewmatrix: torch.Tensor, rays_d: torch.Tensor,
+                 ray_o: torch.Tensor) -> torch.Tensor:
+    """Depth-normal consistency error [H, W] of the training loss (ns_normal_error):
+    1 - <world rendered normal, depth_to_normal(expected depth) * alpha>."""
+    lib = _lib.load()
+    _require_cuda(allmap, viewmatrix, rays_d, ray_o)
+    H, W = allmap.shape[1], allmap.shape[2]
+    err = torch.empty((H, W), dtype=torch.float32, device=allmap.device)
+    check("ns_normal_error", lib.ns_normal_error(ptr(allmap), ptr(viewmatrix), ptr(rays_d), ptr(ray_o), W, H,
+                                                 ptr(err), _lib.stream_handle(allmap.device)))
+    return err
+
+
+def normal_error_backward(allmap: torch.Tensor, viewmatrix: torch.Tensor, rays_d: torch.Tensor,
+                          ray_o: torch.Tensor, dL_derr: torch.Tensor) -> torch.Tensor:
+    """d loss / d allmap (all channels; 5 and up zero) from d loss / d err. dL_derr is
+    [H, W], or a broadcast view of one value (stride 0, as the gradient of a mean)."""
+    lib = _lib.load()
+    _require_cuda(allmap, viewmatrix, rays_d, ray_o)
+    H, W = allmap.shape[1], allmap.shape[2]
+    if dL_derr.numel() == 1 or all(st == 0 for st in dL_derr.stride()):
+        g, stride = dL_derr[(0,) * dL_derr.dim()].reshape(1).float().contiguous(), 0
+    else:
+        g, stride = dL_derr.reshape(H, W).float().contiguous(), 1
+    out = torch.empty_like(allmap)
+    out[5:].zero_()
+    scratch = torch.empty(lib.ns_normal_error_scratch_bytes(W, H), dtype=torch.uint8, device=allmap.device)
+    check("ns_normal_error_backward",
+          lib.ns_normal_error_backward(ptr(allmap), ptr(viewmatrix), ptr(rays_d), ptr(ray_o), W, H, ptr(g), stride,
+                                       ptr(out), ptr(scratch), scratch.numel(), _lib.stream_handle(allmap.device)))
+    return out
+
+
 def rvq_decode(idx: torch.Tensor, codebooks: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
     lib = _lib.load()
     _require_cuda(idx, codebooks)

@@ -2,9 +2,10 @@
 autograd around the library's kernels.
 
 Forward: the drop-in rasterizer (ns_rasterize_forward) -> the fp16 MLP
-(ns_mlp_forward) -> the losses. Backward: ns_rasterize_backward for the
-surfels and the hash table; the MLP's backward is four small GEMMs (torch /
-cuBLAS) on activations recomputed from the features.
+(ns_mlp_forward) -> the losses, the depth-normal term fused into one kernel
+(ns_normal_error). Backward: ns_normal_error_backward for that term,
+ns_rasterize_backward for the surfels and the hash table; the MLP's backward is
+four small GEMMs (torch / cuBLAS) on activations recomputed from the features.
 
 Restated from the reference: the allmap decode (gaussian_renderer/__init__.py
 :763-797: alpha, view-to-world normal, expected depth = depth / alpha with NaN
@@ -141,12 +142,39 @@ def decode_allmap(allmap, cam):
     return alpha, rend_normal, surf_normal, depth
 
 
+class _NormalError(torch.autograd.Function):
+    """normal_error [H, W] of train.py:674 from the allmap, on the library's kernels."""
+
+    @staticmethod
+    def forward(ctx, allmap, viewmatrix, rays_d, ray_o):
+        allmap = allmap.detach().contiguous()
+        ctx.save_for_backward(allmap, viewmatrix, rays_d, ray_o)
+        return raster.normal_error(allmap, viewmatrix, rays_d, ray_o)
+
+    @staticmethod
+    def backward(ctx, gerr):
+        allmap, viewmatrix, rays_d, ray_o = ctx.saved_tensors
+        return raster.normal_error_backward(allmap, viewmatrix, rays_d, ray_o, gerr), None, None, None
+
+
+def normal_error(allmap, cam):
+    """1 - sum_c rend_normal * surf_normal per pixel ([H, W]); differentiable in allmap."""
+    dev = allmap.device
+    rays_d, rays_o = _camera_rays(cam, dev)
+    vm = cam.world_view_transform.to(dev).float().contiguous()
+    return _NormalError.apply(allmap, vm, rays_d.contiguous(), rays_o.contiguous())
+
+
+def normal_error_torch(allmap, cam):
+    """The same error from the torch restatement (decode_allmap), for comparison."""
+    _, rend_normal, surf_normal, _ = decode_allmap(allmap, cam)
+    return 1 - (rend_normal * surf_normal).sum(dim=0)
+
+
 def config4_loss(rgb, allmap, cam, target, lambda_normal=0.05):
     """train.py:651, 674-675 with lambda_dssim 0: L1 + lambda_normal * normal error."""
-    _, rend_normal, surf_normal, _ = decode_allmap(allmap, cam)
     l1 = (rgb - target).abs().mean()
-    normal_error = (1 - (rend_normal * surf_normal).sum(dim=0))[None]
-    return l1 + lambda_normal * normal_error.mean()
+    return l1 + lambda_normal * normal_error(allmap, cam).mean()
 
 
 @dataclass

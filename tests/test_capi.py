@@ -74,6 +74,8 @@ def test_status_strings_and_scratch_sizes():
     assert b > a >= 1000 * 36
     assert lib.ns_radix_sort_temp_bytes(1 << 20) > 0
     assert lib.ns_backward_scratch_bytes(1000) >= 1000 * 18 * 4
+    assert lib.ns_normal_error_scratch_bytes(64, 48) >= 64 * 48 * 6 * 4
+    assert lib.ns_normal_error_scratch_bytes(0, 48) == 0
 
 
 def test_invalid_arguments_return_status_without_launching():
@@ -100,6 +102,14 @@ def test_invalid_arguments_return_status_without_launching():
     gi, go = _lib.GradsIn(), _lib.GradsOut()  # null gradient buffers
     assert lib.ns_rasterize_backward(C.byref(s), C.byref(surf), C.byref(gi), C.byref(go), None, 0, None, 0,
                                      None, 0, 0, None, 0, None) == _lib.NS_ERR_INVALID
+    p = 1 << 20  # never dereferenced: every call below fails validation first
+    assert lib.ns_normal_error(None, p, p, p, 4, 4, p, None) == _lib.NS_ERR_INVALID
+    assert lib.ns_normal_error(p, p, p, p, -1, 4, p, None) == _lib.NS_ERR_INVALID
+    assert lib.ns_normal_error(None, None, None, None, 0, 7, None, None) == _lib.NS_OK
+    sb = lib.ns_normal_error_scratch_bytes(4, 4)
+    assert lib.ns_normal_error_backward(p, p, p, p, 4, 4, p, -1, p, p, sb, None) == _lib.NS_ERR_INVALID
+    assert lib.ns_normal_error_backward(p, p, p, p, 4, 4, p, 0, p, None, sb, None) == _lib.NS_ERR_INVALID
+    assert lib.ns_normal_error_backward(p, p, p, p, 4, 4, p, 0, p, p, sb - 1, None) == _lib.NS_ERR_SCRATCH
 
 
 def test_python_api_surface_matches_reference():
