@@ -20,7 +20,9 @@ def test_rvq_config0_bit_exact(n):
 @pytest.mark.parametrize("n,K,E,D", [(1, 6, 256, 59), (511, 6, 256, 59), (513, 6, 256, 59),
                                      (100_003, 6, 256, 59), (4097, 1, 256, 59), (3000, 6, 16, 17),
                                      (3000, 4, 256, 32), (3000, 6, 256, 64), (3000, 8, 256, 59),
-                                     (2000, 3, 100, 33)])
+                                     (2000, 3, 100, 33), (3001, 2, 256, 48), (2999, 5, 256, 40),
+                                     (1000, 7, 64, 59), (128, 6, 256, 59), (129 * 128 + 3, 6, 256, 59),
+                                     ((1 << 20) + 5, 6, 256, 59)])
 def test_rvq_shapes_bit_exact(n, K, E, D):
     g = torch.Generator().manual_seed(n + K + E + D)
     cb = torch.randn(K, E, D, generator=g)
@@ -28,6 +30,19 @@ def test_rvq_shapes_bit_exact(n, K, E, D):
     out = raster.rvq_decode(idx.cuda(), cb.cuda()).cpu().numpy()
     ref = oracle.rvq_decode_np(idx.numpy(), cb.numpy())
     assert np.array_equal(out.view(np.uint32), ref.view(np.uint32))
+
+
+def test_rvq_unaligned_output():
+    # an output 4 bytes past a 16-byte boundary: rows are written without the bulk copies
+    g = torch.Generator().manual_seed(12)
+    cb = torch.randn(6, 256, 59, generator=g)
+    idx = torch.randint(0, 256, (20_000, 6), generator=g).to(torch.uint8)
+    buf = torch.full((20_000 * 59 + 4,), -1.0, device="cuda")
+    out = buf[1:1 + 20_000 * 59].view(20_000, 59)
+    raster.rvq_decode(idx.cuda(), cb.cuda(), out=out)
+    ref = oracle.rvq_decode_np(idx.numpy(), cb.numpy())
+    assert np.array_equal(out.cpu().numpy().view(np.uint32), ref.view(np.uint32))
+    assert float(buf[0]) == -1.0 and torch.all(buf[1 + 20_000 * 59:] == -1.0)
 
 
 def test_rvq_unaligned_index_view():
