@@ -225,6 +225,7 @@ int bin_and_render(const ns_raster_settings* st, int P, const GeomState& g, cons
   rp.n_contrib = im.n_contrib;
   rp.cover_pixels = cover_pixels;
   rp.trans_avg = trans_avg;
+  rp.err = g.err;
   if (ev) NS_CUDA_TRY(cudaEventRecord((cudaEvent_t)ev[6], stream));
   rc = render_launch(rp, st->table_fp16, stream);
   if (rc) return rc;

@@ -29,6 +29,7 @@ struct RenderParams {
   uint32_t* n_contrib;
   float* cover_pixels;
   float* trans_avg;
+  uint32_t* err;  // device status word (kErr* bits)
 };
 struct BackwardParams {
   int W, H;

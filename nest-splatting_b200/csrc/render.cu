@@ -9,9 +9,11 @@
 //   (:1945-1957), transmittance record (:1961-1964), outputs (:2008-2048).
 //
 // One CTA of 256 threads per 16x16 tile, one thread per pixel; warp w owns tile
-// rows 2w and 2w+1. Batches of up to 256 surfel records are gathered into shared
-// memory with cp.async. Each warp then alternates, on its own 32 pixels and
-// without CTA-wide barriers, between two phases:
+// rows 2w and 2w+1. The tile's surfel records stream through a ring of four
+// 64-record slots in shared memory (cp.async, completion on an mbarrier per
+// slot); the last warp to finish a batch refills its slot, so warps never meet
+// at a CTA barrier and drift up to three batches apart. Each warp alternates,
+// on its own 32 pixels, between two phases:
 //
 //   Phase A (intersect). The warp walks the batch in the reference's
 //   front-to-back order, all lanes at the same position (a warp-uniform skip
@@ -21,7 +23,8 @@
 //   1e-4, depth >= near, max_intersections), keeps the auxiliary maps in
 //   registers and appends each blended sample (hit point mapped to [0,1]^3,
 //   weight, number of levels to query) to its pixel's queue in shared memory.
-//   The warp stops when one of its queues is full or the batch is done.
+//   The warp stops when one of its queues is full; queues carry over between
+//   batches.
 //
 //   Phase B (hash lookups). The warp's queued samples are compacted into one
 //   k-major list (every pixel's sample k, then k+1, ...) so all 32 lanes look up
@@ -42,11 +45,13 @@ namespace {
 constexpr int kThreads = kTilePixels;  // 256: one pixel per thread
 constexpr int kQueue = 8;              // queued samples per pixel between drains
 constexpr int kWarps = kThreads / 32;
+constexpr int kBatch = 64;             // surfel records per ring slot
+constexpr int kSlots = 4;              // ring slots (batches in flight)
 constexpr int kChunk = 64;             // compacted samples looked up per warp step (2 per lane)
 constexpr int kMaxChannels = 32;
 
 struct BlendSmem {
-  float4 rec[kThreads][kRecordFloat4];  // surfel records of the current batch
+  float4 rec[kSlots][kBatch][kRecordFloat4];  // ring of surfel-record batches
   float4 samp[kQueue][kThreads];        // (hit point in [0,1]^3, weight)
   uint8_t lvl[kQueue][kThreads];        // levels to query for the sample (0: none)
   uint8_t item[kWarps][kThreads];       // per warp: queued samples in k-major order, (k << 5) | lane
@@ -54,6 +59,9 @@ struct BlendSmem {
   float4 res[kWarps][kChunk];           // lookups of the current chunk: level l (xy), l+1 (zw)
   float acc[kThreads * kAccStride];     // feature accumulators, see acc_pair()
   LevelConst lv[kMaxLevels];
+  uint64_t full[kSlots];                // slot filled (32 cp.async arrivals per fill)
+  int used[kSlots];                     // warps done with the slot's current batch
+  int ndone;                            // warps whose pixels are all done
 };
 
 // Trilinear lookup of one level at a point of [0,1]^3 (hashgrid.h:140-193),
@@ -97,6 +105,26 @@ __device__ __forceinline__ float2 lookup_finish(const float (&f)[3], const Corne
   return r;
 }
 
+// Bounded wait for ring slot s to hold its batch of parity `parity`. Returns 1
+// when it does, 0 when every warp of the tile is done (nothing left to wait
+// for), -1 when the spin limit runs out.
+__device__ __forceinline__ int wait_slot(BlendSmem& S, int s, uint32_t parity) {
+  const unsigned bar = (unsigned)__cvta_generic_to_shared(&S.full[s]);
+  for (uint32_t spins = 0; spins < kSpinLimit; spins++) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    if (ok) return 1;
+    if (*(volatile int*)&S.ndone == kWarps) return 0;
+  }
+  return -1;
+}
+
 template <typename TableT>
 __global__ void __launch_bounds__(kThreads, 2) blend_kernel(const RenderParams p) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
@@ -116,10 +144,16 @@ __global__ void __launch_bounds__(kThreads, 2) blend_kernel(const RenderParams p
 
   if (t < (int)L) S.lv[t] = make_level<TableT>(p.table, p.offsets, p.S, p.Hres, p.align_corners, t);
   for (int c = 0; c < kAccStride; c++) S.acc[t * kAccStride + c] = 0.f;  // only this thread's row
+  if (t < kSlots) {
+    const unsigned bar = (unsigned)__cvta_generic_to_shared(&S.full[t]);
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], 32;" ::"r"(bar) : "memory");
+    S.used[t] = 0;
+  }
+  if (t == 0) S.ndone = 0;
 
   const uint2 range = p.ranges[tile];
   const int total = (int)(range.y - range.x);
-  const int rounds = div_up(total, kThreads);
+  const int rounds = div_up(total, kBatch);
   const float vmin = p.gridrange[0], vmax = p.gridrange[1];
 
   float T = 1.0f;
@@ -129,241 +163,279 @@ __global__ void __launch_bounds__(kThreads, 2) blend_kernel(const RenderParams p
   float pos0 = 0, pos1 = 0, pos2 = 0, vis0 = 0, vis1 = 0;
   bool done = !inside;
 
-  auto fetch = [&](int round) {
-    const int k = round * kThreads + t;
-    if (k < total) {
-      const uint32_t id = p.point_list[range.x + k];
-      const float4* src = reinterpret_cast<const float4*>(p.records + id);
+  // Record ring: slot s holds batch b (b % kSlots == s). Warp w < kSlots fills
+  // batch w; after that the last warp to finish batch b refills its slot with
+  // batch b + kSlots, so warps drift up to kSlots - 1 batches apart instead of
+  // meeting at a CTA barrier per batch. Each lane of the filling warp copies two
+  // records and arrives on full[s] when its copies have landed.
+  const int lane = t & 31, wid = t >> 5, pbase = wid * 32;
+  auto fetch = [&](int b) {
+    const int s = b & (kSlots - 1);
 #pragma unroll
-      for (int q = 0; q < kRecordFloat4; q++) {
-        const unsigned dst = (unsigned)__cvta_generic_to_shared(&S.rec[t][q]);
-        asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src + q));
+    for (int h = 0; h < kBatch / 32; h++) {
+      const int jj = h * 32 + lane;
+      const int k = b * kBatch + jj;
+      if (k < total) {
+        const uint32_t id = p.point_list[range.x + k];
+        const float4* src = reinterpret_cast<const float4*>(p.records + id);
+#pragma unroll
+        for (int q = 0; q < kRecordFloat4; q++) {
+          const unsigned dst = (unsigned)__cvta_generic_to_shared(&S.rec[s][jj][q]);
+          asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src + q));
+        }
       }
     }
-    asm volatile("cp.async.commit_group;");
+    const unsigned bar = (unsigned)__cvta_generic_to_shared(&S.full[s]);
+    asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(bar) : "memory");
   };
 
-  if (rounds > 0) fetch(0);
-  for (int r = 0; r < rounds; r++) {
-    asm volatile("cp.async.wait_group 0;");
-    // End when the whole tile is done (forward.cu:791-796); the barrier also
-    // publishes the batch copied into S.rec (and, first time, the level table).
-    if (__syncthreads_count(done) == kThreads) break;
-    const int todo = min(kThreads, total - r * kThreads);
-    int j = 0;
-    while (true) {
-      // ---------------- phase A: intersect, composite aux maps, queue samples.
-      // Warp-synchronous walk: all lanes share `j`; votes only at the loop head.
-      int cnt = 0;
-      while (j < todo) {
-        const bool active = !done;
-        if (!__any_sync(0xffffffffu, active)) break;
-        if (__any_sync(0xffffffffu, cnt == kQueue)) break;
-        const int jj = j++;
-        if (active) contributor++;
-        // Outside the surfel's alpha >= 1/255 box the reference would reach
-        // `alpha < 1/255 -> continue` (or an earlier continue): skip the math,
-        // for the whole warp when no lane is inside.
-        const float4 box = S.rec[jj][0];
-        const bool cand = active && !(pxf < box.x || pxf > box.y || pyf < box.z || pyf > box.w);
-        if (!__any_sync(0xffffffffu, cand)) continue;
-        if (!cand) continue;
-        const float4 q0 = S.rec[jj][1], q1 = S.rec[jj][2], q2 = S.rec[jj][3];
-        const float3 Tu = f3(q0.x, q0.y, q0.z), Tv = f3(q0.w, q1.x, q1.y), Tw = f3(q1.z, q1.w, q2.x);
-        const float3 kk = pxf * Tw - Tu;
-        const float3 ll = pyf * Tw - Tv;
-        const float3 pp = cross3(kk, ll);
-        const float dx = q2.y - pxf, dy = q2.z - pyf;
-        const float rho2d = kFilterInvSquare * (dx * dx + dy * dy);
-        // Division-free pre-test: rho3d = |p.xy|^2 / p.z^2 and rho2d both above the
-        // surfel's (margined) alpha cutoff means alpha < 1/255 on the reference path.
-        const float rho_cut = S.rec[jj][7].y;
-        if (pp.x * pp.x + pp.y * pp.y > rho_cut * (pp.z * pp.z) && rho2d > rho_cut) continue;
-        if (pp.z == 0.0f) continue;
-        const float sx = pp.x / pp.z, sy = pp.y / pp.z;
-        const float rho3d = sx * sx + sy * sy;
-        const float rho = fminf(rho3d, rho2d);
-        const bool on_plane = rho3d <= rho2d;
-        const float depth = on_plane ? (sx * Tw.x + sy * Tw.y) + Tw.z : Tw.z;
-        if (depth < kNear) continue;
-        const float power = -0.5f * rho;
-        if (power > 0.0f) continue;
-        float G = expf(power);
-        if (p.beta > 0.0f) G = (float)((1.0 + (double)p.beta) * G / (1.0 + (double)p.beta * G));
-        const float alpha = fminf(0.99f, q2.w * G);
-        if (alpha < 1.0f / 255.0f) continue;
-        const float test_T = T * (1 - alpha);
-        if (test_T < 0.0001f) {
-          done = true;
-          continue;
-        }
-        const float w = alpha * T;
-        render_number++;
-        if (p.max_intersections > 0 && render_number >= p.max_intersections) done = true;
-
-        const float A = 1 - T;
-        const float m = kFar / (kFar - kNear) * (1 - kNear / depth);
-        distortion += (m * m * A + M2 - 2 * m * M1) * w;
-        D += depth * w;
-        M1 += m * w;
-        M2 += m * m * w;
-        if (T > 0.5f) {
-          median_depth = depth;
-          median_contributor = (float)contributor;
-        }
-        const float4 q3 = S.rec[jj][4];
-        N0 += q3.x * w;
-        N1 += q3.y * w;
-        N2 += q3.z * w;
-
-        const float4 q4 = S.rec[jj][5], q5 = S.rec[jj][6], q6 = S.rec[jj][7];
-        float3 xyz;
-        if (on_plane) {
-          xyz = f3(sx * q4.x + sy * q4.w + q5.z, sx * q4.y + sy * q5.x + q5.w,
-                   sx * q4.z + sy * q5.y + q6.x);
-        } else {
-          xyz = f3(q5.z, q5.w, q6.x);
-        }
-        pos0 += w * xyz.x;
-        pos1 += w * xyz.y;
-        pos2 += w * xyz.z;
-
-        // query_feature's mapping of the hit point to [0,1]^3 (hashgrid.h:63-114).
-        const uint32_t apl = __float_as_uint(q3.w);
-        float in0, in1, in2;
-        bool oob = false;
-        if (!p.contract) {
-          const float inv = 1.0f / (vmax - vmin);
-          in0 = (xyz.x - vmin) * inv;
-          in1 = (xyz.y - vmin) * inv;
-          in2 = (xyz.z - vmin) * inv;
-          oob = in0 < 0 || in0 > 1 || in1 < 0 || in1 > 1 || in2 < 0 || in2 > 1;
-        } else {
-          const float vmid = (vmax + vmin) * 0.5f;
-          const float inv = 1.0f / ((vmax - vmin) * 0.5f);
-          in0 = (xyz.x - vmid) * inv;
-          in1 = (xyz.y - vmid) * inv;
-          in2 = (xyz.z - vmid) * inv;
-          const float nrm = sqrtf(in0 * in0 + in1 * in1 + in2 * in2);
-          const float inv_n = 1.0f / nrm;
-          const float st = (nrm <= 1.0f) ? 1.0f : (2.0f - inv_n) * inv_n;
-          in0 = (st * in0 + 2.0f) * 0.25f;
-          in1 = (st * in1 + 2.0f) * 0.25f;
-          in2 = (st * in2 + 2.0f) * 0.25f;
-        }
-        S.samp[cnt][t] = make_float4(in0, in1, in2, w);
-        S.lvl[cnt][t] = (uint8_t)(oob ? 0u : min(apl, L));
-        cnt++;
-
-        float ac0, ac1;
-        if (apl <= 4) {
-          ac0 = (float)((apl - 2) * 0.5);
-          ac1 = 1.0f;
-        } else {
-          ac0 = 1.0f;
-          ac1 = (float)(1.0 - (apl - 4) * 0.5);
-        }
-        vis0 += ac0 * w;
-        vis1 += ac1 * w;
-        if (p.record_transmittance) {
-          const uint32_t id = p.point_list[range.x + r * kThreads + jj];
-          atomicAdd(p.cover_pixels + id, 1.0f);
-          atomicAdd(p.trans_avg + id, T);
-        }
-        T = test_T;
-        last_contributor = contributor;
-      }
-
-      // ---------------- phase B: this warp's hash lookups. Each lane reads
-      // only its own queue and accumulator row, so no synchronisation is needed.
-      const int kmax = __reduce_max_sync(0xffffffffu, cnt);
-      if (kmax > 0) {
-        // Compact the warp's queued samples into one k-major list (sample k of
-        // every pixel that has one, then k+1, ...), so all 32 lanes look up real
-        // samples; neighbouring pixels' k-th samples stay adjacent (coalescing).
-        const int lane = t & 31, wid = t >> 5, pbase = wid * 32;
-        const uint32_t lt = lane_mask_lt();
-        int nitems = 0;
+  int cnt = 0;  // this pixel's queued samples (kept across batches)
+  // Phase B: the warp's queued hash lookups (see the file comment); empties
+  // every queue of the warp.
+  auto drain = [&]() {
+    if (!__any_sync(0xffffffffu, cnt > 0)) return;
+    // Compact the warp's queued samples into one k-major list (sample k of
+    // every pixel that has one, then k+1, ...), so all 32 lanes look up real
+    // samples; neighbouring pixels' k-th samples stay adjacent (coalescing).
+    const uint32_t lt = lane_mask_lt();
+    int nitems = 0;
 #pragma unroll
-        for (int k = 0; k < kQueue; k++) {
-          const uint32_t m = __ballot_sync(0xffffffffu, cnt > k);
-          if (cnt > k) {
-            const int ps = nitems + __popc(m & lt);
-            S.item[wid][ps] = (uint8_t)((k << 5) | lane);
-            S.pos[k][t] = (uint8_t)ps;
-          }
-          nitems += __popc(m);
+    for (int k = 0; k < kQueue; k++) {
+      const uint32_t m = __ballot_sync(0xffffffffu, cnt > k);
+      if (cnt > k) {
+        const int ps = nitems + __popc(m & lt);
+        S.item[wid][ps] = (uint8_t)((k << 5) | lane);
+        S.pos[k][t] = (uint8_t)ps;
+      }
+      nitems += __popc(m);
+    }
+    __syncwarp();
+    // Two levels per pass, 64 list entries (two per lane) per step: four
+    // lookups in flight per lane. Each pixel's owner lane then adds its own
+    // results from the step, in sample order.
+    for (uint32_t l = 0; l < L; l += 2) {
+      const bool has1 = l + 1 < L;
+      const LevelConst lc0 = S.lv[l];
+      const LevelConst lc1 = S.lv[has1 ? l + 1 : l];
+      float2* ap0 = acc_pair(S.acc, t, l);
+      float2* ap1 = acc_pair(S.acc, t, has1 ? l + 1 : l);
+      float2 c0 = *ap0;
+      float2 c1 = has1 ? *ap1 : make_float2(0.f, 0.f);
+      int nk = 0;
+      for (int ch = 0; ch < nitems; ch += kChunk) {
+        float4 sa = make_float4(0.f, 0.f, 0.f, 0.f), sb = sa;
+        uint32_t ma = 0, mb = 0;
+        const int ia = ch + lane, ib = ch + 32 + lane;
+        if (ia < nitems) {
+          const uint32_t tb = S.item[wid][ia];
+          const int pp = pbase + (int)(tb & 31u), k = (int)(tb >> 5);
+          sa = S.samp[k][pp];
+          ma = S.lvl[k][pp];
+        }
+        if (ib < nitems) {
+          const uint32_t tb = S.item[wid][ib];
+          const int pp = pbase + (int)(tb & 31u), k = (int)(tb >> 5);
+          sb = S.samp[k][pp];
+          mb = S.lvl[k][pp];
+        }
+        const bool ua0 = l < ma, ub0 = l < mb, ua1 = has1 && l + 1 < ma, ub1 = has1 && l + 1 < mb;
+        float fa0[3], fb0[3], fa1[3], fb1[3];
+        Corner8<TableT> va0, vb0, va1, vb1;
+        if (ua0) lookup_issue<TableT>(lc0, p.table, sa, half_shift, p.interp, fa0, va0);
+        if (ub0) lookup_issue<TableT>(lc0, p.table, sb, half_shift, p.interp, fb0, vb0);
+        if (ua1) lookup_issue<TableT>(lc1, p.table, sa, half_shift, p.interp, fa1, va1);
+        if (ub1) lookup_issue<TableT>(lc1, p.table, sb, half_shift, p.interp, fb1, vb1);
+        const float2 z = make_float2(0.f, 0.f);
+        const float2 ra0 = ua0 ? lookup_finish<TableT>(fa0, va0) : z;
+        const float2 rb0 = ub0 ? lookup_finish<TableT>(fb0, vb0) : z;
+        const float2 ra1 = ua1 ? lookup_finish<TableT>(fa1, va1) : z;
+        const float2 rb1 = ub1 ? lookup_finish<TableT>(fb1, vb1) : z;
+        S.res[wid][lane] = make_float4(ra0.x, ra0.y, ra1.x, ra1.y);
+        S.res[wid][32 + lane] = make_float4(rb0.x, rb0.y, rb1.x, rb1.y);
+        __syncwarp();
+        while (nk < cnt) {
+          const int ps = S.pos[nk][t];
+          if (ps >= ch + kChunk) break;
+          const float4 rv = S.res[wid][ps - ch];
+          const uint32_t mk = S.lvl[nk][t];
+          const float w = S.samp[nk][t].w;
+          const float2 ww = make_float2(w, w);
+          if (l < mk) c0 = __ffma2_rn(make_float2(rv.x, rv.y), ww, c0);
+          if (has1 && l + 1 < mk) c1 = __ffma2_rn(make_float2(rv.z, rv.w), ww, c1);
+          nk++;
         }
         __syncwarp();
-        // Two levels per pass, 64 list entries (two per lane) per step: four
-        // lookups in flight per lane. Each pixel's owner lane then adds its own
-        // results from the step, in sample order.
-        for (uint32_t l = 0; l < L; l += 2) {
-          const bool has1 = l + 1 < L;
-          const LevelConst lc0 = S.lv[l];
-          const LevelConst lc1 = S.lv[has1 ? l + 1 : l];
-          float2* ap0 = acc_pair(S.acc, t, l);
-          float2* ap1 = acc_pair(S.acc, t, has1 ? l + 1 : l);
-          float2 c0 = *ap0;
-          float2 c1 = has1 ? *ap1 : make_float2(0.f, 0.f);
-          int nk = 0;
-          for (int ch = 0; ch < nitems; ch += kChunk) {
-            float4 sa = make_float4(0.f, 0.f, 0.f, 0.f), sb = sa;
-            uint32_t ma = 0, mb = 0;
-            const int ia = ch + lane, ib = ch + 32 + lane;
-            if (ia < nitems) {
-              const uint32_t tb = S.item[wid][ia];
-              const int pp = pbase + (int)(tb & 31u), k = (int)(tb >> 5);
-              sa = S.samp[k][pp];
-              ma = S.lvl[k][pp];
-            }
-            if (ib < nitems) {
-              const uint32_t tb = S.item[wid][ib];
-              const int pp = pbase + (int)(tb & 31u), k = (int)(tb >> 5);
-              sb = S.samp[k][pp];
-              mb = S.lvl[k][pp];
-            }
-            const bool ua0 = l < ma, ub0 = l < mb, ua1 = has1 && l + 1 < ma, ub1 = has1 && l + 1 < mb;
-            float fa0[3], fb0[3], fa1[3], fb1[3];
-            Corner8<TableT> va0, vb0, va1, vb1;
-            if (ua0) lookup_issue<TableT>(lc0, p.table, sa, half_shift, p.interp, fa0, va0);
-            if (ub0) lookup_issue<TableT>(lc0, p.table, sb, half_shift, p.interp, fb0, vb0);
-            if (ua1) lookup_issue<TableT>(lc1, p.table, sa, half_shift, p.interp, fa1, va1);
-            if (ub1) lookup_issue<TableT>(lc1, p.table, sb, half_shift, p.interp, fb1, vb1);
-            const float2 z = make_float2(0.f, 0.f);
-            const float2 ra0 = ua0 ? lookup_finish<TableT>(fa0, va0) : z;
-            const float2 rb0 = ub0 ? lookup_finish<TableT>(fb0, vb0) : z;
-            const float2 ra1 = ua1 ? lookup_finish<TableT>(fa1, va1) : z;
-            const float2 rb1 = ub1 ? lookup_finish<TableT>(fb1, vb1) : z;
-            S.res[wid][lane] = make_float4(ra0.x, ra0.y, ra1.x, ra1.y);
-            S.res[wid][32 + lane] = make_float4(rb0.x, rb0.y, rb1.x, rb1.y);
-            __syncwarp();
-            while (nk < cnt) {
-              const int ps = S.pos[nk][t];
-              if (ps >= ch + kChunk) break;
-              const float4 rv = S.res[wid][ps - ch];
-              const uint32_t mk = S.lvl[nk][t];
-              const float w = S.samp[nk][t].w;
-              const float2 ww = make_float2(w, w);
-              if (l < mk) c0 = __ffma2_rn(make_float2(rv.x, rv.y), ww, c0);
-              if (has1 && l + 1 < mk) c1 = __ffma2_rn(make_float2(rv.z, rv.w), ww, c1);
-              nk++;
-            }
-            __syncwarp();
+      }
+      *ap0 = c0;
+      if (has1) *ap1 = c1;
+    }
+    __syncwarp();
+    cnt = 0;
+  };
+
+  __syncthreads();  // level table, accumulators and ring barriers are initialised
+  if (wid < kSlots && wid < rounds) fetch(wid);
+  bool wdone = !__any_sync(0xffffffffu, !done);
+  if (wdone && lane == 0) atomicAdd(&S.ndone, 1);
+  for (int b = 0; b < rounds; b++) {
+    const int s = b & (kSlots - 1);
+    const int ws = wait_slot(S, s, (uint32_t)(b / kSlots) & 1u);
+    if (ws <= 0) {
+      if (ws < 0) set_error(p.err, kErrSpinTimeout);
+      break;
+    }
+    if (!wdone) {
+      const int todo = min(kBatch, total - b * kBatch);
+      int j = 0;
+      while (true) {
+        // ---------------- phase A: intersect, composite aux maps, queue samples.
+        // Warp-synchronous walk: all lanes share `j`; votes only at the loop head.
+        while (j < todo) {
+          const bool active = !done;
+          if (!__any_sync(0xffffffffu, active)) break;
+          if (__any_sync(0xffffffffu, cnt == kQueue)) break;
+          const int jj = j++;
+          if (active) contributor++;
+          // Outside the surfel's alpha >= 1/255 box the reference would reach
+          // `alpha < 1/255 -> continue` (or an earlier continue): skip the math,
+          // for the whole warp when no lane is inside.
+          const float4 box = S.rec[s][jj][0];
+          const bool cand = active && !(pxf < box.x || pxf > box.y || pyf < box.z || pyf > box.w);
+          if (!__any_sync(0xffffffffu, cand)) continue;
+          if (!cand) continue;
+          const float4 q0 = S.rec[s][jj][1], q1 = S.rec[s][jj][2], q2 = S.rec[s][jj][3];
+          const float3 Tu = f3(q0.x, q0.y, q0.z), Tv = f3(q0.w, q1.x, q1.y), Tw = f3(q1.z, q1.w, q2.x);
+          const float3 kk = pxf * Tw - Tu;
+          const float3 ll = pyf * Tw - Tv;
+          const float3 pp = cross3(kk, ll);
+          const float dx = q2.y - pxf, dy = q2.z - pyf;
+          const float rho2d = kFilterInvSquare * (dx * dx + dy * dy);
+          // Division-free pre-test: rho3d = |p.xy|^2 / p.z^2 and rho2d both above the
+          // surfel's (margined) alpha cutoff means alpha < 1/255 on the reference path.
+          const float rho_cut = S.rec[s][jj][7].y;
+          if (pp.x * pp.x + pp.y * pp.y > rho_cut * (pp.z * pp.z) && rho2d > rho_cut) continue;
+          if (pp.z == 0.0f) continue;
+          const float sx = pp.x / pp.z, sy = pp.y / pp.z;
+          const float rho3d = sx * sx + sy * sy;
+          const float rho = fminf(rho3d, rho2d);
+          const bool on_plane = rho3d <= rho2d;
+          const float depth = on_plane ? (sx * Tw.x + sy * Tw.y) + Tw.z : Tw.z;
+          if (depth < kNear) continue;
+          const float power = -0.5f * rho;
+          if (power > 0.0f) continue;
+          float G = expf(power);
+          if (p.beta > 0.0f) G = (float)((1.0 + (double)p.beta) * G / (1.0 + (double)p.beta * G));
+          const float alpha = fminf(0.99f, q2.w * G);
+          if (alpha < 1.0f / 255.0f) continue;
+          const float test_T = T * (1 - alpha);
+          if (test_T < 0.0001f) {
+            done = true;
+            continue;
           }
-          *ap0 = c0;
-          if (has1) *ap1 = c1;
+          const float w = alpha * T;
+          render_number++;
+          if (p.max_intersections > 0 && render_number >= p.max_intersections) done = true;
+
+          const float A = 1 - T;
+          const float m = kFar / (kFar - kNear) * (1 - kNear / depth);
+          distortion += (m * m * A + M2 - 2 * m * M1) * w;
+          D += depth * w;
+          M1 += m * w;
+          M2 += m * m * w;
+          if (T > 0.5f) {
+            median_depth = depth;
+            median_contributor = (float)contributor;
+          }
+          const float4 q3 = S.rec[s][jj][4];
+          N0 += q3.x * w;
+          N1 += q3.y * w;
+          N2 += q3.z * w;
+
+          const float4 q4 = S.rec[s][jj][5], q5 = S.rec[s][jj][6], q6 = S.rec[s][jj][7];
+          float3 xyz;
+          if (on_plane) {
+            xyz = f3(sx * q4.x + sy * q4.w + q5.z, sx * q4.y + sy * q5.x + q5.w,
+                     sx * q4.z + sy * q5.y + q6.x);
+          } else {
+            xyz = f3(q5.z, q5.w, q6.x);
+          }
+          pos0 += w * xyz.x;
+          pos1 += w * xyz.y;
+          pos2 += w * xyz.z;
+
+          // query_feature's mapping of the hit point to [0,1]^3 (hashgrid.h:63-114).
+          const uint32_t apl = __float_as_uint(q3.w);
+          float in0, in1, in2;
+          bool oob = false;
+          if (!p.contract) {
+            const float inv = 1.0f / (vmax - vmin);
+            in0 = (xyz.x - vmin) * inv;
+            in1 = (xyz.y - vmin) * inv;
+            in2 = (xyz.z - vmin) * inv;
+            oob = in0 < 0 || in0 > 1 || in1 < 0 || in1 > 1 || in2 < 0 || in2 > 1;
+          } else {
+            const float vmid = (vmax + vmin) * 0.5f;
+            const float inv = 1.0f / ((vmax - vmin) * 0.5f);
+            in0 = (xyz.x - vmid) * inv;
+            in1 = (xyz.y - vmid) * inv;
+            in2 = (xyz.z - vmid) * inv;
+            const float nrm = sqrtf(in0 * in0 + in1 * in1 + in2 * in2);
+            const float inv_n = 1.0f / nrm;
+            const float st = (nrm <= 1.0f) ? 1.0f : (2.0f - inv_n) * inv_n;
+            in0 = (st * in0 + 2.0f) * 0.25f;
+            in1 = (st * in1 + 2.0f) * 0.25f;
+            in2 = (st * in2 + 2.0f) * 0.25f;
+          }
+          S.samp[cnt][t] = make_float4(in0, in1, in2, w);
+          S.lvl[cnt][t] = (uint8_t)(oob ? 0u : min(apl, L));
+          cnt++;
+
+          float ac0, ac1;
+          if (apl <= 4) {
+            ac0 = (float)((apl - 2) * 0.5);
+            ac1 = 1.0f;
+          } else {
+            ac0 = 1.0f;
+            ac1 = (float)(1.0 - (apl - 4) * 0.5);
+          }
+          vis0 += ac0 * w;
+          vis1 += ac1 * w;
+          if (p.record_transmittance) {
+            const uint32_t id = p.point_list[range.x + b * kBatch + jj];
+            atomicAdd(p.cover_pixels + id, 1.0f);
+            atomicAdd(p.trans_avg + id, T);
+          }
+          T = test_T;
+          last_contributor = contributor;
+        }
+
+        // ---------------- phase B: this warp's hash lookups, when a queue is
+        // full or the warp's pixels are all done (queues carry over between
+        // batches). Each lane reads only its own queue and accumulator row.
+        const bool qfull = __any_sync(0xffffffffu, cnt == kQueue);
+        const bool alldone = !__any_sync(0xffffffffu, !done);
+        if (qfull || alldone) drain();
+        if (j >= todo || alldone) {
+          wdone = alldone;
+          break;
         }
       }
-      // Warp-uniform: the batch is finished for this warp when the walk reached
-      // its end or every lane is done.
-      if (j >= todo || !__any_sync(0xffffffffu, !done)) break;
+      if (wdone && lane == 0) atomicAdd(&S.ndone, 1);
     }
-    // Every warp is past this batch before the next one overwrites S.rec.
-    __syncthreads();
-    if (r + 1 < rounds) fetch(r + 1);
+    // Release slot s; the last warp out refills it.
+    __syncwarp();
+    int last = 0;
+    if (lane == 0) {
+      __threadfence_block();
+      last = atomicAdd(&S.used[s], 1) == kWarps - 1;
+      if (last) S.used[s] = 0;
+    }
+    last = __shfl_sync(0xffffffffu, last, 0);
+    if (last && b + kSlots < rounds && *(volatile int*)&S.ndone < kWarps) fetch(b + kSlots);
+    if (wdone && *(volatile int*)&S.ndone == kWarps) break;
   }
-  asm volatile("cp.async.wait_group 0;");
+  if (__any_sync(0xffffffffu, cnt > 0)) drain();
+  asm volatile("cp.async.wait_all;" ::: "memory");
 
   if (inside) {
     const size_t HW = (size_t)p.H * p.W;
