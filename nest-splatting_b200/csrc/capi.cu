@@ -48,11 +48,22 @@ struct GeomState {
   SurfelRecord* records;
   BinInfo* bin;
   uint32_t* tiles;
-  uint32_t* excl_local;
-  uint32_t* block_sums;
+  uint32_t* block_sums;    // per preprocess CTA: tile-count totals
   uint32_t* block_prefix;
-  int64_t* count;
+  int64_t* count;          // instance total
   uint32_t* err;
+  // Depth sort of the surfels (binning step 1) and the per-CTA totals of the
+  // tile counts in depth order.
+  uint64_t* depth_keys;
+  uint64_t* depth_keys_alt;
+  uint64_t* depth_keys_sorted;
+  uint32_t* depth_vals;
+  uint32_t* depth_vals_alt;
+  uint32_t* depth_vals_sorted;  // surfel indices in depth order
+  uint32_t* sorted_sums;
+  uint32_t* sorted_prefix;
+  void* depth_sort_temp;
+  size_t depth_sort_temp_bytes;
 };
 
 GeomState carve_geom(void* base, int P, size_t* used) {
@@ -62,11 +73,21 @@ GeomState carve_geom(void* base, int P, size_t* used) {
   g.records = c.take<SurfelRecord>((size_t)max(P, 1));
   g.bin = c.take<BinInfo>((size_t)max(P, 1));
   g.tiles = c.take<uint32_t>((size_t)max(P, 1));
-  g.excl_local = c.take<uint32_t>((size_t)max(P, 1));
   g.block_sums = c.take<uint32_t>((size_t)nb);
   g.block_prefix = c.take<uint32_t>((size_t)nb);
   g.count = c.take<int64_t>(1);
   g.err = c.take<uint32_t>(4);
+  const size_t np = (size_t)max(P, 1);
+  g.depth_keys = c.take<uint64_t>(np);
+  g.depth_keys_alt = c.take<uint64_t>(np);
+  g.depth_keys_sorted = c.take<uint64_t>(np);
+  g.depth_vals = c.take<uint32_t>(np);
+  g.depth_vals_alt = c.take<uint32_t>(np);
+  g.depth_vals_sorted = c.take<uint32_t>(np);
+  g.sorted_sums = c.take<uint32_t>((size_t)nb);
+  g.sorted_prefix = c.take<uint32_t>((size_t)nb);
+  g.depth_sort_temp_bytes = radix_sort_temp_bytes(P);
+  g.depth_sort_temp = c.take<char>(g.depth_sort_temp_bytes);
   if (used) *used = align_up(c.off);
   return g;
 }
@@ -181,17 +202,23 @@ int bin_and_render(const ns_raster_settings* st, int P, const GeomState& g, cons
   const int64_t cap = bin_capacity(binning_bytes);
   if (cap < 0) return NS_ERR_SCRATCH;
   if (flags & NS_FLAG_DEVICE_COUNT) return NS_ERR_UNSUPPORTED;
+  // Binning step 1, the depth sort of the surfels, runs while the host waits
+  // for the instance count.
+  rc = radix_sort_launch(g.depth_keys, g.depth_vals, g.depth_keys_sorted, g.depth_vals_sorted,
+                         g.depth_keys_alt, g.depth_vals_alt, P, 32, g.depth_sort_temp,
+                         g.depth_sort_temp_bytes, stream);
+  if (rc) return rc;
   int64_t count = 0;
   NS_CUDA_TRY(cudaMemcpyAsync(&count, g.count, sizeof(int64_t), cudaMemcpyDeviceToHost, stream));
   NS_CUDA_TRY(cudaStreamSynchronize(stream));
   if (num_rendered) *num_rendered = count;
   if (count > cap) return NS_ERR_CAPACITY;
   BinState b = carve_bin(binning, cap, nullptr);
-  rc = duplicate_keys_launch(P, preprocess_block_size(), g.bin, g.excl_local, g.block_prefix,
-                             g.block_sums, gx, gy, b.keys_unsorted, b.vals_unsorted, cap, g.err,
-                             stream);
+  rc = duplicate_keys_launch(P, g.depth_vals_sorted, g.bin, g.tiles, g.sorted_sums,
+                             g.sorted_prefix, g.count, gx, b.keys_unsorted, b.vals_unsorted, cap,
+                             g.err, stream);
   if (rc) return rc;
-  const int end_bit = 32 + (int)higher_msb((uint32_t)tiles);
+  const int end_bit = (int)higher_msb((uint32_t)tiles);
   rc = radix_sort_launch(b.keys_unsorted, b.vals_unsorted, b.keys_sorted, b.vals_sorted, b.keys_alt,
                          b.vals_alt, count, end_bit, b.sort_temp, b.sort_temp_bytes, stream);
   if (rc) return rc;
@@ -294,8 +321,8 @@ int ns_rasterize_forward(const ns_raster_settings* settings, const ns_surfels* s
   rc = preprocess_api_launch(P, *surfels, settings->scale_modifier, settings->beta,
                              settings->viewmatrix,
                              settings->projmatrix, settings->image_width, settings->image_height,
-                             g.records, g.bin, outputs->radii, g.tiles, g.excl_local, g.block_sums,
-                             stream);
+                             g.records, g.bin, outputs->radii, g.tiles, g.depth_keys, g.depth_vals,
+                             g.block_sums, stream);
   if (rc) return rc;
   return bin_and_render(settings, P, g, im, binning, binning_bytes, surfels->features,
                         surfels->offsets, surfels->gridrange, outputs->out_color,
@@ -497,8 +524,8 @@ int ns_render_frame(const ns_raster_settings* settings, const ns_frame_inputs* i
   rc = preprocess_mix_launch(P, in->base, in->decoded, in->dims, in->mix, in->ap_level,
                              settings->scale_modifier, settings->beta, settings->viewmatrix,
                              settings->projmatrix,
-                             W, H, g.records, g.bin, out->radii, g.tiles, g.excl_local,
-                             g.block_sums, stream);
+                             W, H, g.records, g.bin, out->radii, g.tiles, g.depth_keys,
+                             g.depth_vals, g.block_sums, stream);
   if (rc) return rc;
   if (ev) NS_CUDA_TRY(cudaEventRecord((cudaEvent_t)ev[3], stream));
   if (ev) NS_CUDA_TRY(cudaEventRecord((cudaEvent_t)ev[4], stream));

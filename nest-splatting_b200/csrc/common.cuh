@@ -35,7 +35,8 @@ constexpr uint32_t kSpinLimit = 1u << 22;
 //   q1 = (Tu.x, Tu.y, Tu.z, Tv.x)      q2 = (Tv.y, Tv.z, Tw.x, Tw.y)
 //   q3 = (Tw.z, xy.x, xy.y, opacity)    q4 = (n.x, n.y, n.z, ap_level bits)
 //   q5 = (SuTu.x, SuTu.y, SuTu.z, SvTv.x)  q6 = (SvTv.y, SvTv.z, pk.x, pk.y)
-//   q7 = (pk.z, rho_cut, 0, 0): rho_cut bounds min(rho3d, rho2d) where alpha >= 1/255
+//   q7 = (pk.z, rho_cut, surfel index bits, 0): rho_cut bounds min(rho3d, rho2d)
+//        where alpha >= 1/255
 struct alignas(16) SurfelRecord {
   float4 q[8];
 };
@@ -76,6 +77,38 @@ __device__ __forceinline__ void tile_rect(float px, float py, int r, int gx, int
 
 __device__ __forceinline__ void set_error(uint32_t* err, uint32_t bit) {
   if (err) atomicOr(err, bit);
+}
+
+// Bounded wait on a shared-memory mbarrier for the completion of the phase
+// with parity `parity`. Returns 1 when it completed, 0 when *stop (if given)
+// reached `stop_at` first, -1 when the spin limit ran out.
+__device__ __forceinline__ int mbar_wait_parity(const uint64_t* bar, uint32_t parity,
+                                                const int* stop = nullptr, int stop_at = 0) {
+  const unsigned a = (unsigned)__cvta_generic_to_shared(bar);
+  for (uint32_t spins = 0; spins < kSpinLimit; spins++) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(a), "r"(parity)
+        : "memory");
+    if (ok) return 1;
+    if (stop && *(const volatile int*)stop == stop_at) return 0;
+  }
+  return -1;
+}
+
+__device__ __forceinline__ void mbar_init_shared(uint64_t* bar, uint32_t count) {
+  const unsigned a = (unsigned)__cvta_generic_to_shared(bar);
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(a), "r"(count) : "memory");
+}
+
+// Arrive on `bar` once all cp.async copies this thread issued so far have landed.
+__device__ __forceinline__ void cp_async_arrive(uint64_t* bar) {
+  const unsigned a = (unsigned)__cvta_generic_to_shared(bar);
+  asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(a) : "memory");
 }
 
 }  // namespace ns

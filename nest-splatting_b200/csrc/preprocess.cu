@@ -103,8 +103,9 @@ struct PreOut {
   BinInfo* bin;
   int32_t* radii;
   uint32_t* tiles;       // tiles touched
-  uint32_t* excl_local;  // exclusive offset of the surfel inside its CTA
-  uint32_t* block_sums;  // per-CTA total
+  uint64_t* depth_keys;  // float bits of the view depth (all ones when no tile is touched)
+  uint32_t* depth_vals;  // surfel index
+  uint32_t* block_sums;  // per-CTA total of the tile counts
 };
 
 // Squared radius rho (in the units of the blend kernel's rho = min(rho3d, rho2d))
@@ -280,6 +281,7 @@ preprocess_kernel(int P, Attrs attrs, float mod, float beta, const float* __rest
     int radius = 0;
     const SurfelIn a = attrs.load(i);
     tiles = preprocess_one(a, mod, beta, vm, pm, W, H, gx, gy, rec, bi, radius);
+    rec.q[7].z = __uint_as_float((uint32_t)i);
     if (tiles) {
       float4* dst = reinterpret_cast<float4*>(out.records + i);
 #pragma unroll
@@ -288,8 +290,10 @@ preprocess_kernel(int P, Attrs attrs, float mod, float beta, const float* __rest
     out.bin[i] = bi;
     out.radii[i] = radius;
     out.tiles[i] = tiles;
+    out.depth_keys[i] = tiles ? (uint64_t)__float_as_uint(bi.depth) : 0xffffffffull;
+    out.depth_vals[i] = (uint32_t)i;
   }
-  // CTA-local exclusive scan of the tile counts.
+  // CTA total of the tile counts (the instance count is their sum).
   const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
   uint32_t x = tiles;
 #pragma unroll
@@ -301,7 +305,6 @@ preprocess_kernel(int P, Attrs attrs, float mod, float beta, const float* __rest
   __syncthreads();
   uint32_t add = 0;
   for (int k = 0; k < w; k++) add += warp_sums[k];
-  if (i < P) out.excl_local[i] = x - tiles + add;
   if (threadIdx.x == kPreThreads - 1) out.block_sums[blockIdx.x] = x + add;
 }
 
@@ -321,10 +324,10 @@ int preprocess_block_size() { return kPreThreads; }
 
 int preprocess_api_launch(int P, const ns_surfels& s, float mod, float beta, const float* vm,
                           const float* pm, int W, int H, SurfelRecord* records, BinInfo* bin,
-                          int32_t* radii, uint32_t* tiles, uint32_t* excl_local,
-                          uint32_t* block_sums, cudaStream_t stream) {
+                          int32_t* radii, uint32_t* tiles, uint64_t* depth_keys,
+                          uint32_t* depth_vals, uint32_t* block_sums, cudaStream_t stream) {
   ApiAttrs a{s.means3D, s.scales, s.rotations, s.opacities, s.homotrans, s.ap_level};
-  PreOut o{records, bin, radii, tiles, excl_local, block_sums};
+  PreOut o{records, bin, radii, tiles, depth_keys, depth_vals, block_sums};
   preprocess_kernel<ApiAttrs><<<preprocess_blocks(P), kPreThreads, 0, stream>>>(P, a, mod, beta, vm,
                                                                                 pm, W, H, o);
   NS_LAUNCH_CHECK();
@@ -334,10 +337,10 @@ int preprocess_api_launch(int P, const ns_surfels& s, float mod, float beta, con
 int preprocess_mix_launch(int P, const float* base, const float* decoded, int dims, float mix,
                           const float* ap_level, float mod, float beta, const float* vm,
                           const float* pm, int W, int H, SurfelRecord* records, BinInfo* bin,
-                          int32_t* radii, uint32_t* tiles, uint32_t* excl_local,
-                          uint32_t* block_sums, cudaStream_t stream) {
+                          int32_t* radii, uint32_t* tiles, uint64_t* depth_keys,
+                          uint32_t* depth_vals, uint32_t* block_sums, cudaStream_t stream) {
   MixAttrs a{base, decoded, dims, mix, ap_level};
-  PreOut o{records, bin, radii, tiles, excl_local, block_sums};
+  PreOut o{records, bin, radii, tiles, depth_keys, depth_vals, block_sums};
   preprocess_kernel<MixAttrs><<<preprocess_blocks(P), kPreThreads, 0, stream>>>(P, a, mod, beta, vm,
                                                                                 pm, W, H, o);
   NS_LAUNCH_CHECK();

@@ -105,26 +105,6 @@ __device__ __forceinline__ float2 lookup_finish(const float (&f)[3], const Corne
   return r;
 }
 
-// Bounded wait for ring slot s to hold its batch of parity `parity`. Returns 1
-// when it does, 0 when every warp of the tile is done (nothing left to wait
-// for), -1 when the spin limit runs out.
-__device__ __forceinline__ int wait_slot(BlendSmem& S, int s, uint32_t parity) {
-  const unsigned bar = (unsigned)__cvta_generic_to_shared(&S.full[s]);
-  for (uint32_t spins = 0; spins < kSpinLimit; spins++) {
-    uint32_t ok;
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-        "selp.u32 %0, 1, 0, p;\n\t}"
-        : "=r"(ok)
-        : "r"(bar), "r"(parity)
-        : "memory");
-    if (ok) return 1;
-    if (*(volatile int*)&S.ndone == kWarps) return 0;
-  }
-  return -1;
-}
-
 template <typename TableT>
 __global__ void __launch_bounds__(kThreads, 2) blend_kernel(const RenderParams p) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
@@ -145,8 +125,7 @@ __global__ void __launch_bounds__(kThreads, 2) blend_kernel(const RenderParams p
   if (t < (int)L) S.lv[t] = make_level<TableT>(p.table, p.offsets, p.S, p.Hres, p.align_corners, t);
   for (int c = 0; c < kAccStride; c++) S.acc[t * kAccStride + c] = 0.f;  // only this thread's row
   if (t < kSlots) {
-    const unsigned bar = (unsigned)__cvta_generic_to_shared(&S.full[t]);
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], 32;" ::"r"(bar) : "memory");
+    mbar_init_shared(&S.full[t], 32);
     S.used[t] = 0;
   }
   if (t == 0) S.ndone = 0;
@@ -185,8 +164,7 @@ __global__ void __launch_bounds__(kThreads, 2) blend_kernel(const RenderParams p
         }
       }
     }
-    const unsigned bar = (unsigned)__cvta_generic_to_shared(&S.full[s]);
-    asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(bar) : "memory");
+    cp_async_arrive(&S.full[s]);
   };
 
   int cnt = 0;  // this pixel's queued samples (kept across batches)
@@ -279,7 +257,8 @@ __global__ void __launch_bounds__(kThreads, 2) blend_kernel(const RenderParams p
   if (wdone && lane == 0) atomicAdd(&S.ndone, 1);
   for (int b = 0; b < rounds; b++) {
     const int s = b & (kSlots - 1);
-    const int ws = wait_slot(S, s, (uint32_t)(b / kSlots) & 1u);
+    // Wait for batch b (gives up when every warp of the tile is done).
+    const int ws = mbar_wait_parity(&S.full[s], (uint32_t)(b / kSlots) & 1u, &S.ndone, kWarps);
     if (ws <= 0) {
       if (ws < 0) set_error(p.err, kErrSpinTimeout);
       break;
@@ -401,7 +380,7 @@ __global__ void __launch_bounds__(kThreads, 2) blend_kernel(const RenderParams p
           vis0 += ac0 * w;
           vis1 += ac1 * w;
           if (p.record_transmittance) {
-            const uint32_t id = p.point_list[range.x + b * kBatch + jj];
+            const uint32_t id = __float_as_uint(S.rec[s][jj][7].z);  // the record's surfel index
             atomicAdd(p.cover_pixels + id, 1.0f);
             atomicAdd(p.trans_avg + id, T);
           }
