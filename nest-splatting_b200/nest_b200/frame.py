@@ -3,7 +3,9 @@
 One `FrameRenderer.render(camera)` is one call of ns_render_frame on torch's
 current stream. Scene tensors are uploaded once (the model: codebooks, base
 attributes, hash table, MLP weights); the per-frame input is the RVQ index
-stream, which `upload_indices` copies host -> device.
+stream, which `upload_indices` copies host -> device. `FramePipeline` renders
+a sequence of frames with each frame's host <-> device copies overlapping the
+neighbouring frames' kernels.
 """
 from __future__ import annotations
 
@@ -77,14 +79,21 @@ class FrameRenderer:
         self.rvq_idx.copy_(host_idx, non_blocking=True)
 
     def render(self, cam: Camera, view: torch.Tensor | None = None, proj: torch.Tensor | None = None,
-               events=None, skip_decode: bool = False):
+               events=None, skip_decode: bool = False, rvq_idx: torch.Tensor | None = None,
+               rgb: torch.Tensor | None = None):
         """Renders one frame; returns the rgb [3,H,W] tensor (reused across calls).
 
         events: optional 2*NS_FRAME_STAGES torch.cuda.Event(enable_timing=True),
         recorded before/after decode, preprocess, binning, blend and MLP.
-        skip_decode: `self.decoded` already holds the decoded attributes."""
+        skip_decode: `self.decoded` already holds the decoded attributes.
+        rvq_idx / rgb: device index stream to decode and image to write, in place
+        of the renderer's own buffers."""
         lib = _lib.load()
         self._outputs(cam)
+        idx_t = self.rvq_idx if rvq_idx is None else rvq_idx
+        rgb_t = self.rgb if rgb is None else rgb
+        if idx_t.shape != self.rvq_idx.shape or rgb_t.shape != self.rgb.shape:
+            raise ValueError("rvq_idx / rgb do not match the renderer's buffers")
         if view is None:
             view = cam.world_view_transform.to(self.device).contiguous()
         if proj is None:
@@ -92,7 +101,7 @@ class FrameRenderer:
         st = self.settings(cam, view, proj)
         fin = _lib.FrameInputs()
         fin.P = self.P
-        fin.rvq_idx, fin.codebooks = ptr(self.rvq_idx), ptr(self.codebooks)
+        fin.rvq_idx, fin.codebooks = ptr(idx_t), ptr(self.codebooks)
         fin.stages, fin.entries, fin.dims = self.stages, self.entries, self.dims
         fin.base, fin.mix, fin.decoded = ptr(self.base), self.mix, ptr(self.decoded)
         fin.ap_level, fin.features = ptr(self.ap_level), ptr(self.table)
@@ -106,7 +115,7 @@ class FrameRenderer:
             fin.stage_events = C.cast(ev_arr, C.c_void_p)
         flags = _lib.NS_FLAG_SKIP_DECODE if skip_decode else 0
         fout = _lib.FrameOutputs()
-        fout.rgb, fout.out_color = ptr(self.rgb), ptr(self.features)
+        fout.rgb, fout.out_color = ptr(rgb_t), ptr(self.features)
         fout.out_others, fout.radii = ptr(self.others), ptr(self.radii)
         geom = self.scratch.geometry(self.P, self.device)
         image = self.scratch.image_buf(cam.width, cam.height, self.device)
@@ -123,4 +132,80 @@ class FrameRenderer:
             check("ns_render_frame", rc)
             break
         self.num_rendered = int(n.value)
-        return self.rgb
+        return rgb_t
+
+
+class FramePipeline:
+    """A sequence of frames with the host <-> device copies off the critical path.
+
+    Frame i's inputs (its RVQ index stream and its [2,4,4] view / projection
+    matrices, from pinned host memory) are copied on an input stream while
+    frame i-1 renders, and frame i's image is copied back on an output stream
+    while frame i+1 renders. Two device buffers of each, guarded by CUDA
+    events; every frame still copies its own inputs in and its image out.
+    With a DecodeShard (several ranks), each rank copies its own rows of the
+    index stream and the frame decodes them and all-gathers the attributes.
+    """
+
+    def __init__(self, renderer: FrameRenderer, shard=None, depth: int = 2):
+        self.fr = renderer
+        self.shard = shard
+        d = renderer.device
+        self.in_stream = torch.cuda.Stream(device=d)
+        self.out_stream = torch.cuda.Stream(device=d)
+        src = renderer.rvq_idx if shard is None else shard.idx_shard
+        self.idx = [torch.zeros_like(src) for _ in range(depth)]
+        self.cam = [torch.empty((2, 4, 4), dtype=torch.float32, device=d) for _ in range(depth)]
+        self.rgb = [None] * depth
+        self.depth = depth
+        self.ev_in = [torch.cuda.Event() for _ in range(depth)]     # inputs on the device
+        self.ev_done = [torch.cuda.Event() for _ in range(depth)]   # frame rendered, inputs free
+        self.ev_host = [torch.cuda.Event() for _ in range(depth)]   # image on the host
+        self.used = [False] * depth
+
+    def run(self, n: int, cam: Camera, host_idx, host_cam, host_rgb, before_frame=None):
+        """Renders n frames of camera `cam`'s size. host_idx(i) and host_cam(i) return
+        frame i's pinned host inputs (the full [P, stages] index stream; [2,4,4] view and
+        projection matrices), host_rgb(i) its pinned host image [3,H,W]. before_frame(i),
+        if given, runs on the compute stream before frame i. Returns with the last
+        copy enqueued; synchronise the output stream (or the device) to read it."""
+        fr, sh = self.fr, self.shard
+        cs = torch.cuda.current_stream(fr.device)
+        fr._outputs(cam)
+        for i in range(n):
+            k = i % self.depth
+            if self.rgb[k] is None or self.rgb[k].shape != fr.rgb.shape:
+                self.rgb[k] = torch.empty_like(fr.rgb)
+            with torch.cuda.stream(self.in_stream):
+                if self.used[k]:
+                    self.in_stream.wait_event(self.ev_done[k])
+                hi = host_idx(i)
+                if sh is None:
+                    self.idx[k].copy_(hi, non_blocking=True)
+                else:
+                    from .views import shard_range
+                    lo_, hi_ = shard_range(sh.P, sh.world, sh.rank)
+                    self.idx[k][: hi_ - lo_].copy_(hi[lo_:hi_], non_blocking=True)
+                self.cam[k].copy_(host_cam(i), non_blocking=True)
+                self.ev_in[k].record(self.in_stream)
+            cs.wait_event(self.ev_in[k])
+            if self.used[k]:
+                cs.wait_event(self.ev_host[k])
+            if before_frame is not None:
+                before_frame(i)
+            if sh is None:
+                fr.render(cam, self.cam[k][0], self.cam[k][1], rvq_idx=self.idx[k], rgb=self.rgb[k])
+            else:
+                sh.decode_and_gather(fr.codebooks, _rvq_decode, idx=self.idx[k])
+                fr.render(cam, self.cam[k][0], self.cam[k][1], skip_decode=True, rgb=self.rgb[k])
+            self.ev_done[k].record(cs)
+            with torch.cuda.stream(self.out_stream):
+                self.out_stream.wait_event(self.ev_done[k])
+                host_rgb(i).copy_(self.rgb[k], non_blocking=True)
+                self.ev_host[k].record(self.out_stream)
+            self.used[k] = True
+
+
+def _rvq_decode(idx, codebooks, out=None):
+    from .raster import rvq_decode
+    return rvq_decode(idx, codebooks, out=out)

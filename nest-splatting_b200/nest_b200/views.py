@@ -75,7 +75,9 @@ class DecodeShard:
             self.dec_full.copy_(self.dec_shard)
         return self.decoded
 
-    def decode_and_gather(self, codebooks: torch.Tensor, decode_fn, group=None) -> torch.Tensor:
-        """decode_fn(idx, codebooks, out=...) on this rank's rows, then the all-gather."""
-        decode_fn(self.idx_shard, codebooks, out=self.dec_shard)
+    def decode_and_gather(self, codebooks: torch.Tensor, decode_fn, group=None,
+                          idx: torch.Tensor | None = None) -> torch.Tensor:
+        """decode_fn(idx, codebooks, out=...) on this rank's rows (idx_shard, or `idx`
+        of the same shape), then the all-gather."""
+        decode_fn(self.idx_shard if idx is None else idx, codebooks, out=self.dec_shard)
         return self.gather(group)

@@ -74,3 +74,31 @@ def test_fused_frame_repeatable_and_index_upload():
     b = fr.render(sc.camera).clone()
     torch.cuda.synchronize()
     assert torch.equal(a, b)
+
+
+def test_frame_pipeline_sequence_matches_single_frames():
+    """FramePipeline: every frame's image, copied back to the host, equals the same
+    frame rendered alone (frames alternate between two index streams and cameras)."""
+    from nest_b200.camera import orbit_camera
+    from nest_b200.frame import FramePipeline
+
+    sc = small_scene(n=3000, seed=23, rvq=True)
+    fr = FrameRenderer(sc)
+    W, H = sc.camera.width, sc.camera.height
+    cams = [orbit_camera(W, H, 50.0, 4.0, az) for az in (0.0, 40.0)]
+    g = torch.Generator().manual_seed(5)
+    streams = [sc.rvq_idx.clone(), torch.randint(0, 256, sc.rvq_idx.shape, generator=g).to(torch.uint8)]
+    ref = []
+    for i in range(2):
+        fr.upload_indices(streams[i].cuda())
+        ref.append(fr.render(cams[i]).cpu())
+    host_idx = [s.pin_memory() for s in streams]
+    host_cam = [torch.stack([c.world_view_transform, c.full_proj_transform]).contiguous().pin_memory()
+                for c in cams]
+    n = 7
+    host_rgb = [torch.empty((3, H, W)).pin_memory() for _ in range(n)]
+    pipe = FramePipeline(fr)
+    pipe.run(n, cams[0], lambda i: host_idx[i % 2], lambda i: host_cam[i % 2], lambda i: host_rgb[i])
+    torch.cuda.synchronize()
+    for i in range(n):
+        assert torch.equal(host_rgb[i], ref[i % 2]), i
