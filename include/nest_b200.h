@@ -26,6 +26,8 @@
  *                            and CudaRasterizer::Rasterizer::backward,
  *                            rasterizer_impl.cu:444-592 (BACKWARD::render,
  *                            backward.cu:445-2052; BACKWARD::preprocess, :2216-2273)
+ *   ns_mlp_backward       <- tiny-cuda-nn's backward of the same MLP (autograd of
+ *                            INGP.get_color in the training step, train.py:651)
  *   ns_normal_error       <- the depth-normal term of the 2DGS training loss:
  *                            gaussian_renderer/__init__.py:763-792 (allmap decode,
  *                            depth_ratio 0), utils/point_utils.py:10-30,48-60
@@ -197,6 +199,16 @@ int ns_mark_visible(int32_t P, const float* means3D, const float* viewmatrix,
 int ns_mlp_forward(const float* feat, int32_t in_dims, int64_t npix, const uint16_t* weights,
                    int32_t hidden, int32_t out_dims, const float* alpha, const float* bg_host,
                    float* rgb, void* stream);
+
+/* Backward of ns_mlp_forward (without the background term) given dL_drgb
+ * [3, npix] fp32: dL_dfeat [in_dims, npix] fp32 and dL_dweights fp32 in the
+ * packed-weight layout (W1 [hidden, in_dims], W2 [hidden, hidden], W3 [3,
+ * hidden]; overwritten). The forward is recomputed exactly as ns_mlp_forward
+ * computes it; the backward runs on TF32 tensor cores with fp32 accumulation,
+ * treating the fp16 roundings as identity. alpha may be NULL (no mask). */
+int ns_mlp_backward(const float* feat, int32_t in_dims, int64_t npix, const uint16_t* weights,
+                    int32_t hidden, int32_t out_dims, const float* alpha, const float* dL_drgb,
+                    float* dL_dfeat, float* dL_dweights, void* stream);
 
 /* ------------------------------------------------------------------ RVQ */
 

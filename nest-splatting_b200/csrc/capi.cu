@@ -469,6 +469,13 @@ int ns_normal_error_backward(const float* allmap, const float* viewmatrix, const
                                       reinterpret_cast<cudaStream_t>(stream));
 }
 
+int ns_mlp_backward(const float* feat, int32_t in_dims, int64_t npix, const uint16_t* weights,
+                    int32_t hidden, int32_t out_dims, const float* alpha, const float* dL_drgb,
+                    float* dL_dfeat, float* dL_dweights, void* stream) {
+  return mlp_backward_launch(feat, in_dims, npix, weights, hidden, out_dims, alpha, dL_drgb,
+                             dL_dfeat, dL_dweights, reinterpret_cast<cudaStream_t>(stream));
+}
+
 int ns_rvq_decode(const uint8_t* idx, const float* codebooks, float* out, int64_t n,
                   int32_t stages, int32_t entries, int32_t dims, void* stream) {
   return rvq_decode_launch(idx, codebooks, out, n, stages, entries, dims,

@@ -241,6 +241,23 @@ def mlp_forward(feat_chw: torch.Tensor, packed_weights: torch.Tensor, alpha=None
     return rgb
 
 
+def mlp_backward(feat_chw: torch.Tensor, packed_weights: torch.Tensor, dL_drgb: torch.Tensor,
+                 alpha=None, hidden: int = 64):
+    """(dL/dfeat [C, ...], dL/dweights fp32 in the packed layout) of mlp_forward
+    without the background term, from dL/drgb [3, ...]."""
+    lib = _lib.load()
+    Cin = feat_chw.shape[0]
+    npix = feat_chw[0].numel()
+    g = dL_drgb.float().contiguous()
+    _require_cuda(feat_chw, packed_weights, alpha, g)
+    dfeat = torch.empty_like(feat_chw, dtype=torch.float32)
+    dW = torch.empty(packed_weights.numel(), dtype=torch.float32, device=feat_chw.device)
+    check("ns_mlp_backward", lib.ns_mlp_backward(ptr(feat_chw), Cin, npix, ptr(packed_weights), hidden, 3,
+                                                 ptr(alpha), ptr(g), ptr(dfeat), ptr(dW),
+                                                 _lib.stream_handle(feat_chw.device)))
+    return dfeat, dW
+
+
 def normal_error(allmap: torch.Tensor, viewmatrix: torch.Tensor, rays_d: torch.Tensor,
                  ray_o: torch.Tensor) -> torch.Tensor:
     """Depth-normal consistency error [H, W] of the training loss (ns_normal_error):

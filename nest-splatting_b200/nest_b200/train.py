@@ -4,8 +4,8 @@ autograd around the library's kernels.
 Forward: the drop-in rasterizer (ns_rasterize_forward) -> the fp16 MLP
 (ns_mlp_forward) -> the losses, the depth-normal term fused into one kernel
 (ns_normal_error). Backward: ns_normal_error_backward for that term,
-ns_rasterize_backward for the surfels and the hash table; the MLP's backward is
-four small GEMMs (torch / cuBLAS) on activations recomputed from the features.
+ns_mlp_backward for the MLP (features and weights), ns_rasterize_backward for
+the surfels and the hash table.
 
 Restated from the reference: the allmap decode (gaussian_renderer/__init__.py
 :763-797: alpha, view-to-world normal, expected depth = depth / alpha with NaN
@@ -28,60 +28,39 @@ class _MLP(torch.autograd.Function):
     """rgb [3,H,W] = sigmoid(W3 relu(W2 relu(W1 feat)))[:3] * (alpha > 0) (+ (1 - alpha) bg).
 
     Forward on the library's tensor-core kernel (fp16 operands, fp32
-    accumulation, each layer rounded to fp16). Backward treats the fp16
-    roundings as identity and runs on the recomputed fp16 activations with
-    TF32 tensor-core GEMMs (fp32 range: the per-pixel gradients of a mean
-    loss over megapixels are ~1e-7, below fp16's normal range).
+    accumulation, each layer rounded to fp16). Backward on the library's fused
+    kernel (ns_mlp_backward: the forward recomputed, the backward on TF32
+    tensor cores in fp32 range -- the per-pixel gradients of a mean loss over
+    megapixels are ~1e-7, below fp16's normal range -- and the weight
+    gradients reduced on chip); the fp16 roundings are treated as identity.
     """
 
     @staticmethod
     def forward(ctx, feat, w1, w2, w3, alpha, bg):
         packed = raster.pack_mlp([w1.detach(), w2.detach(), w3.detach()])
-        rgb = raster.mlp_forward(feat.detach().contiguous(), packed, alpha=alpha.detach().contiguous(), bg=bg,
-                                 hidden=w1.shape[0])
-        ctx.save_for_backward(feat, w1, w2, w3, alpha)
+        feat_c = feat.detach().contiguous()
+        alpha_c = alpha.detach().contiguous()
+        rgb = raster.mlp_forward(feat_c, packed, alpha=alpha_c, bg=bg, hidden=w1.shape[0])
+        ctx.save_for_backward(feat_c, packed, alpha_c)
+        ctx.shapes = (w1.shape, w2.shape, w3.shape, w1.dtype)
         ctx.bg = bg
         return rgb
 
     @staticmethod
     def backward(ctx, grgb):
-        prev = torch.backends.cuda.matmul.allow_tf32
-        torch.backends.cuda.matmul.allow_tf32 = True
-        try:
-            return _MLP._backward(ctx, grgb)
-        finally:
-            torch.backends.cuda.matmul.allow_tf32 = prev
-
-    @staticmethod
-    def _backward(ctx, grgb):
-        feat, w1, w2, w3, alpha = ctx.saved_tensors
-        C = feat.shape[0]
-        x = feat.detach().reshape(C, -1).T.half().float()
-        W1, W2, W3 = (w.detach().half().float() for w in (w1, w2, w3))
-        z1 = (x @ W1.T).half().float()
-        a1 = torch.relu(z1)
-        z2 = (a1 @ W2.T).half().float()
-        a2 = torch.relu(z2)
-        z3 = (a2 @ W3.T).half().float()[:, :3]
-        s = torch.sigmoid(z3)
-        a = alpha.detach().reshape(-1)
-        g = grgb.reshape(3, -1).T.float()
-        dz3 = g * (a > 0).float()[:, None] * s * (1 - s)
-        dW3 = torch.zeros_like(W3)
-        dW3[:3] = dz3.T @ a2
-        dz2 = (dz3 @ W3[:3]) * (z2 > 0).float()
-        dW2 = dz2.T @ a1
-        dz1 = (dz2 @ W2) * (z1 > 0).float()
-        dW1 = dz1.T @ x
-        dfeat = (dz1 @ W1).T.reshape(feat.shape)
+        feat, packed, alpha = ctx.saved_tensors
+        (s1, s2, s3, wdt) = ctx.shapes
+        dfeat, dW = raster.mlp_backward(feat, packed, grgb, alpha=alpha, hidden=s1[0])
+        n1, n2 = s1.numel(), s2.numel()
+        dW1, dW2, dW3 = dW[:n1].view(s1), dW[n1:n1 + n2].view(s2), dW[n1 + n2:].view(s3)
         dalpha = None
         bg = ctx.bg
         if ctx.needs_input_grad[4]:
             dalpha = torch.zeros_like(alpha)
             if bg is not None and float(sum(float(b) for b in bg)) > 0:
-                bgt = torch.as_tensor([float(b) for b in bg], device=g.device)
-                dalpha = -(g * bgt[None]).sum(1).reshape(alpha.shape)
-        return dfeat, dW1.to(w1.dtype), dW2.to(w2.dtype), dW3.to(w3.dtype), dalpha, None
+                bgt = torch.as_tensor([float(b) for b in bg], device=grgb.device).view(3, *([1] * (grgb.dim() - 1)))
+                dalpha = -(grgb.float() * bgt).sum(0).reshape(alpha.shape)
+        return dfeat.to(feat.dtype), dW1.to(wdt), dW2.to(wdt), dW3.to(wdt), dalpha, None
 
 
 def mlp(feat, w1, w2, w3, alpha, bg=None):

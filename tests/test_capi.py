@@ -85,6 +85,9 @@ def test_invalid_arguments_return_status_without_launching():
     assert lib.ns_rvq_decode(None, None, None, 10, 9, 256, 59, None) == _lib.NS_ERR_UNSUPPORTED
     assert lib.ns_rvq_decode(None, None, None, 0, 6, 256, 59, None) == _lib.NS_OK
     assert lib.ns_mlp_forward(None, 16, 10, None, 64, 3, None, None, None, None) == _lib.NS_ERR_UNSUPPORTED
+    assert lib.ns_mlp_backward(None, 16, 10, None, 64, 3, None, None, None, None, None) == \
+        _lib.NS_ERR_UNSUPPORTED
+    assert lib.ns_mlp_backward(None, 32, 10, None, 64, 3, None, None, None, None, None) == _lib.NS_ERR_INVALID
     assert lib.ns_rasterize_forward(None, None, None, None, 0, None, 0, None, 0, None, 0, None) == \
         _lib.NS_ERR_INVALID
     assert lib.ns_mark_visible(-1, None, None, None, None, None) == _lib.NS_ERR_INVALID

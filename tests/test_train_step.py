@@ -96,26 +96,35 @@ def test_train_step_gradients_match_oracle():
 
 
 @pytest.mark.gpu
-def test_mlp_backward_matches_torch_autograd():
+@pytest.mark.parametrize("H,W,scale", [(40, 56, 1.0), (37, 53, 1e-7), (2, 5, 1.0)])
+def test_mlp_backward_matches_torch_autograd(H, W, scale):
+    """The fused MLP backward (ns_mlp_backward) against torch autograd of the same
+    network on fp16-rounded operands, in fp32; scale 1e-7 is the size of a mean
+    loss's per-pixel gradient over a megapixel image (below fp16's normal range)."""
     g = torch.Generator().manual_seed(3)
-    feat = (torch.rand(32, 40, 56, generator=g) * 2 - 1).cuda().requires_grad_(True)
-    alpha = (torch.rand(40, 56, generator=g)).cuda()
+    feat = (torch.rand(32, H, W, generator=g) * 2 - 1).cuda().requires_grad_(True)
+    alpha = (torch.rand(H, W, generator=g)).cuda()
     alpha[::7] = 0.0
     ws = [((torch.rand(o, i, generator=g) * 2 - 1) * (6 / (i + o)) ** 0.5).cuda().requires_grad_(True)
           for i, o in ((32, 64), (64, 64), (64, 3))]
-    up = torch.randn(3, 40, 56, generator=g).cuda()
+    up = torch.randn(3, H, W, generator=g).cuda() * scale
     rgb = train.mlp(feat, *ws, alpha)
     (rgb * up).sum().backward()
     got = [feat.grad] + [w.grad for w in ws]
-    # torch fp32 reference of the same network on fp16-rounded operands
+    # torch fp32 reference of the same network on fp16-rounded operands; the
+    # roundings pass gradients through unchanged (autograd through .half() would
+    # round the gradients to fp16 too, and flush the 1e-7-scale case to zero)
+    def r16(t):
+        return t + (t.half().float() - t).detach()
+
     f2 = feat.detach().clone().requires_grad_(True)
     w2 = [w.detach().clone().requires_grad_(True) for w in ws]
-    x = f2.reshape(32, -1).T.half().float()
+    x = r16(f2.reshape(32, -1).T)
     h = x
     for i, w in enumerate(w2):
-        h = h @ w.half().float().T
-        h = h.half().float() if i == 2 else torch.relu(h).half().float()
-    ref_rgb = torch.sigmoid(h[:, :3]).T.reshape(3, 40, 56) * (alpha > 0).float()
+        h = h @ r16(w).T
+        h = r16(h) if i == 2 else r16(torch.relu(h))
+    ref_rgb = torch.sigmoid(h[:, :3]).T.reshape(3, H, W) * (alpha > 0).float()
     assert torch.allclose(ref_rgb, rgb, atol=2e-3)
     (ref_rgb * up).sum().backward()
     for a, b in zip(got, [f2.grad] + [w.grad for w in w2]):
