@@ -28,6 +28,9 @@
  *                            backward.cu:445-2052; BACKWARD::preprocess, :2216-2273)
  *   ns_mlp_backward       <- tiny-cuda-nn's backward of the same MLP (autograd of
  *                            INGP.get_color in the training step, train.py:651)
+ *   ns_allmap_decode      <- the render_pkg maps of gaussian_renderer/__init__.py
+ *                            :763-797,1035-1045 (rend_normal, depth_expected,
+ *                            depth_median, surf_depth, surf_normal)
  *   ns_normal_error       <- the depth-normal term of the 2DGS training loss:
  *                            gaussian_renderer/__init__.py:763-792 (allmap decode,
  *                            depth_ratio 0), utils/point_utils.py:10-30,48-60
@@ -284,6 +287,21 @@ int ns_render_frame(const ns_raster_settings* settings, const ns_frame_inputs* i
                     const ns_frame_outputs* outputs, void* geom, size_t geom_bytes,
                     void* binning, size_t binning_bytes, void* image, size_t image_bytes,
                     int64_t* num_rendered, int flags, void* stream);
+
+/* --------------------------------------------------------- allmap decode */
+
+/* The per-frame maps the reference's render() derives from the allmap
+ * (allmap = out_others: 0 depth*w, 1 alpha, 2-4 view-space normal, 5 median
+ * depth), in one pass. maps fp32 [9, H, W]: 0-2 rend_normal (R^T n_view),
+ * 3 depth_expected (nan_to_num(D / alpha)), 4 depth_median (nan_to_num),
+ * 5 surf_depth = expected * (1 - depth_ratio) + depth_ratio * median,
+ * 6-8 surf_normal = normalize(cross(P(x, y+1) - P(x, y-1), P(x+1, y) - P(x-1, y)))
+ * * alpha with P = surf_depth * rays_d + ray_o (zero on the border). Inputs as
+ * ns_normal_error. rend_alpha, rend_dist and gaussian_num are allmap channels
+ * 1, 6 and 7 as they are. */
+int ns_allmap_decode(const float* allmap, const float* viewmatrix, const float* rays_d,
+                     const float* ray_o, int32_t width, int32_t height, float depth_ratio,
+                     float* maps, void* stream);
 
 /* --------------------------------------------------------- normal error */
 

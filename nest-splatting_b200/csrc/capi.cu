@@ -441,6 +441,16 @@ int ns_mlp_forward(const float* feat, int32_t in_dims, int64_t npix, const uint1
                     reinterpret_cast<cudaStream_t>(stream));
 }
 
+int ns_allmap_decode(const float* allmap, const float* viewmatrix, const float* rays_d,
+                     const float* ray_o, int32_t width, int32_t height, float depth_ratio,
+                     float* maps, void* stream) {
+  if (width < 0 || height < 0) return NS_ERR_INVALID;
+  if ((int64_t)width * height == 0) return NS_OK;
+  if (!allmap || !viewmatrix || !rays_d || !ray_o || !maps) return NS_ERR_INVALID;
+  return allmap_decode_launch(allmap, viewmatrix, rays_d, ray_o, width, height, depth_ratio, maps,
+                              reinterpret_cast<cudaStream_t>(stream));
+}
+
 int ns_normal_error(const float* allmap, const float* viewmatrix, const float* rays_d,
                     const float* ray_o, int32_t width, int32_t height, float* err, void* stream) {
   if (width < 0 || height < 0) return NS_ERR_INVALID;

@@ -99,6 +99,9 @@ int mlp_launch(const float* feat, int in_dims, int64_t npix, const uint16_t* wei
 int mlp_backward_launch(const float* feat, int in_dims, int64_t npix, const uint16_t* weights,
                         int hidden, int out_dims, const float* alpha, const float* grgb,
                         float* dfeat, float* dW, cudaStream_t stream);
+int allmap_decode_launch(const float* allmap, const float* vm, const float* rays_d,
+                         const float* ray_o, int W, int H, float depth_ratio, float* out,
+                         cudaStream_t stream);
 int normal_error_launch(const float* allmap, const float* vm, const float* rays_d,
                         const float* ray_o, int W, int H, float* err, cudaStream_t stream);
 int normal_error_backward_launch(const float* allmap, const float* vm, const float* rays_d,

@@ -1,6 +1,7 @@
-// normals.cu -- the depth-normal consistency term of training (config 4):
-// allmap decode, pseudo surface normal from the expected depth, and the
-// per-pixel normal error, forward and backward.
+// normals.cu -- the allmap decode of a rendered frame (the render_pkg maps) and
+// the depth-normal consistency term of training (config 4): pseudo surface
+// normal from the expected depth and the per-pixel normal error, forward and
+// backward.
 //
 // Restates, per pixel, the reference's torch code:
 //   gaussian_renderer/__init__.py:763-797 (depth_ratio 0): alpha = allmap[1];
@@ -179,7 +180,71 @@ normal_error_bw2_kernel(const float* __restrict__ allmap, const float* __restric
   dallmap[HW + q] = da;
 }
 
+// nan_to_num(x, 0, 0) of torch: NaN and +inf to 0, -inf to the lowest finite float.
+__device__ __forceinline__ float nan_to_num0(float v) {
+  if (isfinite(v)) return v;
+  return (isinf(v) && v < 0.0f) ? -FLT_MAX : 0.0f;
+}
+
+// Surface depth of pixel q (gaussian_renderer/__init__.py:770-786):
+// expected * (1 - ratio) + ratio * median.
+__device__ __forceinline__ float surf_depth_at(const float* __restrict__ allmap, size_t HW, size_t q,
+                                               float one_minus_ratio, float ratio) {
+  const float e = expected_depth(allmap, HW, q);
+  const float m = nan_to_num0(allmap[5 * HW + q]);
+  return e * one_minus_ratio + ratio * m;
+}
+
+// The render_pkg maps of one frame from its allmap (gaussian_renderer/__init__.py
+// :763-797 and :1035-1045): out channels 0-2 rend_normal (world), 3
+// depth_expected, 4 depth_median, 5 surf_depth, 6-8 surf_normal
+// (= depth_to_normal(surf_depth) * alpha, zero on the image border).
+__global__ void __launch_bounds__(kNormThreads)
+allmap_decode_kernel(const float* __restrict__ allmap, const float* __restrict__ vm,
+                     const float* __restrict__ rays_d, const float* __restrict__ ray_o, int W, int H,
+                     float one_minus_ratio, float ratio, float* __restrict__ out) {
+  const int64_t p = (int64_t)blockIdx.x * kNormThreads + threadIdx.x;
+  const size_t HW = (size_t)W * H;
+  if (p >= (int64_t)HW) return;
+  const int x = (int)(p % W), y = (int)(p / W);
+  const V3f rn = world_normal(allmap, vm, HW, p);
+  out[0 * HW + p] = rn.x;
+  out[1 * HW + p] = rn.y;
+  out[2 * HW + p] = rn.z;
+  out[3 * HW + p] = expected_depth(allmap, HW, p);
+  out[4 * HW + p] = nan_to_num0(allmap[5 * HW + p]);
+  out[5 * HW + p] = surf_depth_at(allmap, HW, p, one_minus_ratio, ratio);
+  V3f sn = v3(0.f, 0.f, 0.f);
+  if (x > 0 && x < W - 1 && y > 0 && y < H - 1) {
+    auto point = [&](size_t q) {
+      const float d = surf_depth_at(allmap, HW, q, one_minus_ratio, ratio);
+      return v3(d * rays_d[3 * q] + ray_o[0], d * rays_d[3 * q + 1] + ray_o[1],
+                d * rays_d[3 * q + 2] + ray_o[2]);
+    };
+    const V3f dx = vsub3(point((size_t)(y + 1) * W + x), point((size_t)(y - 1) * W + x));
+    const V3f dy = vsub3(point((size_t)y * W + x + 1), point((size_t)y * W + x - 1));
+    const V3f m = vcross(dx, dy);
+    const float inv = 1.0f / fmaxf(sqrtf(vdot(m, m)), 1e-12f);
+    const float alpha = allmap[HW + p];
+    sn = v3(m.x * inv * alpha, m.y * inv * alpha, m.z * inv * alpha);
+  }
+  out[6 * HW + p] = sn.x;
+  out[7 * HW + p] = sn.y;
+  out[8 * HW + p] = sn.z;
+}
+
 }  // namespace
+
+int allmap_decode_launch(const float* allmap, const float* vm, const float* rays_d,
+                         const float* ray_o, int W, int H, float depth_ratio, float* out,
+                         cudaStream_t stream) {
+  const int64_t HW = (int64_t)W * H;
+  if (HW <= 0) return NS_OK;
+  allmap_decode_kernel<<<(unsigned)div_up64(HW, kNormThreads), kNormThreads, 0, stream>>>(
+      allmap, vm, rays_d, ray_o, W, H, 1.0f - depth_ratio, depth_ratio, out);
+  NS_LAUNCH_CHECK();
+  return NS_OK;
+}
 
 int normal_error_launch(const float* allmap, const float* vm, const float* rays_d,
                         const float* ray_o, int W, int H, float* err, cudaStream_t stream) {

@@ -25,6 +25,7 @@ EXPORTED = [
     "ns_rvq_decode", "ns_radix_sort_temp_bytes", "ns_radix_sort_pairs", "ns_render_frame",
     "ns_radix_sort_pairs_noalloc", "ns_backward_scratch_bytes", "ns_rasterize_backward",
     "ns_normal_error", "ns_normal_error_scratch_bytes", "ns_normal_error_backward", "ns_mlp_backward",
+    "ns_allmap_decode",
 ]
 
 
@@ -150,6 +151,8 @@ def load() -> C.CDLL:
                                           C.POINTER(GradsOut), vp, sz, vp, sz, vp, sz, i64, vp, sz, vp]
     lib.ns_mlp_backward.restype = C.c_int
     lib.ns_mlp_backward.argtypes = [vp, i32, i64, vp, i32, i32, vp, vp, vp, vp, vp]
+    lib.ns_allmap_decode.restype = C.c_int
+    lib.ns_allmap_decode.argtypes = [vp, vp, vp, vp, i32, i32, C.c_float, vp, vp]
     lib.ns_normal_error.restype = C.c_int
     lib.ns_normal_error.argtypes = [vp, vp, vp, vp, i32, i32, vp, vp]
     lib.ns_normal_error_scratch_bytes.restype = sz

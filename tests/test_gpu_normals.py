@@ -130,3 +130,28 @@ def test_normal_error_on_rasterized_allmap():
     err, ref, g, gr = kernel_and_torch(allmap, cam)
     assert float((err - ref).abs().max()) < 2e-3
     check_grads(g, gr, alpha.cuda())
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("ratio", [0.0, 1.0, 0.3])
+def test_render_maps_match_torch(ratio):
+    """ns_allmap_decode (the render_pkg maps) against the reference's torch
+    expressions, including NaN / +inf median depths (nan_to_num -> 0)."""
+    from nest_b200 import maps
+
+    W, H = 120, 90
+    cam = camera.orbit_camera(W, H, 55.0, azimuth_deg=15.0, elevation_deg=5.0)
+    allmap = synthetic_allmap(W, H, 4)
+    allmap[5, 0, 3] = float("nan")
+    allmap[5, 0, 4] = float("inf")
+    allmap[5, 40, 50] = float("nan")
+    a = allmap.cuda()
+    got = maps.render_maps(a, cam, ratio)
+    ref = maps.render_maps_torch(a, cam, ratio)
+    assert set(got) == set(ref)
+    for k in ref:
+        g, r = got[k], ref[k]
+        assert g.shape == r.shape, k
+        assert torch.isfinite(g).all(), k
+        err = float((g - r).abs().max())
+        assert err < 2e-3, (k, err)
