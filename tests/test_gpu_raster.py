@@ -119,6 +119,19 @@ def test_raster_settings_variants(opt):
     compare(out, color, allmap)
 
 
+@pytest.mark.parametrize("ac,interp", [(True, 0), (False, 1), (True, 1)])
+def test_raster_grid_variants(ac, interp):
+    """align_corners (dense levels index R = res, hashgrid.h:28-31) and the
+    smoothstep interpolation (hashgrid.h:140-152)."""
+    sc = small_scene(n=1200, seed=15)
+    sc.grid.align_corners = ac
+    sc.grid.interpolation = interp
+    inp = api_inputs(sc)
+    out, pre, n = oracle_render(sc, inp, align_corners=ac, interp=interp)
+    color, radii, allmap, _, _ = run_api(sc, inp)
+    compare(out, color, allmap)
+
+
 def test_raster_homotrans_computed_when_absent():
     sc = small_scene(n=1000, seed=14)
     inp = api_inputs(sc)
