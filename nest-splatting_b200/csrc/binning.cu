@@ -99,10 +99,10 @@ sorted_block_totals_kernel(int P, const uint32_t* __restrict__ order,
 __global__ void __launch_bounds__(kDupThreads)
 duplicate_keys_kernel(int P, const uint32_t* __restrict__ order, const BinInfo* __restrict__ bin,
                       const uint32_t* __restrict__ tiles, const uint32_t* __restrict__ block_prefix,
-                      int gx, uint64_t* __restrict__ keys, uint32_t* __restrict__ vals,
+                      int gx, uint32_t* __restrict__ keys, uint32_t* __restrict__ vals,
                       int64_t capacity, uint32_t* __restrict__ err) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
-  uint64_t* sk = reinterpret_cast<uint64_t*>(smem_raw);
+  uint32_t* sk = reinterpret_cast<uint32_t*>(smem_raw);
   uint32_t* sv = reinterpret_cast<uint32_t*>(sk + kDupStage);
   __shared__ uint32_t warp_tot[kDupThreads / 32];
   const int k = blockIdx.x * kDupThreads + threadIdx.x;
@@ -120,7 +120,7 @@ duplicate_keys_kernel(int P, const uint32_t* __restrict__ order, const BinInfo* 
     int64_t off = (int64_t)(incl - n);
     for (int y = b.y0; y < b.y1; y++) {
       for (int x = b.x0; x < b.x1; x++) {
-        const uint64_t key = (uint64_t)(uint32_t)(y * gx + x);
+        const uint32_t key = (uint32_t)(y * gx + x);
         if (off < kDupStage) {
           sk[off] = key;
           sv[off] = i;
@@ -140,7 +140,7 @@ duplicate_keys_kernel(int P, const uint32_t* __restrict__ order, const BinInfo* 
   }
 }
 
-__global__ void identify_ranges_kernel(const uint64_t* __restrict__ keys,
+__global__ void identify_ranges_kernel(const uint32_t* __restrict__ keys,
                                        const int64_t* __restrict__ count_dev, int64_t count_host,
                                        int64_t capacity, uint2* __restrict__ ranges) {
   int64_t n = count_dev ? min(*count_dev, capacity) : count_host;
@@ -171,7 +171,7 @@ int scan_block_sums_launch(const uint32_t* sums, uint32_t* prefix, int nb, int64
 
 int duplicate_keys_launch(int P, const uint32_t* order, const BinInfo* bin, const uint32_t* tiles,
                           uint32_t* sorted_sums, uint32_t* sorted_prefix, int64_t* total, int gx,
-                          uint64_t* keys, uint32_t* vals, int64_t capacity, uint32_t* err,
+                          uint32_t* keys, uint32_t* vals, int64_t capacity, uint32_t* err,
                           cudaStream_t stream) {
   if (P <= 0) return NS_OK;
   const int nb = div_up(P, kDupThreads);
@@ -179,7 +179,7 @@ int duplicate_keys_launch(int P, const uint32_t* order, const BinInfo* bin, cons
   NS_LAUNCH_CHECK();
   int rc = scan_block_sums_launch(sorted_sums, sorted_prefix, nb, total, stream);
   if (rc) return rc;
-  const int smem = kDupStage * (int)(sizeof(uint64_t) + sizeof(uint32_t));
+  const int smem = kDupStage * (int)(2 * sizeof(uint32_t));
   NS_CUDA_TRY(cudaFuncSetAttribute(duplicate_keys_kernel,
                                    cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
   duplicate_keys_kernel<<<nb, kDupThreads, smem, stream>>>(P, order, bin, tiles, sorted_prefix, gx,
@@ -188,7 +188,7 @@ int duplicate_keys_launch(int P, const uint32_t* order, const BinInfo* bin, cons
   return NS_OK;
 }
 
-int identify_ranges_launch(const uint64_t* keys, const int64_t* count_dev, int64_t count_host,
+int identify_ranges_launch(const uint32_t* keys, const int64_t* count_dev, int64_t count_host,
                            int64_t capacity, uint2* ranges, int tiles, int sms,
                            cudaStream_t stream) {
   NS_CUDA_TRY(cudaMemsetAsync(ranges, 0, sizeof(uint2) * (size_t)tiles, stream));

@@ -54,9 +54,9 @@ struct GeomState {
   uint32_t* err;
   // Depth sort of the surfels (binning step 1) and the per-CTA totals of the
   // tile counts in depth order.
-  uint64_t* depth_keys;
-  uint64_t* depth_keys_alt;
-  uint64_t* depth_keys_sorted;
+  uint32_t* depth_keys;
+  uint32_t* depth_keys_alt;
+  uint32_t* depth_keys_sorted;
   uint32_t* depth_vals;
   uint32_t* depth_vals_alt;
   uint32_t* depth_vals_sorted;  // surfel indices in depth order
@@ -78,9 +78,9 @@ GeomState carve_geom(void* base, int P, size_t* used) {
   g.count = c.take<int64_t>(1);
   g.err = c.take<uint32_t>(4);
   const size_t np = (size_t)max(P, 1);
-  g.depth_keys = c.take<uint64_t>(np);
-  g.depth_keys_alt = c.take<uint64_t>(np);
-  g.depth_keys_sorted = c.take<uint64_t>(np);
+  g.depth_keys = c.take<uint32_t>(np);
+  g.depth_keys_alt = c.take<uint32_t>(np);
+  g.depth_keys_sorted = c.take<uint32_t>(np);
   g.depth_vals = c.take<uint32_t>(np);
   g.depth_vals_alt = c.take<uint32_t>(np);
   g.depth_vals_sorted = c.take<uint32_t>(np);
@@ -111,9 +111,9 @@ ImageState carve_image(void* base, int W, int H, size_t* used) {
 }
 
 struct BinState {
-  uint64_t* keys_unsorted;
-  uint64_t* keys_alt;
-  uint64_t* keys_sorted;
+  uint32_t* keys_unsorted;  // tile ids
+  uint32_t* keys_alt;
+  uint32_t* keys_sorted;
   uint32_t* vals_unsorted;
   uint32_t* vals_alt;
   uint32_t* vals_sorted;
@@ -125,9 +125,9 @@ BinState carve_bin(void* base, int64_t cap, size_t* used) {
   Carver c{reinterpret_cast<char*>(base)};
   BinState b;
   const size_t n = (size_t)max64(cap, 1);
-  b.keys_unsorted = c.take<uint64_t>(n);
-  b.keys_alt = c.take<uint64_t>(n);
-  b.keys_sorted = c.take<uint64_t>(n);
+  b.keys_unsorted = c.take<uint32_t>(n);
+  b.keys_alt = c.take<uint32_t>(n);
+  b.keys_sorted = c.take<uint32_t>(n);
   b.vals_unsorted = c.take<uint32_t>(n);
   b.vals_alt = c.take<uint32_t>(n);
   b.vals_sorted = c.take<uint32_t>(n);
@@ -204,7 +204,7 @@ int bin_and_render(const ns_raster_settings* st, int P, const GeomState& g, cons
   if (flags & NS_FLAG_DEVICE_COUNT) return NS_ERR_UNSUPPORTED;
   // Binning step 1, the depth sort of the surfels, runs while the host waits
   // for the instance count.
-  rc = radix_sort_launch(g.depth_keys, g.depth_vals, g.depth_keys_sorted, g.depth_vals_sorted,
+  rc = radix_sort32_launch(g.depth_keys, g.depth_vals, g.depth_keys_sorted, g.depth_vals_sorted,
                          g.depth_keys_alt, g.depth_vals_alt, P, 32, g.depth_sort_temp,
                          g.depth_sort_temp_bytes, stream);
   if (rc) return rc;
@@ -219,7 +219,7 @@ int bin_and_render(const ns_raster_settings* st, int P, const GeomState& g, cons
                              g.err, stream);
   if (rc) return rc;
   const int end_bit = (int)higher_msb((uint32_t)tiles);
-  rc = radix_sort_launch(b.keys_unsorted, b.vals_unsorted, b.keys_sorted, b.vals_sorted, b.keys_alt,
+  rc = radix_sort32_launch(b.keys_unsorted, b.vals_unsorted, b.keys_sorted, b.vals_sorted, b.keys_alt,
                          b.vals_alt, count, end_bit, b.sort_temp, b.sort_temp_bytes, stream);
   if (rc) return rc;
   rc = identify_ranges_launch(b.keys_sorted, nullptr, count, cap, im.ranges, tiles, num_sms(),

@@ -69,12 +69,12 @@ int preprocess_blocks(int P);
 int preprocess_block_size();
 int preprocess_api_launch(int P, const ns_surfels& s, float mod, float beta, const float* vm,
                           const float* pm, int W, int H, SurfelRecord* records, BinInfo* bin,
-                          int32_t* radii, uint32_t* tiles, uint64_t* depth_keys,
+                          int32_t* radii, uint32_t* tiles, uint32_t* depth_keys,
                           uint32_t* depth_vals, uint32_t* block_sums, cudaStream_t stream);
 int preprocess_mix_launch(int P, const float* base, const float* decoded, int dims, float mix,
                           const float* ap_level, float mod, float beta, const float* vm,
                           const float* pm, int W, int H, SurfelRecord* records, BinInfo* bin,
-                          int32_t* radii, uint32_t* tiles, uint64_t* depth_keys,
+                          int32_t* radii, uint32_t* tiles, uint32_t* depth_keys,
                           uint32_t* depth_vals, uint32_t* block_sums, cudaStream_t stream);
 int mark_visible_launch(int P, const float* means3D, const float* vm, uint8_t* present,
                         cudaStream_t stream);
@@ -82,15 +82,18 @@ int scan_block_sums_launch(const uint32_t* sums, uint32_t* prefix, int nb, int64
                            cudaStream_t stream);
 int duplicate_keys_launch(int P, const uint32_t* order, const BinInfo* bin, const uint32_t* tiles,
                           uint32_t* sorted_sums, uint32_t* sorted_prefix, int64_t* total, int gx,
-                          uint64_t* keys, uint32_t* vals, int64_t capacity, uint32_t* err,
+                          uint32_t* keys, uint32_t* vals, int64_t capacity, uint32_t* err,
                           cudaStream_t stream);
-int identify_ranges_launch(const uint64_t* keys, const int64_t* count_dev, int64_t count_host,
+int identify_ranges_launch(const uint32_t* keys, const int64_t* count_dev, int64_t count_host,
                            int64_t capacity, uint2* ranges, int tiles, int sms,
                            cudaStream_t stream);
 size_t radix_sort_temp_bytes(int64_t n);
 int radix_sort_launch(const uint64_t* keys_in, const uint32_t* vals_in, uint64_t* keys_out,
                       uint32_t* vals_out, uint64_t* keys_alt, uint32_t* vals_alt, int64_t n,
                       int end_bit, void* temp, size_t temp_bytes, cudaStream_t stream);
+int radix_sort32_launch(const uint32_t* keys_in, const uint32_t* vals_in, uint32_t* keys_out,
+                        uint32_t* vals_out, uint32_t* keys_alt, uint32_t* vals_alt, int64_t n,
+                        int end_bit, void* temp, size_t temp_bytes, cudaStream_t stream);
 uint32_t* radix_sort_error_word(void* temp);
 int render_launch(const RenderParams& p, int fp16, cudaStream_t stream);
 int mlp_launch(const float* feat, int in_dims, int64_t npix, const uint16_t* weights, int hidden,

@@ -103,7 +103,7 @@ struct PreOut {
   BinInfo* bin;
   int32_t* radii;
   uint32_t* tiles;       // tiles touched
-  uint64_t* depth_keys;  // float bits of the view depth (all ones when no tile is touched)
+  uint32_t* depth_keys;  // float bits of the view depth (all ones when no tile is touched)
   uint32_t* depth_vals;  // surfel index
   uint32_t* block_sums;  // per-CTA total of the tile counts
 };
@@ -290,7 +290,7 @@ preprocess_kernel(int P, Attrs attrs, float mod, float beta, const float* __rest
     out.bin[i] = bi;
     out.radii[i] = radius;
     out.tiles[i] = tiles;
-    out.depth_keys[i] = tiles ? (uint64_t)__float_as_uint(bi.depth) : 0xffffffffull;
+    out.depth_keys[i] = tiles ? __float_as_uint(bi.depth) : 0xffffffffu;
     out.depth_vals[i] = (uint32_t)i;
   }
   // CTA total of the tile counts (the instance count is their sum).
@@ -324,7 +324,7 @@ int preprocess_block_size() { return kPreThreads; }
 
 int preprocess_api_launch(int P, const ns_surfels& s, float mod, float beta, const float* vm,
                           const float* pm, int W, int H, SurfelRecord* records, BinInfo* bin,
-                          int32_t* radii, uint32_t* tiles, uint64_t* depth_keys,
+                          int32_t* radii, uint32_t* tiles, uint32_t* depth_keys,
                           uint32_t* depth_vals, uint32_t* block_sums, cudaStream_t stream) {
   ApiAttrs a{s.means3D, s.scales, s.rotations, s.opacities, s.homotrans, s.ap_level};
   PreOut o{records, bin, radii, tiles, depth_keys, depth_vals, block_sums};
@@ -337,7 +337,7 @@ int preprocess_api_launch(int P, const ns_surfels& s, float mod, float beta, con
 int preprocess_mix_launch(int P, const float* base, const float* decoded, int dims, float mix,
                           const float* ap_level, float mod, float beta, const float* vm,
                           const float* pm, int W, int H, SurfelRecord* records, BinInfo* bin,
-                          int32_t* radii, uint32_t* tiles, uint64_t* depth_keys,
+                          int32_t* radii, uint32_t* tiles, uint32_t* depth_keys,
                           uint32_t* depth_vals, uint32_t* block_sums, cudaStream_t stream) {
   MixAttrs a{base, decoded, dims, mix, ap_level};
   PreOut o{records, bin, radii, tiles, depth_keys, depth_vals, block_sums};

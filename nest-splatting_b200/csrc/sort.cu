@@ -38,6 +38,8 @@ constexpr uint32_t kValueMask = ~kFlagMask;
 // Layout of the temp buffer (all u32).
 struct SortTemp {
   uint32_t* hist;      // [kMaxPasses][256]
+  uint32_t* count;     // [kMaxPasses][256]
+  uint32_t* nz;        // [kMaxPasses]
   uint32_t* tile_ctr;  // [kMaxPasses]
   uint32_t* err;       // [1]
   uint32_t* status;    // [kMaxPasses][tiles][256]
@@ -46,7 +48,7 @@ struct SortTemp {
 __host__ __device__ inline int64_t sort_tiles(int64_t n) { return div_up64(n, kSortTile); }
 
 __host__ inline size_t sort_temp_words(int64_t n) {
-  return (size_t)kMaxPasses * kRadix + kMaxPasses + 1 + 1 /*pad*/ +
+  return (size_t)2 * kMaxPasses * kRadix + 2 * kMaxPasses + 1 + 1 /*pad*/ +
          (size_t)kMaxPasses * (size_t)max64(1, sort_tiles(n)) * kRadix;
 }
 
@@ -54,7 +56,9 @@ __host__ inline SortTemp carve(void* temp, int64_t n) {
   SortTemp t;
   uint32_t* p = reinterpret_cast<uint32_t*>(temp);
   t.hist = p;
-  t.tile_ctr = p + kMaxPasses * kRadix;
+  t.count = p + kMaxPasses * kRadix;
+  t.nz = t.count + kMaxPasses * kRadix;
+  t.tile_ctr = t.nz + kMaxPasses;
   t.err = t.tile_ctr + kMaxPasses;
   t.status = t.err + 2;
   (void)n;
@@ -73,32 +77,48 @@ __device__ __forceinline__ uint32_t load_volatile(const uint32_t* p) {
   return v;
 }
 
-// Histogram of every digit position in one pass over the keys.
-__global__ void __launch_bounds__(256) upfront_histogram_kernel(const uint64_t* __restrict__ keys,
-                                                                int64_t n, int passes,
-                                                                uint32_t* __restrict__ hist) {
-  __shared__ uint32_t h[kMaxPasses][kRadix];
-  for (int i = threadIdx.x; i < kMaxPasses * kRadix; i += blockDim.x) (&h[0][0])[i] = 0;
+// Histogram of every digit position in one pass over the keys. Each warp
+// counts into its own shared-memory histogram (keys with few distinct digits
+// would otherwise serialise all the CTA's atomics on a few words).
+constexpr int kHistThreads = 256;
+template <typename KeyT>
+__global__ void __launch_bounds__(kHistThreads) upfront_histogram_kernel(const KeyT* __restrict__ keys,
+                                                                         int64_t n, int passes,
+                                                                         uint32_t* __restrict__ hist) {
+  extern __shared__ uint32_t hw[];  // [warps][passes][kRadix]
+  const int w = threadIdx.x >> 5;
+  const int words = (kHistThreads / 32) * passes * kRadix;
+  for (int i = threadIdx.x; i < words; i += blockDim.x) hw[i] = 0;
   __syncthreads();
+  uint32_t* h = hw + w * passes * kRadix;
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
        i += (int64_t)gridDim.x * blockDim.x) {
-    const uint64_t k = keys[i];
-    for (int p = 0; p < passes; p++) atomicAdd(&h[p][(k >> (p * kRadixBits)) & (kRadix - 1)], 1u);
+    const uint64_t k = (uint64_t)keys[i];
+    for (int p = 0; p < passes; p++) atomicAdd(&h[p * kRadix + ((k >> (p * kRadixBits)) & (kRadix - 1))], 1u);
   }
   __syncthreads();
   for (int i = threadIdx.x; i < passes * kRadix; i += blockDim.x) {
-    uint32_t v = (&h[0][0])[i];
+    uint32_t v = 0;
+    for (int ww = 0; ww < kHistThreads / 32; ww++) v += hw[ww * passes * kRadix + i];
     if (v) atomicAdd(hist + i, v);
   }
 }
 
-// In place: hist[p][d] -> exclusive prefix over d (the bucket base of digit d).
-__global__ void bucket_scan_kernel(uint32_t* __restrict__ hist, int passes) {
+// In place: hist[p][d] -> exclusive prefix over d (the bucket base of digit d);
+// the digit counts are kept in cnt[p][d], the number of digits that occur in
+// nz[p].
+__global__ void bucket_scan_kernel(uint32_t* __restrict__ hist, uint32_t* __restrict__ cnt,
+                                   uint32_t* __restrict__ nz, int passes) {
   __shared__ uint32_t warp_tot[kRadix / 32];
   const int p = blockIdx.x;
   if (p >= passes) return;
   const int t = threadIdx.x, lane = t & 31, w = t >> 5;
   uint32_t v = hist[p * kRadix + t];
+  cnt[p * kRadix + t] = v;
+  {
+    const uint32_t m = __ballot_sync(0xffffffffu, v != 0);
+    if (lane == 0) atomicAdd(nz + p, (uint32_t)__popc(m));
+  }
   uint32_t x = v;
 #pragma unroll
   for (int o = 1; o < 32; o <<= 1) {
@@ -112,23 +132,39 @@ __global__ void bucket_scan_kernel(uint32_t* __restrict__ hist, int passes) {
   hist[p * kRadix + t] = x - v + add;
 }
 
+template <typename KeyT>
 struct PassSmem {
   uint32_t warp_hist[kSortWarps][kRadix];
   uint32_t digit_excl[kRadix];
   uint32_t global_base[kRadix];
   uint32_t warp_tot[kSortWarps];
   uint32_t tile;
-  uint64_t keys[kSortTile];
+  KeyT keys[kSortTile];
   uint32_t vals[kSortTile];
 };
 
+// Lanes of the warp whose 8-bit digit equals this lane's: eight ballots, one
+// per digit bit (the warp multi-split of a radix pass).
+__device__ __forceinline__ uint32_t equal_digit_lanes(uint32_t d) {
+  uint32_t eq = 0xffffffffu;
+#pragma unroll
+  for (int b = 0; b < kRadixBits; b++) {
+    const uint32_t bit = (d >> b) & 1u;
+    const uint32_t bal = __ballot_sync(0xffffffffu, bit);
+    eq &= bit ? bal : ~bal;
+  }
+  return eq;
+}
+
+template <typename KeyT>
 __global__ void __launch_bounds__(kSortThreads)
-onesweep_pass_kernel(const uint64_t* __restrict__ keys_in, const uint32_t* __restrict__ vals_in,
-                     uint64_t* __restrict__ keys_out, uint32_t* __restrict__ vals_out, int64_t n,
-                     int shift, const uint32_t* __restrict__ bucket_base, uint32_t* status,
-                     uint32_t* tile_ctr, uint32_t* err) {
+onesweep_pass_kernel(const KeyT* __restrict__ keys_in, const uint32_t* __restrict__ vals_in,
+                     KeyT* __restrict__ keys_out, uint32_t* __restrict__ vals_out, int64_t n,
+                     int shift, const uint32_t* __restrict__ bucket_base,
+                     const uint32_t* __restrict__ bucket_count, const uint32_t* __restrict__ nz_digits,
+                     uint32_t* status, uint32_t* tile_ctr, uint32_t* err) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
-  PassSmem& S = *reinterpret_cast<PassSmem*>(smem_raw);
+  PassSmem<KeyT>& S = *reinterpret_cast<PassSmem<KeyT>*>(smem_raw);
   const int t = threadIdx.x, lane = t & 31, w = t >> 5;
 
   if (t == 0) S.tile = atomicAdd(tile_ctr, 1u);
@@ -137,7 +173,7 @@ onesweep_pass_kernel(const uint64_t* __restrict__ keys_in, const uint32_t* __res
   const uint32_t tile = S.tile;
   const int64_t tile_base = (int64_t)tile * kSortTile;
 
-  uint64_t key[kSortItems];
+  KeyT key[kSortItems];
   uint32_t val[kSortItems];
   uint32_t rank[kSortItems];
 #pragma unroll
@@ -147,15 +183,18 @@ onesweep_pass_kernel(const uint64_t* __restrict__ keys_in, const uint32_t* __res
       key[k] = keys_in[i];
       val[k] = vals_in[i];
     } else {
-      key[k] = ~0ull;  // digit 255: ranks after every valid key of the tile
+      key[k] = (KeyT)~(KeyT)0;  // digit 255: ranks after every valid key of the tile
       val[k] = 0;
     }
   }
   const uint32_t lt = lanemask_lt();
+  // match-any is cheap when a warp's keys share few digits, the ballots when
+  // they are spread: choose by the number of digits the pass has (uniform).
+  const bool spread = *nz_digits > 32u;
 #pragma unroll
   for (int k = 0; k < kSortItems; k++) {
     const uint32_t d = (uint32_t)(key[k] >> shift) & (kRadix - 1);
-    const uint32_t peers = __match_any_sync(0xffffffffu, d);
+    const uint32_t peers = spread ? equal_digit_lanes(d) : __match_any_sync(0xffffffffu, d);
     const uint32_t before = __popc(peers & lt);
     const uint32_t prior = S.warp_hist[w][d];
     __syncwarp();
@@ -196,9 +235,9 @@ onesweep_pass_kernel(const uint64_t* __restrict__ keys_in, const uint32_t* __res
     S.digit_excl[t] = x - count + add;
   }
 
-  // Decoupled look-back for digit t.
+  // Decoupled look-back for digit t (none for a digit no key of the pass has).
   uint32_t prefix = 0;
-  if (tile > 0) {
+  if (tile > 0 && bucket_count[t] != 0) {
     int64_t j = (int64_t)tile - 1;
     bool ok = true;
     while (j >= 0) {
@@ -232,7 +271,7 @@ onesweep_pass_kernel(const uint64_t* __restrict__ keys_in, const uint32_t* __res
 
   const int valid = (int)min64(kSortTile, n - tile_base);
   for (int i = t; i < valid; i += kSortThreads) {
-    const uint64_t k = S.keys[i];
+    const KeyT k = S.keys[i];
     const uint32_t d = (uint32_t)(k >> shift) & (kRadix - 1);
     const uint32_t dst = S.global_base[d] + (uint32_t)i - S.digit_excl[d];
     // dst < n whenever the look-back completed; the guard keeps a timed-out
@@ -244,6 +283,54 @@ onesweep_pass_kernel(const uint64_t* __restrict__ keys_in, const uint32_t* __res
   }
 }
 
+template <typename KeyT>
+int radix_sort_impl(const KeyT* keys_in, const uint32_t* vals_in, KeyT* keys_out, uint32_t* vals_out,
+                    KeyT* keys_alt, uint32_t* vals_alt, int64_t n, int end_bit, void* temp,
+                    size_t temp_bytes, cudaStream_t stream) {
+  if (n < 0 || end_bit < 0 || end_bit > (int)(8 * sizeof(KeyT))) return NS_ERR_INVALID;
+  if (n >= (int64_t)kValueMask) return NS_ERR_UNSUPPORTED;
+  if (temp_bytes < sort_temp_words(n) * sizeof(uint32_t)) return NS_ERR_SCRATCH;
+  if (n == 0) return NS_OK;
+  int passes = div_up(max(end_bit, 1), kRadixBits);
+  SortTemp T = carve(temp, n);
+  const int64_t tiles = sort_tiles(n);
+  NS_CUDA_TRY(cudaMemsetAsync(temp, 0,
+                              ((size_t)2 * kMaxPasses * kRadix + 2 * kMaxPasses + 2 +
+                               (size_t)passes * tiles * kRadix) * sizeof(uint32_t),
+                              stream));
+  int dev = 0, sms = 0;
+  NS_CUDA_TRY(cudaGetDevice(&dev));
+  NS_CUDA_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+  const int hblocks = (int)min64(div_up64(n, 256 * 8), (int64_t)sms * 4);
+  const size_t hsmem = (size_t)(kHistThreads / 32) * passes * kRadix * sizeof(uint32_t);
+  if (hsmem > 48 * 1024)
+    NS_CUDA_TRY(cudaFuncSetAttribute(upfront_histogram_kernel<KeyT>,
+                                     cudaFuncAttributeMaxDynamicSharedMemorySize, (int)hsmem));
+  upfront_histogram_kernel<KeyT><<<max(1, hblocks), kHistThreads, hsmem, stream>>>(keys_in, n, passes,
+                                                                                  T.hist);
+  NS_LAUNCH_CHECK();
+  bucket_scan_kernel<<<passes, kRadix, 0, stream>>>(T.hist, T.count, T.nz, passes);
+  NS_LAUNCH_CHECK();
+  const size_t smem = sizeof(PassSmem<KeyT>);
+  NS_CUDA_TRY(cudaFuncSetAttribute(onesweep_pass_kernel<KeyT>,
+                                   cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  // Ping-pong so that the last pass writes keys_out/vals_out.
+  const KeyT* kin = keys_in;
+  const uint32_t* vin = vals_in;
+  for (int p = 0; p < passes; p++) {
+    const bool to_out = ((passes - 1 - p) % 2) == 0;
+    KeyT* kout = to_out ? keys_out : keys_alt;
+    uint32_t* vout = to_out ? vals_out : vals_alt;
+    onesweep_pass_kernel<KeyT><<<(unsigned)tiles, kSortThreads, smem, stream>>>(
+        kin, vin, kout, vout, n, p * kRadixBits, T.hist + p * kRadix, T.count + p * kRadix,
+        T.nz + p, T.status + (size_t)p * tiles * kRadix, T.tile_ctr + p, T.err);
+    NS_LAUNCH_CHECK();
+    kin = kout;
+    vin = vout;
+  }
+  return NS_OK;
+}
+
 }  // namespace
 
 size_t radix_sort_temp_bytes(int64_t n) { return sort_temp_words(n) * sizeof(uint32_t); }
@@ -253,43 +340,16 @@ size_t radix_sort_temp_bytes(int64_t n) { return sort_temp_words(n) * sizeof(uin
 int radix_sort_launch(const uint64_t* keys_in, const uint32_t* vals_in, uint64_t* keys_out,
                       uint32_t* vals_out, uint64_t* keys_alt, uint32_t* vals_alt, int64_t n,
                       int end_bit, void* temp, size_t temp_bytes, cudaStream_t stream) {
-  if (n < 0 || end_bit < 0 || end_bit > 64) return NS_ERR_INVALID;
-  if (n >= (int64_t)kValueMask) return NS_ERR_UNSUPPORTED;
-  if (temp_bytes < radix_sort_temp_bytes(n)) return NS_ERR_SCRATCH;
-  if (n == 0) return NS_OK;
-  int passes = div_up(max(end_bit, 1), kRadixBits);
-  SortTemp T = carve(temp, n);
-  const int64_t tiles = sort_tiles(n);
-  NS_CUDA_TRY(cudaMemsetAsync(temp, 0,
-                              ((size_t)kMaxPasses * kRadix + kMaxPasses + 2 +
-                               (size_t)passes * tiles * kRadix) * sizeof(uint32_t),
-                              stream));
-  int dev = 0, sms = 0;
-  NS_CUDA_TRY(cudaGetDevice(&dev));
-  NS_CUDA_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
-  const int hblocks = (int)min64(div_up64(n, 256 * 8), (int64_t)sms * 4);
-  upfront_histogram_kernel<<<max(1, hblocks), 256, 0, stream>>>(keys_in, n, passes, T.hist);
-  NS_LAUNCH_CHECK();
-  bucket_scan_kernel<<<passes, kRadix, 0, stream>>>(T.hist, passes);
-  NS_LAUNCH_CHECK();
-  const size_t smem = sizeof(PassSmem);
-  NS_CUDA_TRY(cudaFuncSetAttribute(onesweep_pass_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                   (int)smem));
-  // Ping-pong so that the last pass writes keys_out/vals_out.
-  const uint64_t* kin = keys_in;
-  const uint32_t* vin = vals_in;
-  for (int p = 0; p < passes; p++) {
-    const bool to_out = ((passes - 1 - p) % 2) == 0;
-    uint64_t* kout = to_out ? keys_out : keys_alt;
-    uint32_t* vout = to_out ? vals_out : vals_alt;
-    onesweep_pass_kernel<<<(unsigned)tiles, kSortThreads, smem, stream>>>(
-        kin, vin, kout, vout, n, p * kRadixBits, T.hist + p * kRadix,
-        T.status + (size_t)p * tiles * kRadix, T.tile_ctr + p, T.err);
-    NS_LAUNCH_CHECK();
-    kin = kout;
-    vin = vout;
-  }
-  return NS_OK;
+  return radix_sort_impl<uint64_t>(keys_in, vals_in, keys_out, vals_out, keys_alt, vals_alt, n,
+                                   end_bit, temp, temp_bytes, stream);
+}
+
+// The same for 32-bit keys (end_bit <= 32): two thirds of the traffic per pass.
+int radix_sort32_launch(const uint32_t* keys_in, const uint32_t* vals_in, uint32_t* keys_out,
+                        uint32_t* vals_out, uint32_t* keys_alt, uint32_t* vals_alt, int64_t n,
+                        int end_bit, void* temp, size_t temp_bytes, cudaStream_t stream) {
+  return radix_sort_impl<uint32_t>(keys_in, vals_in, keys_out, vals_out, keys_alt, vals_alt, n,
+                                   end_bit, temp, temp_bytes, stream);
 }
 
 // Address of the sort's device error word inside temp (for status reads).

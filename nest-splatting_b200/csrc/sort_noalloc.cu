@@ -28,7 +28,11 @@ constexpr int64_t kNoAllocMaxPairs = int64_t(1) << 20;
 // keys_alt (8 B) + vals_alt (4 B) per pair, then the sort's temp words.
 constexpr size_t kAltKeysBytes = size_t(kNoAllocMaxPairs) * sizeof(uint64_t);
 constexpr size_t kAltValsBytes = size_t(kNoAllocMaxPairs) * sizeof(uint32_t);
-constexpr size_t kTempBytesMax = (size_t(8) * 256 + 8 + 2 + size_t(8) * 256 * 256) * sizeof(uint32_t);
+// histograms + digit counts (2 x 8 x 256), digits-present and tile counters
+// (2 x 8), error word, pad, look-back words of 8 passes x 256 tiles x 256
+// digits (radix_sort_temp_bytes(kNoAllocMaxPairs)).
+constexpr size_t kTempBytesMax =
+    (size_t(2) * 8 * 256 + 2 * 8 + 2 + size_t(8) * 256 * 256) * sizeof(uint32_t);
 constexpr size_t kNoAllocBytes = kAltKeysBytes + kAltValsBytes + kTempBytesMax;
 
 __device__ __align__(256) unsigned char g_sort_scratch[kNoAllocBytes];
