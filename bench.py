@@ -311,7 +311,7 @@ def run_ours(args):
         "rvq_decode": {"gbs": round(rvq_gbs, 1) if rvq_gbs else None,
                        "frac_of_hbm": round(rvq_gbs / hbm_peak, 4) if rvq_gbs else None,
                        "bytes_per_surfel": fr.stages + 4 * fr.dims},
-        "roofline": {"kernel": "blend_kernel<__half>", "bound": "hbm",
+        "roofline": {"kernel": "blend_kernel<__half, false>", "bound": "hbm",
                      "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s",
                      "frac": round(achieved / hbm_peak, 4), "traffic": traffic,
                      "peak_kind": peak_kind, "algorithmic_bytes": int(blend_bytes),

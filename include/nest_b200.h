@@ -91,6 +91,11 @@ typedef struct ns_raster_settings {
   uint32_t channels;          /* C = shape_dims[2], output feature channels */
   uint32_t level_dim;         /* LD = features.size(1) */
   int32_t table_fp16;         /* 1: features are fp16, 0: fp32 */
+  /* Splat kernel (forward.cu:864-919): 0 Gaussian (with beta above), 1 beta
+   * kernel alpha = o (1 - rho)^shape for rho < 1, 2 flex (per-surfel beta =
+   * shape), 3 general G = exp(-0.5 rho^(shape / 2)); 1-3 read ns_surfels.shapes.
+   * Forward only: ns_rasterize_backward and ns_render_frame take kernel 0. */
+  int32_t kernel_type;
 } ns_raster_settings;
 
 /* Per-surfel inputs of the rasterizer (render_mode 0). */
@@ -105,6 +110,7 @@ typedef struct ns_surfels {
   const void* features;   /* hash table [sum_l T_l, LD], fp32 or fp16 */
   const int32_t* offsets; /* [L+1] int32 level offsets (rows) */
   const float* gridrange; /* [2] = (vmin, vmax) */
+  const float* shapes;    /* [P] per-surfel kernel parameter for kernel_type 1-3, else NULL */
 } ns_surfels;
 
 /* Outputs (caller-owned, device). cover_pixels / trans_avg may be NULL when

@@ -183,6 +183,7 @@ int validate_settings(const ns_raster_settings* s) {
   if (s->levels == 0) return NS_ERR_UNSUPPORTED;  // level == 0 (per-surfel colours) not built
   if (s->level_dim == 0 || s->channels == 0) return NS_ERR_INVALID;
   if (s->levels * s->level_dim > s->channels) return NS_ERR_INVALID;
+  if (s->kernel_type < 0 || s->kernel_type > 3) return NS_ERR_UNSUPPORTED;
   return NS_OK;
 }
 
@@ -238,6 +239,7 @@ int bin_and_render(const ns_raster_settings* st, int P, const GeomState& g, cons
   rp.interp = st->interpolation;
   rp.contract = st->if_contract;
   rp.beta = st->beta;
+  rp.kernel_type = st->kernel_type;
   rp.max_intersections = st->max_intersections;
   rp.record_transmittance = st->record_transmittance;
   rp.ranges = im.ranges;
@@ -309,6 +311,7 @@ int ns_rasterize_forward(const ns_raster_settings* settings, const ns_surfels* s
       !surfels->features || !surfels->offsets || !surfels->gridrange)
     return NS_ERR_INVALID;
   if (!outputs->out_color || !outputs->out_others || !outputs->radii) return NS_ERR_INVALID;
+  if (settings->kernel_type != 0 && P > 0 && !surfels->shapes) return NS_ERR_INVALID;
   if (settings->record_transmittance && (!outputs->cover_pixels || !outputs->trans_avg))
     return NS_ERR_INVALID;
   if (settings->level_dim != 2) return NS_ERR_UNSUPPORTED;
@@ -319,7 +322,7 @@ int ns_rasterize_forward(const ns_raster_settings* settings, const ns_surfels* s
   ImageState im = carve_image(image, settings->image_width, settings->image_height, nullptr);
   NS_CUDA_TRY(cudaMemsetAsync(g.err, 0, sizeof(uint32_t), stream));
   rc = preprocess_api_launch(P, *surfels, settings->scale_modifier, settings->beta,
-                             settings->viewmatrix,
+                             settings->kernel_type, settings->viewmatrix,
                              settings->projmatrix, settings->image_width, settings->image_height,
                              g.records, g.bin, outputs->radii, g.tiles, g.depth_keys, g.depth_vals,
                              g.block_sums, stream);
@@ -340,6 +343,7 @@ int ns_rasterize_backward(const ns_raster_settings* settings, const ns_surfels* 
                           void* stream_) {
   cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_);
   int rc = validate_settings(settings);
+  if (settings && settings->kernel_type != 0) return NS_ERR_UNSUPPORTED;  // forward only
   if (rc) return rc;
   if (!surfels || !gi || !go) return NS_ERR_INVALID;
   const int P = surfels->P;
@@ -510,6 +514,7 @@ int ns_render_frame(const ns_raster_settings* settings, const ns_frame_inputs* i
                     int64_t* num_rendered, int flags, void* stream_) {
   cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_);
   int rc = validate_settings(settings);
+  if (settings && settings->kernel_type != 0) return NS_ERR_UNSUPPORTED;
   if (rc) return rc;
   if (!in || !out) return NS_ERR_INVALID;
   const int P = in->P;

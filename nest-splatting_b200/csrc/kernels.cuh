@@ -15,6 +15,7 @@ struct RenderParams {
   uint32_t interp;
   int contract;
   float beta;
+  int kernel_type;  // 0 Gaussian, 1 beta, 2 flex, 3 general (record word q7.w = shape)
   uint32_t max_intersections;
   int record_transmittance;
   const uint2* ranges;
@@ -67,7 +68,8 @@ int preprocess_backward_launch(int P, const float* means3D, const float* scales,
 int rvq_decode_launch(const uint8_t*, const float*, float*, int64_t, int, int, int, cudaStream_t);
 int preprocess_blocks(int P);
 int preprocess_block_size();
-int preprocess_api_launch(int P, const ns_surfels& s, float mod, float beta, const float* vm,
+int preprocess_api_launch(int P, const ns_surfels& s, float mod, float beta, int kernel_type,
+                          const float* vm,
                           const float* pm, int W, int H, SurfelRecord* records, BinInfo* bin,
                           int32_t* radii, uint32_t* tiles, uint32_t* depth_keys,
                           uint32_t* depth_vals, uint32_t* block_sums, cudaStream_t stream);

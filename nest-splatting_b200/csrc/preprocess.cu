@@ -28,6 +28,7 @@ struct SurfelIn {
   float opacity;
   float3 su, sv, pk;  // homotrans columns 0, 1 and translation
   float ap;
+  float shape;        // kernel parameter (kernel types 1-3)
 };
 
 struct ApiAttrs {
@@ -37,8 +38,10 @@ struct ApiAttrs {
   const float* opacities;
   const float* homotrans;
   const float* ap_level;
+  const float* shapes;
   __device__ SurfelIn load(int i) const {
     SurfelIn a;
+    a.shape = shapes ? shapes[i] : 0.0f;
     a.p = f3(means3D[3 * i], means3D[3 * i + 1], means3D[3 * i + 2]);
     a.s = make_float2(scales[2 * i], scales[2 * i + 1]);
     a.q = make_float4(rotations[4 * i], rotations[4 * i + 1], rotations[4 * i + 2],
@@ -75,9 +78,10 @@ struct MixAttrs {
     const float* b = base + 10 * (size_t)i;
     const float* d = decoded + (size_t)dims * i;
     float raw[10];
+    SurfelIn a;
+    a.shape = 0.0f;
 #pragma unroll
     for (int k = 0; k < 10; k++) raw[k] = b[k] + mix * d[k];
-    SurfelIn a;
     a.p = f3(raw[0], raw[1], raw[2]);
     a.s = make_float2(expf(raw[3]), expf(raw[4]));
     // torch.nn.functional.normalize: q / max(|q|, 1e-12)
@@ -109,12 +113,40 @@ struct PreOut {
 };
 
 // Squared radius rho (in the units of the blend kernel's rho = min(rho3d, rho2d))
-// beyond which alpha = min(0.99, o * G(rho)) < 1/255, G(rho) = exp(-rho/2) or, for
-// beta > 0, (1+beta) G / (1 + beta G). Returns false when no rho reaches 1/255.
-// A relative margin keeps the bound conservative under float rounding.
-__device__ __forceinline__ bool alpha_cutoff(float o, float beta, float& rho_cut) {
-  const double a = 1.0 / (255.0 * (double)o);  // G' needed
-  if (!(o > 0.0f) || a > 1.001) return false;
+// beyond which alpha = min(0.99, o * G(rho)) < 1/255 (forward.cu:864-919):
+//   kernel 0: G = exp(-rho/2), or for beta > 0 (1+beta) G / (1 + beta G);
+//   kernel 1: G = (1 - rho)^shape on rho < 1;   kernel 2: as 0 with beta = shape;
+//   kernel 3: G = exp(-0.5 max(rho, 1e-8)^(shape/2)).
+// Returns false when no rho reaches 1/255; rho_cut = +inf when G does not fall
+// with rho (kernel 3 with shape <= 0). A relative margin keeps the bound
+// conservative under float rounding.
+__device__ __forceinline__ bool alpha_cutoff(float o, float beta, int kernel_type, float shape,
+                                             float& rho_cut) {
+  if (!(o > 0.0f)) return false;
+  const double a = 1.0 / (255.0 * (double)o);  // G needed
+  if (kernel_type == 1) {
+    if (!(shape > 0.0f)) {  // G >= 1 everywhere on rho < 1
+      rho_cut = 1.0f;
+      return true;
+    }
+    if (a > 1.001) return false;
+    const double rc = 1.0 - pow(a < 1.0 ? a : 1.0, 1.0 / (double)shape);
+    rho_cut = (float)fmin(rc * 1.002 + 1e-3, 1.0);
+    return true;
+  }
+  if (kernel_type == 3) {
+    if (!(shape > 0.0f)) {
+      rho_cut = __int_as_float(0x7f800000);  // +inf
+      return true;
+    }
+    if (a > 1.001) return false;
+    const double lg = a >= 1.0 ? 0.0 : -2.0 * log(a);  // rho^(shape/2) <= 2 ln(255 o)
+    const double rc = pow(lg, 2.0 / (double)shape);
+    rho_cut = (float)(rc * 1.002 + 1e-3);
+    return true;
+  }
+  if (kernel_type == 2) beta = shape > 0.0f ? shape : 0.0f;
+  if (a > 1.001) return false;
   double g = a;
   if (beta > 0.0f) g = a / (1.0 + beta - beta * a);  // invert G' = (1+b) G / (1 + b G)
   const double rc = g >= 1.0 ? 0.0 : -2.0 * log(g);
@@ -125,9 +157,9 @@ __device__ __forceinline__ bool alpha_cutoff(float o, float beta, float& rho_cut
 // Returns the number of tiles that receive instances (0 when culled) and fills
 // the record, the binning info and the reference's radius.
 __device__ __forceinline__ uint32_t preprocess_one(const SurfelIn& a, float mod, float beta,
-                                                   const float* vm, const float* pm, int W, int H,
-                                                   int gx, int gy, SurfelRecord& rec, BinInfo& bi,
-                                                   int& radius_out) {
+                                                   int kernel_type, const float* vm, const float* pm,
+                                                   int W, int H, int gx, int gy, SurfelRecord& rec,
+                                                   BinInfo& bi, int& radius_out) {
   // in_frustum: view-space depth must exceed 0.2 (auxiliary.h:190-215).
   const float3 pv = f3(vm[0] * a.p.x + vm[4] * a.p.y + vm[8] * a.p.z + vm[12],
                        vm[1] * a.p.x + vm[5] * a.p.y + vm[9] * a.p.z + vm[13],
@@ -201,10 +233,11 @@ __device__ __forceinline__ uint32_t preprocess_one(const SurfelIn& a, float mod,
   float bx0 = 1.f, bx1 = 0.f, by0 = 1.f, by1 = 0.f;  // empty
   uint32_t tiles = 0;
   int tx0 = x0, tx1 = x0, ty0 = y0, ty1 = y0;
-  if (alpha_cutoff(a.opacity, beta, rho_cut)) {
+  if (alpha_cutoff(a.opacity, beta, kernel_type, a.shape, rho_cut)) {
+    const bool bounded = isfinite(rho_cut);
     const float dc = rho_cut * (Tw.x * Tw.x) + rho_cut * (Tw.y * Tw.y) - (Tw.z * Tw.z);
     float ex0, ex1, ey0, ey1;
-    bool ok = dc > 0.0f;
+    bool ok = bounded && dc > 0.0f;
     if (ok) {
       const float idc = 1.0f / dc;
       const float3 fc = f3(idc * rho_cut, idc * rho_cut, -idc);
@@ -227,7 +260,7 @@ __device__ __forceinline__ uint32_t preprocess_one(const SurfelIn& a, float mod,
       ey0 = (float)(y0 * kTile);
       ey1 = (float)(y1 * kTile - 1);
     }
-    const float r2 = sqrtf(0.5f * rho_cut) * 1.01f + 1.0f;
+    const float r2 = bounded ? sqrtf(0.5f * rho_cut) * 1.01f + 1.0f : 0.0f;
     bx0 = fmaxf(fminf(ex0, ppx - r2), -1.0f);
     bx1 = fminf(fmaxf(ex1, ppx + r2), (float)W);
     by0 = fmaxf(fminf(ey0, ppy - r2), -1.0f);
@@ -250,7 +283,7 @@ __device__ __forceinline__ uint32_t preprocess_one(const SurfelIn& a, float mod,
   rec.q[4] = make_float4(n.x, n.y, n.z, __uint_as_float(ap_bits));
   rec.q[5] = make_float4(a.su.x, a.su.y, a.su.z, a.sv.x);
   rec.q[6] = make_float4(a.sv.y, a.sv.z, a.pk.x, a.pk.y);
-  rec.q[7] = make_float4(a.pk.z, rho_cut, 0.f, 0.f);
+  rec.q[7] = make_float4(a.pk.z, rho_cut, 0.f, a.shape);
   bi.x0 = (int16_t)tx0;
   bi.x1 = (int16_t)tx1;
   bi.y0 = (int16_t)ty0;
@@ -262,8 +295,9 @@ __device__ __forceinline__ uint32_t preprocess_one(const SurfelIn& a, float mod,
 
 template <class Attrs>
 __global__ void __launch_bounds__(kPreThreads)
-preprocess_kernel(int P, Attrs attrs, float mod, float beta, const float* __restrict__ viewmatrix,
-                  const float* __restrict__ projmatrix, int W, int H, PreOut out) {
+preprocess_kernel(int P, Attrs attrs, float mod, float beta, int kernel_type,
+                  const float* __restrict__ viewmatrix, const float* __restrict__ projmatrix, int W,
+                  int H, PreOut out) {
   __shared__ float vm[16], pm[16];
   __shared__ uint32_t warp_sums[kPreThreads / 32];
   if (threadIdx.x < 16) vm[threadIdx.x] = viewmatrix[threadIdx.x];
@@ -280,7 +314,7 @@ preprocess_kernel(int P, Attrs attrs, float mod, float beta, const float* __rest
     bi.pad = 0;
     int radius = 0;
     const SurfelIn a = attrs.load(i);
-    tiles = preprocess_one(a, mod, beta, vm, pm, W, H, gx, gy, rec, bi, radius);
+    tiles = preprocess_one(a, mod, beta, kernel_type, vm, pm, W, H, gx, gy, rec, bi, radius);
     rec.q[7].z = __uint_as_float((uint32_t)i);
     if (tiles) {
       float4* dst = reinterpret_cast<float4*>(out.records + i);
@@ -322,14 +356,15 @@ __global__ void mark_visible_kernel(int P, const float* __restrict__ means3D,
 int preprocess_blocks(int P) { return div_up(max(P, 1), kPreThreads); }
 int preprocess_block_size() { return kPreThreads; }
 
-int preprocess_api_launch(int P, const ns_surfels& s, float mod, float beta, const float* vm,
+int preprocess_api_launch(int P, const ns_surfels& s, float mod, float beta, int kernel_type,
+                          const float* vm,
                           const float* pm, int W, int H, SurfelRecord* records, BinInfo* bin,
                           int32_t* radii, uint32_t* tiles, uint32_t* depth_keys,
                           uint32_t* depth_vals, uint32_t* block_sums, cudaStream_t stream) {
-  ApiAttrs a{s.means3D, s.scales, s.rotations, s.opacities, s.homotrans, s.ap_level};
+  ApiAttrs a{s.means3D, s.scales, s.rotations, s.opacities, s.homotrans, s.ap_level, s.shapes};
   PreOut o{records, bin, radii, tiles, depth_keys, depth_vals, block_sums};
-  preprocess_kernel<ApiAttrs><<<preprocess_blocks(P), kPreThreads, 0, stream>>>(P, a, mod, beta, vm,
-                                                                                pm, W, H, o);
+  preprocess_kernel<ApiAttrs><<<preprocess_blocks(P), kPreThreads, 0, stream>>>(
+      P, a, mod, beta, kernel_type, vm, pm, W, H, o);
   NS_LAUNCH_CHECK();
   return NS_OK;
 }
@@ -341,8 +376,8 @@ int preprocess_mix_launch(int P, const float* base, const float* decoded, int di
                           uint32_t* depth_vals, uint32_t* block_sums, cudaStream_t stream) {
   MixAttrs a{base, decoded, dims, mix, ap_level};
   PreOut o{records, bin, radii, tiles, depth_keys, depth_vals, block_sums};
-  preprocess_kernel<MixAttrs><<<preprocess_blocks(P), kPreThreads, 0, stream>>>(P, a, mod, beta, vm,
-                                                                                pm, W, H, o);
+  preprocess_kernel<MixAttrs><<<preprocess_blocks(P), kPreThreads, 0, stream>>>(
+      P, a, mod, beta, 0, vm, pm, W, H, o);
   NS_LAUNCH_CHECK();
   return NS_OK;
 }

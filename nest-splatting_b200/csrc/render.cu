@@ -105,7 +105,9 @@ __device__ __forceinline__ float2 lookup_finish(const float (&f)[3], const Corne
   return r;
 }
 
-template <typename TableT>
+// kAnyKernel: built with the splat kernels 1-3 (p.kernel_type); the Gaussian-only
+// instantiation keeps the hot loop free of them.
+template <typename TableT, bool kAnyKernel>
 __global__ void __launch_bounds__(kThreads, 2) blend_kernel(const RenderParams p) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   BlendSmem& S = *reinterpret_cast<BlendSmem*>(smem_raw);
@@ -300,10 +302,29 @@ __global__ void __launch_bounds__(kThreads, 2) blend_kernel(const RenderParams p
           const bool on_plane = rho3d <= rho2d;
           const float depth = on_plane ? (sx * Tw.x + sy * Tw.y) + Tw.z : Tw.z;
           if (depth < kNear) continue;
-          const float power = -0.5f * rho;
-          if (power > 0.0f) continue;
-          float G = expf(power);
-          if (p.beta > 0.0f) G = (float)((1.0 + (double)p.beta) * G / (1.0 + (double)p.beta * G));
+          float G;
+          if (!kAnyKernel || p.kernel_type == 0) {
+            const float power = -0.5f * rho;
+            if (power > 0.0f) continue;
+            G = expf(power);
+            if (p.beta > 0.0f) G = (float)((1.0 + (double)p.beta) * G / (1.0 + (double)p.beta * G));
+          } else {
+            // The other splat kernels of forward.cu:864-902, with the record's shape.
+            const float shape = S.rec[s][jj][7].w;
+            if (p.kernel_type == 1) {  // beta kernel: (1 - rho)^shape inside the unit circle
+              if (rho >= 1.0f) continue;
+              G = powf(1.0f - rho, shape);
+            } else if (p.kernel_type == 2) {  // flex: per-surfel beta
+              const float power = -0.5f * rho;
+              if (power > 0.0f) continue;
+              G = expf(power);
+              if (shape > 0.0f) G = (1.0f + shape) * G / (1.0f + shape * G);
+            } else {  // general: exp(-0.5 rho^(shape / 2))
+              const float power = -0.5f * powf(fmaxf(rho, 1e-8f), 0.5f * shape);
+              if (power > 0.0f) continue;
+              G = expf(power);
+            }
+          }
           const float alpha = fminf(0.99f, q2.w * G);
           if (alpha < 1.0f / 255.0f) continue;
           const float test_T = T * (1 - alpha);
@@ -445,12 +466,13 @@ __global__ void __launch_bounds__(kThreads, 2) blend_kernel(const RenderParams p
   }
 }
 
-template <typename TableT>
+template <typename TableT, bool kAnyKernel>
 int launch_blend(const RenderParams& p, int tiles, cudaStream_t stream) {
   const int smem = (int)sizeof(BlendSmem);
-  NS_CUDA_TRY(cudaFuncSetAttribute(blend_kernel<TableT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+  NS_CUDA_TRY(cudaFuncSetAttribute(blend_kernel<TableT, kAnyKernel>,
+                                   cudaFuncAttributeMaxDynamicSharedMemorySize,
                                    smem));
-  blend_kernel<TableT><<<tiles, kThreads, smem, stream>>>(p);
+  blend_kernel<TableT, kAnyKernel><<<tiles, kThreads, smem, stream>>>(p);
   NS_LAUNCH_CHECK();
   return NS_OK;
 }
@@ -465,7 +487,9 @@ int render_launch(const RenderParams& p, int fp16, cudaStream_t stream) {
   if (p.L > (uint32_t)(p.C / p.LD) || p.L > (uint32_t)kMaxLevels) return NS_ERR_UNSUPPORTED;
   const int tiles = div_up(p.W, kTile) * div_up(p.H, kTile);
   if (tiles == 0) return NS_OK;
-  return fp16 ? launch_blend<__half>(p, tiles, stream) : launch_blend<float>(p, tiles, stream);
+  if (p.kernel_type != 0)
+    return fp16 ? launch_blend<__half, true>(p, tiles, stream) : launch_blend<float, true>(p, tiles, stream);
+  return fp16 ? launch_blend<__half, false>(p, tiles, stream) : launch_blend<float, false>(p, tiles, stream);
 }
 
 }  // namespace ns

@@ -6,10 +6,11 @@ NilKel/nest-splatting (GaussianRasterizationSettings :277-293,
 HashGridSettings :295-302, GaussianRasterizer :304-396, rasterize_gaussians
 :21-66, _RasterizeGaussians :68-275, compute_relocation :398-414). The forward
 and backward passes run the sm_100a kernels of libnest_b200.so through its
-C-ABI; there is no CPU fallback. Built: render_mode 0 (baseline hash grid) with
-the Gaussian kernel (kernel_type 0) and level_dim 2. Other modes raise
-NotImplementedError instead of silently rendering nothing as the reference does
-for shapes it was not compiled for.
+C-ABI; there is no CPU fallback. Built: render_mode 0 (baseline hash grid),
+level_dim 2, the Gaussian splat kernel (kernel_type 0) forward and backward and
+the beta / flex / general kernels (kernel_type 1-3, per-surfel `shapes`)
+forward. Other modes raise NotImplementedError instead of silently rendering
+nothing as the reference does for shapes it was not compiled for.
 
 Backward (__init__.py:174-275 of the reference): the 21 gradients come back in
 argument order; means2D's slot carries the densification statistic and
@@ -69,8 +70,15 @@ class _RasterizeGaussians(torch.autograd.Function):
                 gridrange_diffuse, raster_settings, hashgrid_settings, render_mode, shapes, kernel_type):
         if int(render_mode) != 0:
             raise NotImplementedError(f"render_mode {render_mode}: only 0 (baseline hash grid) is built")
+        if int(kernel_type) not in (0, 1, 2, 3):
+            raise NotImplementedError(f"kernel_type {kernel_type}: 0-3 are built")
+        shp = _nonempty(shapes)
         if int(kernel_type) != 0:
-            raise NotImplementedError(f"kernel_type {kernel_type}: only 0 (Gaussian) is built")
+            if shp is None or shp.numel() != means3D.shape[0]:
+                raise RuntimeError(f"kernel_type {kernel_type} needs shapes with one value per surfel")
+            shp = shp.detach().contiguous().float().reshape(-1)
+        else:
+            shp = None
         if _nonempty(cov3Ds_precomp) is not None:
             raise NotImplementedError("precomputed transforms (cov3D_precomp) are not built")
         if means3D.ndim != 2 or means3D.shape[1] != 3:
@@ -94,14 +102,16 @@ class _RasterizeGaussians(torch.autograd.Function):
             prefiltered=bool(raster_settings.prefiltered), levels=L, S=float(hashgrid_settings.S),
             base_resolution=int(hashgrid_settings.H), align_corners=bool(hashgrid_settings.align_corners),
             interpolation=int(hashgrid_settings.interpolation), channels=int(OS),
-            level_dim=int(feats.shape[1]), table_fp16=feats.dtype == torch.float16)
+            level_dim=int(feats.shape[1]), table_fp16=feats.dtype == torch.float16,
+            kernel_type=int(kernel_type))
         ap = _nonempty(ap_level)
         args = (means3D.detach().contiguous().float(), scales.detach().contiguous().float(),
                 rotations.detach().contiguous().float(), opacities.detach().contiguous().float().reshape(-1),
                 None if _nonempty(homotrans) is None else homotrans.detach().contiguous().float().reshape(-1, 16),
                 None if ap is None else ap.detach().contiguous().float().reshape(-1), feats.detach(),
                 offsets.contiguous().to(torch.int32), gridrange.contiguous().float())
-        num_rendered, color, others, radii, cover, trans, scratch = _raster.rasterize_forward(cfg, *args)
+        num_rendered, color, others, radii, cover, trans, scratch = _raster.rasterize_forward(cfg, *args,
+                                                                                              shapes=shp)
         ctx.cfg = cfg
         ctx.args = args
         ctx.radii = radii
@@ -114,6 +124,8 @@ class _RasterizeGaussians(torch.autograd.Function):
 
     @staticmethod
     def backward(ctx, grad_out_color, grad_radii, grad_depth, grad_0, grad_1):
+        if ctx.cfg.kernel_type != 0:
+            raise NotImplementedError(f"backward of kernel_type {ctx.cfg.kernel_type}: only 0 (Gaussian) is built")
         dev = ctx.radii.device
         H, W = ctx.cfg.image_height, ctx.cfg.image_width
         if grad_out_color is None:

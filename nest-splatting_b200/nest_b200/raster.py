@@ -45,6 +45,7 @@ class RasterConfig:
     channels: int = 32
     level_dim: int = 2
     table_fp16: bool = True
+    kernel_type: int = 0  # 0 Gaussian, 1 beta, 2 flex, 3 general (forward only)
 
     def to_c(self) -> _lib.RasterSettings:
         s = _lib.RasterSettings()
@@ -56,6 +57,7 @@ class RasterConfig:
         s.viewmatrix = self.viewmatrix.data_ptr()
         s.projmatrix = self.projmatrix.data_ptr()
         s.beta = float(self.beta)
+        s.kernel_type = int(self.kernel_type)
         s.if_contract = int(bool(self.if_contract))
         s.record_transmittance = int(bool(self.record_transmittance))
         s.max_intersections = int(self.max_intersections)
@@ -107,7 +109,7 @@ class Scratch:
 
 def rasterize_forward(cfg: RasterConfig, means3D, scales, rotations, opacities, homotrans, ap_level,
                       features, offsets, gridrange, scratch: Scratch | None = None,
-                      capacity_hint: int | None = None):
+                      capacity_hint: int | None = None, shapes=None):
     """Forward rasterization (render_mode 0) through ns_rasterize_forward.
 
     Returns (num_rendered, out_color [C,H,W], out_others [14,H,W], radii [P] int32,
@@ -135,6 +137,7 @@ def rasterize_forward(cfg: RasterConfig, means3D, scales, rotations, opacities, 
     surf.means3D, surf.scales, surf.rotations = ptr(means3D), ptr(scales), ptr(rotations)
     surf.opacities, surf.homotrans, surf.ap_level = ptr(opacities), ptr(homotrans), ptr(ap_level)
     surf.features, surf.offsets, surf.gridrange = ptr(features), ptr(offsets), ptr(gridrange)
+    surf.shapes = ptr(shapes)
     outs = _lib.RasterOutputs()
     outs.out_color, outs.out_others, outs.radii = ptr(out_color), ptr(out_others), ptr(radii)
     outs.cover_pixels = ptr(cover) if rec_P else None

@@ -141,7 +141,8 @@ int64_t oracle_bin(int P, const float* means2D, const float* depths, const int* 
   return n;
 }
 
-// forward.cu:639-2049, render_mode 0 with level > 0, kernel_type 0 (Gaussian):
+// forward.cu:639-2049, render_mode 0 with level > 0, kernel_type 0 (Gaussian) or
+// the beta / flex / general kernels of :864-902 (kernel_type 1-3, shapes[P]):
 // ray/surfel intersection (:839-858), alpha and termination (:903-939),
 // auxiliary maps (:941-959), hit point and hash query (:1099-1145, 1914-1916),
 // level visualisation colour (:1945-1957), transmittance record (:1961-1964),
@@ -154,7 +155,8 @@ void oracle_render(int W, int H, const uint32_t* ranges, const uint32_t* point_l
                    float S, uint32_t Hres, int align_corners, uint32_t interp, int contract,
                    float beta, uint32_t max_intersections, int record_transmittance,
                    float* out_color, float* out_others, float* final_T, uint32_t* n_contrib,
-                   float* cover_pixels, float* trans_avg, int row_stride) {
+                   float* cover_pixels, float* trans_avg, int row_stride, int kernel_type,
+                   const float* shapes) {
   const int gx = (W + kBlock - 1) / kBlock, gy = (H + kBlock - 1) / kBlock;
   const size_t HW = (size_t)H * W;
   const float vmin = gridrange[0], vmax = gridrange[1];
@@ -192,10 +194,27 @@ void oracle_render(int W, int H, const uint32_t* ranges, const uint32_t* point_l
           float depth = (rho3d <= rho2d) ? (sx * Tw.x + sy * Tw.y) + Tw.z : Tw.z;
           if (depth < kNear) continue;
           const float* no = normal_opacity + 4 * (size_t)id;
-          float power = -0.5f * rho;
-          if (power > 0.0f) continue;
-          float G = std::exp(power);
-          if (beta > 0.0) G = (float)((1.0 + beta) * G / (1.0 + beta * G));
+          float G;
+          if (kernel_type == 1) {
+            if (rho >= 1.0f) continue;
+            G = powf(1.0f - rho, shapes[id]);
+          } else if (kernel_type == 2) {
+            float power = -0.5f * rho;
+            if (power > 0.0f) continue;
+            G = std::exp(power);
+            const float b = shapes[id];
+            if (b > 0.0f) G = (1.0f + b) * G / (1.0f + b * G);
+          } else if (kernel_type == 3) {
+            const float pt = powf(std::max(rho, 1e-8f), 0.5f * shapes[id]);
+            float power = -0.5f * pt;
+            if (power > 0.0f) continue;
+            G = std::exp(power);
+          } else {
+            float power = -0.5f * rho;
+            if (power > 0.0f) continue;
+            G = std::exp(power);
+            if (beta > 0.0) G = (float)((1.0 + beta) * G / (1.0 + beta * G));
+          }
           float alpha = std::min(0.99f, no[3] * G);
           if (alpha < 1.0f / 255.0f) continue;
           float test_T = T * (1 - alpha);

@@ -52,7 +52,7 @@ def load() -> C.CDLL:
     lib.oracle_bin.restype = i64
     lib.oracle_bin.argtypes = [i32, vp, vp, vp, i32, i32, vp, vp, i64, vp]
     lib.oracle_render.argtypes = [i32, i32, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, i32, i32, u32, f32, u32,
-                                  i32, u32, i32, f32, u32, i32, vp, vp, vp, vp, vp, vp, i32]
+                                  i32, u32, i32, f32, u32, i32, vp, vp, vp, vp, vp, vp, i32, i32, vp]
     lib.oracle_query.argtypes = [i32, vp, vp, vp, vp, f32, f32, i32, i32, u32, f32, u32, i32, u32, i32, vp]
     lib.oracle_grid_index.restype = u32
     lib.oracle_grid_index.argtypes = [i32, u32, u32, u32, u32, u32]
@@ -109,8 +109,9 @@ def bin_surfels(pre, W, H):
 
 def render(pre, vals, ranges, homotrans, ap_level, table_f32, offsets, gridrange, W, H, C_out, LD, L, S, Hres,
            align_corners=False, interp=0, contract=False, beta=0.0, max_intersections=0,
-           record_transmittance=False, row_stride=1):
+           record_transmittance=False, row_stride=1, kernel_type=0, shapes=None):
     """renderCUDAsurfelForward<C> mode 0 restated. Returns dict of output images.
+    kernel_type 1-3 (beta / flex / general splat kernels) read shapes [P].
 
     row_stride > 1 renders only tile rows ty with ty % row_stride == 0 (a bounded
     sample for CPU timing); other pixels stay zero."""
@@ -131,7 +132,8 @@ def render(pre, vals, ranges, homotrans, ap_level, table_f32, offsets, gridrange
                       int(LD), int(L), float(S), int(Hres), int(bool(align_corners)), int(interp),
                       int(bool(contract)), float(beta), int(max_intersections), int(bool(record_transmittance)),
                       _p(out["out_color"]), _p(out["out_others"]), _p(out["final_T"]), _p(out["n_contrib"]),
-                      _p(out["cover_pixels"]), _p(out["trans_avg"]), int(row_stride))
+                      _p(out["cover_pixels"]), _p(out["trans_avg"]), int(row_stride), int(kernel_type),
+                      _p(_f32(shapes).reshape(-1)) if shapes is not None else None)
     assert HW == W * H
     return out
 
