@@ -172,6 +172,8 @@ typedef struct ns_raster_grads_out {
   int64_t table_rows;   /* rows of dL_dtable (offsets[levels]) */
   float* dL_gradsum;    /* [P] sum over samples of alpha*T*|dL/dcolor|_1 (the
                            reference's dL_gradsum, returned in ap_level's slot) */
+  float* dL_dshapes;    /* [P] or NULL: gradient of the splat kernel's shape
+                           (kernel_type 1-3, backward.cu:1864-1909) */
 } ns_raster_grads_out;
 
 /* Scratch of the backward pass: per-surfel gradient accumulators. */

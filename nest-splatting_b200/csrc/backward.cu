@@ -47,7 +47,8 @@ constexpr int kGradWords = 20;  // per-surfel accumulator words (18 used), 80 by
 constexpr float kAggScale = 128.f;  // table-gradient aggregation below this level resolution
 
 // Accumulator words of one surfel (80 bytes, five float4 groups; the last group
-// is non-zero only for samples of the rho2d branch).
+// is non-zero only for samples of the rho2d branch and for the shape gradient of
+// the splat kernels 1-3).
 enum : int {
   kGM = 0,          // dL/dM columns 0..2 (rows 0..2): L0, L1, mean -> words 0..8
   kGTuz = 9,        // dL/dT[0].z, dL/dT[1].z: the densification statistic
@@ -56,6 +57,7 @@ enum : int {
   kGNormal = 12,    // dL/dnormal (view space) x, y, z
   kGGradSum = 15,
   kGMean2D = 16,    // dL/dmean2D x, y (rho2d branch)
+  kGShape = 18,     // dL/dshape (splat kernels 1-3)
 };
 
 // a * b - c * d with one rounding error at most (Kahan's difference of products
@@ -92,7 +94,9 @@ struct BwSmem {
   LevelConst lv[kMaxLevels];
 };
 
-template <typename TableT>
+// kAnyKernel: built with the splat kernels 1-3 (p.kernel_type); the Gaussian-only
+// instantiation keeps them out of the hot loop.
+template <typename TableT, bool kAnyKernel>
 __global__ void __launch_bounds__(kThreads, 2) blend_backward_kernel(const BackwardParams p) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   BwSmem& S = *reinterpret_cast<BwSmem*>(smem_raw);
@@ -239,12 +243,31 @@ __global__ void __launch_bounds__(kThreads, 2) blend_backward_kernel(const Backw
         const bool on_plane = rho3d <= rho2d;
         const float depth = on_plane ? (sx * Tw.x + sy * Tw.y) + Tw.z : Tw.z;
         if (depth < kNear) continue;
-        const float power = -0.5f * rho;
-        if (power > 0.0f) continue;
-        float G = expf(power);
-        if (p.beta > 0.0f) {
-          const float demon = (float)(1.0 + (double)p.beta * G);
-          G = (float)((1.0 + (double)p.beta) * G / demon);
+        float G;
+        if (!kAnyKernel || p.kernel_type == 0) {
+          const float power = -0.5f * rho;
+          if (power > 0.0f) continue;
+          G = expf(power);
+          if (p.beta > 0.0f) {
+            const float demon = (float)(1.0 + (double)p.beta * G);
+            G = (float)((1.0 + (double)p.beta) * G / demon);
+          }
+        } else {
+          // Splat kernels 1-3 (backward.cu:765-803), as the forward evaluates them.
+          const float shape = S.rec[jj][7].w;
+          if (p.kernel_type == 1) {
+            if (rho >= 1.0f) continue;
+            G = powf(1.0f - rho, shape);
+          } else if (p.kernel_type == 2) {
+            const float power = -0.5f * rho;
+            if (power > 0.0f) continue;
+            G = expf(power);
+            if (shape > 0.0f) G = (1.0f + shape) * G / (1.0f + shape * G);
+          } else {
+            const float power = -0.5f * powf(fmaxf(rho, 1e-8f), 0.5f * shape);
+            if (power > 0.0f) continue;
+            G = expf(power);
+          }
         }
         const float alpha = fminf(0.99f, q2.w * G);
         if (alpha < 1.0f / 255.0f) continue;
@@ -457,11 +480,31 @@ __global__ void __launch_bounds__(kThreads, 2) blend_backward_kernel(const Backw
         const float rho = fminf(rho3d, rho2d);
         const bool on_plane = rho3d <= rho2d;
         const float c_d = on_plane ? (sx * Tw.x + sy * Tw.y) + Tw.z : Tw.z;
-        float G = expf(-0.5f * rho);
-        float demon = 1.0f;
-        if (p.beta > 0.0f) {
-          demon = (float)(1.0 + (double)p.beta * G);
-          G = (float)((1.0 + (double)p.beta) * G / demon);
+        float G, demon = 1.0f;
+        float shape = 0.f, G_raw = 0.f, base = 0.f, pow_term = 0.f, rho_safe = 0.f;
+        if (!kAnyKernel || p.kernel_type == 0) {
+          G = expf(-0.5f * rho);
+          if (p.beta > 0.0f) {
+            demon = (float)(1.0 + (double)p.beta * G);
+            G = (float)((1.0 + (double)p.beta) * G / demon);
+          }
+        } else {
+          shape = q6.w;
+          if (p.kernel_type == 1) {
+            base = 1.0f - rho;
+            G = powf(base, shape);
+          } else if (p.kernel_type == 2) {
+            G_raw = expf(-0.5f * rho);
+            G = G_raw;
+            if (shape > 0.0f) {
+              demon = 1.0f + shape * G_raw;
+              G = (1.0f + shape) * G_raw / demon;
+            }
+          } else {
+            rho_safe = fmaxf(rho, 1e-8f);
+            pow_term = powf(rho_safe, 0.5f * shape);
+            G = expf(-0.5f * pow_term);
+          }
         }
         const float opa = q2.w;
         const float alpha = fminf(0.99f, opa * G);
@@ -499,7 +542,23 @@ __global__ void __launch_bounds__(kThreads, 2) blend_backward_kernel(const Backw
         last_alpha = alpha;
 
         float dL_dG = opa * dL_dalpha;
-        if (p.beta > 0.0f) dL_dG *= (float)((1.0 + (double)p.beta) / ((double)demon * demon));
+        // dL/dshape and the kernel's dG/drho factor (backward.cu:1862-1914, :1960-2038).
+        float dG_factor = -G, dshape = 0.f;
+        if (!kAnyKernel || p.kernel_type == 0) {
+          if (p.beta > 0.0f) dL_dG *= (float)((1.0 + (double)p.beta) / ((double)demon * demon));
+        } else if (p.kernel_type == 1) {
+          if (base > 1e-7f) dshape = dL_dalpha * opa * G * logf(base);
+          dG_factor = base > 1e-7f ? -shape * G / base : 0.0f;
+        } else if (p.kernel_type == 2) {
+          if (shape > 0.0f) {
+            dL_dG *= (1.0f + shape) / (demon * demon);
+            dshape = dL_dalpha * opa * (G_raw * (1.0f - G_raw) / (demon * demon));
+          }
+          dG_factor = -G_raw;
+        } else {
+          dshape = dL_dalpha * opa * (-0.25f * G * pow_term * logf(rho_safe));
+          dG_factor = -0.5f * shape * G * pow_term / rho_safe;
+        }
         dL_dz += aT * dL_ddepth;
 
         // dL/dxyz from the hit-point gradient (query_feature's grad_scale).
@@ -532,7 +591,6 @@ __global__ void __launch_bounds__(kThreads, 2) blend_backward_kernel(const Backw
         if (on_plane) {
           const float du = gx_ * q4.x + gy_ * q4.y + gz_ * q4.z;
           const float dv = gx_ * q4.w + gy_ * q5.x + gz_ * q5.y;
-          const float dG_factor = -G;
           float dsx = dL_dG * dG_factor * sx + dL_dz * Tw.x;
           float dsy = dL_dG * dG_factor * sy + dL_dz * Tw.y;
           if (!p.ray_hit) {
@@ -590,7 +648,7 @@ __global__ void __launch_bounds__(kThreads, 2) blend_backward_kernel(const Backw
             tvz -= dop(hx, kk.y, hy, kk.x);
           }
         } else {
-          const float dG_factor_2d = -G * kFilterInvSquare;
+          const float dG_factor_2d = dG_factor * kFilterInvSquare;
           dmx = dL_dG * (dG_factor_2d * dx);
           dmy = dL_dG * (dG_factor_2d * dy);
           dTw.z = dL_dz;
@@ -608,7 +666,7 @@ __global__ void __launch_bounds__(kThreads, 2) blend_backward_kernel(const Backw
         atomicAdd(ga + 2, make_float4(P02 * dTu.z + P12 * dTv.z + P22 * dTw.z + h2z, tuz, tvz,
                                       G * dL_dalpha));
         atomicAdd(ga + 3, make_float4(aT * dn0, aT * dn1, aT * dn2, aT * gabs));
-        if (!on_plane) atomicAdd(ga + 4, make_float4(dmx, dmy, 0.f, 0.f));
+        if (!on_plane || dshape != 0.f) atomicAdd(ga + 4, make_float4(dmx, dmy, dshape, 0.f));
       }
       __syncwarp();
     }
@@ -653,6 +711,7 @@ preprocess_backward_kernel(int P, const float* __restrict__ means3D, const float
     dm2[0] = dm2[1] = dm2[2] = 0.f;
     o.dL_dopacity[i] = 0.f;
     o.dL_gradsum[i] = 0.f;
+    if (o.dL_dshapes) o.dL_dshapes[i] = 0.f;
     return;
   }
   const float4* a4 = reinterpret_cast<const float4*>(accum + (size_t)i * kGradWords);
@@ -761,14 +820,15 @@ preprocess_backward_kernel(int P, const float* __restrict__ means3D, const float
   dm2[2] = 0.f;
   o.dL_dopacity[i] = a[kGOpacity];
   o.dL_gradsum[i] = a[kGGradSum];
+  if (o.dL_dshapes) o.dL_dshapes[i] = a[kGShape];
 }
 
-template <typename TableT>
+template <typename TableT, bool kAnyKernel>
 int launch_backward(const BackwardParams& p, int tiles, cudaStream_t stream) {
   const int smem = (int)sizeof(BwSmem);
-  NS_CUDA_TRY(cudaFuncSetAttribute(blend_backward_kernel<TableT>,
+  NS_CUDA_TRY(cudaFuncSetAttribute(blend_backward_kernel<TableT, kAnyKernel>,
                                    cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-  blend_backward_kernel<TableT><<<tiles, kThreads, smem, stream>>>(p);
+  blend_backward_kernel<TableT, kAnyKernel><<<tiles, kThreads, smem, stream>>>(p);
   NS_LAUNCH_CHECK();
   return NS_OK;
 }
@@ -782,7 +842,11 @@ int blend_backward_launch(const BackwardParams& p, int fp16, cudaStream_t stream
   if (p.L > (uint32_t)(p.C / p.LD) || p.L > (uint32_t)kMaxLevels) return NS_ERR_UNSUPPORTED;
   const int tiles = div_up(p.W, kTile) * div_up(p.H, kTile);
   if (tiles == 0) return NS_OK;
-  return fp16 ? launch_backward<__half>(p, tiles, stream) : launch_backward<float>(p, tiles, stream);
+  if (p.kernel_type != 0)
+    return fp16 ? launch_backward<__half, true>(p, tiles, stream)
+                : launch_backward<float, true>(p, tiles, stream);
+  return fp16 ? launch_backward<__half, false>(p, tiles, stream)
+              : launch_backward<float, false>(p, tiles, stream);
 }
 
 int preprocess_backward_launch(int P, const float* means3D, const float* scales,

@@ -343,11 +343,12 @@ int ns_rasterize_backward(const ns_raster_settings* settings, const ns_surfels* 
                           void* stream_) {
   cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_);
   int rc = validate_settings(settings);
-  if (settings && settings->kernel_type != 0) return NS_ERR_UNSUPPORTED;  // forward only
   if (rc) return rc;
   if (!surfels || !gi || !go) return NS_ERR_INVALID;
   const int P = surfels->P;
   if (P < 0 || num_rendered < 0) return NS_ERR_INVALID;
+  if (settings->kernel_type != 0 && P > 0 && (!surfels->shapes || !go->dL_dshapes))
+    return NS_ERR_INVALID;
   if (settings->level_dim != 2) return NS_ERR_UNSUPPORTED;
   if (!go->dL_dmeans3D || !go->dL_dmean2D || !go->dL_dopacity || !go->dL_dscales ||
       !go->dL_drots || !go->dL_dtable || !go->dL_gradsum || go->table_rows < 0)
@@ -391,6 +392,7 @@ int ns_rasterize_backward(const ns_raster_settings* settings, const ns_surfels* 
   bp.interp = settings->interpolation;
   bp.contract = settings->if_contract;
   bp.beta = settings->beta;
+  bp.kernel_type = settings->kernel_type;
   bp.Wq = Wq;
   bp.Hq = Hq;
   bp.projmatrix = settings->projmatrix;

@@ -42,6 +42,7 @@ struct BackwardParams {
   uint32_t interp;
   int contract;
   float beta;
+  int kernel_type;            // splat kernel 0-3; 1-3 read the shape in record word 31
   int Wq, Hq;                 // image size as the reference's preprocess backward recomputes it
   const float* projmatrix;
   const float* viewmatrix;

@@ -235,9 +235,13 @@ __device__ __forceinline__ uint32_t preprocess_one(const SurfelIn& a, float mod,
   int tx0 = x0, tx1 = x0, ty0 = y0, ty1 = y0;
   if (alpha_cutoff(a.opacity, beta, kernel_type, a.shape, rho_cut)) {
     const bool bounded = isfinite(rho_cut);
+    // The disc u^2 + v^2 <= rho_cut of the splat plane projects to an ellipse
+    // when the whole disc lies in front of the camera: w = Tw.x u + Tw.y v + Tw.z
+    // > 0 on it, i.e. dc < 0 (with a relative margin against near-degenerate
+    // conics). Otherwise its image is unbounded and the reference rectangle stays.
     const float dc = rho_cut * (Tw.x * Tw.x) + rho_cut * (Tw.y * Tw.y) - (Tw.z * Tw.z);
     float ex0, ex1, ey0, ey1;
-    bool ok = bounded && dc > 0.0f;
+    bool ok = bounded && dc < -1e-4f * (Tw.z * Tw.z);
     if (ok) {
       const float idc = 1.0f / dc;
       const float3 fc = f3(idc * rho_cut, idc * rho_cut, -idc);

@@ -7,10 +7,11 @@ HashGridSettings :295-302, GaussianRasterizer :304-396, rasterize_gaussians
 :21-66, _RasterizeGaussians :68-275, compute_relocation :398-414). The forward
 and backward passes run the sm_100a kernels of libnest_b200.so through its
 C-ABI; there is no CPU fallback. Built: render_mode 0 (baseline hash grid),
-level_dim 2, the Gaussian splat kernel (kernel_type 0) forward and backward and
-the beta / flex / general kernels (kernel_type 1-3, per-surfel `shapes`)
-forward. Other modes raise NotImplementedError instead of silently rendering
-nothing as the reference does for shapes it was not compiled for.
+level_dim 2, the Gaussian splat kernel (kernel_type 0) and the beta / flex /
+general kernels (kernel_type 1-3, per-surfel `shapes`, whose gradient comes back
+in shapes' slot), forward and backward. Other modes raise NotImplementedError
+instead of silently rendering nothing as the reference does for shapes it was
+not compiled for.
 
 Backward (__init__.py:174-275 of the reference): the 21 gradients come back in
 argument order; means2D's slot carries the densification statistic and
@@ -118,14 +119,14 @@ class _RasterizeGaussians(torch.autograd.Function):
         ctx.num_rendered = num_rendered
         ctx.scratch = scratch
         ctx.shapes = dict(opacities=opacities.shape, ap_level=ap_level.shape, features=features.dtype,
-                          sh=sh.shape, colors_precomp=colors_precomp.shape)
+                          sh=sh.shape, colors_precomp=colors_precomp.shape,
+                          shapes=None if shp is None else shapes.shape)
+        ctx.shape_values = shp
         ctx.mark_non_differentiable(radii)
         return color, radii, others, trans, cover
 
     @staticmethod
     def backward(ctx, grad_out_color, grad_radii, grad_depth, grad_0, grad_1):
-        if ctx.cfg.kernel_type != 0:
-            raise NotImplementedError(f"backward of kernel_type {ctx.cfg.kernel_type}: only 0 (Gaussian) is built")
         dev = ctx.radii.device
         H, W = ctx.cfg.image_height, ctx.cfg.image_width
         if grad_out_color is None:
@@ -133,7 +134,7 @@ class _RasterizeGaussians(torch.autograd.Function):
         if grad_depth is None:
             grad_depth = torch.zeros((_raster.OTHER_CHANNELS, H, W), dtype=torch.float32, device=dev)
         g = _raster.rasterize_backward(ctx.cfg, *ctx.args, ctx.radii, ctx.num_rendered, ctx.scratch,
-                                       grad_out_color, grad_depth)
+                                       grad_out_color, grad_depth, shapes=ctx.shape_values)
         ctx.scratch = None
         need = ctx.needs_input_grad
         sh = ctx.shapes
@@ -154,7 +155,9 @@ class _RasterizeGaussians(torch.autograd.Function):
                 None,  # homotrans: folded into means / scales / rotations
                 gradsum,
                 g["table"].to(sh["features"]) if need[10] else None,
-                None, None, None, None, None, None, None, None, None, None)
+                None, None, None, None, None, None, None, None,
+                g["shapes"].reshape(sh["shapes"]) if (need[19] and sh["shapes"] is not None) else None,
+                None)
 
 
 class GaussianRasterizationSettings(NamedTuple):

@@ -163,15 +163,16 @@ def rasterize_forward(cfg: RasterConfig, means3D, scales, rotations, opacities, 
 
 def rasterize_backward(cfg: RasterConfig, means3D, scales, rotations, opacities, homotrans, ap_level, features,
                        offsets, gridrange, radii, num_rendered: int, scratch: Scratch, dL_dcolor, dL_dothers,
-                       return_accumulators: bool = False):
+                       return_accumulators: bool = False, shapes=None):
     """Backward rasterization (render_mode 0) through ns_rasterize_backward.
 
     `scratch` and every input must be the ones of the forward call. Returns a dict
     of fp32 gradients: means3D [P,3], means2D [P,3] (densification statistic),
     opacity [P,1], scales [P,2], rotations [P,4], table [rows, level_dim],
-    gradsum [P,1]. With return_accumulators, also "accum": the render pass's
+    gradsum [P,1]; for kernel_type 1-3 (`shapes` [P] as in the forward) also
+    shapes [P]. With return_accumulators, also "accum": the render pass's
     per-surfel accumulators [P,20] (dL/dM 9, dL/dT[0].z, dL/dT[1].z, opacity,
-    dL/dnormal 3, gradsum, dL/dmean2D 2, 2 unused), for tests.
+    dL/dnormal 3, gradsum, dL/dmean2D 2, dL/dshape, 1 unused), for tests.
     """
     lib = _lib.load()
     dev = means3D.device
@@ -188,6 +189,12 @@ def rasterize_backward(cfg: RasterConfig, means3D, scales, rotations, opacities,
              rotations=torch.empty((P, 4), dtype=torch.float32, device=dev),
              table=torch.empty((rows, int(cfg.level_dim)), dtype=torch.float32, device=dev),
              gradsum=torch.empty((P, 1), dtype=torch.float32, device=dev))
+    if cfg.kernel_type != 0:
+        if shapes is None or shapes.numel() != P:
+            raise ValueError(f"kernel_type {cfg.kernel_type} needs shapes with one value per surfel")
+        shapes = shapes.contiguous().float().reshape(-1)
+        _require_cuda(shapes)
+        g["shapes"] = torch.empty((P,), dtype=torch.float32, device=dev)
     if P == 0:
         g["table"].zero_()
         return g
@@ -197,9 +204,12 @@ def rasterize_backward(cfg: RasterConfig, means3D, scales, rotations, opacities,
     surf.means3D, surf.scales, surf.rotations = ptr(means3D), ptr(scales), ptr(rotations)
     surf.opacities, surf.homotrans, surf.ap_level = ptr(opacities), ptr(homotrans), ptr(ap_level)
     surf.features, surf.offsets, surf.gridrange = ptr(features), ptr(offsets), ptr(gridrange)
+    if cfg.kernel_type != 0:
+        surf.shapes = ptr(shapes)
     gi = _lib.GradsIn(ptr(dL_dcolor), ptr(dL_dothers), ptr(radii))
     go = _lib.GradsOut(ptr(g["means3D"]), ptr(g["means2D"]), ptr(g["opacity"]), ptr(g["scales"]),
-                       ptr(g["rotations"]), ptr(g["table"]), rows, ptr(g["gradsum"]))
+                       ptr(g["rotations"]), ptr(g["table"]), rows, ptr(g["gradsum"]),
+                       ptr(g["shapes"]) if "shapes" in g else None)
     acc = torch.empty(lib.ns_backward_scratch_bytes(P), dtype=torch.uint8, device=dev)
     check("ns_rasterize_backward",
           lib.ns_rasterize_backward(C.byref(settings), C.byref(surf), C.byref(gi), C.byref(go),

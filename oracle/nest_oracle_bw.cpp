@@ -176,7 +176,8 @@ void render_backward(int W, int H, const uint32_t* ranges, const uint32_t* point
                      uint32_t Hres, int align_corners, uint32_t interp, int contract, float beta,
                      const float* final_T, const uint32_t* n_contrib, const float* dL_dout_color,
                      const float* dL_dout_others, R* dL_dtable, R* dL_dtransMat, R* dL_dhomoMat,
-                     R* dL_dmean2D, R* dL_dnormal, R* dL_dopacity, R* dL_gradsum) {
+                     R* dL_dmean2D, R* dL_dnormal, R* dL_dopacity, R* dL_gradsum, int kernel_type,
+                     const float* shapes, R* dL_dshapes) {
   using V = V3<R>;
   const int gx = (W + kBlock - 1) / kBlock, gy = (H + kBlock - 1) / kBlock;
   const size_t HW = (size_t)H * W;
@@ -233,13 +234,37 @@ void render_backward(int W, int H, const uint32_t* ranges, const uint32_t* point
           const float* no = normal_opacity + 4 * (size_t)id;
           const R normal[3] = {no[0], no[1], no[2]};
           const R opa = no[3];
-          const R power = R(-0.5) * rho;
-          if (power > 0) continue;
-          R G = std::exp(power);
+          // Splat kernels (backward.cu:765-818): Gaussian (+ beta), beta, flex, general.
+          const R shape = kernel_type != 0 ? (R)shapes[id] : R(0);
+          R G, G_raw = 0, base = 0, pow_term = 0, rho_safe = 0;
           R demon = 1;
-          if (beta > 0.0) {
-            demon = (R)(1.0 + beta * G);
-            G = (R)((1.0 + beta) * G / demon);
+          if (kernel_type == 1) {
+            if (rho >= R(1)) continue;
+            base = R(1) - rho;
+            G = std::pow(base, shape);
+          } else if (kernel_type == 2) {
+            const R power = R(-0.5) * rho;
+            if (power > 0) continue;
+            G_raw = std::exp(power);
+            G = G_raw;
+            if (shape > 0) {
+              demon = R(1) + shape * G_raw;
+              G = (R(1) + shape) * G_raw / demon;
+            }
+          } else if (kernel_type == 3) {
+            rho_safe = std::max(rho, R(1e-8f));
+            pow_term = std::pow(rho_safe, R(0.5) * shape);
+            const R power = R(-0.5) * pow_term;
+            if (power > 0) continue;
+            G = std::exp(power);
+          } else {
+            const R power = R(-0.5) * rho;
+            if (power > 0) continue;
+            G = std::exp(power);
+            if (beta > 0.0) {
+              demon = (R)(1.0 + beta * G);
+              G = (R)((1.0 + beta) * G / demon);
+            }
           }
           const R alpha = std::min(R(0.99f), opa * G);
           if (alpha < R(1.0f / 255.0f)) continue;
@@ -301,7 +326,21 @@ void render_backward(int W, int H, const uint32_t* ranges, const uint32_t* point
           last_alpha = alpha;
 
           R dL_dG = opa * dL_dalpha;
-          if (beta > 0.0) {
+          // dL/dshape and the kernel's dG/drho (backward.cu:1864-2040).
+          R dG_factor = -G;
+          if (kernel_type == 1) {
+            if (base > R(1e-7f)) atomic_add<R>(&dL_dshapes[id], dL_dalpha * opa * G * std::log(base));
+            dG_factor = base > R(1e-7f) ? -shape * G / base : R(0);
+          } else if (kernel_type == 2) {
+            if (shape > 0) {
+              dL_dG *= (R(1) + shape) / (demon * demon);
+              atomic_add<R>(&dL_dshapes[id], dL_dalpha * opa * (G_raw * (R(1) - G_raw) / (demon * demon)));
+            }
+            dG_factor = -G_raw;
+          } else if (kernel_type == 3) {
+            atomic_add<R>(&dL_dshapes[id], dL_dalpha * opa * (R(-0.25) * G * pow_term * std::log(rho_safe)));
+            dG_factor = R(-0.5) * shape * G * pow_term / rho_safe;
+          } else if (beta > 0.0) {
             const R dG_dg = (R)((1.0 + beta) / (demon * demon));
             dL_dG *= dG_dg;
           }
@@ -326,8 +365,7 @@ void render_backward(int W, int H, const uint32_t* ranges, const uint32_t* point
 
           R* tm = dL_dtransMat + (size_t)id * 9;
           if (rho3d <= rho2d) {
-            // :1956-2017, Gaussian kernel: dG_factor = -G.
-            const R dG_factor = -G;
+            // :1956-2017 (dG_factor per kernel above; -G for the Gaussian).
             R dsx = dL_dG * dG_factor * sx + dL_dz * Tw.x;
             R dsy = dL_dG * dG_factor * sy + dL_dz * Tw.y;
             dsx += dL_du;
@@ -348,7 +386,7 @@ void render_backward(int W, int H, const uint32_t* ranges, const uint32_t* point
             atomic_add<R>(&tm[8], pxf * dL_dk.z + pyf * dL_dl.z + dL_dz * R(1));
           } else {
             // :2018-2045
-            const R dG_factor_2d = -G * R(kFilterInvSquare);
+            const R dG_factor_2d = dG_factor * R(kFilterInvSquare);
             const R dG_ddelx = dG_factor_2d * dx;
             const R dG_ddely = dG_factor_2d * dy;
             atomic_add<R>(&dL_dmean2D[(size_t)id * 3 + 0], dL_dG * dG_ddelx);
@@ -515,12 +553,13 @@ void oracle_render_backward(int W, int H, const uint32_t* ranges, const uint32_t
                             const float* dL_dout_color, const float* dL_dout_others,
                             float* dL_dtable, float* dL_dtransMat, float* dL_dhomoMat,
                             float* dL_dmean2D, float* dL_dnormal, float* dL_dopacity,
-                            float* dL_gradsum) {
+                            float* dL_gradsum, int kernel_type, const float* shapes,
+                            float* dL_dshapes) {
   render_backward<float>(W, H, ranges, point_list, means2D, transMat, normal_opacity, homotrans,
                          ap_level, table, offsets, gridrange, C, LD, L, S, Hres, align_corners,
                          interp, contract, beta, final_T, n_contrib, dL_dout_color, dL_dout_others,
                          dL_dtable, dL_dtransMat, dL_dhomoMat, dL_dmean2D, dL_dnormal, dL_dopacity,
-                         dL_gradsum);
+                         dL_gradsum, kernel_type, shapes, dL_dshapes);
 }
 
 // Working precision double: the same formulas and decisions, without float
@@ -536,12 +575,13 @@ void oracle_render_backward_f64(int W, int H, const uint32_t* ranges, const uint
                                 const float* dL_dout_color, const float* dL_dout_others,
                                 double* dL_dtable, double* dL_dtransMat, double* dL_dhomoMat,
                                 double* dL_dmean2D, double* dL_dnormal, double* dL_dopacity,
-                                double* dL_gradsum) {
+                                double* dL_gradsum, int kernel_type, const float* shapes,
+                                double* dL_dshapes) {
   render_backward<double>(W, H, ranges, point_list, means2D, transMat, normal_opacity, homotrans,
                           ap_level, table, offsets, gridrange, C, LD, L, S, Hres, align_corners,
                           interp, contract, beta, final_T, n_contrib, dL_dout_color,
                           dL_dout_others, dL_dtable, dL_dtransMat, dL_dhomoMat, dL_dmean2D,
-                          dL_dnormal, dL_dopacity, dL_gradsum);
+                          dL_dnormal, dL_dopacity, dL_gradsum, kernel_type, shapes, dL_dshapes);
 }
 
 void oracle_preprocess_backward(int P, const float* means3D, const float* scales,

@@ -59,7 +59,8 @@ def load() -> C.CDLL:
     lib.oracle_rvq_decode.argtypes = [i64, i32, i32, i32, vp, vp, vp]
     lib.oracle_num_threads.restype = i32
     lib.oracle_render_backward.argtypes = [i32, i32, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, i32, i32, u32, f32,
-                                           u32, i32, u32, i32, f32, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp]
+                                           u32, i32, u32, i32, f32, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp,
+                                           i32, vp, vp]
     lib.oracle_preprocess_backward.argtypes = [i32, vp, vp, vp, vp, vp, vp, vp, i32, i32, f32, f32, vp, vp, vp,
                                                vp, vp, vp, vp]
     lib.oracle_render_backward_f64.argtypes = lib.oracle_render_backward.argtypes
@@ -221,17 +222,22 @@ def forward(means3D, scales, rotations, opacities, homotrans, ap_level, table_f3
 
 def render_backward(pre, vals, ranges, fwd, homotrans, ap_level, table_f32, offsets, gridrange, W, H, C_out, LD,
                     L, S, Hres, dL_dcolor, dL_dothers, align_corners=False, interp=0, contract=False, beta=0.0,
-                    f64=False):
+                    f64=False, kernel_type=0, shapes=None):
     """renderCUDAsurfelBackward<C> mode 0 restated (nest_oracle_bw.cpp). `fwd` is the
     dict returned by render(). Returns the render-pass gradients (reference layouts).
-    f64=True evaluates the same formulas in double (float64 outputs)."""
+    f64=True evaluates the same formulas in double (float64 outputs). kernel_type
+    1-3 take per-surfel `shapes` [P] and add dL_dshapes [P]."""
     lib = load()
     P = pre["radii"].shape[0]
     table = _f32(table_f32)
     dt = np.float64 if f64 else np.float32
     g = dict(dL_dtable=np.zeros(table.shape, dt), dL_dtransMat=np.zeros((P, 9), dt),
              dL_dhomoMat=np.zeros((P, 9), dt), dL_dmean2D=np.zeros((P, 3), dt),
-             dL_dnormal=np.zeros((P, 3), dt), dL_dopacity=np.zeros(P, dt), dL_gradsum=np.zeros(P, dt))
+             dL_dnormal=np.zeros((P, 3), dt), dL_dopacity=np.zeros(P, dt), dL_gradsum=np.zeros(P, dt),
+             dL_dshapes=np.zeros(P, dt))
+    if kernel_type != 0:
+        assert shapes is not None
+        shapes = _f32(shapes).reshape(P)
     homotrans = _f32(homotrans).reshape(-1, 16)
     ap = _f32(ap_level).reshape(-1) if ap_level is not None else np.full(P, 1e9, np.float32)
     offs = np.ascontiguousarray(np.asarray(offsets, dtype=np.int32))
@@ -245,7 +251,8 @@ def render_backward(pre, vals, ranges, fwd, homotrans, ap_level, table_f32, offs
                                int(bool(align_corners)), int(interp), int(bool(contract)), float(beta),
                                _p(fwd["final_T"]), _p(fwd["n_contrib"]), _p(gc), _p(go), _p(g["dL_dtable"]),
                                _p(g["dL_dtransMat"]), _p(g["dL_dhomoMat"]), _p(g["dL_dmean2D"]),
-                               _p(g["dL_dnormal"]), _p(g["dL_dopacity"]), _p(g["dL_gradsum"]))
+                               _p(g["dL_dnormal"]), _p(g["dL_dopacity"]), _p(g["dL_gradsum"]), int(kernel_type),
+                               _p(shapes if kernel_type != 0 else None), _p(g["dL_dshapes"]))
     return g
 
 

@@ -17,6 +17,11 @@ places; the model states them explicitly so the comparison covers the rest:
     model feeds unit quaternions to that formula directly.
   * beta > 0 and the 0.99 alpha clamp are not modelled (the pin uses beta = 0 and
     opacities below 0.99).
+  * splat kernel 1 (beta, (1 - rho)^shape): the reference's dG/ds factor
+    -shape G / (1 - rho) (backward.cu:1965, :2025) is half of d/ds of its
+    forward (rho = s.x^2 + s.y^2 gives 2 shape G / (1 - rho) s); the model's G
+    has the forward's value, the full shape derivative and half the rho
+    derivative.
 """
 from __future__ import annotations
 
@@ -91,7 +96,28 @@ def query(xyz, apl, table, offsets, L, LD, S, Hres, vmin, vmax, align_corners=Fa
     return torch.cat(feats, 1)
 
 
-def render(means, scales, rots, opac, table, cam, lists, grid, apl_int, W, H):
+def splat_value(rho, shape, kernel_type: int):
+    """G of the splat kernels (forward.cu:864-902) and the kernel's own validity
+    mask (kernel 1 stops at the unit circle). shape: 0-d tensor."""
+    if kernel_type == 1:
+        inside = (rho < 1.0).detach()
+        base = torch.where(inside, 1.0 - rho, torch.ones_like(rho))
+        f = lambda b, s: b ** s  # noqa: E731
+        Gv = f(base, shape).detach()
+        G = Gv + 0.5 * (f(base, shape.detach()) - Gv) + (f(base.detach(), shape) - Gv)
+        return G, inside
+    if kernel_type == 2:
+        g = torch.exp(-0.5 * rho)
+        if float(shape.detach()) > 0:
+            g = (1.0 + shape) * g / (1.0 + shape * g)
+        return g, torch.ones_like(rho, dtype=torch.bool)
+    if kernel_type == 3:
+        pt = torch.clamp_min(rho, 1e-8) ** (0.5 * shape)
+        return torch.exp(-0.5 * pt), torch.ones_like(rho, dtype=torch.bool)
+    return torch.exp(-0.5 * rho), torch.ones_like(rho, dtype=torch.bool)
+
+
+def render(means, scales, rots, opac, table, cam, lists, grid, apl_int, W, H, kernel_type=0, shapes=None):
     """Forward pass over the oracle's tile lists. Returns (color [C,H,W], others [7,H,W], margins).
 
     margins: the smallest relative distance of any decision (alpha >= 1/255, the
@@ -146,9 +172,9 @@ def render(means, scales, rots, opac, table, cam, lists, grid, apl_int, W, H):
             b3 = (rho3d <= rho2d).detach()
             rho = torch.where(b3, rho3d, rho2d)
             c_d = torch.where(b3, sx * Tw[i, 0] + sy * Tw[i, 1] + Tw[i, 2], Tw[i, 2].expand(npx))
-            G = torch.exp(-0.5 * rho)
+            G, inside = splat_value(rho, shapes[i] if kernel_type else None, kernel_type)
             alpha = opac[i] * G
-            valid = (~done) & (c_d.detach() >= NEAR) & (alpha.detach() >= 1.0 / 255.0)
+            valid = (~done) & (c_d.detach() >= NEAR) & (alpha.detach() >= 1.0 / 255.0) & inside
             test_T = T * (1 - alpha)
             stop = valid & (test_T.detach() < 1e-4)
             live = (~done)
@@ -159,6 +185,8 @@ def render(means, scales, rots, opac, table, cam, lists, grid, apl_int, W, H):
                      np.abs(c_d.detach()[live].numpy() - NEAR)]
                 tt = test_T.detach()[live].numpy()
                 m.append(np.abs(tt - 1e-4) / 1e-4)
+                if kernel_type == 1:
+                    m.append(np.abs(rho.detach()[live].numpy() - 1.0))
                 margin = min(margin, *[float(np.min(x)) for x in m])
             done = done | stop
             valid = valid & ~stop

@@ -72,17 +72,18 @@ def make_cfg(scene, fp16=True, **kw):
         channels=g.channels, level_dim=g.level_dim, table_fp16=fp16, **kw)
 
 
-def gpu_grads(scene, inputs, gc, go, fp16=True, accum=False, **kw):
+def gpu_grads(scene, inputs, gc, go, fp16=True, accum=False, shapes=None, **kw):
     g = scene.grid
     cfg = make_cfg(scene, fp16, **kw)
+    shapes = None if shapes is None else shapes.cuda().contiguous()
     table = g.table.cuda() if fp16 else g.table.float().cuda()
     args = (inputs["means3D"].cuda().contiguous(), inputs["scales"].cuda().contiguous(),
             inputs["rotations"].cuda().contiguous(), inputs["opacities"].cuda().reshape(-1).contiguous(),
             inputs["homotrans"].cuda().reshape(-1, 16).contiguous(), inputs["ap_level"].cuda().reshape(-1).contiguous(),
             table.contiguous(), g.offsets.cuda().contiguous(), g.gridrange.cuda().contiguous())
-    n, color, others, radii, _, _, scratch = raster.rasterize_forward(cfg, *args)
+    n, color, others, radii, _, _, scratch = raster.rasterize_forward(cfg, *args, shapes=shapes)
     grads = raster.rasterize_backward(cfg, *args, radii, n, scratch, gc.cuda(), go.cuda(),
-                                      return_accumulators=accum)
+                                      return_accumulators=accum, shapes=shapes)
     torch.cuda.synchronize()
     return {k: v.cpu().numpy() for k, v in grads.items()}, radii.cpu().numpy()
 
@@ -94,7 +95,8 @@ def oracle_grads(scene, inputs, gc, go, **kw):
     pre = oracle.preprocess(inputs["means3D"].numpy(), inputs["scales"].numpy(), inputs["rotations"].numpy(),
                             inputs["opacities"].numpy(), vm, pm, W, H, kw.get("scale_modifier", 1.0))
     _, vals, ranges = oracle.bin_surfels(pre, W, H)
-    rkw = {k: v for k, v in kw.items() if k in ("interp", "contract", "beta", "align_corners")}
+    rkw = {k: v for k, v in kw.items() if k in ("interp", "contract", "beta", "align_corners", "kernel_type",
+                                                 "shapes")}
     f64 = bool(kw.get("f64", False))
     table = g.table.float().numpy()
     common = (inputs["homotrans"].numpy(), inputs["ap_level"].numpy(), table, g.offsets.numpy(),
@@ -124,14 +126,14 @@ def robust_rel_l2(a, b, frac=OUTLIER_FRAC):
     return float(np.sqrt(keep.sum()) / max(np.linalg.norm(b), 1e-30))
 
 
-def check_all(got, ref, exact=None, tol=REL_TOL):
+def check_all(got, ref, exact=None, tol=REL_TOL, keys=GRAD_KEYS):
     """Per gradient: robust relative L2 to the float32 oracle `ref` within tol;
     where that fails, robust relative L2 to the double-precision oracle `exact`
     within max(tol, 2 x the float32 oracle's own robust distance to it; 3 x
     for the densification statistic, a sum of transform-gradient rows).
     The hash-table gradient is compared whole (rows are table entries)."""
     report, ok = [], True
-    for k, (src, key) in GRAD_KEYS.items():
+    for k, (src, key) in keys.items():
         want = ref[src][key]
         assert np.isfinite(got[k]).all(), k
         assert np.linalg.norm(want) > 0, k
@@ -296,3 +298,68 @@ def test_dropin_autograd_matches_oracle():
            "table": table.grad, "gradsum": ap.grad, "means2D": means2D.grad}
     assert opac.grad.shape == opac.shape and ap.grad.shape == ap.shape and table.grad.dtype == table.dtype
     check_all({k: v.detach().cpu().numpy() for k, v in got.items()}, ref, exact)
+
+
+SHAPE_KEYS = {**GRAD_KEYS, "shapes": ("g", "dL_dshapes")}
+
+
+@pytest.mark.parametrize("kernel_type,lo,hi", [(1, 0.3, 4.0), (1, -0.5, 0.0), (2, 0.0, 2.0), (2, -1.0, 0.0),
+                                               (3, 2.0, 8.0), (3, 0.5, 2.0)])
+def test_backward_splat_kernels_match_oracle(kernel_type, lo, hi):
+    """kernel_type 1 (beta), 2 (flex), 3 (general): every gradient and dL/dshape
+    (backward.cu:1862-2045) against the oracle, shapes drawn in [lo, hi]
+    (flex shapes <= 0 leave the plain Gaussian; beta exponents <= 0 give an
+    alpha that grows towards the unit circle)."""
+    sc = small_scene(seed=19, table_range=1e-4)  # radii on no rounding boundary
+    inputs = api_inputs(sc)
+    g = torch.Generator().manual_seed(100 + kernel_type)
+    shapes = (torch.rand(sc.P, generator=g) * (hi - lo) + lo).float()
+    gc, go = upstream(sc, seed=5)
+    got, radii = gpu_grads(sc, inputs, gc, go, kernel_type=kernel_type, shapes=shapes)
+    kw = dict(interp=sc.grid.interpolation, align_corners=sc.grid.align_corners, kernel_type=kernel_type,
+              shapes=shapes.numpy())
+    ref, pre = oracle_grads(sc, inputs, gc, go, **kw)
+    np.testing.assert_array_equal(radii, pre["radii"])
+    exact, _ = oracle_grads(sc, inputs, gc, go, f64=True, **kw)
+    if kernel_type == 2 and hi <= 0:
+        assert not ref["g"]["dL_dshapes"].any() and not got["shapes"].any()
+        check_all(got, ref, exact)
+    else:
+        check_all(got, ref, exact, keys=SHAPE_KEYS)
+
+
+def test_dropin_autograd_shapes_gradient():
+    """The drop-in Function returns dL/dshapes in shapes' slot (kernel_type 3)."""
+    sc = small_scene(seed=18, table_range=1e-4)
+    inputs = api_inputs(sc)
+    gc, go = upstream(sc, seed=6)
+    cam, g = sc.camera, sc.grid
+    dev = "cuda"
+    rs = dsr.GaussianRasterizationSettings(
+        image_height=cam.height, image_width=cam.width, tanfovx=cam.tanfovx, tanfovy=cam.tanfovy,
+        bg=torch.zeros(3, device=dev), scale_modifier=1.0, viewmatrix=cam.world_view_transform.to(dev),
+        projmatrix=cam.full_proj_transform.to(dev), sh_degree=0, campos=cam.camera_center.to(dev),
+        prefiltered=False, debug=False, beta=0.0, if_contract=False, record_transmittance=False,
+        max_intersections=0)
+    hs = dsr.HashGridSettings(L=g.levels, S=g.S, H=g.base_resolution, align_corners=g.align_corners,
+                              interpolation=g.interpolation,
+                              shape_dims=torch.tensor([0, g.channels, g.channels], dtype=torch.int32, device=dev))
+    r = dsr.GaussianRasterizer(rs, hs)
+    P = sc.P
+    gen = torch.Generator().manual_seed(7)
+    shapes = torch.rand(P, 1, generator=gen) * 6 + 2
+    leaf = lambda t: t.to(dev).clone().requires_grad_(True)  # noqa: E731
+    means, opac, shp = leaf(inputs["means3D"]), leaf(inputs["opacities"]), leaf(shapes)
+    color, radii, allmap, _, _ = r(
+        means3D=means, means2D=torch.zeros(P, 3, device=dev), shs=torch.zeros(P, 1, 3, device=dev),
+        opacities=opac, scales=inputs["scales"].to(dev), rotations=inputs["rotations"].to(dev),
+        homotrans=inputs["homotrans"].to(dev), ap_level=inputs["ap_level"].to(dev), features=g.table.to(dev),
+        offsets=g.offsets.to(dev), gridrange=g.gridrange.to(dev), render_mode=0, shapes=shp, kernel_type=3)
+    ((color * gc.to(dev)).sum() + (allmap * go.to(dev)).sum()).backward()
+    assert shp.grad is not None and shp.grad.shape == shp.shape
+    kw = dict(interp=g.interpolation, align_corners=g.align_corners, kernel_type=3, shapes=shapes.numpy())
+    ref, _ = oracle_grads(sc, inputs, gc, go, **kw)
+    exact, _ = oracle_grads(sc, inputs, gc, go, f64=True, **kw)
+    keys = {k: SHAPE_KEYS[k] for k in ("means3D", "opacity", "shapes")}
+    got = {"means3D": means.grad, "opacity": opac.grad, "shapes": shp.grad}
+    check_all({k: v.detach().cpu().numpy().reshape(P, -1) for k, v in got.items()}, ref, exact, keys=keys)

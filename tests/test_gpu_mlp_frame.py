@@ -54,7 +54,9 @@ def test_fused_frame_matches_oracle(table_range):
     rgb = fr.render(sc.camera)
     torch.cuda.synchronize()
     assert np.array_equal(fr.decoded.cpu().numpy().view(np.uint32), decoded.view(np.uint32))
-    assert abs(fr.num_rendered - n) <= max(2, n // 1000)
+    # Tile instances: the reference's rectangles minus the tiles the surfel's
+    # alpha box (alpha >= 1/255) does not reach, so never more than the oracle's.
+    assert 0 < fr.num_rendered <= n
     feats = fr.features.cpu().numpy()
     assert np.abs(feats - out["out_color"]).max() <= TOL
     others = fr.others.cpu().numpy()

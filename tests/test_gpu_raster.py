@@ -205,7 +205,7 @@ def test_scene_from_reference_ply_renders_like_the_direct_inputs(tmp_path):
 
 
 @pytest.mark.parametrize("kernel_type,lo,hi", [(1, 0.3, 4.0), (1, -0.5, 0.0), (2, 0.0, 2.0), (3, 2.0, 8.0),
-                                               (3, -1.0, 0.5)])
+                                               (3, 0.5, 2.0), (3, -1.0, 0.5)])
 def test_raster_splat_kernels_match_oracle(kernel_type, lo, hi):
     """kernel_type 1 (beta), 2 (flex), 3 (general) of forward.cu:864-902 with
     per-surfel shapes drawn in [lo, hi] (including the shapes for which alpha
@@ -240,29 +240,3 @@ def test_raster_splat_kernels_match_oracle(kernel_type, lo, hi):
     allmap = allmap.cpu().numpy()
     assert allmap[7].sum() > 100
     compare(out, color.cpu().numpy(), allmap)
-
-
-def test_raster_splat_kernel_backward_not_built():
-    sc = small_scene(n=200, seed=30)
-    inp = api_inputs(sc)
-    cam, grid = sc.camera, sc.grid
-    dev = "cuda"
-    rs = dsr.GaussianRasterizationSettings(
-        image_height=cam.height, image_width=cam.width, tanfovx=cam.tanfovx, tanfovy=cam.tanfovy,
-        bg=torch.zeros(3, device=dev), scale_modifier=1.0, viewmatrix=cam.world_view_transform.to(dev),
-        projmatrix=cam.full_proj_transform.to(dev), sh_degree=0, campos=cam.camera_center.to(dev),
-        prefiltered=False, debug=False, beta=0.0, if_contract=False, record_transmittance=False,
-        max_intersections=0)
-    hs = dsr.HashGridSettings(L=grid.levels, S=grid.S, H=grid.base_resolution, align_corners=False,
-                              interpolation=0, shape_dims=torch.tensor([0, grid.channels, grid.channels],
-                                                                       dtype=torch.int32, device=dev))
-    r = dsr.GaussianRasterizer(rs, hs)
-    m = inp["means3D"].to(dev).requires_grad_(True)
-    color, _, _, _, _ = r(means3D=m, means2D=torch.zeros(sc.P, 3, device=dev), shs=torch.zeros(sc.P, 1, 3, device=dev),
-                          opacities=inp["opacities"].to(dev), scales=inp["scales"].to(dev),
-                          rotations=inp["rotations"].to(dev), homotrans=None, ap_level=inp["ap_level"].to(dev),
-                          features=grid.table.to(dev), offsets=grid.offsets.to(dev),
-                          gridrange=grid.gridrange.to(dev), render_mode=0, shapes=torch.ones(sc.P, device=dev),
-                          kernel_type=1)
-    with pytest.raises(NotImplementedError):
-        color.sum().backward()

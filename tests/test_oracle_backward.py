@@ -53,6 +53,8 @@ def oracle_grads(c):
                             W, H)
     _, vals, ranges = oracle.bin_surfels(pre, W, H)
     kw = dict(interp=c["interp"])
+    if c.get("kernel_type"):
+        kw.update(kernel_type=c["kernel_type"], shapes=c["shapes"].numpy())
     fwd = oracle.render(pre, vals, ranges, c["homo"].numpy(), c["ap"].numpy(), c["table"].numpy(),
                         grid.offsets.numpy(), grid.gridrange.numpy(), W, H, grid.channels, grid.level_dim,
                         grid.levels, grid.S, grid.base_resolution, **kw)
@@ -66,18 +68,21 @@ def oracle_grads(c):
 
 def model_grads(c, pre, vals, ranges):
     cam, grid = c["cam"], c["grid"]
-    leaves = [c[k].double().clone().requires_grad_(True) for k in ("means", "scales", "rots", "opac", "table")]
-    means, scales, rots, opac, table = leaves
+    names = ("means", "scales", "rots", "opac", "table") + (("shapes",) if c.get("kernel_type") else ())
+    leaves = [c[k].double().clone().requires_grad_(True) for k in names]
+    means, scales, rots, opac, table = leaves[:5]
     info = dict(L=grid.levels, LD=grid.level_dim, S=grid.S, H=grid.base_resolution, offsets=grid.offsets.numpy(),
                 vmin=float(grid.gridrange[0]), vmax=float(grid.gridrange[1]), interp=c["interp"])
     visible = torch.as_tensor(pre["radii"] > 0)
     color, others, margin, _ = bw_model.render(
         means, scales, rots, opac, table,
         dict(viewmatrix=cam.world_view_transform.numpy(), projmatrix=cam.full_proj_transform.numpy()),
-        (ranges, vals), info, np.floor(c["ap"].numpy()).astype(np.int64), c["W"], c["H"])
+        (ranges, vals), info, np.floor(c["ap"].numpy()).astype(np.int64), c["W"], c["H"],
+        kernel_type=c.get("kernel_type", 0), shapes=leaves[5] if len(leaves) > 5 else None)
     loss = (color * c["gc"].double()).sum() + (others * c["go"][:7].double()).sum()
     loss.backward()
-    grads = {k: v.grad.detach().numpy() for k, v in zip(("means", "scales", "rots", "opac", "table"), leaves)}
+    grads = {k: (v.grad if v.grad is not None else torch.zeros_like(v)).detach().numpy()
+             for k, v in zip(names, leaves)}
     for k in ("means", "scales", "rots", "opac"):
         grads[k][~visible.numpy()] = 0.0
     return color.detach().numpy(), others.detach().numpy(), margin, grads
@@ -114,3 +119,28 @@ def test_oracle_backward_gradsum_and_mean2d_statistic():
     vis = pre["radii"] > 0
     expect = (g["dL_dtransMat"][:, 2] * pre["transMat"][:, 8]).astype(np.float64) * 0.5 * Wq
     np.testing.assert_allclose(pg["dL_dmean2D"][vis, 0], expect[vis].astype(np.float32), rtol=1e-6, atol=0)
+
+
+@pytest.mark.parametrize("kernel_type,lo,hi,seed", [(1, 0.5, 3.0, 11), (2, 0.2, 2.0, 12), (2, -1.0, 0.0, 5),
+                                                    (3, 2.0, 6.0, 14)])
+def test_oracle_backward_splat_kernels_match_autograd(kernel_type, lo, hi, seed):
+    """The splat kernels' gradients (backward.cu:1862-2045), dL/dshape included,
+    against autograd of the same forward (kernel 1 with the reference's halved
+    rho derivative, stated in bw_model)."""
+    c = tiny_case(seed)
+    g = torch.Generator().manual_seed(seed)
+    c["kernel_type"] = kernel_type
+    c["shapes"] = (torch.rand(c["means"].shape[0], generator=g) * (hi - lo) + lo).float()
+    pre, vals, ranges, fwd, gr, pg = oracle_grads(c)
+    color, others, margin, mg = model_grads(c, pre, vals, ranges)
+    assert margin > 1e-5, "a branch sits on its threshold; pick another seed"
+    assert np.max(np.abs(color - fwd["out_color"])) < 2e-5
+    assert np.max(np.abs(others - fwd["out_others"][:7])) < 2e-4
+    checks = {"means": pg["dL_dmeans3D"], "scales": pg["dL_dscales"], "rots": pg["dL_drots"],
+              "opac": gr["dL_dopacity"], "table": gr["dL_dtable"], "shapes": gr["dL_dshapes"]}
+    if hi <= 0:  # flex kernel with shape <= 0: the plain Gaussian, no shape gradient
+        assert not gr["dL_dshapes"].any()
+        checks.pop("shapes")
+    for k, got in checks.items():
+        assert np.linalg.norm(mg[k]) > 0, k
+        assert rel_l2(got, mg[k]) < 1e-4, (k, rel_l2(got, mg[k]))
