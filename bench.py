@@ -283,6 +283,8 @@ def run_ours(args):
     h2d += host_cam.numel() * 4
     d2h = host_rgb[0].numel() * 4
 
+    exchange = exchange_timing(shard, fr.codebooks, dev, P, fr.stages, fr.dims) if world > 1 else None
+
     # Work statistics of the (identical) frames.
     samples = float(fr.others[7].sum().item())
     num_rendered = fr.num_rendered
@@ -324,6 +326,8 @@ def run_ours(args):
         "gpu_launches": int(launches),
         "clocks": clk.summary(),
     }
+    if exchange is not None:
+        line["rvq_exchange"] = exchange
     if not args.no_train:
         line["train_step"] = train_step_timing(sc, cam, dev, steps=min(args.steps, 10))
     if not args.no_multiview:
@@ -337,6 +341,39 @@ def run_ours(args):
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
+
+
+def exchange_timing(shard, codebooks, dev, P, stages, dims, iters=20):
+    """N > 1: the north_star's exchange (decode this rank's rows, all-gather the
+    decoded attributes) against all-gathering the RVQ indices and decoding every
+    row on every rank. Device time per exchange, max over ranks; both leave the
+    same rows in the frame's attribute buffer."""
+    import torch
+    import torch.distributed as dist
+
+    from nest_b200 import raster
+    out = {}
+    world = shard.world
+    for name, fn in (("attributes", lambda: shard.decode_and_gather(codebooks, raster.rvq_decode)),
+                     ("indices", lambda: shard.gather_indices_and_decode(codebooks, raster.rvq_decode))):
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize()
+        dist.barrier()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        for _ in range(iters):
+            fn()
+        e.record()
+        torch.cuda.synchronize()
+        t = torch.tensor([s.elapsed_time(e) / iters], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        out[f"{name}_ms"] = round(float(t.item()), 4)
+    out["received_bytes_per_rank"] = {"attributes": int(P * (world - 1) / world) * 4 * dims,
+                                      "indices": int(P * (world - 1) / world) * stages}
+    out["note"] = ("attributes: decode own shard + NCCL all-gather of fp32 rows (the frame's path); "
+                   "indices: NCCL all-gather of uint8 indices + decode of all rows on every rank")
+    return out
 
 
 def oracle_frame(sc, row_stride, threads=None):

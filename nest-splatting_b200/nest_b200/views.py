@@ -75,6 +75,19 @@ class DecodeShard:
             self.dec_full.copy_(self.dec_shard)
         return self.decoded
 
+    def gather_indices_and_decode(self, codebooks: torch.Tensor, decode_fn, group=None) -> torch.Tensor:
+        """The alternative exchange: all-gather the index shards (K bytes per row
+        instead of 4 D) and decode every row on every rank. Same dec_full rows."""
+        if getattr(self, "idx_full", None) is None:
+            self.idx_full = torch.empty((self.idx_shard.shape[0] * self.world, self.idx_shard.shape[1]),
+                                        dtype=torch.uint8, device=self.idx_shard.device)
+        if self.world > 1:
+            dist.all_gather_into_tensor(self.idx_full, self.idx_shard, group=group)
+        else:
+            self.idx_full.copy_(self.idx_shard)
+        decode_fn(self.idx_full[: self.P], codebooks, out=self.dec_full[: self.P])
+        return self.decoded
+
     def decode_and_gather(self, codebooks: torch.Tensor, decode_fn, group=None,
                           idx: torch.Tensor | None = None) -> torch.Tensor:
         """decode_fn(idx, codebooks, out=...) on this rank's rows (idx_shard, or `idx`

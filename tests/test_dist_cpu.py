@@ -40,8 +40,10 @@ def _worker(rank, world, port, n, result_dir):
     try:
         cb, idx = synth.config0(n=n, seed=7)
         sh = DecodeShard.create(idx, cb.shape[2], world, rank)
-        full = sh.decode_and_gather(cb, _decode_cpu)
-        torch.save({"full": full.clone(), "views": camera_share(64, world, rank)},
+        full = sh.decode_and_gather(cb, _decode_cpu).clone()
+        sh.dec_full.zero_()
+        alt = sh.gather_indices_and_decode(cb, _decode_cpu)
+        torch.save({"full": full, "alt": alt.clone(), "views": camera_share(64, world, rank)},
                    os.path.join(result_dir, f"rank{rank}.pt"))
     finally:
         dist.destroy_process_group()
@@ -59,6 +61,7 @@ def test_sharded_decode_all_gather_matches_full_decode(tmp_path, world, n):
     for r in range(world):
         d = torch.load(tmp_path / f"rank{r}.pt")
         assert np.array_equal(d["full"].numpy().view(np.uint32), ref.view(np.uint32))
+        assert np.array_equal(d["alt"].numpy().view(np.uint32), ref.view(np.uint32))
         views += d["views"]
     assert sorted(views) == list(range(64))
 
