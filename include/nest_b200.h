@@ -94,8 +94,13 @@ typedef struct ns_raster_settings {
   /* Splat kernel (forward.cu:864-919): 0 Gaussian (with beta above), 1 beta
    * kernel alpha = o (1 - rho)^shape for rho < 1, 2 flex (per-surfel beta =
    * shape), 3 general G = exp(-0.5 rho^(shape / 2)); 1-3 read ns_surfels.shapes.
-   * Forward only: ns_rasterize_backward and ns_render_frame take kernel 0. */
+   * ns_render_frame takes kernel 0. */
   int32_t kernel_type;
+  /* Backward only. 1: the hash-table gradient is reduced in 64-bit fixed point
+   * (2^32 / 2^ceil(log2 max|dL_dout_color|) units), so it is bit-identical from
+   * run to run; needs ns_backward_scratch_bytes_deterministic. 0: float atomics,
+   * whose summation order varies, as in the reference. */
+  int32_t deterministic;
 } ns_raster_settings;
 
 /* Per-surfel inputs of the rasterizer (render_mode 0). */
@@ -178,6 +183,9 @@ typedef struct ns_raster_grads_out {
 
 /* Scratch of the backward pass: per-surfel gradient accumulators. */
 size_t ns_backward_scratch_bytes(int32_t P);
+/* Scratch of the backward pass with settings->deterministic = 1: the per-surfel
+ * accumulators, the fixed-point table gradient and its scale. */
+size_t ns_backward_scratch_bytes_deterministic(int32_t P, int64_t table_rows, int32_t level_dim);
 
 /* Backward rasterization, render_mode 0. settings, surfels, geom, binning and
  * image must be those of the forward call whose outputs the gradients refer to

@@ -60,6 +60,22 @@ enum : int {
   kGShape = 18,     // dL/dshape (splat kernels 1-3)
 };
 
+// Fixed-point unit of the deterministic table gradient: 2^32 units per
+// 2^ceil(log2 gmax), gmax = max |dL/dcolor|. A sample's contribution to a table
+// entry is w * alpha * T * dL/dcolor with w, alpha * T <= 1, so it stays below
+// 2^32 units, a warp's aggregated sum below 2^37, and an entry's sum fits in 63
+// bits while fewer than 2^31 maximal contributions land on it. Integer addition
+// is associative, so the sums do not depend on the order of the atomics.
+// Returns 0 for a non-finite gmax (the finish kernel then writes NaN).
+__device__ __forceinline__ float fixed_point_scale(uint32_t gmax_bits) {
+  const float g = __uint_as_float(gmax_bits);
+  if (!(g <= 3.0e38f)) return 0.0f;
+  if (g == 0.0f) return 1.0f;
+  int e;
+  frexpf(g, &e);  // g < 2^e
+  return ldexpf(1.0f, 32 - max(e, -90));
+}
+
 // a * b - c * d with one rounding error at most (Kahan's difference of products
 // with fused multiply-adds): the z rows of the transform gradient that feed the
 // densification statistic subtract nearly equal products.
@@ -95,8 +111,9 @@ struct BwSmem {
 };
 
 // kAnyKernel: built with the splat kernels 1-3 (p.kernel_type); the Gaussian-only
-// instantiation keeps them out of the hot loop.
-template <typename TableT, bool kAnyKernel>
+// instantiation keeps them out of the hot loop. kFixed: the table gradient goes
+// to p.dL_dtable_fixed in fixed point (deterministic mode).
+template <typename TableT, bool kAnyKernel, bool kFixed>
 __global__ void __launch_bounds__(kThreads, 2) blend_backward_kernel(const BackwardParams p) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   BwSmem& S = *reinterpret_cast<BwSmem*>(smem_raw);
@@ -114,6 +131,7 @@ __global__ void __launch_bounds__(kThreads, 2) blend_backward_kernel(const Backw
   const float half_shift = p.align_corners ? 0.0f : 0.5f;
   const uint32_t L = p.L;
   const float vmin = p.gridrange[0], vmax = p.gridrange[1];
+  const float fscale = kFixed ? fixed_point_scale(*p.grad_max_bits) : 0.0f;
 
   if (t < (int)L) S.lv[t] = make_level<TableT>(p.table, p.offsets, p.S, p.Hres, p.align_corners, t);
   if (t < 9) {
@@ -441,9 +459,18 @@ __global__ void __launch_bounds__(kThreads, 2) blend_backward_kernel(const Backw
             nxt = nxt >= 0 ? nn : -1;
           }
           if (on && head) {
-            float2* dtab = reinterpret_cast<float2*>(p.dL_dtable) + lcst.row0;
+            if (kFixed) {
+              unsigned long long* dfx = p.dL_dtable_fixed + 2 * (size_t)lcst.row0;
 #pragma unroll
-            for (int c = 0; c < 8; c++) atomicAdd(dtab + idx[c], v[c]);
+              for (int c = 0; c < 8; c++) {
+                atomicAdd(dfx + 2 * (size_t)idx[c], (unsigned long long)llrintf(v[c].x * fscale));
+                atomicAdd(dfx + 2 * (size_t)idx[c] + 1, (unsigned long long)llrintf(v[c].y * fscale));
+              }
+            } else {
+              float2* dtab = reinterpret_cast<float2*>(p.dL_dtable) + lcst.row0;
+#pragma unroll
+              for (int c = 0; c < 8; c++) atomicAdd(dtab + idx[c], v[c]);
+            }
           }
         }
         if (has) S.samp[k][pp] = make_float4(fdot, d0, d1, d2);
@@ -823,19 +850,73 @@ preprocess_backward_kernel(int P, const float* __restrict__ means3D, const float
   if (o.dL_dshapes) o.dL_dshapes[i] = a[kGShape];
 }
 
-template <typename TableT, bool kAnyKernel>
-int launch_backward(const BackwardParams& p, int tiles, cudaStream_t stream) {
+// max |g| over n floats as float bits, by atomicMax on the bit patterns (their
+// order is the order of the non-negative values; NaN sorts above +inf).
+// n4: float4 groups read vectorised (0 when g is not 16-byte aligned).
+__global__ void __launch_bounds__(256) grad_abs_max_kernel(const float* __restrict__ g, size_t n,
+                                                           size_t n4, uint32_t* __restrict__ out) {
+  uint32_t m = 0;
+  const size_t stride = (size_t)gridDim.x * blockDim.x;
+  const float4* g4 = reinterpret_cast<const float4*>(g);
+  for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += stride) {
+    const float4 v = g4[i];
+    m = max(m, max(max(__float_as_uint(v.x) & 0x7fffffffu, __float_as_uint(v.y) & 0x7fffffffu),
+                   max(__float_as_uint(v.z) & 0x7fffffffu, __float_as_uint(v.w) & 0x7fffffffu)));
+  }
+  for (size_t i = 4 * n4 + (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride)
+    m = max(m, __float_as_uint(g[i]) & 0x7fffffffu);
+  m = __reduce_max_sync(0xffffffffu, m);
+  if ((threadIdx.x & 31) == 0 && m != 0) atomicMax(out, m);
+}
+
+// Fixed point -> float: one rounding of the exact sum (a power-of-two scale).
+__global__ void __launch_bounds__(256) table_fixed_finish_kernel(const unsigned long long* __restrict__ fx,
+                                                                 size_t n, const uint32_t* __restrict__ gmax,
+                                                                 float* __restrict__ out) {
+  const float scale = fixed_point_scale(*gmax);
+  const size_t stride = (size_t)gridDim.x * blockDim.x;
+  for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride)
+    out[i] = scale != 0.0f ? (float)((double)(long long)fx[i] / (double)scale) : __int_as_float(0x7fc00000);
+}
+
+template <typename TableT, bool kAnyKernel, bool kFixed>
+int launch_backward3(const BackwardParams& p, int tiles, cudaStream_t stream) {
   const int smem = (int)sizeof(BwSmem);
-  NS_CUDA_TRY(cudaFuncSetAttribute(blend_backward_kernel<TableT, kAnyKernel>,
+  NS_CUDA_TRY(cudaFuncSetAttribute(blend_backward_kernel<TableT, kAnyKernel, kFixed>,
                                    cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-  blend_backward_kernel<TableT, kAnyKernel><<<tiles, kThreads, smem, stream>>>(p);
+  blend_backward_kernel<TableT, kAnyKernel, kFixed><<<tiles, kThreads, smem, stream>>>(p);
   NS_LAUNCH_CHECK();
   return NS_OK;
+}
+
+template <typename TableT, bool kAnyKernel>
+int launch_backward(const BackwardParams& p, int tiles, cudaStream_t stream) {
+  return p.dL_dtable_fixed ? launch_backward3<TableT, kAnyKernel, true>(p, tiles, stream)
+                           : launch_backward3<TableT, kAnyKernel, false>(p, tiles, stream);
 }
 
 }  // namespace
 
 size_t backward_accum_bytes(int64_t P) { return (size_t)max64(P, 1) * kGradWords * sizeof(float); }
+
+int table_grad_max_launch(const float* dL_dcolor, size_t n, uint32_t* gmax, cudaStream_t stream) {
+  NS_CUDA_TRY(cudaMemsetAsync(gmax, 0, sizeof(uint32_t), stream));
+  if (n == 0) return NS_OK;
+  const int blocks = (int)min64((int64_t)div_up64((int64_t)(n / 4 + 1), 256), 148 * 8);
+  const size_t n4 = (reinterpret_cast<uintptr_t>(dL_dcolor) & 15u) ? 0 : n / 4;
+  grad_abs_max_kernel<<<blocks, 256, 0, stream>>>(dL_dcolor, n, n4, gmax);
+  NS_LAUNCH_CHECK();
+  return NS_OK;
+}
+
+int table_grad_finish_launch(const unsigned long long* fx, size_t n, const uint32_t* gmax, float* out,
+                             cudaStream_t stream) {
+  if (n == 0) return NS_OK;
+  const int blocks = (int)min64((int64_t)div_up64((int64_t)n, 256), 148 * 16);
+  table_fixed_finish_kernel<<<blocks, 256, 0, stream>>>(fx, n, gmax, out);
+  NS_LAUNCH_CHECK();
+  return NS_OK;
+}
 
 int blend_backward_launch(const BackwardParams& p, int fp16, cudaStream_t stream) {
   if (p.LD != 2 || p.C > kAccStride || p.C <= 0) return NS_ERR_UNSUPPORTED;

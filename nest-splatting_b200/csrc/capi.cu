@@ -335,6 +335,12 @@ int ns_rasterize_forward(const ns_raster_settings* settings, const ns_surfels* s
 
 size_t ns_backward_scratch_bytes(int32_t P) { return align_up(backward_accum_bytes(P)); }
 
+size_t ns_backward_scratch_bytes_deterministic(int32_t P, int64_t table_rows, int32_t level_dim) {
+  const int64_t entries = max64(table_rows, 0) * max64(level_dim, 0);
+  return ns_backward_scratch_bytes(P) + align_up((size_t)entries * sizeof(unsigned long long)) +
+         align_up(sizeof(uint32_t));
+}
+
 int ns_rasterize_backward(const ns_raster_settings* settings, const ns_surfels* surfels,
                           const ns_raster_grads_in* gi, const ns_raster_grads_out* go,
                           const void* geom, size_t geom_bytes, const void* binning,
@@ -353,6 +359,7 @@ int ns_rasterize_backward(const ns_raster_settings* settings, const ns_surfels* 
   if (!go->dL_dmeans3D || !go->dL_dmean2D || !go->dL_dopacity || !go->dL_dscales ||
       !go->dL_drots || !go->dL_dtable || !go->dL_gradsum || go->table_rows < 0)
     return NS_ERR_INVALID;
+  const bool det = settings->deterministic != 0;
   if (go->table_rows > 0)
     NS_CUDA_TRY(cudaMemsetAsync(go->dL_dtable, 0,
                                 (size_t)go->table_rows * settings->level_dim * sizeof(float), stream));
@@ -365,7 +372,9 @@ int ns_rasterize_backward(const ns_raster_settings* settings, const ns_surfels* 
   if (geom_bytes < ns_geometry_scratch_bytes(P)) return NS_ERR_SCRATCH;
   if (image_bytes < ns_image_scratch_bytes(settings->image_width, settings->image_height))
     return NS_ERR_SCRATCH;
-  if (scratch_bytes < ns_backward_scratch_bytes(P)) return NS_ERR_SCRATCH;
+  if (scratch_bytes < (det ? ns_backward_scratch_bytes_deterministic(P, go->table_rows, settings->level_dim)
+                           : ns_backward_scratch_bytes(P)))
+    return NS_ERR_SCRATCH;
   const int64_t cap = bin_capacity(binning_bytes);
   if (cap < 0 || num_rendered > cap) return NS_ERR_SCRATCH;
   const int W = settings->image_width, H = settings->image_height;
@@ -374,6 +383,20 @@ int ns_rasterize_backward(const ns_raster_settings* settings, const ns_surfels* 
   BinState b = carve_bin(const_cast<void*>(binning), cap, nullptr);
   float* accum = static_cast<float*>(scratch);
   NS_CUDA_TRY(cudaMemsetAsync(accum, 0, backward_accum_bytes(P), stream));
+  const size_t table_entries = (size_t)go->table_rows * settings->level_dim;
+  unsigned long long* table_fixed = nullptr;
+  uint32_t* grad_max = nullptr;
+  if (det) {
+    unsigned char* base = static_cast<unsigned char*>(scratch) + ns_backward_scratch_bytes(P);
+    table_fixed = reinterpret_cast<unsigned long long*>(base);
+    grad_max = reinterpret_cast<uint32_t*>(base + align_up(table_entries * sizeof(unsigned long long)));
+    NS_CUDA_TRY(cudaMemsetAsync(table_fixed, 0, table_entries * sizeof(unsigned long long), stream));
+    rc = table_grad_max_launch(gi->dL_dout_color,
+                               (size_t)settings->channels * (size_t)settings->image_width *
+                                   (size_t)settings->image_height,
+                               grad_max, stream);
+    if (rc) return rc;
+  }
   // W and H as preprocessCUDA's backward recomputes them from the focal length
   // (backward.cu:2247-2248, focal from rasterizer_impl.cu:508-509), in float.
   const float focal_x = (float)W / (2.0f * settings->tanfovx);
@@ -412,9 +435,15 @@ int ns_rasterize_backward(const ns_raster_settings* settings, const ns_surfels* 
   bp.dL_dcolor = gi->dL_dout_color;
   bp.dL_dothers = gi->dL_dout_others;
   bp.dL_dtable = go->dL_dtable;
+  bp.dL_dtable_fixed = table_fixed;
+  bp.grad_max_bits = grad_max;
   bp.accum = accum;
   rc = blend_backward_launch(bp, settings->table_fp16, stream);
   if (rc) return rc;
+  if (det) {
+    rc = table_grad_finish_launch(table_fixed, table_entries, grad_max, go->dL_dtable, stream);
+    if (rc) return rc;
+  }
   return preprocess_backward_launch(P, surfels->means3D, surfels->scales, surfels->rotations,
                                     gi->radii, settings->viewmatrix, settings->projmatrix, Wq, Hq,
                                     accum, *go, stream);

@@ -58,9 +58,14 @@ struct BackwardParams {
   const float* dL_dcolor;
   const float* dL_dothers;
   float* dL_dtable;
+  unsigned long long* dL_dtable_fixed;  // non-null: fixed-point table gradient (deterministic)
+  const uint32_t* grad_max_bits;        // max |dL/dcolor| as float bits (deterministic)
   float* accum;
 };
 size_t backward_accum_bytes(int64_t P);
+int table_grad_max_launch(const float* dL_dcolor, size_t n, uint32_t* gmax, cudaStream_t stream);
+int table_grad_finish_launch(const unsigned long long* fx, size_t n, const uint32_t* gmax, float* out,
+                             cudaStream_t stream);
 int blend_backward_launch(const BackwardParams& p, int fp16, cudaStream_t stream);
 int preprocess_backward_launch(int P, const float* means3D, const float* scales,
                                const float* rotations, const int32_t* radii, const float* vm,

@@ -21,6 +21,10 @@ them).
 
 `features` may be fp32 (as the reference stores the table) or fp16 (read as
 fp16 pairs by the kernels, half the L2 traffic).
+
+Under `torch.use_deterministic_algorithms(True)` the backward reduces the
+hash-table gradient in 64-bit fixed point, so it is bit-identical from run to
+run (the per-surfel gradients keep float atomics, as in the reference).
 """
 from __future__ import annotations
 
@@ -104,7 +108,7 @@ class _RasterizeGaussians(torch.autograd.Function):
             base_resolution=int(hashgrid_settings.H), align_corners=bool(hashgrid_settings.align_corners),
             interpolation=int(hashgrid_settings.interpolation), channels=int(OS),
             level_dim=int(feats.shape[1]), table_fp16=feats.dtype == torch.float16,
-            kernel_type=int(kernel_type))
+            kernel_type=int(kernel_type), deterministic=torch.are_deterministic_algorithms_enabled())
         ap = _nonempty(ap_level)
         args = (means3D.detach().contiguous().float(), scales.detach().contiguous().float(),
                 rotations.detach().contiguous().float(), opacities.detach().contiguous().float().reshape(-1),

@@ -23,7 +23,8 @@ EXPORTED = [
     "ns_geometry_scratch_bytes", "ns_image_scratch_bytes", "ns_binning_scratch_bytes",
     "ns_rasterize_forward", "ns_read_device_status", "ns_mark_visible", "ns_mlp_forward",
     "ns_rvq_decode", "ns_radix_sort_temp_bytes", "ns_radix_sort_pairs", "ns_render_frame",
-    "ns_radix_sort_pairs_noalloc", "ns_backward_scratch_bytes", "ns_rasterize_backward",
+    "ns_radix_sort_pairs_noalloc", "ns_backward_scratch_bytes", "ns_backward_scratch_bytes_deterministic",
+    "ns_rasterize_backward",
     "ns_normal_error", "ns_normal_error_scratch_bytes", "ns_normal_error_backward", "ns_mlp_backward",
     "ns_allmap_decode",
 ]
@@ -39,6 +40,7 @@ class RasterSettings(C.Structure):
         ("levels", C.c_uint32), ("level_scale_log2", C.c_float), ("base_resolution", C.c_uint32),
         ("align_corners", C.c_int32), ("interpolation", C.c_uint32), ("channels", C.c_uint32),
         ("level_dim", C.c_uint32), ("table_fp16", C.c_int32), ("kernel_type", C.c_int32),
+        ("deterministic", C.c_int32),
     ]
 
 
@@ -146,6 +148,8 @@ def load() -> C.CDLL:
                                     C.POINTER(C.c_int64), C.c_int, vp]
     lib.ns_backward_scratch_bytes.restype = sz
     lib.ns_backward_scratch_bytes.argtypes = [i32]
+    lib.ns_backward_scratch_bytes_deterministic.restype = sz
+    lib.ns_backward_scratch_bytes_deterministic.argtypes = [i32, C.c_int64, i32]
     lib.ns_rasterize_backward.restype = C.c_int
     lib.ns_rasterize_backward.argtypes = [C.POINTER(RasterSettings), C.POINTER(Surfels), C.POINTER(GradsIn),
                                           C.POINTER(GradsOut), vp, sz, vp, sz, vp, sz, i64, vp, sz, vp]

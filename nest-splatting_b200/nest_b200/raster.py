@@ -45,7 +45,8 @@ class RasterConfig:
     channels: int = 32
     level_dim: int = 2
     table_fp16: bool = True
-    kernel_type: int = 0  # 0 Gaussian, 1 beta, 2 flex, 3 general (forward only)
+    kernel_type: int = 0  # 0 Gaussian, 1 beta, 2 flex, 3 general
+    deterministic: bool = False  # backward: fixed-point (bit-reproducible) table gradient
 
     def to_c(self) -> _lib.RasterSettings:
         s = _lib.RasterSettings()
@@ -58,6 +59,7 @@ class RasterConfig:
         s.projmatrix = self.projmatrix.data_ptr()
         s.beta = float(self.beta)
         s.kernel_type = int(self.kernel_type)
+        s.deterministic = int(bool(self.deterministic))
         s.if_contract = int(bool(self.if_contract))
         s.record_transmittance = int(bool(self.record_transmittance))
         s.max_intersections = int(self.max_intersections)
@@ -210,7 +212,9 @@ def rasterize_backward(cfg: RasterConfig, means3D, scales, rotations, opacities,
     go = _lib.GradsOut(ptr(g["means3D"]), ptr(g["means2D"]), ptr(g["opacity"]), ptr(g["scales"]),
                        ptr(g["rotations"]), ptr(g["table"]), rows, ptr(g["gradsum"]),
                        ptr(g["shapes"]) if "shapes" in g else None)
-    acc = torch.empty(lib.ns_backward_scratch_bytes(P), dtype=torch.uint8, device=dev)
+    nbytes = (lib.ns_backward_scratch_bytes_deterministic(P, rows, int(cfg.level_dim)) if cfg.deterministic
+              else lib.ns_backward_scratch_bytes(P))
+    acc = torch.empty(nbytes, dtype=torch.uint8, device=dev)
     check("ns_rasterize_backward",
           lib.ns_rasterize_backward(C.byref(settings), C.byref(surf), C.byref(gi), C.byref(go),
                                     scratch.geom.data_ptr(), scratch.geom.numel(), scratch.binning.data_ptr(),

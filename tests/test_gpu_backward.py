@@ -253,6 +253,36 @@ def test_backward_is_repeatable():
         assert rel_l2(a[k], b[k]) < 1e-4, k
 
 
+@pytest.mark.parametrize("fp16,table_range", [(True, 1e-4), (False, 1.0)])
+def test_backward_deterministic_table_gradient(fp16, table_range):
+    """settings.deterministic: the table gradient in 64-bit fixed point is
+    bit-identical across runs, within rounding of the float-atomic result and of
+    the oracle (every gradient checked)."""
+    sc = small_scene(seed=19, table_range=table_range)
+    inputs = api_inputs(sc)
+    gc, go = upstream(sc)
+    runs = [gpu_grads(sc, inputs, gc, go, fp16=fp16, deterministic=True)[0] for _ in range(3)]
+    for r in runs[1:]:
+        assert np.array_equal(r["table"].view(np.uint32), runs[0]["table"].view(np.uint32))
+    plain, _ = gpu_grads(sc, inputs, gc, go, fp16=fp16)
+    assert rel_l2(runs[0]["table"], plain["table"]) < 1e-6
+    kw = dict(interp=sc.grid.interpolation, align_corners=sc.grid.align_corners)
+    ref, _ = oracle_grads(sc, inputs, gc, go, **kw)
+    exact, _ = oracle_grads(sc, inputs, gc, go, f64=True, **kw)
+    check_all(runs[0], ref, exact)
+
+
+def test_backward_deterministic_zero_colour_gradient():
+    """A zero dL/dcolor gives an exactly zero table gradient (scale of a zero
+    maximum) while the other gradients still flow from the allmap channels."""
+    sc = small_scene(seed=19, table_range=1e-4)
+    inputs = api_inputs(sc)
+    gc, go = upstream(sc)
+    got, _ = gpu_grads(sc, inputs, torch.zeros_like(gc), go, deterministic=True)
+    assert not got["table"].any()
+    assert np.abs(got["opacity"]).sum() > 0
+
+
 def test_backward_empty_and_offscreen():
     sc = small_scene(n=64, seed=17)
     inputs = api_inputs(sc)
@@ -363,3 +393,42 @@ def test_dropin_autograd_shapes_gradient():
     keys = {k: SHAPE_KEYS[k] for k in ("means3D", "opacity", "shapes")}
     got = {"means3D": means.grad, "opacity": opac.grad, "shapes": shp.grad}
     check_all({k: v.detach().cpu().numpy().reshape(P, -1) for k, v in got.items()}, ref, exact, keys=keys)
+
+
+def test_dropin_deterministic_algorithms_flag():
+    """Under torch.use_deterministic_algorithms the drop-in Function asks for the
+    fixed-point table gradient: two backward passes give identical bits."""
+    sc = small_scene(seed=18, table_range=1e-4)
+    inputs = api_inputs(sc)
+    gc, go = upstream(sc, seed=9)
+    cam, g = sc.camera, sc.grid
+    dev = "cuda"
+    rs = dsr.GaussianRasterizationSettings(
+        image_height=cam.height, image_width=cam.width, tanfovx=cam.tanfovx, tanfovy=cam.tanfovy,
+        bg=torch.zeros(3, device=dev), scale_modifier=1.0, viewmatrix=cam.world_view_transform.to(dev),
+        projmatrix=cam.full_proj_transform.to(dev), sh_degree=0, campos=cam.camera_center.to(dev),
+        prefiltered=False, debug=False, beta=0.0, if_contract=False, record_transmittance=False,
+        max_intersections=0)
+    hs = dsr.HashGridSettings(L=g.levels, S=g.S, H=g.base_resolution, align_corners=g.align_corners,
+                              interpolation=g.interpolation,
+                              shape_dims=torch.tensor([0, g.channels, g.channels], dtype=torch.int32, device=dev))
+    r = dsr.GaussianRasterizer(rs, hs)
+    P = sc.P
+    grads = []
+    was = torch.are_deterministic_algorithms_enabled()
+    torch.use_deterministic_algorithms(True, warn_only=True)
+    try:
+        for _ in range(2):
+            table = g.table.to(dev).float().requires_grad_(True)
+            color, _, allmap, _, _ = r(
+                means3D=inputs["means3D"].to(dev), means2D=torch.zeros(P, 3, device=dev),
+                shs=torch.zeros(P, 1, 3, device=dev), opacities=inputs["opacities"].to(dev),
+                scales=inputs["scales"].to(dev), rotations=inputs["rotations"].to(dev),
+                homotrans=inputs["homotrans"].to(dev), ap_level=inputs["ap_level"].to(dev), features=table,
+                offsets=g.offsets.to(dev), gridrange=g.gridrange.to(dev), render_mode=0)
+            ((color * gc.to(dev)).sum() + (allmap * go.to(dev)).sum()).backward()
+            grads.append(table.grad.detach().cpu().numpy())
+    finally:
+        torch.use_deterministic_algorithms(was)
+    assert np.abs(grads[0]).sum() > 0
+    assert np.array_equal(grads[0].view(np.uint32), grads[1].view(np.uint32))

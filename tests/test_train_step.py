@@ -66,7 +66,7 @@ def test_train_step_gradients_match_oracle():
         t.grad = None
     loss, rgb, allmap = train.forward(state, rast, cam, keep_upstream=True)
     loss.backward()
-    assert np.isfinite(float(loss))
+    assert np.isfinite(float(loss.detach()))
     for t in state.leaves():
         assert t.grad is not None and torch.isfinite(t.grad).all()
 
