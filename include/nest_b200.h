@@ -101,6 +101,17 @@ typedef struct ns_raster_settings {
    * run to run; needs ns_backward_scratch_bytes_deterministic. 0: float atomics,
    * whose summation order varies, as in the reference. */
   int32_t deterministic;
+  /* Render mode (forward.cu:1126-1824; base | inference flag << 8): 0 baseline
+   * hash grid; 4 cat: per-surfel features (hybrid_levels levels) then the hash
+   * grid's `levels` levels; 12 adaptive_cat and 14 adaptive_zero: per-surfel
+   * features blended with the hash levels by a per-surfel weight (flag 256:
+   * inference rules). hybrid_levels / total_levels: the reference's level
+   * encoding (total << 16 | active << 8 | hybrid) split out; `levels` is the
+   * number of hash levels queried. Forward only: ns_rasterize_backward and
+   * ns_render_frame take mode 0. */
+  int32_t render_mode;
+  uint32_t hybrid_levels;
+  uint32_t total_levels;
 } ns_raster_settings;
 
 /* Per-surfel inputs of the rasterizer (render_mode 0). */
@@ -116,6 +127,10 @@ typedef struct ns_surfels {
   const int32_t* offsets; /* [L+1] int32 level offsets (rows) */
   const float* gridrange; /* [2] = (vmin, vmax) */
   const float* shapes;    /* [P] per-surfel kernel parameter for kernel_type 1-3, else NULL */
+  const float* colors_precomp; /* render_mode 4 / 12 / 14: per-surfel feature rows (the
+                                  reference's colors_precomp): mode 4 [P, hybrid LD],
+                                  12 [P, total LD + 1], 14 [P, hybrid LD + 1] (blend
+                                  weight last); else NULL */
 } ns_surfels;
 
 /* Outputs (caller-owned, device). cover_pixels / trans_avg may be NULL when

@@ -180,10 +180,19 @@ int validate_settings(const ns_raster_settings* s) {
   if (!s) return NS_ERR_INVALID;
   if (s->image_width <= 0 || s->image_height <= 0) return NS_ERR_INVALID;
   if (!s->viewmatrix || !s->projmatrix) return NS_ERR_INVALID;
-  if (s->levels == 0) return NS_ERR_UNSUPPORTED;  // level == 0 (per-surfel colours) not built
+  // level == 0 (per-surfel colours) is not built; the modes may query no hash level
+  if (s->levels == 0 && s->render_mode == 0) return NS_ERR_UNSUPPORTED;
   if (s->level_dim == 0 || s->channels == 0) return NS_ERR_INVALID;
   if (s->levels * s->level_dim > s->channels) return NS_ERR_INVALID;
   if (s->kernel_type < 0 || s->kernel_type > 3) return NS_ERR_UNSUPPORTED;
+  const int base = s->render_mode & 0xFF, flag = s->render_mode >> 8;
+  if (base != 0 && base != 4 && base != 12 && base != 14) return NS_ERR_UNSUPPORTED;
+  if (flag > 1 || (flag && base != 12 && base != 14)) return NS_ERR_UNSUPPORTED;
+  if (base != 0) {
+    if (s->hybrid_levels > 16 || s->total_levels > 16) return NS_ERR_INVALID;
+    if ((s->hybrid_levels + s->levels) * s->level_dim > s->channels) return NS_ERR_INVALID;
+    if (base == 12 && s->total_levels * s->level_dim > s->channels) return NS_ERR_INVALID;
+  }
   return NS_OK;
 }
 
@@ -191,7 +200,7 @@ int validate_settings(const ns_raster_settings* s) {
 int bin_and_render(const ns_raster_settings* st, int P, const GeomState& g, const ImageState& im,
                    void* binning, size_t binning_bytes, const void* features,
                    const int32_t* offsets, const float* gridrange, float* out_color,
-                   float* out_others, float* cover_pixels, float* trans_avg,
+                   float* out_others, float* cover_pixels, float* trans_avg, const float* gauss,
                    int64_t* num_rendered, int flags, cudaStream_t stream,
                    void* const* ev = nullptr) {
   const int W = st->image_width, H = st->image_height;
@@ -240,6 +249,10 @@ int bin_and_render(const ns_raster_settings* st, int P, const GeomState& g, cons
   rp.contract = st->if_contract;
   rp.beta = st->beta;
   rp.kernel_type = st->kernel_type;
+  rp.render_mode = st->render_mode;
+  rp.hybrid_levels = (int)st->hybrid_levels;
+  rp.total_levels = (int)st->total_levels;
+  rp.gauss = gauss;
   rp.max_intersections = st->max_intersections;
   rp.record_transmittance = st->record_transmittance;
   rp.ranges = im.ranges;
@@ -312,6 +325,7 @@ int ns_rasterize_forward(const ns_raster_settings* settings, const ns_surfels* s
     return NS_ERR_INVALID;
   if (!outputs->out_color || !outputs->out_others || !outputs->radii) return NS_ERR_INVALID;
   if (settings->kernel_type != 0 && P > 0 && !surfels->shapes) return NS_ERR_INVALID;
+  if (settings->render_mode != 0 && P > 0 && !surfels->colors_precomp) return NS_ERR_INVALID;
   if (settings->record_transmittance && (!outputs->cover_pixels || !outputs->trans_avg))
     return NS_ERR_INVALID;
   if (settings->level_dim != 2) return NS_ERR_UNSUPPORTED;
@@ -330,7 +344,7 @@ int ns_rasterize_forward(const ns_raster_settings* settings, const ns_surfels* s
   return bin_and_render(settings, P, g, im, binning, binning_bytes, surfels->features,
                         surfels->offsets, surfels->gridrange, outputs->out_color,
                         outputs->out_others, outputs->cover_pixels, outputs->trans_avg,
-                        num_rendered, flags, stream);
+                        surfels->colors_precomp, num_rendered, flags, stream);
 }
 
 size_t ns_backward_scratch_bytes(int32_t P) { return align_up(backward_accum_bytes(P)); }
@@ -350,6 +364,7 @@ int ns_rasterize_backward(const ns_raster_settings* settings, const ns_surfels* 
   cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_);
   int rc = validate_settings(settings);
   if (rc) return rc;
+  if (settings->render_mode != 0) return NS_ERR_UNSUPPORTED;  // forward only
   if (!surfels || !gi || !go) return NS_ERR_INVALID;
   const int P = surfels->P;
   if (P < 0 || num_rendered < 0) return NS_ERR_INVALID;
@@ -545,7 +560,7 @@ int ns_render_frame(const ns_raster_settings* settings, const ns_frame_inputs* i
                     int64_t* num_rendered, int flags, void* stream_) {
   cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_);
   int rc = validate_settings(settings);
-  if (settings && settings->kernel_type != 0) return NS_ERR_UNSUPPORTED;
+  if (settings && (settings->kernel_type != 0 || settings->render_mode != 0)) return NS_ERR_UNSUPPORTED;
   if (rc) return rc;
   if (!in || !out) return NS_ERR_INVALID;
   const int P = in->P;
@@ -583,7 +598,7 @@ int ns_render_frame(const ns_raster_settings* settings, const ns_frame_inputs* i
   if (ev) NS_CUDA_TRY(cudaEventRecord((cudaEvent_t)ev[3], stream));
   if (ev) NS_CUDA_TRY(cudaEventRecord((cudaEvent_t)ev[4], stream));
   rc = bin_and_render(settings, P, g, im, binning, binning_bytes, in->features, in->offsets,
-                      in->gridrange, out->out_color, out->out_others, nullptr, nullptr,
+                      in->gridrange, out->out_color, out->out_others, nullptr, nullptr, nullptr,
                       num_rendered, flags & ~NS_FLAG_SKIP_DECODE, stream, ev);
   if (rc) return rc;
   const size_t HW = (size_t)W * H;

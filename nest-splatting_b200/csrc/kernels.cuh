@@ -16,6 +16,13 @@ struct RenderParams {
   int contract;
   float beta;
   int kernel_type;  // 0 Gaussian, 1 beta, 2 flex, 3 general (record word q7.w = shape)
+  // Render modes 4 / 12 / 14 (render_mode = base | inference flag << 8): the
+  // per-surfel features `gauss` (colors_precomp rows) fill channels from 0 and
+  // the L hash levels land at level hybrid_levels (channel hybrid_levels * LD).
+  int render_mode;
+  int hybrid_levels;
+  int total_levels;
+  const float* gauss;
   uint32_t max_intersections;
   int record_transmittance;
   const uint2* ranges;

@@ -105,9 +105,56 @@ __device__ __forceinline__ float2 lookup_finish(const float (&f)[3], const Corne
   return r;
 }
 
-// kAnyKernel: built with the splat kernels 1-3 (p.kernel_type); the Gaussian-only
-// instantiation keeps the hot loop free of them.
-template <typename TableT, bool kAnyKernel>
+// Render modes 4 / 12 / 14 (forward.cu:1218-1282, 1593-1790): adds this
+// sample's per-surfel features, weighted by w, to the pixel's accumulators and
+// returns the factor of the hash features (0: the mode does not query the grid).
+// Mode 4 (cat): features [0, hybrid LD), hash levels after them. Mode 12
+// (adaptive_cat, rows of total LD + 1 with the blend weight last): coarse
+// channels from the surfel, fine channels wgt * surfel + (1 - wgt) * hash; with
+// the inference flag all channels from the surfel when wgt >= 0.9, else coarse
+// from the surfel and fine from the grid. Mode 14 (adaptive_zero, rows of
+// hybrid LD + 1): coarse from the surfel, fine wgt * hash (training: wgt > 1e-6;
+// inference: wgt >= 0.1, else zeros).
+__device__ __forceinline__ float mode_features(const RenderParams& p, uint32_t id, float w, float* acc,
+                                               int t) {
+  const int base = p.render_mode & 0xFF;
+  const bool infer = ((p.render_mode >> 8) & 1) != 0;
+  const int pg = 2 * p.hybrid_levels, hd = 2 * (int)p.L;
+  auto add = [&](const float* g, int c0, int c1, float scale) {
+    for (int c = c0; c < c1 && c < p.C; c += 2) {
+      float2* a = acc_pair(acc, t, c >> 1);
+      a->x += __ldg(g + c) * scale;
+      if (c + 1 < p.C) a->y += __ldg(g + c + 1) * scale;
+    }
+  };
+  if (base == 4) {
+    add(p.gauss + (size_t)id * pg, 0, pg, w);
+    return p.L > 0 ? 1.0f : 0.0f;
+  }
+  if (base == 12) {
+    const int td = 2 * p.total_levels;
+    const float* g = p.gauss + (size_t)id * (td + 1);
+    const float wgt = __ldg(g + td);
+    if (infer && wgt >= 0.9f) {
+      add(g, 0, td, w);
+      return 0.0f;
+    }
+    add(g, 0, pg, w);
+    if (p.L == 0) return 0.0f;
+    if (infer) return 1.0f;
+    add(g, pg, pg + hd, wgt * w);
+    return 1.0f - wgt;
+  }
+  const float* g = p.gauss + (size_t)id * (pg + 1);  // base == 14
+  const float wgt = __ldg(g + pg);
+  add(g, 0, pg, w);
+  return (p.L > 0 && (infer ? wgt >= 0.1f : wgt > 1e-6f)) ? wgt : 0.0f;
+}
+
+// kGeneral: built with the splat kernels 1-3 (p.kernel_type) and the render
+// modes 4 / 12 / 14 (p.render_mode); the Gaussian mode-0 instantiation keeps the
+// hot loop free of them.
+template <typename TableT, bool kGeneral>
 __global__ void __launch_bounds__(kThreads, 2) blend_kernel(const RenderParams p) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   BlendSmem& S = *reinterpret_cast<BlendSmem*>(smem_raw);
@@ -136,6 +183,7 @@ __global__ void __launch_bounds__(kThreads, 2) blend_kernel(const RenderParams p
   const int total = (int)(range.y - range.x);
   const int rounds = div_up(total, kBatch);
   const float vmin = p.gridrange[0], vmax = p.gridrange[1];
+  const int hoff = (kGeneral && p.render_mode != 0) ? p.hybrid_levels : 0;  // level of hash level 0
 
   float T = 1.0f;
   uint32_t contributor = 0, last_contributor = 0, render_number = 0;
@@ -197,8 +245,8 @@ __global__ void __launch_bounds__(kThreads, 2) blend_kernel(const RenderParams p
       const bool has1 = l + 1 < L;
       const LevelConst lc0 = S.lv[l];
       const LevelConst lc1 = S.lv[has1 ? l + 1 : l];
-      float2* ap0 = acc_pair(S.acc, t, l);
-      float2* ap1 = acc_pair(S.acc, t, has1 ? l + 1 : l);
+      float2* ap0 = acc_pair(S.acc, t, hoff + l);
+      float2* ap1 = acc_pair(S.acc, t, hoff + (has1 ? l + 1 : l));
       float2 c0 = *ap0;
       float2 c1 = has1 ? *ap1 : make_float2(0.f, 0.f);
       int nk = 0;
@@ -303,7 +351,7 @@ __global__ void __launch_bounds__(kThreads, 2) blend_kernel(const RenderParams p
           const float depth = on_plane ? (sx * Tw.x + sy * Tw.y) + Tw.z : Tw.z;
           if (depth < kNear) continue;
           float G;
-          if (!kAnyKernel || p.kernel_type == 0) {
+          if (!kGeneral || p.kernel_type == 0) {
             const float power = -0.5f * rho;
             if (power > 0.0f) continue;
             G = expf(power);
@@ -386,8 +434,11 @@ __global__ void __launch_bounds__(kThreads, 2) blend_kernel(const RenderParams p
             in1 = (st * in1 + 2.0f) * 0.25f;
             in2 = (st * in2 + 2.0f) * 0.25f;
           }
-          S.samp[cnt][t] = make_float4(in0, in1, in2, w);
-          S.lvl[cnt][t] = (uint8_t)(oob ? 0u : min(apl, L));
+          float hw = w;  // weight of this sample's hash features
+          if (kGeneral && p.render_mode != 0)
+            hw = w * mode_features(p, __float_as_uint(q6.z), w, S.acc, t);
+          S.samp[cnt][t] = make_float4(in0, in1, in2, hw);
+          S.lvl[cnt][t] = (uint8_t)((oob || hw == 0.0f) ? 0u : min(apl, L));
           cnt++;
 
           float ac0, ac1;
@@ -466,13 +517,13 @@ __global__ void __launch_bounds__(kThreads, 2) blend_kernel(const RenderParams p
   }
 }
 
-template <typename TableT, bool kAnyKernel>
+template <typename TableT, bool kGeneral>
 int launch_blend(const RenderParams& p, int tiles, cudaStream_t stream) {
   const int smem = (int)sizeof(BlendSmem);
-  NS_CUDA_TRY(cudaFuncSetAttribute(blend_kernel<TableT, kAnyKernel>,
+  NS_CUDA_TRY(cudaFuncSetAttribute(blend_kernel<TableT, kGeneral>,
                                    cudaFuncAttributeMaxDynamicSharedMemorySize,
                                    smem));
-  blend_kernel<TableT, kAnyKernel><<<tiles, kThreads, smem, stream>>>(p);
+  blend_kernel<TableT, kGeneral><<<tiles, kThreads, smem, stream>>>(p);
   NS_LAUNCH_CHECK();
   return NS_OK;
 }
@@ -484,10 +535,12 @@ int launch_blend(const RenderParams& p, int tiles, cudaStream_t stream) {
 // renders nothing for shapes it was not compiled for).
 int render_launch(const RenderParams& p, int fp16, cudaStream_t stream) {
   if (p.LD != 2 || p.C > kMaxChannels || p.C <= 0) return NS_ERR_UNSUPPORTED;
-  if (p.L > (uint32_t)(p.C / p.LD) || p.L > (uint32_t)kMaxLevels) return NS_ERR_UNSUPPORTED;
+  const int hoff = p.render_mode != 0 ? p.hybrid_levels : 0;
+  if (hoff < 0 || (int64_t)hoff + p.L > (uint32_t)(p.C / p.LD) || p.L > (uint32_t)kMaxLevels)
+    return NS_ERR_UNSUPPORTED;
   const int tiles = div_up(p.W, kTile) * div_up(p.H, kTile);
   if (tiles == 0) return NS_OK;
-  if (p.kernel_type != 0)
+  if (p.kernel_type != 0 || p.render_mode != 0)
     return fp16 ? launch_blend<__half, true>(p, tiles, stream) : launch_blend<float, true>(p, tiles, stream);
   return fp16 ? launch_blend<__half, false>(p, tiles, stream) : launch_blend<float, false>(p, tiles, stream);
 }

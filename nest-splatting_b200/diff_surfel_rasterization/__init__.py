@@ -9,9 +9,13 @@ and backward passes run the sm_100a kernels of libnest_b200.so through its
 C-ABI; there is no CPU fallback. Built: render_mode 0 (baseline hash grid),
 level_dim 2, the Gaussian splat kernel (kernel_type 0) and the beta / flex /
 general kernels (kernel_type 1-3, per-surfel `shapes`, whose gradient comes back
-in shapes' slot), forward and backward. Other modes raise NotImplementedError
-instead of silently rendering nothing as the reference does for shapes it was
-not compiled for.
+in shapes' slot), forward and backward; render modes 4 (cat), 12 (adaptive_cat)
+and 14 (adaptive_zero, both with the inference flag 256) forward, the per-surfel
+features read from colors_precomp and the level word hashgrid_settings.L =
+total << 16 | active << 8 | hybrid as the reference's renderer encodes it
+(gaussian_renderer/__init__.py:216-241, 334-447). Other modes raise
+NotImplementedError instead of silently rendering nothing as the reference does
+for shapes it was not compiled for.
 
 Backward (__init__.py:174-275 of the reference): the 21 gradients come back in
 argument order; means2D's slot carries the densification statistic and
@@ -73,8 +77,11 @@ class _RasterizeGaussians(torch.autograd.Function):
     def forward(ctx, means3D, means2D, sh, colors_precomp, opacities, scales, rotations, cov3Ds_precomp,
                 homotrans, ap_level, features, offsets, gridrange, features_diffuse, offsets_diffuse,
                 gridrange_diffuse, raster_settings, hashgrid_settings, render_mode, shapes, kernel_type):
-        if int(render_mode) != 0:
-            raise NotImplementedError(f"render_mode {render_mode}: only 0 (baseline hash grid) is built")
+        mode = int(render_mode)
+        base_mode = mode & 0xFF
+        if base_mode not in (0, 4, 12, 14) or (mode >> 8) > 1 or ((mode >> 8) and base_mode == 4):
+            raise NotImplementedError(f"render_mode {render_mode}: 0 (baseline hash grid), 4 (cat), "
+                                      f"12 (adaptive_cat), 14 (adaptive_zero) are built")
         if int(kernel_type) not in (0, 1, 2, 3):
             raise NotImplementedError(f"kernel_type {kernel_type}: 0-3 are built")
         shp = _nonempty(shapes)
@@ -91,6 +98,22 @@ class _RasterizeGaussians(torch.autograd.Function):
         L = int(hashgrid_settings.L)
         if L <= 0 or _nonempty(features) is None:
             raise NotImplementedError("level == 0 (per-surfel colours) is not built")
+        hybrid = total = 0
+        gauss = None
+        if base_mode != 0:
+            # The reference's level word: total << 16 | active hash levels << 8 | hybrid.
+            total, active, hybrid = (L >> 16) & 0xFF, (L >> 8) & 0xFF, L & 0xFF
+            if base_mode == 4:
+                # Mode 4 queries every level of the (fine-levels-only) table: the last
+                # offset that grows (forward.cu:1236-1242).
+                offs = offsets.detach().to("cpu", torch.int64).reshape(-1).tolist()
+                L = max([i for i in range(1, min(len(offs), 17)) if offs[i] > offs[i - 1]], default=0)
+            else:
+                L = active
+            gauss = _nonempty(colors_precomp)
+            if gauss is None:
+                raise RuntimeError(f"render_mode {mode} needs colors_precomp (per-surfel features)")
+            gauss = gauss.detach().contiguous().float()
         _, _, OS = _shape_dims(hashgrid_settings)
         feats = features.contiguous()
         if feats.dtype not in (torch.float16, torch.float32):
@@ -108,15 +131,16 @@ class _RasterizeGaussians(torch.autograd.Function):
             base_resolution=int(hashgrid_settings.H), align_corners=bool(hashgrid_settings.align_corners),
             interpolation=int(hashgrid_settings.interpolation), channels=int(OS),
             level_dim=int(feats.shape[1]), table_fp16=feats.dtype == torch.float16,
-            kernel_type=int(kernel_type), deterministic=torch.are_deterministic_algorithms_enabled())
+            kernel_type=int(kernel_type), deterministic=torch.are_deterministic_algorithms_enabled(),
+            render_mode=mode, hybrid_levels=hybrid, total_levels=total)
         ap = _nonempty(ap_level)
         args = (means3D.detach().contiguous().float(), scales.detach().contiguous().float(),
                 rotations.detach().contiguous().float(), opacities.detach().contiguous().float().reshape(-1),
                 None if _nonempty(homotrans) is None else homotrans.detach().contiguous().float().reshape(-1, 16),
                 None if ap is None else ap.detach().contiguous().float().reshape(-1), feats.detach(),
                 offsets.contiguous().to(torch.int32), gridrange.contiguous().float())
-        num_rendered, color, others, radii, cover, trans, scratch = _raster.rasterize_forward(cfg, *args,
-                                                                                              shapes=shp)
+        num_rendered, color, others, radii, cover, trans, scratch = _raster.rasterize_forward(
+            cfg, *args, shapes=shp, colors_precomp=gauss)
         ctx.cfg = cfg
         ctx.args = args
         ctx.radii = radii
@@ -131,6 +155,8 @@ class _RasterizeGaussians(torch.autograd.Function):
 
     @staticmethod
     def backward(ctx, grad_out_color, grad_radii, grad_depth, grad_0, grad_1):
+        if ctx.cfg.render_mode != 0:
+            raise NotImplementedError(f"backward of render_mode {ctx.cfg.render_mode}: only mode 0 is built")
         dev = ctx.radii.device
         H, W = ctx.cfg.image_height, ctx.cfg.image_width
         if grad_out_color is None:

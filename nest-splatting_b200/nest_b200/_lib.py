@@ -40,7 +40,8 @@ class RasterSettings(C.Structure):
         ("levels", C.c_uint32), ("level_scale_log2", C.c_float), ("base_resolution", C.c_uint32),
         ("align_corners", C.c_int32), ("interpolation", C.c_uint32), ("channels", C.c_uint32),
         ("level_dim", C.c_uint32), ("table_fp16", C.c_int32), ("kernel_type", C.c_int32),
-        ("deterministic", C.c_int32),
+        ("deterministic", C.c_int32), ("render_mode", C.c_int32), ("hybrid_levels", C.c_uint32),
+        ("total_levels", C.c_uint32),
     ]
 
 
@@ -49,7 +50,7 @@ class Surfels(C.Structure):
         ("P", C.c_int32), ("means3D", C.c_void_p), ("scales", C.c_void_p),
         ("rotations", C.c_void_p), ("opacities", C.c_void_p), ("homotrans", C.c_void_p),
         ("ap_level", C.c_void_p), ("features", C.c_void_p), ("offsets", C.c_void_p),
-        ("gridrange", C.c_void_p), ("shapes", C.c_void_p),
+        ("gridrange", C.c_void_p), ("shapes", C.c_void_p), ("colors_precomp", C.c_void_p),
     ]
 
 

@@ -47,6 +47,9 @@ class RasterConfig:
     table_fp16: bool = True
     kernel_type: int = 0  # 0 Gaussian, 1 beta, 2 flex, 3 general
     deterministic: bool = False  # backward: fixed-point (bit-reproducible) table gradient
+    render_mode: int = 0     # 0 baseline; 4 cat, 12 adaptive_cat, 14 adaptive_zero (| 256 inference)
+    hybrid_levels: int = 0   # per-surfel feature levels of modes 4 / 12 / 14
+    total_levels: int = 0    # all levels (mode 12 rows hold total_levels * level_dim + 1)
 
     def to_c(self) -> _lib.RasterSettings:
         s = _lib.RasterSettings()
@@ -60,6 +63,9 @@ class RasterConfig:
         s.beta = float(self.beta)
         s.kernel_type = int(self.kernel_type)
         s.deterministic = int(bool(self.deterministic))
+        s.render_mode = int(self.render_mode)
+        s.hybrid_levels = int(self.hybrid_levels)
+        s.total_levels = int(self.total_levels)
         s.if_contract = int(bool(self.if_contract))
         s.record_transmittance = int(bool(self.record_transmittance))
         s.max_intersections = int(self.max_intersections)
@@ -111,8 +117,9 @@ class Scratch:
 
 def rasterize_forward(cfg: RasterConfig, means3D, scales, rotations, opacities, homotrans, ap_level,
                       features, offsets, gridrange, scratch: Scratch | None = None,
-                      capacity_hint: int | None = None, shapes=None):
-    """Forward rasterization (render_mode 0) through ns_rasterize_forward.
+                      capacity_hint: int | None = None, shapes=None, colors_precomp=None):
+    """Forward rasterization through ns_rasterize_forward. Render modes 4 / 12 /
+    14 read the per-surfel feature rows `colors_precomp` (contiguous fp32).
 
     Returns (num_rendered, out_color [C,H,W], out_others [14,H,W], radii [P] int32,
     cover_pixels [P,1], trans_avg [P,1], scratch).
@@ -140,6 +147,11 @@ def rasterize_forward(cfg: RasterConfig, means3D, scales, rotations, opacities, 
     surf.opacities, surf.homotrans, surf.ap_level = ptr(opacities), ptr(homotrans), ptr(ap_level)
     surf.features, surf.offsets, surf.gridrange = ptr(features), ptr(offsets), ptr(gridrange)
     surf.shapes = ptr(shapes)
+    if cfg.render_mode != 0:
+        if colors_precomp is None:
+            raise ValueError(f"render_mode {cfg.render_mode} needs colors_precomp")
+        _require_cuda(colors_precomp)
+        surf.colors_precomp = ptr(colors_precomp)
     outs = _lib.RasterOutputs()
     outs.out_color, outs.out_others, outs.radii = ptr(out_color), ptr(out_others), ptr(radii)
     outs.cover_pixels = ptr(cover) if rec_P else None

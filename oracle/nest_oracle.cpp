@@ -18,6 +18,49 @@
 
 using namespace oracle;
 
+// The feature vector of one blended sample in render modes 4, 12, 14: the
+// per-surfel features of `gauss` (row id) and, where the mode asks for it, the
+// L hash levels queried at the hit point (query() fills hf[0, L * LD)).
+template <class Q>
+void mode_feature(float* feat, int C, int LD, int render_mode, int hybrid_levels, int total_levels,
+                  uint32_t L, const float* gauss, int id, float* hf, Q query) {
+  const int base = render_mode & 0xFF;
+  const bool infer = ((render_mode >> 8) & 1) != 0;
+  const int pg = hybrid_levels * LD;
+  const int hd = (int)L * LD;
+  for (int c = 0; c < C; c++) feat[c] = 0.0f;
+  if (base == 4) {  // :1218-1282
+    const float* g = gauss + (size_t)id * pg;
+    for (int i = 0; i < pg; i++) feat[i] = g[i];
+    if (L > 0) {
+      query();
+      for (int i = 0; i < hd && pg + i < C; i++) feat[pg + i] = hf[i];
+    }
+  } else if (base == 12) {  // :1593-1700
+    const int td = total_levels * LD;
+    const float* g = gauss + (size_t)id * (td + 1);
+    const float wgt = g[td];
+    if (infer && wgt >= 0.9f) {
+      for (int i = 0; i < td && i < C; i++) feat[i] = g[i];
+    } else {
+      for (int i = 0; i < pg; i++) feat[i] = g[i];
+      if (L > 0) {
+        query();
+        for (int i = 0; i < hd && pg + i < C; i++)
+          feat[pg + i] = infer ? hf[i] : wgt * g[pg + i] + (1.0f - wgt) * hf[i];
+      }
+    }
+  } else if (base == 14) {  // :1701-1790
+    const float* g = gauss + (size_t)id * (pg + 1);
+    const float wgt = g[pg];
+    for (int i = 0; i < pg && i < C; i++) feat[i] = g[i];
+    if (L > 0 && (infer ? wgt >= 0.1f : wgt > 1e-6f)) {
+      query();
+      for (int i = 0; i < hd && pg + i < C; i++) feat[pg + i] = wgt * hf[i];
+    }
+  }
+}
+
 extern "C" {
 
 // forward.cu:237-290 (compute_transmat), 294-320 (compute_aabb), 323-441
@@ -148,6 +191,10 @@ int64_t oracle_bin(int P, const float* means2D, const float* depths, const int* 
 // level visualisation colour (:1945-1957), transmittance record (:1961-1964),
 // outputs (:2008-2048). homotrans is [P,16] row-major (general_utils.py:101-113).
 // table is fp32 [sum_l T_l, LD]; offsets int32 [L+1].
+// render_mode (base | inference flag << 8): 0, or the modes that combine
+// per-surfel features `gauss` (colors_precomp) with the hash grid's L levels at
+// channel hybrid_levels * LD: 4 cat (:1218-1282), 12 adaptive_cat (:1593-1700),
+// 14 adaptive_zero (:1701-1790); see mode_feature().
 void oracle_render(int W, int H, const uint32_t* ranges, const uint32_t* point_list,
                    const float* means2D, const float* transMat, const float* normal_opacity,
                    const float* homotrans, const float* ap_level, const float* table,
@@ -156,13 +203,14 @@ void oracle_render(int W, int H, const uint32_t* ranges, const uint32_t* point_l
                    float beta, uint32_t max_intersections, int record_transmittance,
                    float* out_color, float* out_others, float* final_T, uint32_t* n_contrib,
                    float* cover_pixels, float* trans_avg, int row_stride, int kernel_type,
-                   const float* shapes) {
+                   const float* shapes, int render_mode, int hybrid_levels, int total_levels,
+                   const float* gauss) {
   const int gx = (W + kBlock - 1) / kBlock, gy = (H + kBlock - 1) / kBlock;
   const size_t HW = (size_t)H * W;
   const float vmin = gridrange[0], vmax = gridrange[1];
 #pragma omp parallel for schedule(dynamic, 1)
   for (int tile = 0; tile < gx * gy; tile++) {
-    std::vector<float> Cacc(C), feat(C > 0 ? C : 1);
+    std::vector<float> Cacc(C), feat(C > 0 ? C : 1), hf(16 * LD);
     const int tx = tile % gx, ty = tile / gx;
     if (row_stride > 1 && ty % row_stride != 0) continue;
     const uint32_t r0 = ranges[2 * tile], r1 = ranges[2 * tile + 1];
@@ -243,8 +291,17 @@ void oracle_render(int W, int H, const uint32_t* ranges, const uint32_t* point_l
           pos[1] += w * xyz.y;
           pos[2] += w * xyz.z;
           uint32_t apl = (uint32_t)std::floor(ap_level[id]);
-          query_feature(feat.data(), C, LD, xyz, vmin, vmax, offsets, apl, table, L, S, Hres,
-                        align_corners != 0, interp, contract != 0);
+          if ((render_mode & 0xFF) == 0) {
+            query_feature(feat.data(), C, LD, xyz, vmin, vmax, offsets, apl, table, L, S, Hres,
+                          align_corners != 0, interp, contract != 0);
+          } else {
+            auto query = [&]() {
+              query_feature(hf.data(), (int)L * LD, LD, xyz, vmin, vmax, offsets, apl, table, L, S,
+                            Hres, align_corners != 0, interp, contract != 0);
+            };
+            mode_feature(feat.data(), C, LD, render_mode, hybrid_levels, total_levels, L, gauss, id,
+                         hf.data(), query);
+          }
           for (int c = 0; c < C; c++) Cacc[c] += feat[c] * w;
           float apc[3] = {0, 0, 0};
           if (apl <= 4) { apc[0] = (float)((apl - 2) * 0.5); apc[1] = 1.0f; }

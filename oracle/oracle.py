@@ -52,7 +52,8 @@ def load() -> C.CDLL:
     lib.oracle_bin.restype = i64
     lib.oracle_bin.argtypes = [i32, vp, vp, vp, i32, i32, vp, vp, i64, vp]
     lib.oracle_render.argtypes = [i32, i32, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, i32, i32, u32, f32, u32,
-                                  i32, u32, i32, f32, u32, i32, vp, vp, vp, vp, vp, vp, i32, i32, vp]
+                                  i32, u32, i32, f32, u32, i32, vp, vp, vp, vp, vp, vp, i32, i32, vp,
+                                  i32, i32, i32, vp]
     lib.oracle_query.argtypes = [i32, vp, vp, vp, vp, f32, f32, i32, i32, u32, f32, u32, i32, u32, i32, vp]
     lib.oracle_grid_index.restype = u32
     lib.oracle_grid_index.argtypes = [i32, u32, u32, u32, u32, u32]
@@ -110,9 +111,13 @@ def bin_surfels(pre, W, H):
 
 def render(pre, vals, ranges, homotrans, ap_level, table_f32, offsets, gridrange, W, H, C_out, LD, L, S, Hres,
            align_corners=False, interp=0, contract=False, beta=0.0, max_intersections=0,
-           record_transmittance=False, row_stride=1, kernel_type=0, shapes=None):
-    """renderCUDAsurfelForward<C> mode 0 restated. Returns dict of output images.
+           record_transmittance=False, row_stride=1, kernel_type=0, shapes=None, render_mode=0,
+           hybrid_levels=0, total_levels=0, gauss=None):
+    """renderCUDAsurfelForward<C> restated. Returns dict of output images.
     kernel_type 1-3 (beta / flex / general splat kernels) read shapes [P].
+    render_mode 4 / 12 / 14 (| 256 for the inference flag) combine per-surfel
+    features `gauss` (colors_precomp rows) with the L hash levels at channel
+    hybrid_levels * LD.
 
     row_stride > 1 renders only tile rows ty with ty % row_stride == 0 (a bounded
     sample for CPU timing); other pixels stay zero."""
@@ -134,7 +139,8 @@ def render(pre, vals, ranges, homotrans, ap_level, table_f32, offsets, gridrange
                       int(bool(contract)), float(beta), int(max_intersections), int(bool(record_transmittance)),
                       _p(out["out_color"]), _p(out["out_others"]), _p(out["final_T"]), _p(out["n_contrib"]),
                       _p(out["cover_pixels"]), _p(out["trans_avg"]), int(row_stride), int(kernel_type),
-                      _p(_f32(shapes).reshape(-1)) if shapes is not None else None)
+                      _p(_f32(shapes).reshape(-1)) if shapes is not None else None, int(render_mode),
+                      int(hybrid_levels), int(total_levels), _p(_f32(gauss).reshape(-1)) if gauss is not None else None)
     assert HW == W * H
     return out
 

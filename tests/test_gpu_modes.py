@@ -1,0 +1,134 @@
+"""GPU parity of the render modes that combine per-surfel features with the hash
+grid (forward.cu:1218-1282 mode 4 cat, :1593-1700 mode 12 adaptive_cat,
+:1701-1790 mode 14 adaptive_zero; the inference flag 256 of 12 and 14) through
+the drop-in module, against the oracle's restatement (oracle/nest_oracle.cpp
+mode_feature). The level word and the feature rows are built as the
+reference's renderer builds them (gaussian_renderer/__init__.py:216-241,
+334-447): hashgrid_settings.L = total << 16 | active << 8 | hybrid,
+colors_precomp = per-surfel features (+ the blend weight for 12 / 14), offsets
+padded to 17 entries for mode 4."""
+import numpy as np
+import pytest
+import torch
+
+import diff_surfel_rasterization as dsr
+from helpers import api_inputs, small_scene
+from nest_b200 import synth
+from oracle import oracle
+from test_gpu_raster import compare
+
+pytestmark = pytest.mark.gpu
+
+
+def mode_case(mode, total, hybrid, active, seed, weights="uniform"):
+    sc = small_scene(n=1500, seed=seed)
+    inp = api_inputs(sc)
+    g = torch.Generator().manual_seed(seed)
+    LD = 2
+    grid = synth.hash_grid(g, levels=max(active, 1), log2_T=13, lo=-1.0, hi=1.0, base_resolution=64,
+                           per_level_scale=1.5)
+    P = sc.P
+    base = mode & 0xFF
+    if base == 4:
+        gauss = torch.rand(P, hybrid * LD, generator=g) * 2 - 1
+    else:
+        width = total * LD if base == 12 else hybrid * LD
+        feats = torch.rand(P, width, generator=g) * 2 - 1
+        if weights == "uniform":
+            wgt = torch.rand(P, 1, generator=g)
+        else:  # thresholds of the inference rules and exact zeros / ones
+            wgt = torch.tensor([0.0, 1e-7, 0.05, 0.1, 0.5, 0.89, 0.9, 0.95, 1.0])[
+                torch.randint(0, 9, (P, 1), generator=g)]
+        gauss = torch.cat([feats, wgt], 1)
+    return sc, inp, grid, gauss.float().contiguous()
+
+
+def run_mode(sc, inp, grid, gauss, mode, total, hybrid, active):
+    cam = sc.camera
+    dev = "cuda"
+    base = mode & 0xFF
+    C = total * 2
+    hash_levels = grid.levels if base == 4 else active
+    offsets = grid.offsets
+    if base == 4 and offsets.numel() < 17:
+        offsets = torch.cat([offsets, torch.zeros(17 - offsets.numel(), dtype=offsets.dtype)])
+    rs = dsr.GaussianRasterizationSettings(
+        image_height=cam.height, image_width=cam.width, tanfovx=cam.tanfovx, tanfovy=cam.tanfovy,
+        bg=torch.zeros(3, device=dev), scale_modifier=1.0, viewmatrix=cam.world_view_transform.to(dev),
+        projmatrix=cam.full_proj_transform.to(dev), sh_degree=0, campos=cam.camera_center.to(dev),
+        prefiltered=False, debug=False, beta=0.0, if_contract=False, record_transmittance=False,
+        max_intersections=0)
+    hs = dsr.HashGridSettings(L=(total << 16) | (active << 8) | hybrid, S=grid.S, H=grid.base_resolution,
+                              align_corners=False, interpolation=0,
+                              shape_dims=torch.tensor([hybrid * 2, active * 2, C], dtype=torch.int32, device=dev))
+    r = dsr.GaussianRasterizer(rs, hs)
+    P = sc.P
+    with torch.no_grad():
+        color, radii, allmap, _, _ = r(
+            means3D=inp["means3D"].to(dev), means2D=torch.zeros(P, 3, device=dev), shs=None,
+            colors_precomp=gauss.to(dev), opacities=inp["opacities"].to(dev), scales=inp["scales"].to(dev),
+            rotations=inp["rotations"].to(dev), homotrans=inp["homotrans"].to(dev),
+            ap_level=inp["ap_level"].to(dev), features=grid.table.to(dev), offsets=offsets.to(dev),
+            gridrange=grid.gridrange.to(dev), render_mode=mode)
+    torch.cuda.synchronize()
+    out, pre, n = oracle.forward(inp["means3D"].numpy(), inp["scales"].numpy(), inp["rotations"].numpy(),
+                                 inp["opacities"].numpy(), inp["homotrans"].numpy(), inp["ap_level"].numpy(),
+                                 grid.table.float().numpy(), grid.offsets.numpy(), grid.gridrange.numpy(),
+                                 cam.world_view_transform.numpy(), cam.full_proj_transform.numpy(), cam.width,
+                                 cam.height, C, 2, hash_levels, grid.S, grid.base_resolution, render_mode=mode,
+                                 hybrid_levels=hybrid, total_levels=total, gauss=gauss.numpy())
+    return out, color.cpu().numpy(), allmap.cpu().numpy()
+
+
+@pytest.mark.parametrize("mode,total,hybrid,active,weights", [
+    (4, 16, 6, 10, "uniform"),
+    (4, 12, 4, 8, "uniform"),
+    (12, 16, 6, 10, "uniform"),
+    (12, 16, 6, 10, "thresholds"),
+    (12 | 256, 16, 6, 10, "thresholds"),
+    (12, 14, 5, 7, "uniform"),
+    (14, 16, 6, 10, "thresholds"),
+    (14 | 256, 16, 6, 10, "thresholds"),
+    (14, 16, 16, 0, "uniform"),
+])
+def test_render_modes_match_oracle(mode, total, hybrid, active, weights):
+    sc, inp, grid, gauss = mode_case(mode, total, hybrid, active, seed=50 + (mode & 0xFF), weights=weights)
+    out, color, allmap = run_mode(sc, inp, grid, gauss, mode, total, hybrid, active)
+    assert allmap[7].sum() > 100
+    assert np.abs(out["out_color"]).max() > 0.1
+    compare(out, color, allmap)
+
+
+def test_render_mode_4_channels_split():
+    """Mode 4: the first hybrid * LD channels are the blended per-surfel features
+    alone (an all-zero table leaves them unchanged and zeroes the hash channels)."""
+    sc, inp, grid, gauss = mode_case(4, 16, 6, 10, seed=61)
+    grid.table = torch.zeros_like(grid.table)
+    out, color, allmap = run_mode(sc, inp, grid, gauss, 4, 16, 6, 10)
+    assert np.abs(color[:12]).max() > 0.1
+    assert not color[12:].any()
+    compare(out, color, allmap)
+
+
+def test_render_mode_backward_not_built():
+    sc, inp, grid, gauss = mode_case(4, 16, 6, 10, seed=62)
+    cam = sc.camera
+    dev = "cuda"
+    rs = dsr.GaussianRasterizationSettings(
+        image_height=cam.height, image_width=cam.width, tanfovx=cam.tanfovx, tanfovy=cam.tanfovy,
+        bg=torch.zeros(3, device=dev), scale_modifier=1.0, viewmatrix=cam.world_view_transform.to(dev),
+        projmatrix=cam.full_proj_transform.to(dev), sh_degree=0, campos=cam.camera_center.to(dev),
+        prefiltered=False, debug=False, beta=0.0, if_contract=False, record_transmittance=False,
+        max_intersections=0)
+    hs = dsr.HashGridSettings(L=(16 << 16) | (10 << 8) | 6, S=grid.S, H=grid.base_resolution, align_corners=False,
+                              interpolation=0, shape_dims=torch.tensor([12, 20, 32], dtype=torch.int32, device=dev))
+    r = dsr.GaussianRasterizer(rs, hs)
+    P = sc.P
+    feats = gauss.to(dev).requires_grad_(True)
+    color, _, _, _, _ = r(means3D=inp["means3D"].to(dev), means2D=torch.zeros(P, 3, device=dev), shs=None,
+                          colors_precomp=feats, opacities=inp["opacities"].to(dev), scales=inp["scales"].to(dev),
+                          rotations=inp["rotations"].to(dev), homotrans=None, ap_level=inp["ap_level"].to(dev),
+                          features=grid.table.to(dev), offsets=grid.offsets.to(dev),
+                          gridrange=grid.gridrange.to(dev), render_mode=4)
+    with pytest.raises(NotImplementedError):
+        color.sum().backward()
