@@ -107,8 +107,8 @@ typedef struct ns_raster_settings {
    * features blended with the hash levels by a per-surfel weight (flag 256:
    * inference rules). hybrid_levels / total_levels: the reference's level
    * encoding (total << 16 | active << 8 | hybrid) split out; `levels` is the
-   * number of hash levels queried. Forward only: ns_rasterize_backward and
-   * ns_render_frame take mode 0. */
+   * number of hash levels queried. ns_rasterize_backward takes 0, 4, 12 and 14
+   * without the inference flag (training rules); ns_render_frame takes 0. */
   int32_t render_mode;
   uint32_t hybrid_levels;
   uint32_t total_levels;
@@ -194,6 +194,9 @@ typedef struct ns_raster_grads_out {
                            reference's dL_gradsum, returned in ap_level's slot) */
   float* dL_dshapes;    /* [P] or NULL: gradient of the splat kernel's shape
                            (kernel_type 1-3, backward.cu:1864-1909) */
+  float* dL_dcolors_precomp; /* render_mode 4 / 12 / 14: gradient of the per-surfel
+                           rows (ns_surfels.colors_precomp layout, blend weight
+                           included; backward.cu:987-1033, 1425-1606), else NULL */
 } ns_raster_grads_out;
 
 /* Scratch of the backward pass: per-surfel gradient accumulators. */

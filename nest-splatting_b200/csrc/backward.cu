@@ -110,9 +110,68 @@ struct BwSmem {
   LevelConst lv[kMaxLevels];
 };
 
-// kAnyKernel: built with the splat kernels 1-3 (p.kernel_type); the Gaussian-only
-// instantiation keeps them out of the hot loop. kFixed: the table gradient goes
-// to p.dL_dtable_fixed in fixed point (deterministic mode).
+// Render modes 4 / 12 / 14 in the backward (backward.cu:987-1033, 1425-1606):
+// the factor of the hash features in this sample (0 with `query` false: the
+// mode does not read the grid here).
+__device__ __forceinline__ float mode_hash_factor(const BackwardParams& p, uint32_t id, bool& query) {
+  const int base = p.render_mode & 0xFF;
+  const int pg = 2 * p.hybrid_levels;
+  query = p.L > 0;
+  if (base == 4) return 1.0f;
+  if (base == 12) return 1.0f - __ldg(p.gauss + (size_t)id * (2 * p.total_levels + 1) + 2 * p.total_levels);
+  const float wgt = __ldg(p.gauss + (size_t)id * (pg + 1) + pg);
+  query = query && wgt > 1e-6f;
+  return query ? wgt : 0.0f;
+}
+
+// The per-surfel side of a sample in modes 4 / 12 / 14: adds the gradients of
+// the surfel's row (coarse channels aT g, mode 12's fine channels wgt aT g, the
+// blend weight's aT (sum_fine row g - hdot) for 12 and aT hdot for 14) and
+// returns feat . dL/dcolor for the colour recursion, hdot being the hash
+// features' dot product with dL/dcolor (phase B). The reference's cases 12 and
+// 14 leave the feature array of that recursion unwritten; this uses the
+// forward's features.
+__device__ __forceinline__ float mode_backward(const BackwardParams& p, uint32_t id, float aT, float hdot,
+                                               const float* g, int t) {
+  const int base = p.render_mode & 0xFF;
+  const int pg = 2 * p.hybrid_levels, hd = 2 * (int)p.L, td = 2 * p.total_levels;
+  auto gc = [&](int c) {
+    const float2 v = *acc_pair(const_cast<float*>(g), t, c >> 1);
+    return (c & 1) ? v.y : v.x;
+  };
+  const size_t stride = base == 4 ? (size_t)pg : (base == 12 ? (size_t)td + 1 : (size_t)pg + 1);
+  const float* row = p.gauss + (size_t)id * stride;
+  float* drow = p.dL_dcolors + (size_t)id * stride;
+  float f = 0.0f;
+  for (int c = 0; c < pg; c++) {
+    const float gv = gc(c);
+    f += __ldg(row + c) * gv;
+    atomicAdd(drow + c, aT * gv);
+  }
+  if (base == 4) return f + hdot;
+  if (base == 12) {
+    const float wgt = __ldg(row + td);
+    float gdot = 0.0f;
+    if (p.L > 0) {
+      for (int c = pg; c < pg + hd; c++) {
+        const float gv = gc(c);
+        gdot += __ldg(row + c) * gv;
+        atomicAdd(drow + c, wgt * (aT * gv));
+      }
+    }
+    atomicAdd(drow + td, aT * (gdot - hdot));
+    return f + wgt * gdot + (1.0f - wgt) * hdot;
+  }
+  const float wgt = __ldg(row + pg);
+  const bool query = p.L > 0 && wgt > 1e-6f;
+  atomicAdd(drow + pg, query ? aT * hdot : 0.0f);
+  return query ? f + wgt * hdot : f;
+}
+
+// kAnyKernel: built with the splat kernels 1-3 (p.kernel_type) and the render
+// modes 4 / 12 / 14 (p.render_mode); the Gaussian mode-0 instantiation keeps
+// them out of the hot loop. kFixed: the table gradient goes to
+// p.dL_dtable_fixed in fixed point (deterministic mode).
 template <typename TableT, bool kAnyKernel, bool kFixed>
 __global__ void __launch_bounds__(kThreads, 2) blend_backward_kernel(const BackwardParams p) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
@@ -132,6 +191,7 @@ __global__ void __launch_bounds__(kThreads, 2) blend_backward_kernel(const Backw
   const uint32_t L = p.L;
   const float vmin = p.gridrange[0], vmax = p.gridrange[1];
   const float fscale = kFixed ? fixed_point_scale(*p.grad_max_bits) : 0.0f;
+  const int hoff = (kAnyKernel && p.render_mode != 0) ? p.hybrid_levels : 0;  // level of hash level 0
 
   if (t < (int)L) S.lv[t] = make_level<TableT>(p.table, p.offsets, p.S, p.Hres, p.align_corners, t);
   if (t < 9) {
@@ -321,8 +381,11 @@ __global__ void __launch_bounds__(kThreads, 2) blend_backward_kernel(const Backw
           in1 = (st * in1 + 2.0f) * 0.25f;
           in2 = (st * in2 + 2.0f) * 0.25f;
         }
-        S.samp[cnt][t] = make_float4(in0, in1, in2, alpha * T);
-        S.lvl[cnt][t] = (uint8_t)(oob ? 0u : min(apl, L));
+        float hw = alpha * T;  // weight of this sample's hash features
+        bool query = true;
+        if (kAnyKernel && p.render_mode != 0) hw *= mode_hash_factor(p, S.ids[jj], query);
+        S.samp[cnt][t] = make_float4(in0, in1, in2, hw);
+        S.lvl[cnt][t] = (uint8_t)((oob || !query) ? 0u : min(apl, L));
         S.jj[cnt][t] = (uint8_t)jj;
         S.Ts[cnt][t] = T;
         cnt++;
@@ -385,7 +448,7 @@ __global__ void __launch_bounds__(kThreads, 2) blend_backward_kernel(const Backw
             corner_rows(lcst, gc, idx);
 #pragma unroll
             for (int c = 0; c < 8; c++) cv.load(lcst.base, c, idx[c]);
-            gl = *acc_pair(S.g, pp, (int)l);
+            gl = *acc_pair(S.g, pp, hoff + (int)l);
             const float2 grad = make_float2(aT * gl.x, aT * gl.y);
             const float wx[2] = {1 - f[0], f[0]}, wy[2] = {1 - f[1], f[1]}, wz[2] = {1 - f[2], f[2]};
             float2 feat = make_float2(0.f, 0.f);
@@ -539,8 +602,10 @@ __global__ void __launch_bounds__(kThreads, 2) blend_backward_kernel(const Backw
 
         // Colour term (:1786-1797) with the scalar recursion.
         acc_f = last_alpha * last_f + (1.f - last_alpha) * acc_f;
-        last_f = res.x;
-        float dL_dalpha = res.x - acc_f;
+        const float fsc = (kAnyKernel && p.render_mode != 0) ? mode_backward(p, S.ids[jj], aT, res.x, S.g, t)
+                                                             : res.x;
+        last_f = fsc;
+        float dL_dalpha = fsc - acc_f;
 
         // Auxiliary maps (:1799-1852).
         float dL_dz = 0.0f;
@@ -920,10 +985,13 @@ int table_grad_finish_launch(const unsigned long long* fx, size_t n, const uint3
 
 int blend_backward_launch(const BackwardParams& p, int fp16, cudaStream_t stream) {
   if (p.LD != 2 || p.C > kAccStride || p.C <= 0) return NS_ERR_UNSUPPORTED;
-  if (p.L > (uint32_t)(p.C / p.LD) || p.L > (uint32_t)kMaxLevels) return NS_ERR_UNSUPPORTED;
+  const int hoff = p.render_mode != 0 ? p.hybrid_levels : 0;
+  if (hoff < 0 || (int64_t)hoff + p.L > (uint32_t)(p.C / p.LD) || p.L > (uint32_t)kMaxLevels)
+    return NS_ERR_UNSUPPORTED;
+  if ((p.render_mode >> 8) != 0) return NS_ERR_UNSUPPORTED;  // training rules only
   const int tiles = div_up(p.W, kTile) * div_up(p.H, kTile);
   if (tiles == 0) return NS_OK;
-  if (p.kernel_type != 0)
+  if (p.kernel_type != 0 || p.render_mode != 0)
     return fp16 ? launch_backward<__half, true>(p, tiles, stream)
                 : launch_backward<float, true>(p, tiles, stream);
   return fp16 ? launch_backward<__half, false>(p, tiles, stream)

@@ -364,12 +364,19 @@ int ns_rasterize_backward(const ns_raster_settings* settings, const ns_surfels* 
   cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_);
   int rc = validate_settings(settings);
   if (rc) return rc;
-  if (settings->render_mode != 0) return NS_ERR_UNSUPPORTED;  // forward only
+  if ((settings->render_mode >> 8) != 0) return NS_ERR_UNSUPPORTED;  // training rules only
   if (!surfels || !gi || !go) return NS_ERR_INVALID;
   const int P = surfels->P;
   if (P < 0 || num_rendered < 0) return NS_ERR_INVALID;
   if (settings->kernel_type != 0 && P > 0 && (!surfels->shapes || !go->dL_dshapes))
     return NS_ERR_INVALID;
+  const int base_mode = settings->render_mode & 0xFF;
+  if (base_mode != 0 && P > 0 && (!surfels->colors_precomp || !go->dL_dcolors_precomp))
+    return NS_ERR_INVALID;
+  const size_t mode_stride = base_mode == 4    ? (size_t)settings->hybrid_levels * settings->level_dim
+                             : base_mode == 12 ? (size_t)settings->total_levels * settings->level_dim + 1
+                             : base_mode == 14 ? (size_t)settings->hybrid_levels * settings->level_dim + 1
+                                               : 0;
   if (settings->level_dim != 2) return NS_ERR_UNSUPPORTED;
   if (!go->dL_dmeans3D || !go->dL_dmean2D || !go->dL_dopacity || !go->dL_dscales ||
       !go->dL_drots || !go->dL_dtable || !go->dL_gradsum || go->table_rows < 0)
@@ -431,6 +438,13 @@ int ns_rasterize_backward(const ns_raster_settings* settings, const ns_surfels* 
   bp.contract = settings->if_contract;
   bp.beta = settings->beta;
   bp.kernel_type = settings->kernel_type;
+  bp.render_mode = settings->render_mode;
+  bp.hybrid_levels = (int)settings->hybrid_levels;
+  bp.total_levels = (int)settings->total_levels;
+  bp.gauss = surfels->colors_precomp;
+  bp.dL_dcolors = go->dL_dcolors_precomp;
+  if (base_mode != 0)
+    NS_CUDA_TRY(cudaMemsetAsync(go->dL_dcolors_precomp, 0, (size_t)P * mode_stride * sizeof(float), stream));
   bp.Wq = Wq;
   bp.Hq = Hq;
   bp.projmatrix = settings->projmatrix;

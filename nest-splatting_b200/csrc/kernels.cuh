@@ -50,6 +50,11 @@ struct BackwardParams {
   int contract;
   float beta;
   int kernel_type;            // splat kernel 0-3; 1-3 read the shape in record word 31
+  int render_mode;            // 0, or 4 / 12 / 14 (training rules) as in RenderParams
+  int hybrid_levels;
+  int total_levels;
+  const float* gauss;         // per-surfel rows of the render modes
+  float* dL_dcolors;          // their gradient (same layout), accumulated
   int Wq, Hq;                 // image size as the reference's preprocess backward recomputes it
   const float* projmatrix;
   const float* viewmatrix;

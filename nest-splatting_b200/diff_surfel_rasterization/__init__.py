@@ -10,18 +10,19 @@ C-ABI; there is no CPU fallback. Built: render_mode 0 (baseline hash grid),
 level_dim 2, the Gaussian splat kernel (kernel_type 0) and the beta / flex /
 general kernels (kernel_type 1-3, per-surfel `shapes`, whose gradient comes back
 in shapes' slot), forward and backward; render modes 4 (cat), 12 (adaptive_cat)
-and 14 (adaptive_zero, both with the inference flag 256) forward, the per-surfel
-features read from colors_precomp and the level word hashgrid_settings.L =
-total << 16 | active << 8 | hybrid as the reference's renderer encodes it
-(gaussian_renderer/__init__.py:216-241, 334-447). Other modes raise
-NotImplementedError instead of silently rendering nothing as the reference does
-for shapes it was not compiled for.
+and 14 (adaptive_zero), forward (also with the inference flag 256) and backward
+(training rules; the per-surfel rows' gradient, blend weight included, comes
+back in colors_precomp's slot), the per-surfel features read from
+colors_precomp and the level word hashgrid_settings.L = total << 16 | active << 8
+| hybrid as the reference's renderer encodes it (gaussian_renderer/__init__.py:
+216-241, 334-447). Other modes raise NotImplementedError instead of silently
+rendering nothing as the reference does for shapes it was not compiled for.
 
 Backward (__init__.py:174-275 of the reference): the 21 gradients come back in
 argument order; means2D's slot carries the densification statistic and
 ap_level's slot dL_gradsum, homotrans gets None (its gradient is folded into
-means, scales and rotations), sh / colors_precomp get zeros (mode 0 never reads
-them).
+means, scales and rotations), sh gets zeros and colors_precomp zeros in mode 0
+(which never reads them).
 
 `features` may be fp32 (as the reference stores the table) or fp16 (read as
 fp16 pairs by the kernels, half the L2 traffic).
@@ -150,13 +151,15 @@ class _RasterizeGaussians(torch.autograd.Function):
                           sh=sh.shape, colors_precomp=colors_precomp.shape,
                           shapes=None if shp is None else shapes.shape)
         ctx.shape_values = shp
+        ctx.gauss = gauss
         ctx.mark_non_differentiable(radii)
         return color, radii, others, trans, cover
 
     @staticmethod
     def backward(ctx, grad_out_color, grad_radii, grad_depth, grad_0, grad_1):
-        if ctx.cfg.render_mode != 0:
-            raise NotImplementedError(f"backward of render_mode {ctx.cfg.render_mode}: only mode 0 is built")
+        if (ctx.cfg.render_mode >> 8) != 0:
+            raise NotImplementedError(f"backward of render_mode {ctx.cfg.render_mode}: the inference flag "
+                                      f"has no backward (training rules only)")
         dev = ctx.radii.device
         H, W = ctx.cfg.image_height, ctx.cfg.image_width
         if grad_out_color is None:
@@ -164,7 +167,8 @@ class _RasterizeGaussians(torch.autograd.Function):
         if grad_depth is None:
             grad_depth = torch.zeros((_raster.OTHER_CHANNELS, H, W), dtype=torch.float32, device=dev)
         g = _raster.rasterize_backward(ctx.cfg, *ctx.args, ctx.radii, ctx.num_rendered, ctx.scratch,
-                                       grad_out_color, grad_depth, shapes=ctx.shape_values)
+                                       grad_out_color, grad_depth, shapes=ctx.shape_values,
+                                       colors_precomp=ctx.gauss)
         ctx.scratch = None
         need = ctx.needs_input_grad
         sh = ctx.shapes
@@ -177,7 +181,8 @@ class _RasterizeGaussians(torch.autograd.Function):
         return (g["means3D"] if need[0] else None,
                 g["means2D"] if need[1] else None,
                 zeros_if(2, sh["sh"]),
-                zeros_if(3, sh["colors_precomp"]),
+                (g["colors_precomp"].reshape(sh["colors_precomp"]) if "colors_precomp" in g
+                 else zeros_if(3, sh["colors_precomp"])) if need[3] else None,
                 g["opacity"].reshape(sh["opacities"]) if need[4] else None,
                 g["scales"] if need[5] else None,
                 g["rotations"] if need[6] else None,

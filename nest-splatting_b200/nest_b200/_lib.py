@@ -88,6 +88,7 @@ class GradsOut(C.Structure):
         ("dL_dmeans3D", C.c_void_p), ("dL_dmean2D", C.c_void_p), ("dL_dopacity", C.c_void_p),
         ("dL_dscales", C.c_void_p), ("dL_drots", C.c_void_p), ("dL_dtable", C.c_void_p),
         ("table_rows", C.c_int64), ("dL_gradsum", C.c_void_p), ("dL_dshapes", C.c_void_p),
+        ("dL_dcolors_precomp", C.c_void_p),
     ]
 
 

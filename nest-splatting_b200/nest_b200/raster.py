@@ -177,14 +177,15 @@ def rasterize_forward(cfg: RasterConfig, means3D, scales, rotations, opacities, 
 
 def rasterize_backward(cfg: RasterConfig, means3D, scales, rotations, opacities, homotrans, ap_level, features,
                        offsets, gridrange, radii, num_rendered: int, scratch: Scratch, dL_dcolor, dL_dothers,
-                       return_accumulators: bool = False, shapes=None):
+                       return_accumulators: bool = False, shapes=None, colors_precomp=None):
     """Backward rasterization (render_mode 0) through ns_rasterize_backward.
 
     `scratch` and every input must be the ones of the forward call. Returns a dict
     of fp32 gradients: means3D [P,3], means2D [P,3] (densification statistic),
     opacity [P,1], scales [P,2], rotations [P,4], table [rows, level_dim],
     gradsum [P,1]; for kernel_type 1-3 (`shapes` [P] as in the forward) also
-    shapes [P]. With return_accumulators, also "accum": the render pass's
+    shapes [P]; for render modes 4 / 12 / 14 (`colors_precomp` as in the forward)
+    also colors_precomp (same shape). With return_accumulators, also "accum": the render pass's
     per-surfel accumulators [P,20] (dL/dM 9, dL/dT[0].z, dL/dT[1].z, opacity,
     dL/dnormal 3, gradsum, dL/dmean2D 2, dL/dshape, 1 unused), for tests.
     """
@@ -209,6 +210,12 @@ def rasterize_backward(cfg: RasterConfig, means3D, scales, rotations, opacities,
         shapes = shapes.contiguous().float().reshape(-1)
         _require_cuda(shapes)
         g["shapes"] = torch.empty((P,), dtype=torch.float32, device=dev)
+    if cfg.render_mode != 0:
+        if colors_precomp is None:
+            raise ValueError(f"render_mode {cfg.render_mode} needs colors_precomp")
+        colors_precomp = colors_precomp.contiguous().float()
+        _require_cuda(colors_precomp)
+        g["colors_precomp"] = torch.zeros_like(colors_precomp)
     if P == 0:
         g["table"].zero_()
         return g
@@ -220,10 +227,13 @@ def rasterize_backward(cfg: RasterConfig, means3D, scales, rotations, opacities,
     surf.features, surf.offsets, surf.gridrange = ptr(features), ptr(offsets), ptr(gridrange)
     if cfg.kernel_type != 0:
         surf.shapes = ptr(shapes)
+    if cfg.render_mode != 0:
+        surf.colors_precomp = ptr(colors_precomp)
     gi = _lib.GradsIn(ptr(dL_dcolor), ptr(dL_dothers), ptr(radii))
     go = _lib.GradsOut(ptr(g["means3D"]), ptr(g["means2D"]), ptr(g["opacity"]), ptr(g["scales"]),
                        ptr(g["rotations"]), ptr(g["table"]), rows, ptr(g["gradsum"]),
-                       ptr(g["shapes"]) if "shapes" in g else None)
+                       ptr(g["shapes"]) if "shapes" in g else None,
+                       ptr(g["colors_precomp"]) if "colors_precomp" in g else None)
     nbytes = (lib.ns_backward_scratch_bytes_deterministic(P, rows, int(cfg.level_dim)) if cfg.deterministic
               else lib.ns_backward_scratch_bytes(P))
     acc = torch.empty(nbytes, dtype=torch.uint8, device=dev)

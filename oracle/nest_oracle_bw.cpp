@@ -177,14 +177,18 @@ void render_backward(int W, int H, const uint32_t* ranges, const uint32_t* point
                      const float* final_T, const uint32_t* n_contrib, const float* dL_dout_color,
                      const float* dL_dout_others, R* dL_dtable, R* dL_dtransMat, R* dL_dhomoMat,
                      R* dL_dmean2D, R* dL_dnormal, R* dL_dopacity, R* dL_gradsum, int kernel_type,
-                     const float* shapes, R* dL_dshapes) {
+                     const float* shapes, R* dL_dshapes, int render_mode, int hybrid_levels,
+                     int total_levels, const float* gauss, R* dL_dcolors) {
   using V = V3<R>;
+  const int base_mode = render_mode & 0xFF;
+  const int pg = hybrid_levels * LD, hd = (int)L * LD, td = total_levels * LD;
   const int gx = (W + kBlock - 1) / kBlock, gy = (H + kBlock - 1) / kBlock;
   const size_t HW = (size_t)H * W;
   const R vmin = gridrange[0], vmax = gridrange[1];
 #pragma omp parallel for schedule(dynamic, 1)
   for (int tile = 0; tile < gx * gy; tile++) {
     std::vector<R> dL_dpixel(C), accum_rec(C), last_color(C), grad_feat(C), feat(C);
+    std::vector<R> hfeat(hd > 0 ? hd : 1), grad_hash(hd > 0 ? hd : 1);
     const int tx = tile % gx, ty = tile / gx;
     const uint32_t r0 = ranges[2 * tile], r1 = ranges[2 * tile + 1];
     for (int py = ty * kBlock; py < std::min(H, (ty + 1) * kBlock); py++) {
@@ -291,9 +295,71 @@ void render_backward(int W, int H, const uint32_t* ranges, const uint32_t* point
           atomic_add<R>(&dL_gradsum[id], sum_grad);
           const uint32_t apl = (uint32_t)std::floor(ap_level[id]);
           R dL_dxyz[3];
-          query_feature_bw<R>(feat.data(), C, LD, xyz, vmin, vmax, offsets, apl, table, L, S, Hres,
-                           align_corners != 0, interp, contract != 0, grad_feat.data(), dL_dtable,
-                           dL_dxyz);
+          if (base_mode == 0) {
+            query_feature_bw<R>(feat.data(), C, LD, xyz, vmin, vmax, offsets, apl, table, L, S, Hres,
+                             align_corners != 0, interp, contract != 0, grad_feat.data(), dL_dtable,
+                             dL_dxyz);
+          } else {
+            // Render modes 4 / 12 / 14 (backward.cu:987-1033, 1425-1606): the hash
+            // levels see the fine channels' gradient times the mode's factor b; the
+            // per-surfel rows get theirs in dL_dcolors (blend weight last). The
+            // colour term of dL/dalpha below uses the forward's feature vector: the
+            // reference's cases 12 and 14 leave `feat` unwritten there.
+            R b = 1;
+            bool query = L > 0;
+            const float* g = nullptr;
+            R wgt = 0;
+            size_t row = 0;
+            if (base_mode == 4) {
+              row = (size_t)id * pg;
+              g = gauss + row;
+            } else if (base_mode == 12) {
+              row = (size_t)id * (td + 1);
+              g = gauss + row;
+              wgt = g[td];
+              b = R(1) - wgt;
+            } else {
+              row = (size_t)id * (pg + 1);
+              g = gauss + row;
+              wgt = g[pg];
+              b = wgt;
+              query = query && wgt > R(1e-6f);
+            }
+            for (int i = 0; i < hd; i++) grad_hash[i] = b * grad_feat[pg + i];
+            dL_dxyz[0] = dL_dxyz[1] = dL_dxyz[2] = 0;
+            std::fill(hfeat.begin(), hfeat.end(), R(0));
+            if (query)
+              query_feature_bw<R>(hfeat.data(), hd, LD, xyz, vmin, vmax, offsets, apl, table, L, S,
+                                  Hres, align_corners != 0, interp, contract != 0, grad_hash.data(),
+                                  dL_dtable, dL_dxyz);
+            std::fill(feat.begin(), feat.end(), R(0));
+            for (int c = 0; c < pg; c++) {
+              feat[c] = g[c];
+              atomic_add<R>(&dL_dcolors[row + c], grad_feat[c]);
+            }
+            if (base_mode == 4) {
+              for (int i = 0; i < hd; i++) feat[pg + i] = hfeat[i];
+            } else if (base_mode == 12) {
+              R dw = 0;
+              if (L > 0) {
+                for (int i = 0; i < hd; i++) {
+                  feat[pg + i] = wgt * R(g[pg + i]) + (R(1) - wgt) * hfeat[i];
+                  atomic_add<R>(&dL_dcolors[row + pg + i], wgt * grad_feat[pg + i]);
+                  dw += (R(g[pg + i]) - hfeat[i]) * grad_feat[pg + i];
+                }
+              }
+              atomic_add<R>(&dL_dcolors[row + td], dw);
+            } else {
+              R dw = 0;
+              if (query) {
+                for (int i = 0; i < hd; i++) {
+                  feat[pg + i] = wgt * hfeat[i];
+                  dw += hfeat[i] * grad_feat[pg + i];
+                }
+              }
+              atomic_add<R>(&dL_dcolors[row + pg], dw);
+            }
+          }
           for (int c = 0; c < C; c++) {
             accum_rec[c] = last_alpha * last_color[c] + (R(1) - last_alpha) * accum_rec[c];
             last_color[c] = feat[c];
@@ -554,12 +620,14 @@ void oracle_render_backward(int W, int H, const uint32_t* ranges, const uint32_t
                             float* dL_dtable, float* dL_dtransMat, float* dL_dhomoMat,
                             float* dL_dmean2D, float* dL_dnormal, float* dL_dopacity,
                             float* dL_gradsum, int kernel_type, const float* shapes,
-                            float* dL_dshapes) {
+                            float* dL_dshapes, int render_mode, int hybrid_levels,
+                            int total_levels, const float* gauss, float* dL_dcolors) {
   render_backward<float>(W, H, ranges, point_list, means2D, transMat, normal_opacity, homotrans,
                          ap_level, table, offsets, gridrange, C, LD, L, S, Hres, align_corners,
                          interp, contract, beta, final_T, n_contrib, dL_dout_color, dL_dout_others,
                          dL_dtable, dL_dtransMat, dL_dhomoMat, dL_dmean2D, dL_dnormal, dL_dopacity,
-                         dL_gradsum, kernel_type, shapes, dL_dshapes);
+                         dL_gradsum, kernel_type, shapes, dL_dshapes, render_mode, hybrid_levels,
+                         total_levels, gauss, dL_dcolors);
 }
 
 // Working precision double: the same formulas and decisions, without float
@@ -576,12 +644,14 @@ void oracle_render_backward_f64(int W, int H, const uint32_t* ranges, const uint
                                 double* dL_dtable, double* dL_dtransMat, double* dL_dhomoMat,
                                 double* dL_dmean2D, double* dL_dnormal, double* dL_dopacity,
                                 double* dL_gradsum, int kernel_type, const float* shapes,
-                                double* dL_dshapes) {
+                                double* dL_dshapes, int render_mode, int hybrid_levels,
+                                int total_levels, const float* gauss, double* dL_dcolors) {
   render_backward<double>(W, H, ranges, point_list, means2D, transMat, normal_opacity, homotrans,
                           ap_level, table, offsets, gridrange, C, LD, L, S, Hres, align_corners,
                           interp, contract, beta, final_T, n_contrib, dL_dout_color,
                           dL_dout_others, dL_dtable, dL_dtransMat, dL_dhomoMat, dL_dmean2D,
-                          dL_dnormal, dL_dopacity, dL_gradsum, kernel_type, shapes, dL_dshapes);
+                          dL_dnormal, dL_dopacity, dL_gradsum, kernel_type, shapes, dL_dshapes,
+                          render_mode, hybrid_levels, total_levels, gauss, dL_dcolors);
 }
 
 void oracle_preprocess_backward(int P, const float* means3D, const float* scales,

@@ -61,7 +61,7 @@ def load() -> C.CDLL:
     lib.oracle_num_threads.restype = i32
     lib.oracle_render_backward.argtypes = [i32, i32, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, i32, i32, u32, f32,
                                            u32, i32, u32, i32, f32, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp,
-                                           i32, vp, vp]
+                                           i32, vp, vp, i32, i32, i32, vp, vp]
     lib.oracle_preprocess_backward.argtypes = [i32, vp, vp, vp, vp, vp, vp, vp, i32, i32, f32, f32, vp, vp, vp,
                                                vp, vp, vp, vp]
     lib.oracle_render_backward_f64.argtypes = lib.oracle_render_backward.argtypes
@@ -228,11 +228,13 @@ def forward(means3D, scales, rotations, opacities, homotrans, ap_level, table_f3
 
 def render_backward(pre, vals, ranges, fwd, homotrans, ap_level, table_f32, offsets, gridrange, W, H, C_out, LD,
                     L, S, Hres, dL_dcolor, dL_dothers, align_corners=False, interp=0, contract=False, beta=0.0,
-                    f64=False, kernel_type=0, shapes=None):
+                    f64=False, kernel_type=0, shapes=None, render_mode=0, hybrid_levels=0, total_levels=0,
+                    gauss=None):
     """renderCUDAsurfelBackward<C> mode 0 restated (nest_oracle_bw.cpp). `fwd` is the
     dict returned by render(). Returns the render-pass gradients (reference layouts).
     f64=True evaluates the same formulas in double (float64 outputs). kernel_type
-    1-3 take per-surfel `shapes` [P] and add dL_dshapes [P]."""
+    1-3 take per-surfel `shapes` [P] and add dL_dshapes [P]. Render modes 4 / 12 /
+    14 take the per-surfel rows `gauss` and add dL_dcolors (same shape)."""
     lib = load()
     P = pre["radii"].shape[0]
     table = _f32(table_f32)
@@ -241,6 +243,9 @@ def render_backward(pre, vals, ranges, fwd, homotrans, ap_level, table_f32, offs
              dL_dhomoMat=np.zeros((P, 9), dt), dL_dmean2D=np.zeros((P, 3), dt),
              dL_dnormal=np.zeros((P, 3), dt), dL_dopacity=np.zeros(P, dt), dL_gradsum=np.zeros(P, dt),
              dL_dshapes=np.zeros(P, dt))
+    if render_mode != 0:
+        gauss = _f32(gauss).reshape(P, -1)
+        g["dL_dcolors"] = np.zeros(gauss.shape, dt)
     if kernel_type != 0:
         assert shapes is not None
         shapes = _f32(shapes).reshape(P)
@@ -258,7 +263,9 @@ def render_backward(pre, vals, ranges, fwd, homotrans, ap_level, table_f32, offs
                                _p(fwd["final_T"]), _p(fwd["n_contrib"]), _p(gc), _p(go), _p(g["dL_dtable"]),
                                _p(g["dL_dtransMat"]), _p(g["dL_dhomoMat"]), _p(g["dL_dmean2D"]),
                                _p(g["dL_dnormal"]), _p(g["dL_dopacity"]), _p(g["dL_gradsum"]), int(kernel_type),
-                               _p(shapes if kernel_type != 0 else None), _p(g["dL_dshapes"]))
+                               _p(shapes if kernel_type != 0 else None), _p(g["dL_dshapes"]), int(render_mode),
+                               int(hybrid_levels), int(total_levels), _p(gauss if render_mode != 0 else None),
+                               _p(g.get("dL_dcolors")))
     return g
 
 

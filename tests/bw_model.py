@@ -117,7 +117,28 @@ def splat_value(rho, shape, kernel_type: int):
     return torch.exp(-0.5 * rho), torch.ones_like(rho, dtype=torch.bool)
 
 
-def render(means, scales, rots, opac, table, cam, lists, grid, apl_int, W, H, kernel_type=0, shapes=None):
+def mode_feature(f_hash, row, mode, pg, td, C):
+    """Feature vectors [n, C] of render modes 4 / 12 / 14 (forward.cu:1218-1282,
+    1593-1790, training rules) from the hash features f_hash [n, L*LD] and the
+    surfel's row of colors_precomp (blend weight last for 12 / 14)."""
+    n, hd = f_hash.shape
+    coarse = row[:pg].expand(n, pg)
+    if mode == 4:
+        fine = f_hash
+    elif mode == 12:
+        wgt = row[td]
+        fine = wgt * row[pg:pg + hd].expand(n, hd) + (1 - wgt) * f_hash
+    else:
+        wgt = row[pg]
+        fine = wgt * f_hash if float(wgt.detach()) > 1e-6 else torch.zeros_like(f_hash)
+    feat = torch.cat([coarse, fine], 1)
+    if feat.shape[1] < C:
+        feat = torch.cat([feat, feat.new_zeros(n, C - feat.shape[1])], 1)
+    return feat
+
+
+def render(means, scales, rots, opac, table, cam, lists, grid, apl_int, W, H, kernel_type=0, shapes=None,
+           modes=None):
     """Forward pass over the oracle's tile lists. Returns (color [C,H,W], others [7,H,W], margins).
 
     margins: the smallest relative distance of any decision (alpha >= 1/255, the
@@ -140,7 +161,7 @@ def render(means, scales, rots, opac, table, cam, lists, grid, apl_int, W, H, ke
     xy = xy3 + (centre(Tu, Tv, Tw, 4.0) - xy3).detach()
 
     ranges, point_list = lists
-    C = grid["L"] * grid["LD"]
+    C = grid["L"] * grid["LD"] if modes is None else modes["C"]
     color = torch.zeros(C, H * W, dtype=torch.float64)
     others = torch.zeros(7, H * W, dtype=torch.float64)
     gx = (W + TILE - 1) // TILE
@@ -204,6 +225,8 @@ def render(means, scales, rots, opac, table, cam, lists, grid, apl_int, W, H, ke
             f = query(hit, np.full(npx, apl_int[i]), table, grid["offsets"], grid["L"], grid["LD"], grid["S"],
                       grid["H"], grid["vmin"], grid["vmax"], grid.get("align_corners", False),
                       grid.get("interp", 0))
+            if modes is not None:
+                f = mode_feature(f, modes["gauss"][i], modes["mode"], modes["pg"], modes["td"], C)
             Cacc = Cacc + f * w[:, None]
             T = torch.where(valid, test_T, T)
         color = color.index_copy(1, pid, Cacc.T)

@@ -110,25 +110,106 @@ def test_render_mode_4_channels_split():
     compare(out, color, allmap)
 
 
-def test_render_mode_backward_not_built():
-    sc, inp, grid, gauss = mode_case(4, 16, 6, 10, seed=62)
+def mode_grads(sc, inp, grid, gauss, mode, total, hybrid, active, gc, go):
+    """GPU gradients of modes 4 / 12 / 14 through raster.rasterize_forward /
+    rasterize_backward, and the oracle's (float32 and float64) on the same lists."""
+    from nest_b200 import raster
+    from test_gpu_backward import GRAD_KEYS
+    cam = sc.camera
+    base = mode & 0xFF
+    hash_levels = grid.levels if base == 4 else active
+    C = total * 2
+    cfg = raster.RasterConfig(
+        image_height=cam.height, image_width=cam.width, tanfovx=cam.tanfovx, tanfovy=cam.tanfovy,
+        viewmatrix=cam.world_view_transform.cuda().contiguous(),
+        projmatrix=cam.full_proj_transform.cuda().contiguous(), levels=hash_levels, S=grid.S,
+        base_resolution=grid.base_resolution, channels=C, level_dim=2, table_fp16=True, render_mode=mode,
+        hybrid_levels=hybrid, total_levels=total)
+    args = (inp["means3D"].cuda().contiguous(), inp["scales"].cuda().contiguous(),
+            inp["rotations"].cuda().contiguous(), inp["opacities"].cuda().reshape(-1).contiguous(),
+            inp["homotrans"].cuda().reshape(-1, 16).contiguous(), inp["ap_level"].cuda().reshape(-1).contiguous(),
+            grid.table.cuda().contiguous(), grid.offsets.cuda().contiguous(), grid.gridrange.cuda().contiguous())
+    gcol = gauss.cuda().contiguous()
+    n, color, others, radii, _, _, scratch = raster.rasterize_forward(cfg, *args, colors_precomp=gcol)
+    got = raster.rasterize_backward(cfg, *args, radii, n, scratch, gc.cuda(), go.cuda(), colors_precomp=gcol)
+    torch.cuda.synchronize()
+    got = {k: v.cpu().numpy() for k, v in got.items()}
+    vm, pm = cam.world_view_transform.numpy(), cam.full_proj_transform.numpy()
+    W, H = cam.width, cam.height
+    pre = oracle.preprocess(inp["means3D"].numpy(), inp["scales"].numpy(), inp["rotations"].numpy(),
+                            inp["opacities"].numpy(), vm, pm, W, H)
+    _, vals, ranges = oracle.bin_surfels(pre, W, H)
+    common = (inp["homotrans"].numpy(), inp["ap_level"].numpy(), grid.table.float().numpy(), grid.offsets.numpy(),
+              grid.gridrange.numpy(), W, H, C, 2, hash_levels, grid.S, grid.base_resolution)
+    mkw = dict(render_mode=mode, hybrid_levels=hybrid, total_levels=total, gauss=gauss.numpy())
+    fwd = oracle.render(pre, vals, ranges, *common, **mkw)
+    refs = []
+    for f64 in (False, True):
+        gr = oracle.render_backward(pre, vals, ranges, fwd, *common, gc.numpy(), go.numpy(), f64=f64, **mkw)
+        pg = oracle.preprocess_backward(inp["means3D"].numpy(), inp["scales"].numpy(), inp["rotations"].numpy(),
+                                        pre, gr, vm, pm, W, H, cam.tanfovx, cam.tanfovy, f64=f64)
+        refs.append(dict(g=gr, pg=pg))
+    np.testing.assert_array_equal(radii.cpu().numpy(), pre["radii"])
+    return got, refs[0], refs[1], {**GRAD_KEYS, "colors_precomp": ("g", "dL_dcolors")}
+
+
+@pytest.mark.parametrize("mode,total,hybrid,active,seed", [
+    (4, 16, 6, 10, 19), (12, 16, 6, 10, 19), (14, 16, 6, 10, 19), (12, 14, 5, 7, 18), (14, 16, 16, 0, 18)])
+def test_render_modes_backward_match_oracle(mode, total, hybrid, active, seed):
+    """Every gradient, the per-surfel rows' (blend weight included) among them,
+    against the oracle's restatement of backward.cu:987-1033, 1425-1606 (itself
+    pinned to float64 autograd in test_oracle_backward.py); table U(-1e-4, 1e-4)
+    as in the benchmark."""
+    from test_gpu_backward import check_all, upstream
+    sc, inp, grid, gauss = mode_case(mode, total, hybrid, active, seed=seed)
+    grid.table = (grid.table.float() * 1e-4).half()
+    g = torch.Generator().manual_seed(seed)
+    gc = torch.randn(total * 2, sc.camera.height, sc.camera.width, generator=g)
+    _, go = upstream(sc, seed=5)
+    got, ref, exact, keys = mode_grads(sc, inp, grid, gauss, mode, total, hybrid, active, gc, go)
+    if active == 0:
+        keys = {k: v for k, v in keys.items() if k != "table"}
+        assert not got["table"].any()
+    check_all(got, ref, exact, keys=keys)
+
+
+def test_dropin_mode_gradients_in_colors_precomp_slot():
+    """The drop-in Function returns the per-surfel rows' gradient in
+    colors_precomp's slot (mode 14); the inference flag has no backward."""
+    from test_gpu_backward import upstream
+    mode, total, hybrid, active = 14, 16, 6, 10
+    sc, inp, grid, gauss = mode_case(mode, total, hybrid, active, seed=19)
     cam = sc.camera
     dev = "cuda"
-    rs = dsr.GaussianRasterizationSettings(
-        image_height=cam.height, image_width=cam.width, tanfovx=cam.tanfovx, tanfovy=cam.tanfovy,
-        bg=torch.zeros(3, device=dev), scale_modifier=1.0, viewmatrix=cam.world_view_transform.to(dev),
-        projmatrix=cam.full_proj_transform.to(dev), sh_degree=0, campos=cam.camera_center.to(dev),
-        prefiltered=False, debug=False, beta=0.0, if_contract=False, record_transmittance=False,
-        max_intersections=0)
-    hs = dsr.HashGridSettings(L=(16 << 16) | (10 << 8) | 6, S=grid.S, H=grid.base_resolution, align_corners=False,
-                              interpolation=0, shape_dims=torch.tensor([12, 20, 32], dtype=torch.int32, device=dev))
-    r = dsr.GaussianRasterizer(rs, hs)
-    P = sc.P
-    feats = gauss.to(dev).requires_grad_(True)
-    color, _, _, _, _ = r(means3D=inp["means3D"].to(dev), means2D=torch.zeros(P, 3, device=dev), shs=None,
-                          colors_precomp=feats, opacities=inp["opacities"].to(dev), scales=inp["scales"].to(dev),
-                          rotations=inp["rotations"].to(dev), homotrans=None, ap_level=inp["ap_level"].to(dev),
-                          features=grid.table.to(dev), offsets=grid.offsets.to(dev),
-                          gridrange=grid.gridrange.to(dev), render_mode=4)
-    with pytest.raises(NotImplementedError):
-        color.sum().backward()
+    g = torch.Generator().manual_seed(19)
+    gc = torch.randn(total * 2, cam.height, cam.width, generator=g)
+    _, go = upstream(sc, seed=5)
+    _, ref, _, _ = mode_grads(sc, inp, grid, gauss, mode, total, hybrid, active, gc, go)
+    for flag in (0, 256):
+        rs = dsr.GaussianRasterizationSettings(
+            image_height=cam.height, image_width=cam.width, tanfovx=cam.tanfovx, tanfovy=cam.tanfovy,
+            bg=torch.zeros(3, device=dev), scale_modifier=1.0, viewmatrix=cam.world_view_transform.to(dev),
+            projmatrix=cam.full_proj_transform.to(dev), sh_degree=0, campos=cam.camera_center.to(dev),
+            prefiltered=False, debug=False, beta=0.0, if_contract=False, record_transmittance=False,
+            max_intersections=0)
+        hs = dsr.HashGridSettings(L=(total << 16) | (active << 8) | hybrid, S=grid.S, H=grid.base_resolution,
+                                  align_corners=False, interpolation=0,
+                                  shape_dims=torch.tensor([12, 20, 32], dtype=torch.int32, device=dev))
+        r = dsr.GaussianRasterizer(rs, hs)
+        P = sc.P
+        feats = gauss.to(dev).clone().requires_grad_(True)
+        color, _, allmap, _, _ = r(
+            means3D=inp["means3D"].to(dev), means2D=torch.zeros(P, 3, device=dev), shs=None, colors_precomp=feats,
+            opacities=inp["opacities"].to(dev), scales=inp["scales"].to(dev), rotations=inp["rotations"].to(dev),
+            homotrans=inp["homotrans"].to(dev), ap_level=inp["ap_level"].to(dev), features=grid.table.to(dev),
+            offsets=grid.offsets.to(dev), gridrange=grid.gridrange.to(dev), render_mode=mode | flag)
+        loss = (color * gc.to(dev)).sum() + (allmap * go.to(dev)).sum()
+        if flag:
+            with pytest.raises(NotImplementedError):
+                loss.backward()
+            continue
+        loss.backward()
+        got = feats.grad.cpu().numpy()
+        want = ref["g"]["dL_dcolors"]
+        assert got.shape == want.shape
+        assert np.linalg.norm(got - want) / np.linalg.norm(want) < 1e-3
