@@ -186,12 +186,12 @@ int validate_settings(const ns_raster_settings* s) {
   if (s->levels * s->level_dim > s->channels) return NS_ERR_INVALID;
   if (s->kernel_type < 0 || s->kernel_type > 3) return NS_ERR_UNSUPPORTED;
   const int base = s->render_mode & 0xFF, flag = s->render_mode >> 8;
-  if (base != 0 && base != 4 && base != 12 && base != 14) return NS_ERR_UNSUPPORTED;
-  if (flag > 1 || (flag && base != 12 && base != 14)) return NS_ERR_UNSUPPORTED;
+  if (base != 0 && base != 4 && base != 12 && base != 13 && base != 14) return NS_ERR_UNSUPPORTED;
+  if (flag > 1 || (flag && base != 12 && base != 13 && base != 14)) return NS_ERR_UNSUPPORTED;
   if (base != 0) {
     if (s->hybrid_levels > 16 || s->total_levels > 16) return NS_ERR_INVALID;
     if ((s->hybrid_levels + s->levels) * s->level_dim > s->channels) return NS_ERR_INVALID;
-    if (base == 12 && s->total_levels * s->level_dim > s->channels) return NS_ERR_INVALID;
+    if ((base == 12 || base == 13) && s->total_levels * s->level_dim > s->channels) return NS_ERR_INVALID;
   }
   return NS_OK;
 }
@@ -364,7 +364,8 @@ int ns_rasterize_backward(const ns_raster_settings* settings, const ns_surfels* 
   cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_);
   int rc = validate_settings(settings);
   if (rc) return rc;
-  if ((settings->render_mode >> 8) != 0) return NS_ERR_UNSUPPORTED;  // training rules only
+  // training rules of modes 4 / 12 / 14 only (the reference has no mode-13 backward)
+  if ((settings->render_mode >> 8) != 0 || (settings->render_mode & 0xFF) == 13) return NS_ERR_UNSUPPORTED;
   if (!surfels || !gi || !go) return NS_ERR_INVALID;
   const int P = surfels->P;
   if (P < 0 || num_rendered < 0) return NS_ERR_INVALID;

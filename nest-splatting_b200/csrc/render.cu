@@ -114,7 +114,10 @@ __device__ __forceinline__ float2 lookup_finish(const float (&f)[3], const Corne
 // the inference flag all channels from the surfel when wgt >= 0.9, else coarse
 // from the surfel and fine from the grid. Mode 14 (adaptive_zero, rows of
 // hybrid LD + 1): coarse from the surfel, fine wgt * hash (training: wgt > 1e-6;
-// inference: wgt >= 0.1, else zeros).
+// inference: wgt >= 0.1, else zeros). Mode 13 (adaptive_cat_fast, mode 12's
+// rows, :964-1091): with the inference flag all channels from the surfel when
+// wgt > 0.5, else coarse from the surfel and fine from the grid; without it
+// coarse wgt * surfel and fine as mode 12.
 __device__ __forceinline__ float mode_features(const RenderParams& p, uint32_t id, float w, float* acc,
                                                int t) {
   const int base = p.render_mode & 0xFF;
@@ -130,6 +133,20 @@ __device__ __forceinline__ float mode_features(const RenderParams& p, uint32_t i
   if (base == 4) {
     add(p.gauss + (size_t)id * pg, 0, pg, w);
     return p.L > 0 ? 1.0f : 0.0f;
+  }
+  if (base == 13) {
+    const int td = 2 * p.total_levels;
+    const float* g = p.gauss + (size_t)id * (td + 1);
+    const float wgt = __ldg(g + td);
+    if (infer && wgt > 0.5f) {
+      add(g, 0, td, w);
+      return 0.0f;
+    }
+    add(g, 0, pg, infer ? w : wgt * w);
+    if (p.L == 0) return 0.0f;
+    if (infer) return 1.0f;
+    add(g, pg, pg + hd, wgt * w);
+    return 1.0f - wgt;
   }
   if (base == 12) {
     const int td = 2 * p.total_levels;
@@ -407,9 +424,18 @@ __global__ void __launch_bounds__(kThreads, 2) blend_kernel(const RenderParams p
           } else {
             xyz = f3(q5.z, q5.w, q6.x);
           }
-          pos0 += w * xyz.x;
-          pos1 += w * xyz.y;
-          pos2 += w * xyz.z;
+          // Mode 13 (forward.cu:964-1091) skips the hit point of its fast path
+          // and, for every sample, the level colours, the transmittance record
+          // and the last-contributor update.
+          const bool m13 = kGeneral && (p.render_mode & 0xFF) == 13;
+          const bool fast13 = m13 && (p.render_mode >> 8) != 0 &&
+                              __ldg(p.gauss + (size_t)__float_as_uint(q6.z) * (2 * p.total_levels + 1) +
+                                    2 * p.total_levels) > 0.5f;
+          if (!fast13) {
+            pos0 += w * xyz.x;
+            pos1 += w * xyz.y;
+            pos2 += w * xyz.z;
+          }
 
           // query_feature's mapping of the hit point to [0,1]^3 (hashgrid.h:63-114).
           const uint32_t apl = __float_as_uint(q3.w);
@@ -441,6 +467,10 @@ __global__ void __launch_bounds__(kThreads, 2) blend_kernel(const RenderParams p
           S.lvl[cnt][t] = (uint8_t)((oob || hw == 0.0f) ? 0u : min(apl, L));
           cnt++;
 
+          if (m13) {
+            T = test_T;
+            continue;
+          }
           float ac0, ac1;
           if (apl <= 4) {
             ac0 = (float)((apl - 2) * 0.5);

@@ -11,7 +11,7 @@ level_dim 2, the Gaussian splat kernel (kernel_type 0) and the beta / flex /
 general kernels (kernel_type 1-3, per-surfel `shapes`, whose gradient comes back
 in shapes' slot), forward and backward; render modes 4 (cat), 12 (adaptive_cat)
 and 14 (adaptive_zero), forward (also with the inference flag 256) and backward
-(training rules; the per-surfel rows' gradient, blend weight included, comes
+(training rules; mode 13, adaptive_cat_fast, forward only as in the reference; the per-surfel rows' gradient, blend weight included, comes
 back in colors_precomp's slot), the per-surfel features read from
 colors_precomp and the level word hashgrid_settings.L = total << 16 | active << 8
 | hybrid as the reference's renderer encodes it (gaussian_renderer/__init__.py:
@@ -80,9 +80,9 @@ class _RasterizeGaussians(torch.autograd.Function):
                 gridrange_diffuse, raster_settings, hashgrid_settings, render_mode, shapes, kernel_type):
         mode = int(render_mode)
         base_mode = mode & 0xFF
-        if base_mode not in (0, 4, 12, 14) or (mode >> 8) > 1 or ((mode >> 8) and base_mode == 4):
+        if base_mode not in (0, 4, 12, 13, 14) or (mode >> 8) > 1 or ((mode >> 8) and base_mode == 4):
             raise NotImplementedError(f"render_mode {render_mode}: 0 (baseline hash grid), 4 (cat), "
-                                      f"12 (adaptive_cat), 14 (adaptive_zero) are built")
+                                      f"12 (adaptive_cat), 13 (adaptive_cat_fast), 14 (adaptive_zero) are built")
         if int(kernel_type) not in (0, 1, 2, 3):
             raise NotImplementedError(f"kernel_type {kernel_type}: 0-3 are built")
         shp = _nonempty(shapes)
@@ -157,9 +157,9 @@ class _RasterizeGaussians(torch.autograd.Function):
 
     @staticmethod
     def backward(ctx, grad_out_color, grad_radii, grad_depth, grad_0, grad_1):
-        if (ctx.cfg.render_mode >> 8) != 0:
-            raise NotImplementedError(f"backward of render_mode {ctx.cfg.render_mode}: the inference flag "
-                                      f"has no backward (training rules only)")
+        if (ctx.cfg.render_mode >> 8) != 0 or (ctx.cfg.render_mode & 0xFF) == 13:
+            raise NotImplementedError(f"backward of render_mode {ctx.cfg.render_mode}: the inference flag and "
+                                      f"mode 13 have no backward (the reference's has none either)")
         dev = ctx.radii.device
         H, W = ctx.cfg.image_height, ctx.cfg.image_width
         if grad_out_color is None:

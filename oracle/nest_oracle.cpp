@@ -50,6 +50,25 @@ void mode_feature(float* feat, int C, int LD, int render_mode, int hybrid_levels
           feat[pg + i] = infer ? hf[i] : wgt * g[pg + i] + (1.0f - wgt) * hf[i];
       }
     }
+  } else if (base == 13) {  // :964-1091
+    const int td = total_levels * LD;
+    const float* g = gauss + (size_t)id * (td + 1);
+    const float wgt = g[td];
+    if (infer && wgt > 0.5f) {
+      for (int i = 0; i < td && i < C; i++) feat[i] = g[i];
+    } else if (infer) {
+      for (int i = 0; i < pg && i < C; i++) feat[i] = g[i];
+      if (L > 0) {
+        query();
+        for (int i = 0; i < hd && pg + i < C; i++) feat[pg + i] = hf[i];
+      }
+    } else {
+      for (int i = 0; i < pg && i < C; i++) feat[i] = g[i] * wgt;
+      if (L > 0) {
+        query();
+        for (int i = 0; i < hd && pg + i < C; i++) feat[pg + i] = wgt * g[pg + i] + (1.0f - wgt) * hf[i];
+      }
+    }
   } else if (base == 14) {  // :1701-1790
     const float* g = gauss + (size_t)id * (pg + 1);
     const float wgt = g[pg];
@@ -194,7 +213,10 @@ int64_t oracle_bin(int P, const float* means2D, const float* depths, const int* 
 // render_mode (base | inference flag << 8): 0, or the modes that combine
 // per-surfel features `gauss` (colors_precomp) with the hash grid's L levels at
 // channel hybrid_levels * LD: 4 cat (:1218-1282), 12 adaptive_cat (:1593-1700),
-// 14 adaptive_zero (:1701-1790); see mode_feature().
+// 13 adaptive_cat_fast (:964-1091), 14 adaptive_zero (:1701-1790); see
+// mode_feature(). Mode 13 leaves out the hit point of its fast path and, for
+// every sample, the level colours, the transmittance record and the
+// last-contributor update (its `continue` at :1088-1090).
 void oracle_render(int W, int H, const uint32_t* ranges, const uint32_t* point_list,
                    const float* means2D, const float* transMat, const float* normal_opacity,
                    const float* homotrans, const float* ap_level, const float* table,
@@ -287,9 +309,14 @@ void oracle_render(int W, int H, const uint32_t* ranges, const uint32_t* point_l
           } else {
             xyz = pk;
           }
-          pos[0] += w * xyz.x;
-          pos[1] += w * xyz.y;
-          pos[2] += w * xyz.z;
+          const bool m13 = (render_mode & 0xFF) == 13;
+          const bool fast13 = m13 && ((render_mode >> 8) & 1) &&
+                              gauss[(size_t)id * (total_levels * LD + 1) + total_levels * LD] > 0.5f;
+          if (!fast13) {
+            pos[0] += w * xyz.x;
+            pos[1] += w * xyz.y;
+            pos[2] += w * xyz.z;
+          }
           uint32_t apl = (uint32_t)std::floor(ap_level[id]);
           if ((render_mode & 0xFF) == 0) {
             query_feature(feat.data(), C, LD, xyz, vmin, vmax, offsets, apl, table, L, S, Hres,
@@ -303,6 +330,10 @@ void oracle_render(int W, int H, const uint32_t* ranges, const uint32_t* point_l
                          hf.data(), query);
           }
           for (int c = 0; c < C; c++) Cacc[c] += feat[c] * w;
+          if (m13) {
+            T = T * (1 - alpha);
+            continue;
+          }
           float apc[3] = {0, 0, 0};
           if (apl <= 4) { apc[0] = (float)((apl - 2) * 0.5); apc[1] = 1.0f; }
           else { apc[0] = 1.0f; apc[1] = (float)(1.0 - (apl - 4) * 0.5); }

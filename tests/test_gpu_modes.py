@@ -32,7 +32,7 @@ def mode_case(mode, total, hybrid, active, seed, weights="uniform"):
     if base == 4:
         gauss = torch.rand(P, hybrid * LD, generator=g) * 2 - 1
     else:
-        width = total * LD if base == 12 else hybrid * LD
+        width = total * LD if base in (12, 13) else hybrid * LD
         feats = torch.rand(P, width, generator=g) * 2 - 1
         if weights == "uniform":
             wgt = torch.rand(P, 1, generator=g)
@@ -90,6 +90,8 @@ def run_mode(sc, inp, grid, gauss, mode, total, hybrid, active):
     (14, 16, 6, 10, "thresholds"),
     (14 | 256, 16, 6, 10, "thresholds"),
     (14, 16, 16, 0, "uniform"),
+    (13, 16, 6, 10, "uniform"),
+    (13 | 256, 16, 6, 10, "thresholds"),
 ])
 def test_render_modes_match_oracle(mode, total, hybrid, active, weights):
     sc, inp, grid, gauss = mode_case(mode, total, hybrid, active, seed=50 + (mode & 0xFF), weights=weights)
