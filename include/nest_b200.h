@@ -101,14 +101,15 @@ typedef struct ns_raster_settings {
    * run to run; needs ns_backward_scratch_bytes_deterministic. 0: float atomics,
    * whose summation order varies, as in the reference. */
   int32_t deterministic;
-  /* Render mode (forward.cu:1126-1824; base | inference flag << 8): 0 baseline
+  /* Render mode (forward.cu:964-1824; base | inference flag << 8): 0 baseline
    * hash grid; 4 cat: per-surfel features (hybrid_levels levels) then the hash
-   * grid's `levels` levels; 12 adaptive_cat and 14 adaptive_zero: per-surfel
-   * features blended with the hash levels by a per-surfel weight (flag 256:
-   * inference rules). hybrid_levels / total_levels: the reference's level
-   * encoding (total << 16 | active << 8 | hybrid) split out; `levels` is the
-   * number of hash levels queried. ns_rasterize_backward takes 0, 4, 12 and 14
-   * without the inference flag (training rules); ns_render_frame takes 0. */
+   * grid's `levels` levels; 12 adaptive_cat, 13 adaptive_cat_fast and 14
+   * adaptive_zero: per-surfel features blended with the hash levels by a
+   * per-surfel weight (flag 256: inference rules). hybrid_levels / total_levels:
+   * the reference's level encoding (total << 16 | active << 8 | hybrid) split
+   * out; `levels` is the number of hash levels queried. ns_rasterize_backward
+   * takes 0, 4, 12 and 14 without the inference flag (training rules; the
+   * reference has no mode-13 backward); ns_render_frame takes 0. */
   int32_t render_mode;
   uint32_t hybrid_levels;
   uint32_t total_levels;
