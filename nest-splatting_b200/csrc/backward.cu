@@ -42,6 +42,7 @@ namespace {
 
 constexpr int kThreads = kTilePixels;
 constexpr int kWarps = kThreads / 32;
+constexpr int kBatch = 256;     // records per batch (gathered back to front, one per thread)
 constexpr int kQueue = 4;       // queued samples per pixel between drains
 constexpr int kGradWords = 20;  // per-surfel accumulator words (18 used), 80 bytes
 constexpr float kAggScale = 128.f;  // table-gradient aggregation below this level resolution
@@ -95,14 +96,14 @@ enum : int {
 };
 
 struct BwSmem {
-  float4 rec[kThreads][kRecordFloat4];  // records of the batch, back to front
+  float4 rec[kBatch][kRecordFloat4];    // records of the batch, back to front
   float g[kThreads * kAccStride];       // dL/dcolor per pixel (acc_pair layout)
   float4 samp[kQueue][kThreads];        // (hit in [0,1]^3, alpha T) -> (f, dL/dhit)
   float Ts[kQueue][kThreads];           // T at the sample
   uint8_t jj[kQueue][kThreads];         // record of the sample
   uint8_t lvl[kQueue][kThreads];        // levels to query
   uint8_t item[kWarps][kQueue * 32];    // per warp: samples in k-major order, (k << 5) | lane
-  uint32_t ids[kThreads];
+  uint32_t ids[kBatch];
   uint32_t wmax[kWarps];
   float pix[kPxWords][kThreads];        // per-pixel constants of phase C
   float Pm[9];                          // P[k][r], k = T column, r = 0..2
@@ -265,7 +266,7 @@ __global__ void __launch_bounds__(kThreads, 2) blend_backward_kernel(const Backw
   for (int w = 0; w < kWarps; w++) maxlc = max(maxlc, S.wmax[w]);
   const uint2 range = p.ranges[tile];
   const int total = (int)maxlc;
-  const int rounds = div_up(total, kThreads);
+  const int rounds = div_up(total, kBatch);
 
   // Back-to-front recursions of the reference (scalar colour term: the
   // feature vector only enters through f = feat . dL/dcolor).
@@ -274,8 +275,8 @@ __global__ void __launch_bounds__(kThreads, 2) blend_backward_kernel(const Backw
   float ln0 = 0.f, ln1 = 0.f, ln2 = 0.f, an0 = 0.f, an1 = 0.f, an2 = 0.f;
 
   for (int r = 0; r < rounds; r++) {
-    const int hi = total - r * kThreads;
-    const int lo = max(0, hi - kThreads);
+    const int hi = total - r * kBatch;
+    const int lo = max(0, hi - kBatch);
     const int todo = hi - lo;
     if (t < todo) {
       const uint32_t id = p.point_list[range.x + hi - 1 - t];

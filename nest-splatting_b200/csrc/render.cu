@@ -45,7 +45,7 @@ namespace {
 constexpr int kThreads = kTilePixels;  // 256: one pixel per thread
 constexpr int kQueue = 8;              // queued samples per pixel between drains
 constexpr int kWarps = kThreads / 32;
-constexpr int kBatch = 64;             // surfel records per ring slot
+constexpr int kBatch = 32;             // surfel records per ring slot
 constexpr int kSlots = 4;              // ring slots (batches in flight)
 constexpr int kChunk = 64;             // compacted samples looked up per warp step (2 per lane)
 constexpr int kMaxChannels = 32;
