@@ -86,6 +86,20 @@ def test_raster_small_scene_matches_oracle(fp16):
     assert allmap[7].sum() > 1000  # the scene really blends samples
 
 
+def test_raster_large_tilted_surfels_match_oracle():
+    """Surfels a few times larger (median radius ~80 px in a 100x70 image): for
+    dozens of them the alpha-cutoff disc reaches the camera plane, so its image
+    is unbounded and the tile box must fall back to the reference rectangle;
+    the rest take the tight ellipse box."""
+    sc = small_scene(seed=19, log_scale=-0.5)
+    inp = api_inputs(sc)
+    out, pre, n = oracle_render(sc, inp)
+    color, radii, allmap, _, _ = run_api(sc, inp)
+    assert (radii == pre["radii"]).mean() > 0.999
+    compare(out, color, allmap)
+    assert allmap[7].sum() > 10000
+
+
 def test_raster_partial_levels_and_transmittance():
     sc = small_scene(n=1500, seed=12)
     inp = api_inputs(sc)
