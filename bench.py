@@ -217,16 +217,25 @@ def run_ours(args):
     proj = cam.full_proj_transform.to(dev).contiguous()
     P = sc.P
     from nest_b200 import raster
-    from nest_b200.views import DecodeShard, shard_range
+    from nest_b200.views import DecodeRing, DecodeShard, shard_range
     lo, hi = shard_range(P, world, rank)
     if world > 1:
         shard = DecodeShard.create(fr.rvq_idx, fr.dims, world, rank)
-        fr.decoded = shard.decoded  # the frame reads the gathered rows
+        # Frame i+1's decode + all-gather runs on a side stream while frame i
+        # renders (two attribute buffers); every step still decodes and
+        # exchanges its own frame.
+        ring = DecodeRing(fr.rvq_idx, fr.dims, world, rank)
 
-    def step(events=None):
+    def step(i, events=None, n=None):
         if world > 1:
-            shard.decode_and_gather(fr.codebooks, raster.rvq_decode)
-            return fr.render(cam, view, proj, events=events, skip_decode=True)
+            if i == 0:
+                ring.prefetch(0, fr.codebooks, raster.rvq_decode)
+            if n is None or i + 1 < n:
+                ring.prefetch(i + 1, fr.codebooks, raster.rvq_decode)
+            fr.decoded = ring.acquire(i)
+            out = fr.render(cam, view, proj, events=events, skip_decode=True)
+            ring.release(i)
+            return out
         return fr.render(cam, view, proj, events=events)
 
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
@@ -235,26 +244,39 @@ def run_ours(args):
     for evs in stage_ev:
         for e in evs:
             e.record()  # creates the underlying cudaEvent
-    for _ in range(max(args.warmup, 3)):
-        step()
+    nw = max(args.warmup, 3)
+    for i in range(nw):
+        step(i, n=nw)
     torch.cuda.synchronize()
     starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    flush_start = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     launches0 = lib.ns_kernel_launches()
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
     with ClockSampler(local) as clk:
         for i in range(args.steps):
+            if world > 1 and i > 0:
+                ring.acquire(i)  # frame i's exchange is complete before the flush
+            flush_start[i].record()
             flush_l2(flush)
             starts[i].record()
-            step(stage_ev[i])
+            step(i, stage_ev[i], n=args.steps)
             ends[i].record()
         torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
     launches = lib.ns_kernel_launches() - launches0
-    step_ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
+    if world > 1:
+        # Frame i+1's exchange overlaps frame i's render, so the steps are timed
+        # as one sequence minus the L2 flushes between them; each flush starts
+        # only after the next frame's exchange has completed, and frame 0's
+        # exchange runs after the first flush, inside the timed interval.
+        step_ms = [flush_start[0].elapsed_time(ends[-1]) -
+                   sum(f.elapsed_time(s) for f, s in zip(flush_start, starts))]
+    else:
+        step_ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
     stage_ms = {name: statistics.mean(ev[2 * k].elapsed_time(ev[2 * k + 1]) for ev in stage_ev)
                 for k, name in enumerate(_lib.STAGE_NAMES)}
     total_ms = sum(step_ms)

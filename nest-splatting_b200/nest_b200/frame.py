@@ -196,7 +196,7 @@ class FramePipeline:
             if sh is None:
                 fr.render(cam, self.cam[k][0], self.cam[k][1], rvq_idx=self.idx[k], rgb=self.rgb[k])
             else:
-                sh.decode_and_gather(fr.codebooks, _rvq_decode, idx=self.idx[k])
+                fr.decoded = sh.decode_and_gather(fr.codebooks, _rvq_decode, idx=self.idx[k])
                 fr.render(cam, self.cam[k][0], self.cam[k][1], skip_decode=True, rgb=self.rgb[k])
             self.ev_done[k].record(cs)
             with torch.cuda.stream(self.out_stream):

@@ -94,3 +94,49 @@ class DecodeShard:
         of the same shape), then the all-gather."""
         decode_fn(self.idx_shard if idx is None else idx, codebooks, out=self.dec_shard)
         return self.gather(group)
+
+
+class DecodeRing:
+    """Frame i's decode + all-gather overlapped with frame i-1's render.
+
+    Two DecodeShards (frames alternate between them) and, on CUDA, a side
+    stream: prefetch(i) enqueues frame i's decode and all-gather there, after
+    the render that last read the same buffer; acquire(i) makes the render
+    stream wait for it and returns the gathered rows; release(i) marks the
+    render of frame i as enqueued. Every rank calls prefetch in the same frame
+    order, so the collectives match. On CPU (gloo) the calls run in order.
+    """
+
+    def __init__(self, rvq_idx: torch.Tensor, dims: int, world: int, rank: int):
+        self.shards = [DecodeShard.create(rvq_idx, dims, world, rank) for _ in range(2)]
+        dev = rvq_idx.device
+        self.cuda = dev.type == "cuda"
+        if self.cuda:
+            self.stream = torch.cuda.Stream(device=dev)
+            self.ready = [torch.cuda.Event() for _ in range(2)]
+            self.free = [torch.cuda.Event() for _ in range(2)]
+        self.used = [False, False]
+
+    def prefetch(self, i: int, codebooks: torch.Tensor, decode_fn, group=None) -> None:
+        k = i % 2
+        sh = self.shards[k]
+        if not self.cuda:
+            sh.decode_and_gather(codebooks, decode_fn, group=group)
+            return
+        with torch.cuda.stream(self.stream):
+            if self.used[k]:
+                self.stream.wait_event(self.free[k])
+            sh.decode_and_gather(codebooks, decode_fn, group=group)
+            self.ready[k].record(self.stream)
+
+    def acquire(self, i: int, stream=None) -> torch.Tensor:
+        k = i % 2
+        if self.cuda:
+            (stream or torch.cuda.current_stream()).wait_event(self.ready[k])
+        return self.shards[k].decoded
+
+    def release(self, i: int, stream=None) -> None:
+        k = i % 2
+        if self.cuda:
+            self.free[k].record(stream or torch.cuda.current_stream())
+        self.used[k] = True

@@ -11,7 +11,7 @@ import torch.distributed as dist
 import torch.multiprocessing as mp
 
 from nest_b200 import synth
-from nest_b200.views import DecodeShard, camera_share, shard_range
+from nest_b200.views import DecodeRing, DecodeShard, camera_share, shard_range
 
 
 def _free_port():
@@ -43,6 +43,14 @@ def _worker(rank, world, port, n, result_dir):
         full = sh.decode_and_gather(cb, _decode_cpu).clone()
         sh.dec_full.zero_()
         alt = sh.gather_indices_and_decode(cb, _decode_cpu)
+        # DecodeRing (CPU: in order): frames alternate between two buffers.
+        ring = DecodeRing(idx, cb.shape[2], world, rank)
+        for i in range(3):
+            ring.prefetch(i, cb, _decode_cpu)
+            got = ring.acquire(i)
+            assert got.data_ptr() == ring.shards[i % 2].decoded.data_ptr()
+            assert torch.equal(got, full)
+            ring.release(i)
         torch.save({"full": full, "alt": alt.clone(), "views": camera_share(64, world, rank)},
                    os.path.join(result_dir, f"rank{rank}.pt"))
     finally:
