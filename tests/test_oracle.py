@@ -42,7 +42,7 @@ def test_hashed_index(x, y, z):
     assert oracle.grid_index(False, T19, res, x, y, z) == h % T19
 
 
-def test_level_resolutions_match_survey():
+def test_level_resolutions_and_dense_levels():
     # scale = exp2(l*S)*16 - 1, res = ceil(scale) + 1; dense iff (res+1)^3 <= 2^19
     S = math.log2(1.447)
     res = [math.ceil(np.float32(2.0 ** (l * S)) * 16 - 1) + 1 for l in range(16)]
