@@ -297,7 +297,7 @@ def run_ours(args):
     host_idx = sc.rvq_idx.clone().pin_memory()
     host_cam = torch.stack([cam.world_view_transform, cam.full_proj_transform]).contiguous().pin_memory()
     host_rgb = [torch.empty((3, H, W), dtype=torch.float32).pin_memory() for _ in range(2)]
-    pipe = FramePipeline(fr, shard if world > 1 else None)
+    pipe = FramePipeline(fr, shard if world > 1 else None, graphs=world == 1)
     run_args = (cam, lambda i: host_idx, lambda i: host_cam, lambda i: host_rgb[i % 2])
     pipe.run(2, *run_args)
     torch.cuda.synchronize()
@@ -321,6 +321,7 @@ def run_ours(args):
     d2h = host_rgb[0].numel() * 4
 
     exchange = exchange_timing(shard, fr.codebooks, dev, P, fr.stages, fr.dims) if world > 1 else None
+    graph = graph_timing(fr, cam, view, proj, flush, args.steps) if world == 1 else None
 
     # Work statistics of the (identical) frames.
     samples = float(fr.others[7].sum().item())
@@ -358,13 +359,15 @@ def run_ours(args):
         "e2e": {"value": round(world * mpix * 1000.0 / e2e_ms_step, 3), "unit": UNIT,
                 "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h),
                 "ms_per_step": round(e2e_ms_step, 4),
-                "timing": "one device-timed sequence of `steps` frames through FramePipeline, "
-                          "L2 flush before every frame included"},
+                "timing": "one device-timed sequence of `steps` frames through FramePipeline "
+                          "(one CUDA graph per frame at N=1), L2 flush before every frame included"},
         "gpu_launches": int(launches),
         "clocks": clk.summary(),
     }
     if exchange is not None:
         line["rvq_exchange"] = exchange
+    if graph is not None:
+        line["graph_frame"] = graph
     if not args.no_train:
         line["train_step"] = train_step_timing(sc, cam, dev, steps=min(args.steps, 10))
     if not args.no_multiview:
@@ -378,6 +381,32 @@ def run_ours(args):
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
+
+
+def graph_timing(fr, cam, view, proj, flush, steps):
+    """The same frame as one CUDA-graph launch (FrameGraph: device-side instance
+    count, no host sync inside the frame), timed like the value line."""
+    import torch
+
+    from nest_b200.frame import FrameGraph
+    fg = FrameGraph(fr, cam, view, proj)
+    for _ in range(3):
+        fg.replay()
+    torch.cuda.synchronize()
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+    for s, e in ev:
+        flush_l2(flush)
+        s.record()
+        fg.replay()
+        e.record()
+    torch.cuda.synchronize()
+    status = fg.status()
+    ms = sum(s.elapsed_time(e) for s, e in ev) / steps
+    mpix = cam.width * cam.height / 1e6
+    return {"ms_per_step": round(ms, 4), "value": round(mpix * 1000.0 / ms, 3), "unit": UNIT,
+            "device_status": int(status),
+            "note": "one graph launch per frame (decode, preprocess, binning with the device-side count, "
+                    "blend, MLP); L2 flushed between frames"}
 
 
 def exchange_timing(shard, codebooks, dev, P, stages, dims, iters=20):

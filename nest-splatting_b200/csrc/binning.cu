@@ -100,7 +100,7 @@ __global__ void __launch_bounds__(kDupThreads)
 duplicate_keys_kernel(int P, const uint32_t* __restrict__ order, const BinInfo* __restrict__ bin,
                       const uint32_t* __restrict__ tiles, const uint32_t* __restrict__ block_prefix,
                       int gx, uint32_t* __restrict__ keys, uint32_t* __restrict__ vals,
-                      int64_t capacity, uint32_t* __restrict__ err) {
+                      int64_t capacity, uint32_t* __restrict__ err, int64_t* __restrict__ count) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   uint32_t* sk = reinterpret_cast<uint32_t*>(smem_raw);
   uint32_t* sv = reinterpret_cast<uint32_t*>(sk + kDupStage);
@@ -112,7 +112,13 @@ duplicate_keys_kernel(int P, const uint32_t* __restrict__ order, const BinInfo* 
   const int64_t total = (int64_t)cta_scan(n, incl, warp_tot);
   const int64_t base = (int64_t)block_prefix[blockIdx.x];
   if (base + total > capacity) {  // uniform over the CTA
-    if (threadIdx.x == 0) set_error(err, kErrCapacity);
+    // Overflow: flag it and zero the instance count, so that the sort and the
+    // ranges that read the count on the device (device-count mode) see no
+    // instances instead of the unwritten part of the buffers.
+    if (threadIdx.x == 0) {
+      set_error(err, kErrCapacity);
+      *count = 0;
+    }
     return;
   }
   if (n) {
@@ -183,7 +189,7 @@ int duplicate_keys_launch(int P, const uint32_t* order, const BinInfo* bin, cons
   NS_CUDA_TRY(cudaFuncSetAttribute(duplicate_keys_kernel,
                                    cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
   duplicate_keys_kernel<<<nb, kDupThreads, smem, stream>>>(P, order, bin, tiles, sorted_prefix, gx,
-                                                           keys, vals, capacity, err);
+                                                           keys, vals, capacity, err, total);
   NS_LAUNCH_CHECK();
   return NS_OK;
 }

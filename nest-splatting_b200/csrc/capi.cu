@@ -211,18 +211,22 @@ int bin_and_render(const ns_raster_settings* st, int P, const GeomState& g, cons
   if (rc) return rc;
   const int64_t cap = bin_capacity(binning_bytes);
   if (cap < 0) return NS_ERR_SCRATCH;
-  if (flags & NS_FLAG_DEVICE_COUNT) return NS_ERR_UNSUPPORTED;
+  const bool device_count = (flags & NS_FLAG_DEVICE_COUNT) != 0;
   // Binning step 1, the depth sort of the surfels, runs while the host waits
   // for the instance count.
   rc = radix_sort32_launch(g.depth_keys, g.depth_vals, g.depth_keys_sorted, g.depth_vals_sorted,
                          g.depth_keys_alt, g.depth_vals_alt, P, 32, g.depth_sort_temp,
                          g.depth_sort_temp_bytes, stream);
   if (rc) return rc;
-  int64_t count = 0;
-  NS_CUDA_TRY(cudaMemcpyAsync(&count, g.count, sizeof(int64_t), cudaMemcpyDeviceToHost, stream));
-  NS_CUDA_TRY(cudaStreamSynchronize(stream));
-  if (num_rendered) *num_rendered = count;
-  if (count > cap) return NS_ERR_CAPACITY;
+  int64_t count = cap;  // device-count mode: the tile sort and ranges are sized by the capacity
+  if (!device_count) {
+    NS_CUDA_TRY(cudaMemcpyAsync(&count, g.count, sizeof(int64_t), cudaMemcpyDeviceToHost, stream));
+    NS_CUDA_TRY(cudaStreamSynchronize(stream));
+    if (num_rendered) *num_rendered = count;
+    if (count > cap) return NS_ERR_CAPACITY;
+  } else if (num_rendered) {
+    *num_rendered = -1;  // on the device only (g.count); overflow sets the device error word
+  }
   BinState b = carve_bin(binning, cap, nullptr);
   rc = duplicate_keys_launch(P, g.depth_vals_sorted, g.bin, g.tiles, g.sorted_sums,
                              g.sorted_prefix, g.count, gx, b.keys_unsorted, b.vals_unsorted, cap,
@@ -230,10 +234,11 @@ int bin_and_render(const ns_raster_settings* st, int P, const GeomState& g, cons
   if (rc) return rc;
   const int end_bit = (int)higher_msb((uint32_t)tiles);
   rc = radix_sort32_launch(b.keys_unsorted, b.vals_unsorted, b.keys_sorted, b.vals_sorted, b.keys_alt,
-                         b.vals_alt, count, end_bit, b.sort_temp, b.sort_temp_bytes, stream);
+                         b.vals_alt, count, end_bit, b.sort_temp, b.sort_temp_bytes, stream,
+                         device_count ? g.count : nullptr);
   if (rc) return rc;
-  rc = identify_ranges_launch(b.keys_sorted, nullptr, count, cap, im.ranges, tiles, num_sms(),
-                              stream);
+  rc = identify_ranges_launch(b.keys_sorted, device_count ? g.count : nullptr, count, cap, im.ranges,
+                              tiles, num_sms(), stream);
   if (rc) return rc;
   if (ev) NS_CUDA_TRY(cudaEventRecord((cudaEvent_t)ev[5], stream));
   RenderParams rp;

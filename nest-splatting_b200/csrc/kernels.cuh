@@ -113,7 +113,8 @@ int radix_sort_launch(const uint64_t* keys_in, const uint32_t* vals_in, uint64_t
                       int end_bit, void* temp, size_t temp_bytes, cudaStream_t stream);
 int radix_sort32_launch(const uint32_t* keys_in, const uint32_t* vals_in, uint32_t* keys_out,
                         uint32_t* vals_out, uint32_t* keys_alt, uint32_t* vals_alt, int64_t n,
-                        int end_bit, void* temp, size_t temp_bytes, cudaStream_t stream);
+                        int end_bit, void* temp, size_t temp_bytes, cudaStream_t stream,
+                        const int64_t* n_dev = nullptr);
 uint32_t* radix_sort_error_word(void* temp);
 int render_launch(const RenderParams& p, int fp16, cudaStream_t stream);
 int mlp_launch(const float* feat, int in_dims, int64_t npix, const uint16_t* weights, int hidden,

@@ -83,9 +83,11 @@ __device__ __forceinline__ uint32_t load_volatile(const uint32_t* p) {
 constexpr int kHistThreads = 256;
 template <typename KeyT>
 __global__ void __launch_bounds__(kHistThreads) upfront_histogram_kernel(const KeyT* __restrict__ keys,
-                                                                         int64_t n, int passes,
+                                                                         int64_t n, const int64_t* n_dev,
+                                                                         int passes,
                                                                          uint32_t* __restrict__ hist) {
   extern __shared__ uint32_t hw[];  // [warps][passes][kRadix]
+  if (n_dev) n = min(*n_dev, n);  // device-side count, at most the launch capacity
   const int w = threadIdx.x >> 5;
   const int words = (kHistThreads / 32) * passes * kRadix;
   for (int i = threadIdx.x; i < words; i += blockDim.x) hw[i] = 0;
@@ -160,7 +162,7 @@ template <typename KeyT>
 __global__ void __launch_bounds__(kSortThreads)
 onesweep_pass_kernel(const KeyT* __restrict__ keys_in, const uint32_t* __restrict__ vals_in,
                      KeyT* __restrict__ keys_out, uint32_t* __restrict__ vals_out, int64_t n,
-                     int shift, const uint32_t* __restrict__ bucket_base,
+                     const int64_t* n_dev, int shift, const uint32_t* __restrict__ bucket_base,
                      const uint32_t* __restrict__ bucket_count, const uint32_t* __restrict__ nz_digits,
                      uint32_t* status, uint32_t* tile_ctr, uint32_t* err) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
@@ -171,6 +173,11 @@ onesweep_pass_kernel(const KeyT* __restrict__ keys_in, const uint32_t* __restric
   for (int i = lane; i < kRadix; i += 32) S.warp_hist[w][i] = 0;
   __syncthreads();
   const uint32_t tile = S.tile;
+  // Device-side count: the grid covers the capacity; tiles past the count
+  // leave at once (tiles are numbered in launch order, and a tile only looks
+  // back at lower tiles, so no tile waits for one that left).
+  if (n_dev) n = min(*n_dev, n);
+  if ((int64_t)tile >= sort_tiles(n)) return;
   const int64_t tile_base = (int64_t)tile * kSortTile;
 
   KeyT key[kSortItems];
@@ -286,7 +293,7 @@ onesweep_pass_kernel(const KeyT* __restrict__ keys_in, const uint32_t* __restric
 template <typename KeyT>
 int radix_sort_impl(const KeyT* keys_in, const uint32_t* vals_in, KeyT* keys_out, uint32_t* vals_out,
                     KeyT* keys_alt, uint32_t* vals_alt, int64_t n, int end_bit, void* temp,
-                    size_t temp_bytes, cudaStream_t stream) {
+                    size_t temp_bytes, cudaStream_t stream, const int64_t* n_dev) {
   if (n < 0 || end_bit < 0 || end_bit > (int)(8 * sizeof(KeyT))) return NS_ERR_INVALID;
   if (n >= (int64_t)kValueMask) return NS_ERR_UNSUPPORTED;
   if (temp_bytes < sort_temp_words(n) * sizeof(uint32_t)) return NS_ERR_SCRATCH;
@@ -306,8 +313,8 @@ int radix_sort_impl(const KeyT* keys_in, const uint32_t* vals_in, KeyT* keys_out
   if (hsmem > 48 * 1024)
     NS_CUDA_TRY(cudaFuncSetAttribute(upfront_histogram_kernel<KeyT>,
                                      cudaFuncAttributeMaxDynamicSharedMemorySize, (int)hsmem));
-  upfront_histogram_kernel<KeyT><<<max(1, hblocks), kHistThreads, hsmem, stream>>>(keys_in, n, passes,
-                                                                                  T.hist);
+  upfront_histogram_kernel<KeyT><<<max(1, hblocks), kHistThreads, hsmem, stream>>>(keys_in, n, n_dev,
+                                                                                  passes, T.hist);
   NS_LAUNCH_CHECK();
   bucket_scan_kernel<<<passes, kRadix, 0, stream>>>(T.hist, T.count, T.nz, passes);
   NS_LAUNCH_CHECK();
@@ -322,7 +329,7 @@ int radix_sort_impl(const KeyT* keys_in, const uint32_t* vals_in, KeyT* keys_out
     KeyT* kout = to_out ? keys_out : keys_alt;
     uint32_t* vout = to_out ? vals_out : vals_alt;
     onesweep_pass_kernel<KeyT><<<(unsigned)tiles, kSortThreads, smem, stream>>>(
-        kin, vin, kout, vout, n, p * kRadixBits, T.hist + p * kRadix, T.count + p * kRadix,
+        kin, vin, kout, vout, n, n_dev, p * kRadixBits, T.hist + p * kRadix, T.count + p * kRadix,
         T.nz + p, T.status + (size_t)p * tiles * kRadix, T.tile_ctr + p, T.err);
     NS_LAUNCH_CHECK();
     kin = kout;
@@ -341,15 +348,18 @@ int radix_sort_launch(const uint64_t* keys_in, const uint32_t* vals_in, uint64_t
                       uint32_t* vals_out, uint64_t* keys_alt, uint32_t* vals_alt, int64_t n,
                       int end_bit, void* temp, size_t temp_bytes, cudaStream_t stream) {
   return radix_sort_impl<uint64_t>(keys_in, vals_in, keys_out, vals_out, keys_alt, vals_alt, n,
-                                   end_bit, temp, temp_bytes, stream);
+                                   end_bit, temp, temp_bytes, stream, nullptr);
 }
 
 // The same for 32-bit keys (end_bit <= 32): two thirds of the traffic per pass.
+// n_dev (optional): the number of pairs as a device value, at most n; the
+// launches are sized by n and read the count on the device (no host sync).
 int radix_sort32_launch(const uint32_t* keys_in, const uint32_t* vals_in, uint32_t* keys_out,
                         uint32_t* vals_out, uint32_t* keys_alt, uint32_t* vals_alt, int64_t n,
-                        int end_bit, void* temp, size_t temp_bytes, cudaStream_t stream) {
+                        int end_bit, void* temp, size_t temp_bytes, cudaStream_t stream,
+                        const int64_t* n_dev) {
   return radix_sort_impl<uint32_t>(keys_in, vals_in, keys_out, vals_out, keys_alt, vals_alt, n,
-                                   end_bit, temp, temp_bytes, stream);
+                                   end_bit, temp, temp_bytes, stream, n_dev);
 }
 
 // Address of the sort's device error word inside temp (for status reads).

@@ -47,6 +47,7 @@ class FrameRenderer:
         self.bg = (C.c_float * 3)(*[float(x) for x in bg])
         self._out_shape = None
         self.num_rendered = 0
+        self._extra_flags = 0
 
     def _outputs(self, cam: Camera):
         shape = (cam.height, cam.width)
@@ -113,7 +114,7 @@ class FrameRenderer:
             assert len(events) == 2 * _lib.NS_FRAME_STAGES
             ev_arr = (C.c_void_p * len(events))(*[e.cuda_event for e in events])
             fin.stage_events = C.cast(ev_arr, C.c_void_p)
-        flags = _lib.NS_FLAG_SKIP_DECODE if skip_decode else 0
+        flags = (_lib.NS_FLAG_SKIP_DECODE if skip_decode else 0) | self._extra_flags
         fout = _lib.FrameOutputs()
         fout.rgb, fout.out_color = ptr(rgb_t), ptr(self.features)
         fout.out_others, fout.radii = ptr(self.others), ptr(self.radii)
@@ -121,6 +122,12 @@ class FrameRenderer:
         image = self.scratch.image_buf(cam.width, cam.height, self.device)
         stream = _lib.stream_handle(self.device)
         n = C.c_int64(0)
+        if self._extra_flags & _lib.NS_FLAG_DEVICE_COUNT:
+            binning = self.scratch.bins(self.capacity, self.device)
+            check("ns_render_frame", lib.ns_render_frame(
+                C.byref(st), C.byref(fin), C.byref(fout), geom.data_ptr(), geom.numel(), binning.data_ptr(),
+                binning.numel(), image.data_ptr(), image.numel(), C.byref(n), flags, stream))
+            return rgb_t
         for _ in range(2):
             binning = self.scratch.bins(self.capacity, self.device)
             rc = lib.ns_render_frame(C.byref(st), C.byref(fin), C.byref(fout), geom.data_ptr(),
@@ -145,11 +152,16 @@ class FramePipeline:
     events; every frame still copies its own inputs in and its image out.
     With a DecodeShard (several ranks), each rank copies its own rows of the
     index stream and the frame decodes them and all-gathers the attributes.
+    graphs=True (single rank): each buffer set's frame is a FrameGraph, so no
+    frame waits for the host and the host never waits inside a frame.
     """
 
-    def __init__(self, renderer: FrameRenderer, shard=None, depth: int = 2):
+    def __init__(self, renderer: FrameRenderer, shard=None, depth: int = 2, graphs: bool = False):
         self.fr = renderer
         self.shard = shard
+        if graphs and shard is not None:
+            raise ValueError("graphs=True renders unsharded frames only")
+        self.graphs = [] if graphs else None
         d = renderer.device
         self.in_stream = torch.cuda.Stream(device=d)
         self.out_stream = torch.cuda.Stream(device=d)
@@ -193,7 +205,12 @@ class FramePipeline:
                 cs.wait_event(self.ev_host[k])
             if before_frame is not None:
                 before_frame(i)
-            if sh is None:
+            if self.graphs is not None:
+                if len(self.graphs) <= k:
+                    self.graphs.append(FrameGraph(fr, cam, self.cam[k][0], self.cam[k][1], rvq_idx=self.idx[k],
+                                                  rgb=self.rgb[k]))
+                self.graphs[k].replay()
+            elif sh is None:
                 fr.render(cam, self.cam[k][0], self.cam[k][1], rvq_idx=self.idx[k], rgb=self.rgb[k])
             else:
                 fr.decoded = sh.decode_and_gather(fr.codebooks, _rvq_decode, idx=self.idx[k])
@@ -209,3 +226,51 @@ class FramePipeline:
 def _rvq_decode(idx, codebooks, out=None):
     from .raster import rvq_decode
     return rvq_decode(idx, codebooks, out=out)
+
+
+class FrameGraph:
+    """One frame recorded as a CUDA graph and replayed on the current stream.
+
+    The frame runs with the device-side instance count (NS_FLAG_DEVICE_COUNT):
+    binning never reads the count back, so nothing in the frame waits for the
+    host and the whole decode -> preprocess -> binning -> blend -> MLP sequence
+    replays as one graph launch. The binning buffers are sized from an ordinary
+    frame of the same camera times `headroom`; a frame that outgrows them sets
+    the device error word (ns_read_device_status) and renders nothing.
+    Inputs are read from the renderer's buffers (rvq_idx, or `decoded` with
+    skip_decode) and the given view / projection tensors, in place; the image
+    lands in renderer.rgb.
+    """
+
+    def __init__(self, renderer: FrameRenderer, cam: Camera, view: torch.Tensor, proj: torch.Tensor,
+                 skip_decode: bool = False, headroom: float = 1.5, rvq_idx: torch.Tensor | None = None,
+                 rgb: torch.Tensor | None = None):
+        fr = self.fr = renderer
+        kw = dict(skip_decode=skip_decode, rvq_idx=rvq_idx, rgb=rgb)
+        fr.render(cam, view, proj, **kw)  # sizes the buffers (host count)
+        fr.capacity = max(fr.capacity, int(fr.num_rendered * headroom) + 1024)
+        fr.scratch.bins(fr.capacity, fr.device)
+        fr._extra_flags = _lib.NS_FLAG_DEVICE_COUNT
+        try:
+            side = torch.cuda.Stream(device=fr.device)
+            side.wait_stream(torch.cuda.current_stream(fr.device))
+            with torch.cuda.stream(side):
+                fr.render(cam, view, proj, **kw)  # first device-count frame, uncaptured
+            torch.cuda.current_stream(fr.device).wait_stream(side)
+            torch.cuda.synchronize(fr.device)
+            self.graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(self.graph, stream=side):
+                fr.render(cam, view, proj, **kw)
+        finally:
+            fr._extra_flags = 0
+        self.rgb = fr.rgb if rgb is None else rgb
+
+    def replay(self) -> torch.Tensor:
+        self.graph.replay()
+        return self.rgb
+
+    def status(self) -> int:
+        """Reads and clears the frame's device error word (syncs the stream)."""
+        lib = _lib.load()
+        geom = self.fr.scratch.geom
+        return lib.ns_read_device_status(geom.data_ptr(), self.fr.P, _lib.stream_handle(self.fr.device))

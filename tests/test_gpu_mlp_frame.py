@@ -78,9 +78,11 @@ def test_fused_frame_repeatable_and_index_upload():
     assert torch.equal(a, b)
 
 
-def test_frame_pipeline_sequence_matches_single_frames():
+@pytest.mark.parametrize("graphs", [False, True])
+def test_frame_pipeline_sequence_matches_single_frames(graphs):
     """FramePipeline: every frame's image, copied back to the host, equals the same
-    frame rendered alone (frames alternate between two index streams and cameras)."""
+    frame rendered alone (frames alternate between two index streams and cameras;
+    graphs=True replays one captured frame per buffer set)."""
     from nest_b200.camera import orbit_camera
     from nest_b200.frame import FramePipeline
 
@@ -99,8 +101,52 @@ def test_frame_pipeline_sequence_matches_single_frames():
                 for c in cams]
     n = 7
     host_rgb = [torch.empty((3, H, W)).pin_memory() for _ in range(n)]
-    pipe = FramePipeline(fr)
+    pipe = FramePipeline(fr, graphs=graphs)
     pipe.run(n, cams[0], lambda i: host_idx[i % 2], lambda i: host_cam[i % 2], lambda i: host_rgb[i])
     torch.cuda.synchronize()
     for i in range(n):
         assert torch.equal(host_rgb[i], ref[i % 2]), i
+
+
+def test_frame_graph_replays_the_frame():
+    """FrameGraph: the frame with the device-side instance count, captured as a
+    CUDA graph, gives the same image bits as the host-count frame, also after
+    new indices are uploaded into the captured buffer."""
+    from nest_b200.frame import FrameGraph
+    sc = small_scene(n=2500, seed=21, rvq=True)
+    fr = FrameRenderer(sc)
+    cam = sc.camera
+    view = cam.world_view_transform.cuda().contiguous()
+    proj = cam.full_proj_transform.cuda().contiguous()
+    ref = fr.render(cam, view, proj).clone()
+    graph = FrameGraph(fr, cam, view, proj)
+    out = graph.replay().clone()
+    torch.cuda.synchronize()
+    assert graph.status() == 0
+    assert torch.equal(out, ref) and ref.abs().sum() > 0
+    g = torch.Generator().manual_seed(5)
+    new_idx = torch.randint(0, sc.codebooks.shape[1], sc.rvq_idx.shape, generator=g).to(torch.uint8)
+    fr.upload_indices(new_idx.cuda())
+    out2 = graph.replay().clone()
+    ref2 = fr.render(cam, view, proj).clone()
+    torch.cuda.synchronize()
+    assert torch.equal(out2, ref2) and not torch.equal(out2, ref)
+
+
+def test_device_count_overflow_reports_error():
+    """Device-count mode with binning buffers too small: the frame renders no
+    instances and the device error word reports it (no host check in between)."""
+    from nest_b200 import _lib
+    sc = small_scene(n=2500, seed=21, rvq=True)
+    fr = FrameRenderer(sc, capacity=100)
+    cam = sc.camera
+    fr._extra_flags = _lib.NS_FLAG_DEVICE_COUNT
+    try:
+        rgb = fr.render(cam).clone()
+    finally:
+        fr._extra_flags = 0
+    lib = _lib.load()
+    st = lib.ns_read_device_status(fr.scratch.geom.data_ptr(), fr.P, _lib.stream_handle(fr.device))
+    assert st == _lib.NS_ERR_DEVICE
+    assert not rgb.any()
+    assert lib.ns_read_device_status(fr.scratch.geom.data_ptr(), fr.P, _lib.stream_handle(fr.device)) == 0
