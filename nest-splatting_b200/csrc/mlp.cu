@@ -128,20 +128,41 @@ mlp_kernel(const float* __restrict__ feat, int64_t npix, const uint16_t* __restr
   __syncthreads();
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, g = lane >> 2, tig = lane & 3;
   const int64_t ntiles = div_up64(npix, 16);
-  for (int64_t tile = (int64_t)blockIdx.x * kMlpWarps + warp; tile < ntiles;
-       tile += (int64_t)gridDim.x * kMlpWarps) {
+  const int64_t tstride = (int64_t)gridDim.x * kMlpWarps;
+  // The next tile's feature loads are issued before this tile's MMAs (one tile
+  // of loads in flight per warp while the tensor cores run).
+  float fr[2][8];
+  auto fetch = [&](int64_t tl) {
+    const int64_t q0 = tl * 16 + g, q1 = q0 + 8;
+    const bool w0 = tl < ntiles && q0 < npix, w1 = tl < ntiles && q1 < npix;
+#pragma unroll
+    for (int s = 0; s < 2; s++) {
+      const int c = 16 * s + 2 * tig;
+      auto ld = [&](int ch, int64_t px, bool v) { return v ? __ldg(feat + ch * npix + px) : 0.f; };
+      fr[s][0] = ld(c, q0, w0);
+      fr[s][1] = ld(c + 1, q0, w0);
+      fr[s][2] = ld(c, q1, w1);
+      fr[s][3] = ld(c + 1, q1, w1);
+      fr[s][4] = ld(c + 8, q0, w0);
+      fr[s][5] = ld(c + 9, q0, w0);
+      fr[s][6] = ld(c + 8, q1, w1);
+      fr[s][7] = ld(c + 9, q1, w1);
+    }
+  };
+  fetch((int64_t)blockIdx.x * kMlpWarps + warp);
+  for (int64_t tile = (int64_t)blockIdx.x * kMlpWarps + warp; tile < ntiles; tile += tstride) {
     const int64_t p0 = tile * 16 + g, p1 = p0 + 8;
     const bool v0 = p0 < npix, v1 = p1 < npix;
     uint32_t a[2][4];
 #pragma unroll
     for (int s = 0; s < 2; s++) {
-      const int c = 16 * s + 2 * tig;
-      auto ld = [&](int ch, int64_t px, bool v) { return v ? __ldg(feat + ch * npix + px) : 0.f; };
-      a[s][0] = pack_half2(ld(c, p0, v0), ld(c + 1, p0, v0));
-      a[s][1] = pack_half2(ld(c, p1, v1), ld(c + 1, p1, v1));
-      a[s][2] = pack_half2(ld(c + 8, p0, v0), ld(c + 9, p0, v0));
-      a[s][3] = pack_half2(ld(c + 8, p1, v1), ld(c + 9, p1, v1));
+      a[s][0] = pack_half2(fr[s][0], fr[s][1]);
+      a[s][1] = pack_half2(fr[s][2], fr[s][3]);
+      a[s][2] = pack_half2(fr[s][4], fr[s][5]);
+      a[s][3] = pack_half2(fr[s][6], fr[s][7]);
     }
+    fetch(tile + tstride);
+
     float y[4];
     mlp16(S, a, y);
     // y[0..1]: row g cols 2tig, 2tig+1; y[2..3]: row g+8.
