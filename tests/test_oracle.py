@@ -160,3 +160,78 @@ def test_mlp_oracle_shapes_and_mask():
     assert rgb.shape == (3, 4, 5)
     assert np.all(rgb[:, 0, 0] == 0)
     assert np.all((rgb[:, 1:, :] > 0) & (rgb[:, 1:, :] < 1))
+
+
+def _oracle_kernels(cam, base, kernel_type, shapes, beta=0.0):
+    g = torch.Generator().manual_seed(0)
+    grid = synth.hash_grid(g, levels=2, log2_T=12, lo=0.0, hi=0.0)
+    sc = synth.Scene(base, grid, [], cam, torch.full((base.shape[0], 1), 24.0))
+    inp = api_inputs(sc)
+    out, pre, n = oracle.forward(inp["means3D"].numpy(), inp["scales"].numpy(), inp["rotations"].numpy(),
+                                 inp["opacities"].numpy(), inp["homotrans"].numpy(), inp["ap_level"].numpy(),
+                                 grid.table.float().numpy(), grid.offsets.numpy(), grid.gridrange.numpy(),
+                                 cam.world_view_transform.numpy(), cam.full_proj_transform.numpy(),
+                                 cam.width, cam.height, 4, 2, 2, grid.S, 16, kernel_type=kernel_type,
+                                 shapes=np.asarray(shapes, np.float32), beta=beta)
+    return out
+
+
+@pytest.mark.parametrize("kernel_type,shape", [(1, 2.0), (1, 0.0), (2, 1.5), (3, 4.0)])
+def test_splat_kernels_alpha_at_centre(kernel_type, shape):
+    """Every splat kernel has G = 1 at the surfel centre (forward.cu:864-902):
+    alpha = opacity there."""
+    cam, base = _facing_surfels([4.0], [0.6])
+    out = _oracle_kernels(cam, base, kernel_type, [shape])
+    assert abs(out["out_others"][1, 32, 32] - 0.6) < 1e-5
+
+
+def test_beta_kernel_shape_zero_is_flat_disc():
+    """Kernel 1 with shape 0: G = (1 - rho)^0 = 1 inside the unit circle and no
+    sample outside it, so every covered pixel has alpha = opacity exactly."""
+    cam, base = _facing_surfels([4.0], [0.6])
+    base[:, 3:5] = math.log(0.3)  # a disc a few pixels wide
+    out = _oracle_kernels(cam, base, 1, [0.0])
+    a = out["out_others"][1]
+    covered = a > 0
+    assert covered.sum() > 20
+    assert np.all(np.abs(a[covered] - 0.6) < 1e-6)
+
+
+def test_flex_kernel_equals_global_beta():
+    """Kernel 2 with per-surfel shape b renders what kernel 0 renders with the
+    global beta b (forward.cu:873-885 against :903-915)."""
+    cam, base = _facing_surfels([3.0, 3.5, 4.0], [0.5, 0.4, 0.3])
+    base[:, 3:5] = math.log(0.2)
+    flex = _oracle_kernels(cam, base, 2, [0.7, 0.7, 0.7])
+    glob = _oracle_kernels(cam, base, 0, [0.0, 0.0, 0.0], beta=0.7)
+    assert np.abs(flex["out_others"][:7] - glob["out_others"][:7]).max() < 1e-5
+    assert flex["out_others"][1].max() > 0.1
+
+
+@pytest.mark.parametrize("mode", [4, 12, 14, 13 | 256])
+def test_render_modes_single_surfel_features(mode):
+    """One facing surfel and a zero hash table: the features at its centre are
+    alpha times the surfel's row as each mode combines it (forward.cu:964-1091,
+    1218-1282, 1593-1790): mode 4 and 14 copy the coarse channels, mode 12
+    copies them and scales the fine ones by the blend weight, mode 13 with the
+    inference flag and weight > 0.5 copies every channel."""
+    cam, base = _facing_surfels([4.0], [0.6])
+    g = torch.Generator().manual_seed(0)
+    total, hybrid, L = 2, 1, 1
+    grid = synth.hash_grid(g, levels=L, log2_T=12, lo=0.0, hi=0.0)
+    sc = synth.Scene(base, grid, [], cam, torch.full((1, 1), 24.0))
+    inp = api_inputs(sc)
+    base_mode = mode & 0xFF
+    row = {4: [0.5, -0.25], 12: [0.5, -0.25, 0.75, 1.5, 0.8], 14: [0.5, -0.25, 0.8],
+           13: [0.5, -0.25, 0.75, 1.5, 0.8]}[base_mode]
+    gauss = np.asarray([row], np.float32)
+    out, _, _ = oracle.forward(inp["means3D"].numpy(), inp["scales"].numpy(), inp["rotations"].numpy(),
+                               inp["opacities"].numpy(), inp["homotrans"].numpy(), inp["ap_level"].numpy(),
+                               grid.table.float().numpy(), grid.offsets.numpy(), grid.gridrange.numpy(),
+                               cam.world_view_transform.numpy(), cam.full_proj_transform.numpy(),
+                               cam.width, cam.height, 2 * total, 2, L, grid.S, 16, render_mode=mode,
+                               hybrid_levels=hybrid, total_levels=total, gauss=gauss)
+    f = out["out_color"][:, 32, 32] / 0.6
+    want = {4: [0.5, -0.25, 0, 0], 12: [0.5, -0.25, 0.8 * 0.75, 0.8 * 1.5], 14: [0.5, -0.25, 0, 0],
+            13: [0.5, -0.25, 0.75, 1.5]}[base_mode]
+    assert np.allclose(f, want, atol=1e-5), f
