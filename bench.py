@@ -173,8 +173,11 @@ def train_step_timing(sc, cam, dev, steps, warmup=2):
     for i in range(steps):
         losses.append(one(evs[i]))
     torch.cuda.synchronize()
-    fwd = statistics.mean(e[0].elapsed_time(e[1]) for e in evs)
-    bwd = statistics.mean(e[1].elapsed_time(e[2]) for e in evs)
+    # Medians over the steps (a step's float-atomic backward occasionally runs
+    # far longer than its neighbours; the mean is reported beside).
+    fwd = statistics.median(e[0].elapsed_time(e[1]) for e in evs)
+    bwd = statistics.median(e[1].elapsed_time(e[2]) for e in evs)
+    bwd_mean = statistics.mean(e[1].elapsed_time(e[2]) for e in evs)
     ms = fwd + bwd
     # The same steps with the fixed-point (bit-reproducible) table gradient, as
     # the drop-in selects it under torch.use_deterministic_algorithms.
@@ -189,11 +192,12 @@ def train_step_timing(sc, cam, dev, steps, warmup=2):
         torch.cuda.synchronize()
     finally:
         torch.use_deterministic_algorithms(was)
-    bwd_det = statistics.mean(e[1].elapsed_time(e[2]) for e in evs)
+    bwd_det = statistics.median(e[1].elapsed_time(e[2]) for e in evs)
     return {"workload": "config 4: config-2 scene, forward + backward of L1(rgb, target) + 0.05 normal loss; "
                         "leaves means, scales, rotations, opacities, hash table, MLP weights",
             "steps": steps, "ms_per_step": round(ms, 3), "forward_ms": round(fwd, 3),
-            "backward_ms": round(bwd, 3), "mpix_per_s": round(cam.width * cam.height / 1e6 * 1000.0 / ms, 3),
+            "backward_ms": round(bwd, 3), "backward_ms_mean": round(bwd_mean, 3),
+            "mpix_per_s": round(cam.width * cam.height / 1e6 * 1000.0 / ms, 3), "statistic": "median over steps",
             "backward_ms_deterministic_table": round(bwd_det, 3),
             "loss_first": round(float(losses[0].detach()), 6)}
 
