@@ -10,7 +10,8 @@
  *   ns_rasterize_forward  <- RasterizeGaussiansCUDA
  *                            submodules/diff-surfel-rasterization/rasterize_points.cu:39-242
  *                            and CudaRasterizer::Rasterizer::forward
- *                            .../cuda_rasterizer/rasterizer_impl.cu:255-440 (render_mode 0)
+ *                            .../cuda_rasterizer/rasterizer_impl.cu:255-440 (render_mode
+ *                            0, 4, 12-14; forward.cu:639-2049)
  *   ns_mark_visible       <- markVisible, rasterize_points.cu:452-471 and
  *                            rasterizer_impl.cu:54-66,198-210
  *   ns_mlp_forward        <- INGP.rgb_decode / get_color, hash_encoder/modules.py:587-602
@@ -115,7 +116,7 @@ typedef struct ns_raster_settings {
   uint32_t total_levels;
 } ns_raster_settings;
 
-/* Per-surfel inputs of the rasterizer (render_mode 0). */
+/* Per-surfel inputs of the rasterizer. */
 typedef struct ns_surfels {
   int32_t P;
   const float* means3D;   /* [P,3] */
@@ -161,7 +162,8 @@ size_t ns_binning_scratch_bytes(int64_t max_instances);
                                   Overflow is reported as NS_ERR_DEVICE by
                                   ns_read_device_status. */
 
-/* Forward rasterization, render_mode 0 (baseline hash grid).
+/* Forward rasterization: render_mode 0 (baseline hash grid) or 4 / 12 / 13 / 14
+ * (settings->render_mode), splat kernel settings->kernel_type.
  * geom/image/binning are scratch buffers of at least the ns_*_scratch_bytes size.
  * num_rendered (host, may be NULL): number of surfel/tile instances. Without
  * NS_FLAG_DEVICE_COUNT the call synchronises the stream once to read it and
@@ -206,8 +208,8 @@ size_t ns_backward_scratch_bytes(int32_t P);
  * accumulators, the fixed-point table gradient and its scale. */
 size_t ns_backward_scratch_bytes_deterministic(int32_t P, int64_t table_rows, int32_t level_dim);
 
-/* Backward rasterization, render_mode 0. settings, surfels, geom, binning and
- * image must be those of the forward call whose outputs the gradients refer to
+/* Backward rasterization (render_mode 0, 4, 12, 14; kernel_type 0-3). settings,
+ * surfels, geom, binning and image must be those of the forward call whose outputs the gradients refer to
  * (the scratch buffers unchanged since). homotrans, when given to the forward,
  * is treated as build_H(rotations, scales, means3D): its gradient is folded into
  * the mean, scale and rotation gradients, as the reference does. The transform
