@@ -74,6 +74,9 @@ def test_status_strings_and_scratch_sizes():
     assert b > a >= 1000 * 36
     assert lib.ns_radix_sort_temp_bytes(1 << 20) > 0
     assert lib.ns_backward_scratch_bytes(1000) >= 1000 * 18 * 4
+    # deterministic mode: + a 64-bit fixed-point word per table entry and the scale word
+    assert lib.ns_backward_scratch_bytes_deterministic(1000, 4096, 2) >= \
+        lib.ns_backward_scratch_bytes(1000) + 4096 * 2 * 8 + 4
     assert lib.ns_normal_error_scratch_bytes(64, 48) >= 64 * 48 * 6 * 4
     assert lib.ns_normal_error_scratch_bytes(0, 48) == 0
 
