@@ -151,7 +151,8 @@ class FramePipeline:
     while frame i+1 renders. Two device buffers of each, guarded by CUDA
     events; every frame still copies its own inputs in and its image out.
     With a DecodeShard (several ranks), each rank copies its own rows of the
-    index stream and the frame decodes them and all-gathers the attributes.
+    index stream; frame i+1's decode and all-gather run on a side stream
+    (views.DecodeRing) while frame i renders.
     graphs=True (single rank): each buffer set's frame is a FrameGraph, so no
     frame waits for the host and the host never waits inside a frame.
     """
@@ -162,6 +163,12 @@ class FramePipeline:
         if graphs and shard is not None:
             raise ValueError("graphs=True renders unsharded frames only")
         self.graphs = [] if graphs else None
+        if shard is not None and depth != 2:
+            raise ValueError("sharded frames alternate between two attribute buffers: depth must be 2")
+        self.ring = None
+        if shard is not None:
+            from .views import DecodeRing
+            self.ring = DecodeRing(renderer.rvq_idx, renderer.dims, shard.world, shard.rank)
         d = renderer.device
         self.in_stream = torch.cuda.Stream(device=d)
         self.out_stream = torch.cuda.Stream(device=d)
@@ -184,6 +191,8 @@ class FramePipeline:
         fr, sh = self.fr, self.shard
         cs = torch.cuda.current_stream(fr.device)
         fr._outputs(cam)
+        if sh is not None:
+            return self._run_sharded(n, cam, host_idx, host_cam, host_rgb, before_frame, cs)
         for i in range(n):
             k = i % self.depth
             if self.rgb[k] is None or self.rgb[k].shape != fr.rgb.shape:
@@ -191,13 +200,7 @@ class FramePipeline:
             with torch.cuda.stream(self.in_stream):
                 if self.used[k]:
                     self.in_stream.wait_event(self.ev_done[k])
-                hi = host_idx(i)
-                if sh is None:
-                    self.idx[k].copy_(hi, non_blocking=True)
-                else:
-                    from .views import shard_range
-                    lo_, hi_ = shard_range(sh.P, sh.world, sh.rank)
-                    self.idx[k][: hi_ - lo_].copy_(hi[lo_:hi_], non_blocking=True)
+                self.idx[k].copy_(host_idx(i), non_blocking=True)
                 self.cam[k].copy_(host_cam(i), non_blocking=True)
                 self.ev_in[k].record(self.in_stream)
             cs.wait_event(self.ev_in[k])
@@ -210,11 +213,49 @@ class FramePipeline:
                     self.graphs.append(FrameGraph(fr, cam, self.cam[k][0], self.cam[k][1], rvq_idx=self.idx[k],
                                                   rgb=self.rgb[k]))
                 self.graphs[k].replay()
-            elif sh is None:
-                fr.render(cam, self.cam[k][0], self.cam[k][1], rvq_idx=self.idx[k], rgb=self.rgb[k])
             else:
-                fr.decoded = sh.decode_and_gather(fr.codebooks, _rvq_decode, idx=self.idx[k])
-                fr.render(cam, self.cam[k][0], self.cam[k][1], skip_decode=True, rgb=self.rgb[k])
+                fr.render(cam, self.cam[k][0], self.cam[k][1], rvq_idx=self.idx[k], rgb=self.rgb[k])
+            self.ev_done[k].record(cs)
+            with torch.cuda.stream(self.out_stream):
+                self.out_stream.wait_event(self.ev_done[k])
+                host_rgb(i).copy_(self.rgb[k], non_blocking=True)
+                self.ev_host[k].record(self.out_stream)
+            self.used[k] = True
+
+    def _run_sharded(self, n, cam, host_idx, host_cam, host_rgb, before_frame, cs):
+        from .views import shard_range
+        fr, sh, ring = self.fr, self.shard, self.ring
+        lo, hi = shard_range(sh.P, sh.world, sh.rank)
+
+        def stage(i):
+            # Frame i's inputs on the input stream, then its decode + all-gather on
+            # the ring's stream (collectives in frame order on every rank).
+            k = i % 2
+            with torch.cuda.stream(self.in_stream):
+                if self.used[k]:
+                    self.in_stream.wait_event(self.ev_done[k])
+                ring.shards[k].idx_shard[: hi - lo].copy_(host_idx(i)[lo:hi], non_blocking=True)
+                self.cam[k].copy_(host_cam(i), non_blocking=True)
+                self.ev_in[k].record(self.in_stream)
+            ring.stream.wait_event(self.ev_in[k])
+            ring.prefetch(i, fr.codebooks, _rvq_decode)
+
+        if n > 0:
+            stage(0)
+        for i in range(n):
+            k = i % 2
+            if i + 1 < n:
+                stage(i + 1)
+            if self.rgb[k] is None or self.rgb[k].shape != fr.rgb.shape:
+                self.rgb[k] = torch.empty_like(fr.rgb)
+            cs.wait_event(self.ev_in[k])
+            if self.used[k]:
+                cs.wait_event(self.ev_host[k])
+            if before_frame is not None:
+                before_frame(i)
+            fr.decoded = ring.acquire(i, cs)
+            fr.render(cam, self.cam[k][0], self.cam[k][1], skip_decode=True, rgb=self.rgb[k])
+            ring.release(i, cs)
             self.ev_done[k].record(cs)
             with torch.cuda.stream(self.out_stream):
                 self.out_stream.wait_event(self.ev_done[k])
