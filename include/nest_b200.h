@@ -278,7 +278,12 @@ int ns_radix_sort_pairs(const uint64_t* keys_in, const uint32_t* vals_in, uint64
  * that array: calls whose kernels overlap on the GPU (other streams or host
  * threads) race, so serialise them. The first call on a device looks up the
  * array's address for that device (cudaGetSymbolAddress); make it before any
- * stream capture. Same result as ns_radix_sort_pairs. */
+ * stream capture. The address is cached per device and CUDA context, so the
+ * first call after a context reset (cudaDeviceReset) looks it up again. Same
+ * result and argument checks as ns_radix_sort_pairs, except that device-side
+ * errors (a look-back wait that ran out of its bound, which only a GPU that has
+ * stopped making progress produces) are not reported: the call returns
+ * argument and launch errors only, and the output is then undefined. */
 int ns_radix_sort_pairs_noalloc(const uint64_t* keys_in, const uint32_t* vals_in,
                                 uint64_t* keys_out, uint32_t* vals_out, int64_t n,
                                 int32_t end_bit, void* stream);

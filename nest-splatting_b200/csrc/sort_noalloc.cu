@@ -16,7 +16,18 @@
 //     callers must serialise them (one stream is enough);
 //   * the first call on a device looks up the array's device address with
 //     cudaGetSymbolAddress for that device; make that first call before any
-//     stream capture.
+//     stream capture. The address is cached per device together with the
+//     identity of the device's current CUDA context: after a context reset
+//     (cudaDeviceReset, a primary context released and retained again) the
+//     next call looks it up again, so a reloaded module is never addressed
+//     through a stale pointer;
+//   * the sort's bounded look-back waits record a timeout in an error word
+//     inside the array, which this entry point does not read back (that would
+//     cost a stream synchronisation per call): it reports argument and launch
+//     errors only. A look-back wait runs out only on a GPU that has stopped
+//     making progress; the sorted output is then undefined.
+#include <cuda.h>
+
 #include <mutex>
 
 #include "kernels.cuh"
@@ -40,17 +51,52 @@ __device__ __align__(256) unsigned char g_sort_scratch[kNoAllocBytes];
 constexpr int kMaxDevices = 64;
 std::mutex g_mutex;
 void* g_scratch_addr[kMaxDevices] = {};
+unsigned long long g_scratch_ctx[kMaxDevices] = {};  // context id the address belongs to
 
-// Device address of g_sort_scratch on the current device (looked up once per device).
+// Unique id of the calling thread's current context (cuCtxGetId: ids are never
+// reused within a process), through the runtime's driver entry points so the
+// library needs no link against libcuda. 0 when unavailable.
+unsigned long long current_context_id() {
+  using GetCurrentFn = CUresult (*)(CUcontext*);
+  using GetIdFn = CUresult (*)(CUcontext, unsigned long long*);
+  static GetCurrentFn get_current = nullptr;
+  static GetIdFn get_id = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &f, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_current = reinterpret_cast<GetCurrentFn>(f);
+    f = nullptr;
+    if (cudaGetDriverEntryPoint("cuCtxGetId", &f, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_id = reinterpret_cast<GetIdFn>(f);
+  });
+  CUcontext ctx = nullptr;
+  unsigned long long id = 0;
+  if (!get_current || !get_id || get_current(&ctx) != CUDA_SUCCESS || !ctx ||
+      get_id(ctx, &id) != CUDA_SUCCESS)
+    return 0;
+  return id;
+}
+
+// Device address of g_sort_scratch on the current device, looked up once per
+// device and context (without a context id, on every call).
 int scratch_address(void** out) {
   int dev = 0;
   NS_CUDA_TRY(cudaGetDevice(&dev));
   if (dev < 0 || dev >= kMaxDevices) return NS_ERR_UNSUPPORTED;
+  // Id 0: no context is current on this thread yet (the runtime makes the
+  // device's primary context current on its first call that needs one, e.g.
+  // the lookup below) or the driver lacks cuCtxGetId.
+  const unsigned long long ctx = current_context_id();
   std::lock_guard<std::mutex> lock(g_mutex);
-  if (!g_scratch_addr[dev]) {
+  if (!g_scratch_addr[dev] || ctx == 0 || g_scratch_ctx[dev] != ctx) {
     void* ptr = nullptr;
     NS_CUDA_TRY(cudaGetSymbolAddress(&ptr, g_sort_scratch));
     g_scratch_addr[dev] = ptr;
+    g_scratch_ctx[dev] = ctx ? ctx : current_context_id();
   }
   *out = g_scratch_addr[dev];
   return NS_OK;
@@ -63,7 +109,7 @@ extern "C" int ns_radix_sort_pairs_noalloc(const uint64_t* keys_in, const uint32
                                            uint64_t* keys_out, uint32_t* vals_out, int64_t n,
                                            int32_t end_bit, void* stream) {
   using namespace ns;
-  if (n < 0) return NS_ERR_INVALID;
+  if (n < 0 || end_bit < 0 || end_bit > 64) return NS_ERR_INVALID;  // as ns_radix_sort_pairs
   if (n > kNoAllocMaxPairs) return NS_ERR_CAPACITY;
   if (n > 0 && (!keys_in || !vals_in || !keys_out || !vals_out)) return NS_ERR_INVALID;
   if (n == 0) return NS_OK;

@@ -370,13 +370,15 @@ void oracle_render(int W, int H, const uint32_t* ranges, const uint32_t* point_l
 
 // Hash-grid lookup of a batch of points (hashgrid.h:53-212), exported for the
 // known-answer tests of grid_index and the trilinear gather.
+// level_exp2: NULL, or [L] values of exp2f(l S) to use instead of the host's.
 void oracle_query(int n, const float* xyz, const uint32_t* ap_level, const float* table,
                   const int* offsets, float vmin, float vmax, int C, int LD, uint32_t L, float S,
-                  uint32_t Hres, int align_corners, uint32_t interp, int contract, float* out) {
+                  uint32_t Hres, int align_corners, uint32_t interp, int contract,
+                  const float* level_exp2, float* out) {
   for (int i = 0; i < n; i++) {
     F3 p = {xyz[3 * i], xyz[3 * i + 1], xyz[3 * i + 2]};
     query_feature(out + (size_t)i * C, C, LD, p, vmin, vmax, offsets, ap_level[i], table, L, S,
-                  Hres, align_corners != 0, interp, contract != 0);
+                  Hres, align_corners != 0, interp, contract != 0, level_exp2);
   }
 }
 

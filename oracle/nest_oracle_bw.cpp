@@ -50,7 +50,7 @@ template <typename R>
 void query_feature_bw(R* feat, int C, int LD, V3<R> xyz, R vmin, R vmax, const int* offsets,
                       uint32_t ap_level, const float* table, uint32_t L, float S, uint32_t Hres,
                       bool align_corners, uint32_t interp, bool contract, const R* grad_feat,
-                      R* dL_dtable, R dL_dxyz[3]) {
+                      R* dL_dtable, R dL_dxyz[3], const float* lexp2 = nullptr) {
   R in[3];
   bool oob = false;
   R grad_scale = 0;
@@ -80,7 +80,7 @@ void query_feature_bw(R* feat, int C, int LD, V3<R> xyz, R vmin, R vmax, const i
   std::vector<R> dy_dx((size_t)3 * C, R(0));
   for (uint32_t lv = 0; lv < max_level; lv++) {
     const uint32_t hsize = (uint32_t)(offsets[lv + 1] - offsets[lv]);
-    const float scale_f = std::exp2(lv * S) * Hres - 1.0f;  // the level scale as the reference forms it
+    const float scale_f = level_exp2(lv, S, lexp2) * Hres - 1.0f;  // the level scale as the reference forms it
     const R scale = scale_f;
     const uint32_t res = (uint32_t)std::ceil(scale_f) + 1;
     const float* grid = table + (size_t)(uint32_t)offsets[lv] * LD;
@@ -89,7 +89,7 @@ void query_feature_bw(R* feat, int C, int LD, V3<R> xyz, R vmin, R vmax, const i
     R pos[3], deriv[3];
     uint32_t pg[3];
     for (int d = 0; d < 3; d++) {
-      pos[d] = in[d] * scale + (align_corners ? R(0) : R(0.5));
+      pos[d] = std::fma(in[d], scale, align_corners ? R(0) : R(0.5));  // contracted as nvcc does
       pg[d] = (uint32_t)std::floor(pos[d]);
       pos[d] -= (R)pg[d];
       if (interp == 1) {
@@ -108,7 +108,7 @@ void query_feature_bw(R* feat, int C, int LD, V3<R> xyz, R vmin, R vmax, const i
         else { w *= pos[d]; g[d] = pg[d] + 1; }
       }
       const uint32_t idx = grid_index(align_corners, hsize, res, g) * LD;
-      for (int ch = 0; ch < LD; ch++) r[ch] += w * (R)grid[idx + ch];
+      for (int ch = 0; ch < LD; ch++) r[ch] = std::fma(w, (R)grid[idx + ch], r[ch]);
       for (int ch = 0; ch < LD; ch++) atomic_add<R>(&dgrid[idx + ch], w * gl[ch]);
     }
     for (int ch = 0; ch < LD; ch++) feat[lv * LD + ch] = r[ch];
@@ -127,7 +127,8 @@ void query_feature_bw(R* feat, int C, int LD, V3<R> xyz, R vmin, R vmax, const i
         const uint32_t il = grid_index(align_corners, hsize, res, g) * LD;
         g[gd] = pg[gd] + 1;
         const uint32_t ir = grid_index(align_corners, hsize, res, g) * LD;
-        for (int ch = 0; ch < LD; ch++) rg[ch] += w * ((R)grid[ir + ch] - (R)grid[il + ch]) * deriv[gd];
+        for (int ch = 0; ch < LD; ch++)
+          rg[ch] = std::fma(w * ((R)grid[ir + ch] - (R)grid[il + ch]), deriv[gd], rg[ch]);
       }
       for (int ch = 0; ch < LD; ch++) dy_dx[(size_t)gd * C + lv * LD + ch] = rg[ch];
     }
@@ -137,7 +138,7 @@ void query_feature_bw(R* feat, int C, int LD, V3<R> xyz, R vmin, R vmax, const i
     R acc = 0;
     for (uint32_t lv = 0; lv < max_level; lv++)
       for (int ch = 0; ch < LD; ch++)
-        acc += grad_feat[lv * LD + ch] * dy_dx[(size_t)d * C + lv * LD + ch];
+        acc = std::fma(grad_feat[lv * LD + ch], dy_dx[(size_t)d * C + lv * LD + ch], acc);
     dL_dxyz[d] = acc;
   }
 }
@@ -676,6 +677,25 @@ void oracle_preprocess_backward_f64(int P, const float* means3D, const float* sc
   preprocess_backward<double>(P, means3D, scales, rotations, radii, transMat, viewmatrix,
                               projmatrix, width, height, tanfovx, tanfovy, dL_dmean2D, dL_dnormal,
                               dL_dtransMat, dL_dhomoMat, dL_dmeans3D, dL_dscales, dL_drots);
+}
+
+// Per-point query_feature<true> (hashgrid.h:106-299) with a given upstream
+// gradient: grad_feat [n, C] in, table gradient accumulated into dL_dtable
+// ([rows, LD], caller-zeroed) and dL/dxyz [n, 3] out. Serial (the table
+// gradient's float additions in point order). level_exp2 as oracle_query.
+void oracle_query_backward(int n, const float* xyz, const uint32_t* ap_level, const float* table,
+                           const int* offsets, float vmin, float vmax, int C, int LD, uint32_t L,
+                           float S, uint32_t Hres, int align_corners, uint32_t interp, int contract,
+                           const float* level_exp2, const float* grad_feat, float* dL_dtable,
+                           float* dL_dxyz) {
+  std::vector<float> feat((size_t)C);
+  for (int i = 0; i < n; i++) {
+    const V3<float> p{xyz[3 * i], xyz[3 * i + 1], xyz[3 * i + 2]};
+    query_feature_bw<float>(feat.data(), C, LD, p, vmin, vmax, offsets, ap_level[i], table, L, S,
+                            Hres, align_corners != 0, interp, contract != 0,
+                            grad_feat + (size_t)i * C, dL_dtable, dL_dxyz + 3 * (size_t)i,
+                            level_exp2);
+  }
 }
 
 }  // extern "C"

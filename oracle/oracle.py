@@ -54,7 +54,9 @@ def load() -> C.CDLL:
     lib.oracle_render.argtypes = [i32, i32, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, i32, i32, u32, f32, u32,
                                   i32, u32, i32, f32, u32, i32, vp, vp, vp, vp, vp, vp, i32, i32, vp,
                                   i32, i32, i32, vp]
-    lib.oracle_query.argtypes = [i32, vp, vp, vp, vp, f32, f32, i32, i32, u32, f32, u32, i32, u32, i32, vp]
+    lib.oracle_query.argtypes = [i32, vp, vp, vp, vp, f32, f32, i32, i32, u32, f32, u32, i32, u32, i32, vp, vp]
+    lib.oracle_query_backward.argtypes = [i32, vp, vp, vp, vp, f32, f32, i32, i32, u32, f32, u32, i32, u32, i32,
+                                          vp, vp, vp, vp]
     lib.oracle_grid_index.restype = u32
     lib.oracle_grid_index.argtypes = [i32, u32, u32, u32, u32, u32]
     lib.oracle_rvq_decode.argtypes = [i64, i32, i32, i32, vp, vp, vp]
@@ -146,16 +148,38 @@ def render(pre, vals, ranges, homotrans, ap_level, table_f32, offsets, gridrange
 
 
 def query(xyz, ap_level, table_f32, offsets, vmin, vmax, C_out, LD, L, S, Hres, align_corners=False, interp=0,
-          contract=False):
+          contract=False, level_exp2=None):
+    """hashgrid.h:53-212 per point -> [n, C_out]. level_exp2: optional [L] values of
+    exp2f(l S) (e.g. the device's) in place of the host's."""
     lib = load()
+    lexp = None if level_exp2 is None else _f32(level_exp2).reshape(-1)
     xyz = _f32(xyz).reshape(-1, 3)
     n = xyz.shape[0]
     ap = np.ascontiguousarray(np.asarray(ap_level, dtype=np.uint32).reshape(-1))
     out = np.zeros((n, C_out), np.float32)
     lib.oracle_query(n, _p(xyz), _p(ap), _p(_f32(table_f32)), _p(np.ascontiguousarray(offsets, np.int32)),
                      float(vmin), float(vmax), int(C_out), int(LD), int(L), float(S), int(Hres),
-                     int(bool(align_corners)), int(interp), int(bool(contract)), _p(out))
+                     int(bool(align_corners)), int(interp), int(bool(contract)), _p(lexp), _p(out))
     return out
+
+
+def query_backward(xyz, ap_level, table_f32, offsets, vmin, vmax, C_out, LD, L, S, Hres, grad_feat,
+                   align_corners=False, interp=0, contract=False, level_exp2=None):
+    """hashgrid.h:106-299 per point: (dL_dtable [rows, LD], dL_dxyz [n, 3]) for grad_feat [n, C_out]."""
+    lib = load()
+    lexp = None if level_exp2 is None else _f32(level_exp2).reshape(-1)
+    xyz = _f32(xyz).reshape(-1, 3)
+    n = xyz.shape[0]
+    ap = np.ascontiguousarray(np.asarray(ap_level, dtype=np.uint32).reshape(-1))
+    table_f32 = _f32(table_f32)
+    dtab = np.zeros_like(table_f32)
+    dxyz = np.zeros((n, 3), np.float32)
+    g = _f32(grad_feat).reshape(n, C_out)
+    lib.oracle_query_backward(n, _p(xyz), _p(ap), _p(table_f32), _p(np.ascontiguousarray(offsets, np.int32)),
+                              float(vmin), float(vmax), int(C_out), int(LD), int(L), float(S), int(Hres),
+                              int(bool(align_corners)), int(interp), int(bool(contract)), _p(lexp), _p(g),
+                              _p(dtab), _p(dxyz))
+    return dtab, dxyz
 
 
 def grid_index(align_corners, hashmap_size, res, x, y, z) -> int:

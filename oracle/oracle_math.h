@@ -76,10 +76,19 @@ inline uint32_t grid_index(bool align_corners, uint32_t hashmap_size, uint32_t r
   return index % hashmap_size;
 }
 
+// exp2f(l * S) of hashgrid.h:128 (the level scale is exp2f(l S) H - 1). The
+// host's exp2f and the device's may differ in the last place (CUDA documents
+// up to 2 ulp for exp2f); level_exp2, when given, supplies the device's value
+// per level so a check can take that difference out.
+inline float level_exp2(uint32_t l, float S, const float* level_exp2) {
+  return level_exp2 ? level_exp2[l] : std::exp2(l * S);
+}
+
 // hashgrid.h:53-212 (forward only, BW = false). feat has room for C channels.
 inline void query_feature(float* feat, int C, int LD, F3 xyz, float vmin, float vmax, const int* offsets,
                    uint32_t ap_level, const float* table, uint32_t L, float S, uint32_t Hres,
-                   bool align_corners, uint32_t interp, bool contract) {
+                   bool align_corners, uint32_t interp, bool contract,
+                   const float* lexp2 = nullptr) {
   float in[3];
   bool oob = false;
   if (!contract) {
@@ -104,13 +113,15 @@ inline void query_feature(float* feat, int C, int LD, F3 xyz, float vmin, float 
   if (oob) return;
   for (uint32_t lv = 0; lv < max_level; lv++) {
     uint32_t hsize = (uint32_t)(offsets[lv + 1] - offsets[lv]);
-    float scale = std::exp2(lv * S) * Hres - 1.0f;
+    float scale = level_exp2(lv, S, lexp2) * Hres - 1.0f;
     uint32_t res = (uint32_t)std::ceil(scale) + 1;
     const float* grid = table + (size_t)(uint32_t)offsets[lv] * LD;
     float pos[3];
     uint32_t pg[3];
     for (int d = 0; d < 3; d++) {
-      pos[d] = in[d] * scale + (align_corners ? 0.0f : 0.5f);
+      // nvcc contracts the reference's `inputs[d] * scale + 0.5f` (and the
+      // corner sums below) into fused multiply-adds; std::fma does the same.
+      pos[d] = std::fma(in[d], scale, align_corners ? 0.0f : 0.5f);
       pg[d] = (uint32_t)std::floor(pos[d]);
       pos[d] -= (float)pg[d];
       if (interp == 1) pos[d] = pos[d] * pos[d] * (3.0f - 2.0f * pos[d]);
@@ -124,7 +135,7 @@ inline void query_feature(float* feat, int C, int LD, F3 xyz, float vmin, float 
         else { w *= pos[d]; g[d] = pg[d] + 1; }
       }
       uint32_t idx = grid_index(align_corners, hsize, res, g) * LD;
-      for (int ch = 0; ch < LD; ch++) r[ch] += w * grid[idx + ch];
+      for (int ch = 0; ch < LD; ch++) r[ch] = std::fma(w, grid[idx + ch], r[ch]);
     }
     for (int ch = 0; ch < LD; ch++) feat[lv * LD + ch] = r[ch];
   }

@@ -51,3 +51,17 @@ def test_noalloc_sort_refuses_sizes_above_limit():
     lib = _lib.load()
     rc = lib.ns_radix_sort_pairs_noalloc(None, None, None, None, MAX_PAIRS + 1, 45, None)
     assert rc == _lib.NS_ERR_CAPACITY
+
+
+@pytest.mark.parametrize("n", [0, 16])
+@pytest.mark.parametrize("end_bit", [-1, 65])
+def test_noalloc_sort_checks_end_bit_like_regular_sort(n, end_bit):
+    """end_bit outside [0, 64] is refused by both entry points, also for n == 0."""
+    lib = _lib.load()
+    keys, vals = _keys(max(n, 1), 45, 5)
+    ko, vo = torch.empty_like(keys), torch.empty_like(vals)
+    rc = lib.ns_radix_sort_pairs_noalloc(keys.data_ptr(), vals.data_ptr(), ko.data_ptr(), vo.data_ptr(), n,
+                                         end_bit, _lib.stream_handle(keys.device))
+    assert rc == _lib.NS_ERR_INVALID
+    with pytest.raises(RuntimeError):
+        raster.radix_sort_pairs(keys[:n], vals[:n], end_bit=end_bit)
