@@ -37,6 +37,11 @@
  *                            depth_ratio 0), utils/point_utils.py:10-30,48-60
  *                            (depths_to_points, depth_to_normal), train.py:674-675
  *   ns_normal_error_backward <- torch autograd of the same expressions
+ *   ns_grid_encode_forward   <- grid_encode_forward, gridencoder/src/gridencoder.h:9 and
+ *                               gridencoder.cu:450-473 (kernel_grid, :88-242)
+ *   ns_grid_encode_backward  <- grid_encode_backward, gridencoder/src/gridencoder.h:10 and
+ *                               gridencoder.cu:475-505 (kernel_grid_backward, :246-338;
+ *                               kernel_input_backward, :341-367)
  */
 #ifndef NEST_B200_H_
 #define NEST_B200_H_
@@ -221,6 +226,28 @@ int ns_rasterize_backward(const ns_raster_settings* settings, const ns_surfels* 
                           size_t binning_bytes, const void* image, size_t image_bytes,
                           int64_t num_rendered, void* scratch, size_t scratch_bytes, void* stream);
 
+/* Copies what a forward call left in its scratch buffers into caller buffers
+ * (device; any output may be NULL), for inspection and tests. The reference
+ * keeps the same state in its binningBuffer / geomBuffer / imgBuffer
+ * (rasterizer_impl.cu:212-251, BinningState::point_list, ImageState::ranges):
+ *   point_list [num_rendered] u32  surfel ids, per tile in (tile, depth) order
+ *   ranges     [tiles, 2] u32      [start, end) of each tile in point_list
+ *   tile_rects [P, 4] i16          x0, y0, x1, y1: the tiles that received the
+ *                                  surfel (the reference's getRect rectangle cut
+ *                                  to the surfel's alpha >= 1/255 box)
+ *   depths     [P] f32             view-space depth of the sort key
+ *   pixel_boxes [P, 4] f32         x0, x1, y0, y1 pixel box outside which the
+ *                                  surfel's alpha < 1/255 (valid where the tile
+ *                                  rectangle is non-empty)
+ *   means2D    [P, 2] f32          the screen centre of the tile rectangle
+ *                                  (compute_aabb's point_image; same validity)
+ * num_rendered is the forward's instance count. Asynchronous on `stream`. */
+int ns_read_binning(const void* geom, size_t geom_bytes, int32_t P, const void* binning,
+                    size_t binning_bytes, const void* image, size_t image_bytes, int32_t width,
+                    int32_t height, int64_t num_rendered, uint32_t* point_list, uint32_t* ranges,
+                    int16_t* tile_rects, float* depths, float* pixel_boxes, float* means2D,
+                    void* stream);
+
 /* Reads (and clears) the device error word of a geometry scratch buffer; syncs. */
 int ns_read_device_status(void* geom, int32_t P, void* stream);
 
@@ -375,6 +402,35 @@ int ns_normal_error_backward(const float* allmap, const float* viewmatrix, const
                              const float* ray_o, int32_t width, int32_t height,
                              const float* dL_derr, int64_t derr_stride, float* dL_dallmap,
                              void* scratch, size_t scratch_bytes, void* stream);
+
+/* ------------------------------------------------------ hash-grid encoding */
+
+/* The multiresolution hash-grid encoding as a standalone op, with the
+ * reference gridencoder's arguments (gridencoder.h:9-10; B points, D = 3
+ * dims, C = 2 features per level, L levels, S = log2(per-level scale), H base
+ * resolution, gridtype 0 = hash; interp 0 linear / 1 smoothstep). The lookup is
+ * the blend kernel's (the rasterizer's per-level query_feature arithmetic).
+ *   inputs     fp32 [B, 3] in [0, 1]; points outside give zeros / no gradient
+ *   embeddings [offsets[L], 2], fp16 (embeddings_fp16 = 1) or fp32
+ *   offsets    int32 [L + 1] level row offsets
+ *   outputs    fp32 [L, B, 2] (also for an fp16 table: computed in fp32, where
+ *              the reference's fp16 path accumulates in half precision)
+ *   dy_dx      fp32 [B, L * 3 * 2] or NULL: d output / d input
+ * Supported: D 3, C 2, gridtype 0 (others NS_ERR_UNSUPPORTED). */
+int ns_grid_encode_forward(const float* inputs, const void* embeddings, int32_t embeddings_fp16,
+                           const int32_t* offsets, float* outputs, uint32_t B, uint32_t D, uint32_t C,
+                           uint32_t L, float S, uint32_t H, float* dy_dx, uint32_t gridtype,
+                           int32_t align_corners, uint32_t interp, void* stream);
+
+/* Backward of ns_grid_encode_forward for grad fp32 [L, B, 2]: grad_embeddings
+ * fp32 [offsets[L], 2] is accumulated into (zero it first, as the reference's
+ * caller does) with float atomics; grad_inputs fp32 [B, 3] (or NULL) is
+ * formed from dy_dx, which must then be the forward's dy_dx. */
+int ns_grid_encode_backward(const float* grad, const float* inputs, const void* embeddings,
+                            int32_t embeddings_fp16, const int32_t* offsets, float* grad_embeddings,
+                            uint32_t B, uint32_t D, uint32_t C, uint32_t L, float S, uint32_t H,
+                            const float* dy_dx, float* grad_inputs, uint32_t gridtype,
+                            int32_t align_corners, uint32_t interp, void* stream);
 
 #ifdef __cplusplus
 }

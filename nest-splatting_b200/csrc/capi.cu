@@ -352,6 +352,48 @@ int ns_rasterize_forward(const ns_raster_settings* settings, const ns_surfels* s
                         surfels->colors_precomp, num_rendered, flags, stream);
 }
 
+int ns_read_binning(const void* geom, size_t geom_bytes, int32_t P, const void* binning,
+                    size_t binning_bytes, const void* image, size_t image_bytes, int32_t width,
+                    int32_t height, int64_t num_rendered, uint32_t* point_list, uint32_t* ranges,
+                    int16_t* tile_rects, float* depths, float* pixel_boxes, float* means2D,
+                    void* stream_) {
+  cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_);
+  if (P < 0 || width <= 0 || height <= 0 || num_rendered < 0) return NS_ERR_INVALID;
+  if (!geom || !image || (num_rendered > 0 && point_list && !binning)) return NS_ERR_INVALID;
+  if (geom_bytes < ns_geometry_scratch_bytes(P) || image_bytes < ns_image_scratch_bytes(width, height))
+    return NS_ERR_SCRATCH;
+  GeomState g = carve_geom(const_cast<void*>(geom), P, nullptr);
+  ImageState im = carve_image(const_cast<void*>(image), width, height, nullptr);
+  if (point_list && num_rendered > 0) {
+    const int64_t cap = bin_capacity(binning_bytes);
+    if (cap < 0 || num_rendered > cap) return NS_ERR_SCRATCH;
+    BinState b = carve_bin(const_cast<void*>(binning), cap, nullptr);
+    NS_CUDA_TRY(cudaMemcpyAsync(point_list, b.vals_sorted, (size_t)num_rendered * sizeof(uint32_t),
+                                cudaMemcpyDeviceToDevice, stream));
+  }
+  if (ranges) {
+    const size_t tiles = (size_t)div_up(width, kTile) * div_up(height, kTile);
+    NS_CUDA_TRY(cudaMemcpyAsync(ranges, im.ranges, tiles * sizeof(uint2), cudaMemcpyDeviceToDevice, stream));
+  }
+  if (P == 0) return NS_OK;
+  // Strided copies out of the 16-byte BinInfo and 128-byte SurfelRecord arrays.
+  if (tile_rects)
+    NS_CUDA_TRY(cudaMemcpy2DAsync(tile_rects, 4 * sizeof(int16_t), g.bin, sizeof(BinInfo),
+                                  4 * sizeof(int16_t), (size_t)P, cudaMemcpyDeviceToDevice, stream));
+  if (depths)
+    NS_CUDA_TRY(cudaMemcpy2DAsync(depths, sizeof(float), reinterpret_cast<const char*>(g.bin) + 8,
+                                  sizeof(BinInfo), sizeof(float), (size_t)P, cudaMemcpyDeviceToDevice,
+                                  stream));
+  if (pixel_boxes)
+    NS_CUDA_TRY(cudaMemcpy2DAsync(pixel_boxes, sizeof(float4), g.records, sizeof(SurfelRecord),
+                                  sizeof(float4), (size_t)P, cudaMemcpyDeviceToDevice, stream));
+  if (means2D)  // record words 13, 14 (q3.y, q3.z)
+    NS_CUDA_TRY(cudaMemcpy2DAsync(means2D, 2 * sizeof(float), reinterpret_cast<const char*>(g.records) + 52,
+                                  sizeof(SurfelRecord), 2 * sizeof(float), (size_t)P,
+                                  cudaMemcpyDeviceToDevice, stream));
+  return NS_OK;
+}
+
 size_t ns_backward_scratch_bytes(int32_t P) { return align_up(backward_accum_bytes(P)); }
 
 size_t ns_backward_scratch_bytes_deterministic(int32_t P, int64_t table_rows, int32_t level_dim) {

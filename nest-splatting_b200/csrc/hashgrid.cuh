@@ -124,4 +124,45 @@ __device__ __forceinline__ void corner_rows(const LevelConst& lc, const uint32_t
   }
 }
 
+// Trilinear lookup of one level at a point of [0,1]^3 (hashgrid.h:140-193),
+// split so that two lookups' loads are in flight together: lookup_issue()
+// finds the cell and issues the 8 corner loads; lookup_finish() weights corner
+// c by ((wx * wy) * wz) and accumulates corners in order c = 0..7.
+template <typename TableT>
+__device__ __forceinline__ void lookup_issue(const LevelConst& lc, const void* table, float4 in,
+                                             float half_shift, uint32_t interp, float (&f)[3],
+                                             Corner8<TableT>& cv) {
+  uint32_t g[3];
+  const float pin[3] = {in.x, in.y, in.z};
+#pragma unroll
+  for (int d = 0; d < 3; d++) {
+    const float pos = pin[d] * lc.scale + half_shift;
+    const float fl = floorf(pos);  // pos in (0, 2^24): the integer converts exactly
+    g[d] = (uint32_t)fl;
+    f[d] = pos - fl;
+    if (interp == 1) f[d] = f[d] * f[d] * (3.0f - 2.0f * f[d]);
+  }
+  uint32_t idx[8];
+  corner_rows(lc, g, idx);
+#pragma unroll
+  for (int c = 0; c < 8; c++) cv.load(lc.base, c, idx[c]);
+}
+
+// Corner weights ((wx * wy) * wz) and the weighted sum in packed fp32
+// (__fmul2_rn / __ffma2_rn round each lane like the scalar operations).
+template <typename TableT>
+__device__ __forceinline__ float2 lookup_finish(const float (&f)[3], const Corner8<TableT>& cv) {
+  const float2 wx = make_float2(1 - f[0], f[0]);
+  const float2 wxy0 = __fmul2_rn(wx, make_float2(1 - f[1], 1 - f[1]));  // corners 0, 1
+  const float2 wxy1 = __fmul2_rn(wx, make_float2(f[1], f[1]));          // corners 2, 3
+  const float2 z0 = make_float2(1 - f[2], 1 - f[2]), z1 = make_float2(f[2], f[2]);
+  const float2 w01 = __fmul2_rn(wxy0, z0), w23 = __fmul2_rn(wxy1, z0);
+  const float2 w45 = __fmul2_rn(wxy0, z1), w67 = __fmul2_rn(wxy1, z1);
+  const float w[8] = {w01.x, w01.y, w23.x, w23.y, w45.x, w45.y, w67.x, w67.y};
+  float2 r = make_float2(0.f, 0.f);
+#pragma unroll
+  for (int c = 0; c < 8; c++) r = __ffma2_rn(make_float2(w[c], w[c]), cv.get(c), r);
+  return r;
+}
+
 }  // namespace ns

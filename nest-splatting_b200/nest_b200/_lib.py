@@ -26,7 +26,7 @@ EXPORTED = [
     "ns_radix_sort_pairs_noalloc", "ns_backward_scratch_bytes", "ns_backward_scratch_bytes_deterministic",
     "ns_rasterize_backward",
     "ns_normal_error", "ns_normal_error_scratch_bytes", "ns_normal_error_backward", "ns_mlp_backward",
-    "ns_allmap_decode",
+    "ns_allmap_decode", "ns_grid_encode_forward", "ns_grid_encode_backward", "ns_read_binning",
 ]
 
 
@@ -165,6 +165,15 @@ def load() -> C.CDLL:
     lib.ns_normal_error_scratch_bytes.argtypes = [i32, i32]
     lib.ns_normal_error_backward.restype = C.c_int
     lib.ns_normal_error_backward.argtypes = [vp, vp, vp, vp, i32, i32, vp, i64, vp, vp, sz, vp]
+    lib.ns_read_binning.restype = C.c_int
+    lib.ns_read_binning.argtypes = [vp, sz, i32, vp, sz, vp, sz, i32, i32, i64, vp, vp, vp, vp, vp, vp, vp]
+    u32, f32 = C.c_uint32, C.c_float
+    lib.ns_grid_encode_forward.restype = C.c_int
+    lib.ns_grid_encode_forward.argtypes = [vp, vp, i32, vp, vp, u32, u32, u32, u32, f32, u32, vp, u32, i32, u32,
+                                           vp]
+    lib.ns_grid_encode_backward.restype = C.c_int
+    lib.ns_grid_encode_backward.argtypes = [vp, vp, vp, i32, vp, vp, u32, u32, u32, u32, f32, u32, vp, vp, u32,
+                                            i32, u32, vp]
     _lib = lib
     return lib
 

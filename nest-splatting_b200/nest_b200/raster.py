@@ -175,6 +175,30 @@ def rasterize_forward(cfg: RasterConfig, means3D, scales, rotations, opacities, 
     return int(n.value), out_color, out_others, radii, cover, trans, scratch
 
 
+def read_binning(scratch: Scratch, P: int, width: int, height: int, num_rendered: int) -> dict:
+    """What the last forward call on `scratch` left in it (ns_read_binning):
+    point_list [num_rendered] int32 (surfel ids per tile in depth order),
+    ranges [tiles, 2] int32, tile_rects [P, 4] int16 (x0, y0, x1, y1),
+    depths [P], pixel_boxes [P, 4] (x0, x1, y0, y1), means2D [P, 2]."""
+    lib = _lib.load()
+    dev = scratch.geom.device
+    tiles = ((width + 15) // 16) * ((height + 15) // 16)
+    out = dict(point_list=torch.empty(max(num_rendered, 1), dtype=torch.int32, device=dev),
+               ranges=torch.empty((tiles, 2), dtype=torch.int32, device=dev),
+               tile_rects=torch.empty((max(P, 1), 4), dtype=torch.int16, device=dev),
+               depths=torch.empty(max(P, 1), dtype=torch.float32, device=dev),
+               pixel_boxes=torch.empty((max(P, 1), 4), dtype=torch.float32, device=dev),
+               means2D=torch.empty((max(P, 1), 2), dtype=torch.float32, device=dev))
+    binning = scratch.binning
+    check("ns_read_binning", lib.ns_read_binning(
+        scratch.geom.data_ptr(), scratch.geom.numel(), P, ptr(binning), 0 if binning is None else binning.numel(),
+        scratch.image.data_ptr(), scratch.image.numel(), width, height, num_rendered, ptr(out["point_list"]),
+        ptr(out["ranges"]), ptr(out["tile_rects"]), ptr(out["depths"]), ptr(out["pixel_boxes"]),
+        ptr(out["means2D"]), _lib.stream_handle(dev)))
+    out["point_list"] = out["point_list"][:num_rendered]
+    return {k: v[:P] if k in ("tile_rects", "depths", "pixel_boxes", "means2D") else v for k, v in out.items()}
+
+
 def rasterize_backward(cfg: RasterConfig, means3D, scales, rotations, opacities, homotrans, ap_level, features,
                        offsets, gridrange, radii, num_rendered: int, scratch: Scratch, dL_dcolor, dL_dothers,
                        return_accumulators: bool = False, shapes=None, colors_precomp=None):

@@ -179,7 +179,7 @@ void render_backward(int W, int H, const uint32_t* ranges, const uint32_t* point
                      const float* dL_dout_others, R* dL_dtable, R* dL_dtransMat, R* dL_dhomoMat,
                      R* dL_dmean2D, R* dL_dnormal, R* dL_dopacity, R* dL_gradsum, int kernel_type,
                      const float* shapes, R* dL_dshapes, int render_mode, int hybrid_levels,
-                     int total_levels, const float* gauss, R* dL_dcolors) {
+                     int total_levels, const float* gauss, R* dL_dcolors, int row_stride) {
   using V = V3<R>;
   const int base_mode = render_mode & 0xFF;
   const int pg = hybrid_levels * LD, hd = (int)L * LD, td = total_levels * LD;
@@ -191,6 +191,9 @@ void render_backward(int W, int H, const uint32_t* ranges, const uint32_t* point
     std::vector<R> dL_dpixel(C), accum_rec(C), last_color(C), grad_feat(C), feat(C);
     std::vector<R> hfeat(hd > 0 ? hd : 1), grad_hash(hd > 0 ? hd : 1);
     const int tx = tile % gx, ty = tile / gx;
+    // row_stride > 1: only tile rows ty % row_stride == 0 (a bounded sample; the
+    // caller's upstream gradient is zero on the others)
+    if (row_stride > 1 && ty % row_stride != 0) continue;
     const uint32_t r0 = ranges[2 * tile], r1 = ranges[2 * tile + 1];
     for (int py = ty * kBlock; py < std::min(H, (ty + 1) * kBlock); py++) {
       for (int px = tx * kBlock; px < std::min(W, (tx + 1) * kBlock); px++) {
@@ -622,13 +625,14 @@ void oracle_render_backward(int W, int H, const uint32_t* ranges, const uint32_t
                             float* dL_dmean2D, float* dL_dnormal, float* dL_dopacity,
                             float* dL_gradsum, int kernel_type, const float* shapes,
                             float* dL_dshapes, int render_mode, int hybrid_levels,
-                            int total_levels, const float* gauss, float* dL_dcolors) {
+                            int total_levels, const float* gauss, float* dL_dcolors,
+                            int row_stride) {
   render_backward<float>(W, H, ranges, point_list, means2D, transMat, normal_opacity, homotrans,
                          ap_level, table, offsets, gridrange, C, LD, L, S, Hres, align_corners,
                          interp, contract, beta, final_T, n_contrib, dL_dout_color, dL_dout_others,
                          dL_dtable, dL_dtransMat, dL_dhomoMat, dL_dmean2D, dL_dnormal, dL_dopacity,
                          dL_gradsum, kernel_type, shapes, dL_dshapes, render_mode, hybrid_levels,
-                         total_levels, gauss, dL_dcolors);
+                         total_levels, gauss, dL_dcolors, row_stride);
 }
 
 // Working precision double: the same formulas and decisions, without float
@@ -646,13 +650,14 @@ void oracle_render_backward_f64(int W, int H, const uint32_t* ranges, const uint
                                 double* dL_dmean2D, double* dL_dnormal, double* dL_dopacity,
                                 double* dL_gradsum, int kernel_type, const float* shapes,
                                 double* dL_dshapes, int render_mode, int hybrid_levels,
-                                int total_levels, const float* gauss, double* dL_dcolors) {
+                                int total_levels, const float* gauss, double* dL_dcolors,
+                                int row_stride) {
   render_backward<double>(W, H, ranges, point_list, means2D, transMat, normal_opacity, homotrans,
                           ap_level, table, offsets, gridrange, C, LD, L, S, Hres, align_corners,
                           interp, contract, beta, final_T, n_contrib, dL_dout_color,
                           dL_dout_others, dL_dtable, dL_dtransMat, dL_dhomoMat, dL_dmean2D,
                           dL_dnormal, dL_dopacity, dL_gradsum, kernel_type, shapes, dL_dshapes,
-                          render_mode, hybrid_levels, total_levels, gauss, dL_dcolors);
+                          render_mode, hybrid_levels, total_levels, gauss, dL_dcolors, row_stride);
 }
 
 void oracle_preprocess_backward(int P, const float* means3D, const float* scales,

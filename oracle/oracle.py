@@ -63,7 +63,7 @@ def load() -> C.CDLL:
     lib.oracle_num_threads.restype = i32
     lib.oracle_render_backward.argtypes = [i32, i32, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, i32, i32, u32, f32,
                                            u32, i32, u32, i32, f32, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp,
-                                           i32, vp, vp, i32, i32, i32, vp, vp]
+                                           i32, vp, vp, i32, i32, i32, vp, vp, i32]
     lib.oracle_preprocess_backward.argtypes = [i32, vp, vp, vp, vp, vp, vp, vp, i32, i32, f32, f32, vp, vp, vp,
                                                vp, vp, vp, vp]
     lib.oracle_render_backward_f64.argtypes = lib.oracle_render_backward.argtypes
@@ -253,12 +253,14 @@ def forward(means3D, scales, rotations, opacities, homotrans, ap_level, table_f3
 def render_backward(pre, vals, ranges, fwd, homotrans, ap_level, table_f32, offsets, gridrange, W, H, C_out, LD,
                     L, S, Hres, dL_dcolor, dL_dothers, align_corners=False, interp=0, contract=False, beta=0.0,
                     f64=False, kernel_type=0, shapes=None, render_mode=0, hybrid_levels=0, total_levels=0,
-                    gauss=None):
+                    gauss=None, row_stride=1):
     """renderCUDAsurfelBackward<C> mode 0 restated (nest_oracle_bw.cpp). `fwd` is the
     dict returned by render(). Returns the render-pass gradients (reference layouts).
     f64=True evaluates the same formulas in double (float64 outputs). kernel_type
     1-3 take per-surfel `shapes` [P] and add dL_dshapes [P]. Render modes 4 / 12 /
-    14 take the per-surfel rows `gauss` and add dL_dcolors (same shape)."""
+    14 take the per-surfel rows `gauss` and add dL_dcolors (same shape).
+    row_stride > 1 walks only tile rows ty % row_stride == 0 (the upstream
+    gradient must be zero on the others, e.g. after a sampled forward)."""
     lib = load()
     P = pre["radii"].shape[0]
     table = _f32(table_f32)
@@ -289,7 +291,7 @@ def render_backward(pre, vals, ranges, fwd, homotrans, ap_level, table_f32, offs
                                _p(g["dL_dnormal"]), _p(g["dL_dopacity"]), _p(g["dL_gradsum"]), int(kernel_type),
                                _p(shapes if kernel_type != 0 else None), _p(g["dL_dshapes"]), int(render_mode),
                                int(hybrid_levels), int(total_levels), _p(gauss if render_mode != 0 else None),
-                               _p(g.get("dL_dcolors")))
+                               _p(g.get("dL_dcolors")), int(row_stride))
     return g
 
 

@@ -44,3 +44,39 @@ def small_scene(n=2000, width=100, height=70, table_range=1.0, seed=11, log_scal
 def psnr(a: np.ndarray, b: np.ndarray, peak: float = 1.0) -> float:
     mse = float(np.mean((np.asarray(a, np.float64) - np.asarray(b, np.float64)) ** 2))
     return float("inf") if mse == 0 else 10 * np.log10(peak * peak / mse)
+
+
+def compare(out, got_color, got_allmap, tol=2e-3, max_bad_frac=1e-3, rows=None, feat_tol=None):
+    """max-abs <= tol per channel (features, depth, alpha, normal, median depth,
+    distortion, position) on at least 99.9% of the pixels, and PSNR >= 60 dB.
+
+    The remaining pixels are threshold decisions that flip between the CPU and
+    GPU float evaluation (FMA contraction and expf ulps differ): a sample at
+    alpha = 1/255 or T = 1e-4 kept on one side and dropped on the other (the
+    count channel differs there), or the hit point switching between the
+    surfel plane and its centre at rho3d == rho2d (forward.cu:855-857, 1102-1109),
+    which moves the hash lookup to another position. Both are discrete events
+    of probability ~1e-4 per pixel; a systematic error fails the 99.9% bound.
+
+    rows: optional pixel-row selection (e.g. the tile rows a sampled oracle
+    render covered); only those rows are compared. feat_tol: tolerance of the
+    feature channels when it must differ from tol (a table of small entries
+    needs one scaled to its magnitude, or any error would pass)."""
+    ref_c, ref_o = out["out_color"], out["out_others"]
+    if rows is not None:
+        ref_c, ref_o = ref_c[:, rows], ref_o[:, rows]
+        got_color, got_allmap = got_color[:, rows], got_allmap[:, rows]
+    npx = ref_c.shape[1] * ref_c.shape[2]
+    flips = got_allmap[7] != ref_o[7]
+    assert flips.mean() <= max_bad_frac, ("count flips", flips.mean())
+    err_c = np.abs(got_color - ref_c).max(axis=0)
+    ft = tol if feat_tol is None else feat_tol
+    assert (err_c > ft).sum() <= max(1, int(max_bad_frac * npx)), ("features", (err_c > ft).sum(), err_c.max())
+    for ch in range(14):
+        if ch == 7:
+            continue
+        err = np.abs(got_allmap[ch] - ref_o[ch])
+        scale = max(1.0, np.abs(ref_o[ch]).max())
+        assert (err > tol * scale).sum() <= max(1, int(max_bad_frac * npx)), (ch, err.max())
+    assert psnr(got_color, ref_c, peak=max(1.0, np.abs(ref_c).max())) >= 60
+    assert psnr(got_allmap[1], ref_o[1]) >= 60

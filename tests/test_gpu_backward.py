@@ -98,11 +98,13 @@ def oracle_grads(scene, inputs, gc, go, **kw):
     rkw = {k: v for k, v in kw.items() if k in ("interp", "contract", "beta", "align_corners", "kernel_type",
                                                  "shapes")}
     f64 = bool(kw.get("f64", False))
+    stride = int(kw.get("row_stride", 1))
     table = g.table.float().numpy()
     common = (inputs["homotrans"].numpy(), inputs["ap_level"].numpy(), table, g.offsets.numpy(),
               g.gridrange.numpy(), W, H, g.channels, g.level_dim, g.levels, g.S, g.base_resolution)
-    fwd = oracle.render(pre, vals, ranges, *common, **rkw)
-    gr = oracle.render_backward(pre, vals, ranges, fwd, *common, gc.numpy(), go.numpy(), f64=f64, **rkw)
+    fwd = oracle.render(pre, vals, ranges, *common, row_stride=stride, **rkw)
+    gr = oracle.render_backward(pre, vals, ranges, fwd, *common, gc.numpy(), go.numpy(), f64=f64,
+                                row_stride=stride, **rkw)
     pg = oracle.preprocess_backward(inputs["means3D"].numpy(), inputs["scales"].numpy(),
                                     inputs["rotations"].numpy(), pre, gr, vm, pm, W, H, cam.tanfovx, cam.tanfovy,
                                     f64=f64)

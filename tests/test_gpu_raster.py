@@ -12,8 +12,7 @@ import pytest
 import torch
 
 import diff_surfel_rasterization as dsr
-from helpers import api_inputs, oracle_render, psnr, small_scene
-from nest_b200 import synth
+from helpers import api_inputs, compare, oracle_render, small_scene
 
 pytestmark = pytest.mark.gpu
 TOL = 2e-3
@@ -46,33 +45,6 @@ def run_api(scene, inputs, fp16=True, record=False, max_int=0, beta=0.0, contrac
             render_mode=0)
     torch.cuda.synchronize()
     return color.cpu().numpy(), radii.cpu().numpy(), allmap.cpu().numpy(), trans.cpu().numpy(), cover.cpu().numpy()
-
-
-def compare(out, got_color, got_allmap, tol=TOL, max_bad_frac=1e-3):
-    """max-abs <= tol per channel (features, depth, alpha, normal, median depth,
-    distortion, position) on at least 99.9% of the pixels, and PSNR >= 60 dB.
-
-    The remaining pixels are threshold decisions that flip between the CPU and
-    GPU float evaluation (FMA contraction and expf ulps differ): a sample at
-    alpha = 1/255 or T = 1e-4 kept on one side and dropped on the other (the
-    count channel differs there), or the hit point switching between the
-    surfel plane and its centre at rho3d == rho2d (forward.cu:855-857, 1102-1109),
-    which moves the hash lookup to another position. Both are discrete events
-    of probability ~1e-4 per pixel; a systematic error fails the 99.9% bound."""
-    ref_c, ref_o = out["out_color"], out["out_others"]
-    npx = ref_c.shape[1] * ref_c.shape[2]
-    flips = got_allmap[7] != ref_o[7]
-    assert flips.mean() <= max_bad_frac, ("count flips", flips.mean())
-    err_c = np.abs(got_color - ref_c).max(axis=0)
-    assert (err_c > tol).sum() <= max(1, int(max_bad_frac * npx)), ("features", (err_c > tol).sum(), err_c.max())
-    for ch in range(14):
-        if ch == 7:
-            continue
-        err = np.abs(got_allmap[ch] - ref_o[ch])
-        scale = max(1.0, np.abs(ref_o[ch]).max())
-        assert (err > tol * scale).sum() <= max(1, int(max_bad_frac * npx)), (ch, err.max())
-    assert psnr(got_color, ref_c, peak=max(1.0, np.abs(ref_c).max())) >= 60
-    assert psnr(got_allmap[1], ref_o[1]) >= 60
 
 
 @pytest.mark.parametrize("fp16", [True, False])
@@ -181,19 +153,6 @@ def test_mark_visible():
     vm = cam.world_view_transform.numpy()
     z = pts.numpy() @ vm[:3, 2] + vm[3, 2]
     assert np.array_equal(vis, z > 0.2)
-
-
-def test_config1_fullsize_parity():
-    """BASELINE config 1 at full size (200k surfels, 800x800) on the default table."""
-    sc = synth.config1()
-    inp = api_inputs(sc)
-    out, pre, n = oracle_render(sc, inp)
-    color, radii, allmap, _, _ = run_api(sc, inp)
-    assert np.abs(color - out["out_color"]).max() <= TOL
-    for ch in (0, 1, 2, 3, 4, 5):
-        err = np.abs(allmap[ch] - out["out_others"][ch])
-        assert np.quantile(err, 0.9999) <= TOL * max(1.0, np.abs(out["out_others"][ch]).max()), ch
-    assert psnr(allmap[1], out["out_others"][1]) >= 60
 
 
 def test_scene_from_reference_ply_renders_like_the_direct_inputs(tmp_path):
