@@ -21,6 +21,7 @@ from __future__ import annotations
 
 import argparse
 import json
+import math
 import os
 import statistics
 import subprocess
@@ -202,6 +203,167 @@ def train_step_timing(sc, cam, dev, steps, warmup=2):
             "loss_first": round(float(losses[0].detach()), 6)}
 
 
+def gather_peak(fr, dev, cam, lookups=64, reps=5):
+    """The blend's gather roofline: hash-grid lookups per second of a kernel that
+    does nothing else (ns_gather_probe: the blend's lookup code at full
+    occupancy, four lookups in flight per thread), in corner bytes per second,
+    for two point patterns on the same table:
+      * "coherent" (the roofline denominator): the blend's pattern, a warp's 32
+        lanes at the hit points of a 16 x 2 pixel strip on one surfel, all 16
+        levels; the strip spacing is this camera's pixel footprint at the scene
+        (distance 4 - 1 from the camera) in grid units;
+      * "random_hashed": every lane an independent point of the hashed levels
+        (5-15), the pattern's worst case, for context."""
+    import torch
+
+    from nest_b200 import _lib
+    lib = _lib.load()
+    g = fr.grid
+    T = int(g.offsets[1] - g.offsets[0])
+    level0 = next(l for l in range(g.levels)
+                  if (int(math.ceil(2 ** (l * g.S) * g.base_resolution - 1)) + 2) ** 3 > T)
+    sms = torch.cuda.get_device_properties(dev).multi_processor_count
+    blocks = sms * 8
+    sink = torch.empty(blocks * 256, dtype=torch.float32, device=dev)
+    fp16 = int(fr.table.dtype == torch.float16)
+    stream = _lib.stream_handle(dev)
+    grid_range = float(g.gridrange[1] - g.gridrange[0])
+    spacing = 2.0 * cam.tanfovx / cam.width * 3.0 / grid_range  # pixel footprint at distance 3
+    out = {}
+    for name, l0, nl, sp in (("coherent", 0, g.levels, spacing), ("random_hashed", level0, g.levels - level0, 0.0)):
+        def run():
+            _lib.check("ns_gather_probe", lib.ns_gather_probe(
+                fr.table.data_ptr(), fp16, fr.offsets.data_ptr(), l0, nl, float(g.S), g.base_resolution, lookups,
+                float(sp), blocks, sink.data_ptr(), stream))
+
+        for _ in range(2):
+            run()
+        torch.cuda.synchronize()
+        times = []
+        for _ in range(reps):
+            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s.record()
+            run()
+            e.record()
+            torch.cuda.synchronize()
+            times.append(s.elapsed_time(e))
+        ms = statistics.median(times)
+        nbytes = blocks * 256 * lookups * 8 * fr.table.element_size() * fr.table.shape[1]
+        out[name] = {"gbs": round(nbytes / (ms * 1e-3) / 1e9, 1), "ms": round(ms, 4), "levels": [l0, l0 + nl - 1],
+                     "spacing_grid_units": round(sp, 6)}
+    out["lookups"] = blocks * 256 * lookups
+    out["gbs"] = out["coherent"]["gbs"]
+    return out
+
+
+def rvq_timing(dev, hbm_peak, sizes=(200_000, 1_000_000, 3_000_000), iters=20, warmup=3):
+    """RVQ decode (BASELINE config 0 codebooks and indices) on the GPU at the
+    sizes the scope names: median device time of `iters` runs after `warmup`,
+    L2 flushed before each (the 200k output fits in L2)."""
+    import torch
+
+    from nest_b200 import raster, synth
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    out = {}
+    for n in sizes:
+        cb, idx = synth.config0(n)
+        cb, idx = cb.to(dev), idx.to(dev)
+        dec = torch.empty((n, cb.shape[2]), dtype=torch.float32, device=dev)
+        for _ in range(warmup):
+            raster.rvq_decode(idx, cb, dec)
+        times = []
+        for _ in range(iters):
+            flush_l2(flush)
+            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s.record()
+            raster.rvq_decode(idx, cb, dec)
+            e.record()
+            torch.cuda.synchronize()
+            times.append(s.elapsed_time(e))
+        ms = statistics.median(times)
+        nbytes = n * (cb.shape[0] + 4 * cb.shape[2])
+        out[str(n)] = {"ms": round(ms, 4), "gbs": round(nbytes / (ms * 1e-3) / 1e9, 1),
+                       "frac_of_hbm": round(nbytes / (ms * 1e-3) / 1e9 / hbm_peak, 4)}
+        del cb, idx, dec
+    return out
+
+
+def rvq_cpu_timing(n=200_000, iters=20, warmup=3):
+    """The reference's PyTorch CPU path of the RVQ decode:
+    index_select + in-order adds on the host cores, all of them."""
+    import torch
+
+    from nest_b200 import synth
+    from oracle import oracle
+    prev = torch.get_num_threads()
+    cores = os.cpu_count() or 1
+    torch.set_num_threads(cores)
+    try:
+        cb, idx = synth.config0(n)
+        for _ in range(warmup):
+            oracle.rvq_decode_torch(idx, cb)
+        times = []
+        for _ in range(iters):
+            t0 = time.perf_counter()
+            oracle.rvq_decode_torch(idx, cb)
+            times.append(time.perf_counter() - t0)
+    finally:
+        torch.set_num_threads(prev)
+    sec = statistics.median(times)
+    nbytes = n * (cb.shape[0] + 4 * cb.shape[2])
+    return {"surfels": n, "ms": round(sec * 1e3, 3), "surfels_per_s": round(n / sec, 1),
+            "gbs": round(nbytes / sec / 1e9, 3), "cores": cores, "threads": cores,
+            "statistic": f"median of {iters} after {warmup} warm-ups",
+            "path": "torch CPU: index_select per stage + in-order fp32 adds (oracle.rvq_decode_torch)"}
+
+
+def config1_timing(dev, steps=20, warmup=3):
+    """single-view forward render of 200k surfels at 800x800
+    (rasterizer forward with its instance-count read-back, then the MLP with the
+    alpha mask), device-timed per frame with the L2 flushed before each."""
+    import torch
+
+    from nest_b200 import raster, synth
+    sc = synth.config1()
+    means, scales, rots, opac = synth.activate(sc.base)
+    homo = synth.build_homotrans(sc.base)
+    cam, g = sc.camera, sc.grid
+    t = [x.to(dev).contiguous() for x in (means, scales, rots, opac.reshape(-1), homo,
+                                          sc.ap_level.reshape(-1))]
+    cfg = raster.RasterConfig(image_height=cam.height, image_width=cam.width, tanfovx=cam.tanfovx,
+                              tanfovy=cam.tanfovy, viewmatrix=cam.world_view_transform.to(dev).contiguous(),
+                              projmatrix=cam.full_proj_transform.to(dev).contiguous(), levels=g.levels, S=g.S,
+                              base_resolution=g.base_resolution, channels=g.channels, level_dim=g.level_dim)
+    table, offs, gr = g.table.to(dev), g.offsets.to(dev), g.gridrange.to(dev)
+    weights = raster.pack_mlp(sc.mlp).to(dev)
+    scratch = raster.Scratch()
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+
+    def frame():
+        n, color, others, radii, _, _, _ = raster.rasterize_forward(cfg, *t, table, offs, gr, scratch=scratch)
+        raster.mlp_forward(color, weights, alpha=others[1])
+        return n
+
+    for _ in range(warmup):
+        frame()
+    torch.cuda.synchronize()
+    times = []
+    for _ in range(steps):
+        flush_l2(flush)
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        n = frame()
+        e.record()
+        torch.cuda.synchronize()
+        times.append(s.elapsed_time(e))
+    ms = statistics.median(times)
+    return {"workload": "config 1: 200k surfels, 800x800, 16x2 fp16 hash grid (U(+-1e-4)), MLP 32-64-64-3",
+            "ms_per_frame": round(ms, 4), "frames_per_s": round(1000.0 / ms, 2),
+            "mpix_per_s": round(cam.width * cam.height / 1e6 * 1000.0 / ms, 3), "instances": int(n),
+            "statistic": f"median of {steps} frames after {warmup} warm-ups, L2 flushed before each",
+            "path": "raster.rasterize_forward (ns_rasterize_forward, one count read-back) + ns_mlp_forward"}
+
+
 def run_ours(args):
     import torch
     import torch.distributed as dist
@@ -224,11 +386,13 @@ def run_ours(args):
     from nest_b200.views import DecodeRing, DecodeShard, shard_range
     lo, hi = shard_range(P, world, rank)
     if world > 1:
-        shard = DecodeShard.create(fr.rvq_idx, fr.dims, world, rank)
+        # Every rank decodes all 59 columns of its surfel range; the all-gather
+        # carries the 10 the rasterizer reads (views.DecodeShard).
+        shard = DecodeShard.create(fr.rvq_idx, fr.dims, world, rank, columns=synth.BASE_DIMS)
         # Frame i+1's decode + all-gather runs on a side stream while frame i
         # renders (two attribute buffers); every step still decodes and
         # exchanges its own frame.
-        ring = DecodeRing(fr.rvq_idx, fr.dims, world, rank)
+        ring = DecodeRing(fr.rvq_idx, fr.dims, world, rank, columns=synth.BASE_DIMS)
 
     def step(i, events=None, n=None):
         if world > 1:
@@ -325,6 +489,7 @@ def run_ours(args):
     d2h = host_rgb[0].numel() * 4
 
     exchange = exchange_timing(shard, fr.codebooks, dev, P, fr.stages, fr.dims) if world > 1 else None
+    identical = frame_identity(fr, shard, cam, view, proj, dev) if world > 1 else None
     graph = graph_timing(fr, cam, view, proj, flush, args.steps) if world == 1 else None
 
     # Work statistics of the (identical) frames.
@@ -340,6 +505,7 @@ def run_ours(args):
     rvq_gbs = rvq_bytes / (stage_ms["decode"] * 1e-3) / 1e9 if world == 1 else None
     gather_tbs = samples * 16 * 8 * 4 / (blend_ms * 1e-3) / 1e12
     gather_gbs = gather_tbs * 1e3
+    gpeak = gather_peak(fr, dev, cam)
 
     line = {
         "metric": METRIC, "value": round(value, 3), "unit": UNIT, "n_gpus": world, "steps": args.steps,
@@ -356,17 +522,19 @@ def run_ours(args):
         "rvq_decode": {"gbs": round(rvq_gbs, 1) if rvq_gbs else None,
                        "frac_of_hbm": round(rvq_gbs / hbm_peak, 4) if rvq_gbs else None,
                        "bytes_per_surfel": fr.stages + 4 * fr.dims},
-        "roofline": {"kernel": "blend_kernel<__half, false>", "bound": "hbm",
-                     "achieved": round(max(achieved, gather_gbs), 1), "peak": hbm_peak, "unit": "GB/s",
-                     "frac": round(max(achieved, gather_gbs) / hbm_peak, 4), "traffic": traffic,
-                     "peak_kind": peak_kind,
-                     "figure": "the larger of (i) unique DRAM bytes and (ii) hash-table gather bytes "
-                               "(blended samples x 16 levels x 8 corners x 4 B fp16 pair) per launch time; "
-                               "(ii) is served mostly by L1/L2, no L2 peak is measured, so the HBM copy "
-                               "peak is the denominator of both",
-                     "dram_figure": {"achieved": round(achieved, 1), "algorithmic_bytes": int(blend_bytes)},
-                     "gather_figure": {"achieved": round(gather_gbs, 1),
-                                       "algorithmic_bytes": int(samples * 16 * 8 * 4)},
+        "roofline": {"kernel": "blend_kernel<__half, false>", "bound": "l1/l2 gather",
+                     "achieved": round(gather_gbs, 1), "peak": gpeak["gbs"], "unit": "GB/s",
+                     "frac": round(gather_gbs / gpeak["gbs"], 4), "traffic": traffic,
+                     "peak_kind": "measured in this run (gather_peak: ns_gather_probe on the same table)",
+                     "figure": "hash-table gather bytes (blended samples x 16 levels x 8 corners x 4 B fp16 "
+                               "pair) per blend launch time, against the gather rate of a lookup-only kernel "
+                               "with the blend's point pattern (gather_peak.coherent); the launch's DRAM "
+                               "traffic is far below HBM (dram_figure)",
+                     "gather_peak": gpeak,
+                     "dram_figure": {"achieved": round(achieved, 1), "algorithmic_bytes": int(blend_bytes),
+                                     "peak": hbm_peak, "peak_kind": peak_kind,
+                                     "frac": round(achieved / hbm_peak, 4)},
+                     "gather_figure_vs_hbm": round(gather_gbs / hbm_peak, 4),
                      "hash_gather_tbs": round(gather_tbs, 3)},
         "e2e": {"value": round(world * mpix * 1000.0 / e2e_ms_step, 3), "unit": UNIT,
                 "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h),
@@ -376,8 +544,14 @@ def run_ours(args):
         "gpu_launches": int(launches),
         "clocks": clk.summary(),
     }
+    if world == 1:
+        line["rvq_decode"]["gpu_sizes"] = rvq_timing(dev, hbm_peak)
+        if not args.no_config1:
+            line["config1"] = config1_timing(dev)
     if exchange is not None:
         line["rvq_exchange"] = exchange
+    if identical is not None:
+        line["frame_bit_identical"] = identical
     if graph is not None:
         line["graph_frame"] = graph
     if not args.no_train:
@@ -388,6 +562,7 @@ def run_ours(args):
         line["multiview"] = multiview_timing(world, rank, dev)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(sc, budget_s=args.cpu_budget)
+        line["rvq_decode"]["cpu_config0"] = rvq_cpu_timing()
     if rank == 0:
         print(json.dumps(line), flush=True)
     if world > 1:
@@ -430,9 +605,13 @@ def exchange_timing(shard, codebooks, dev, P, stages, dims, iters=20):
     import torch.distributed as dist
 
     from nest_b200 import raster
+    from nest_b200.views import DecodeShard
     out = {}
     world = shard.world
+    full = DecodeShard.create(shard.idx_shard.new_zeros((P, shard.idx_shard.shape[1])), dims, world, shard.rank)
+    full.idx_shard.copy_(shard.idx_shard)
     for name, fn in (("attributes", lambda: shard.decode_and_gather(codebooks, raster.rvq_decode)),
+                     ("attributes_all_columns", lambda: full.decode_and_gather(codebooks, raster.rvq_decode)),
                      ("indices", lambda: shard.gather_indices_and_decode(codebooks, raster.rvq_decode))):
         for _ in range(3):
             fn()
@@ -447,11 +626,37 @@ def exchange_timing(shard, codebooks, dev, P, stages, dims, iters=20):
         t = torch.tensor([s.elapsed_time(e) / iters], dtype=torch.float64, device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         out[f"{name}_ms"] = round(float(t.item()), 4)
-    out["received_bytes_per_rank"] = {"attributes": int(P * (world - 1) / world) * 4 * dims,
+    out["received_bytes_per_rank"] = {"attributes": int(P * (world - 1) / world) * 4 * shard.columns,
+                                      "attributes_all_columns": int(P * (world - 1) / world) * 4 * dims,
                                       "indices": int(P * (world - 1) / world) * stages}
-    out["note"] = ("attributes: decode own shard + NCCL all-gather of fp32 rows (the frame's path); "
+    out["note"] = (f"attributes: decode all {dims} columns of this rank's rows + NCCL all-gather of the "
+                   f"{shard.columns} fp32 columns the rasterizer reads (the frame's path); "
+                   "attributes_all_columns: the same exchange of every column; "
                    "indices: NCCL all-gather of uint8 indices + decode of all rows on every rank")
+    del full
     return out
+
+
+def frame_identity(fr, shard, cam, view, proj, dev):
+    """N > 1 correctness: this rank's frame rendered from the all-gathered
+    attribute rows (decode sharded over the ranks) against the same frame from
+    a full decode on this rank alone; true when rgb, features and the 14 aux
+    channels are bit-identical on every rank."""
+    import torch
+    import torch.distributed as dist
+
+    from nest_b200 import raster
+    shard.decode_and_gather(fr.codebooks, raster.rvq_decode)
+    fr.decoded = shard.decoded
+    fr.render(cam, view, proj, skip_decode=True)
+    sharded = [fr.rgb.clone(), fr.features.clone(), fr.others.clone()]
+    fr.decoded = torch.empty((fr.P, fr.dims), dtype=torch.float32, device=dev)
+    fr.render(cam, view, proj)  # decodes all rows locally
+    local = [fr.rgb, fr.features, fr.others]
+    same = all(torch.equal(a, b) for a, b in zip(sharded, local))
+    flag = torch.tensor([1 if same else 0], dtype=torch.int32, device=dev)
+    dist.all_reduce(flag, op=dist.ReduceOp.MIN)
+    return bool(flag.item())
 
 
 def oracle_frame(sc, row_stride, threads=None):
@@ -484,7 +689,7 @@ def oracle_frame(sc, row_stride, threads=None):
 
 def cpu_baseline(sc, budget_s=30.0, row_stride=4):
     from oracle import oracle
-    threads = oracle.num_threads()
+    threads = oracle.set_num_threads(os.cpu_count() or 1)
     dt, px = oracle_frame(sc, row_stride)
     return {"value": round(px / dt / 1e6, 4), "unit": UNIT, "cores": threads, "kind": "port",
             "sample": f"one config-2 frame on the CPU oracle (C++/OpenMP restatement): full RVQ decode, "
@@ -501,7 +706,10 @@ def run_reference(args):
     from nest_b200 import synth
     from oracle import oracle
     sc = synth.config2()
-    threads = oracle.num_threads()
+    # every host core, whatever the launcher set (torchrun exports OMP_NUM_THREADS=1)
+    threads = oracle.set_num_threads(os.cpu_count() or 1)
+    import torch
+    torch.set_num_threads(os.cpu_count() or 1)
     # Bounded sample: choose the tile-row stride so that warmup + steps fit ~3 minutes.
     stride = 4
     dt, px = oracle_frame(sc, stride)
@@ -549,7 +757,7 @@ def multiview_timing(world, rank, dev, batches=2):
     mine = camera_share(len(cams), world, rank)
     fr = FrameRenderer(sc, device=dev, capacity=24_000_000)
     if world > 1:
-        shard = DecodeShard.create(fr.rvq_idx, fr.dims, world, rank)
+        shard = DecodeShard.create(fr.rvq_idx, fr.dims, world, rank, columns=synth.BASE_DIMS)
         fr.decoded = shard.decoded
     views = [(cams[i], cams[i].world_view_transform.to(dev).contiguous(),
               cams[i].full_proj_transform.to(dev).contiguous()) for i in mine]
@@ -599,6 +807,7 @@ def main():
     ap.add_argument("--no-train", action="store_true", help="skip the config-4 training-step timing")
     ap.add_argument("--no-multiview", action="store_true", help="skip the config-3 64-view batch timing")
     ap.add_argument("--cpu-budget", type=float, default=30.0)
+    ap.add_argument("--no-config1", action="store_true", help="skip the config-1 single-view timing")
     args = ap.parse_args()
     if args.impl == "reference":
         run_reference(args)

@@ -27,6 +27,7 @@ EXPORTED = [
     "ns_rasterize_backward",
     "ns_normal_error", "ns_normal_error_scratch_bytes", "ns_normal_error_backward", "ns_mlp_backward",
     "ns_allmap_decode", "ns_grid_encode_forward", "ns_grid_encode_backward", "ns_read_binning",
+    "ns_gather_probe",
 ]
 
 
@@ -174,6 +175,8 @@ def load() -> C.CDLL:
     lib.ns_grid_encode_backward.restype = C.c_int
     lib.ns_grid_encode_backward.argtypes = [vp, vp, vp, i32, vp, vp, u32, u32, u32, u32, f32, u32, vp, vp, u32,
                                             i32, u32, vp]
+    lib.ns_gather_probe.restype = C.c_int
+    lib.ns_gather_probe.argtypes = [vp, i32, vp, u32, u32, f32, u32, u32, f32, i32, vp, vp]
     _lib = lib
     return lib
 

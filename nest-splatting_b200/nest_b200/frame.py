@@ -103,7 +103,17 @@ class FrameRenderer:
         fin = _lib.FrameInputs()
         fin.P = self.P
         fin.rvq_idx, fin.codebooks = ptr(idx_t), ptr(self.codebooks)
-        fin.stages, fin.entries, fin.dims = self.stages, self.entries, self.dims
+        # with skip_decode, `decoded` may hold only the leading attribute columns
+        # (e.g. the 10 an exchange gathered): dims is then its row stride; the
+        # decode writes every column, so it needs a full [P, dims] buffer
+        if skip_decode:
+            if self.decoded.dim() != 2 or self.decoded.shape[0] != self.P or self.decoded.shape[1] < 10 \
+                    or not self.decoded.is_contiguous():
+                raise ValueError("decoded must be a contiguous [P, >=10] buffer")
+        elif tuple(self.decoded.shape) != (self.P, self.dims) or not self.decoded.is_contiguous():
+            raise ValueError(f"decoding needs a contiguous [{self.P}, {self.dims}] `decoded` buffer")
+        fin.stages, fin.entries = self.stages, self.entries
+        fin.dims = self.decoded.shape[1] if skip_decode else self.dims
         fin.base, fin.mix, fin.decoded = ptr(self.base), self.mix, ptr(self.decoded)
         fin.ap_level, fin.features = ptr(self.ap_level), ptr(self.table)
         fin.offsets, fin.gridrange = ptr(self.offsets), ptr(self.gridrange)
@@ -168,7 +178,8 @@ class FramePipeline:
         self.ring = None
         if shard is not None:
             from .views import DecodeRing
-            self.ring = DecodeRing(renderer.rvq_idx, renderer.dims, shard.world, shard.rank)
+            self.ring = DecodeRing(renderer.rvq_idx, renderer.dims, shard.world, shard.rank,
+                                   columns=shard.columns)
         d = renderer.device
         self.in_stream = torch.cuda.Stream(device=d)
         self.out_stream = torch.cuda.Stream(device=d)

@@ -8,6 +8,13 @@ gloo on CPU in the tests) -- the only collective of the path.
 Shard layout: the surfel axis is padded to world * ceil(P / world) rows so that
 every rank decodes the same number of rows; rank r owns rows
 [r * shard, (r + 1) * shard) and rows >= P are padding (never read).
+
+Exchanged columns: every rank decodes all D attribute columns of its rows; the
+all-gather carries the first `columns` of them (default all D). The frame's
+rasterizer reads only the 10 geometric columns (mean, log-scale, quaternion,
+opacity logit; the SH and texture-scale columns have no consumer in the render
+path), so a frame exchange with columns = 10 moves 40 B per row instead of
+4 D = 236 B.
 """
 from __future__ import annotations
 
@@ -43,23 +50,34 @@ class DecodeShard:
     world: int
     rank: int
     idx_shard: torch.Tensor   # [shard, K] uint8 (padding rows are zero)
-    dec_shard: torch.Tensor   # [shard, D] fp32
-    dec_full: torch.Tensor    # [world * shard, D] fp32; rows [:P] are the decoded attributes
+    dec_shard: torch.Tensor   # [shard, D] fp32: this rank's rows, every column
+    dec_full: torch.Tensor    # [world * shard, columns] fp32; rows [:P] are the gathered attributes
+    send: torch.Tensor | None = None  # [shard, columns] packed send buffer when columns < D
 
     @classmethod
-    def create(cls, rvq_idx: torch.Tensor, dims: int, world: int, rank: int) -> "DecodeShard":
+    def create(cls, rvq_idx: torch.Tensor, dims: int, world: int, rank: int,
+               columns: int | None = None) -> "DecodeShard":
         P, K = rvq_idx.shape
         s = shard_size(P, world)
         lo, hi = shard_range(P, world, rank)
         dev = rvq_idx.device
+        cols = dims if columns is None else int(columns)
+        if not 0 < cols <= dims:
+            raise ValueError(f"columns must be in [1, {dims}]")
         idx_shard = torch.zeros((s, K), dtype=torch.uint8, device=dev)
         idx_shard[: hi - lo].copy_(rvq_idx[lo:hi])
         dec_shard = torch.empty((s, dims), dtype=torch.float32, device=dev)
-        dec_full = torch.empty((s * world, dims), dtype=torch.float32, device=dev)
-        return cls(P, world, rank, idx_shard, dec_shard, dec_full)
+        dec_full = torch.empty((s * world, cols), dtype=torch.float32, device=dev)
+        send = torch.empty((s, cols), dtype=torch.float32, device=dev) if cols < dims else None
+        return cls(P, world, rank, idx_shard, dec_shard, dec_full, send)
+
+    @property
+    def columns(self) -> int:
+        return self.dec_full.shape[1]
 
     @property
     def decoded(self) -> torch.Tensor:
+        """[P, columns] gathered rows (the frame reads them with row stride `columns`)."""
         return self.dec_full[: self.P]
 
     def upload(self, host_idx: torch.Tensor) -> None:
@@ -68,11 +86,16 @@ class DecodeShard:
         self.idx_shard[: hi - lo].copy_(host_idx[lo:hi], non_blocking=True)
 
     def gather(self, group=None) -> torch.Tensor:
-        """All-gather of the decoded shards into dec_full (every rank gets every row)."""
+        """All-gather of the decoded shards' exchanged columns into dec_full
+        (every rank gets every row)."""
+        src = self.dec_shard
+        if self.send is not None:
+            self.send.copy_(self.dec_shard[:, : self.columns])
+            src = self.send
         if self.world > 1:
-            dist.all_gather_into_tensor(self.dec_full, self.dec_shard, group=group)
+            dist.all_gather_into_tensor(self.dec_full, src, group=group)
         else:
-            self.dec_full.copy_(self.dec_shard)
+            self.dec_full.copy_(src)
         return self.decoded
 
     def gather_indices_and_decode(self, codebooks: torch.Tensor, decode_fn, group=None) -> torch.Tensor:
@@ -85,7 +108,14 @@ class DecodeShard:
             dist.all_gather_into_tensor(self.idx_full, self.idx_shard, group=group)
         else:
             self.idx_full.copy_(self.idx_shard)
-        decode_fn(self.idx_full[: self.P], codebooks, out=self.dec_full[: self.P])
+        if self.send is None:
+            decode_fn(self.idx_full[: self.P], codebooks, out=self.dec_full[: self.P])
+        else:  # every column decoded, the exchanged ones kept
+            if getattr(self, "dec_all", None) is None:
+                self.dec_all = torch.empty((self.P, self.dec_shard.shape[1]), dtype=torch.float32,
+                                           device=self.dec_shard.device)
+            decode_fn(self.idx_full[: self.P], codebooks, out=self.dec_all)
+            self.dec_full[: self.P].copy_(self.dec_all[:, : self.columns])
         return self.decoded
 
     def decode_and_gather(self, codebooks: torch.Tensor, decode_fn, group=None,
@@ -107,8 +137,8 @@ class DecodeRing:
     order, so the collectives match. On CPU (gloo) the calls run in order.
     """
 
-    def __init__(self, rvq_idx: torch.Tensor, dims: int, world: int, rank: int):
-        self.shards = [DecodeShard.create(rvq_idx, dims, world, rank) for _ in range(2)]
+    def __init__(self, rvq_idx: torch.Tensor, dims: int, world: int, rank: int, columns: int | None = None):
+        self.shards = [DecodeShard.create(rvq_idx, dims, world, rank, columns) for _ in range(2)]
         dev = rvq_idx.device
         self.cuda = dev.type == "cuda"
         if self.cuda:

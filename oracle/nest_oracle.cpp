@@ -404,6 +404,16 @@ void oracle_rvq_decode(int64_t n, int K, int E, int Dm, const uint8_t* idx, cons
   }
 }
 
+// Threads of the OpenMP regions from now on (n <= 0: leave unchanged); a
+// launcher's OMP_NUM_THREADS=1 would otherwise pin the CPU baseline to one core.
+void oracle_set_num_threads(int n) {
+#ifdef _OPENMP
+  if (n > 0) omp_set_num_threads(n);
+#else
+  (void)n;
+#endif
+}
+
 int oracle_num_threads() {
 #ifdef _OPENMP
   return omp_get_max_threads();

@@ -320,5 +320,13 @@ def num_threads() -> int:
     return int(load().oracle_num_threads())
 
 
+def set_num_threads(n: int) -> int:
+    """Sets the oracle's OpenMP thread count; returns the count now in effect."""
+    lib = load()
+    lib.oracle_set_num_threads.argtypes = [C.c_int]
+    lib.oracle_set_num_threads(int(n))
+    return num_threads()
+
+
 if __name__ == "__main__":
     print(build(), os.cpu_count())

@@ -1,16 +1,17 @@
 """Run by test_gpu_multi.py under torch.distributed.run with two ranks (one GPU
-each): the sharded FramePipeline, whose next frame's decode and all-gather run
-ahead of the current render, must give the images of frames rendered one at a
-time with the exchange in line. Exits non-zero on any difference."""
+each): the sharded FramePipeline (each rank decodes its surfel range, the
+10 geometric attribute columns are all-gathered, the next frame's exchange runs
+ahead of the current render) must give, bit for bit, the images of the same
+frames rendered on one GPU alone from a full local decode. Exits non-zero on
+any difference."""
 import os, sys, torch, torch.distributed as dist
 from datetime import timedelta
 HERE = os.path.dirname(os.path.abspath(__file__))
 sys.path[:0] = [os.path.join(HERE, "..", "nest-splatting_b200"), os.path.join(HERE, ".."), HERE]
 from helpers import small_scene
 from nest_b200.frame import FrameRenderer, FramePipeline
-from nest_b200.views import DecodeShard, shard_range
+from nest_b200.views import DecodeShard
 from nest_b200.camera import orbit_camera
-from nest_b200 import raster
 rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
 torch.cuda.set_device(rank)
 dist.init_process_group("nccl", timeout=timedelta(seconds=60), device_id=torch.device("cuda", rank))
@@ -24,16 +25,16 @@ host_idx = [s.pin_memory() for s in streams]
 host_cam = [torch.stack([c.world_view_transform, c.full_proj_transform]).contiguous().pin_memory() for c in cams]
 n = 6
 host_rgb = [torch.empty((3, H, W)).pin_memory() for _ in range(n)]
-shard = DecodeShard.create(fr.rvq_idx, fr.dims, world, rank)
+shard = DecodeShard.create(fr.rvq_idx, fr.dims, world, rank, columns=10)
 pipe = FramePipeline(fr, shard)
 pipe.run(n, cams[0], lambda i: host_idx[i % 2], lambda i: host_cam[i % 2], lambda i: host_rgb[i])
 torch.cuda.synchronize()
 ok = True
-lo, hi = shard_range(shard.P, world, rank)
+local = torch.empty((fr.P, fr.dims), dtype=torch.float32, device=fr.device)
 for i in range(n):
-    shard.idx_shard[: hi - lo].copy_(streams[i % 2][lo:hi].cuda())
-    fr.decoded = shard.decode_and_gather(fr.codebooks, raster.rvq_decode)
-    ref = fr.render(cams[i % 2], skip_decode=True).cpu()
+    # the single-GPU frame: every row decoded on this GPU, no exchange
+    fr.decoded = local
+    ref = fr.render(cams[i % 2], rvq_idx=streams[i % 2].to(fr.device)).cpu()
     same = torch.equal(ref, host_rgb[i])
     ok &= same
     print(rank, i, same, float(ref.abs().sum()), flush=True)

@@ -51,8 +51,19 @@ def _worker(rank, world, port, n, result_dir):
             assert got.data_ptr() == ring.shards[i % 2].decoded.data_ptr()
             assert torch.equal(got, full)
             ring.release(i)
-        torch.save({"full": full, "alt": alt.clone(), "views": camera_share(64, world, rank)},
-                   os.path.join(result_dir, f"rank{rank}.pt"))
+        # The frame's exchange: every column decoded, the 10 geometric ones gathered.
+        sh10 = DecodeShard.create(idx, cb.shape[2], world, rank, columns=synth.BASE_DIMS)
+        part = sh10.decode_and_gather(cb, _decode_cpu).clone()
+        assert part.shape == (n, synth.BASE_DIMS) and sh10.dec_shard.shape[1] == cb.shape[2]
+        sh10.dec_full.zero_()
+        part_alt = sh10.gather_indices_and_decode(cb, _decode_cpu).clone()
+        ring10 = DecodeRing(idx, cb.shape[2], world, rank, columns=synth.BASE_DIMS)
+        for i in range(2):
+            ring10.prefetch(i, cb, _decode_cpu)
+            assert torch.equal(ring10.acquire(i), part)
+            ring10.release(i)
+        torch.save({"full": full, "alt": alt.clone(), "part": part, "part_alt": part_alt,
+                    "views": camera_share(64, world, rank)}, os.path.join(result_dir, f"rank{rank}.pt"))
     finally:
         dist.destroy_process_group()
 
@@ -70,6 +81,9 @@ def test_sharded_decode_all_gather_matches_full_decode(tmp_path, world, n):
         d = torch.load(tmp_path / f"rank{r}.pt")
         assert np.array_equal(d["full"].numpy().view(np.uint32), ref.view(np.uint32))
         assert np.array_equal(d["alt"].numpy().view(np.uint32), ref.view(np.uint32))
+        sub = np.ascontiguousarray(ref[:, : synth.BASE_DIMS])
+        assert np.array_equal(d["part"].numpy().view(np.uint32), sub.view(np.uint32))
+        assert np.array_equal(d["part_alt"].numpy().view(np.uint32), sub.view(np.uint32))
         views += d["views"]
     assert sorted(views) == list(range(64))
 
