@@ -203,15 +203,15 @@ def train_step_timing(sc, cam, dev, steps, warmup=2):
             "loss_first": round(float(losses[0].detach()), 6)}
 
 
-def gather_peak(fr, dev, cam, lookups=64, reps=5):
+def gather_peak(fr, dev, cam, lookups=128, reps=5):
     """The blend's gather roofline: hash-grid lookups per second of a kernel that
     does nothing else (ns_gather_probe: the blend's lookup code at full
     occupancy, four lookups in flight per thread), in corner bytes per second,
     for two point patterns on the same table:
-      * "coherent" (the roofline denominator): the blend's pattern, a warp's 32
-        lanes at the hit points of a 16 x 2 pixel strip on one surfel, all 16
-        levels; the strip spacing is this camera's pixel footprint at the scene
-        (distance 4 - 1 from the camera) in grid units;
+      * "coherent" (the roofline denominator): the blend's pattern and order,
+        a warp's 32 lanes as a 16 x 2 pixel strip with 8 samples each on
+        stacked surfels, all 16 levels in an outer loop; the strip spacing is
+        this camera's pixel footprint at the scene (distance 3) in grid units;
       * "random_hashed": every lane an independent point of the hashed levels
         (5-15), the pattern's worst case, for context."""
     import torch

@@ -439,10 +439,11 @@ int ns_grid_encode_backward(const float* grad, const float* inputs, const void* 
  * lookups_per_thread (a multiple of 4) hash-grid lookups at pseudo-random
  * points of levels [level0, level0 + levels) of `table`, with the blend
  * kernel's lookup code, and write one float per thread to sink (blocks * 256
- * floats). spacing = 0: independent points per lane; spacing > 0: the 32
- * lanes of a warp on a 16 x 2 grid of that spacing (grid units) in a random
- * plane, as neighbouring pixels' hit points on one surfel. Corner bytes read =
- * blocks * 256 * lookups_per_thread * 8 * row bytes (4 for an fp16 pair table). */
+ * floats). spacing = 0: independent points and levels per lane; spacing > 0:
+ * the blend's pattern (a warp's 32 lanes as a 16 x 2 pixel strip of that
+ * spacing in grid units on 8 stacked surfels, levels in an outer loop;
+ * lookups_per_thread a multiple of 8 * levels). Corner bytes read = blocks *
+ * 256 * lookups_per_thread * 8 * row bytes (4 for an fp16 pair table). */
 int ns_gather_probe(const void* table, int32_t table_fp16, const int32_t* offsets, uint32_t level0,
                     uint32_t levels, float S, uint32_t H, uint32_t lookups_per_thread, float spacing,
                     int32_t blocks, float* sink, void* stream);
