@@ -248,6 +248,21 @@ int ns_read_binning(const void* geom, size_t geom_bytes, int32_t P, const void* 
                     int16_t* tile_rects, float* depths, float* pixel_boxes, float* means2D,
                     void* stream);
 
+/* Poll bound of every bounded device wait in this library's kernels (the
+ * radix sort's look-back on earlier tiles, the blend's record ring): a wait
+ * that polls `spins` times without success records an error bit (reported by
+ * ns_read_device_status, or lost where no status word is read) and the kernel
+ * finishes. 0 restores the default 2^22. Applies to launches made after the
+ * call, in the whole process; returns the previous bound. */
+uint32_t ns_set_wait_limit(uint32_t spins);
+
+/* Self-test of that wait path (no reference counterpart): one thread waits,
+ * with the current bound and the sort's wait code, for the device word *flag
+ * to become non-zero; if the bound runs out it records the timeout in the
+ * error word of the geometry scratch `geom` (sized for P surfels), which
+ * ns_read_device_status then reports as NS_ERR_DEVICE. Nothing traps. */
+int ns_wait_selftest(const uint32_t* flag, void* geom, int32_t P, void* stream);
+
 /* Reads (and clears) the device error word of a geometry scratch buffer; syncs. */
 int ns_read_device_status(void* geom, int32_t P, void* stream);
 

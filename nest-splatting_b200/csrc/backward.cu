@@ -180,7 +180,7 @@ __global__ void __launch_bounds__(kThreads, 2) blend_backward_kernel(const Backw
 
   const int t = threadIdx.x, lane = t & 31, wid = t >> 5;
   const int gx = div_up(p.W, kTile);
-  const int tile = blockIdx.x;
+  const int tile = p.tile_order ? (int)p.tile_order[blockIdx.x] : (int)blockIdx.x;  // heaviest first
   const int tx = tile % gx, ty = tile / gx;
   const uint32_t px = tx * kTile + (t & (kTile - 1));
   const uint32_t py = ty * kTile + (t >> 4);

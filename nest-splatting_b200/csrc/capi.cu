@@ -17,6 +17,8 @@
 namespace ns_host {
 static thread_local int g_last_cuda_error = 0;
 static std::atomic<uint64_t> g_launches{0};
+static std::atomic<uint32_t> g_wait_limit{ns::kSpinLimit};
+uint32_t wait_limit() { return g_wait_limit.load(std::memory_order_relaxed); }
 int record_cuda(cudaError_t e) {
   g_last_cuda_error = (int)e;
   return NS_ERR_CUDA;
@@ -94,6 +96,7 @@ GeomState carve_geom(void* base, int P, size_t* used) {
 
 struct ImageState {
   uint2* ranges;
+  uint32_t* order;  // tiles, heaviest first (launch order of the per-tile kernels)
   float* final_T;
   uint32_t* n_contrib;
 };
@@ -104,6 +107,7 @@ ImageState carve_image(void* base, int W, int H, size_t* used) {
   const size_t tiles = (size_t)div_up(W, kTile) * div_up(H, kTile);
   const size_t HW = (size_t)W * H;
   s.ranges = c.take<uint2>((size_t)max64(tiles, 1));
+  s.order = c.take<uint32_t>((size_t)max64(tiles, 1));
   s.final_T = c.take<float>((size_t)max64(3 * HW, 1));
   s.n_contrib = c.take<uint32_t>((size_t)max64(2 * HW, 1));
   if (used) *used = align_up(c.off);
@@ -240,6 +244,8 @@ int bin_and_render(const ns_raster_settings* st, int P, const GeomState& g, cons
   rc = identify_ranges_launch(b.keys_sorted, device_count ? g.count : nullptr, count, cap, im.ranges,
                               tiles, num_sms(), stream);
   if (rc) return rc;
+  rc = tile_order_launch(im.ranges, tiles, im.order, stream);
+  if (rc) return rc;
   if (ev) NS_CUDA_TRY(cudaEventRecord((cudaEvent_t)ev[5], stream));
   RenderParams rp;
   rp.W = W;
@@ -261,6 +267,7 @@ int bin_and_render(const ns_raster_settings* st, int P, const GeomState& g, cons
   rp.max_intersections = st->max_intersections;
   rp.record_transmittance = st->record_transmittance;
   rp.ranges = im.ranges;
+  rp.tile_order = im.order;
   rp.point_list = b.vals_sorted;
   rp.records = g.records;
   rp.table = features;
@@ -273,6 +280,7 @@ int bin_and_render(const ns_raster_settings* st, int P, const GeomState& g, cons
   rp.cover_pixels = cover_pixels;
   rp.trans_avg = trans_avg;
   rp.err = g.err;
+  rp.spin_limit = ns_host::wait_limit();
   if (ev) NS_CUDA_TRY(cudaEventRecord((cudaEvent_t)ev[6], stream));
   rc = render_launch(rp, st->table_fp16, stream);
   if (rc) return rc;
@@ -298,6 +306,10 @@ const char* ns_status_string(int status) {
 }
 
 int ns_last_cuda_error(void) { return ns_host::g_last_cuda_error; }
+
+uint32_t ns_set_wait_limit(uint32_t spins) {
+  return ns_host::g_wait_limit.exchange(spins ? spins : ns::kSpinLimit);
+}
 uint64_t ns_kernel_launches(void) { return ns_host::g_launches.load(); }
 int ns_version(void) { return 1; }
 
@@ -502,6 +514,7 @@ int ns_rasterize_backward(const ns_raster_settings* settings, const ns_surfels* 
   // are the same matrix: scale_modifier 1 and the same image size.
   bp.ray_hit = (settings->scale_modifier == 1.0f && Wq == W && Hq == H) ? 1 : 0;
   bp.ranges = im.ranges;
+  bp.tile_order = im.order;
   bp.point_list = b.vals_sorted;
   bp.records = g.records;
   bp.table = surfels->features;
@@ -535,6 +548,12 @@ int ns_read_device_status(void* geom, int32_t P, void* stream_) {
   NS_CUDA_TRY(cudaMemsetAsync(g.err, 0, sizeof(uint32_t), stream));
   NS_CUDA_TRY(cudaStreamSynchronize(stream));
   return err ? NS_ERR_DEVICE : NS_OK;
+}
+
+int ns_wait_selftest(const uint32_t* flag, void* geom, int32_t P, void* stream) {
+  if (!flag || !geom || P < 0) return NS_ERR_INVALID;
+  GeomState g = carve_geom(geom, P, nullptr);
+  return wait_selftest_launch(flag, g.err, reinterpret_cast<cudaStream_t>(stream));
 }
 
 int ns_mark_visible(int32_t P, const float* means3D, const float* viewmatrix,

@@ -25,8 +25,10 @@ constexpr uint32_t kErrLookbackTimeout = 1u;
 constexpr uint32_t kErrCapacity = 2u;
 constexpr uint32_t kErrSpinTimeout = 4u;
 
-// Upper bound on spin iterations of any wait in these kernels. A wait that runs
-// out records an error bit and continues, so no kernel can hang the GPU.
+// Default bound on the polls of any wait in these kernels (ns_set_wait_limit
+// changes it for later launches; the launchers pass the current value to the
+// kernels). A wait that runs out records an error bit and continues, so no
+// kernel can hang the GPU.
 constexpr uint32_t kSpinLimit = 1u << 22;
 
 // Per-surfel render record: 8 float4 = 128 bytes, one L2 line, written by the
@@ -79,13 +81,28 @@ __device__ __forceinline__ void set_error(uint32_t* err, uint32_t bit) {
   if (err) atomicOr(err, bit);
 }
 
+__device__ __forceinline__ uint32_t ld_volatile_u32(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.volatile.global.u32 %0, [%1];" : "=r"(v) : "l"(p));
+  return v;
+}
+
+// Bounded wait on a global word that another CTA publishes: polls *p until
+// (value & mask) != 0 and returns the value, or returns 0 after `limit` polls
+// (the caller records the timeout in its error word).
+__device__ __forceinline__ uint32_t wait_word(const uint32_t* p, uint32_t mask, uint32_t limit) {
+  uint32_t v = ld_volatile_u32(p);
+  for (uint32_t spins = 0; (v & mask) == 0 && spins < limit; spins++) v = ld_volatile_u32(p);
+  return (v & mask) ? v : 0u;
+}
+
 // Bounded wait on a shared-memory mbarrier for the completion of the phase
 // with parity `parity`. Returns 1 when it completed, 0 when *stop (if given)
-// reached `stop_at` first, -1 when the spin limit ran out.
-__device__ __forceinline__ int mbar_wait_parity(const uint64_t* bar, uint32_t parity,
+// reached `stop_at` first, -1 when `limit` polls ran out.
+__device__ __forceinline__ int mbar_wait_parity(const uint64_t* bar, uint32_t parity, uint32_t limit,
                                                 const int* stop = nullptr, int stop_at = 0) {
   const unsigned a = (unsigned)__cvta_generic_to_shared(bar);
-  for (uint32_t spins = 0; spins < kSpinLimit; spins++) {
+  for (uint32_t spins = 0; spins < limit; spins++) {
     uint32_t ok;
     asm volatile(
         "{\n\t.reg .pred p;\n\t"
@@ -117,6 +134,7 @@ __device__ __forceinline__ void cp_async_arrive(uint64_t* bar) {
 namespace ns_host {
 int record_cuda(cudaError_t e);  // stores e as the last CUDA error, returns NS_ERR_CUDA
 void count_launch();             // one more kernel launched by this library
+uint32_t wait_limit();           // poll bound passed to the kernels' waits (ns_set_wait_limit)
 }
 
 #define NS_CUDA_TRY(expr)                                       \

@@ -26,6 +26,7 @@ struct RenderParams {
   uint32_t max_intersections;
   int record_transmittance;
   const uint2* ranges;
+  const uint32_t* tile_order;  // blockIdx.x -> tile (heaviest first), or NULL: row-major
   const uint32_t* point_list;
   const SurfelRecord* records;
   const void* table;
@@ -38,6 +39,7 @@ struct RenderParams {
   float* cover_pixels;
   float* trans_avg;
   uint32_t* err;  // device status word (kErr* bits)
+  uint32_t spin_limit;  // poll bound of the record-ring waits
 };
 struct BackwardParams {
   int W, H;
@@ -60,6 +62,7 @@ struct BackwardParams {
   const float* viewmatrix;
   int ray_hit;                // 1: hit-point gradient in the ray/plane form (see backward.cu)
   const uint2* ranges;
+  const uint32_t* tile_order;  // blockIdx.x -> tile (heaviest first), or NULL: row-major
   const uint32_t* point_list;
   const SurfelRecord* records;
   const void* table;
@@ -84,6 +87,8 @@ int preprocess_backward_launch(int P, const float* means3D, const float* scales,
                                const float* pm, int Wq, int Hq, const float* accum,
                                const ns_raster_grads_out& o, cudaStream_t stream);
 int rvq_decode_launch(const uint8_t*, const float*, float*, int64_t, int, int, int, cudaStream_t);
+int wait_selftest_launch(const uint32_t* flag, uint32_t* err, cudaStream_t stream);
+int tile_order_launch(const uint2* ranges, int tiles, uint32_t* order, cudaStream_t stream);
 int preprocess_blocks(int P);
 int preprocess_block_size();
 int preprocess_api_launch(int P, const ns_surfels& s, float mod, float beta, int kernel_type,

@@ -137,7 +137,7 @@ __global__ void __launch_bounds__(kThreads, 2) blend_kernel(const RenderParams p
 
   const int t = threadIdx.x;
   const int gx = div_up(p.W, kTile);
-  const int tile = blockIdx.x;
+  const int tile = p.tile_order ? (int)p.tile_order[blockIdx.x] : (int)blockIdx.x;  // heaviest first
   const int tx = tile % gx, ty = tile / gx;
   const uint32_t px = tx * kTile + (t & (kTile - 1));
   const uint32_t py = ty * kTile + (t >> 4);
@@ -284,7 +284,7 @@ __global__ void __launch_bounds__(kThreads, 2) blend_kernel(const RenderParams p
   for (int b = 0; b < rounds; b++) {
     const int s = b & (kSlots - 1);
     // Wait for batch b (gives up when every warp of the tile is done).
-    const int ws = mbar_wait_parity(&S.full[s], (uint32_t)(b / kSlots) & 1u, &S.ndone, kWarps);
+    const int ws = mbar_wait_parity(&S.full[s], (uint32_t)(b / kSlots) & 1u, p.spin_limit, &S.ndone, kWarps);
     if (ws <= 0) {
       if (ws < 0) set_error(p.err, kErrSpinTimeout);
       break;

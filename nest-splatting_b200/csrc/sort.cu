@@ -16,7 +16,8 @@
 //      memory so global writes come out in digit runs.
 // Stability: within a tile keys are ranked in (warp, item, lane) order, which
 // is the input order of the warp-striped layout; tiles are prefixed in order.
-// Every wait on another CTA's word is bounded (kSpinLimit); running out sets an
+// Every wait on another CTA's word is bounded (wait_word with the launch's poll
+// limit, ns_set_wait_limit); running out sets an
 // error bit and the pass continues, so a fault elsewhere cannot hang the GPU.
 #include "common.cuh"
 
@@ -71,11 +72,6 @@ __device__ __forceinline__ uint32_t lanemask_lt() {
   return m;
 }
 
-__device__ __forceinline__ uint32_t load_volatile(const uint32_t* p) {
-  uint32_t v;
-  asm volatile("ld.volatile.global.u32 %0, [%1];" : "=r"(v) : "l"(p));
-  return v;
-}
 
 // Histogram of every digit position in one pass over the keys. Each warp
 // counts into its own shared-memory histogram (keys with few distinct digits
@@ -164,7 +160,7 @@ onesweep_pass_kernel(const KeyT* __restrict__ keys_in, const uint32_t* __restric
                      KeyT* __restrict__ keys_out, uint32_t* __restrict__ vals_out, int64_t n,
                      const int64_t* n_dev, int shift, const uint32_t* __restrict__ bucket_base,
                      const uint32_t* __restrict__ bucket_count, const uint32_t* __restrict__ nz_digits,
-                     uint32_t* status, uint32_t* tile_ctr, uint32_t* err) {
+                     uint32_t* status, uint32_t* tile_ctr, uint32_t* err, uint32_t spin_limit) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   PassSmem<KeyT>& S = *reinterpret_cast<PassSmem<KeyT>*>(smem_raw);
   const int t = threadIdx.x, lane = t & 31, w = t >> 5;
@@ -248,11 +244,8 @@ onesweep_pass_kernel(const KeyT* __restrict__ keys_in, const uint32_t* __restric
     int64_t j = (int64_t)tile - 1;
     bool ok = true;
     while (j >= 0) {
-      const uint32_t* p = status + (size_t)j * kRadix + t;
-      uint32_t s = load_volatile(p);
-      uint32_t spins = 0;
-      while ((s & kFlagMask) == 0 && ++spins < kSpinLimit) s = load_volatile(p);
-      if ((s & kFlagMask) == 0) {
+      const uint32_t s = wait_word(status + (size_t)j * kRadix + t, kFlagMask, spin_limit);
+      if (s == 0u) {
         ok = false;
         break;
       }
@@ -330,7 +323,7 @@ int radix_sort_impl(const KeyT* keys_in, const uint32_t* vals_in, KeyT* keys_out
     uint32_t* vout = to_out ? vals_out : vals_alt;
     onesweep_pass_kernel<KeyT><<<(unsigned)tiles, kSortThreads, smem, stream>>>(
         kin, vin, kout, vout, n, n_dev, p * kRadixBits, T.hist + p * kRadix, T.count + p * kRadix,
-        T.nz + p, T.status + (size_t)p * tiles * kRadix, T.tile_ctr + p, T.err);
+        T.nz + p, T.status + (size_t)p * tiles * kRadix, T.tile_ctr + p, T.err, ns_host::wait_limit());
     NS_LAUNCH_CHECK();
     kin = kout;
     vin = vout;

@@ -27,7 +27,7 @@ EXPORTED = [
     "ns_rasterize_backward",
     "ns_normal_error", "ns_normal_error_scratch_bytes", "ns_normal_error_backward", "ns_mlp_backward",
     "ns_allmap_decode", "ns_grid_encode_forward", "ns_grid_encode_backward", "ns_read_binning",
-    "ns_gather_probe",
+    "ns_gather_probe", "ns_set_wait_limit", "ns_wait_selftest",
 ]
 
 
@@ -175,6 +175,10 @@ def load() -> C.CDLL:
     lib.ns_grid_encode_backward.restype = C.c_int
     lib.ns_grid_encode_backward.argtypes = [vp, vp, vp, i32, vp, vp, u32, u32, u32, u32, f32, u32, vp, vp, u32,
                                             i32, u32, vp]
+    lib.ns_set_wait_limit.restype = C.c_uint32
+    lib.ns_set_wait_limit.argtypes = [C.c_uint32]
+    lib.ns_wait_selftest.restype = C.c_int
+    lib.ns_wait_selftest.argtypes = [vp, vp, i32, vp]
     lib.ns_gather_probe.restype = C.c_int
     lib.ns_gather_probe.argtypes = [vp, i32, vp, u32, u32, f32, u32, u32, f32, i32, vp, vp]
     _lib = lib
