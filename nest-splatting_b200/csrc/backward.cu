@@ -118,7 +118,13 @@ __device__ __forceinline__ float mode_hash_factor(const BackwardParams& p, uint3
   const int base = p.render_mode & 0xFF;
   const int pg = 2 * p.hybrid_levels;
   query = p.L > 0;
+  if (base == 0) {  // level 0: no hash query
+    query = false;
+    return 0.0f;
+  }
   if (base == 4) return 1.0f;
+  if (base == 6) return 0.5f;
+  if (base == 7) return 1.0f - __ldg(p.gauss + (size_t)id * (2 * p.total_levels + 1) + 2 * p.total_levels);
   if (base == 12) return 1.0f - __ldg(p.gauss + (size_t)id * (2 * p.total_levels + 1) + 2 * p.total_levels);
   const float wgt = __ldg(p.gauss + (size_t)id * (pg + 1) + pg);
   query = query && wgt > 1e-6f;
@@ -140,9 +146,42 @@ __device__ __forceinline__ float mode_backward(const BackwardParams& p, uint32_t
     const float2 v = *acc_pair(const_cast<float*>(g), t, c >> 1);
     return (c & 1) ? v.y : v.x;
   };
-  const size_t stride = base == 4 ? (size_t)pg : (base == 12 ? (size_t)td + 1 : (size_t)pg + 1);
+  const size_t stride = (base == 0 || base == 6) ? (size_t)p.C
+                        : base == 4                ? (size_t)pg
+                        : (base == 7 || base == 12) ? (size_t)td + 1
+                                                    : (size_t)pg + 1;
   const float* row = p.gauss + (size_t)id * stride;
   float* drow = p.dL_dcolors + (size_t)id * stride;
+  if (base == 0 || base == 6) {
+    // level 0: per-surfel colours, dL/drow = aT dL/dC. Mode 6: feat = 0.5 row +
+    // 0.5 hash on the hash levels' channels, dL/drow = 0.5 aT dL/dC there (the
+    // derivative of the forward; the reference's case 6 backward reads a row
+    // of 2 L LD values with a per-channel mask that its forward does not have,
+    // backward.cu:1041-1106).
+    const int n = base == 0 ? p.C : min(hd, p.C);
+    const float sc = base == 0 ? 1.0f : 0.5f;
+    float gdot = 0.0f;
+    for (int c = 0; c < n; c++) {
+      const float gv = gc(c);
+      gdot += __ldg(row + c) * gv;
+      atomicAdd(drow + c, sc * (aT * gv));
+    }
+    return base == 0 ? gdot : 0.5f * gdot + 0.5f * hdot;
+  }
+  if (base == 7) {
+    // adaptive_add (backward.cu:1108-1190): dL/drow = wgt aT dL/dC; the weight
+    // slot gets the reference's d_gamma = aT (row - hash) . dL/dC wgt (1 - wgt)
+    // (the gradient of the pre-sigmoid parameter, as the reference returns it)
+    const float wgt = __ldg(row + td);
+    float gdot = 0.0f;
+    for (int c = 0; c < td; c++) {
+      const float gv = gc(c);
+      gdot += __ldg(row + c) * gv;
+      atomicAdd(drow + c, wgt * (aT * gv));
+    }
+    atomicAdd(drow + td, aT * (gdot - hdot) * (wgt * (1.0f - wgt)));
+    return wgt * gdot + (1.0f - wgt) * hdot;
+  }
   float f = 0.0f;
   for (int c = 0; c < pg; c++) {
     const float gv = gc(c);
@@ -192,7 +231,7 @@ __global__ void __launch_bounds__(kThreads, 2) blend_backward_kernel(const Backw
   const uint32_t L = p.L;
   const float vmin = p.gridrange[0], vmax = p.gridrange[1];
   const float fscale = kFixed ? fixed_point_scale(*p.grad_max_bits) : 0.0f;
-  const int hoff = (kAnyKernel && p.render_mode != 0) ? p.hybrid_levels : 0;  // level of hash level 0
+  const int hoff = kAnyKernel ? hash_level_offset(p.render_mode, p.hybrid_levels) : 0;  // level of hash level 0
 
   if (t < (int)L) S.lv[t] = make_level<TableT>(p.table, p.offsets, p.S, p.Hres, p.align_corners, t);
   if (t < 9) {
@@ -384,7 +423,7 @@ __global__ void __launch_bounds__(kThreads, 2) blend_backward_kernel(const Backw
         }
         float hw = alpha * T;  // weight of this sample's hash features
         bool query = true;
-        if (kAnyKernel && p.render_mode != 0) hw *= mode_hash_factor(p, S.ids[jj], query);
+        if (kAnyKernel && uses_surfel_rows(p.render_mode, p.L)) hw *= mode_hash_factor(p, S.ids[jj], query);
         S.samp[cnt][t] = make_float4(in0, in1, in2, hw);
         S.lvl[cnt][t] = (uint8_t)((oob || !query) ? 0u : min(apl, L));
         S.jj[cnt][t] = (uint8_t)jj;
@@ -603,7 +642,8 @@ __global__ void __launch_bounds__(kThreads, 2) blend_backward_kernel(const Backw
 
         // Colour term (:1786-1797) with the scalar recursion.
         acc_f = last_alpha * last_f + (1.f - last_alpha) * acc_f;
-        const float fsc = (kAnyKernel && p.render_mode != 0) ? mode_backward(p, S.ids[jj], aT, res.x, S.g, t)
+        const float fsc = (kAnyKernel && uses_surfel_rows(p.render_mode, p.L))
+                              ? mode_backward(p, S.ids[jj], aT, res.x, S.g, t)
                                                              : res.x;
         last_f = fsc;
         float dL_dalpha = fsc - acc_f;
@@ -758,7 +798,9 @@ __global__ void __launch_bounds__(kThreads, 2) blend_backward_kernel(const Backw
                                       P01 * dTu.z + P11 * dTv.z + P21 * dTw.z + h2y));
         atomicAdd(ga + 2, make_float4(P02 * dTu.z + P12 * dTv.z + P22 * dTw.z + h2z, tuz, tvz,
                                       G * dL_dalpha));
-        atomicAdd(ga + 3, make_float4(aT * dn0, aT * dn1, aT * dn2, aT * gabs));
+        // level 0 adds nothing to the densification sum (backward.cu:833-849)
+        const float gsum = (kAnyKernel && p.render_mode == 0 && p.L == 0) ? 0.f : aT * gabs;
+        atomicAdd(ga + 3, make_float4(aT * dn0, aT * dn1, aT * dn2, gsum));
         if (!on_plane || dshape != 0.f) atomicAdd(ga + 4, make_float4(dmx, dmy, dshape, 0.f));
       }
       __syncwarp();
@@ -986,13 +1028,13 @@ int table_grad_finish_launch(const unsigned long long* fx, size_t n, const uint3
 
 int blend_backward_launch(const BackwardParams& p, int fp16, cudaStream_t stream) {
   if (p.LD != 2 || p.C > kAccStride || p.C <= 0) return NS_ERR_UNSUPPORTED;
-  const int hoff = p.render_mode != 0 ? p.hybrid_levels : 0;
+  const int hoff = hash_level_offset(p.render_mode, p.hybrid_levels);
   if (hoff < 0 || (int64_t)hoff + p.L > (uint32_t)(p.C / p.LD) || p.L > (uint32_t)kMaxLevels)
     return NS_ERR_UNSUPPORTED;
   if ((p.render_mode >> 8) != 0) return NS_ERR_UNSUPPORTED;  // training rules only
   const int tiles = div_up(p.W, kTile) * div_up(p.H, kTile);
   if (tiles == 0) return NS_OK;
-  if (p.kernel_type != 0 || p.render_mode != 0)
+  if (p.kernel_type != 0 || uses_surfel_rows(p.render_mode, p.L))
     return fp16 ? launch_backward<__half, true>(p, tiles, stream)
                 : launch_backward<float, true>(p, tiles, stream);
   return fp16 ? launch_backward<__half, false>(p, tiles, stream)

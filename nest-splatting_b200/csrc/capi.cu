@@ -184,18 +184,22 @@ int validate_settings(const ns_raster_settings* s) {
   if (!s) return NS_ERR_INVALID;
   if (s->image_width <= 0 || s->image_height <= 0) return NS_ERR_INVALID;
   if (!s->viewmatrix || !s->projmatrix) return NS_ERR_INVALID;
-  // level == 0 (per-surfel colours) is not built; the modes may query no hash level
-  if (s->levels == 0 && s->render_mode == 0) return NS_ERR_UNSUPPORTED;
+  // levels == 0 in mode 0: per-surfel colours (colors_precomp, C channels)
   if (s->level_dim == 0 || s->channels == 0) return NS_ERR_INVALID;
   if (s->levels * s->level_dim > s->channels) return NS_ERR_INVALID;
   if (s->kernel_type < 0 || s->kernel_type > 3) return NS_ERR_UNSUPPORTED;
   const int base = s->render_mode & 0xFF, flag = s->render_mode >> 8;
-  if (base != 0 && base != 4 && base != 12 && base != 13 && base != 14) return NS_ERR_UNSUPPORTED;
+  if (base != 0 && base != 4 && base != 6 && base != 7 && base != 12 && base != 13 && base != 14)
+    return NS_ERR_UNSUPPORTED;
   if (flag > 1 || (flag && base != 12 && base != 13 && base != 14)) return NS_ERR_UNSUPPORTED;
   if (base != 0) {
     if (s->hybrid_levels > 16 || s->total_levels > 16) return NS_ERR_INVALID;
+    // modes 6 and 7 have no per-surfel levels before the hash levels
+    if ((base == 6 || base == 7) && s->hybrid_levels != 0) return NS_ERR_INVALID;
     if ((s->hybrid_levels + s->levels) * s->level_dim > s->channels) return NS_ERR_INVALID;
-    if ((base == 12 || base == 13) && s->total_levels * s->level_dim > s->channels) return NS_ERR_INVALID;
+    if ((base == 7 || base == 12 || base == 13) && s->total_levels * s->level_dim > s->channels)
+      return NS_ERR_INVALID;
+    if (base == 7 && s->levels > s->total_levels) return NS_ERR_INVALID;
   }
   return NS_OK;
 }
@@ -342,7 +346,8 @@ int ns_rasterize_forward(const ns_raster_settings* settings, const ns_surfels* s
     return NS_ERR_INVALID;
   if (!outputs->out_color || !outputs->out_others || !outputs->radii) return NS_ERR_INVALID;
   if (settings->kernel_type != 0 && P > 0 && !surfels->shapes) return NS_ERR_INVALID;
-  if (settings->render_mode != 0 && P > 0 && !surfels->colors_precomp) return NS_ERR_INVALID;
+  if (uses_surfel_rows(settings->render_mode, settings->levels) && P > 0 && !surfels->colors_precomp)
+    return NS_ERR_INVALID;
   if (settings->record_transmittance && (!outputs->cover_pixels || !outputs->trans_avg))
     return NS_ERR_INVALID;
   if (settings->level_dim != 2) return NS_ERR_UNSUPPORTED;
@@ -423,7 +428,7 @@ int ns_rasterize_backward(const ns_raster_settings* settings, const ns_surfels* 
   cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_);
   int rc = validate_settings(settings);
   if (rc) return rc;
-  // training rules of modes 4 / 12 / 14 only (the reference has no mode-13 backward)
+  // training rules of modes 4 / 6 / 7 / 12 / 14 only (the reference has no mode-13 backward)
   if ((settings->render_mode >> 8) != 0 || (settings->render_mode & 0xFF) == 13) return NS_ERR_UNSUPPORTED;
   if (!surfels || !gi || !go) return NS_ERR_INVALID;
   const int P = surfels->P;
@@ -431,12 +436,16 @@ int ns_rasterize_backward(const ns_raster_settings* settings, const ns_surfels* 
   if (settings->kernel_type != 0 && P > 0 && (!surfels->shapes || !go->dL_dshapes))
     return NS_ERR_INVALID;
   const int base_mode = settings->render_mode & 0xFF;
-  if (base_mode != 0 && P > 0 && (!surfels->colors_precomp || !go->dL_dcolors_precomp))
-    return NS_ERR_INVALID;
-  const size_t mode_stride = base_mode == 4    ? (size_t)settings->hybrid_levels * settings->level_dim
-                             : base_mode == 12 ? (size_t)settings->total_levels * settings->level_dim + 1
-                             : base_mode == 14 ? (size_t)settings->hybrid_levels * settings->level_dim + 1
-                                               : 0;
+  const bool rows = uses_surfel_rows(settings->render_mode, settings->levels);
+  if (rows && P > 0 && (!surfels->colors_precomp || !go->dL_dcolors_precomp)) return NS_ERR_INVALID;
+  // row length of colors_precomp: level 0 and mode 6 C, mode 4 hybrid LD,
+  // modes 7 / 12 total LD + 1, mode 14 hybrid LD + 1
+  const size_t mode_stride = !rows                              ? 0
+                             : (base_mode == 0 || base_mode == 6) ? (size_t)settings->channels
+                             : base_mode == 4 ? (size_t)settings->hybrid_levels * settings->level_dim
+                             : (base_mode == 7 || base_mode == 12)
+                                 ? (size_t)settings->total_levels * settings->level_dim + 1
+                                 : (size_t)settings->hybrid_levels * settings->level_dim + 1;
   if (settings->level_dim != 2) return NS_ERR_UNSUPPORTED;
   if (!go->dL_dmeans3D || !go->dL_dmean2D || !go->dL_dopacity || !go->dL_dscales ||
       !go->dL_drots || !go->dL_dtable || !go->dL_gradsum || go->table_rows < 0)
@@ -503,7 +512,7 @@ int ns_rasterize_backward(const ns_raster_settings* settings, const ns_surfels* 
   bp.total_levels = (int)settings->total_levels;
   bp.gauss = surfels->colors_precomp;
   bp.dL_dcolors = go->dL_dcolors_precomp;
-  if (base_mode != 0)
+  if (rows)
     NS_CUDA_TRY(cudaMemsetAsync(go->dL_dcolors_precomp, 0, (size_t)P * mode_stride * sizeof(float), stream));
   bp.Wq = Wq;
   bp.Hq = Hq;
@@ -641,7 +650,8 @@ int ns_render_frame(const ns_raster_settings* settings, const ns_frame_inputs* i
                     int64_t* num_rendered, int flags, void* stream_) {
   cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_);
   int rc = validate_settings(settings);
-  if (settings && (settings->kernel_type != 0 || settings->render_mode != 0)) return NS_ERR_UNSUPPORTED;
+  if (settings && (settings->kernel_type != 0 || settings->render_mode != 0 || settings->levels == 0))
+    return NS_ERR_UNSUPPORTED;  // the frame renders the hash grid (no per-surfel colours)
   if (rc) return rc;
   if (!in || !out) return NS_ERR_INVALID;
   const int P = in->P;

@@ -5,6 +5,19 @@
 #include "common.cuh"
 
 namespace ns {
+// The render modes that put the hash levels after hybrid_levels per-surfel
+// levels (4 cat, 12-14 adaptive_cat / _fast / adaptive_zero); in modes 6 and 7
+// (adaptive, adaptive_add) the hash levels start at channel 0, as in mode 0.
+__host__ __device__ inline int hash_level_offset(int render_mode, int hybrid_levels) {
+  const int base = render_mode & 0xFF;
+  return (base == 4 || base == 12 || base == 13 || base == 14) ? hybrid_levels : 0;
+}
+// Samples read per-surfel rows (colors_precomp) in every mode but 0, and in
+// mode 0 with no hash level (level 0: per-surfel colours, forward.cu:1093-1096).
+__host__ __device__ inline bool uses_surfel_rows(int render_mode, uint32_t levels) {
+  return render_mode != 0 || levels == 0;
+}
+
 struct RenderParams {
   int W, H;
   int C, LD;

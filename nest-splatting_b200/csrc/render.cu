@@ -10,7 +10,7 @@
 //
 // One CTA of 256 threads per 16x16 tile, one thread per pixel; warp w owns tile
 // rows 2w and 2w+1. The tile's surfel records stream through a ring of four
-// 64-record slots in shared memory (cp.async, completion on an mbarrier per
+// 32-record slots in shared memory (cp.async, completion on an mbarrier per
 // slot); the last warp to finish a batch refills its slot, so warps never meet
 // at a CTA barrier and drift up to three batches apart. Each warp alternates,
 // on its own 32 pixels, between two phases:
@@ -30,9 +30,10 @@
 //   k-major list (every pixel's sample k, then k+1, ...) so all 32 lanes look up
 //   real samples; neighbouring pixels' k-th samples usually hit nearby points,
 //   so their corner loads coalesce at the coarse levels. Levels run in a
-//   warp-uniform outer loop (the dense/hashed choice is a uniform branch), two
-//   levels x two list entries (four lookups) in flight per lane. Each pixel's
-//   owner lane adds its results in queue order, the reference's per-pixel order.
+//   warp-uniform outer loop (the dense/hashed choice is a uniform branch), four
+//   levels of one list entry (four lookups) in flight per lane, so the list and
+//   the owners' queues are walked once per four levels. Each pixel's owner lane
+//   adds its results in queue order, the reference's per-pixel order.
 //
 // The hash table is read as fp16 (or fp32) pairs through the read-only path;
 // at 16 levels x 2^19 x 2 fp16 it is 32 MB and stays resident in the 126 MB L2.
@@ -47,7 +48,7 @@ constexpr int kQueue = 8;              // queued samples per pixel between drain
 constexpr int kWarps = kThreads / 32;
 constexpr int kBatch = 32;             // surfel records per ring slot
 constexpr int kSlots = 4;              // ring slots (batches in flight)
-constexpr int kChunk = 64;             // compacted samples looked up per warp step (2 per lane)
+constexpr int kChunk = 32;             // compacted samples looked up per warp step (1 per lane)
 constexpr int kMaxChannels = 32;
 
 struct BlendSmem {
@@ -56,7 +57,7 @@ struct BlendSmem {
   uint8_t lvl[kQueue][kThreads];        // levels to query for the sample (0: none)
   uint8_t item[kWarps][kThreads];       // per warp: queued samples in k-major order, (k << 5) | lane
   uint8_t pos[kQueue][kThreads];        // position of a pixel's k-th sample in its warp's list
-  float4 res[kWarps][kChunk];           // lookups of the current chunk: level l (xy), l+1 (zw)
+  float4 res[kWarps][2 * kChunk];       // lookups of the current chunk: levels l..l+3, two float4 per entry
   float acc[kThreads * kAccStride];     // feature accumulators, see acc_pair()
   LevelConst lv[kMaxLevels];
   uint64_t full[kSlots];                // slot filled (32 cp.async arrivals per fill)
@@ -64,9 +65,10 @@ struct BlendSmem {
   int ndone;                            // warps whose pixels are all done
 };
 
-// Render modes 4 / 12 / 14 (forward.cu:1218-1282, 1593-1790): adds this
-// sample's per-surfel features, weighted by w, to the pixel's accumulators and
-// returns the factor of the hash features (0: the mode does not query the grid).
+// Render modes 4 / 6 / 7 / 12-14 and level 0 (forward.cu:1093-1096,
+// 1218-1377, 1593-1790): adds this sample's per-surfel features, weighted by
+// w, to the pixel's accumulators and returns the factor of the hash features
+// (0: the mode does not query the grid).
 // Mode 4 (cat): features [0, hybrid LD), hash levels after them. Mode 12
 // (adaptive_cat, rows of total LD + 1 with the blend weight last): coarse
 // channels from the surfel, fine channels wgt * surfel + (1 - wgt) * hash; with
@@ -121,6 +123,26 @@ __device__ __forceinline__ float mode_features(const RenderParams& p, uint32_t i
     add(g, pg, pg + hd, wgt * w);
     return 1.0f - wgt;
   }
+  if (base == 6) {
+    // adaptive (forward.cu:1283-1325): rows of C channels, feat = 0.5 row +
+    // 0.5 hash over the L hash levels' channels
+    add(p.gauss + (size_t)id * p.C, 0, min(hd, p.C), 0.5f * w);
+    return p.L > 0 ? 0.5f : 0.0f;
+  }
+  if (base == 7) {
+    // adaptive_add (:1326-1377): rows of total LD + 1, feat = wgt row +
+    // (1 - wgt) hash, the hash levels' channels from 0
+    const int td = 2 * p.total_levels;
+    const float* g = p.gauss + (size_t)id * (td + 1);
+    const float wgt = __ldg(g + td);
+    add(g, 0, td, wgt * w);
+    return p.L > 0 ? 1.0f - wgt : 0.0f;
+  }
+  if (base == 0) {
+    // level 0 (:1093-1096): per-surfel colours of C channels, no hash query
+    add(p.gauss + (size_t)id * p.C, 0, p.C, w);
+    return 0.0f;
+  }
   const float* g = p.gauss + (size_t)id * (pg + 1);  // base == 14
   const float wgt = __ldg(g + pg);
   add(g, 0, pg, w);
@@ -159,7 +181,7 @@ __global__ void __launch_bounds__(kThreads, 2) blend_kernel(const RenderParams p
   const int total = (int)(range.y - range.x);
   const int rounds = div_up(total, kBatch);
   const float vmin = p.gridrange[0], vmax = p.gridrange[1];
-  const int hoff = (kGeneral && p.render_mode != 0) ? p.hybrid_levels : 0;  // level of hash level 0
+  const int hoff = kGeneral ? hash_level_offset(p.render_mode, p.hybrid_levels) : 0;  // level of hash level 0
 
   float T = 1.0f;
   uint32_t contributor = 0, last_contributor = 0, render_number = 0;
@@ -214,64 +236,62 @@ __global__ void __launch_bounds__(kThreads, 2) blend_kernel(const RenderParams p
       nitems += __popc(m);
     }
     __syncwarp();
-    // Two levels per pass, 64 list entries (two per lane) per step: four
+    // Four levels per pass, 32 list entries (one per lane) per step: four
     // lookups in flight per lane. Each pixel's owner lane then adds its own
     // results from the step, in sample order.
-    for (uint32_t l = 0; l < L; l += 2) {
-      const bool has1 = l + 1 < L;
-      const LevelConst lc0 = S.lv[l];
-      const LevelConst lc1 = S.lv[has1 ? l + 1 : l];
-      float2* ap0 = acc_pair(S.acc, t, hoff + l);
-      float2* ap1 = acc_pair(S.acc, t, hoff + (has1 ? l + 1 : l));
-      float2 c0 = *ap0;
-      float2 c1 = has1 ? *ap1 : make_float2(0.f, 0.f);
+    for (uint32_t l = 0; l < L; l += 4) {
+      const uint32_t nl = min(4u, L - l);
+      float2 c[4];
+      float2* ap[4];
+#pragma unroll
+      for (int q = 0; q < 4; q++) {
+        ap[q] = acc_pair(S.acc, t, hoff + (int)(l + min((uint32_t)q, nl - 1)));
+        c[q] = (uint32_t)q < nl ? *ap[q] : make_float2(0.f, 0.f);
+      }
       int nk = 0;
       for (int ch = 0; ch < nitems; ch += kChunk) {
-        float4 sa = make_float4(0.f, 0.f, 0.f, 0.f), sb = sa;
-        uint32_t ma = 0, mb = 0;
-        const int ia = ch + lane, ib = ch + 32 + lane;
+        float4 sa = make_float4(0.f, 0.f, 0.f, 0.f);
+        uint32_t ma = 0;
+        const int ia = ch + lane;
         if (ia < nitems) {
           const uint32_t tb = S.item[wid][ia];
           const int pp = pbase + (int)(tb & 31u), k = (int)(tb >> 5);
           sa = S.samp[k][pp];
           ma = S.lvl[k][pp];
         }
-        if (ib < nitems) {
-          const uint32_t tb = S.item[wid][ib];
-          const int pp = pbase + (int)(tb & 31u), k = (int)(tb >> 5);
-          sb = S.samp[k][pp];
-          mb = S.lvl[k][pp];
+        float f[4][3];
+        Corner8<TableT> v[4];
+        bool u[4];
+#pragma unroll
+        for (int q = 0; q < 4; q++) {
+          u[q] = (uint32_t)q < nl && l + q < ma;
+          if (u[q]) lookup_issue<TableT>(S.lv[l + q], p.table, sa, half_shift, p.interp, f[q], v[q]);
         }
-        const bool ua0 = l < ma, ub0 = l < mb, ua1 = has1 && l + 1 < ma, ub1 = has1 && l + 1 < mb;
-        float fa0[3], fb0[3], fa1[3], fb1[3];
-        Corner8<TableT> va0, vb0, va1, vb1;
-        if (ua0) lookup_issue<TableT>(lc0, p.table, sa, half_shift, p.interp, fa0, va0);
-        if (ub0) lookup_issue<TableT>(lc0, p.table, sb, half_shift, p.interp, fb0, vb0);
-        if (ua1) lookup_issue<TableT>(lc1, p.table, sa, half_shift, p.interp, fa1, va1);
-        if (ub1) lookup_issue<TableT>(lc1, p.table, sb, half_shift, p.interp, fb1, vb1);
-        const float2 z = make_float2(0.f, 0.f);
-        const float2 ra0 = ua0 ? lookup_finish<TableT>(fa0, va0) : z;
-        const float2 rb0 = ub0 ? lookup_finish<TableT>(fb0, vb0) : z;
-        const float2 ra1 = ua1 ? lookup_finish<TableT>(fa1, va1) : z;
-        const float2 rb1 = ub1 ? lookup_finish<TableT>(fb1, vb1) : z;
-        S.res[wid][lane] = make_float4(ra0.x, ra0.y, ra1.x, ra1.y);
-        S.res[wid][32 + lane] = make_float4(rb0.x, rb0.y, rb1.x, rb1.y);
+        float2 r[4];
+#pragma unroll
+        for (int q = 0; q < 4; q++) r[q] = u[q] ? lookup_finish<TableT>(f[q], v[q]) : make_float2(0.f, 0.f);
+        S.res[wid][2 * lane] = make_float4(r[0].x, r[0].y, r[1].x, r[1].y);
+        S.res[wid][2 * lane + 1] = make_float4(r[2].x, r[2].y, r[3].x, r[3].y);
         __syncwarp();
         while (nk < cnt) {
           const int ps = S.pos[nk][t];
           if (ps >= ch + kChunk) break;
-          const float4 rv = S.res[wid][ps - ch];
+          const float4 r01 = S.res[wid][2 * (ps - ch)];
+          const float4 r23 = S.res[wid][2 * (ps - ch) + 1];
           const uint32_t mk = S.lvl[nk][t];
           const float w = S.samp[nk][t].w;
           const float2 ww = make_float2(w, w);
-          if (l < mk) c0 = __ffma2_rn(make_float2(rv.x, rv.y), ww, c0);
-          if (has1 && l + 1 < mk) c1 = __ffma2_rn(make_float2(rv.z, rv.w), ww, c1);
+          if (l < mk) c[0] = __ffma2_rn(make_float2(r01.x, r01.y), ww, c[0]);
+          if (l + 1 < mk && nl > 1) c[1] = __ffma2_rn(make_float2(r01.z, r01.w), ww, c[1]);
+          if (l + 2 < mk && nl > 2) c[2] = __ffma2_rn(make_float2(r23.x, r23.y), ww, c[2]);
+          if (l + 3 < mk && nl > 3) c[3] = __ffma2_rn(make_float2(r23.z, r23.w), ww, c[3]);
           nk++;
         }
         __syncwarp();
       }
-      *ap0 = c0;
-      if (has1) *ap1 = c1;
+#pragma unroll
+      for (int q = 0; q < 4; q++)
+        if ((uint32_t)q < nl) *ap[q] = c[q];
     }
     __syncwarp();
     cnt = 0;
@@ -390,7 +410,10 @@ __global__ void __launch_bounds__(kThreads, 2) blend_kernel(const RenderParams p
           const bool fast13 = m13 && (p.render_mode >> 8) != 0 &&
                               __ldg(p.gauss + (size_t)__float_as_uint(q6.z) * (2 * p.total_levels + 1) +
                                     2 * p.total_levels) > 0.5f;
-          if (!fast13) {
+          // Level 0 (forward.cu:1093-1096) adds the per-surfel colours only: no
+          // position, no level colour, nothing queued for the hash grid.
+          const bool lvl0 = kGeneral && p.render_mode == 0 && L == 0;
+          if (!fast13 && !lvl0) {
             pos0 += w * xyz.x;
             pos1 += w * xyz.y;
             pos2 += w * xyz.z;
@@ -420,11 +443,13 @@ __global__ void __launch_bounds__(kThreads, 2) blend_kernel(const RenderParams p
             in2 = (st * in2 + 2.0f) * 0.25f;
           }
           float hw = w;  // weight of this sample's hash features
-          if (kGeneral && p.render_mode != 0)
+          if (kGeneral && uses_surfel_rows(p.render_mode, p.L))
             hw = w * mode_features(p, __float_as_uint(q6.z), w, S.acc, t);
-          S.samp[cnt][t] = make_float4(in0, in1, in2, hw);
-          S.lvl[cnt][t] = (uint8_t)((oob || hw == 0.0f) ? 0u : min(apl, L));
-          cnt++;
+          if (!lvl0) {
+            S.samp[cnt][t] = make_float4(in0, in1, in2, hw);
+            S.lvl[cnt][t] = (uint8_t)((oob || hw == 0.0f) ? 0u : min(apl, L));
+            cnt++;
+          }
 
           if (m13) {
             T = test_T;
@@ -438,8 +463,10 @@ __global__ void __launch_bounds__(kThreads, 2) blend_kernel(const RenderParams p
             ac0 = 1.0f;
             ac1 = (float)(1.0 - (apl - 4) * 0.5);
           }
-          vis0 += ac0 * w;
-          vis1 += ac1 * w;
+          if (!lvl0) {
+            vis0 += ac0 * w;
+            vis1 += ac1 * w;
+          }
           if (p.record_transmittance) {
             const uint32_t id = __float_as_uint(S.rec[s][jj][7].z);  // the record's surfel index
             atomicAdd(p.cover_pixels + id, 1.0f);
@@ -524,12 +551,12 @@ int launch_blend(const RenderParams& p, int tiles, cudaStream_t stream) {
 // renders nothing for shapes it was not compiled for).
 int render_launch(const RenderParams& p, int fp16, cudaStream_t stream) {
   if (p.LD != 2 || p.C > kMaxChannels || p.C <= 0) return NS_ERR_UNSUPPORTED;
-  const int hoff = p.render_mode != 0 ? p.hybrid_levels : 0;
+  const int hoff = hash_level_offset(p.render_mode, p.hybrid_levels);
   if (hoff < 0 || (int64_t)hoff + p.L > (uint32_t)(p.C / p.LD) || p.L > (uint32_t)kMaxLevels)
     return NS_ERR_UNSUPPORTED;
   const int tiles = div_up(p.W, kTile) * div_up(p.H, kTile);
   if (tiles == 0) return NS_OK;
-  if (p.kernel_type != 0 || p.render_mode != 0)
+  if (p.kernel_type != 0 || uses_surfel_rows(p.render_mode, p.L))
     return fp16 ? launch_blend<__half, true>(p, tiles, stream) : launch_blend<float, true>(p, tiles, stream);
   return fp16 ? launch_blend<__half, false>(p, tiles, stream) : launch_blend<float, false>(p, tiles, stream);
 }

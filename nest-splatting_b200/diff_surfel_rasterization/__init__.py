@@ -80,9 +80,11 @@ class _RasterizeGaussians(torch.autograd.Function):
                 gridrange_diffuse, raster_settings, hashgrid_settings, render_mode, shapes, kernel_type):
         mode = int(render_mode)
         base_mode = mode & 0xFF
-        if base_mode not in (0, 4, 12, 13, 14) or (mode >> 8) > 1 or ((mode >> 8) and base_mode == 4):
-            raise NotImplementedError(f"render_mode {render_mode}: 0 (baseline hash grid), 4 (cat), "
-                                      f"12 (adaptive_cat), 13 (adaptive_cat_fast), 14 (adaptive_zero) are built")
+        if base_mode not in (0, 4, 6, 7, 12, 13, 14) or (mode >> 8) > 1 or \
+                ((mode >> 8) and base_mode not in (12, 13, 14)):
+            raise NotImplementedError(f"render_mode {render_mode}: 0 (baseline hash grid; level 0: per-surfel "
+                                      f"colours), 4 (cat), 6 (adaptive), 7 (adaptive_add), 12 (adaptive_cat), "
+                                      f"13 (adaptive_cat_fast), 14 (adaptive_zero) are built")
         if int(kernel_type) not in (0, 1, 2, 3):
             raise NotImplementedError(f"kernel_type {kernel_type}: 0-3 are built")
         shp = _nonempty(shapes)
@@ -97,11 +99,36 @@ class _RasterizeGaussians(torch.autograd.Function):
         if means3D.ndim != 2 or means3D.shape[1] != 3:
             raise RuntimeError("means3D must have dimensions (num_points, 3)")
         L = int(hashgrid_settings.L)
-        if L <= 0 or _nonempty(features) is None:
-            raise NotImplementedError("level == 0 (per-surfel colours) is not built")
         hybrid = total = 0
         gauss = None
-        if base_mode != 0:
+        if base_mode == 0 and L <= 0:
+            # level 0 (forward.cu:1093-1096): the precomputed per-surfel colours are
+            # blended (SH colours from preprocess are not built)
+            gauss = _nonempty(colors_precomp)
+            if gauss is None:
+                raise NotImplementedError("level 0 from SH coefficients is not built: pass colors_precomp")
+            gauss = gauss.detach().contiguous().float()
+            L = 0
+            if _nonempty(features) is None:  # the C-ABI wants a table; level 0 reads none
+                features = torch.zeros((1, 2), dtype=torch.float32, device=means3D.device)
+                offsets = torch.zeros(1, dtype=torch.int32, device=means3D.device)
+                gridrange = torch.tensor([-1.0, 1.0], device=means3D.device)
+        elif L <= 0 or _nonempty(features) is None:
+            raise RuntimeError(f"render_mode {mode} needs hash-grid features and levels")
+        elif base_mode == 6:
+            # adaptive: the level word is the number of hash levels; rows of C channels
+            gauss = _nonempty(colors_precomp)
+            if gauss is None:
+                raise RuntimeError("render_mode 6 needs colors_precomp (per-surfel features)")
+            gauss = gauss.detach().contiguous().float()
+        elif base_mode == 7:
+            # adaptive_add: level word total << 16 | active hash levels << 8
+            total, L = (L >> 16) & 0xFF, (L >> 8) & 0xFF
+            gauss = _nonempty(colors_precomp)
+            if gauss is None:
+                raise RuntimeError("render_mode 7 needs colors_precomp (per-surfel features + weight)")
+            gauss = gauss.detach().contiguous().float()
+        elif base_mode != 0:
             # The reference's level word: total << 16 | active hash levels << 8 | hybrid.
             total, active, hybrid = (L >> 16) & 0xFF, (L >> 8) & 0xFF, L & 0xFF
             if base_mode == 4:
@@ -116,6 +143,8 @@ class _RasterizeGaussians(torch.autograd.Function):
                 raise RuntimeError(f"render_mode {mode} needs colors_precomp (per-surfel features)")
             gauss = gauss.detach().contiguous().float()
         _, _, OS = _shape_dims(hashgrid_settings)
+        if base_mode == 0 and L == 0 and OS == 0:
+            OS = gauss.shape[-1]
         feats = features.contiguous()
         if feats.dtype not in (torch.float16, torch.float32):
             feats = feats.float()

@@ -47,9 +47,15 @@ class RasterConfig:
     table_fp16: bool = True
     kernel_type: int = 0  # 0 Gaussian, 1 beta, 2 flex, 3 general
     deterministic: bool = False  # backward: fixed-point (bit-reproducible) table gradient
-    render_mode: int = 0     # 0 baseline; 4 cat, 12 adaptive_cat, 14 adaptive_zero (| 256 inference)
+    render_mode: int = 0     # 0 baseline (levels 0: per-surfel colours); 4 cat, 6 adaptive, 7 adaptive_add,
+    #                          12 adaptive_cat, 13 adaptive_cat_fast, 14 adaptive_zero (| 256 inference)
     hybrid_levels: int = 0   # per-surfel feature levels of modes 4 / 12 / 14
     total_levels: int = 0    # all levels (mode 12 rows hold total_levels * level_dim + 1)
+
+    @property
+    def uses_rows(self) -> bool:
+        """Samples read per-surfel rows (colors_precomp): every mode but 0, and level 0."""
+        return int(self.render_mode) != 0 or int(self.levels) == 0
 
     def to_c(self) -> _lib.RasterSettings:
         s = _lib.RasterSettings()
@@ -147,9 +153,9 @@ def rasterize_forward(cfg: RasterConfig, means3D, scales, rotations, opacities, 
     surf.opacities, surf.homotrans, surf.ap_level = ptr(opacities), ptr(homotrans), ptr(ap_level)
     surf.features, surf.offsets, surf.gridrange = ptr(features), ptr(offsets), ptr(gridrange)
     surf.shapes = ptr(shapes)
-    if cfg.render_mode != 0:
+    if cfg.uses_rows:
         if colors_precomp is None:
-            raise ValueError(f"render_mode {cfg.render_mode} needs colors_precomp")
+            raise ValueError(f"render_mode {cfg.render_mode} with {cfg.levels} levels needs colors_precomp")
         _require_cuda(colors_precomp)
         surf.colors_precomp = ptr(colors_precomp)
     outs = _lib.RasterOutputs()
@@ -234,9 +240,9 @@ def rasterize_backward(cfg: RasterConfig, means3D, scales, rotations, opacities,
         shapes = shapes.contiguous().float().reshape(-1)
         _require_cuda(shapes)
         g["shapes"] = torch.empty((P,), dtype=torch.float32, device=dev)
-    if cfg.render_mode != 0:
+    if cfg.uses_rows:
         if colors_precomp is None:
-            raise ValueError(f"render_mode {cfg.render_mode} needs colors_precomp")
+            raise ValueError(f"render_mode {cfg.render_mode} with {cfg.levels} levels needs colors_precomp")
         colors_precomp = colors_precomp.contiguous().float()
         _require_cuda(colors_precomp)
         g["colors_precomp"] = torch.zeros_like(colors_precomp)
@@ -251,7 +257,7 @@ def rasterize_backward(cfg: RasterConfig, means3D, scales, rotations, opacities,
     surf.features, surf.offsets, surf.gridrange = ptr(features), ptr(offsets), ptr(gridrange)
     if cfg.kernel_type != 0:
         surf.shapes = ptr(shapes)
-    if cfg.render_mode != 0:
+    if cfg.uses_rows:
         surf.colors_precomp = ptr(colors_precomp)
     gi = _lib.GradsIn(ptr(dL_dcolor), ptr(dL_dothers), ptr(radii))
     go = _lib.GradsOut(ptr(g["means3D"]), ptr(g["means2D"]), ptr(g["opacity"]), ptr(g["scales"]),

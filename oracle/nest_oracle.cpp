@@ -69,6 +69,17 @@ void mode_feature(float* feat, int C, int LD, int render_mode, int hybrid_levels
         for (int i = 0; i < hd && pg + i < C; i++) feat[pg + i] = wgt * g[pg + i] + (1.0f - wgt) * hf[i];
       }
     }
+  } else if (base == 6) {  // :1283-1325: rows of C, uniform blend with the hash levels
+    const float* g = gauss + (size_t)id * C;
+    if (L > 0) query();
+    for (int i = 0; i < hd && i < C; i++) feat[i] = 0.5f * g[i] + 0.5f * (L > 0 ? hf[i] : 0.0f);
+  } else if (base == 7) {  // :1326-1377: rows of total LD + 1, weight last
+    const int td = total_levels * LD;
+    const float* g = gauss + (size_t)id * (td + 1);
+    const float wgt = g[td];
+    if (L > 0) query();
+    for (int i = 0; i < td && i < C; i++)
+      feat[i] = wgt * g[i] + (1.0f - wgt) * (L > 0 && i < hd ? hf[i] : 0.0f);
   } else if (base == 14) {  // :1701-1790
     const float* g = gauss + (size_t)id * (pg + 1);
     const float wgt = g[pg];
@@ -312,6 +323,21 @@ void oracle_render(int W, int H, const uint32_t* ranges, const uint32_t* point_l
           const bool m13 = (render_mode & 0xFF) == 13;
           const bool fast13 = m13 && ((render_mode >> 8) & 1) &&
                               gauss[(size_t)id * (total_levels * LD + 1) + total_levels * LD] > 0.5f;
+          // level 0 (forward.cu:1093-1096): the per-surfel colours only; no hit
+          // point, position or level colour
+          const bool lvl0 = render_mode == 0 && L == 0;
+          if (lvl0) {
+            for (int c = 0; c < C; c++) Cacc[c] += gauss[(size_t)id * C + c] * w;
+            if (record_transmittance) {
+#pragma omp atomic
+              cover_pixels[id] += 1.0f;
+#pragma omp atomic
+              trans_avg[id] += T;
+            }
+            T = test_T;
+            last_contributor = contributor;
+            continue;
+          }
           if (!fast13) {
             pos[0] += w * xyz.x;
             pos[1] += w * xyz.y;

@@ -296,10 +296,19 @@ void render_backward(int W, int H, const uint32_t* ranges, const uint32_t* point
             grad_feat[c] = dchannel_dcolor * dL_dpixel[c];
             sum_grad += std::fabs(grad_feat[c]);
           }
-          atomic_add<R>(&dL_gradsum[id], sum_grad);
           const uint32_t apl = (uint32_t)std::floor(ap_level[id]);
           R dL_dxyz[3];
-          if (base_mode == 0) {
+          const bool lvl0 = base_mode == 0 && L == 0;
+          // level 0 (backward.cu:833-849): the per-surfel colours' gradient only,
+          // no densification sum, no hit-point gradient
+          if (!lvl0) atomic_add<R>(&dL_gradsum[id], sum_grad);
+          if (lvl0) {
+            dL_dxyz[0] = dL_dxyz[1] = dL_dxyz[2] = 0;
+            for (int c = 0; c < C; c++) {
+              feat[c] = gauss[(size_t)id * C + c];
+              atomic_add<R>(&dL_dcolors[(size_t)id * C + c], grad_feat[c]);
+            }
+          } else if (base_mode == 0) {
             query_feature_bw<R>(feat.data(), C, LD, xyz, vmin, vmax, offsets, apl, table, L, S, Hres,
                              align_corners != 0, interp, contract != 0, grad_feat.data(), dL_dtable,
                              dL_dxyz);
@@ -317,6 +326,15 @@ void render_backward(int W, int H, const uint32_t* ranges, const uint32_t* point
             if (base_mode == 4) {
               row = (size_t)id * pg;
               g = gauss + row;
+            } else if (base_mode == 6) {  // rows of C, hash factor 1/2
+              row = (size_t)id * C;
+              g = gauss + row;
+              b = R(0.5);
+            } else if (base_mode == 7) {  // rows of total LD + 1, hash factor 1 - wgt
+              row = (size_t)id * (td + 1);
+              g = gauss + row;
+              wgt = g[td];
+              b = R(1) - wgt;
             } else if (base_mode == 12) {
               row = (size_t)id * (td + 1);
               g = gauss + row;
@@ -343,6 +361,25 @@ void render_backward(int W, int H, const uint32_t* ranges, const uint32_t* point
             }
             if (base_mode == 4) {
               for (int i = 0; i < hd; i++) feat[pg + i] = hfeat[i];
+            } else if (base_mode == 6) {
+              // the derivative of the forward (feat = (row + hash) / 2 on the hash
+              // levels' channels); the reference's case 6 backward reads a row of
+              // 2 L LD values with a per-channel mask its forward does not have
+              for (int i = 0; i < hd && i < C; i++) {
+                feat[i] = R(0.5) * R(g[i]) + R(0.5) * hfeat[i];
+                atomic_add<R>(&dL_dcolors[row + i], R(0.5) * grad_feat[i]);
+              }
+            } else if (base_mode == 7) {
+              // backward.cu:1108-1190: the weight slot gets d_gamma = (row - hash) .
+              // grad_feat * wgt (1 - wgt), the pre-sigmoid parameter's gradient
+              R dw = 0;
+              for (int i = 0; i < td && i < C; i++) {
+                const R hv = (L > 0 && i < hd) ? hfeat[i] : R(0);
+                feat[i] = wgt * R(g[i]) + (R(1) - wgt) * hv;
+                atomic_add<R>(&dL_dcolors[row + i], wgt * grad_feat[i]);
+                dw += grad_feat[i] * (R(g[i]) - hv);
+              }
+              atomic_add<R>(&dL_dcolors[row + td], dw * wgt * (R(1) - wgt));
             } else if (base_mode == 12) {
               R dw = 0;
               if (L > 0) {

@@ -258,7 +258,8 @@ def render_backward(pre, vals, ranges, fwd, homotrans, ap_level, table_f32, offs
     dict returned by render(). Returns the render-pass gradients (reference layouts).
     f64=True evaluates the same formulas in double (float64 outputs). kernel_type
     1-3 take per-surfel `shapes` [P] and add dL_dshapes [P]. Render modes 4 / 12 /
-    14 take the per-surfel rows `gauss` and add dL_dcolors (same shape).
+    14 (and 6 / 7, and level 0: mode 0 with L = 0) take the per-surfel rows
+    `gauss` and add dL_dcolors (same shape).
     row_stride > 1 walks only tile rows ty % row_stride == 0 (the upstream
     gradient must be zero on the others, e.g. after a sampled forward)."""
     lib = load()
@@ -269,7 +270,10 @@ def render_backward(pre, vals, ranges, fwd, homotrans, ap_level, table_f32, offs
              dL_dhomoMat=np.zeros((P, 9), dt), dL_dmean2D=np.zeros((P, 3), dt),
              dL_dnormal=np.zeros((P, 3), dt), dL_dopacity=np.zeros(P, dt), dL_gradsum=np.zeros(P, dt),
              dL_dshapes=np.zeros(P, dt))
-    if render_mode != 0:
+    rows = render_mode != 0 or int(L) == 0  # per-surfel rows: every mode but 0, and level 0
+    if rows:
+        if gauss is None:
+            raise ValueError(f"render_mode {render_mode} with {L} levels needs the per-surfel rows (gauss)")
         gauss = _f32(gauss).reshape(P, -1)
         g["dL_dcolors"] = np.zeros(gauss.shape, dt)
     if kernel_type != 0:
@@ -290,7 +294,7 @@ def render_backward(pre, vals, ranges, fwd, homotrans, ap_level, table_f32, offs
                                _p(g["dL_dtransMat"]), _p(g["dL_dhomoMat"]), _p(g["dL_dmean2D"]),
                                _p(g["dL_dnormal"]), _p(g["dL_dopacity"]), _p(g["dL_gradsum"]), int(kernel_type),
                                _p(shapes if kernel_type != 0 else None), _p(g["dL_dshapes"]), int(render_mode),
-                               int(hybrid_levels), int(total_levels), _p(gauss if render_mode != 0 else None),
+                               int(hybrid_levels), int(total_levels), _p(gauss if rows else None),
                                _p(g.get("dL_dcolors")), int(row_stride))
     return g
 

@@ -93,6 +93,8 @@ def query(xyz, apl, table, offsets, L, LD, S, Hres, vmin, vmax, align_corners=Fa
             acc = acc + w[:, None] * table[rows]
         on = torch.as_tensor(lv < apl, dtype=table.dtype)[:, None] * (~oob)[:, None].to(table.dtype)
         feats.append(acc * on)
+    if not feats:  # no level (level 0)
+        return xyz.new_zeros(xyz.shape[0], 0)
     return torch.cat(feats, 1)
 
 
@@ -118,10 +120,23 @@ def splat_value(rho, shape, kernel_type: int):
 
 
 def mode_feature(f_hash, row, mode, pg, td, C):
-    """Feature vectors [n, C] of render modes 4 / 12 / 14 (forward.cu:1218-1282,
-    1593-1790, training rules) from the hash features f_hash [n, L*LD] and the
-    surfel's row of colors_precomp (blend weight last for 12 / 14)."""
+    """Feature vectors [n, C] of render modes 4 / 6 / 7 / 12 / 14
+    (forward.cu:1218-1377, 1593-1790, training rules) and of level 0 (mode 0
+    without hash levels, :1093-1096) from the hash features f_hash [n, L*LD]
+    and the surfel's row of colors_precomp (blend weight last for 7 / 12 / 14)."""
     n, hd = f_hash.shape
+    if mode == 0:  # level 0: the row is the colour
+        return row[:C].expand(n, C)
+    if mode in (6, 7):
+        if mode == 6:  # uniform blend on the hash levels' channels
+            feat = 0.5 * row[:hd].expand(n, hd) + 0.5 * f_hash
+        else:  # weighted blend over total LD channels, hash zero past its levels
+            wgt = row[td]
+            hpad = torch.cat([f_hash, f_hash.new_zeros(n, td - hd)], 1)
+            feat = wgt * row[:td].expand(n, td) + (1 - wgt) * hpad
+        if feat.shape[1] < C:
+            feat = torch.cat([feat, feat.new_zeros(n, C - feat.shape[1])], 1)
+        return feat[:, :C]
     coarse = row[:pg].expand(n, pg)
     if mode == 4:
         fine = f_hash

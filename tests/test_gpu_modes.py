@@ -1,6 +1,8 @@
 """GPU parity of the render modes that combine per-surfel features with the hash
-grid (forward.cu:1218-1282 mode 4 cat, :1593-1700 mode 12 adaptive_cat,
-:1701-1790 mode 14 adaptive_zero; the inference flag 256 of 12 and 14) through
+grid (forward.cu:1218-1282 mode 4 cat, :1283-1325 mode 6 adaptive, :1326-1377
+mode 7 adaptive_add, :1593-1700 mode 12 adaptive_cat, :1701-1790 mode 14
+adaptive_zero; the inference flag 256 of 12 and 14) and of level 0
+(:1093-1096, per-surfel colours without a hash grid) through
 the drop-in module, against the oracle's restatement (oracle/nest_oracle.cpp
 mode_feature). The level word and the feature rows are built as the
 reference's renderer builds them (gaussian_renderer/__init__.py:216-241,
@@ -31,8 +33,10 @@ def mode_case(mode, total, hybrid, active, seed, weights="uniform"):
     base = mode & 0xFF
     if base == 4:
         gauss = torch.rand(P, hybrid * LD, generator=g) * 2 - 1
+    elif base in (0, 6):  # level 0 / adaptive: rows of C = total LD channels
+        gauss = torch.rand(P, total * LD, generator=g) * 2 - 1
     else:
-        width = total * LD if base in (12, 13) else hybrid * LD
+        width = total * LD if base in (7, 12, 13) else hybrid * LD
         feats = torch.rand(P, width, generator=g) * 2 - 1
         if weights == "uniform":
             wgt = torch.rand(P, 1, generator=g)
@@ -41,6 +45,18 @@ def mode_case(mode, total, hybrid, active, seed, weights="uniform"):
                 torch.randint(0, 9, (P, 1), generator=g)]
         gauss = torch.cat([feats, wgt], 1)
     return sc, inp, grid, gauss.float().contiguous()
+
+
+def level_word(mode, total, hybrid, active):
+    """hashgrid_settings.L as the reference's renderer sets it: the level count
+    for mode 6 and for mode 0 (0: per-surfel colours), total << 16 | active << 8
+    for mode 7, and total << 16 | active << 8 | hybrid for 4 and 12-14."""
+    base = mode & 0xFF
+    if base in (0, 6):
+        return active
+    if base == 7:
+        return (total << 16) | (active << 8)
+    return (total << 16) | (active << 8) | hybrid
 
 
 def run_mode(sc, inp, grid, gauss, mode, total, hybrid, active):
@@ -58,7 +74,7 @@ def run_mode(sc, inp, grid, gauss, mode, total, hybrid, active):
         projmatrix=cam.full_proj_transform.to(dev), sh_degree=0, campos=cam.camera_center.to(dev),
         prefiltered=False, debug=False, beta=0.0, if_contract=False, record_transmittance=False,
         max_intersections=0)
-    hs = dsr.HashGridSettings(L=(total << 16) | (active << 8) | hybrid, S=grid.S, H=grid.base_resolution,
+    hs = dsr.HashGridSettings(L=level_word(mode, total, hybrid, active), S=grid.S, H=grid.base_resolution,
                               align_corners=False, interpolation=0,
                               shape_dims=torch.tensor([hybrid * 2, active * 2, C], dtype=torch.int32, device=dev))
     r = dsr.GaussianRasterizer(rs, hs)
@@ -92,6 +108,12 @@ def run_mode(sc, inp, grid, gauss, mode, total, hybrid, active):
     (14, 16, 16, 0, "uniform"),
     (13, 16, 6, 10, "uniform"),
     (13 | 256, 16, 6, 10, "thresholds"),
+    (6, 16, 0, 10, "uniform"),
+    (6, 12, 0, 12, "uniform"),
+    (7, 16, 0, 10, "uniform"),
+    (7, 16, 0, 10, "thresholds"),
+    (7, 12, 0, 0, "uniform"),
+    (0, 16, 0, 0, "uniform"),
 ])
 def test_render_modes_match_oracle(mode, total, hybrid, active, weights):
     sc, inp, grid, gauss = mode_case(mode, total, hybrid, active, seed=50 + (mode & 0xFF), weights=weights)
@@ -156,7 +178,8 @@ def mode_grads(sc, inp, grid, gauss, mode, total, hybrid, active, gc, go):
 
 
 @pytest.mark.parametrize("mode,total,hybrid,active,seed", [
-    (4, 16, 6, 10, 19), (12, 16, 6, 10, 19), (14, 16, 6, 10, 19), (12, 14, 5, 7, 18), (14, 16, 16, 0, 18)])
+    (4, 16, 6, 10, 19), (12, 16, 6, 10, 19), (14, 16, 6, 10, 19), (12, 14, 5, 7, 18), (14, 16, 16, 0, 18),
+    (6, 16, 0, 10, 19), (7, 16, 0, 10, 19), (7, 12, 0, 0, 18), (0, 16, 0, 0, 19), (0, 2, 0, 0, 18)])
 def test_render_modes_backward_match_oracle(mode, total, hybrid, active, seed):
     """Every gradient, the per-surfel rows' (blend weight included) among them,
     against the oracle's restatement of backward.cu:987-1033, 1425-1606 (itself
@@ -172,6 +195,9 @@ def test_render_modes_backward_match_oracle(mode, total, hybrid, active, seed):
     if active == 0:
         keys = {k: v for k, v in keys.items() if k != "table"}
         assert not got["table"].any()
+    if mode == 0:  # level 0 adds nothing to the densification sum (backward.cu:833-849)
+        keys = {k: v for k, v in keys.items() if k != "gradsum"}
+        assert not got["gradsum"].any() and not ref["g"]["dL_gradsum"].any()
     check_all(got, ref, exact, keys=keys)
 
 

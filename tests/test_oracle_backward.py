@@ -55,15 +55,16 @@ def oracle_grads(c):
     kw = dict(interp=c["interp"])
     if c.get("kernel_type"):
         kw.update(kernel_type=c["kernel_type"], shapes=c["shapes"].numpy())
-    if c.get("mode"):
+    if "mode" in c:
         kw.update(render_mode=c["mode"], hybrid_levels=c["hybrid"], total_levels=c["total"], gauss=c["gauss"].numpy())
-    C = c["total"] * grid.level_dim if c.get("mode") else grid.channels
+    C = c["total"] * grid.level_dim if "mode" in c else grid.channels
+    L = c.get("levels", grid.levels)
     fwd = oracle.render(pre, vals, ranges, c["homo"].numpy(), c["ap"].numpy(), c["table"].numpy(),
                         grid.offsets.numpy(), grid.gridrange.numpy(), W, H, C, grid.level_dim,
-                        grid.levels, grid.S, grid.base_resolution, **kw)
+                        L, grid.S, grid.base_resolution, **kw)
     g = oracle.render_backward(pre, vals, ranges, fwd, c["homo"].numpy(), c["ap"].numpy(), c["table"].numpy(),
                                grid.offsets.numpy(), grid.gridrange.numpy(), W, H, C, grid.level_dim,
-                               grid.levels, grid.S, grid.base_resolution, c["gc"].numpy(), c["go"].numpy(), **kw)
+                               L, grid.S, grid.base_resolution, c["gc"].numpy(), c["go"].numpy(), **kw)
     pg = oracle.preprocess_backward(c["means"].numpy(), c["scales"].numpy(), c["rots"].numpy(), pre, g, vm, pm, W,
                                     H, cam.tanfovx, cam.tanfovy)
     return pre, vals, ranges, fwd, g, pg
@@ -72,19 +73,28 @@ def oracle_grads(c):
 def model_grads(c, pre, vals, ranges):
     cam, grid = c["cam"], c["grid"]
     names = ("means", "scales", "rots", "opac", "table") + (("shapes",) if c.get("kernel_type") else ())
-    names = names + (("gauss",) if c.get("mode") else ())
+    names = names + (("gauss",) if "mode" in c else ())
     leaves = [c[k].double().clone().requires_grad_(True) for k in names]
     means, scales, rots, opac, table = leaves[:5]
-    info = dict(L=grid.levels, LD=grid.level_dim, S=grid.S, H=grid.base_resolution, offsets=grid.offsets.numpy(),
-                vmin=float(grid.gridrange[0]), vmax=float(grid.gridrange[1]), interp=c["interp"])
+    info = dict(L=c.get("levels", grid.levels), LD=grid.level_dim, S=grid.S, H=grid.base_resolution,
+                offsets=grid.offsets.numpy(), vmin=float(grid.gridrange[0]), vmax=float(grid.gridrange[1]),
+                interp=c["interp"])
+    rows = None
+    if "mode" in c:
+        rows = leaves[-1]
+        if c["mode"] == 7:
+            # mode 7's weight slot is differentiated as the pre-sigmoid parameter
+            # (backward.cu:1183-1186): the leaf holds logit(weight)
+            td = c["total"] * grid.level_dim
+            rows = torch.cat([rows[:, :td], torch.sigmoid(rows[:, td:td + 1])], 1)
     visible = torch.as_tensor(pre["radii"] > 0)
     color, others, margin, _ = bw_model.render(
         means, scales, rots, opac, table,
         dict(viewmatrix=cam.world_view_transform.numpy(), projmatrix=cam.full_proj_transform.numpy()),
         (ranges, vals), info, np.floor(c["ap"].numpy()).astype(np.int64), c["W"], c["H"],
         kernel_type=c.get("kernel_type", 0), shapes=leaves[5] if c.get("kernel_type") else None,
-        modes=None if not c.get("mode") else dict(mode=c["mode"], gauss=leaves[-1], pg=c["hybrid"] * grid.level_dim,
-                                                  td=c["total"] * grid.level_dim, C=c["total"] * grid.level_dim))
+        modes=None if "mode" not in c else dict(mode=c["mode"], gauss=rows, pg=c["hybrid"] * grid.level_dim,
+                                                td=c["total"] * grid.level_dim, C=c["total"] * grid.level_dim))
     loss = (color * c["gc"].double()).sum() + (others * c["go"][:7].double()).sum()
     loss.backward()
     grads = {k: (v.grad if v.grad is not None else torch.zeros_like(v)).detach().numpy()
@@ -152,33 +162,41 @@ def test_oracle_backward_splat_kernels_match_autograd(kernel_type, lo, hi, seed)
         assert rel_l2(got, mg[k]) < 1e-4, (k, rel_l2(got, mg[k]))
 
 
-@pytest.mark.parametrize("mode,seed", [(4, 21), (12, 22), (14, 23)])
+@pytest.mark.parametrize("mode,seed", [(4, 21), (12, 22), (14, 23), (6, 24), (7, 27), (0, 26)])
 def test_oracle_backward_render_modes_match_autograd(mode, seed):
-    """Render modes 4 / 12 / 14 (training rules): every gradient, the per-surfel
-    rows' (colors_precomp, blend weight included) among them, against autograd
-    of the same forward. The colour term of dL/dalpha uses the forward's
-    feature vector (the reference's cases 12 and 14 read an unwritten array
-    there)."""
+    """Render modes 4 / 6 / 7 / 12 / 14 (training rules) and level 0 (mode 0
+    without hash levels): every gradient, the per-surfel rows' (colors_precomp,
+    blend weight included) among them, against autograd of the same forward.
+    The colour term of dL/dalpha uses the forward's feature vector (the
+    reference's cases 12 and 14 read an unwritten array there); mode 7's weight
+    slot is the pre-sigmoid parameter's gradient, as the reference returns it."""
     c = tiny_case(seed)
     g = torch.Generator().manual_seed(seed)
     n = c["means"].shape[0]
-    total, hybrid = 4, 1
-    grid = synth.hash_grid(g, levels=total - hybrid, log2_T=12, lo=-1.0, hi=1.0, base_resolution=8,
-                           per_level_scale=2.0)
+    total = 4
+    hybrid = 1 if mode in (4, 12, 14) else 0
+    grid = synth.hash_grid(g, levels=3, log2_T=12, lo=-1.0, hi=1.0, base_resolution=8, per_level_scale=2.0)
     LD = grid.level_dim
     c.update(grid=grid, table=grid.table.float().contiguous(), mode=mode, hybrid=hybrid, total=total)
+    if mode == 0:
+        c["levels"] = 0
     c["gc"] = torch.randn(total * LD, c["H"], c["W"], generator=g)
-    width = {4: hybrid * LD, 12: total * LD + 1, 14: hybrid * LD + 1}[mode]
+    width = {4: hybrid * LD, 12: total * LD + 1, 14: hybrid * LD + 1, 6: total * LD, 7: total * LD + 1,
+             0: total * LD}[mode]
     gauss = torch.rand(n, width, generator=g) * 2 - 1
-    if mode != 4:
+    if mode in (7, 12, 14):
         gauss[:, -1] = torch.rand(n, generator=g) * 0.8 + 0.1
     c["gauss"] = gauss.contiguous()
     pre, vals, ranges, fwd, gr, pg = oracle_grads(c)
+    if mode == 7:  # the model's leaf for the weight slot is logit(weight)
+        c["gauss"] = torch.cat([gauss[:, :-1].double(), torch.logit(gauss[:, -1:].double())], 1)
     color, others, margin, mg = model_grads(c, pre, vals, ranges)
     assert margin > 1e-5, "a branch sits on its threshold; pick another seed"
     assert np.max(np.abs(color - fwd["out_color"])) < 2e-5
     checks = {"means": pg["dL_dmeans3D"], "scales": pg["dL_dscales"], "rots": pg["dL_drots"],
-              "opac": gr["dL_dopacity"], "table": gr["dL_dtable"], "gauss": gr["dL_dcolors"]}
+              "opac": gr["dL_dopacity"], "gauss": gr["dL_dcolors"]}
+    if mode != 0:  # level 0 reads no table
+        checks["table"] = gr["dL_dtable"]
     for k, got in checks.items():
         assert np.linalg.norm(mg[k]) > 0, k
         assert rel_l2(got, mg[k]) < 1e-4, (k, rel_l2(got, mg[k]))
