@@ -7,10 +7,15 @@ It imports, unmodified:
   * utils/graphics_utils.py: getWorld2View2, getProjectionMatrix, focal2fov,
     fov2focal -> camera matrices exactly as scene/cameras.py:63-66 builds them;
   * utils/general_utils.py: build_rotation, build_H -> homotrans of
-    gaussian_model.py:312-317 (get_homotrans).
-build_rotation / build_H hard-code device='cuda'; with no GPU in the generating
-container they are run on CPU by redirecting torch.zeros(device='cuda') and
-Tensor.cuda() to CPU for the duration of the call (arithmetic unchanged).
+    gaussian_model.py:312-317 (get_homotrans);
+  * utils/point_utils.py: depths_to_points, depth_to_normal -> the per-pixel
+    rays, world points and surf_normal of the render_pkg decode
+    (gaussian_renderer/__init__.py:789-792), on two small cameras.
+These functions hard-code device='cuda'; with no GPU in the generating
+container they are run on CPU by redirecting torch.zeros / torch.arange
+(device='cuda') and Tensor.cuda() to CPU for the duration of the call
+(arithmetic unchanged). point_utils imports matplotlib for its plotting
+helpers only; where matplotlib is absent an empty module stands in for it.
 The fixture is committed; tests never import the reference.
 """
 from __future__ import annotations
@@ -27,17 +32,24 @@ OUT = Path(__file__).resolve().parent / "reference_utils.npz"
 
 def _cpu_cuda_shim():
     real_zeros = torch.zeros
+    real_arange = torch.arange
     real_cuda = torch.Tensor.cuda
 
     def zeros(*a, **k):
         k.pop("device", None)
         return real_zeros(*a, **k)
 
+    def arange(*a, **k):
+        k.pop("device", None)
+        return real_arange(*a, **k)
+
     torch.zeros = zeros
+    torch.arange = arange
     torch.Tensor.cuda = lambda self, *a, **k: self
 
     def undo():
         torch.zeros = real_zeros
+        torch.arange = real_arange
         torch.Tensor.cuda = real_cuda
 
     return undo
@@ -97,6 +109,43 @@ def main(ref_root: str) -> None:
     data["homo_log_s"] = log_s.numpy()
     data["homo_xyz"] = xyz.numpy()
     data["homo_H"] = H.reshape(64, 16).numpy()
+
+    # point_utils on two small cameras (one odd-sized) and a smooth depth surface.
+    try:
+        import matplotlib.pyplot  # noqa: F401
+    except ImportError:
+        import types
+        mpl = types.ModuleType("matplotlib")
+        mpl.pyplot = types.ModuleType("matplotlib.pyplot")
+        sys.modules["matplotlib"] = mpl
+        sys.modules["matplotlib.pyplot"] = mpl.pyplot
+    from utils import point_utils as pu  # noqa: E402
+    from types import SimpleNamespace
+
+    for i, (W, H, fovx, eye) in enumerate([(64, 48, math.radians(50.0), (0.3, -4.0, 0.8)),
+                                            (37, 23, math.radians(70.0), (2.5, -2.0, 1.5))]):
+        fovy = gr.focal2fov(gr.fov2focal(fovx, W), H)
+        R, t = look_at(eye)
+        wv = torch.tensor(gr.getWorld2View2(R, t, np.array([0.0, 0.0, 0.0]), 1.0)).transpose(0, 1)
+        proj = gr.getProjectionMatrix(znear=0.2, zfar=100.0, fovX=fovx, fovY=fovy).transpose(0, 1)
+        full = wv.unsqueeze(0).bmm(proj.unsqueeze(0)).squeeze(0)
+        view = SimpleNamespace(world_view_transform=wv, full_proj_transform=full, image_width=W, image_height=H)
+        ys, xs = torch.meshgrid(torch.linspace(0, 1, H), torch.linspace(0, 1, W), indexing="ij")
+        depth = (3.5 + 0.7 * xs - 0.5 * ys + 0.08 * torch.sin(11 * xs) * torch.cos(5 * ys))[None].float()
+        undo = _cpu_cuda_shim()
+        try:
+            points, rays_d, rays_o = pu.depths_to_points(view, depth)
+            normal = pu.depth_to_normal(view, depth)
+        finally:
+            undo()
+        data[f"pu{i}_meta"] = np.array([W, H, fovx, fovy, *eye], np.float64)
+        data[f"pu{i}_R"] = R
+        data[f"pu{i}_t"] = t
+        data[f"pu{i}_depth"] = depth.numpy()
+        data[f"pu{i}_rays_d"] = rays_d.numpy()
+        data[f"pu{i}_rays_o"] = rays_o.numpy()
+        data[f"pu{i}_points"] = points.numpy()
+        data[f"pu{i}_normal"] = normal.numpy()
     np.savez(OUT, **data)
     print("wrote", OUT)
 

@@ -37,3 +37,22 @@ def test_homotrans_matches_reference_build_H():
                      torch.tensor(GOLD["homo_q"]), torch.zeros(64, 1)], 1)
     H = synth.build_homotrans(raw).numpy()
     assert np.array_equal(H, GOLD["homo_H"])
+
+
+def _pu_camera(i):
+    W, H, fovx, fovy = GOLD[f"pu{i}_meta"][:4]
+    return camlib.make_camera(GOLD[f"pu{i}_R"], GOLD[f"pu{i}_t"], int(W), int(H), float(fovx), float(fovy))
+
+
+def test_depth_to_normal_matches_reference_point_utils():
+    """nest_b200.train's rays, world points and normals against utils/point_utils.py:10-30,48-60
+    run unmodified (fp32 on CPU): the same expressions in the same order, so bit-equal."""
+    from nest_b200 import train
+    for i in range(2):
+        cam = _pu_camera(i)
+        depth = torch.tensor(GOLD[f"pu{i}_depth"])
+        rays_d, rays_o = train._camera_rays(cam, depth.device)
+        assert np.array_equal(rays_d.numpy(), GOLD[f"pu{i}_rays_d"])
+        assert np.array_equal(rays_o.numpy(), GOLD[f"pu{i}_rays_o"])
+        assert np.array_equal(train.depths_to_points(cam, depth).numpy(), GOLD[f"pu{i}_points"])
+        assert np.array_equal(train.depth_to_normal(cam, depth).numpy(), GOLD[f"pu{i}_normal"])

@@ -155,3 +155,33 @@ def test_render_maps_match_torch(ratio):
         assert torch.isfinite(g).all(), k
         err = float((g - r).abs().max())
         assert err < 2e-3, (k, err)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("i", [0, 1])
+def test_render_maps_surf_normal_matches_reference_point_utils(i):
+    """surf_normal of ns_allmap_decode against utils/point_utils.py:48-60 run
+    unmodified (tests/golden/reference_utils.npz): alpha 1, expected depth the
+    golden surface. Same fp32 expressions, different evaluation order (the
+    kernel forms rays and differences per pixel): max-abs 1e-4 on unit normals,
+    the zero border exact."""
+    import pathlib
+
+    import numpy as np
+
+    from nest_b200 import maps
+
+    gold = np.load(pathlib.Path(__file__).resolve().parent / "golden" / "reference_utils.npz")
+    W, H, fovx, fovy = gold[f"pu{i}_meta"][:4]
+    W, H = int(W), int(H)
+    cam = camera.make_camera(gold[f"pu{i}_R"], gold[f"pu{i}_t"], W, H, float(fovx), float(fovy))
+    allmap = torch.zeros(14, H, W)
+    allmap[0] = torch.tensor(gold[f"pu{i}_depth"][0])
+    allmap[1] = 1.0
+    allmap[5] = allmap[0]
+    got = maps.render_maps(allmap.cuda(), cam, 0.0)["surf_normal"].permute(1, 2, 0).cpu().numpy()
+    ref = gold[f"pu{i}_normal"]
+    assert np.array_equal(got[0], ref[0]) and np.array_equal(got[-1], ref[-1])
+    assert np.array_equal(got[:, 0], ref[:, 0]) and np.array_equal(got[:, -1], ref[:, -1])
+    err = float(np.abs(got - ref).max())
+    assert err < 1e-4, err
