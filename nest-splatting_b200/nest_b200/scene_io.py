@@ -168,6 +168,39 @@ def save_surfel_ply(path, s: SurfelPLY) -> None:
 INIT_APPEARANCE_LEVEL = 6.0  # load_ply's init_level (gaussian_model.py:664-666)
 
 
+def from_model_tensors(xyz, features_dc, features_rest, opacity, scaling, rotation,
+                       gaussian_features=None, shape=None) -> SurfelPLY:
+    """A SurfelPLY from GaussianModel's parameter tensors as save_ply
+    (gaussian_model.py:557-584) flattens them: features_dc [N, 1, 3] and
+    features_rest [N, (d+1)^2 - 1, 3] transposed to channel-major rows, empty
+    gaussian_features / shape left out."""
+    a = lambda t: (t.detach().cpu().numpy() if torch.is_tensor(t) else np.asarray(t)).astype(np.float32)  # noqa: E731
+    n = a(xyz).shape[0]
+    dc = a(features_dc).transpose(0, 2, 1).reshape(n, -1)
+    rest = a(features_rest).transpose(0, 2, 1).reshape(n, -1)
+    gf = a(gaussian_features) if gaussian_features is not None and np.size(a(gaussian_features)) else None
+    sh = a(shape).reshape(n, 1) if shape is not None and np.size(a(shape)) else None
+    return SurfelPLY(a(xyz), dc, rest, a(opacity).reshape(n, 1), a(scaling), a(rotation), gf, sh)
+
+
+def model_tensors(s: SurfelPLY, device="cpu") -> dict:
+    """GaussianModel's parameter tensors as load_ply (gaussian_model.py:601-666)
+    rebuilds them: features_dc [N, 1, 3], features_rest [N, (d+1)^2 - 1, 3] from
+    the channel-major rows, appearance_level at its initial value, and
+    gaussian_features / shape when the file has them."""
+    t = lambda x: torch.as_tensor(np.ascontiguousarray(x), dtype=torch.float32, device=device)  # noqa: E731
+    n = s.P
+    out = {"xyz": t(s.xyz), "features_dc": t(s.f_dc.reshape(n, 3, 1)).transpose(1, 2).contiguous(),
+           "features_rest": t(s.f_rest.reshape(n, 3, -1)).transpose(1, 2).contiguous(),
+           "opacity": t(s.opacity), "scaling": t(s.scale), "rotation": t(s.rotation),
+           "appearance_level": torch.full((n, 1), INIT_APPEARANCE_LEVEL, device=device)}
+    if s.gf is not None:
+        out["gaussian_features"] = t(s.gf)
+    if s.shape is not None:
+        out["shape"] = t(s.shape)
+    return out
+
+
 def rasterizer_inputs(s: SurfelPLY, device="cuda", ap_level: float = INIT_APPEARANCE_LEVEL,
                       base_opacity: float = 0.0) -> dict:
     """Activated tensors for the rasterizer (gaussian_model.py:231-281): exp

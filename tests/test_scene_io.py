@@ -94,3 +94,51 @@ def test_ngp_checkpoint_layout(tmp_path):
     assert torch.equal(mats[2], w[2][:3].half().float())
     with pytest.raises(ValueError):
         scene_io.ngp_mlp_weights(ck["mlp_params"][:-1])
+
+
+REF_PLY = np.load(__import__("pathlib").Path(__file__).resolve().parent / "golden" / "reference_ply.npz")
+
+
+@pytest.mark.parametrize("case", [0, 1, 2])
+def test_ply_writer_matches_reference_save_ply(tmp_path, case):
+    """The reference's save_ply (run unmodified by tests/golden/make_ply_golden.py)
+    on the same parameter tensors: same property names in the same order and
+    the same float32 records, bit for bit."""
+    g = lambda k: REF_PLY[f"case{case}_saved{k}"]  # noqa: E731
+    _, _, gf, shape = REF_PLY[f"case{case}_meta"]
+    s = scene_io.from_model_tensors(g("_xyz"), g("_features_dc"), g("_features_rest"), g("_opacity"),
+                                    g("_scaling"), g("_rotation"), g("_gaussian_features") if gf else None,
+                                    g("_shape") if shape else None)
+    path = tmp_path / "point_cloud.ply"
+    scene_io.save_surfel_ply(path, s)
+    head, body = path.read_bytes().split(b"end_header\n", 1)
+    props = [line.split()[2] for line in head.decode().splitlines() if line.startswith("property")]
+    assert props == [str(n) for n in REF_PLY[f"case{case}_names"]]
+    rec = np.frombuffer(body, "<f4").reshape(REF_PLY[f"case{case}_records"].shape)
+    assert np.array_equal(rec, REF_PLY[f"case{case}_records"])
+
+
+@pytest.mark.parametrize("case", [0, 1, 2])
+def test_ply_reader_matches_reference_load_ply(tmp_path, case):
+    """The reference's load_ply on the records its save_ply wrote: the same
+    parameter tensors from load_surfel_ply + model_tensors, bit for bit."""
+    names = [str(n) for n in REF_PLY[f"case{case}_names"]]
+    recs = REF_PLY[f"case{case}_records"]
+    head = (f"ply\nformat binary_little_endian 1.0\nelement vertex {recs.shape[0]}\n"
+            + "".join(f"property float {n}\n" for n in names) + "end_header\n")
+    path = tmp_path / "point_cloud.ply"
+    path.write_bytes(head.encode() + recs.astype("<f4").tobytes())
+    deg = int(REF_PLY[f"case{case}_meta"][1])
+    m = scene_io.model_tensors(scene_io.load_surfel_ply(path, max_sh_degree=deg))
+    ref = {"xyz": "_xyz", "features_dc": "_features_dc", "features_rest": "_features_rest",
+           "opacity": "_opacity", "scaling": "_scaling", "rotation": "_rotation", "appearance_level": "_ap_level"}
+    _, _, gf, shape = REF_PLY[f"case{case}_meta"]
+    if gf:
+        ref["gaussian_features"] = "_gaussian_features"
+    if shape:
+        ref["shape"] = "_shape"
+    assert set(m) == set(ref)
+    for k, rk in ref.items():
+        want = REF_PLY[f"case{case}_loaded{rk}"]
+        assert m[k].shape == want.shape, k
+        assert np.array_equal(m[k].numpy(), want), k
