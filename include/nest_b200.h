@@ -108,13 +108,22 @@ typedef struct ns_raster_settings {
    * whose summation order varies, as in the reference. */
   int32_t deterministic;
   /* Render mode (forward.cu:964-1824; base | inference flag << 8): 0 baseline
-   * hash grid; 4 cat: per-surfel features (hybrid_levels levels) then the hash
-   * grid's `levels` levels; 12 adaptive_cat, 13 adaptive_cat_fast and 14
-   * adaptive_zero: per-surfel features blended with the hash levels by a
-   * per-surfel weight (flag 256: inference rules). hybrid_levels / total_levels:
-   * the reference's level encoding (total << 16 | active << 8 | hybrid) split
-   * out; `levels` is the number of hash levels queried. ns_rasterize_backward
-   * takes 0, 4, 12 and 14 without the inference flag (training rules; the
+   * hash grid (levels 0: per-surfel colours); 4 cat: per-surfel features
+   * (hybrid_levels levels) then the hash grid's `levels` levels; 6 adaptive
+   * and 7 adaptive_add: per-surfel rows blended with the hash levels; 12
+   * adaptive_cat, 13 adaptive_cat_fast and 14 adaptive_zero: per-surfel
+   * features blended with the hash levels by a per-surfel weight (flag 256:
+   * inference rules). hybrid_levels / total_levels: the reference's level
+   * encoding (total << 16 | active << 8 | hybrid) split out; `levels` is the
+   * number of hash levels queried. 8 hybrid_SH, 9 hybrid_SH_post, 10
+   * hybrid_SH_raw (:1378-1526): one hash level of level_dim 3, channels 3 (48
+   * for mode 9), the level word decompose << 24 | SH degree << 16 | 1 << 8 split
+   * as hybrid_levels = decompose flag (0 both parts, 1 the surfel only, 2 the
+   * grid only), total_levels = SH degree, levels = 1. 11 residual_hybrid
+   * (:1527-1592): the hash levels from channel 0 (channels + 3 <= 32) and the
+   * rows' degree-3 SH colour in out_others channels 14-16. The dual-grid modes
+   * 1-3 and 5 report NS_ERR_UNSUPPORTED. ns_rasterize_backward takes every
+   * built mode but 13 without the inference flag (training rules; the
    * reference has no mode-13 backward); ns_render_frame takes 0. */
   int32_t render_mode;
   uint32_t hybrid_levels;
@@ -134,10 +143,14 @@ typedef struct ns_surfels {
   const int32_t* offsets; /* [L+1] int32 level offsets (rows) */
   const float* gridrange; /* [2] = (vmin, vmax) */
   const float* shapes;    /* [P] per-surfel kernel parameter for kernel_type 1-3, else NULL */
-  const float* colors_precomp; /* render_mode 4 / 12 / 14: per-surfel feature rows (the
-                                  reference's colors_precomp): mode 4 [P, hybrid LD],
-                                  12 [P, total LD + 1], 14 [P, hybrid LD + 1] (blend
-                                  weight last); else NULL */
+  const float* colors_precomp; /* render modes other than 0, and level 0: per-surfel
+                                  rows (the reference's colors_precomp): mode 4
+                                  [P, hybrid LD], 6 and level 0 [P, C], 7 and 12 / 13
+                                  [P, total LD + 1], 14 [P, hybrid LD + 1] (blend
+                                  weight last), 8 / 10 [P, 3] raw SH colours, 9 and
+                                  11 [P, 48] SH coefficients (mode 11 reads them
+                                  interleaved, coefficient k of channel c at 3 k + c,
+                                  as the reference's kernel does); else NULL */
 } ns_surfels;
 
 /* Outputs (caller-owned, device). cover_pixels / trans_avg may be NULL when
@@ -145,7 +158,10 @@ typedef struct ns_surfels {
 typedef struct ns_raster_outputs {
   float* out_color;   /* [C,H,W] composited features */
   float* out_others;  /* [14,H,W] depth, alpha, normal(3), median depth, distortion,
-                         count, position(3), level colour(3) */
+                         count, position(3), level colour(3); [17,H,W] in render
+                         mode 11, whose SH colour fills channels 14-16 (the
+                         reference writes them past its 14-channel buffer,
+                         rasterize_points.cu:159-163, forward.cu:2039-2045) */
   int32_t* radii;     /* [P] */
   float* cover_pixels;/* [P] or NULL */
   float* trans_avg;   /* [P] or NULL */
@@ -167,8 +183,8 @@ size_t ns_binning_scratch_bytes(int64_t max_instances);
                                   Overflow is reported as NS_ERR_DEVICE by
                                   ns_read_device_status. */
 
-/* Forward rasterization: render_mode 0 (baseline hash grid) or 4 / 12 / 13 / 14
- * (settings->render_mode), splat kernel settings->kernel_type.
+/* Forward rasterization: render_mode 0 (baseline hash grid; levels 0: per-surfel
+ * colours) or 4 / 6-14 (settings->render_mode), splat kernel settings->kernel_type.
  * geom/image/binning are scratch buffers of at least the ns_*_scratch_bytes size.
  * num_rendered (host, may be NULL): number of surfel/tile instances. Without
  * NS_FLAG_DEVICE_COUNT the call synchronises the stream once to read it and
@@ -181,8 +197,9 @@ int ns_rasterize_forward(const ns_raster_settings* settings, const ns_surfels* s
 /* Gradients arriving at the forward outputs. */
 typedef struct ns_raster_grads_in {
   const float* dL_dout_color;   /* [channels, H, W] */
-  const float* dL_dout_others;  /* [14, H, W]; channels 0-6 carry gradient (depth,
-                                   alpha, normal x3, median depth, distortion) */
+  const float* dL_dout_others;  /* [14, H, W] (or mode 11's 17); channels 0-6 carry
+                                   gradient (depth, alpha, normal x3, median depth,
+                                   distortion) */
   const int32_t* radii;         /* [P] as written by the forward call */
 } ns_raster_grads_in;
 
@@ -202,9 +219,12 @@ typedef struct ns_raster_grads_out {
                            reference's dL_gradsum, returned in ap_level's slot) */
   float* dL_dshapes;    /* [P] or NULL: gradient of the splat kernel's shape
                            (kernel_type 1-3, backward.cu:1864-1909) */
-  float* dL_dcolors_precomp; /* render_mode 4 / 12 / 14: gradient of the per-surfel
-                           rows (ns_surfels.colors_precomp layout, blend weight
-                           included; backward.cu:987-1033, 1425-1606), else NULL */
+  float* dL_dcolors_precomp; /* render modes other than 0, and level 0: gradient of
+                           the per-surfel rows (ns_surfels.colors_precomp layout,
+                           blend weight included; backward.cu:987-1033,
+                           1108-1606; modes 8-10 with alpha T applied twice as the
+                           reference's cases 8-10 compute it; zero in mode 11,
+                           whose SH colour has no gradient), else NULL */
 } ns_raster_grads_out;
 
 /* Scratch of the backward pass: per-surfel gradient accumulators. */
@@ -213,7 +233,8 @@ size_t ns_backward_scratch_bytes(int32_t P);
  * accumulators, the fixed-point table gradient and its scale. */
 size_t ns_backward_scratch_bytes_deterministic(int32_t P, int64_t table_rows, int32_t level_dim);
 
-/* Backward rasterization (render_mode 0, 4, 12, 14; kernel_type 0-3). settings,
+/* Backward rasterization (every built render_mode but 13 and the inference
+ * flag; kernel_type 0-3). settings,
  * surfels, geom, binning and image must be those of the forward call whose outputs the gradients refer to
  * (the scratch buffers unchanged since). homotrans, when given to the forward,
  * is treated as build_H(rotations, scales, means3D): its gradient is folded into

@@ -118,11 +118,11 @@ __device__ __forceinline__ float mode_hash_factor(const BackwardParams& p, uint3
   const int base = p.render_mode & 0xFF;
   const int pg = 2 * p.hybrid_levels;
   query = p.L > 0;
-  if (base == 0) {  // level 0: no hash query
+  if (base == 0 || (base >= 8 && base <= 10)) {  // level 0; modes 8-10 query in phase C
     query = false;
     return 0.0f;
   }
-  if (base == 4) return 1.0f;
+  if (base == 4 || base == 11) return 1.0f;
   if (base == 6) return 0.5f;
   if (base == 7) return 1.0f - __ldg(p.gauss + (size_t)id * (2 * p.total_levels + 1) + 2 * p.total_levels);
   if (base == 12) return 1.0f - __ldg(p.gauss + (size_t)id * (2 * p.total_levels + 1) + 2 * p.total_levels);
@@ -141,6 +141,8 @@ __device__ __forceinline__ float mode_hash_factor(const BackwardParams& p, uint3
 __device__ __forceinline__ float mode_backward(const BackwardParams& p, uint32_t id, float aT, float hdot,
                                                const float* g, int t) {
   const int base = p.render_mode & 0xFF;
+  // mode 11 (backward.cu:1372-1424): the hash levels only; its SH rows get no gradient
+  if (base == 11) return hdot;
   const int pg = 2 * p.hybrid_levels, hd = 2 * (int)p.L, td = 2 * p.total_levels;
   auto gc = [&](int c) {
     const float2 v = *acc_pair(const_cast<float*>(g), t, c >> 1);
@@ -208,12 +210,113 @@ __device__ __forceinline__ float mode_backward(const BackwardParams& p, uint32_t
   return query ? f + wgt * hdot : f;
 }
 
-// kAnyKernel: built with the splat kernels 1-3 (p.kernel_type) and the render
-// modes 4 / 12 / 14 (p.render_mode); the Gaussian mode-0 instantiation keeps
-// them out of the hot loop. kFixed: the table gradient goes to
-// p.dL_dtable_fixed in fixed point (deterministic mode).
-template <typename TableT, bool kAnyKernel, bool kFixed>
+// Render modes 8 / 9 / 10 in the backward (backward.cu:1191-1371), one sample:
+// the single 3-wide hash level is looked up here, at the hit point `in`
+// (phase B skips these modes). Adds the row gradients to dL_dcolors and the
+// table gradient, writes dL/d(hit) in grid units (as phase B's d0..d2) to d,
+// and returns feat . dL/dcolor for the colour recursion (the forward's
+// features: the reference's cases leave that array unwritten). As the
+// reference computes them, the row and table gradients carry alpha T twice
+// (grad_feat = aT dL/dC, times aT again in each case).
+template <typename TableT, bool kFixed>
+__device__ __forceinline__ float sh_hybrid_backward(const BackwardParams& p, const LevelConst& lv0, uint32_t id,
+                                                    float aT, float in0, float in1, float in2, bool q,
+                                                    float half_shift, const float* g_sm, int t, uint32_t pid,
+                                                    float fscale, float (&d)[3]) {
+  const int base = p.render_mode & 0xFF, dec = p.hybrid_levels;
+  const size_t HW = (size_t)p.H * p.W;
+  auto gv = [&](int c) {
+    if (c < kAccStride) {
+      const float2 v = *acc_pair(const_cast<float*>(g_sm), t, c >> 1);
+      return (c & 1) ? v.y : v.x;
+    }
+    return p.dL_dcolor[(size_t)c * HW + pid];
+  };
+  float h[3] = {0.f, 0.f, 0.f}, f[3] = {0.f, 0.f, 0.f}, dv[3] = {1.f, 1.f, 1.f}, cv[8][3];
+  uint32_t idx[8];
+  if (q) lookup_rows3<TableT>(lv0, p.table, in0, in1, in2, half_shift, p.interp, f, dv, idx, cv, h);
+  const size_t width = base == 9 ? 48 : 3;
+  const float* row = p.gauss + (size_t)id * width;
+  float* drow = p.dL_dcolors + (size_t)id * width;
+  float hg[3] = {0.f, 0.f, 0.f}, fdot = 0.f;
+  if (base == 9) {
+    for (int c = 0; c < 48; c++) {
+      const float gc = gv(c);
+      float v = __ldg(row + c);
+      if ((c & 15) == 0) {
+        const float hc = h[c >> 4];
+        v = dec == 2 ? hc : (dec != 1 ? v + hc : v);
+        hg[c >> 4] = aT * (aT * gc);
+      }
+      fdot += v * gc;
+      if (dec != 2) atomicAdd(drow + c, aT * (aT * gc));
+    }
+  } else {
+#pragma unroll
+    for (int c = 0; c < 3; c++) {
+      const float gc = gv(c), rv = __ldg(row + c);
+      if (base == 8) {
+        const float gr = fmaxf(0.0f, fminf(1.0f, rv + 0.5f));
+        const float hr = 1.0f / (1.0f + expf(-h[c]));
+        const float sum = gr + hr;
+        fdot += (dec == 2 ? hr : dec == 1 ? gr : fmaxf(0.0f, fminf(1.0f, sum))) * gc;
+        const float gpc = (sum >= 0.0f && sum <= 1.0f) ? aT * gc : 0.0f;
+        const float va = rv + 0.5f;
+        if (dec != 2) atomicAdd(drow + c, aT * ((va >= 0.0f && va <= 1.0f) ? gpc : 0.0f));
+        hg[c] = aT * gpc * hr * (1.0f - hr);
+      } else {
+        const float comb = dec == 2 ? h[c] : dec == 1 ? rv : rv + h[c];
+        const float sg = 1.0f / (1.0f + expf(-comb));
+        fdot += sg * gc;
+        const float gcomb = aT * gc * sg * (1.0f - sg);
+        if (dec != 2) atomicAdd(drow + c, aT * gcomb);
+        hg[c] = aT * gcomb;
+      }
+    }
+  }
+  d[0] = d[1] = d[2] = 0.0f;
+  if (!q) return fdot;
+  const float wx[2] = {1 - f[0], f[0]}, wy[2] = {1 - f[1], f[1]}, wz[2] = {1 - f[2], f[2]};
+  // table gradient (hashgrid.h:184-190), one row of three per corner
+#pragma unroll
+  for (int c = 0; c < 8; c++) {
+    const float w = (wx[c & 1] * wy[(c >> 1) & 1]) * wz[c >> 2];
+    const size_t e = 3 * ((size_t)lv0.row0 + idx[c]);
+#pragma unroll
+    for (int ch = 0; ch < 3; ch++) {
+      if (kFixed) atomicAdd(p.dL_dtable_fixed + e + ch, (unsigned long long)llrintf(w * hg[ch] * fscale));
+      else atomicAdd(p.dL_dtable + e + ch, w * hg[ch]);
+    }
+  }
+  // dL/d(hit): the 4 edges along each axis weighted by the other two axes'
+  // corner weights (hashgrid.h:231-297), dotted with the hash gradient
+  float ex = 0.f, ey = 0.f, ez = 0.f;
+#pragma unroll
+  for (int e = 0; e < 4; e++) {
+    const int b0 = e & 1, b1 = e >> 1;
+#pragma unroll
+    for (int ch = 0; ch < 3; ch++) {
+      ex += (wy[b0] * wz[b1]) * (hg[ch] * (cv[1 + 2 * b0 + 4 * b1][ch] - cv[2 * b0 + 4 * b1][ch]));
+      ey += (wx[b0] * wz[b1]) * (hg[ch] * (cv[b0 + 2 + 4 * b1][ch] - cv[b0 + 4 * b1][ch]));
+      ez += (wx[b0] * wy[b1]) * (hg[ch] * (cv[b0 + 2 * b1 + 4][ch] - cv[b0 + 2 * b1][ch]));
+    }
+  }
+  d[0] = ex * lv0.scale * dv[0];
+  d[1] = ey * lv0.scale * dv[1];
+  d[2] = ez * lv0.scale * dv[2];
+  return fdot;
+}
+
+// kVariant 0: the Gaussian splat kernel in mode 0 (the hot loop free of the
+// rest); 1: the splat kernels 1-3 (p.kernel_type), the render modes 4, 6, 7,
+// 12, 14 and level 0 (p.render_mode); 2: also the spherical-harmonic hybrids,
+// modes 8-11, whose per-sample lookup would otherwise take registers from
+// variant 1's loop. kFixed: the table gradient goes to p.dL_dtable_fixed in
+// fixed point (deterministic mode).
+template <typename TableT, int kVariant, bool kFixed>
 __global__ void __launch_bounds__(kThreads, 2) blend_backward_kernel(const BackwardParams p) {
+  constexpr bool kAnyKernel = kVariant != 0;
+  constexpr bool kSH = kVariant == 2;
   extern __shared__ __align__(16) unsigned char smem_raw[];
   BwSmem& S = *reinterpret_cast<BwSmem*>(smem_raw);
 
@@ -280,6 +383,8 @@ __global__ void __launch_bounds__(kThreads, 2) blend_backward_kernel(const Backw
     gabs += fabsf(v.x) + fabsf(v.y);
     *acc_pair(S.g, t, l) = v;
   }
+  if (inside)  // mode 9's channels past the shared copy
+    for (int c = kAccStride; c < p.C; c++) gabs += fabsf(p.dL_dcolor[(size_t)c * HW + pid]);
   {
     float* px = &S.pix[0][t];
     px[kPxD * kThreads] = final_D;
@@ -596,7 +701,7 @@ __global__ void __launch_bounds__(kThreads, 2) blend_backward_kernel(const Backw
       for (int k = 0; k < cnt; k++) {
         const int jj = S.jj[k][t];
         const float Ti = S.Ts[k][t];
-        const float4 res = S.samp[k][t];
+        float4 res = S.samp[k][t];
         const float4 q0 = S.rec[jj][1], q1 = S.rec[jj][2], q2 = S.rec[jj][3];
         const float4 q3 = S.rec[jj][4], q4 = S.rec[jj][5], q5 = S.rec[jj][6], q6 = S.rec[jj][7];
         const float3 Tu = f3(q0.x, q0.y, q0.z), Tv = f3(q0.w, q1.x, q1.y), Tw = f3(q1.z, q1.w, q2.x);
@@ -639,12 +744,54 @@ __global__ void __launch_bounds__(kThreads, 2) blend_backward_kernel(const Backw
         const float opa = q2.w;
         const float alpha = fminf(0.99f, opa * G);
         const float aT = alpha * Ti;
+        float3 xyz;
+        if (on_plane) {
+          xyz = f3(sx * q4.x + sy * q4.w + q5.z, sx * q4.y + sy * q5.x + q5.w,
+                   sx * q4.z + sy * q5.y + q6.x);
+        } else {
+          xyz = f3(q5.z, q5.w, q6.x);
+        }
 
         // Colour term (:1786-1797) with the scalar recursion.
         acc_f = last_alpha * last_f + (1.f - last_alpha) * acc_f;
-        const float fsc = (kAnyKernel && uses_surfel_rows(p.render_mode, p.L))
-                              ? mode_backward(p, S.ids[jj], aT, res.x, S.g, t)
-                                                             : res.x;
+        float fsc;
+        const int mbase = p.render_mode & 0xFF;
+        if (kSH && mbase >= 8 && mbase <= 10) {
+          // modes 8-10: the one 3-wide level is looked up here (query_feature's
+          // mapping of the hit point, hashgrid.h:63-114, without contraction
+          // for these modes' tables as for the others)
+          float i0, i1, i2;
+          bool oob = false;
+          if (!p.contract) {
+            const float inv = 1.0f / (vmax - vmin);
+            i0 = (xyz.x - vmin) * inv;
+            i1 = (xyz.y - vmin) * inv;
+            i2 = (xyz.z - vmin) * inv;
+            oob = i0 < 0 || i0 > 1 || i1 < 0 || i1 > 1 || i2 < 0 || i2 > 1;
+          } else {
+            const float vmid = (vmax + vmin) * 0.5f;
+            const float inv = 1.0f / ((vmax - vmin) * 0.5f);
+            i0 = (xyz.x - vmid) * inv;
+            i1 = (xyz.y - vmid) * inv;
+            i2 = (xyz.z - vmid) * inv;
+            const float nrm = sqrtf(i0 * i0 + i1 * i1 + i2 * i2);
+            const float inv_n = 1.0f / nrm;
+            const float st = (nrm <= 1.0f) ? 1.0f : (2.0f - inv_n) * inv_n;
+            i0 = (st * i0 + 2.0f) * 0.25f;
+            i1 = (st * i1 + 2.0f) * 0.25f;
+            i2 = (st * i2 + 2.0f) * 0.25f;
+          }
+          const bool q = p.L > 0 && p.hybrid_levels != 1 && !oob && __float_as_uint(q3.w) >= 1u;
+          float dh[3];
+          fsc = sh_hybrid_backward<TableT, kFixed>(p, S.lv[0], S.ids[jj], aT, i0, i1, i2, q, half_shift, S.g, t,
+                                                   pid, fscale, dh);
+          res.y = dh[0];
+          res.z = dh[1];
+          res.w = dh[2];
+        } else {
+          fsc = (kAnyKernel && uses_surfel_rows(p.render_mode, p.L)) ? mode_backward(p, S.ids[jj], aT, res.x, S.g, t)
+                                                                     : res.x;
+        }
         last_f = fsc;
         float dL_dalpha = fsc - acc_f;
 
@@ -695,13 +842,6 @@ __global__ void __launch_bounds__(kThreads, 2) blend_backward_kernel(const Backw
         dL_dz += aT * dL_ddepth;
 
         // dL/dxyz from the hit-point gradient (query_feature's grad_scale).
-        float3 xyz;
-        if (on_plane) {
-          xyz = f3(sx * q4.x + sy * q4.w + q5.z, sx * q4.y + sy * q5.x + q5.w,
-                   sx * q4.z + sy * q5.y + q6.x);
-        } else {
-          xyz = f3(q5.z, q5.w, q6.x);
-        }
         float gscale;
         if (!p.contract) {
           gscale = 1.0f / (vmax - vmin);
@@ -987,20 +1127,20 @@ __global__ void __launch_bounds__(256) table_fixed_finish_kernel(const unsigned 
     out[i] = scale != 0.0f ? (float)((double)(long long)fx[i] / (double)scale) : __int_as_float(0x7fc00000);
 }
 
-template <typename TableT, bool kAnyKernel, bool kFixed>
+template <typename TableT, int kVariant, bool kFixed>
 int launch_backward3(const BackwardParams& p, int tiles, cudaStream_t stream) {
   const int smem = (int)sizeof(BwSmem);
-  NS_CUDA_TRY(cudaFuncSetAttribute(blend_backward_kernel<TableT, kAnyKernel, kFixed>,
+  NS_CUDA_TRY(cudaFuncSetAttribute(blend_backward_kernel<TableT, kVariant, kFixed>,
                                    cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-  blend_backward_kernel<TableT, kAnyKernel, kFixed><<<tiles, kThreads, smem, stream>>>(p);
+  blend_backward_kernel<TableT, kVariant, kFixed><<<tiles, kThreads, smem, stream>>>(p);
   NS_LAUNCH_CHECK();
   return NS_OK;
 }
 
-template <typename TableT, bool kAnyKernel>
+template <typename TableT, int kVariant>
 int launch_backward(const BackwardParams& p, int tiles, cudaStream_t stream) {
-  return p.dL_dtable_fixed ? launch_backward3<TableT, kAnyKernel, true>(p, tiles, stream)
-                           : launch_backward3<TableT, kAnyKernel, false>(p, tiles, stream);
+  return p.dL_dtable_fixed ? launch_backward3<TableT, kVariant, true>(p, tiles, stream)
+                           : launch_backward3<TableT, kVariant, false>(p, tiles, stream);
 }
 
 }  // namespace
@@ -1027,18 +1167,24 @@ int table_grad_finish_launch(const unsigned long long* fx, size_t n, const uint3
 }
 
 int blend_backward_launch(const BackwardParams& p, int fp16, cudaStream_t stream) {
-  if (p.LD != 2 || p.C > kAccStride || p.C <= 0) return NS_ERR_UNSUPPORTED;
-  const int hoff = hash_level_offset(p.render_mode, p.hybrid_levels);
-  if (hoff < 0 || (int64_t)hoff + p.L > (uint32_t)(p.C / p.LD) || p.L > (uint32_t)kMaxLevels)
-    return NS_ERR_UNSUPPORTED;
+  const int base = p.render_mode & 0xFF;
+  if (p.C <= 0) return NS_ERR_UNSUPPORTED;
+  if (base >= 8 && base <= 10) {
+    if (p.LD != 3 || p.L > 1 || p.C != (base == 9 ? 48 : 3)) return NS_ERR_UNSUPPORTED;
+  } else {
+    if (p.LD != 2 || p.C > kAccStride) return NS_ERR_UNSUPPORTED;
+    const int hoff = hash_level_offset(p.render_mode, p.hybrid_levels);
+    if (hoff < 0 || (int64_t)hoff + p.L > (uint32_t)(p.C / p.LD) || p.L > (uint32_t)kMaxLevels)
+      return NS_ERR_UNSUPPORTED;
+  }
   if ((p.render_mode >> 8) != 0) return NS_ERR_UNSUPPORTED;  // training rules only
   const int tiles = div_up(p.W, kTile) * div_up(p.H, kTile);
   if (tiles == 0) return NS_OK;
+  if (base >= 8 && base <= 11)
+    return fp16 ? launch_backward<__half, 2>(p, tiles, stream) : launch_backward<float, 2>(p, tiles, stream);
   if (p.kernel_type != 0 || uses_surfel_rows(p.render_mode, p.L))
-    return fp16 ? launch_backward<__half, true>(p, tiles, stream)
-                : launch_backward<float, true>(p, tiles, stream);
-  return fp16 ? launch_backward<__half, false>(p, tiles, stream)
-              : launch_backward<float, false>(p, tiles, stream);
+    return fp16 ? launch_backward<__half, 1>(p, tiles, stream) : launch_backward<float, 1>(p, tiles, stream);
+  return fp16 ? launch_backward<__half, 0>(p, tiles, stream) : launch_backward<float, 0>(p, tiles, stream);
 }
 
 int preprocess_backward_launch(int P, const float* means3D, const float* scales,

@@ -189,10 +189,16 @@ int validate_settings(const ns_raster_settings* s) {
   if (s->levels * s->level_dim > s->channels) return NS_ERR_INVALID;
   if (s->kernel_type < 0 || s->kernel_type > 3) return NS_ERR_UNSUPPORTED;
   const int base = s->render_mode & 0xFF, flag = s->render_mode >> 8;
-  if (base != 0 && base != 4 && base != 6 && base != 7 && base != 12 && base != 13 && base != 14)
-    return NS_ERR_UNSUPPORTED;
+  if (base == 1 || base == 2 || base == 3 || base == 5 || base > 14) return NS_ERR_UNSUPPORTED;
   if (flag > 1 || (flag && base != 12 && base != 13 && base != 14)) return NS_ERR_UNSUPPORTED;
-  if (base != 0) {
+  if (base >= 8 && base <= 10) {
+    // one 3-wide hash level; hybrid_levels carries the decompose flag
+    if (s->level_dim != 3 || s->levels > 1 || s->hybrid_levels > 2) return NS_ERR_INVALID;
+    if (s->channels != (base == 9 ? 48u : 3u)) return NS_ERR_INVALID;
+  } else if (base == 11) {
+    // hash levels from channel 0; three more accumulators hold the SH colour
+    if (s->channels + 3 > 32) return NS_ERR_INVALID;
+  } else if (base != 0) {
     if (s->hybrid_levels > 16 || s->total_levels > 16) return NS_ERR_INVALID;
     // modes 6 and 7 have no per-surfel levels before the hash levels
     if ((base == 6 || base == 7) && s->hybrid_levels != 0) return NS_ERR_INVALID;
@@ -350,7 +356,8 @@ int ns_rasterize_forward(const ns_raster_settings* settings, const ns_surfels* s
     return NS_ERR_INVALID;
   if (settings->record_transmittance && (!outputs->cover_pixels || !outputs->trans_avg))
     return NS_ERR_INVALID;
-  if (settings->level_dim != 2) return NS_ERR_UNSUPPORTED;
+  const int fbase = settings->render_mode & 0xFF;
+  if (settings->level_dim != ((fbase >= 8 && fbase <= 10) ? 3u : 2u)) return NS_ERR_UNSUPPORTED;
   if (geom_bytes < ns_geometry_scratch_bytes(P)) return NS_ERR_SCRATCH;
   if (image_bytes < ns_image_scratch_bytes(settings->image_width, settings->image_height))
     return NS_ERR_SCRATCH;
@@ -428,7 +435,7 @@ int ns_rasterize_backward(const ns_raster_settings* settings, const ns_surfels* 
   cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_);
   int rc = validate_settings(settings);
   if (rc) return rc;
-  // training rules of modes 4 / 6 / 7 / 12 / 14 only (the reference has no mode-13 backward)
+  // training rules only (the reference has no mode-13 backward)
   if ((settings->render_mode >> 8) != 0 || (settings->render_mode & 0xFF) == 13) return NS_ERR_UNSUPPORTED;
   if (!surfels || !gi || !go) return NS_ERR_INVALID;
   const int P = surfels->P;
@@ -439,14 +446,16 @@ int ns_rasterize_backward(const ns_raster_settings* settings, const ns_surfels* 
   const bool rows = uses_surfel_rows(settings->render_mode, settings->levels);
   if (rows && P > 0 && (!surfels->colors_precomp || !go->dL_dcolors_precomp)) return NS_ERR_INVALID;
   // row length of colors_precomp: level 0 and mode 6 C, mode 4 hybrid LD,
-  // modes 7 / 12 total LD + 1, mode 14 hybrid LD + 1
+  // modes 7 / 12 total LD + 1, mode 14 hybrid LD + 1, modes 8 / 10 3, modes 9 / 11 48
   const size_t mode_stride = !rows                              ? 0
                              : (base_mode == 0 || base_mode == 6) ? (size_t)settings->channels
                              : base_mode == 4 ? (size_t)settings->hybrid_levels * settings->level_dim
+                             : (base_mode == 8 || base_mode == 10) ? 3
+                             : (base_mode == 9 || base_mode == 11) ? 48
                              : (base_mode == 7 || base_mode == 12)
                                  ? (size_t)settings->total_levels * settings->level_dim + 1
                                  : (size_t)settings->hybrid_levels * settings->level_dim + 1;
-  if (settings->level_dim != 2) return NS_ERR_UNSUPPORTED;
+  if (settings->level_dim != ((base_mode >= 8 && base_mode <= 10) ? 3u : 2u)) return NS_ERR_UNSUPPORTED;
   if (!go->dL_dmeans3D || !go->dL_dmean2D || !go->dL_dopacity || !go->dL_dscales ||
       !go->dL_drots || !go->dL_dtable || !go->dL_gradsum || go->table_rows < 0)
     return NS_ERR_INVALID;

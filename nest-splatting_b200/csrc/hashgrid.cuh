@@ -165,4 +165,57 @@ __device__ __forceinline__ float2 lookup_finish(const float (&f)[3], const Corne
   return r;
 }
 
+// One 3-wide level (render modes 8-10 query one level of a table with three
+// channels per row, query_feature<.., 3, 3>, hashgrid.h:53-212). Finds the cell
+// of the point `in` of [0,1]^3, loads its 8 corner rows into cv and returns the
+// trilinear value in r (corner c weighted ((wx * wy) * wz), accumulated in
+// order c = 0..7). f: the cell fractions (smoothstep applied with interp 1),
+// dv: their derivatives, idx: the corner rows relative to the level.
+template <typename TableT>
+__device__ __forceinline__ float ld_table(const TableT* t, size_t i);
+template <>
+__device__ __forceinline__ float ld_table<float>(const float* t, size_t i) {
+  return __ldg(t + i);
+}
+template <>
+__device__ __forceinline__ float ld_table<__half>(const __half* t, size_t i) {
+  return __half2float(__ldg(t + i));
+}
+
+template <typename TableT>
+__device__ __forceinline__ void lookup_rows3(const LevelConst& lc, const void* table, float in0, float in1,
+                                             float in2, float half_shift, uint32_t interp, float (&f)[3],
+                                             float (&dv)[3], uint32_t (&idx)[8], float (&cv)[8][3],
+                                             float (&r)[3]) {
+  uint32_t g[3];
+  const float pin[3] = {in0, in1, in2};
+#pragma unroll
+  for (int d = 0; d < 3; d++) {
+    const float pos = pin[d] * lc.scale + half_shift;
+    const float fl = floorf(pos);
+    g[d] = (uint32_t)fl;
+    f[d] = pos - fl;
+    if (interp == 1) {
+      dv[d] = 6 * f[d] * (1.0f - f[d]);
+      f[d] = f[d] * f[d] * (3.0f - 2.0f * f[d]);
+    } else {
+      dv[d] = 1.0f;
+    }
+  }
+  corner_rows(lc, g, idx);
+  const TableT* base = static_cast<const TableT*>(table) + 3 * (size_t)lc.row0;
+#pragma unroll
+  for (int c = 0; c < 8; c++)
+#pragma unroll
+    for (int ch = 0; ch < 3; ch++) cv[c][ch] = ld_table<TableT>(base, 3 * (size_t)idx[c] + ch);
+  const float wx[2] = {1 - f[0], f[0]}, wy[2] = {1 - f[1], f[1]}, wz[2] = {1 - f[2], f[2]};
+  r[0] = r[1] = r[2] = 0.0f;
+#pragma unroll
+  for (int c = 0; c < 8; c++) {
+    const float w = (wx[c & 1] * wy[(c >> 1) & 1]) * wz[c >> 2];
+#pragma unroll
+    for (int ch = 0; ch < 3; ch++) r[ch] = fmaf(w, cv[c][ch], r[ch]);
+  }
+}
+
 }  // namespace ns

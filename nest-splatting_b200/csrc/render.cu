@@ -149,11 +149,109 @@ __device__ __forceinline__ float mode_features(const RenderParams& p, uint32_t i
   return (p.L > 0 && (infer ? wgt >= 0.1f : wgt > 1e-6f)) ? wgt : 0.0f;
 }
 
-// kGeneral: built with the splat kernels 1-3 (p.kernel_type) and the render
-// modes 4 / 12 / 14 (p.render_mode); the Gaussian mode-0 instantiation keeps the
-// hot loop free of them.
-template <typename TableT, bool kGeneral>
+// Render modes 8 (hybrid_SH), 9 (hybrid_SH_post) and 10 (hybrid_SH_raw),
+// forward.cu:1378-1526: the sample's feature from the surfel's row (3 raw SH
+// colours; 48 SH coefficients for 9) and one 3-wide hash level queried here,
+// at the hit point (no phase-B lookup). p.hybrid_levels holds the level
+// word's decompose flag (0 both parts, 1 the surfel only, 2 the grid only).
+// Mode 9's channels from kMaxChannels on are accumulated in out_color itself
+// (the pixel's own words, zeroed at the kernel's start).
+template <typename TableT>
+__device__ __forceinline__ void sh_hybrid_features(const RenderParams& p, const LevelConst& lv0, uint32_t id,
+                                                   float w, float in0, float in1, float in2, bool oob,
+                                                   uint32_t apl, float half_shift, float* acc, int t,
+                                                   uint32_t pid) {
+  const int base = p.render_mode & 0xFF, dec = p.hybrid_levels;
+  float h[3] = {0.f, 0.f, 0.f};
+  if (p.L > 0 && dec != 1 && !oob && apl >= 1) {
+    float f[3], dv[3], cv[8][3];
+    uint32_t idx[8];
+    lookup_rows3<TableT>(lv0, p.table, in0, in1, in2, half_shift, p.interp, f, dv, idx, cv, h);
+  }
+  auto add = [&](int c, float v) {
+    if (c < kMaxChannels) {
+      float2* a = acc_pair(acc, t, c >> 1);
+      if (c & 1) a->y += v * w;
+      else a->x += v * w;
+    } else {
+      p.out_color[(size_t)c * p.H * p.W + pid] += v * w;
+    }
+  };
+  if (base == 9) {
+    const float* g = p.gauss + (size_t)id * 48;
+    for (int c = 0; c < 48; c++) {
+      float v = __ldg(g + c);
+      if ((c & 15) == 0) {
+        const float hc = h[c >> 4];
+        v = dec == 2 ? hc : (dec != 1 ? v + hc : v);
+      }
+      add(c, v);
+    }
+    return;
+  }
+  const float* g = p.gauss + (size_t)id * 3;
+#pragma unroll
+  for (int c = 0; c < 3; c++) {
+    const float gv = __ldg(g + c);
+    float v;
+    if (base == 8) {
+      const float gr = fmaxf(0.0f, fminf(1.0f, gv + 0.5f));
+      const float hr = 1.0f / (1.0f + expf(-h[c]));
+      v = dec == 2 ? hr : dec == 1 ? gr : fmaxf(0.0f, fminf(1.0f, gr + hr));
+    } else {
+      const float comb = dec == 2 ? h[c] : dec == 1 ? gv : gv + h[c];
+      v = 1.0f / (1.0f + expf(-comb));
+    }
+    add(c, v);
+  }
+}
+
+// Render mode 11 (residual_hybrid), forward.cu:1918-1943: the surfel's degree-3
+// spherical-harmonic colour along the unit direction from its centre to the
+// hit point, its 48 coefficients read interleaved (coefficient k of channel c
+// at 3 k + c), 0.5 added to the DC term, clamped at 0 (eval_sh_inline,
+// :76-155), weighted by w into the three accumulators after the C hash
+// channels. The basis constants are the standard real SH normalisations.
+__device__ __forceinline__ void residual_sh(const RenderParams& p, uint32_t id, float3 xyz, float3 pk, float w,
+                                            float* acc, int t) {
+  constexpr float C0 = 0.28209479177387814f, C1 = 0.4886025119029199f;
+  constexpr float C2a = 1.0925484305920792f, C2b = -1.0925484305920792f, C2c = 0.31539156525252005f,
+                  C2d = -1.0925484305920792f, C2e = 0.5462742152960396f;
+  constexpr float C3a = -0.5900435899266435f, C3b = 2.890611442640554f, C3c = -0.4570457994644658f,
+                  C3d = 0.3731763325901154f, C3e = -0.4570457994644658f, C3f = 1.445305721320277f,
+                  C3g = -0.5900435899266435f;
+  float dx = xyz.x - pk.x, dy = xyz.y - pk.y, dz = xyz.z - pk.z;
+  const float inv = rsqrtf(dx * dx + dy * dy + dz * dz);
+  const float x = dx * inv, y = dy * inv, z = dz * inv;
+  const float xx = x * x, yy = y * y, zz = z * z, xy = x * y, yz = y * z, xz = x * z;
+  const float* sh = p.gauss + (size_t)id * 48;
+#pragma unroll
+  for (int c = 0; c < 3; c++) {
+    auto k = [&](int i) { return __ldg(sh + 3 * i + c); };
+    float r = C0 * k(0) + 0.5f;
+    r = r - C1 * y * k(1) + C1 * z * k(2) - C1 * x * k(3);
+    r = r + C2a * xy * k(4) + C2b * yz * k(5) + C2c * (2.0f * zz - xx - yy) * k(6) + C2d * xz * k(7) +
+        C2e * (xx - yy) * k(8);
+    r = r + C3a * y * (3.0f * xx - yy) * k(9) + C3b * xy * z * k(10) + C3c * y * (4.0f * zz - xx - yy) * k(11) +
+        C3d * z * (2.0f * zz - 3.0f * xx - 3.0f * yy) * k(12) + C3e * x * (4.0f * zz - xx - yy) * k(13) +
+        C3f * z * (xx - yy) * k(14) + C3g * x * (xx - 3.0f * yy) * k(15);
+    r = fmaxf(r, 0.0f);
+    const int ch = p.C + c;
+    float2* a = acc_pair(acc, t, ch >> 1);
+    if (ch & 1) a->y += w * r;
+    else a->x += w * r;
+  }
+}
+
+// kVariant 0: the Gaussian splat kernel in mode 0 (the hot loop free of the
+// rest); 1: the splat kernels 1-3 (p.kernel_type), the render modes 4, 6, 7,
+// 12-14 and level 0 (p.render_mode); 2: also the spherical-harmonic hybrids,
+// modes 8-11, whose per-sample lookup and SH evaluation would otherwise take
+// registers from variant 1's loop.
+template <typename TableT, int kVariant>
 __global__ void __launch_bounds__(kThreads, 2) blend_kernel(const RenderParams p) {
+  constexpr bool kGeneral = kVariant != 0;
+  constexpr bool kSH = kVariant == 2;
   extern __shared__ __align__(16) unsigned char smem_raw[];
   BlendSmem& S = *reinterpret_cast<BlendSmem*>(smem_raw);
 
@@ -171,6 +269,8 @@ __global__ void __launch_bounds__(kThreads, 2) blend_kernel(const RenderParams p
 
   if (t < (int)L) S.lv[t] = make_level<TableT>(p.table, p.offsets, p.S, p.Hres, p.align_corners, t);
   for (int c = 0; c < kAccStride; c++) S.acc[t * kAccStride + c] = 0.f;  // only this thread's row
+  if (kSH && inside)  // mode 9: channels past the shared accumulators add up in out_color
+    for (int c = kMaxChannels; c < p.C; c++) p.out_color[(size_t)c * p.H * p.W + pid] = 0.0f;
   if (t < kSlots) {
     mbar_init_shared(&S.full[t], 32);
     S.used[t] = 0;
@@ -442,10 +542,20 @@ __global__ void __launch_bounds__(kThreads, 2) blend_kernel(const RenderParams p
             in1 = (st * in1 + 2.0f) * 0.25f;
             in2 = (st * in2 + 2.0f) * 0.25f;
           }
-          float hw = w;  // weight of this sample's hash features
-          if (kGeneral && uses_surfel_rows(p.render_mode, p.L))
-            hw = w * mode_features(p, __float_as_uint(q6.z), w, S.acc, t);
-          if (!lvl0) {
+          float hw = w;  // weight of this sample's hash features (0: nothing to look up)
+          if (kGeneral && uses_surfel_rows(p.render_mode, p.L)) {
+            const int base = p.render_mode & 0xFF;
+            const uint32_t sid = __float_as_uint(q6.z);
+            if (kSH && base >= 8 && base <= 10) {
+              sh_hybrid_features<TableT>(p, S.lv[0], sid, w, in0, in1, in2, oob, apl, half_shift, S.acc, t, pid);
+              hw = 0.0f;
+            } else if (kSH && base == 11) {
+              residual_sh(p, sid, xyz, f3(q5.z, q5.w, q6.x), w, S.acc, t);
+            } else {
+              hw = w * mode_features(p, sid, w, S.acc, t);
+            }
+          }
+          if (!lvl0 && !(kGeneral && hw == 0.0f)) {
             S.samp[cnt][t] = make_float4(in0, in1, in2, hw);
             S.lvl[cnt][t] = (uint8_t)((oob || hw == 0.0f) ? 0u : min(apl, L));
             cnt++;
@@ -511,7 +621,7 @@ __global__ void __launch_bounds__(kThreads, 2) blend_kernel(const RenderParams p
     p.final_T[pid + 2 * HW] = M2;
     p.n_contrib[pid] = last_contributor;
     p.n_contrib[pid + HW] = (uint32_t)median_contributor;  // -1 saturates to 0
-    for (int c = 0; c < p.C; c++) {
+    for (int c = 0; c < min(p.C, kMaxChannels); c++) {
       const float2 pr = *acc_pair(S.acc, t, c >> 1);
       p.out_color[c * HW + pid] = (c & 1) ? pr.y : pr.x;
     }
@@ -530,16 +640,24 @@ __global__ void __launch_bounds__(kThreads, 2) blend_kernel(const RenderParams p
     o[11 * HW] = vis0;
     o[12 * HW] = vis1;
     o[13 * HW] = 0.0f;
+    if (kSH && (p.render_mode & 0xFF) == 11) {
+      // mode 11's SH colour (forward.cu:2039-2045): out_others has 17 channels
+#pragma unroll
+      for (int c = 0; c < 3; c++) {
+        const float2 pr = *acc_pair(S.acc, t, (p.C + c) >> 1);
+        o[(14 + c) * HW] = ((p.C + c) & 1) ? pr.y : pr.x;
+      }
+    }
   }
 }
 
-template <typename TableT, bool kGeneral>
+template <typename TableT, int kVariant>
 int launch_blend(const RenderParams& p, int tiles, cudaStream_t stream) {
   const int smem = (int)sizeof(BlendSmem);
-  NS_CUDA_TRY(cudaFuncSetAttribute(blend_kernel<TableT, kGeneral>,
+  NS_CUDA_TRY(cudaFuncSetAttribute(blend_kernel<TableT, kVariant>,
                                    cudaFuncAttributeMaxDynamicSharedMemorySize,
                                    smem));
-  blend_kernel<TableT, kGeneral><<<tiles, kThreads, smem, stream>>>(p);
+  blend_kernel<TableT, kVariant><<<tiles, kThreads, smem, stream>>>(p);
   NS_LAUNCH_CHECK();
   return NS_OK;
 }
@@ -547,18 +665,29 @@ int launch_blend(const RenderParams& p, int tiles, cudaStream_t stream) {
 }  // namespace
 
 // Supported: level_dim 2, up to 16 levels, up to 32 channels (C >= 2 L), fp16 or
-// fp32 table. Other shapes report NS_ERR_UNSUPPORTED (the reference prints and
-// renders nothing for shapes it was not compiled for).
+// fp32 table; modes 8-10: one 3-wide level, C = 3 (48 for mode 9); mode 11: C + 3
+// <= 32 (its SH colour takes three accumulators). Other shapes report
+// NS_ERR_UNSUPPORTED (the reference prints and renders nothing for shapes it was
+// not compiled for).
 int render_launch(const RenderParams& p, int fp16, cudaStream_t stream) {
-  if (p.LD != 2 || p.C > kMaxChannels || p.C <= 0) return NS_ERR_UNSUPPORTED;
-  const int hoff = hash_level_offset(p.render_mode, p.hybrid_levels);
-  if (hoff < 0 || (int64_t)hoff + p.L > (uint32_t)(p.C / p.LD) || p.L > (uint32_t)kMaxLevels)
-    return NS_ERR_UNSUPPORTED;
+  const int base = p.render_mode & 0xFF;
+  if (p.C <= 0) return NS_ERR_UNSUPPORTED;
+  if (base >= 8 && base <= 10) {
+    if (p.LD != 3 || p.L > 1 || p.C != (base == 9 ? 48 : 3)) return NS_ERR_UNSUPPORTED;
+  } else {
+    if (p.LD != 2 || p.C > kMaxChannels) return NS_ERR_UNSUPPORTED;
+    if (base == 11 && p.C + 3 > kMaxChannels) return NS_ERR_UNSUPPORTED;
+    const int hoff = hash_level_offset(p.render_mode, p.hybrid_levels);
+    if (hoff < 0 || (int64_t)hoff + p.L > (uint32_t)(p.C / p.LD) || p.L > (uint32_t)kMaxLevels)
+      return NS_ERR_UNSUPPORTED;
+  }
   const int tiles = div_up(p.W, kTile) * div_up(p.H, kTile);
   if (tiles == 0) return NS_OK;
+  if (base >= 8 && base <= 11)
+    return fp16 ? launch_blend<__half, 2>(p, tiles, stream) : launch_blend<float, 2>(p, tiles, stream);
   if (p.kernel_type != 0 || uses_surfel_rows(p.render_mode, p.L))
-    return fp16 ? launch_blend<__half, true>(p, tiles, stream) : launch_blend<float, true>(p, tiles, stream);
-  return fp16 ? launch_blend<__half, false>(p, tiles, stream) : launch_blend<float, false>(p, tiles, stream);
+    return fp16 ? launch_blend<__half, 1>(p, tiles, stream) : launch_blend<float, 1>(p, tiles, stream);
+  return fp16 ? launch_blend<__half, 0>(p, tiles, stream) : launch_blend<float, 0>(p, tiles, stream);
 }
 
 }  // namespace ns

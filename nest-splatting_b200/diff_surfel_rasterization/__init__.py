@@ -6,16 +6,24 @@ NilKel/nest-splatting (GaussianRasterizationSettings :277-293,
 HashGridSettings :295-302, GaussianRasterizer :304-396, rasterize_gaussians
 :21-66, _RasterizeGaussians :68-275, compute_relocation :398-414). The forward
 and backward passes run the sm_100a kernels of libnest_b200.so through its
-C-ABI; there is no CPU fallback. Built: render_mode 0 (baseline hash grid),
-level_dim 2, the Gaussian splat kernel (kernel_type 0) and the beta / flex /
-general kernels (kernel_type 1-3, per-surfel `shapes`, whose gradient comes back
-in shapes' slot), forward and backward; render modes 4 (cat), 12 (adaptive_cat)
-and 14 (adaptive_zero), forward (also with the inference flag 256) and backward
-(training rules; mode 13, adaptive_cat_fast, forward only as in the reference; the per-surfel rows' gradient, blend weight included, comes
-back in colors_precomp's slot), the per-surfel features read from
-colors_precomp and the level word hashgrid_settings.L = total << 16 | active << 8
-| hybrid as the reference's renderer encodes it (gaussian_renderer/__init__.py:
-216-241, 334-447). Other modes raise NotImplementedError instead of silently
+C-ABI; there is no CPU fallback. Built: render_mode 0 (baseline hash grid,
+level_dim 2; level 0: per-surfel colours), the Gaussian splat kernel
+(kernel_type 0) and the beta / flex / general kernels (kernel_type 1-3,
+per-surfel `shapes`, whose gradient comes back in shapes' slot), forward and
+backward; render modes 4 (cat), 6 (adaptive), 7 (adaptive_add), 12
+(adaptive_cat) and 14 (adaptive_zero), forward (12-14 also with the inference
+flag 256) and backward (training rules; mode 13, adaptive_cat_fast, forward
+only as in the reference; the per-surfel rows' gradient, blend weight
+included, comes back in colors_precomp's slot), the per-surfel features read
+from colors_precomp and the level word hashgrid_settings.L = total << 16 |
+active << 8 | hybrid as the reference's renderer encodes it
+(gaussian_renderer/__init__.py:216-241, 334-447); the spherical-harmonic
+hybrids 8 (hybrid_SH), 9 (hybrid_SH_post) and 10 (hybrid_SH_raw) with a
+single 3-wide hash level and the level word decompose << 24 | SH degree << 16
+| 1 << 8, and 11 (residual_hybrid: hash features in out_color, the rows' SH
+colour in out_others channels 14-16, so out_others has 17 channels), forward
+and backward (:570-686). The dual-grid modes 1-3 and 5 of the reference's
+surface-potential renderer raise NotImplementedError instead of silently
 rendering nothing as the reference does for shapes it was not compiled for.
 
 Backward (__init__.py:174-275 of the reference): the 21 gradients come back in
@@ -80,11 +88,13 @@ class _RasterizeGaussians(torch.autograd.Function):
                 gridrange_diffuse, raster_settings, hashgrid_settings, render_mode, shapes, kernel_type):
         mode = int(render_mode)
         base_mode = mode & 0xFF
-        if base_mode not in (0, 4, 6, 7, 12, 13, 14) or (mode >> 8) > 1 or \
+        if base_mode not in (0, 4, 6, 7, 8, 9, 10, 11, 12, 13, 14) or (mode >> 8) > 1 or \
                 ((mode >> 8) and base_mode not in (12, 13, 14)):
             raise NotImplementedError(f"render_mode {render_mode}: 0 (baseline hash grid; level 0: per-surfel "
-                                      f"colours), 4 (cat), 6 (adaptive), 7 (adaptive_add), 12 (adaptive_cat), "
-                                      f"13 (adaptive_cat_fast), 14 (adaptive_zero) are built")
+                                      f"colours), 4 (cat), 6 (adaptive), 7 (adaptive_add), 8 (hybrid_SH), "
+                                      f"9 (hybrid_SH_post), 10 (hybrid_SH_raw), 11 (residual_hybrid), "
+                                      f"12 (adaptive_cat), 13 (adaptive_cat_fast), 14 (adaptive_zero) are built; "
+                                      f"the dual-grid modes 1-3 and 5 of the surface-potential renderer are not")
         if int(kernel_type) not in (0, 1, 2, 3):
             raise NotImplementedError(f"kernel_type {kernel_type}: 0-3 are built")
         shp = _nonempty(shapes)
@@ -128,6 +138,30 @@ class _RasterizeGaussians(torch.autograd.Function):
             if gauss is None:
                 raise RuntimeError("render_mode 7 needs colors_precomp (per-surfel features + weight)")
             gauss = gauss.detach().contiguous().float()
+        elif base_mode in (8, 9, 10):
+            # hybrid_SH / _post / _raw (gaussian_renderer/__init__.py:598-686): level word
+            # decompose << 24 | SH degree << 16 | hash levels (1) << 8; one 3-wide level;
+            # rows of 3 raw SH colours (48 SH coefficients for 9)
+            hybrid, total, L = (L >> 24) & 0xFF, (L >> 16) & 0xFF, (L >> 8) & 0xFF
+            gauss = _nonempty(colors_precomp)
+            if gauss is None:
+                raise RuntimeError(f"render_mode {mode} needs colors_precomp (per-surfel SH colours)")
+            gauss = gauss.detach().contiguous().float()
+            width = 48 if base_mode == 9 else 3
+            if gauss.reshape(means3D.shape[0], -1).shape[1] != width:
+                raise RuntimeError(f"render_mode {mode} needs colors_precomp rows of {width} values")
+            if _nonempty(features) is not None and features.shape[-1] != 3:
+                raise RuntimeError(f"render_mode {mode} reads a hash table of 3 values per row")
+        elif base_mode == 11:
+            # residual_hybrid (:570-596): level word total << 16 | hash levels << 8 | hybrid;
+            # rows of 48 SH coefficients; hash features from channel 0
+            total, L, hybrid = (L >> 16) & 0xFF, (L >> 8) & 0xFF, L & 0xFF
+            gauss = _nonempty(colors_precomp)
+            if gauss is None:
+                raise RuntimeError("render_mode 11 needs colors_precomp (per-surfel SH coefficients)")
+            gauss = gauss.detach().contiguous().float()
+            if gauss.reshape(means3D.shape[0], -1).shape[1] != 48:
+                raise RuntimeError("render_mode 11 needs colors_precomp rows of 48 SH coefficients")
         elif base_mode != 0:
             # The reference's level word: total << 16 | active hash levels << 8 | hybrid.
             total, active, hybrid = (L >> 16) & 0xFF, (L >> 8) & 0xFF, L & 0xFF
@@ -142,9 +176,15 @@ class _RasterizeGaussians(torch.autograd.Function):
             if gauss is None:
                 raise RuntimeError(f"render_mode {mode} needs colors_precomp (per-surfel features)")
             gauss = gauss.detach().contiguous().float()
-        _, _, OS = _shape_dims(hashgrid_settings)
+        _, HS, OS = _shape_dims(hashgrid_settings)
         if base_mode == 0 and L == 0 and OS == 0:
             OS = gauss.shape[-1]
+        if base_mode in (8, 10):
+            OS = 3
+        elif base_mode == 9:
+            OS = 48  # the 48 coefficients the kernel's case 9 writes
+        elif base_mode == 11:
+            OS = HS if OS == 0 else OS  # dual buffers: the hash features' HS channels
         feats = features.contiguous()
         if feats.dtype not in (torch.float16, torch.float32):
             feats = feats.float()

@@ -48,9 +48,15 @@ class RasterConfig:
     kernel_type: int = 0  # 0 Gaussian, 1 beta, 2 flex, 3 general
     deterministic: bool = False  # backward: fixed-point (bit-reproducible) table gradient
     render_mode: int = 0     # 0 baseline (levels 0: per-surfel colours); 4 cat, 6 adaptive, 7 adaptive_add,
+    #                          8 hybrid_SH, 9 hybrid_SH_post, 10 hybrid_SH_raw, 11 residual_hybrid,
     #                          12 adaptive_cat, 13 adaptive_cat_fast, 14 adaptive_zero (| 256 inference)
-    hybrid_levels: int = 0   # per-surfel feature levels of modes 4 / 12 / 14
+    hybrid_levels: int = 0   # per-surfel feature levels of modes 4 / 12 / 14; modes 8-10: the decompose flag
     total_levels: int = 0    # all levels (mode 12 rows hold total_levels * level_dim + 1)
+
+    @property
+    def other_channels(self) -> int:
+        """out_others channels: 14, and 17 in mode 11 (its SH colour in 14-16)."""
+        return OTHER_CHANNELS + 3 if (int(self.render_mode) & 0xFF) == 11 else OTHER_CHANNELS
 
     @property
     def uses_rows(self) -> bool:
@@ -124,11 +130,11 @@ class Scratch:
 def rasterize_forward(cfg: RasterConfig, means3D, scales, rotations, opacities, homotrans, ap_level,
                       features, offsets, gridrange, scratch: Scratch | None = None,
                       capacity_hint: int | None = None, shapes=None, colors_precomp=None):
-    """Forward rasterization through ns_rasterize_forward. Render modes 4 / 12 /
-    14 read the per-surfel feature rows `colors_precomp` (contiguous fp32).
+    """Forward rasterization through ns_rasterize_forward. Every render mode but
+    0 (and level 0) reads the per-surfel rows `colors_precomp` (contiguous fp32).
 
-    Returns (num_rendered, out_color [C,H,W], out_others [14,H,W], radii [P] int32,
-    cover_pixels [P,1], trans_avg [P,1], scratch).
+    Returns (num_rendered, out_color [C,H,W], out_others [14,H,W] ([17,H,W] in
+    mode 11), radii [P] int32, cover_pixels [P,1], trans_avg [P,1], scratch).
     """
     lib = _lib.load()
     dev = means3D.device
@@ -138,7 +144,7 @@ def rasterize_forward(cfg: RasterConfig, means3D, scales, rotations, opacities, 
     _require_cuda(means3D, scales, rotations, opacities, homotrans, ap_level, features, offsets,
                   gridrange, cfg.viewmatrix, cfg.projmatrix)
     out_color = torch.zeros((Cc, H, W), dtype=torch.float32, device=dev)
-    out_others = torch.zeros((OTHER_CHANNELS, H, W), dtype=torch.float32, device=dev)
+    out_others = torch.zeros((cfg.other_channels, H, W), dtype=torch.float32, device=dev)
     radii = torch.zeros((P,), dtype=torch.int32, device=dev)
     rec_P = P if cfg.record_transmittance else 0
     cover = torch.zeros((rec_P, 1), dtype=torch.float32, device=dev)

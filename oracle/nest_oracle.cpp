@@ -256,7 +256,7 @@ void oracle_render(int W, int H, const uint32_t* ranges, const uint32_t* point_l
         std::fill(Cacc.begin(), Cacc.end(), 0.f);
         float N[3] = {0, 0, 0}, D = 0, M1 = 0, M2 = 0, distortion = 0, median_depth = 0;
         float median_contributor = -1;
-        float pos[3] = {0, 0, 0}, vis[3] = {0, 0, 0};
+        float pos[3] = {0, 0, 0}, vis[3] = {0, 0, 0}, sh_rgb[3] = {0, 0, 0};
         bool done = false;
         for (uint32_t k = r0; k < r1 && !done; k++) {
           contributor++;
@@ -344,9 +344,20 @@ void oracle_render(int W, int H, const uint32_t* ranges, const uint32_t* point_l
             pos[2] += w * xyz.z;
           }
           uint32_t apl = (uint32_t)std::floor(ap_level[id]);
-          if ((render_mode & 0xFF) == 0) {
+          const int base = render_mode & 0xFF;
+          if (base == 0 || base == 11) {
+            // mode 11 (residual_hybrid, forward.cu:1527-1592): the L hash levels
+            // from channel 0, as mode 0; its SH colour is accumulated below
             query_feature(feat.data(), C, LD, xyz, vmin, vmax, offsets, apl, table, L, S, Hres,
                           align_corners != 0, interp, contract != 0);
+          } else if (base >= 8 && base <= 10) {
+            // one 3-wide hash level (query_feature<false, 3, 3> with level 1)
+            const int decompose = hybrid_levels;
+            float h[3] = {0.f, 0.f, 0.f};
+            if (L > 0 && decompose != 1)
+              query_feature(h, 3, 3, xyz, vmin, vmax, offsets, apl, table, 1, S, Hres,
+                            align_corners != 0, interp, contract != 0);
+            sh_hybrid_feature(base, decompose, gauss + (size_t)id * (base == 9 ? 48 : 3), h, feat.data());
           } else {
             auto query = [&]() {
               query_feature(hf.data(), (int)L * LD, LD, xyz, vmin, vmax, offsets, apl, table, L, S,
@@ -356,6 +367,16 @@ void oracle_render(int W, int H, const uint32_t* ranges, const uint32_t* point_l
                          hf.data(), query);
           }
           for (int c = 0; c < C; c++) Cacc[c] += feat[c] * w;
+          if (base == 11) {
+            // forward.cu:1918-1943: the surfel's degree-3 SH (48 coefficients read
+            // interleaved) along the direction from its centre to the hit point
+            F3 dir = {xyz.x - pk.x, xyz.y - pk.y, xyz.z - pk.z};
+            const float inv_len = 1.0f / std::sqrt(dir.x * dir.x + dir.y * dir.y + dir.z * dir.z);
+            dir = {dir.x * inv_len, dir.y * inv_len, dir.z * inv_len};
+            float rgb[3];
+            eval_sh_interleaved(3, gauss + (size_t)id * 48, dir, rgb);
+            for (int c = 0; c < 3; c++) sh_rgb[c] += w * rgb[c];
+          }
           if (m13) {
             T = T * (1 - alpha);
             continue;
@@ -388,6 +409,9 @@ void oracle_render(int W, int H, const uint32_t* ranges, const uint32_t* point_l
         out_others[pid + 7 * HW] = (float)render_number;
         for (int c = 0; c < 3; c++) out_others[pid + (8 + c) * HW] = pos[c];
         for (int c = 0; c < 3; c++) out_others[pid + (11 + c) * HW] = vis[c];
+        // mode 11: channels 14-16 (forward.cu:2039-2045; out_others has 17 channels)
+        if ((render_mode & 0xFF) == 11)
+          for (int c = 0; c < 3; c++) out_others[pid + (14 + c) * HW] = sh_rgb[c];
       }
     }
   }

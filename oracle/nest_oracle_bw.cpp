@@ -308,10 +308,62 @@ void render_backward(int W, int H, const uint32_t* ranges, const uint32_t* point
               feat[c] = gauss[(size_t)id * C + c];
               atomic_add<R>(&dL_dcolors[(size_t)id * C + c], grad_feat[c]);
             }
-          } else if (base_mode == 0) {
+          } else if (base_mode == 0 || base_mode == 11) {
+            // mode 11 (backward.cu:1372-1424): the hash levels from channel 0 as in
+            // mode 0; its SH colour (out_others 14-16) has no gradient here
             query_feature_bw<R>(feat.data(), C, LD, xyz, vmin, vmax, offsets, apl, table, L, S, Hres,
                              align_corners != 0, interp, contract != 0, grad_feat.data(), dL_dtable,
                              dL_dxyz);
+          } else if (base_mode >= 8 && base_mode <= 10) {
+            // Modes 8 / 9 / 10 (backward.cu:1191-1371), one 3-wide hash level. As
+            // the reference computes them, the row and table gradients carry alpha T
+            // twice: grad_feat already holds alpha T dL/dC and each case multiplies
+            // by alpha T again. The colour term below uses the forward's features
+            // (the reference's cases leave `feat` unwritten).
+            const int decompose = hybrid_levels;
+            const size_t row = (size_t)id * (base_mode == 9 ? 48 : 3);
+            const float* g = gauss + row;
+            const bool q = L > 0 && decompose != 1;
+            R h[3] = {0, 0, 0}, zero[3] = {0, 0, 0}, hgrad[3] = {0, 0, 0}, scratch[3];
+            if (q)
+              query_feature_bw<R>(h, 3, 3, xyz, vmin, vmax, offsets, apl, table, 1, S, Hres,
+                                  align_corners != 0, interp, contract != 0, zero, dL_dtable, scratch);
+            const R aT = dchannel_dcolor;
+            if (base_mode == 8) {
+              for (int c = 0; c < 3; c++) {
+                const R gr = std::max(R(0), std::min(R(1), R(g[c]) + R(0.5f)));
+                const R hr = R(1) / (R(1) + std::exp(-h[c]));
+                const R sum = gr + hr;
+                feat[c] = decompose == 2 ? hr : decompose == 1 ? gr : std::max(R(0), std::min(R(1), sum));
+                const R gpc = (sum >= 0 && sum <= 1) ? grad_feat[c] : R(0);
+                const R v = R(g[c]) + R(0.5f);
+                if (decompose != 2) atomic_add<R>(&dL_dcolors[row + c], aT * ((v >= 0 && v <= 1) ? gpc : R(0)));
+                hgrad[c] = aT * gpc * hr * (R(1) - hr);
+              }
+            } else if (base_mode == 10) {
+              for (int c = 0; c < 3; c++) {
+                const R comb = decompose == 2 ? h[c] : decompose == 1 ? R(g[c]) : R(g[c]) + h[c];
+                const R sg = R(1) / (R(1) + std::exp(-comb));
+                feat[c] = sg;
+                const R gc = grad_feat[c] * sg * (R(1) - sg);
+                if (decompose != 2) atomic_add<R>(&dL_dcolors[row + c], aT * gc);
+                hgrad[c] = aT * gc;
+              }
+            } else {
+              for (int i = 0; i < 48; i++) {
+                feat[i] = g[i];
+                if (decompose != 2) atomic_add<R>(&dL_dcolors[row + i], aT * grad_feat[i]);
+              }
+              for (int c = 0; c < 3; c++) {
+                if (decompose == 2) feat[16 * c] = h[c];
+                else if (decompose != 1) feat[16 * c] += h[c];
+                hgrad[c] = aT * grad_feat[16 * c];
+              }
+            }
+            dL_dxyz[0] = dL_dxyz[1] = dL_dxyz[2] = 0;
+            if (q)
+              query_feature_bw<R>(scratch, 3, 3, xyz, vmin, vmax, offsets, apl, table, 1, S, Hres,
+                                  align_corners != 0, interp, contract != 0, hgrad, dL_dtable, dL_dxyz);
           } else {
             // Render modes 4 / 12 / 14 (backward.cu:987-1033, 1425-1606): the hash
             // levels see the fine channels' gradient times the mode's factor b; the

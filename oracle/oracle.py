@@ -119,14 +119,18 @@ def render(pre, vals, ranges, homotrans, ap_level, table_f32, offsets, gridrange
     kernel_type 1-3 (beta / flex / general splat kernels) read shapes [P].
     render_mode 4 / 12 / 14 (| 256 for the inference flag) combine per-surfel
     features `gauss` (colors_precomp rows) with the L hash levels at channel
-    hybrid_levels * LD.
+    hybrid_levels * LD. Modes 8 / 9 / 10 read one 3-wide hash level (LD 3, L 1)
+    and rows of 3 raw SH colours (48 SH coefficients for 9), hybrid_levels
+    carrying the level word's decompose flag; mode 11 adds the rows' degree-3
+    SH colour in out_others channels 14-16 (17 channels for that mode).
 
     row_stride > 1 renders only tile rows ty with ty % row_stride == 0 (a bounded
     sample for CPU timing); other pixels stay zero."""
     lib = load()
     HW = W * H
     P = pre["radii"].shape[0]
-    out = dict(out_color=np.zeros((C_out, H, W), np.float32), out_others=np.zeros((14, H, W), np.float32),
+    n_others = 17 if (int(render_mode) & 0xFF) == 11 else 14
+    out = dict(out_color=np.zeros((C_out, H, W), np.float32), out_others=np.zeros((n_others, H, W), np.float32),
                final_T=np.zeros((3, H, W), np.float32), n_contrib=np.zeros((2, H, W), np.uint32),
                cover_pixels=np.zeros(P, np.float32), trans_avg=np.zeros(P, np.float32))
     homotrans = _f32(homotrans).reshape(-1, 16)
@@ -282,7 +286,7 @@ def render_backward(pre, vals, ranges, fwd, homotrans, ap_level, table_f32, offs
     homotrans = _f32(homotrans).reshape(-1, 16)
     ap = _f32(ap_level).reshape(-1) if ap_level is not None else np.full(P, 1e9, np.float32)
     offs = np.ascontiguousarray(np.asarray(offsets, dtype=np.int32))
-    gc, go = _f32(dL_dcolor), _f32(dL_dothers)
+    gc, go = _f32(dL_dcolor), _f32(np.asarray(dL_dothers)[:14])  # channels 14-16 (mode 11) have no gradient
     assert gc.shape == (C_out, H, W) and go.shape == (14, H, W)
     fn = lib.oracle_render_backward_f64 if f64 else lib.oracle_render_backward
     fn(int(W), int(H), _p(np.ascontiguousarray(ranges, np.uint32)),

@@ -141,4 +141,66 @@ inline void query_feature(float* feat, int C, int LD, F3 xyz, float vmin, float 
   }
 }
 
+// Real spherical-harmonic basis up to degree 3 (the standard normalisation
+// constants of the 3D Gaussian splatting SH colour model), evaluated as the
+// reference's eval_sh_inline (forward.cu:76-155) does for render mode 11: the
+// 48 coefficients are read interleaved (coefficient k of channel c at 3 k + c),
+// 0.5 is added to the DC term and the result is clamped at 0.
+inline void eval_sh_interleaved(int deg, const float* sh, F3 dir, float* out) {
+  const float C0 = 0.28209479177387814f, C1 = 0.4886025119029199f;
+  const float C2[5] = {1.0925484305920792f, -1.0925484305920792f, 0.31539156525252005f,
+                       -1.0925484305920792f, 0.5462742152960396f};
+  const float C3[7] = {-0.5900435899266435f, 2.890611442640554f, -0.4570457994644658f,
+                       0.3731763325901154f, -0.4570457994644658f, 1.445305721320277f,
+                       -0.5900435899266435f};
+  for (int c = 0; c < 3; c++) out[c] = C0 * sh[c] + 0.5f;
+  if (deg > 0) {
+    const float x = dir.x, y = dir.y, z = dir.z;
+    for (int c = 0; c < 3; c++)
+      out[c] = out[c] - C1 * y * sh[3 + c] + C1 * z * sh[6 + c] - C1 * x * sh[9 + c];
+    if (deg > 1) {
+      const float xx = x * x, yy = y * y, zz = z * z, xy = x * y, yz = y * z, xz = x * z;
+      for (int c = 0; c < 3; c++)
+        out[c] = out[c] + C2[0] * xy * sh[12 + c] + C2[1] * yz * sh[15 + c] +
+                 C2[2] * (2.0f * zz - xx - yy) * sh[18 + c] + C2[3] * xz * sh[21 + c] +
+                 C2[4] * (xx - yy) * sh[24 + c];
+      if (deg > 2) {
+        for (int c = 0; c < 3; c++)
+          out[c] = out[c] + C3[0] * y * (3.0f * xx - yy) * sh[27 + c] + C3[1] * xy * z * sh[30 + c] +
+                   C3[2] * y * (4.0f * zz - xx - yy) * sh[33 + c] +
+                   C3[3] * z * (2.0f * zz - 3.0f * xx - 3.0f * yy) * sh[36 + c] +
+                   C3[4] * x * (4.0f * zz - xx - yy) * sh[39 + c] + C3[5] * z * (xx - yy) * sh[42 + c] +
+                   C3[6] * x * (xx - 3.0f * yy) * sh[45 + c];
+      }
+    }
+  }
+  for (int c = 0; c < 3; c++) out[c] = std::fmax(out[c], 0.0f);
+}
+
+// Render modes 8 (hybrid_SH), 9 (hybrid_SH_post) and 10 (hybrid_SH_raw),
+// forward.cu:1378-1526: the sample's feature from the surfel's row `g` (3 raw
+// SH colours; 48 SH coefficients for mode 9) and h, the single-level, 3-wide
+// hash value at the hit point (zero when not queried). decompose: 0 both
+// parts, 1 the surfel only, 2 the grid only. Writes C = 3 (48) channels.
+inline void sh_hybrid_feature(int base, int decompose, const float* g, const float h[3], float* feat) {
+  if (base == 8) {
+    for (int c = 0; c < 3; c++) {
+      const float gr = std::fmax(0.0f, std::fmin(1.0f, g[c] + 0.5f));
+      const float hr = 1.0f / (1.0f + std::exp(-h[c]));
+      feat[c] = decompose == 2 ? hr : decompose == 1 ? gr : std::fmax(0.0f, std::fmin(1.0f, gr + hr));
+    }
+  } else if (base == 10) {
+    for (int c = 0; c < 3; c++) {
+      const float comb = decompose == 2 ? h[c] : decompose == 1 ? g[c] : g[c] + h[c];
+      feat[c] = 1.0f / (1.0f + std::exp(-comb));
+    }
+  } else {
+    for (int i = 0; i < 48; i++) feat[i] = g[i];
+    for (int c = 0; c < 3; c++) {
+      if (decompose == 2) feat[16 * c] = h[c];
+      else if (decompose != 1) feat[16 * c] += h[c];
+    }
+  }
+}
+
 }  // namespace oracle

@@ -119,6 +119,64 @@ def splat_value(rho, shape, kernel_type: int):
     return torch.exp(-0.5 * rho), torch.ones_like(rho, dtype=torch.bool)
 
 
+SH_C0 = 0.28209479177387814
+SH_C1 = 0.4886025119029199
+SH_C2 = (1.0925484305920792, -1.0925484305920792, 0.31539156525252005, -1.0925484305920792, 0.5462742152960396)
+SH_C3 = (-0.5900435899266435, 2.890611442640554, -0.4570457994644658, 0.3731763325901154, -0.4570457994644658,
+         1.445305721320277, -0.5900435899266435)
+
+
+def eval_sh_interleaved(sh, d):
+    """Degree-3 SH colour [n, 3] of 48 coefficients read interleaved (coefficient
+    k of channel c at 3 k + c) along unit directions d [n, 3], + 0.5 on the DC
+    term and clamped at 0 (forward.cu:76-155, render mode 11)."""
+    x, y, z = d[:, 0:1], d[:, 1:2], d[:, 2:3]
+    c = lambda k: sh[3 * k:3 * k + 3][None, :]  # noqa: E731
+    xx, yy, zz, xy, yz, xz = x * x, y * y, z * z, x * y, y * z, x * z
+    r = SH_C0 * c(0) + 0.5 - SH_C1 * y * c(1) + SH_C1 * z * c(2) - SH_C1 * x * c(3)
+    r = (r + SH_C2[0] * xy * c(4) + SH_C2[1] * yz * c(5) + SH_C2[2] * (2 * zz - xx - yy) * c(6)
+         + SH_C2[3] * xz * c(7) + SH_C2[4] * (xx - yy) * c(8))
+    r = (r + SH_C3[0] * y * (3 * xx - yy) * c(9) + SH_C3[1] * xy * z * c(10)
+         + SH_C3[2] * y * (4 * zz - xx - yy) * c(11) + SH_C3[3] * z * (2 * zz - 3 * xx - 3 * yy) * c(12)
+         + SH_C3[4] * x * (4 * zz - xx - yy) * c(13) + SH_C3[5] * z * (xx - yy) * c(14)
+         + SH_C3[6] * x * (xx - 3 * yy) * c(15))
+    return torch.clamp_min(r, 0.0)
+
+
+def sh_hybrid_feature(h, row, mode, decompose):
+    """Features of render modes 8 / 9 / 10 (forward.cu:1378-1526) from the
+    single-level 3-wide hash value h [n, 3] and the surfel's row (3 raw SH
+    colours; 48 SH coefficients for mode 9). With decompose 1 (the surfel only)
+    the grid is not queried (h = 0). Mode 8 keeps the reference backward's
+    mask for every decompose flag: gradients pass only where
+    clamp(row + 0.5) + sigmoid(h) lies in [0, 1], also when the forward used
+    one of the two parts alone."""
+    n = h.shape[0]
+    if decompose == 1:
+        h = torch.zeros_like(h)
+    if mode == 8:
+        gr = torch.clamp(row[:3] + 0.5, 0.0, 1.0).expand(n, 3)
+        hr = torch.sigmoid(h)
+        s = gr + hr
+        if decompose == 0:
+            return torch.clamp(s, 0.0, 1.0)
+        mask = ((s >= 0) & (s <= 1)).detach().to(h.dtype)
+        part = hr if decompose == 2 else gr
+        return part.detach() + mask * (part - part.detach())
+    if mode == 10:
+        comb = h if decompose == 2 else (row[:3].expand(n, 3) if decompose == 1 else row[:3] + h)
+        return torch.sigmoid(comb)
+    feat = row[:48].expand(n, 48)
+    dc = torch.zeros(n, 48, dtype=h.dtype)
+    keep = torch.ones(48, dtype=h.dtype)
+    if decompose != 1:
+        for c in range(3):
+            dc[:, 16 * c] = h[:, c]
+            if decompose == 2:
+                keep[16 * c] = 0.0
+    return feat * keep + dc
+
+
 def mode_feature(f_hash, row, mode, pg, td, C):
     """Feature vectors [n, C] of render modes 4 / 6 / 7 / 12 / 14
     (forward.cu:1218-1377, 1593-1790, training rules) and of level 0 (mode 0
@@ -179,6 +237,7 @@ def render(means, scales, rots, opac, table, cam, lists, grid, apl_int, W, H, ke
     C = grid["L"] * grid["LD"] if modes is None else modes["C"]
     color = torch.zeros(C, H * W, dtype=torch.float64)
     others = torch.zeros(7, H * W, dtype=torch.float64)
+    sh_map = torch.zeros(3, H * W, dtype=torch.float64)
     gx = (W + TILE - 1) // TILE
     margin = np.inf
     for t in range(ranges.shape[0]):
@@ -196,6 +255,7 @@ def render(means, scales, rots, opac, table, cam, lists, grid, apl_int, W, H, ke
         M1, M2, dist, med = D.clone(), D.clone(), D.clone(), D.clone()
         N = torch.zeros(npx, 3, dtype=torch.float64)
         Cacc = torch.zeros(npx, C, dtype=torch.float64)
+        SH = torch.zeros(npx, 3, dtype=torch.float64)
         for k in range(int(ranges[t, 0]), int(ranges[t, 1])):
             i = int(point_list[k])
             kk = pxf[:, None] * Tw[i] - Tu[i]
@@ -240,10 +300,27 @@ def render(means, scales, rots, opac, table, cam, lists, grid, apl_int, W, H, ke
             f = query(hit, np.full(npx, apl_int[i]), table, grid["offsets"], grid["L"], grid["LD"], grid["S"],
                       grid["H"], grid["vmin"], grid["vmax"], grid.get("align_corners", False),
                       grid.get("interp", 0))
-            if modes is not None:
+            if modes is not None and modes["mode"] in (8, 9, 10):
+                # the reference's cases 8-10 scale the row and hash gradients by
+                # alpha T once more (backward.cu:1191-1371): same value, gradient
+                # through f times the detached weight
+                f = sh_hybrid_feature(f, modes["gauss"][i], modes["mode"], modes["decompose"])
+                f = f.detach() + w.detach()[:, None] * (f - f.detach())
+            elif modes is not None and modes["mode"] == 11:
+                # hash levels from channel 0; the surfel's SH colour along hit - centre
+                # goes to its own map (no gradient in the reference's backward)
+                f = torch.cat([f, f.new_zeros(npx, C - f.shape[1])], 1) if f.shape[1] < C else f
+                dvec = (hit - means[i]).detach()
+                rgb = eval_sh_interleaved(modes["gauss"][i].detach(), dvec / dvec.norm(dim=1, keepdim=True))
+                rgb = torch.where(b3[:, None], torch.nan_to_num(rgb, nan=0.0), torch.zeros_like(rgb))
+                SH = SH + rgb * w.detach()[:, None]
+            elif modes is not None:
                 f = mode_feature(f, modes["gauss"][i], modes["mode"], modes["pg"], modes["td"], C)
             Cacc = Cacc + f * w[:, None]
             T = torch.where(valid, test_T, T)
         color = color.index_copy(1, pid, Cacc.T)
+        sh_map = sh_map.index_copy(1, pid, SH.T)
         others = others.index_copy(1, pid, torch.stack([D, 1 - T, N[:, 0], N[:, 1], N[:, 2], med, dist], 0))
+    if modes is not None and modes["mode"] == 11:
+        modes["sh_rgb"] = sh_map.reshape(3, H, W)
     return color.reshape(C, H, W), others.reshape(7, H, W), margin, xy

@@ -57,7 +57,7 @@ def oracle_grads(c):
         kw.update(kernel_type=c["kernel_type"], shapes=c["shapes"].numpy())
     if "mode" in c:
         kw.update(render_mode=c["mode"], hybrid_levels=c["hybrid"], total_levels=c["total"], gauss=c["gauss"].numpy())
-    C = c["total"] * grid.level_dim if "mode" in c else grid.channels
+    C = c.get("C", c["total"] * grid.level_dim) if "mode" in c else grid.channels
     L = c.get("levels", grid.levels)
     fwd = oracle.render(pre, vals, ranges, c["homo"].numpy(), c["ap"].numpy(), c["table"].numpy(),
                         grid.offsets.numpy(), grid.gridrange.numpy(), W, H, C, grid.level_dim,
@@ -88,13 +88,16 @@ def model_grads(c, pre, vals, ranges):
             td = c["total"] * grid.level_dim
             rows = torch.cat([rows[:, :td], torch.sigmoid(rows[:, td:td + 1])], 1)
     visible = torch.as_tensor(pre["radii"] > 0)
+    modes = None if "mode" not in c else dict(
+        mode=c["mode"], gauss=rows, pg=c["hybrid"] * grid.level_dim, td=c["total"] * grid.level_dim,
+        C=c.get("C", c["total"] * grid.level_dim), decompose=c["hybrid"])
+    c["model_modes"] = modes
     color, others, margin, _ = bw_model.render(
         means, scales, rots, opac, table,
         dict(viewmatrix=cam.world_view_transform.numpy(), projmatrix=cam.full_proj_transform.numpy()),
         (ranges, vals), info, np.floor(c["ap"].numpy()).astype(np.int64), c["W"], c["H"],
         kernel_type=c.get("kernel_type", 0), shapes=leaves[5] if c.get("kernel_type") else None,
-        modes=None if "mode" not in c else dict(mode=c["mode"], gauss=rows, pg=c["hybrid"] * grid.level_dim,
-                                                td=c["total"] * grid.level_dim, C=c["total"] * grid.level_dim))
+        modes=modes)
     loss = (color * c["gc"].double()).sum() + (others * c["go"][:7].double()).sum()
     loss.backward()
     grads = {k: (v.grad if v.grad is not None else torch.zeros_like(v)).detach().numpy()
@@ -197,6 +200,82 @@ def test_oracle_backward_render_modes_match_autograd(mode, seed):
               "opac": gr["dL_dopacity"], "gauss": gr["dL_dcolors"]}
     if mode != 0:  # level 0 reads no table
         checks["table"] = gr["dL_dtable"]
+    for k, got in checks.items():
+        assert np.linalg.norm(mg[k]) > 0, k
+        assert rel_l2(got, mg[k]) < 1e-4, (k, rel_l2(got, mg[k]))
+
+
+def sh_grid(g, levels=1):
+    """A single-level hash grid with 3-wide rows U(-2, 2) (modes 8-10 query one
+    3-channel level, query_feature<false, 3, 3>)."""
+    from types import SimpleNamespace
+    base = synth.hash_grid(g, levels=levels, log2_T=12, lo=-1.0, hi=1.0, base_resolution=8, per_level_scale=2.0)
+    rows = int(base.offsets[-1])
+    table = (torch.rand(rows, 3, generator=g) * 4 - 2).contiguous()
+    return SimpleNamespace(table=table, offsets=base.offsets, gridrange=base.gridrange, S=base.S,
+                           base_resolution=base.base_resolution, level_dim=3, levels=levels, channels=3)
+
+
+@pytest.mark.parametrize("mode,decompose,seed", [(8, 0, 31), (8, 1, 42), (8, 2, 33), (10, 0, 34), (10, 1, 38),
+                                                 (10, 2, 44), (9, 0, 36), (9, 2, 39)])
+def test_oracle_backward_sh_hybrid_modes_match_autograd(mode, decompose, seed):
+    """Render modes 8 (hybrid_SH), 9 (hybrid_SH_post) and 10 (hybrid_SH_raw):
+    one 3-wide hash level and per-surfel rows (3 raw SH colours; 48 SH
+    coefficients for 9), with each decompose flag. The reference's backward
+    multiplies the row and table gradients (and so dL/dxyz) by alpha T once more
+    than the derivative of its forward; the model reproduces that by scaling
+    the gradient through the feature by the detached weight."""
+    c = tiny_case(seed)
+    g = torch.Generator().manual_seed(seed)
+    n = c["means"].shape[0]
+    grid = sh_grid(g)
+    C = 48 if mode == 9 else 3
+    c.update(grid=grid, table=grid.table, mode=mode, hybrid=decompose, total=3, levels=1, C=C)
+    c["gc"] = torch.randn(C, c["H"], c["W"], generator=g)
+    c["gauss"] = (torch.rand(n, C, generator=g) * 2 - 1).contiguous()
+    pre, vals, ranges, fwd, gr, pg = oracle_grads(c)
+    color, others, margin, mg = model_grads(c, pre, vals, ranges)
+    assert margin > 1e-5, "a branch sits on its threshold; pick another seed"
+    assert np.max(np.abs(color - fwd["out_color"])) < 2e-5
+    checks = {"means": pg["dL_dmeans3D"], "scales": pg["dL_dscales"], "rots": pg["dL_drots"],
+              "opac": gr["dL_dopacity"]}
+    if decompose != 2:
+        checks["gauss"] = gr["dL_dcolors"]
+    else:
+        assert not np.any(gr["dL_dcolors"])
+    if decompose != 1:
+        checks["table"] = gr["dL_dtable"]
+    else:
+        assert not np.any(gr["dL_dtable"])
+    for k, got in checks.items():
+        assert np.linalg.norm(mg[k]) > 0, k
+        assert rel_l2(got, mg[k]) < 1e-4, (k, rel_l2(got, mg[k]))
+
+
+def test_oracle_residual_hybrid_mode_11():
+    """Render mode 11 (residual_hybrid): the hash levels from channel 0 with
+    mode 0's gradients and no gradient for the SH rows; the rows' degree-3 SH
+    colour (48 coefficients read interleaved, along hit - centre) blended into
+    out_others channels 14-16, against the float64 model."""
+    seed = 41
+    c = tiny_case(seed)
+    g = torch.Generator().manual_seed(seed)
+    n = c["means"].shape[0]
+    grid = synth.hash_grid(g, levels=3, log2_T=12, lo=-1.0, hi=1.0, base_resolution=8, per_level_scale=2.0)
+    c.update(grid=grid, table=grid.table.float().contiguous(), mode=11, hybrid=0, total=3, levels=3, C=6)
+    c["gc"] = torch.randn(6, c["H"], c["W"], generator=g)
+    c["gauss"] = (torch.rand(n, 48, generator=g) * 2 - 1).contiguous()
+    pre, vals, ranges, fwd, gr, pg = oracle_grads(c)
+    assert fwd["out_others"].shape[0] == 17
+    color, others, margin, mg = model_grads(c, pre, vals, ranges)
+    assert margin > 1e-5
+    assert np.max(np.abs(color - fwd["out_color"])) < 2e-5
+    sh = c["model_modes"]["sh_rgb"].numpy()
+    assert np.abs(sh).max() > 0.1
+    assert np.max(np.abs(sh - fwd["out_others"][14:17])) < 2e-5
+    assert not np.any(gr["dL_dcolors"])
+    checks = {"means": pg["dL_dmeans3D"], "scales": pg["dL_dscales"], "rots": pg["dL_drots"],
+              "opac": gr["dL_dopacity"], "table": gr["dL_dtable"]}
     for k, got in checks.items():
         assert np.linalg.norm(mg[k]) > 0, k
         assert rel_l2(got, mg[k]) < 1e-4, (k, rel_l2(got, mg[k]))
