@@ -128,6 +128,14 @@ typedef struct ns_raster_settings {
   int32_t render_mode;
   uint32_t hybrid_levels;
   uint32_t total_levels;
+  /* SH colours (forward.cu:414-423, computeColorFromSH :21-74): with render_mode
+   * 0, levels 0, channels 3, ns_surfels.colors_precomp NULL and ns_surfels.shs
+   * set, the surfels' colours are their degree-sh_degree (0-3) SH along the
+   * unit direction from campos (device [3], the camera centre) to the mean,
+   * + 0.5, clamped at 0; the backward returns dL/dshs and adds the colour's
+   * part of dL/dmeans3D. */
+  int32_t sh_degree;
+  const float* campos;
 } ns_raster_settings;
 
 /* Per-surfel inputs of the rasterizer. */
@@ -151,6 +159,9 @@ typedef struct ns_surfels {
                                   11 [P, 48] SH coefficients (mode 11 reads them
                                   interleaved, coefficient k of channel c at 3 k + c,
                                   as the reference's kernel does); else NULL */
+  const float* shs;       /* [P, sh_coeffs, 3] SH coefficients (RGB triples per
+                             coefficient), read for the level-0 SH colours, else NULL */
+  int32_t sh_coeffs;      /* M >= (sh_degree + 1)^2 */
 } ns_surfels;
 
 /* Outputs (caller-owned, device). cover_pixels / trans_avg may be NULL when
@@ -225,6 +236,8 @@ typedef struct ns_raster_grads_out {
                            1108-1606; modes 8-10 with alpha T applied twice as the
                            reference's cases 8-10 compute it; zero in mode 11,
                            whose SH colour has no gradient), else NULL */
+  float* dL_dshs;       /* [P, sh_coeffs, 3] with the SH colours (written, zero
+                           where radii <= 0; backward.cu:21-140), else NULL */
 } ns_raster_grads_out;
 
 /* Scratch of the backward pass: per-surfel gradient accumulators. */

@@ -64,6 +64,7 @@ struct GeomState {
   uint32_t* depth_vals_sorted;  // surfel indices in depth order
   uint32_t* sorted_sums;
   uint32_t* sorted_prefix;
+  float* rgb;  // [P, 3] SH colours of the level-0 SH path
   void* depth_sort_temp;
   size_t depth_sort_temp_bytes;
 };
@@ -88,6 +89,7 @@ GeomState carve_geom(void* base, int P, size_t* used) {
   g.depth_vals_sorted = c.take<uint32_t>(np);
   g.sorted_sums = c.take<uint32_t>((size_t)nb);
   g.sorted_prefix = c.take<uint32_t>((size_t)nb);
+  g.rgb = c.take<float>(3 * np);
   g.depth_sort_temp_bytes = radix_sort_temp_bytes(P);
   g.depth_sort_temp = c.take<char>(g.depth_sort_temp_bytes);
   if (used) *used = align_up(c.off);
@@ -207,6 +209,17 @@ int validate_settings(const ns_raster_settings* s) {
       return NS_ERR_INVALID;
     if (base == 7 && s->levels > s->total_levels) return NS_ERR_INVALID;
   }
+  return NS_OK;
+}
+
+// The level-0 SH path (forward.cu:414-423): mode 0 without hash levels, no
+// precomputed colours, SH coefficients given.
+bool sh_colours(const ns_raster_settings* s, const ns_surfels* f) {
+  return s->render_mode == 0 && s->levels == 0 && !f->colors_precomp && f->shs;
+}
+int validate_sh(const ns_raster_settings* s, const ns_surfels* f) {
+  if (s->channels != 3 || s->sh_degree < 0 || s->sh_degree > 3 || !s->campos) return NS_ERR_INVALID;
+  if (f->sh_coeffs < (s->sh_degree + 1) * (s->sh_degree + 1)) return NS_ERR_INVALID;
   return NS_OK;
 }
 
@@ -352,7 +365,9 @@ int ns_rasterize_forward(const ns_raster_settings* settings, const ns_surfels* s
     return NS_ERR_INVALID;
   if (!outputs->out_color || !outputs->out_others || !outputs->radii) return NS_ERR_INVALID;
   if (settings->kernel_type != 0 && P > 0 && !surfels->shapes) return NS_ERR_INVALID;
-  if (uses_surfel_rows(settings->render_mode, settings->levels) && P > 0 && !surfels->colors_precomp)
+  const bool shc = sh_colours(settings, surfels);
+  if (shc && (rc = validate_sh(settings, surfels))) return rc;
+  if (uses_surfel_rows(settings->render_mode, settings->levels) && P > 0 && !surfels->colors_precomp && !shc)
     return NS_ERR_INVALID;
   if (settings->record_transmittance && (!outputs->cover_pixels || !outputs->trans_avg))
     return NS_ERR_INVALID;
@@ -370,10 +385,15 @@ int ns_rasterize_forward(const ns_raster_settings* settings, const ns_surfels* s
                              g.records, g.bin, outputs->radii, g.tiles, g.depth_keys, g.depth_vals,
                              g.block_sums, stream);
   if (rc) return rc;
+  if (shc) {
+    rc = sh_color_launch(P, settings->sh_degree, surfels->sh_coeffs, surfels->means3D, settings->campos,
+                         surfels->shs, g.rgb, stream);
+    if (rc) return rc;
+  }
   return bin_and_render(settings, P, g, im, binning, binning_bytes, surfels->features,
                         surfels->offsets, surfels->gridrange, outputs->out_color,
                         outputs->out_others, outputs->cover_pixels, outputs->trans_avg,
-                        surfels->colors_precomp, num_rendered, flags, stream);
+                        shc ? g.rgb : surfels->colors_precomp, num_rendered, flags, stream);
 }
 
 int ns_read_binning(const void* geom, size_t geom_bytes, int32_t P, const void* binning,
@@ -418,7 +438,10 @@ int ns_read_binning(const void* geom, size_t geom_bytes, int32_t P, const void* 
   return NS_OK;
 }
 
-size_t ns_backward_scratch_bytes(int32_t P) { return align_up(backward_accum_bytes(P)); }
+size_t ns_backward_scratch_bytes(int32_t P) {
+  // the per-surfel accumulators, then dL/drgb of the level-0 SH path
+  return align_up(backward_accum_bytes(P)) + align_up((size_t)max64(P, 1) * 3 * sizeof(float));
+}
 
 size_t ns_backward_scratch_bytes_deterministic(int32_t P, int64_t table_rows, int32_t level_dim) {
   const int64_t entries = max64(table_rows, 0) * max64(level_dim, 0);
@@ -444,7 +467,9 @@ int ns_rasterize_backward(const ns_raster_settings* settings, const ns_surfels* 
     return NS_ERR_INVALID;
   const int base_mode = settings->render_mode & 0xFF;
   const bool rows = uses_surfel_rows(settings->render_mode, settings->levels);
-  if (rows && P > 0 && (!surfels->colors_precomp || !go->dL_dcolors_precomp)) return NS_ERR_INVALID;
+  const bool shc = sh_colours(settings, surfels);
+  if (shc && ((rc = validate_sh(settings, surfels)) || (P > 0 && !go->dL_dshs))) return rc ? rc : NS_ERR_INVALID;
+  if (rows && !shc && P > 0 && (!surfels->colors_precomp || !go->dL_dcolors_precomp)) return NS_ERR_INVALID;
   // row length of colors_precomp: level 0 and mode 6 C, mode 4 hybrid LD,
   // modes 7 / 12 total LD + 1, mode 14 hybrid LD + 1, modes 8 / 10 3, modes 9 / 11 48
   const size_t mode_stride = !rows                              ? 0
@@ -519,10 +544,13 @@ int ns_rasterize_backward(const ns_raster_settings* settings, const ns_surfels* 
   bp.render_mode = settings->render_mode;
   bp.hybrid_levels = (int)settings->hybrid_levels;
   bp.total_levels = (int)settings->total_levels;
-  bp.gauss = surfels->colors_precomp;
-  bp.dL_dcolors = go->dL_dcolors_precomp;
+  // SH path: the colours' gradient goes to scratch, then through the SH backward
+  float* drgb = reinterpret_cast<float*>(static_cast<unsigned char*>(scratch) +
+                                         align_up(backward_accum_bytes(P)));
+  bp.gauss = shc ? g.rgb : surfels->colors_precomp;
+  bp.dL_dcolors = shc ? drgb : go->dL_dcolors_precomp;
   if (rows)
-    NS_CUDA_TRY(cudaMemsetAsync(go->dL_dcolors_precomp, 0, (size_t)P * mode_stride * sizeof(float), stream));
+    NS_CUDA_TRY(cudaMemsetAsync(bp.dL_dcolors, 0, (size_t)P * mode_stride * sizeof(float), stream));
   bp.Wq = Wq;
   bp.Hq = Hq;
   bp.projmatrix = settings->projmatrix;
@@ -552,9 +580,12 @@ int ns_rasterize_backward(const ns_raster_settings* settings, const ns_surfels* 
     rc = table_grad_finish_launch(table_fixed, table_entries, grad_max, go->dL_dtable, stream);
     if (rc) return rc;
   }
-  return preprocess_backward_launch(P, surfels->means3D, surfels->scales, surfels->rotations,
-                                    gi->radii, settings->viewmatrix, settings->projmatrix, Wq, Hq,
-                                    accum, *go, stream);
+  rc = preprocess_backward_launch(P, surfels->means3D, surfels->scales, surfels->rotations, gi->radii,
+                                  settings->viewmatrix, settings->projmatrix, Wq, Hq, accum, *go, stream);
+  if (rc || !shc) return rc;
+  // computeColorFromSH's backward after the mean gradient is written (it adds to it)
+  return sh_color_backward_launch(P, settings->sh_degree, surfels->sh_coeffs, surfels->means3D, settings->campos,
+                                  surfels->shs, gi->radii, drgb, go->dL_dshs, go->dL_dmeans3D, stream);
 }
 
 int ns_read_device_status(void* geom, int32_t P, void* stream_) {

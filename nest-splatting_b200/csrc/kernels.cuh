@@ -91,6 +91,13 @@ struct BackwardParams {
   float* accum;
 };
 size_t backward_accum_bytes(int64_t P);
+// SH colours of the level-0 path (sh.cu): rgb [P, 3] from shs [P, M, 3]; the
+// backward writes dL_dshs and adds to dL_dmeans (surfels with radii > 0).
+int sh_color_launch(int P, int deg, int M, const float* means, const float* campos, const float* shs, float* rgb,
+                    cudaStream_t stream);
+int sh_color_backward_launch(int P, int deg, int M, const float* means, const float* campos, const float* shs,
+                             const int32_t* radii, const float* dL_drgb, float* dL_dshs, float* dL_dmeans,
+                             cudaStream_t stream);
 int table_grad_max_launch(const float* dL_dcolor, size_t n, uint32_t* gmax, cudaStream_t stream);
 int table_grad_finish_launch(const unsigned long long* fx, size_t n, const uint32_t* gmax, float* out,
                              cudaStream_t stream);

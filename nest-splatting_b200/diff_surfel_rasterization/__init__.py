@@ -30,7 +30,10 @@ Backward (__init__.py:174-275 of the reference): the 21 gradients come back in
 argument order; means2D's slot carries the densification statistic and
 ap_level's slot dL_gradsum, homotrans gets None (its gradient is folded into
 means, scales and rotations), sh gets zeros and colors_precomp zeros in mode 0
-(which never reads them).
+(which never reads them). Level 0 takes colors_precomp or, like the
+reference's warm-up renders, SH coefficients (`shs`, evaluated at
+raster_settings.sh_degree from raster_settings.campos); their gradient comes
+back in sh's slot.
 
 `features` may be fp32 (as the reference stores the table) or fp16 (read as
 fp16 pairs by the kernels, half the L2 traffic).
@@ -111,13 +114,18 @@ class _RasterizeGaussians(torch.autograd.Function):
         L = int(hashgrid_settings.L)
         hybrid = total = 0
         gauss = None
+        shs_in = None
         if base_mode == 0 and L <= 0:
-            # level 0 (forward.cu:1093-1096): the precomputed per-surfel colours are
-            # blended (SH colours from preprocess are not built)
+            # level 0 (forward.cu:1093-1096): the per-surfel colours are blended, either
+            # colors_precomp or the SH colours preprocess evaluates (:414-423)
             gauss = _nonempty(colors_precomp)
-            if gauss is None:
-                raise NotImplementedError("level 0 from SH coefficients is not built: pass colors_precomp")
-            gauss = gauss.detach().contiguous().float()
+            if gauss is not None:
+                gauss = gauss.detach().contiguous().float()
+            else:
+                shs_in = _nonempty(sh)
+                if shs_in is None:
+                    raise RuntimeError("level 0 needs colors_precomp or SH coefficients")
+                shs_in = shs_in.detach().contiguous().float().reshape(means3D.shape[0], -1, 3)
             L = 0
             if _nonempty(features) is None:  # the C-ABI wants a table; level 0 reads none
                 features = torch.zeros((1, 2), dtype=torch.float32, device=means3D.device)
@@ -178,7 +186,9 @@ class _RasterizeGaussians(torch.autograd.Function):
             gauss = gauss.detach().contiguous().float()
         _, HS, OS = _shape_dims(hashgrid_settings)
         if base_mode == 0 and L == 0 and OS == 0:
-            OS = gauss.shape[-1]
+            OS = gauss.shape[-1] if gauss is not None else 3
+        if shs_in is not None:
+            OS = 3
         if base_mode in (8, 10):
             OS = 3
         elif base_mode == 9:
@@ -202,7 +212,9 @@ class _RasterizeGaussians(torch.autograd.Function):
             interpolation=int(hashgrid_settings.interpolation), channels=int(OS),
             level_dim=int(feats.shape[1]), table_fp16=feats.dtype == torch.float16,
             kernel_type=int(kernel_type), deterministic=torch.are_deterministic_algorithms_enabled(),
-            render_mode=mode, hybrid_levels=hybrid, total_levels=total)
+            render_mode=mode, hybrid_levels=hybrid, total_levels=total,
+            sh_degree=int(raster_settings.sh_degree) if shs_in is not None else 0,
+            campos=raster_settings.campos.detach().contiguous().float() if shs_in is not None else None)
         ap = _nonempty(ap_level)
         args = (means3D.detach().contiguous().float(), scales.detach().contiguous().float(),
                 rotations.detach().contiguous().float(), opacities.detach().contiguous().float().reshape(-1),
@@ -210,7 +222,7 @@ class _RasterizeGaussians(torch.autograd.Function):
                 None if ap is None else ap.detach().contiguous().float().reshape(-1), feats.detach(),
                 offsets.contiguous().to(torch.int32), gridrange.contiguous().float())
         num_rendered, color, others, radii, cover, trans, scratch = _raster.rasterize_forward(
-            cfg, *args, shapes=shp, colors_precomp=gauss)
+            cfg, *args, shapes=shp, colors_precomp=gauss, shs=shs_in)
         ctx.cfg = cfg
         ctx.args = args
         ctx.radii = radii
@@ -221,6 +233,7 @@ class _RasterizeGaussians(torch.autograd.Function):
                           shapes=None if shp is None else shapes.shape)
         ctx.shape_values = shp
         ctx.gauss = gauss
+        ctx.shs = shs_in
         ctx.mark_non_differentiable(radii)
         return color, radii, others, trans, cover
 
@@ -237,7 +250,7 @@ class _RasterizeGaussians(torch.autograd.Function):
             grad_depth = torch.zeros((_raster.OTHER_CHANNELS, H, W), dtype=torch.float32, device=dev)
         g = _raster.rasterize_backward(ctx.cfg, *ctx.args, ctx.radii, ctx.num_rendered, ctx.scratch,
                                        grad_out_color, grad_depth, shapes=ctx.shape_values,
-                                       colors_precomp=ctx.gauss)
+                                       colors_precomp=ctx.gauss, shs=ctx.shs)
         ctx.scratch = None
         need = ctx.needs_input_grad
         sh = ctx.shapes
@@ -249,7 +262,7 @@ class _RasterizeGaussians(torch.autograd.Function):
                                                           sh["ap_level"][0] == g["gradsum"].shape[0]) else None
         return (g["means3D"] if need[0] else None,
                 g["means2D"] if need[1] else None,
-                zeros_if(2, sh["sh"]),
+                (g["shs"].reshape(sh["sh"]) if "shs" in g else zeros_if(2, sh["sh"])) if need[2] else None,
                 (g["colors_precomp"].reshape(sh["colors_precomp"]) if "colors_precomp" in g
                  else zeros_if(3, sh["colors_precomp"])) if need[3] else None,
                 g["opacity"].reshape(sh["opacities"]) if need[4] else None,

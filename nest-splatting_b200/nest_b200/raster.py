@@ -52,6 +52,8 @@ class RasterConfig:
     #                          12 adaptive_cat, 13 adaptive_cat_fast, 14 adaptive_zero (| 256 inference)
     hybrid_levels: int = 0   # per-surfel feature levels of modes 4 / 12 / 14; modes 8-10: the decompose flag
     total_levels: int = 0    # all levels (mode 12 rows hold total_levels * level_dim + 1)
+    sh_degree: int = 0       # level 0 with SH coefficients: the degree evaluated (0-3)
+    campos: object = None    # level 0 with SH coefficients: camera centre, device tensor [3]
 
     @property
     def other_channels(self) -> int:
@@ -90,6 +92,8 @@ class RasterConfig:
         s.channels = int(self.channels)
         s.level_dim = int(self.level_dim)
         s.table_fp16 = int(bool(self.table_fp16))
+        s.sh_degree = int(self.sh_degree)
+        s.campos = None if self.campos is None else self.campos.data_ptr()
         return s
 
 
@@ -129,9 +133,11 @@ class Scratch:
 
 def rasterize_forward(cfg: RasterConfig, means3D, scales, rotations, opacities, homotrans, ap_level,
                       features, offsets, gridrange, scratch: Scratch | None = None,
-                      capacity_hint: int | None = None, shapes=None, colors_precomp=None):
+                      capacity_hint: int | None = None, shapes=None, colors_precomp=None, shs=None):
     """Forward rasterization through ns_rasterize_forward. Every render mode but
-    0 (and level 0) reads the per-surfel rows `colors_precomp` (contiguous fp32).
+    0 (and level 0) reads the per-surfel rows `colors_precomp` (contiguous fp32);
+    level 0 may take SH coefficients `shs` [P, M, 3] instead (colours evaluated
+    at cfg.sh_degree from cfg.campos, C = 3).
 
     Returns (num_rendered, out_color [C,H,W], out_others [14,H,W] ([17,H,W] in
     mode 11), radii [P] int32, cover_pixels [P,1], trans_avg [P,1], scratch).
@@ -160,10 +166,13 @@ def rasterize_forward(cfg: RasterConfig, means3D, scales, rotations, opacities, 
     surf.features, surf.offsets, surf.gridrange = ptr(features), ptr(offsets), ptr(gridrange)
     surf.shapes = ptr(shapes)
     if cfg.uses_rows:
-        if colors_precomp is None:
+        if colors_precomp is None and (shs is None or cfg.render_mode != 0):
             raise ValueError(f"render_mode {cfg.render_mode} with {cfg.levels} levels needs colors_precomp")
-        _require_cuda(colors_precomp)
-        surf.colors_precomp = ptr(colors_precomp)
+        if colors_precomp is not None:
+            _require_cuda(colors_precomp)
+            surf.colors_precomp = ptr(colors_precomp)
+        else:
+            _set_shs(cfg, surf, shs, P)
     outs = _lib.RasterOutputs()
     outs.out_color, outs.out_others, outs.radii = ptr(out_color), ptr(out_others), ptr(radii)
     outs.cover_pixels = ptr(cover) if rec_P else None
@@ -185,6 +194,16 @@ def rasterize_forward(cfg: RasterConfig, means3D, scales, rotations, opacities, 
         check("ns_rasterize_forward", rc)
         break
     return int(n.value), out_color, out_others, radii, cover, trans, scratch
+
+
+def _set_shs(cfg: RasterConfig, surf, shs, P: int) -> None:
+    if shs.numel() % (3 * max(P, 1)) or shs.dtype != torch.float32 or not shs.is_contiguous():
+        raise ValueError("shs must be contiguous fp32 [P, M, 3]")
+    if cfg.campos is None:
+        raise ValueError("SH colours need cfg.campos (the camera centre, device [3])")
+    _require_cuda(shs, cfg.campos)
+    surf.shs = ptr(shs)
+    surf.sh_coeffs = shs.numel() // (3 * max(P, 1))
 
 
 def read_binning(scratch: Scratch, P: int, width: int, height: int, num_rendered: int) -> dict:
@@ -213,15 +232,17 @@ def read_binning(scratch: Scratch, P: int, width: int, height: int, num_rendered
 
 def rasterize_backward(cfg: RasterConfig, means3D, scales, rotations, opacities, homotrans, ap_level, features,
                        offsets, gridrange, radii, num_rendered: int, scratch: Scratch, dL_dcolor, dL_dothers,
-                       return_accumulators: bool = False, shapes=None, colors_precomp=None):
+                       return_accumulators: bool = False, shapes=None, colors_precomp=None, shs=None):
     """Backward rasterization (render_mode 0) through ns_rasterize_backward.
 
     `scratch` and every input must be the ones of the forward call. Returns a dict
     of fp32 gradients: means3D [P,3], means2D [P,3] (densification statistic),
     opacity [P,1], scales [P,2], rotations [P,4], table [rows, level_dim],
     gradsum [P,1]; for kernel_type 1-3 (`shapes` [P] as in the forward) also
-    shapes [P]; for render modes 4 / 12 / 14 (`colors_precomp` as in the forward)
-    also colors_precomp (same shape). With return_accumulators, also "accum": the render pass's
+    shapes [P]; for the modes that read per-surfel rows (`colors_precomp` as in
+    the forward) also colors_precomp (same shape); for level 0 from SH (`shs` as
+    in the forward) also shs [P, M, 3], the colour's mean gradient included in
+    means3D. With return_accumulators, also "accum": the render pass's
     per-surfel accumulators [P,20] (dL/dM 9, dL/dT[0].z, dL/dT[1].z, opacity,
     dL/dnormal 3, gradsum, dL/dmean2D 2, dL/dshape, 1 unused), for tests.
     """
@@ -246,7 +267,9 @@ def rasterize_backward(cfg: RasterConfig, means3D, scales, rotations, opacities,
         shapes = shapes.contiguous().float().reshape(-1)
         _require_cuda(shapes)
         g["shapes"] = torch.empty((P,), dtype=torch.float32, device=dev)
-    if cfg.uses_rows:
+    if cfg.uses_rows and colors_precomp is None and shs is not None and cfg.render_mode == 0:
+        g["shs"] = torch.zeros_like(shs)
+    elif cfg.uses_rows:
         if colors_precomp is None:
             raise ValueError(f"render_mode {cfg.render_mode} with {cfg.levels} levels needs colors_precomp")
         colors_precomp = colors_precomp.contiguous().float()
@@ -263,13 +286,16 @@ def rasterize_backward(cfg: RasterConfig, means3D, scales, rotations, opacities,
     surf.features, surf.offsets, surf.gridrange = ptr(features), ptr(offsets), ptr(gridrange)
     if cfg.kernel_type != 0:
         surf.shapes = ptr(shapes)
-    if cfg.uses_rows:
+    if "shs" in g:
+        _set_shs(cfg, surf, shs, P)
+    elif cfg.uses_rows:
         surf.colors_precomp = ptr(colors_precomp)
     gi = _lib.GradsIn(ptr(dL_dcolor), ptr(dL_dothers), ptr(radii))
     go = _lib.GradsOut(ptr(g["means3D"]), ptr(g["means2D"]), ptr(g["opacity"]), ptr(g["scales"]),
                        ptr(g["rotations"]), ptr(g["table"]), rows, ptr(g["gradsum"]),
                        ptr(g["shapes"]) if "shapes" in g else None,
-                       ptr(g["colors_precomp"]) if "colors_precomp" in g else None)
+                       ptr(g["colors_precomp"]) if "colors_precomp" in g else None,
+                       ptr(g["shs"]) if "shs" in g else None)
     nbytes = (lib.ns_backward_scratch_bytes_deterministic(P, rows, int(cfg.level_dim)) if cfg.deterministic
               else lib.ns_backward_scratch_bytes(P))
     acc = torch.empty(nbytes, dtype=torch.uint8, device=dev)

@@ -418,6 +418,20 @@ void oracle_render(int W, int H, const uint32_t* ranges, const uint32_t* point_l
   (void)kOthers;
 }
 
+// SH colours of P surfels (forward.cu:414-423 with computeColorFromSH, :21-74):
+// shs [P, M, 3], campos [3]; rgb [P, 3] (clamped at 0).
+void oracle_sh_color(int P, int deg, int M, const float* means3D, const float* campos, const float* shs,
+                     float* rgb) {
+#pragma omp parallel for schedule(static)
+  for (int i = 0; i < P; i++) {
+    F3 d = {means3D[3 * i] - campos[0], means3D[3 * i + 1] - campos[1], means3D[3 * i + 2] - campos[2]};
+    const float len = std::sqrt(d.x * d.x + d.y * d.y + d.z * d.z);
+    d = {d.x / len, d.y / len, d.z / len};
+    bool clamped[3];
+    sh_color(deg, shs + (size_t)i * M * 3, d, rgb + 3 * (size_t)i, clamped);
+  }
+}
+
 // Hash-grid lookup of a batch of points (hashgrid.h:53-212), exported for the
 // known-answer tests of grid_index and the trilinear gather.
 // level_exp2: NULL, or [L] values of exp2f(l S) to use instead of the host's.

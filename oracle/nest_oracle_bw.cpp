@@ -699,7 +699,117 @@ void preprocess_backward(int P, const float* means3D, const float* scales, const
 
 }  // namespace
 
+// backward.cu:21-140 (computeColorFromSH backward) for one surfel: dL/dsh
+// (written, M RGB triples) and the view-direction part of dL/dmean (added),
+// with the direction's normalisation through dnormvdv (auxiliary.h:133-143);
+// the colour gradient is cut where the forward clamped.
+template <typename R>
+void sh_color_backward(int deg, int M, const float* sh, V3<R> pos, V3<R> campos, const R dL_drgb_in[3],
+                       R* dL_dsh, R dL_dmean[3]) {
+  const R C0 = R(0.28209479177387814f), C1 = R(0.4886025119029199f);
+  const R C2[5] = {R(1.0925484305920792f), R(-1.0925484305920792f), R(0.31539156525252005f),
+                   R(-1.0925484305920792f), R(0.5462742152960396f)};
+  const R C3[7] = {R(-0.5900435899266435f), R(2.890611442640554f), R(-0.4570457994644658f),
+                   R(0.3731763325901154f), R(-0.4570457994644658f), R(1.445305721320277f),
+                   R(-0.5900435899266435f)};
+  const V3<R> d0 = {pos.x - campos.x, pos.y - campos.y, pos.z - campos.z};
+  const R len = std::sqrt(d0.x * d0.x + d0.y * d0.y + d0.z * d0.z);
+  const R x = d0.x / len, y = d0.y / len, z = d0.z / len;
+  // clamp of the forward, recomputed
+  float rgbf[3];
+  bool clamped[3];
+  oracle::sh_color(deg, sh, F3{(float)x, (float)y, (float)z}, rgbf, clamped);
+  R g[3];
+  for (int c = 0; c < 3; c++) g[c] = clamped[c] ? R(0) : dL_drgb_in[c];
+  for (int i = 0; i < 3 * M; i++) dL_dsh[i] = 0;
+  auto k = [&](int i, int c) { return (R)sh[3 * i + c]; };
+  R dx[3] = {0, 0, 0}, dy[3] = {0, 0, 0}, dz[3] = {0, 0, 0};
+  auto put = [&](int i, R b) { for (int c = 0; c < 3; c++) dL_dsh[3 * i + c] = b * g[c]; };
+  put(0, C0);
+  if (deg > 0) {
+    put(1, -C1 * y);
+    put(2, C1 * z);
+    put(3, -C1 * x);
+    for (int c = 0; c < 3; c++) {
+      dx[c] = -C1 * k(3, c);
+      dy[c] = -C1 * k(1, c);
+      dz[c] = C1 * k(2, c);
+    }
+    if (deg > 1) {
+      const R xx = x * x, yy = y * y, zz = z * z, xy = x * y, yz = y * z, xz = x * z;
+      put(4, C2[0] * xy);
+      put(5, C2[1] * yz);
+      put(6, C2[2] * (R(2) * zz - xx - yy));
+      put(7, C2[3] * xz);
+      put(8, C2[4] * (xx - yy));
+      for (int c = 0; c < 3; c++) {
+        dx[c] += C2[0] * y * k(4, c) + C2[2] * R(2) * -x * k(6, c) + C2[3] * z * k(7, c) + C2[4] * R(2) * x * k(8, c);
+        dy[c] += C2[0] * x * k(4, c) + C2[1] * z * k(5, c) + C2[2] * R(2) * -y * k(6, c) + C2[4] * R(2) * -y * k(8, c);
+        dz[c] += C2[1] * y * k(5, c) + C2[2] * R(2) * R(2) * z * k(6, c) + C2[3] * x * k(7, c);
+      }
+      if (deg > 2) {
+        put(9, C3[0] * y * (R(3) * xx - yy));
+        put(10, C3[1] * xy * z);
+        put(11, C3[2] * y * (R(4) * zz - xx - yy));
+        put(12, C3[3] * z * (R(2) * zz - R(3) * xx - R(3) * yy));
+        put(13, C3[4] * x * (R(4) * zz - xx - yy));
+        put(14, C3[5] * z * (xx - yy));
+        put(15, C3[6] * x * (xx - R(3) * yy));
+        for (int c = 0; c < 3; c++) {
+          dx[c] += C3[0] * k(9, c) * R(3) * R(2) * xy + C3[1] * k(10, c) * yz + C3[2] * k(11, c) * R(-2) * xy +
+                   C3[3] * k(12, c) * R(-3) * R(2) * xz + C3[4] * k(13, c) * (R(-3) * xx + R(4) * zz - yy) +
+                   C3[5] * k(14, c) * R(2) * xz + C3[6] * k(15, c) * R(3) * (xx - yy);
+          dy[c] += C3[0] * k(9, c) * R(3) * (xx - yy) + C3[1] * k(10, c) * xz +
+                   C3[2] * k(11, c) * (R(-3) * yy + R(4) * zz - xx) + C3[3] * k(12, c) * R(-3) * R(2) * yz +
+                   C3[4] * k(13, c) * R(-2) * xy + C3[5] * k(14, c) * R(-2) * yz + C3[6] * k(15, c) * R(-3) * R(2) * xy;
+          dz[c] += C3[1] * k(10, c) * xy + C3[2] * k(11, c) * R(4) * R(2) * yz +
+                   C3[3] * k(12, c) * R(3) * (R(2) * zz - xx - yy) + C3[4] * k(13, c) * R(4) * R(2) * xz +
+                   C3[5] * k(14, c) * (xx - yy);
+        }
+      }
+    }
+  }
+  const R ddx = dx[0] * g[0] + dx[1] * g[1] + dx[2] * g[2];
+  const R ddy = dy[0] * g[0] + dy[1] * g[1] + dy[2] * g[2];
+  const R ddz = dz[0] * g[0] + dz[1] * g[1] + dz[2] * g[2];
+  const R sum2 = d0.x * d0.x + d0.y * d0.y + d0.z * d0.z;
+  const R inv32 = R(1) / std::sqrt(sum2 * sum2 * sum2);
+  dL_dmean[0] += ((sum2 - d0.x * d0.x) * ddx - d0.y * d0.x * ddy - d0.z * d0.x * ddz) * inv32;
+  dL_dmean[1] += (-d0.x * d0.y * ddx + (sum2 - d0.y * d0.y) * ddy - d0.z * d0.y * ddz) * inv32;
+  dL_dmean[2] += (-d0.x * d0.z * ddx - d0.y * d0.z * ddy + (sum2 - d0.z * d0.z) * ddz) * inv32;
+}
+
+template <typename R>
+void sh_color_backward_all(int P, int deg, int M, const float* means3D, const float* campos, const float* shs,
+                           const int* radii, const R* dL_drgb, R* dL_dshs, R* dL_dmeans) {
+#pragma omp parallel for schedule(static)
+  for (int i = 0; i < P; i++) {
+    R* dsh = dL_dshs + (size_t)i * M * 3;
+    if (!(radii[i] > 0)) {
+      for (int j = 0; j < 3 * M; j++) dsh[j] = 0;
+      continue;
+    }
+    const V3<R> pos = {means3D[3 * i], means3D[3 * i + 1], means3D[3 * i + 2]};
+    const V3<R> cp = {campos[0], campos[1], campos[2]};
+    sh_color_backward<R>(deg, M, shs + (size_t)i * M * 3, pos, cp, dL_drgb + 3 * (size_t)i, dsh,
+                         dL_dmeans + 3 * (size_t)i);
+  }
+}
+
 extern "C" {
+
+// SH colour backward of P surfels (preprocess backward, backward.cu:2267 with
+// computeColorFromSH, :21-140): dL_dshs [P, M, 3] written (zero where radii <=
+// 0), dL_dmeans [P, 3] added to.
+void oracle_sh_color_backward(int P, int deg, int M, const float* means3D, const float* campos, const float* shs,
+                              const int* radii, const float* dL_drgb, float* dL_dshs, float* dL_dmeans) {
+  sh_color_backward_all<float>(P, deg, M, means3D, campos, shs, radii, dL_drgb, dL_dshs, dL_dmeans);
+}
+void oracle_sh_color_backward_f64(int P, int deg, int M, const float* means3D, const float* campos,
+                                  const float* shs, const int* radii, const double* dL_drgb, double* dL_dshs,
+                                  double* dL_dmeans) {
+  sh_color_backward_all<double>(P, deg, M, means3D, campos, shs, radii, dL_drgb, dL_dshs, dL_dmeans);
+}
 
 // Working precision float: the reference's arithmetic, the parity checker.
 void oracle_render_backward(int W, int H, const uint32_t* ranges, const uint32_t* point_list,

@@ -57,6 +57,9 @@ def load() -> C.CDLL:
     lib.oracle_query.argtypes = [i32, vp, vp, vp, vp, f32, f32, i32, i32, u32, f32, u32, i32, u32, i32, vp, vp]
     lib.oracle_query_backward.argtypes = [i32, vp, vp, vp, vp, f32, f32, i32, i32, u32, f32, u32, i32, u32, i32,
                                           vp, vp, vp, vp]
+    lib.oracle_sh_color.argtypes = [i32, i32, i32, vp, vp, vp, vp]
+    lib.oracle_sh_color_backward.argtypes = [i32, i32, i32, vp, vp, vp, vp, vp, vp, vp]
+    lib.oracle_sh_color_backward_f64.argtypes = [i32, i32, i32, vp, vp, vp, vp, vp, vp, vp]
     lib.oracle_grid_index.restype = u32
     lib.oracle_grid_index.argtypes = [i32, u32, u32, u32, u32, u32]
     lib.oracle_rvq_decode.argtypes = [i64, i32, i32, i32, vp, vp, vp]
@@ -165,6 +168,35 @@ def query(xyz, ap_level, table_f32, offsets, vmin, vmax, C_out, LD, L, S, Hres, 
                      float(vmin), float(vmax), int(C_out), int(LD), int(L), float(S), int(Hres),
                      int(bool(align_corners)), int(interp), int(bool(contract)), _p(lexp), _p(out))
     return out
+
+
+def sh_color(means3D, campos, shs, deg):
+    """computeColorFromSH (forward.cu:21-74) of every surfel: shs [P, M, 3]
+    (coefficient-major RGB triples), campos [3]; returns rgb [P, 3]."""
+    lib = load()
+    means3D, campos, shs = _f32(means3D).reshape(-1, 3), _f32(campos).reshape(3), _f32(shs)
+    P = means3D.shape[0]
+    M = shs.reshape(P, -1, 3).shape[1] if P else 1
+    rgb = np.zeros((P, 3), np.float32)
+    lib.oracle_sh_color(P, int(deg), int(M), _p(means3D), _p(campos), _p(shs), _p(rgb))
+    return rgb
+
+
+def sh_color_backward(means3D, campos, shs, deg, radii, dL_drgb, f64=False):
+    """The SH colour's backward (backward.cu:21-140): returns (dL_dshs [P, M, 3],
+    dL_dmeans [P, 3], the view-direction part), zero where radii <= 0."""
+    lib = load()
+    means3D, campos, shs = _f32(means3D).reshape(-1, 3), _f32(campos).reshape(3), _f32(shs)
+    P = means3D.shape[0]
+    M = shs.reshape(P, -1, 3).shape[1] if P else 1
+    dt = np.float64 if f64 else np.float32
+    g = np.ascontiguousarray(np.asarray(dL_drgb, dt).reshape(P, 3))
+    dsh = np.zeros((P, M, 3), dt)
+    dmean = np.zeros((P, 3), dt)
+    fn = lib.oracle_sh_color_backward_f64 if f64 else lib.oracle_sh_color_backward
+    fn(P, int(deg), int(M), _p(means3D), _p(campos), _p(shs),
+       _p(np.ascontiguousarray(np.asarray(radii, np.int32))), _p(g), _p(dsh), _p(dmean))
+    return dsh, dmean
 
 
 def query_backward(xyz, ap_level, table_f32, offsets, vmin, vmax, C_out, LD, L, S, Hres, grad_feat,

@@ -177,6 +177,40 @@ inline void eval_sh_interleaved(int deg, const float* sh, F3 dir, float* out) {
   for (int c = 0; c < 3; c++) out[c] = std::fmax(out[c], 0.0f);
 }
 
+// The 3D Gaussian splatting SH colour of a surfel (forward.cu:21-74,
+// computeColorFromSH): sh holds M coefficients as RGB triples (coefficient k
+// at 3 k), dir the unit direction from the camera centre to the mean; degree
+// deg <= 3 terms, + 0.5, clamped at 0 (clamped[c]: the sum was negative).
+inline void sh_color(int deg, const float* sh, F3 dir, float* out, bool* clamped) {
+  const float C0 = 0.28209479177387814f, C1 = 0.4886025119029199f;
+  const float C2[5] = {1.0925484305920792f, -1.0925484305920792f, 0.31539156525252005f,
+                       -1.0925484305920792f, 0.5462742152960396f};
+  const float C3[7] = {-0.5900435899266435f, 2.890611442640554f, -0.4570457994644658f,
+                       0.3731763325901154f, -0.4570457994644658f, 1.445305721320277f,
+                       -0.5900435899266435f};
+  const float x = dir.x, y = dir.y, z = dir.z;
+  const float xx = x * x, yy = y * y, zz = z * z, xy = x * y, yz = y * z, xz = x * z;
+  for (int c = 0; c < 3; c++) {
+    auto k = [&](int i) { return sh[3 * i + c]; };
+    float r = C0 * k(0);
+    if (deg > 0) {
+      r = r - C1 * y * k(1) + C1 * z * k(2) - C1 * x * k(3);
+      if (deg > 1) {
+        r = r + C2[0] * xy * k(4) + C2[1] * yz * k(5) + C2[2] * (2.0f * zz - xx - yy) * k(6) +
+            C2[3] * xz * k(7) + C2[4] * (xx - yy) * k(8);
+        if (deg > 2)
+          r = r + C3[0] * y * (3.0f * xx - yy) * k(9) + C3[1] * xy * z * k(10) +
+              C3[2] * y * (4.0f * zz - xx - yy) * k(11) + C3[3] * z * (2.0f * zz - 3.0f * xx - 3.0f * yy) * k(12) +
+              C3[4] * x * (4.0f * zz - xx - yy) * k(13) + C3[5] * z * (xx - yy) * k(14) +
+              C3[6] * x * (xx - 3.0f * yy) * k(15);
+      }
+    }
+    r += 0.5f;
+    clamped[c] = r < 0;
+    out[c] = std::fmax(r, 0.0f);
+  }
+}
+
 // Render modes 8 (hybrid_SH), 9 (hybrid_SH_post) and 10 (hybrid_SH_raw),
 // forward.cu:1378-1526: the sample's feature from the surfel's row `g` (3 raw
 // SH colours; 48 SH coefficients for mode 9) and h, the single-level, 3-wide

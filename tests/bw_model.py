@@ -126,21 +126,27 @@ SH_C3 = (-0.5900435899266435, 2.890611442640554, -0.4570457994644658, 0.37317633
          1.445305721320277, -0.5900435899266435)
 
 
-def eval_sh_interleaved(sh, d):
-    """Degree-3 SH colour [n, 3] of 48 coefficients read interleaved (coefficient
-    k of channel c at 3 k + c) along unit directions d [n, 3], + 0.5 on the DC
-    term and clamped at 0 (forward.cu:76-155, render mode 11)."""
+def eval_sh_interleaved(sh, d, deg=3):
+    """SH colour [n, 3] of coefficients read interleaved (coefficient k of
+    channel c at 3 k + c; sh [3 M] shared by all rows or [n, 3 M]) along unit
+    directions d [n, 3], degree `deg` terms, + 0.5 and clamped at 0
+    (forward.cu:21-74 computeColorFromSH, :76-155 for render mode 11)."""
     x, y, z = d[:, 0:1], d[:, 1:2], d[:, 2:3]
-    c = lambda k: sh[3 * k:3 * k + 3][None, :]  # noqa: E731
+    sh = sh[None, :] if sh.dim() == 1 else sh
+    c = lambda k: sh[:, 3 * k:3 * k + 3]  # noqa: E731
     xx, yy, zz, xy, yz, xz = x * x, y * y, z * z, x * y, y * z, x * z
-    r = SH_C0 * c(0) + 0.5 - SH_C1 * y * c(1) + SH_C1 * z * c(2) - SH_C1 * x * c(3)
-    r = (r + SH_C2[0] * xy * c(4) + SH_C2[1] * yz * c(5) + SH_C2[2] * (2 * zz - xx - yy) * c(6)
-         + SH_C2[3] * xz * c(7) + SH_C2[4] * (xx - yy) * c(8))
-    r = (r + SH_C3[0] * y * (3 * xx - yy) * c(9) + SH_C3[1] * xy * z * c(10)
-         + SH_C3[2] * y * (4 * zz - xx - yy) * c(11) + SH_C3[3] * z * (2 * zz - 3 * xx - 3 * yy) * c(12)
-         + SH_C3[4] * x * (4 * zz - xx - yy) * c(13) + SH_C3[5] * z * (xx - yy) * c(14)
-         + SH_C3[6] * x * (xx - 3 * yy) * c(15))
-    return torch.clamp_min(r, 0.0)
+    r = SH_C0 * c(0)
+    if deg > 0:
+        r = r - SH_C1 * y * c(1) + SH_C1 * z * c(2) - SH_C1 * x * c(3)
+    if deg > 1:
+        r = (r + SH_C2[0] * xy * c(4) + SH_C2[1] * yz * c(5) + SH_C2[2] * (2 * zz - xx - yy) * c(6)
+             + SH_C2[3] * xz * c(7) + SH_C2[4] * (xx - yy) * c(8))
+    if deg > 2:
+        r = (r + SH_C3[0] * y * (3 * xx - yy) * c(9) + SH_C3[1] * xy * z * c(10)
+             + SH_C3[2] * y * (4 * zz - xx - yy) * c(11) + SH_C3[3] * z * (2 * zz - 3 * xx - 3 * yy) * c(12)
+             + SH_C3[4] * x * (4 * zz - xx - yy) * c(13) + SH_C3[5] * z * (xx - yy) * c(14)
+             + SH_C3[6] * x * (xx - 3 * yy) * c(15))
+    return torch.clamp_min(r + 0.5, 0.0)
 
 
 def sh_hybrid_feature(h, row, mode, decompose):

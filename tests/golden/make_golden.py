@@ -10,7 +10,10 @@ It imports, unmodified:
     gaussian_model.py:312-317 (get_homotrans);
   * utils/point_utils.py: depths_to_points, depth_to_normal -> the per-pixel
     rays, world points and surf_normal of the render_pkg decode
-    (gaussian_renderer/__init__.py:789-792), on two small cameras.
+    (gaussian_renderer/__init__.py:789-792), on two small cameras;
+  * utils/sh_utils.py: eval_sh -> the SH colour basis (degrees 0-3) of 64
+    surfels seen from one camera centre, the sum the rasterizer's
+    computeColorFromSH forms before its + 0.5 and clamp.
 These functions hard-code device='cuda'; with no GPU in the generating
 container they are run on CPU by redirecting torch.zeros / torch.arange
 (device='cuda') and Tensor.cuda() to CPU for the duration of the call
@@ -146,6 +149,20 @@ def main(ref_root: str) -> None:
         data[f"pu{i}_rays_o"] = rays_o.numpy()
         data[f"pu{i}_points"] = points.numpy()
         data[f"pu{i}_normal"] = normal.numpy()
+    # SH colours: GaussianModel's features [N, 16, 3] (DC then rest), viewed as the
+    # renderer does for eval_sh ([N, 3, 16]), along the unit direction camera -> mean.
+    from utils import sh_utils  # noqa: E402
+    g = torch.Generator().manual_seed(321)
+    shs = torch.randn(64, 16, 3, generator=g) * 0.6
+    means = torch.randn(64, 3, generator=g)
+    campos = torch.tensor([0.3, -4.0, 0.8])
+    dirs = means - campos
+    dirs = dirs / dirs.norm(dim=1, keepdim=True)
+    data["sh_shs"] = shs.numpy()
+    data["sh_means"] = means.numpy()
+    data["sh_campos"] = campos.numpy()
+    for deg in range(4):
+        data[f"sh_eval_deg{deg}"] = sh_utils.eval_sh(deg, shs.transpose(1, 2), dirs).numpy()
     np.savez(OUT, **data)
     print("wrote", OUT)
 

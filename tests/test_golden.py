@@ -56,3 +56,16 @@ def test_depth_to_normal_matches_reference_point_utils():
         assert np.array_equal(rays_o.numpy(), GOLD[f"pu{i}_rays_o"])
         assert np.array_equal(train.depths_to_points(cam, depth).numpy(), GOLD[f"pu{i}_points"])
         assert np.array_equal(train.depth_to_normal(cam, depth).numpy(), GOLD[f"pu{i}_normal"])
+
+
+def test_oracle_sh_color_matches_reference_eval_sh():
+    """The oracle's computeColorFromSH (forward.cu:21-74) against the reference's
+    own utils/sh_utils.py eval_sh (tests/golden/make_golden.py), degrees 0-3:
+    the same basis and sum, then + 0.5 and the clamp at 0."""
+    from oracle import oracle
+    shs, means, campos = GOLD["sh_shs"], GOLD["sh_means"], GOLD["sh_campos"]
+    for deg in range(4):
+        got = oracle.sh_color(means, campos, shs, deg)
+        want = np.maximum(GOLD[f"sh_eval_deg{deg}"] + 0.5, 0.0)
+        assert np.abs(got - want).max() < 2e-6, (deg, np.abs(got - want).max())
+        assert (GOLD[f"sh_eval_deg{deg}"] + 0.5 < 0).any() or deg == 0  # the clamp is exercised

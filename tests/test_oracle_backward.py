@@ -279,3 +279,36 @@ def test_oracle_residual_hybrid_mode_11():
     for k, got in checks.items():
         assert np.linalg.norm(mg[k]) > 0, k
         assert rel_l2(got, mg[k]) < 1e-4, (k, rel_l2(got, mg[k]))
+
+
+@pytest.mark.parametrize("deg", [0, 1, 2, 3])
+def test_oracle_sh_color_backward_matches_autograd(deg):
+    """computeColorFromSH's backward (backward.cu:21-140, dnormvdv): dL/dsh and
+    the mean's view-direction gradient against float64 autograd of the SH
+    colour (clamped channels pass no gradient); culled surfels get zeros."""
+    g = torch.Generator().manual_seed(90 + deg)
+    P, M = 50, 16
+    shs = (torch.randn(P, M, 3, generator=g) * 0.6).float()
+    means = torch.randn(P, 3, generator=g).float()
+    campos = torch.tensor([0.3, -4.0, 0.8])
+    radii = np.ones(P, np.int32)
+    radii[::7] = 0
+    up = torch.randn(P, 3, generator=g).double()
+    m = means.double().requires_grad_(True)
+    sh = shs.double().reshape(P, -1).requires_grad_(True)
+    d = m - campos.double()
+    d = d / d.norm(dim=1, keepdim=True)
+    rgb = bw_model.eval_sh_interleaved(sh, d, deg)
+    assert np.abs(rgb.detach().numpy() - oracle.sh_color(means.numpy(), campos.numpy(), shs.numpy(), deg)).max() < 1e-5
+    (rgb * up).sum().backward()
+    dsh, dmean = oracle.sh_color_backward(means.numpy(), campos.numpy(), shs.numpy(), deg, radii, up.numpy())
+    on = radii > 0
+    want_sh = sh.grad.numpy().reshape(P, M, 3)
+    assert not dsh[~on].any() and not dmean[~on].any()
+    assert rel_l2(dsh[on], want_sh[on]) < 1e-5, rel_l2(dsh[on], want_sh[on])
+    if deg > 0:
+        assert rel_l2(dmean[on], m.grad.numpy()[on]) < 1e-4, rel_l2(dmean[on], m.grad.numpy()[on])
+    else:
+        assert np.abs(dmean).max() < 1e-6
+    d64, m64 = oracle.sh_color_backward(means.numpy(), campos.numpy(), shs.numpy(), deg, radii, up.numpy(), f64=True)
+    assert rel_l2(d64[on], want_sh[on]) < 1e-7  # the constants are the reference's float values
