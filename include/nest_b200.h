@@ -162,6 +162,13 @@ typedef struct ns_surfels {
   const float* shs;       /* [P, sh_coeffs, 3] SH coefficients (RGB triples per
                              coefficient), read for the level-0 SH colours, else NULL */
   int32_t sh_coeffs;      /* M >= (sh_degree + 1)^2 */
+  const float* transmat_precomp; /* [P, 9] precomputed splat-to-pixel transforms (columns
+                             Tu, Tv, Tw; the reference's transMat_precomp /
+                             cov3D_precomp, forward.cu:366-380), else NULL: with
+                             them scales and rotations may be NULL, homotrans is
+                             required, the normal is the view axis and the
+                             backward writes dL_dtransmat_precomp instead of mean,
+                             scale and rotation gradients (zeros) */
 } ns_surfels;
 
 /* Outputs (caller-owned, device). cover_pixels / trans_avg may be NULL when
@@ -238,6 +245,9 @@ typedef struct ns_raster_grads_out {
                            whose SH colour has no gradient), else NULL */
   float* dL_dshs;       /* [P, sh_coeffs, 3] with the SH colours (written, zero
                            where radii <= 0; backward.cu:21-140), else NULL */
+  float* dL_dtransmat_precomp; /* [P, 9] with ns_surfels.transmat_precomp (written;
+                           the render pass's dL/dT plus the centre's term,
+                           backward.cu:2128-2158), else NULL */
 } ns_raster_grads_out;
 
 /* Scratch of the backward pass: per-surfel gradient accumulators. */

@@ -926,18 +926,26 @@ __global__ void __launch_bounds__(kThreads, 2) blend_backward_kernel(const Backw
           dmy = dL_dG * (dG_factor_2d * dy);
           dTw.z = dL_dz;
         }
-        // dL/dM column c = sum_k P[k] dL/dT[k][c] + dL/dhomotrans column c.
+        // dL/dM column c = sum_k P[k] dL/dT[k][c] + dL/dhomotrans column c; with
+        // precomputed transforms (p.raw_T) dL/dT itself, columns Tu, Tv, Tw (the
+        // homotrans gradient has no destination there, as in the reference).
         float4* ga = reinterpret_cast<float4*>(p.accum + (size_t)S.ids[jj] * kGradWords);
-        atomicAdd(ga + 0, make_float4(P00 * dTu.x + P10 * dTv.x + P20 * dTw.x + h0x,
-                                      P01 * dTu.x + P11 * dTv.x + P21 * dTw.x + h0y,
-                                      P02 * dTu.x + P12 * dTv.x + P22 * dTw.x + h0z,
-                                      P00 * dTu.y + P10 * dTv.y + P20 * dTw.y + h1x));
-        atomicAdd(ga + 1, make_float4(P01 * dTu.y + P11 * dTv.y + P21 * dTw.y + h1y,
-                                      P02 * dTu.y + P12 * dTv.y + P22 * dTw.y + h1z,
-                                      P00 * dTu.z + P10 * dTv.z + P20 * dTw.z + h2x,
-                                      P01 * dTu.z + P11 * dTv.z + P21 * dTw.z + h2y));
-        atomicAdd(ga + 2, make_float4(P02 * dTu.z + P12 * dTv.z + P22 * dTw.z + h2z, tuz, tvz,
-                                      G * dL_dalpha));
+        if (p.raw_T) {
+          atomicAdd(ga + 0, make_float4(dTu.x, dTu.y, dTu.z, dTv.x));
+          atomicAdd(ga + 1, make_float4(dTv.y, dTv.z, dTw.x, dTw.y));
+          atomicAdd(ga + 2, make_float4(dTw.z, tuz, tvz, G * dL_dalpha));
+        } else {
+          atomicAdd(ga + 0, make_float4(P00 * dTu.x + P10 * dTv.x + P20 * dTw.x + h0x,
+                                        P01 * dTu.x + P11 * dTv.x + P21 * dTw.x + h0y,
+                                        P02 * dTu.x + P12 * dTv.x + P22 * dTw.x + h0z,
+                                        P00 * dTu.y + P10 * dTv.y + P20 * dTw.y + h1x));
+          atomicAdd(ga + 1, make_float4(P01 * dTu.y + P11 * dTv.y + P21 * dTw.y + h1y,
+                                        P02 * dTu.y + P12 * dTv.y + P22 * dTw.y + h1z,
+                                        P00 * dTu.z + P10 * dTv.z + P20 * dTw.z + h2x,
+                                        P01 * dTu.z + P11 * dTv.z + P21 * dTw.z + h2y));
+          atomicAdd(ga + 2, make_float4(P02 * dTu.z + P12 * dTv.z + P22 * dTw.z + h2z, tuz, tvz,
+                                        G * dL_dalpha));
+        }
         // level 0 adds nothing to the densification sum (backward.cu:833-849)
         const float gsum = (kAnyKernel && p.render_mode == 0 && p.L == 0) ? 0.f : aT * gabs;
         atomicAdd(ga + 3, make_float4(aT * dn0, aT * dn1, aT * dn2, gsum));
@@ -961,7 +969,8 @@ __global__ void __launch_bounds__(256)
 preprocess_backward_kernel(int P, const float* __restrict__ means3D, const float* __restrict__ scales,
                            const float* __restrict__ rotations, const int32_t* __restrict__ radii,
                            const float* __restrict__ viewmatrix, const float* __restrict__ projmatrix,
-                           int Wq, int Hq, const float* __restrict__ accum, ns_raster_grads_out o) {
+                           int Wq, int Hq, const float* __restrict__ accum, const float* __restrict__ Ts,
+                           ns_raster_grads_out o) {
   __shared__ float vm[16], Pm[3][4];
   if (threadIdx.x < 16) vm[threadIdx.x] = viewmatrix[threadIdx.x];
   if (threadIdx.x >= 32 && threadIdx.x < 44) {
@@ -987,6 +996,8 @@ preprocess_backward_kernel(int P, const float* __restrict__ means3D, const float
     o.dL_dopacity[i] = 0.f;
     o.dL_gradsum[i] = 0.f;
     if (o.dL_dshapes) o.dL_dshapes[i] = 0.f;
+    if (Ts)
+      for (int k = 0; k < 9; k++) o.dL_dtransmat_precomp[9 * (size_t)i + k] = 0.f;
     return;
   }
   const float4* a4 = reinterpret_cast<const float4*>(accum + (size_t)i * kGradWords);
@@ -998,6 +1009,53 @@ preprocess_backward_kernel(int P, const float* __restrict__ means3D, const float
     a[4 * q + 1] = v.y;
     a[4 * q + 2] = v.z;
     a[4 * q + 3] = v.w;
+  }
+  if (Ts) {
+    // Precomputed transforms (backward.cu:2082-2088, 2128-2158): the render
+    // pass's dL/dT plus, where the centre moved, the compute_aabb term (t = (9,
+    // 9, -1)), written as the transforms' gradient; nothing reaches the mean,
+    // scales or rotations; the densification statistic reads the updated dL/dT.
+    float T[3][3], dT[3][3];
+#pragma unroll
+    for (int c = 0; c < 3; c++)
+#pragma unroll
+      for (int r = 0; r < 3; r++) {
+        T[c][r] = Ts[9 * (size_t)i + 3 * c + r];
+        dT[c][r] = a[kGM + 3 * c + r];
+      }
+    const float gx = a[kGMean2D], gy = a[kGMean2D + 1];
+    if (gx != 0.f || gy != 0.f) {
+      const float tv[3] = {9.0f, 9.0f, -1.0f};
+      const float d = tv[0] * (T[2][0] * T[2][0]) + tv[1] * (T[2][1] * T[2][1]) + tv[2] * (T[2][2] * T[2][2]);
+      const float id = 1.0f / d;
+      float dL_df_dot = 0.f, add2[3];
+#pragma unroll
+      for (int r = 0; r < 3; r++) {
+        const float fv = tv[r] * id;
+        dT[0][r] += gx * fv * T[2][r];
+        dT[1][r] += gy * fv * T[2][r];
+        add2[r] = gx * fv * T[0][r] + gy * fv * T[1][r];
+        dL_df_dot += (gx * T[0][r] * T[2][r] + gy * T[1][r] * T[2][r]) * fv;
+      }
+      const float dL_dd = (float)((double)dL_df_dot * (-1.0 / (double)d));
+#pragma unroll
+      for (int r = 0; r < 3; r++) dT[2][r] += add2[r] + dL_dd * (tv[r] * T[2][r] * 2.0f);
+    }
+#pragma unroll
+    for (int c = 0; c < 3; c++)
+#pragma unroll
+      for (int r = 0; r < 3; r++) o.dL_dtransmat_precomp[9 * (size_t)i + 3 * c + r] = dT[c][r];
+    dmean[0] = dmean[1] = dmean[2] = 0.f;
+    dscale[0] = dscale[1] = 0.f;
+    drot[0] = drot[1] = drot[2] = drot[3] = 0.f;
+    const float depth = T[2][2];
+    dm2[0] = (float)((double)(dT[0][2] * depth) * 0.5 * (double)Wq);
+    dm2[1] = (float)((double)(dT[1][2] * depth) * 0.5 * (double)Hq);
+    dm2[2] = 0.f;
+    o.dL_dopacity[i] = a[kGOpacity];
+    o.dL_gradsum[i] = a[kGGradSum];
+    if (o.dL_dshapes) o.dL_dshapes[i] = a[kGShape];
+    return;
   }
   const float3 pm_ = f3(means3D[3 * i], means3D[3 * i + 1], means3D[3 * i + 2]);
   const float4 q = make_float4(rotations[4 * i], rotations[4 * i + 1], rotations[4 * i + 2],
@@ -1189,11 +1247,11 @@ int blend_backward_launch(const BackwardParams& p, int fp16, cudaStream_t stream
 
 int preprocess_backward_launch(int P, const float* means3D, const float* scales,
                                const float* rotations, const int32_t* radii, const float* vm,
-                               const float* pm, int Wq, int Hq, const float* accum,
+                               const float* pm, int Wq, int Hq, const float* accum, const float* Ts,
                                const ns_raster_grads_out& o, cudaStream_t stream) {
   if (P <= 0) return NS_OK;
   preprocess_backward_kernel<<<div_up(P, 256), 256, 0, stream>>>(P, means3D, scales, rotations,
-                                                                  radii, vm, pm, Wq, Hq, accum, o);
+                                                                  radii, vm, pm, Wq, Hq, accum, Ts, o);
   NS_LAUNCH_CHECK();
   return NS_OK;
 }

@@ -360,8 +360,12 @@ int ns_rasterize_forward(const ns_raster_settings* settings, const ns_surfels* s
   if (P < 0) return NS_ERR_INVALID;
   if (num_rendered) *num_rendered = 0;
   if (P == 0) return NS_OK;
-  if (!surfels->means3D || !surfels->scales || !surfels->rotations || !surfels->opacities ||
-      !surfels->features || !surfels->offsets || !surfels->gridrange)
+  // precomputed transforms replace scales and rotations, and need the homotrans
+  // that places the hit point (transMat_precomp, forward.cu:366-380)
+  const bool given_T = surfels->transmat_precomp != nullptr;
+  if (!surfels->means3D || (!given_T && (!surfels->scales || !surfels->rotations)) ||
+      (given_T && !surfels->homotrans) || !surfels->opacities || !surfels->features || !surfels->offsets ||
+      !surfels->gridrange)
     return NS_ERR_INVALID;
   if (!outputs->out_color || !outputs->out_others || !outputs->radii) return NS_ERR_INVALID;
   if (settings->kernel_type != 0 && P > 0 && !surfels->shapes) return NS_ERR_INVALID;
@@ -489,7 +493,9 @@ int ns_rasterize_backward(const ns_raster_settings* settings, const ns_surfels* 
     NS_CUDA_TRY(cudaMemsetAsync(go->dL_dtable, 0,
                                 (size_t)go->table_rows * settings->level_dim * sizeof(float), stream));
   if (P == 0) return NS_OK;
-  if (!surfels->means3D || !surfels->scales || !surfels->rotations || !surfels->features ||
+  const bool given_T = surfels->transmat_precomp != nullptr;
+  if (!surfels->means3D || (!given_T && (!surfels->scales || !surfels->rotations)) ||
+      (given_T && (!surfels->homotrans || !go->dL_dtransmat_precomp)) || !surfels->features ||
       !surfels->offsets || !surfels->gridrange)
     return NS_ERR_INVALID;
   if (!gi->dL_dout_color || !gi->dL_dout_others || !gi->radii) return NS_ERR_INVALID;
@@ -558,7 +564,8 @@ int ns_rasterize_backward(const ns_raster_settings* settings, const ns_surfels* 
   // The ray/plane form of the hit-point gradient equals the reference's form
   // when the blended transform and the preprocess backward's rebuilt transform
   // are the same matrix: scale_modifier 1 and the same image size.
-  bp.ray_hit = (settings->scale_modifier == 1.0f && Wq == W && Hq == H) ? 1 : 0;
+  bp.ray_hit = (!given_T && settings->scale_modifier == 1.0f && Wq == W && Hq == H) ? 1 : 0;
+  bp.raw_T = given_T ? 1 : 0;
   bp.ranges = im.ranges;
   bp.tile_order = im.order;
   bp.point_list = b.vals_sorted;
@@ -581,7 +588,8 @@ int ns_rasterize_backward(const ns_raster_settings* settings, const ns_surfels* 
     if (rc) return rc;
   }
   rc = preprocess_backward_launch(P, surfels->means3D, surfels->scales, surfels->rotations, gi->radii,
-                                  settings->viewmatrix, settings->projmatrix, Wq, Hq, accum, *go, stream);
+                                  settings->viewmatrix, settings->projmatrix, Wq, Hq, accum,
+                                  surfels->transmat_precomp, *go, stream);
   if (rc || !shc) return rc;
   // computeColorFromSH's backward after the mean gradient is written (it adds to it)
   return sh_color_backward_launch(P, settings->sh_degree, surfels->sh_coeffs, surfels->means3D, settings->campos,

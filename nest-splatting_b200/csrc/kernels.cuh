@@ -74,6 +74,7 @@ struct BackwardParams {
   const float* projmatrix;
   const float* viewmatrix;
   int ray_hit;                // 1: hit-point gradient in the ray/plane form (see backward.cu)
+  int raw_T;                  // 1: precomputed transforms, accumulate dL/dT itself (not folded into dL/dM)
   const uint2* ranges;
   const uint32_t* tile_order;  // blockIdx.x -> tile (heaviest first), or NULL: row-major
   const uint32_t* point_list;
@@ -104,7 +105,7 @@ int table_grad_finish_launch(const unsigned long long* fx, size_t n, const uint3
 int blend_backward_launch(const BackwardParams& p, int fp16, cudaStream_t stream);
 int preprocess_backward_launch(int P, const float* means3D, const float* scales,
                                const float* rotations, const int32_t* radii, const float* vm,
-                               const float* pm, int Wq, int Hq, const float* accum,
+                               const float* pm, int Wq, int Hq, const float* accum, const float* Ts,
                                const ns_raster_grads_out& o, cudaStream_t stream);
 int rvq_decode_launch(const uint8_t*, const float*, float*, int64_t, int, int, int, cudaStream_t);
 int wait_selftest_launch(const uint32_t* flag, uint32_t* err, cudaStream_t stream);

@@ -29,6 +29,8 @@ struct SurfelIn {
   float3 su, sv, pk;  // homotrans columns 0, 1 and translation
   float ap;
   float shape;        // kernel parameter (kernel types 1-3)
+  bool given_T;       // precomputed transform (Tu, Tv, Tw below), scale / rotation unused
+  float3 Tu, Tv, Tw;
 };
 
 struct ApiAttrs {
@@ -39,13 +41,23 @@ struct ApiAttrs {
   const float* homotrans;
   const float* ap_level;
   const float* shapes;
+  const float* transmats;  // [P, 9] precomputed transforms, or NULL (then scales / rotations are read)
   __device__ SurfelIn load(int i) const {
     SurfelIn a;
     a.shape = shapes ? shapes[i] : 0.0f;
     a.p = f3(means3D[3 * i], means3D[3 * i + 1], means3D[3 * i + 2]);
-    a.s = make_float2(scales[2 * i], scales[2 * i + 1]);
-    a.q = make_float4(rotations[4 * i], rotations[4 * i + 1], rotations[4 * i + 2],
-                      rotations[4 * i + 3]);
+    a.given_T = transmats != nullptr;
+    if (a.given_T) {
+      const float* t = transmats + 9 * (size_t)i;
+      a.Tu = f3(t[0], t[1], t[2]);
+      a.Tv = f3(t[3], t[4], t[5]);
+      a.Tw = f3(t[6], t[7], t[8]);
+      a.s = make_float2(0.f, 0.f);
+      a.q = make_float4(1.f, 0.f, 0.f, 0.f);
+    } else {
+      a.s = make_float2(scales[2 * i], scales[2 * i + 1]);
+      a.q = make_float4(rotations[4 * i], rotations[4 * i + 1], rotations[4 * i + 2], rotations[4 * i + 3]);
+    }
     a.opacity = opacities[i];
     if (homotrans) {
       const float* h = homotrans + 16 * (size_t)i;
@@ -80,6 +92,7 @@ struct MixAttrs {
     float raw[10];
     SurfelIn a;
     a.shape = 0.0f;
+    a.given_T = false;
 #pragma unroll
     for (int k = 0; k < 10; k++) raw[k] = b[k] + mix * d[k];
     a.p = f3(raw[0], raw[1], raw[2]);
@@ -166,6 +179,14 @@ __device__ __forceinline__ uint32_t preprocess_one(const SurfelIn& a, float mod,
                        vm[2] * a.p.x + vm[6] * a.p.y + vm[10] * a.p.z + vm[14]);
   if (pv.z <= 0.2f) return 0;
 
+  float3 Tu, Tv, Tw, n;
+  if (a.given_T) {
+    // precomputed transform (forward.cu:366-380): the normal is the view axis
+    Tu = a.Tu;
+    Tv = a.Tv;
+    Tw = a.Tw;
+    n = f3(0.f, 0.f, 1.f);
+  } else {
   // quat_to_rotmat (rsqrt-normalised) -> L = R * diag(mod*s.x, mod*s.y, 1).
   const float qs = rsqrtf(a.q.w * a.q.w + a.q.x * a.q.x + a.q.y * a.q.y + a.q.z * a.q.z);
   const float w = a.q.x * qs, x = a.q.y * qs, y = a.q.z * qs, z = a.q.w * qs;
@@ -185,20 +206,20 @@ __device__ __forceinline__ uint32_t preprocess_one(const SurfelIn& a, float mod,
       Q[c][r] = b[r][0] * pm[c] + b[r][1] * pm[4 + c] + b[r][2] * pm[8 + c] + b[r][3] * pm[12 + c];
   const float hw = float(W) / 2.0f, hh = float(H) / 2.0f;
   const float cw = float(W - 1) / 2.0f, ch = float(H - 1) / 2.0f;
-  float3 Tu, Tv, Tw;
   Tu = f3(Q[0][0] * hw + Q[3][0] * cw, Q[0][1] * hw + Q[3][1] * cw, Q[0][2] * hw + Q[3][2] * cw);
   Tv = f3(Q[1][0] * hh + Q[3][0] * ch, Q[1][1] * hh + Q[3][1] * ch, Q[1][2] * hh + Q[3][2] * ch);
   Tw = f3(Q[3][0], Q[3][1], Q[3][2]);
 
-  // View-space normal (normalised), flipped to face the camera.
-  float3 n = f3(vm[0] * L2.x + vm[4] * L2.y + vm[8] * L2.z,
-                vm[1] * L2.x + vm[5] * L2.y + vm[9] * L2.z,
-                vm[2] * L2.x + vm[6] * L2.y + vm[10] * L2.z);
+  // View-space normal (normalised), flipped to face the camera below.
+  n = f3(vm[0] * L2.x + vm[4] * L2.y + vm[8] * L2.z,
+         vm[1] * L2.x + vm[5] * L2.y + vm[9] * L2.z,
+         vm[2] * L2.x + vm[6] * L2.y + vm[10] * L2.z);
   const float nl = sqrtf(n.x * n.x + n.y * n.y + n.z * n.z);
   if (nl > 1e-7f) {
     n.x /= nl;
     n.y /= nl;
     n.z /= nl;
+  }
   }
   const float cosv = -(pv.x * n.x + pv.y * n.y + pv.z * n.z);
   if (cosv == 0) return 0;
@@ -365,7 +386,7 @@ int preprocess_api_launch(int P, const ns_surfels& s, float mod, float beta, int
                           const float* pm, int W, int H, SurfelRecord* records, BinInfo* bin,
                           int32_t* radii, uint32_t* tiles, uint32_t* depth_keys,
                           uint32_t* depth_vals, uint32_t* block_sums, cudaStream_t stream) {
-  ApiAttrs a{s.means3D, s.scales, s.rotations, s.opacities, s.homotrans, s.ap_level, s.shapes};
+  ApiAttrs a{s.means3D, s.scales, s.rotations, s.opacities, s.homotrans, s.ap_level, s.shapes, s.transmat_precomp};
   PreOut o{records, bin, radii, tiles, depth_keys, depth_vals, block_sums};
   preprocess_kernel<ApiAttrs><<<preprocess_blocks(P), kPreThreads, 0, stream>>>(
       P, a, mod, beta, kernel_type, vm, pm, W, H, o);

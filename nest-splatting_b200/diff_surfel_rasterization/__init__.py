@@ -26,6 +26,11 @@ and backward (:570-686). The dual-grid modes 1-3 and 5 of the reference's
 surface-potential renderer raise NotImplementedError instead of silently
 rendering nothing as the reference does for shapes it was not compiled for.
 
+Precomputed splat-to-pixel transforms (cov3D_precomp [P, 9], the reference's
+transMat_precomp) replace scales and rotations, as the reference's renderer
+passes them on its compute_cov3D_python path; homotrans is then required, and
+their gradient comes back in cov3D_precomp's slot.
+
 Backward (__init__.py:174-275 of the reference): the 21 gradients come back in
 argument order; means2D's slot carries the densification statistic and
 ap_level's slot dL_gradsum, homotrans gets None (its gradient is folded into
@@ -107,8 +112,17 @@ class _RasterizeGaussians(torch.autograd.Function):
             shp = shp.detach().contiguous().float().reshape(-1)
         else:
             shp = None
-        if _nonempty(cov3Ds_precomp) is not None:
-            raise NotImplementedError("precomputed transforms (cov3D_precomp) are not built")
+        # Precomputed splat-to-pixel transforms (the reference's transMat_precomp,
+        # passed as cov3D_precomp by its renderer's compute_cov3D_python path,
+        # gaussian_renderer/__init__.py:64-76): [P, 9] columns Tu, Tv, Tw; the
+        # hit point then needs homotrans.
+        Ts = _nonempty(cov3Ds_precomp)
+        if Ts is not None:
+            Ts = Ts.detach().contiguous().float().reshape(-1, 9)
+            if Ts.shape[0] != means3D.shape[0]:
+                raise RuntimeError("cov3D_precomp must hold 9 values per surfel")
+            if _nonempty(homotrans) is None:
+                raise RuntimeError("precomputed transforms need homotrans (the surfels' plane frames)")
         if means3D.ndim != 2 or means3D.shape[1] != 3:
             raise RuntimeError("means3D must have dimensions (num_points, 3)")
         L = int(hashgrid_settings.L)
@@ -216,13 +230,15 @@ class _RasterizeGaussians(torch.autograd.Function):
             sh_degree=int(raster_settings.sh_degree) if shs_in is not None else 0,
             campos=raster_settings.campos.detach().contiguous().float() if shs_in is not None else None)
         ap = _nonempty(ap_level)
-        args = (means3D.detach().contiguous().float(), scales.detach().contiguous().float(),
-                rotations.detach().contiguous().float(), opacities.detach().contiguous().float().reshape(-1),
+        sc, ro = _nonempty(scales), _nonempty(rotations)
+        args = (means3D.detach().contiguous().float(), None if sc is None else sc.detach().contiguous().float(),
+                None if ro is None else ro.detach().contiguous().float(),
+                opacities.detach().contiguous().float().reshape(-1),
                 None if _nonempty(homotrans) is None else homotrans.detach().contiguous().float().reshape(-1, 16),
                 None if ap is None else ap.detach().contiguous().float().reshape(-1), feats.detach(),
                 offsets.contiguous().to(torch.int32), gridrange.contiguous().float())
         num_rendered, color, others, radii, cover, trans, scratch = _raster.rasterize_forward(
-            cfg, *args, shapes=shp, colors_precomp=gauss, shs=shs_in)
+            cfg, *args, shapes=shp, colors_precomp=gauss, shs=shs_in, transmat_precomp=Ts)
         ctx.cfg = cfg
         ctx.args = args
         ctx.radii = radii
@@ -234,6 +250,8 @@ class _RasterizeGaussians(torch.autograd.Function):
         ctx.shape_values = shp
         ctx.gauss = gauss
         ctx.shs = shs_in
+        ctx.Ts = Ts
+        ctx.cov_shape = cov3Ds_precomp.shape
         ctx.mark_non_differentiable(radii)
         return color, radii, others, trans, cover
 
@@ -250,7 +268,7 @@ class _RasterizeGaussians(torch.autograd.Function):
             grad_depth = torch.zeros((_raster.OTHER_CHANNELS, H, W), dtype=torch.float32, device=dev)
         g = _raster.rasterize_backward(ctx.cfg, *ctx.args, ctx.radii, ctx.num_rendered, ctx.scratch,
                                        grad_out_color, grad_depth, shapes=ctx.shape_values,
-                                       colors_precomp=ctx.gauss, shs=ctx.shs)
+                                       colors_precomp=ctx.gauss, shs=ctx.shs, transmat_precomp=ctx.Ts)
         ctx.scratch = None
         need = ctx.needs_input_grad
         sh = ctx.shapes
@@ -266,9 +284,9 @@ class _RasterizeGaussians(torch.autograd.Function):
                 (g["colors_precomp"].reshape(sh["colors_precomp"]) if "colors_precomp" in g
                  else zeros_if(3, sh["colors_precomp"])) if need[3] else None,
                 g["opacity"].reshape(sh["opacities"]) if need[4] else None,
-                g["scales"] if need[5] else None,
-                g["rotations"] if need[6] else None,
-                None,  # cov3Ds_precomp (not built)
+                g["scales"] if need[5] and ctx.Ts is None else None,
+                g["rotations"] if need[6] and ctx.Ts is None else None,
+                g["transmat_precomp"].reshape(ctx.cov_shape) if (need[7] and ctx.Ts is not None) else None,
                 None,  # homotrans: folded into means / scales / rotations
                 gradsum,
                 g["table"].to(sh["features"]) if need[10] else None,

@@ -52,7 +52,7 @@ class Surfels(C.Structure):
         ("rotations", C.c_void_p), ("opacities", C.c_void_p), ("homotrans", C.c_void_p),
         ("ap_level", C.c_void_p), ("features", C.c_void_p), ("offsets", C.c_void_p),
         ("gridrange", C.c_void_p), ("shapes", C.c_void_p), ("colors_precomp", C.c_void_p),
-        ("shs", C.c_void_p), ("sh_coeffs", C.c_int32),
+        ("shs", C.c_void_p), ("sh_coeffs", C.c_int32), ("transmat_precomp", C.c_void_p),
     ]
 
 
@@ -90,7 +90,7 @@ class GradsOut(C.Structure):
         ("dL_dmeans3D", C.c_void_p), ("dL_dmean2D", C.c_void_p), ("dL_dopacity", C.c_void_p),
         ("dL_dscales", C.c_void_p), ("dL_drots", C.c_void_p), ("dL_dtable", C.c_void_p),
         ("table_rows", C.c_int64), ("dL_gradsum", C.c_void_p), ("dL_dshapes", C.c_void_p),
-        ("dL_dcolors_precomp", C.c_void_p), ("dL_dshs", C.c_void_p),
+        ("dL_dcolors_precomp", C.c_void_p), ("dL_dshs", C.c_void_p), ("dL_dtransmat_precomp", C.c_void_p),
     ]
 
 

@@ -133,11 +133,14 @@ class Scratch:
 
 def rasterize_forward(cfg: RasterConfig, means3D, scales, rotations, opacities, homotrans, ap_level,
                       features, offsets, gridrange, scratch: Scratch | None = None,
-                      capacity_hint: int | None = None, shapes=None, colors_precomp=None, shs=None):
+                      capacity_hint: int | None = None, shapes=None, colors_precomp=None, shs=None,
+                      transmat_precomp=None):
     """Forward rasterization through ns_rasterize_forward. Every render mode but
     0 (and level 0) reads the per-surfel rows `colors_precomp` (contiguous fp32);
     level 0 may take SH coefficients `shs` [P, M, 3] instead (colours evaluated
-    at cfg.sh_degree from cfg.campos, C = 3).
+    at cfg.sh_degree from cfg.campos, C = 3). `transmat_precomp` [P, 9]
+    (contiguous fp32, columns Tu, Tv, Tw) replaces the transforms built from
+    scales and rotations (which may then be None; homotrans is required).
 
     Returns (num_rendered, out_color [C,H,W], out_others [14,H,W] ([17,H,W] in
     mode 11), radii [P] int32, cover_pixels [P,1], trans_avg [P,1], scratch).
@@ -165,6 +168,7 @@ def rasterize_forward(cfg: RasterConfig, means3D, scales, rotations, opacities, 
     surf.opacities, surf.homotrans, surf.ap_level = ptr(opacities), ptr(homotrans), ptr(ap_level)
     surf.features, surf.offsets, surf.gridrange = ptr(features), ptr(offsets), ptr(gridrange)
     surf.shapes = ptr(shapes)
+    _set_transmats(surf, transmat_precomp, homotrans, P)
     if cfg.uses_rows:
         if colors_precomp is None and (shs is None or cfg.render_mode != 0):
             raise ValueError(f"render_mode {cfg.render_mode} with {cfg.levels} levels needs colors_precomp")
@@ -206,6 +210,17 @@ def _set_shs(cfg: RasterConfig, surf, shs, P: int) -> None:
     surf.sh_coeffs = shs.numel() // (3 * max(P, 1))
 
 
+def _set_transmats(surf, transmat_precomp, homotrans, P: int) -> None:
+    if transmat_precomp is None:
+        return
+    if transmat_precomp.numel() != 9 * P or transmat_precomp.dtype != torch.float32:
+        raise ValueError("transmat_precomp must be fp32 [P, 9]")
+    if homotrans is None:
+        raise ValueError("precomputed transforms need homotrans (the hit point's frame)")
+    _require_cuda(transmat_precomp)
+    surf.transmat_precomp = ptr(transmat_precomp)
+
+
 def read_binning(scratch: Scratch, P: int, width: int, height: int, num_rendered: int) -> dict:
     """What the last forward call on `scratch` left in it (ns_read_binning):
     point_list [num_rendered] int32 (surfel ids per tile in depth order),
@@ -232,7 +247,8 @@ def read_binning(scratch: Scratch, P: int, width: int, height: int, num_rendered
 
 def rasterize_backward(cfg: RasterConfig, means3D, scales, rotations, opacities, homotrans, ap_level, features,
                        offsets, gridrange, radii, num_rendered: int, scratch: Scratch, dL_dcolor, dL_dothers,
-                       return_accumulators: bool = False, shapes=None, colors_precomp=None, shs=None):
+                       return_accumulators: bool = False, shapes=None, colors_precomp=None, shs=None,
+                       transmat_precomp=None):
     """Backward rasterization (render_mode 0) through ns_rasterize_backward.
 
     `scratch` and every input must be the ones of the forward call. Returns a dict
@@ -242,7 +258,9 @@ def rasterize_backward(cfg: RasterConfig, means3D, scales, rotations, opacities,
     shapes [P]; for the modes that read per-surfel rows (`colors_precomp` as in
     the forward) also colors_precomp (same shape); for level 0 from SH (`shs` as
     in the forward) also shs [P, M, 3], the colour's mean gradient included in
-    means3D. With return_accumulators, also "accum": the render pass's
+    means3D; with `transmat_precomp` (as in the forward) also transmat_precomp
+    [P, 9], and zeros for means3D, scales and rotations. With
+    return_accumulators, also "accum": the render pass's
     per-surfel accumulators [P,20] (dL/dM 9, dL/dT[0].z, dL/dT[1].z, opacity,
     dL/dnormal 3, gradsum, dL/dmean2D 2, dL/dshape, 1 unused), for tests.
     """
@@ -267,6 +285,8 @@ def rasterize_backward(cfg: RasterConfig, means3D, scales, rotations, opacities,
         shapes = shapes.contiguous().float().reshape(-1)
         _require_cuda(shapes)
         g["shapes"] = torch.empty((P,), dtype=torch.float32, device=dev)
+    if transmat_precomp is not None:
+        g["transmat_precomp"] = torch.empty((P, 9), dtype=torch.float32, device=dev)
     if cfg.uses_rows and colors_precomp is None and shs is not None and cfg.render_mode == 0:
         g["shs"] = torch.zeros_like(shs)
     elif cfg.uses_rows:
@@ -286,6 +306,7 @@ def rasterize_backward(cfg: RasterConfig, means3D, scales, rotations, opacities,
     surf.features, surf.offsets, surf.gridrange = ptr(features), ptr(offsets), ptr(gridrange)
     if cfg.kernel_type != 0:
         surf.shapes = ptr(shapes)
+    _set_transmats(surf, transmat_precomp, homotrans, P)
     if "shs" in g:
         _set_shs(cfg, surf, shs, P)
     elif cfg.uses_rows:
@@ -295,7 +316,8 @@ def rasterize_backward(cfg: RasterConfig, means3D, scales, rotations, opacities,
                        ptr(g["rotations"]), ptr(g["table"]), rows, ptr(g["gradsum"]),
                        ptr(g["shapes"]) if "shapes" in g else None,
                        ptr(g["colors_precomp"]) if "colors_precomp" in g else None,
-                       ptr(g["shs"]) if "shs" in g else None)
+                       ptr(g["shs"]) if "shs" in g else None,
+                       ptr(g["transmat_precomp"]) if "transmat_precomp" in g else None)
     nbytes = (lib.ns_backward_scratch_bytes_deterministic(P, rows, int(cfg.level_dim)) if cfg.deterministic
               else lib.ns_backward_scratch_bytes(P))
     acc = torch.empty(nbytes, dtype=torch.uint8, device=dev)

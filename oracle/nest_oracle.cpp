@@ -98,11 +98,15 @@ extern "C" {
 // (in_frustum). Per surfel outputs use the reference layouts:
 //   means2D [P,2], depths [P], transMat [P,9] (Tu, Tv, Tw), normal_opacity [P,4],
 //   radii [P] int32, tiles_touched [P] uint32.
-void oracle_preprocess(int P, const float* means3D, const float* scales, float mod,
-                       const float* rotations, const float* opacities, const float* viewmatrix,
-                       const float* projmatrix, int W, int H, int* radii, float* means2D,
-                       float* depths, float* transMat, float* normal_opacity,
-                       uint32_t* tiles_touched) {
+// Ts: NULL, or precomputed transforms [P, 9] (columns Tu, Tv, Tw; the
+// reference's transMat_precomp, forward.cu:366-380), whose normal is the view
+// axis (0, 0, 1) before the camera-facing flip; scales and rotations are then
+// not read.
+static void preprocess_impl(int P, const float* means3D, const float* scales, float mod,
+                            const float* rotations, const float* opacities, const float* viewmatrix,
+                            const float* projmatrix, int W, int H, int* radii, float* means2D,
+                            float* depths, float* transMat, float* normal_opacity,
+                            uint32_t* tiles_touched, const float* Ts) {
   const int gx = (W + kBlock - 1) / kBlock, gy = (H + kBlock - 1) / kBlock;
 #pragma omp parallel for schedule(static)
   for (int i = 0; i < P; i++) {
@@ -111,6 +115,14 @@ void oracle_preprocess(int P, const float* means3D, const float* scales, float m
     F3 p = {means3D[3 * i], means3D[3 * i + 1], means3D[3 * i + 2]};
     F3 pv = xform_point4x3(p, viewmatrix);
     if (pv.z <= 0.2f) continue;
+    F3 Tu, Tv, Tw, n;
+    if (Ts) {
+      const float* t = Ts + 9 * (size_t)i;
+      Tu = {t[0], t[1], t[2]};
+      Tv = {t[3], t[4], t[5]};
+      Tw = {t[6], t[7], t[8]};
+      n = {0.f, 0.f, 1.f};
+    } else {
     F3 R[3];
     quat_to_cols(rotations + 4 * i, R);
     F3 L0 = scl(mod * scales[2 * i], R[0]);
@@ -125,16 +137,16 @@ void oracle_preprocess(int P, const float* means3D, const float* scales, float m
                   basis[r][2] * projmatrix[8 + c] + basis[r][3] * projmatrix[12 + c];
     const float hw = float(W) / 2.0f, hh = float(H) / 2.0f;
     const float cw = float(W - 1) / 2.0f, ch = float(H - 1) / 2.0f;
-    F3 Tu, Tv, Tw;
     float* tu = &Tu.x; float* tv = &Tv.x; float* tw = &Tw.x;
     for (int r = 0; r < 3; r++) {
       tu[r] = Q[0][r] * hw + Q[3][r] * cw;
       tv[r] = Q[1][r] * hh + Q[3][r] * ch;
       tw[r] = Q[3][r];
     }
-    F3 n = xform_vec4x3(L2, viewmatrix);
+    n = xform_vec4x3(L2, viewmatrix);
     float nl = std::sqrt(n.x * n.x + n.y * n.y + n.z * n.z);
     if (nl > 1e-7f) { n.x /= nl; n.y /= nl; n.z /= nl; }
+    }
     float cosv = -(pv.x * n.x + pv.y * n.y + pv.z * n.z);
     if (cosv == 0) continue;
     float mult = cosv > 0 ? 1.f : -1.f;
@@ -169,6 +181,24 @@ void oracle_preprocess(int P, const float* means3D, const float* scales, float m
     normal_opacity[4 * i + 3] = opacities[i];
     tiles_touched[i] = (uint32_t)((y1 - y0) * (x1 - x0));
   }
+}
+
+void oracle_preprocess(int P, const float* means3D, const float* scales, float mod,
+                       const float* rotations, const float* opacities, const float* viewmatrix,
+                       const float* projmatrix, int W, int H, int* radii, float* means2D,
+                       float* depths, float* transMat, float* normal_opacity,
+                       uint32_t* tiles_touched) {
+  preprocess_impl(P, means3D, scales, mod, rotations, opacities, viewmatrix, projmatrix, W, H, radii, means2D,
+                  depths, transMat, normal_opacity, tiles_touched, nullptr);
+}
+
+// The same with precomputed transforms Ts [P, 9] (transMat_precomp).
+void oracle_preprocess_precomp(int P, const float* means3D, const float* Ts, const float* opacities,
+                               const float* viewmatrix, const float* projmatrix, int W, int H, int* radii,
+                               float* means2D, float* depths, float* transMat, float* normal_opacity,
+                               uint32_t* tiles_touched) {
+  preprocess_impl(P, means3D, nullptr, 1.0f, nullptr, opacities, viewmatrix, projmatrix, W, H, radii, means2D,
+                  depths, transMat, normal_opacity, tiles_touched, Ts);
 }
 
 // rasterizer_impl.cu:70-111 (duplicateWithKeys), 381-386 (stable radix sort on

@@ -576,7 +576,8 @@ void preprocess_backward(int P, const float* means3D, const float* scales, const
                          const int* radii, const float* transMat, const float* viewmatrix,
                          const float* projmatrix, int width, int height, float tanfovx,
                          float tanfovy, R* dL_dmean2D, const R* dL_dnormal, const R* dL_dtransMat,
-                         const R* dL_dhomoMat, R* dL_dmeans3D, R* dL_dscales, R* dL_drots) {
+                         const R* dL_dhomoMat, R* dL_dmeans3D, R* dL_dscales, R* dL_drots,
+                         R* dL_dTs = nullptr) {
   using V = V3<R>;
   const float focal_x = width / (2.0f * tanfovx);
   const float focal_y = height / (2.0f * tanfovy);
@@ -587,6 +588,44 @@ void preprocess_backward(int P, const float* means3D, const float* scales, const
 #pragma omp parallel for schedule(static)
   for (int i = 0; i < P; i++) {
     if (!(radii[i] > 0)) continue;
+    if (dL_dTs) {
+      // Precomputed transforms (scales == NULL, backward.cu:2082-2088, 2128-2158):
+      // the render-pass dL/dT plus the centre's mean2D term, written back as the
+      // transforms' gradient; nothing reaches means, scales or rotations; the
+      // densification statistic reads the updated dL/dT.
+      V T[3], dT[3];
+      for (int c = 0; c < 3; c++) {
+        T[c] = {transMat[9 * i + 3 * c], transMat[9 * i + 3 * c + 1], transMat[9 * i + 3 * c + 2]};
+        dT[c] = {dL_dtransMat[9 * i + 3 * c], dL_dtransMat[9 * i + 3 * c + 1], dL_dtransMat[9 * i + 3 * c + 2]};
+      }
+      const R gmx = dL_dmean2D[3 * i], gmy = dL_dmean2D[3 * i + 1];
+      if (gmx != 0 || gmy != 0) {
+        const V t_vec = {9, 9, -1};
+        const R d = dot3(t_vec, mul3(T[2], T[2]));
+        const V f_vec = vscl(R(1) / d, t_vec);
+        const V dT0 = mul3(vscl(gmx, f_vec), T[2]);
+        const V dT1 = mul3(vscl(gmy, f_vec), T[2]);
+        V dT3 = add3(mul3(vscl(gmx, f_vec), T[0]), mul3(vscl(gmy, f_vec), T[1]));
+        const V dL_df = add3(mul3(vscl(gmx, T[0]), T[2]), mul3(vscl(gmy, T[1]), T[2]));
+        const R dL_dd = (R)(dot3(dL_df, f_vec) * (-1.0 / d));
+        dT3 = add3(dT3, vscl(dL_dd, vscl(R(2), mul3(t_vec, T[2]))));
+        dT[0] = add3(dT[0], dT0);
+        dT[1] = add3(dT[1], dT1);
+        dT[2] = add3(dT[2], dT3);
+      }
+      for (int c = 0; c < 3; c++) {
+        dL_dTs[9 * i + 3 * c] = dT[c].x;
+        dL_dTs[9 * i + 3 * c + 1] = dT[c].y;
+        dL_dTs[9 * i + 3 * c + 2] = dT[c].z;
+      }
+      for (int k = 0; k < 3; k++) dL_dmeans3D[3 * i + k] = 0;
+      for (int k = 0; k < 2; k++) dL_dscales[2 * i + k] = 0;
+      for (int k = 0; k < 4; k++) dL_drots[4 * i + k] = 0;
+      const R depth = transMat[9 * i + 8];
+      dL_dmean2D[3 * i] = (R)((double)(dT[0].z * depth) * 0.5 * (double)(float)W);
+      dL_dmean2D[3 * i + 1] = (R)((double)(dT[1].z * depth) * 0.5 * (double)(float)H);
+      continue;
+    }
     const V p = {means3D[3 * i], means3D[3 * i + 1], means3D[3 * i + 2]};
     const float* qf = rotations + 4 * i;
     const R q[4] = {qf[0], qf[1], qf[2], qf[3]};
@@ -869,6 +908,25 @@ void oracle_preprocess_backward(int P, const float* means3D, const float* scales
   preprocess_backward<float>(P, means3D, scales, rotations, radii, transMat, viewmatrix, projmatrix,
                              width, height, tanfovx, tanfovy, dL_dmean2D, dL_dnormal, dL_dtransMat,
                              dL_dhomoMat, dL_dmeans3D, dL_dscales, dL_drots);
+}
+
+// Precomputed transforms: dL_dTs [P, 9] written (transMat = the forward's
+// transforms, i.e. the given ones); means, scales and rotations get zeros.
+void oracle_preprocess_backward_precomp(int P, const int* radii, const float* transMat, int width, int height,
+                                        float tanfovx, float tanfovy, float* dL_dmean2D,
+                                        const float* dL_dtransMat, float* dL_dTs, float* dL_dmeans3D,
+                                        float* dL_dscales, float* dL_drots) {
+  preprocess_backward<float>(P, nullptr, nullptr, nullptr, radii, transMat, nullptr, nullptr, width, height,
+                             tanfovx, tanfovy, dL_dmean2D, nullptr, dL_dtransMat, nullptr, dL_dmeans3D,
+                             dL_dscales, dL_drots, dL_dTs);
+}
+void oracle_preprocess_backward_precomp_f64(int P, const int* radii, const float* transMat, int width,
+                                            int height, float tanfovx, float tanfovy, double* dL_dmean2D,
+                                            const double* dL_dtransMat, double* dL_dTs, double* dL_dmeans3D,
+                                            double* dL_dscales, double* dL_drots) {
+  preprocess_backward<double>(P, nullptr, nullptr, nullptr, radii, transMat, nullptr, nullptr, width, height,
+                              tanfovx, tanfovy, dL_dmean2D, nullptr, dL_dtransMat, nullptr, dL_dmeans3D,
+                              dL_dscales, dL_drots, dL_dTs);
 }
 
 void oracle_preprocess_backward_f64(int P, const float* means3D, const float* scales,

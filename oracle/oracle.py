@@ -49,6 +49,9 @@ def load() -> C.CDLL:
     lib = C.CDLL(str(LIB_PATH))
     vp, i32, u32, i64, f32 = C.c_void_p, C.c_int, C.c_uint32, C.c_int64, C.c_float
     lib.oracle_preprocess.argtypes = [i32, vp, vp, f32, vp, vp, vp, vp, i32, i32, vp, vp, vp, vp, vp, vp]
+    lib.oracle_preprocess_precomp.argtypes = [i32, vp, vp, vp, vp, vp, i32, i32, vp, vp, vp, vp, vp, vp]
+    lib.oracle_preprocess_backward_precomp.argtypes = [i32, vp, vp, i32, i32, f32, f32, vp, vp, vp, vp, vp, vp]
+    lib.oracle_preprocess_backward_precomp_f64.argtypes = lib.oracle_preprocess_backward_precomp.argtypes
     lib.oracle_bin.restype = i64
     lib.oracle_bin.argtypes = [i32, vp, vp, vp, i32, i32, vp, vp, i64, vp]
     lib.oracle_render.argtypes = [i32, i32, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, i32, i32, u32, f32, u32,
@@ -83,19 +86,28 @@ def _f32(a) -> np.ndarray:
     return np.ascontiguousarray(np.asarray(a, dtype=np.float32))
 
 
-def preprocess(means3D, scales, rotations, opacities, viewmatrix, projmatrix, W, H, scale_modifier=1.0):
-    """forward.cu:323-441 restated. Returns dict of per-surfel arrays."""
+def preprocess(means3D, scales, rotations, opacities, viewmatrix, projmatrix, W, H, scale_modifier=1.0,
+               transmat_precomp=None):
+    """forward.cu:323-441 restated. Returns dict of per-surfel arrays. With
+    transmat_precomp [P, 9] (columns Tu, Tv, Tw) the transforms are taken as
+    given and scales / rotations are not read (forward.cu:366-380)."""
     lib = load()
-    means3D, scales, rotations = _f32(means3D), _f32(scales), _f32(rotations)
+    means3D = _f32(means3D)
     opacities = _f32(opacities).reshape(-1)
     vm, pm = _f32(viewmatrix).reshape(16), _f32(projmatrix).reshape(16)
     P = means3D.shape[0]
     out = dict(radii=np.zeros(P, np.int32), means2D=np.zeros((P, 2), np.float32), depths=np.zeros(P, np.float32),
                transMat=np.zeros((P, 9), np.float32), normal_opacity=np.zeros((P, 4), np.float32),
                tiles_touched=np.zeros(P, np.uint32))
+    tail = (_p(out["radii"]), _p(out["means2D"]), _p(out["depths"]), _p(out["transMat"]),
+            _p(out["normal_opacity"]), _p(out["tiles_touched"]))
+    if transmat_precomp is not None:
+        Ts = _f32(transmat_precomp).reshape(P, 9)
+        lib.oracle_preprocess_precomp(P, _p(means3D), _p(Ts), _p(opacities), _p(vm), _p(pm), int(W), int(H), *tail)
+        return out
+    scales, rotations = _f32(scales), _f32(rotations)
     lib.oracle_preprocess(P, _p(means3D), _p(scales), float(scale_modifier), _p(rotations), _p(opacities), _p(vm),
-                          _p(pm), int(W), int(H), _p(out["radii"]), _p(out["means2D"]), _p(out["depths"]),
-                          _p(out["transMat"]), _p(out["normal_opacity"]), _p(out["tiles_touched"]))
+                          _p(pm), int(W), int(H), *tail)
     return out
 
 
@@ -279,7 +291,7 @@ def forward(means3D, scales, rotations, opacities, homotrans, ap_level, table_f3
             viewmatrix, projmatrix, W, H, C_out, LD, L, S, Hres, **kw):
     """Full oracle forward: preprocess -> bin -> render. Returns (render dict, pre, num_rendered)."""
     pre = preprocess(means3D, scales, rotations, opacities, viewmatrix, projmatrix, W, H,
-                     kw.pop("scale_modifier", 1.0))
+                     kw.pop("scale_modifier", 1.0), transmat_precomp=kw.pop("transmat_precomp", None))
     keys, vals, ranges = bin_surfels(pre, W, H)
     out = render(pre, vals, ranges, homotrans, ap_level, table_f32, offsets, gridrange, W, H, C_out, LD, L, S,
                  Hres, **kw)
@@ -336,12 +348,25 @@ def render_backward(pre, vals, ranges, fwd, homotrans, ap_level, table_f32, offs
 
 
 def preprocess_backward(means3D, scales, rotations, pre, g, viewmatrix, projmatrix, W, H, tanfovx, tanfovy,
-                        f64=False):
+                        f64=False, precomp=False):
     """preprocessCUDA backward + compute_transmat_aabb restated. Consumes the
     render-pass gradients `g` (from render_backward) and returns
     dL_dmeans3D [P,3], dL_dscales [P,2], dL_drots [P,4] and the densification
-    statistic dL_dmean2D [P,3] (the rasterizer's means2D gradient)."""
+    statistic dL_dmean2D [P,3] (the rasterizer's means2D gradient). With
+    precomp (the forward took transmat_precomp) also dL_dtransMat [P,9], the
+    given transforms' gradient; means, scales and rotations get zeros."""
     lib = load()
+    if precomp:
+        P = pre["radii"].shape[0]
+        dt = np.float64 if f64 else np.float32
+        out = dict(dL_dmeans3D=np.zeros((P, 3), dt), dL_dscales=np.zeros((P, 2), dt),
+                   dL_drots=np.zeros((P, 4), dt), dL_dmean2D=np.array(g["dL_dmean2D"], dt, copy=True),
+                   dL_dtransMat=np.zeros((P, 9), dt))
+        fn = lib.oracle_preprocess_backward_precomp_f64 if f64 else lib.oracle_preprocess_backward_precomp
+        fn(P, _p(pre["radii"]), _p(pre["transMat"]), int(W), int(H), float(tanfovx), float(tanfovy),
+           _p(out["dL_dmean2D"]), _p(np.ascontiguousarray(np.asarray(g["dL_dtransMat"], dt))),
+           _p(out["dL_dtransMat"]), _p(out["dL_dmeans3D"]), _p(out["dL_dscales"]), _p(out["dL_drots"]))
+        return out
     means3D, scales, rotations = _f32(means3D), _f32(scales), _f32(rotations)
     P = means3D.shape[0]
     dt = np.float64 if f64 else np.float32

@@ -217,22 +217,34 @@ def mode_feature(f_hash, row, mode, pg, td, C):
 
 
 def render(means, scales, rots, opac, table, cam, lists, grid, apl_int, W, H, kernel_type=0, shapes=None,
-           modes=None):
+           modes=None, Ts=None, homo=None):
     """Forward pass over the oracle's tile lists. Returns (color [C,H,W], others [7,H,W], margins).
+
+    Ts [P, 9] (columns Tu, Tv, Tw) replaces the transforms built from means,
+    scales and rotations (the reference's transMat_precomp): the normal is then
+    the view axis, flipped to face the camera, and the hit point is formed from
+    the constant homotrans `homo` [P, 16] (its gradient is not returned).
 
     margins: the smallest relative distance of any decision (alpha >= 1/255, the
     rho3d/rho2d branch, near plane, termination) from its threshold, so a test can
     check that float32 and float64 take the same branches."""
     vm = np.asarray(cam["viewmatrix"], np.float64).reshape(4, 4)
     P = ndc_to_pixel(cam["projmatrix"], W, H)
-    r0, r1, r2 = rotation_columns(rots)
-    L0, L1 = r0 * scales[:, 0:1], r1 * scales[:, 1:2]
-    Tu = torch.stack([L0 @ P[0, :3], L1 @ P[0, :3], means @ P[0, :3] + P[0, 3]], 1)
-    Tv = torch.stack([L0 @ P[1, :3], L1 @ P[1, :3], means @ P[1, :3] + P[1, 3]], 1)
-    Tw = torch.stack([L0 @ P[2, :3], L1 @ P[2, :3], means @ P[2, :3] + P[2, 3]], 1)
     vmt = torch.tensor(vm)
-    n = r2 @ vmt[:3, :3]
-    n = n / n.norm(dim=1, keepdim=True)
+    pk = means
+    if Ts is not None:
+        Tu, Tv, Tw = Ts[:, 0:3], Ts[:, 3:6], Ts[:, 6:9]
+        h = torch.as_tensor(np.asarray(homo, np.float64)).reshape(-1, 4, 4)
+        L0, L1, pk = h[:, :3, 0], h[:, :3, 1], h[:, :3, 3]
+        n = torch.tensor([0.0, 0.0, 1.0], dtype=torch.float64).expand(Ts.shape[0], 3)
+    else:
+        r0, r1, r2 = rotation_columns(rots)
+        L0, L1 = r0 * scales[:, 0:1], r1 * scales[:, 1:2]
+        Tu = torch.stack([L0 @ P[0, :3], L1 @ P[0, :3], means @ P[0, :3] + P[0, 3]], 1)
+        Tv = torch.stack([L0 @ P[1, :3], L1 @ P[1, :3], means @ P[1, :3] + P[1, 3]], 1)
+        Tw = torch.stack([L0 @ P[2, :3], L1 @ P[2, :3], means @ P[2, :3] + P[2, 3]], 1)
+        n = r2 @ vmt[:3, :3]
+        n = n / n.norm(dim=1, keepdim=True)
     pv = means @ vmt[:3, :3] + vmt[3, :3]
     flip = torch.where(-(pv * n).sum(1) > 0, 1.0, -1.0).detach()
     n = n * flip[:, None]
@@ -302,7 +314,7 @@ def render(means, scales, rots, opac, table, cam, lists, grid, apl_int, W, H, ke
             M2 = M2 + md * md * w
             med = torch.where(valid & (T.detach() > 0.5), c_d, med)
             N = N + n[i][None, :] * w[:, None]
-            hit = torch.where(b3[:, None], sx[:, None] * L0[i] + sy[:, None] * L1[i] + means[i], means[i].expand(npx, 3))
+            hit = torch.where(b3[:, None], sx[:, None] * L0[i] + sy[:, None] * L1[i] + pk[i], pk[i].expand(npx, 3))
             f = query(hit, np.full(npx, apl_int[i]), table, grid["offsets"], grid["L"], grid["LD"], grid["S"],
                       grid["H"], grid["vmin"], grid["vmax"], grid.get("align_corners", False),
                       grid.get("interp", 0))
@@ -316,7 +328,7 @@ def render(means, scales, rots, opac, table, cam, lists, grid, apl_int, W, H, ke
                 # hash levels from channel 0; the surfel's SH colour along hit - centre
                 # goes to its own map (no gradient in the reference's backward)
                 f = torch.cat([f, f.new_zeros(npx, C - f.shape[1])], 1) if f.shape[1] < C else f
-                dvec = (hit - means[i]).detach()
+                dvec = (hit - pk[i]).detach()
                 rgb = eval_sh_interleaved(modes["gauss"][i].detach(), dvec / dvec.norm(dim=1, keepdim=True))
                 rgb = torch.where(b3[:, None], torch.nan_to_num(rgb, nan=0.0), torch.zeros_like(rgb))
                 SH = SH + rgb * w.detach()[:, None]

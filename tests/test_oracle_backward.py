@@ -312,3 +312,51 @@ def test_oracle_sh_color_backward_matches_autograd(deg):
         assert np.abs(dmean).max() < 1e-6
     d64, m64 = oracle.sh_color_backward(means.numpy(), campos.numpy(), shs.numpy(), deg, radii, up.numpy(), f64=True)
     assert rel_l2(d64[on], want_sh[on]) < 1e-7  # the constants are the reference's float values
+
+
+def test_oracle_precomputed_transforms_match_autograd():
+    """The reference's transMat_precomp path (pipe.compute_cov3D_python;
+    forward.cu:366-380, backward.cu:2082-2088, 2128-2158): transforms given per
+    surfel, the normal the view axis, the hit point from the given homotrans.
+    The transforms' gradient (render pass plus the centre's mean2D term),
+    opacity and table against float64 autograd of the same forward with the
+    transforms as leaves; means, scales and rotations get nothing."""
+    c = tiny_case(52)
+    cam, grid = c["cam"], c["grid"]
+    vm, pm = cam.world_view_transform.numpy(), cam.full_proj_transform.numpy()
+    W, H = c["W"], c["H"]
+    g = torch.Generator().manual_seed(52)
+    pre0 = oracle.preprocess(c["means"].numpy(), c["scales"].numpy(), c["rots"].numpy(), c["opac"].numpy(), vm,
+                             pm, W, H)
+    Ts = (pre0["transMat"] * (1 + 1e-2 * torch.randn(pre0["transMat"].shape, generator=g).numpy())).astype(
+        np.float32)
+    pre = oracle.preprocess(c["means"].numpy(), None, None, c["opac"].numpy(), vm, pm, W, H, transmat_precomp=Ts)
+    assert (pre["radii"] > 0).sum() > 10
+    assert np.allclose(pre["normal_opacity"][pre["radii"] > 0, 2], -1.0)
+    _, vals, ranges = oracle.bin_surfels(pre, W, H)
+    common = (c["homo"].numpy(), c["ap"].numpy(), c["table"].numpy(), grid.offsets.numpy(), grid.gridrange.numpy(),
+              W, H, grid.channels, grid.level_dim, grid.levels, grid.S, grid.base_resolution)
+    fwd = oracle.render(pre, vals, ranges, *common)
+    gr = oracle.render_backward(pre, vals, ranges, fwd, *common, c["gc"].numpy(), c["go"].numpy())
+    pg = oracle.preprocess_backward(None, None, None, pre, gr, vm, pm, W, H, cam.tanfovx, cam.tanfovy,
+                                    precomp=True)
+    assert not pg["dL_dmeans3D"].any() and not pg["dL_dscales"].any() and not pg["dL_drots"].any()
+
+    Tl = torch.tensor(Ts, dtype=torch.float64).requires_grad_(True)
+    opac = c["opac"].double().clone().requires_grad_(True)
+    table = c["table"].double().clone().requires_grad_(True)
+    info = dict(L=grid.levels, LD=grid.level_dim, S=grid.S, H=grid.base_resolution, offsets=grid.offsets.numpy(),
+                vmin=float(grid.gridrange[0]), vmax=float(grid.gridrange[1]), interp=0)
+    color, others, margin, _ = bw_model.render(
+        c["means"].double(), None, None, opac, table,
+        dict(viewmatrix=vm, projmatrix=pm), (ranges, vals), info, np.floor(c["ap"].numpy()).astype(np.int64), W, H,
+        Ts=Tl, homo=c["homo"].numpy())
+    assert margin > 1e-5
+    assert np.max(np.abs(color.detach().numpy() - fwd["out_color"])) < 2e-5
+    ((color * c["gc"].double()).sum() + (others * c["go"][:7].double()).sum()).backward()
+    on = pre["radii"] > 0
+    checks = {"transMat": (pg["dL_dtransMat"][on], Tl.grad.numpy()[on]),
+              "opac": (gr["dL_dopacity"], opac.grad.numpy()), "table": (gr["dL_dtable"], table.grad.numpy())}
+    for k, (got, want) in checks.items():
+        assert np.linalg.norm(want) > 0, k
+        assert rel_l2(got, want) < 1e-4, (k, rel_l2(got, want))
