@@ -57,7 +57,9 @@ struct BlendSmem {
   uint8_t lvl[kQueue][kThreads];        // levels to query for the sample (0: none)
   uint8_t item[kWarps][kThreads];       // per warp: queued samples in k-major order, (k << 5) | lane
   uint8_t pos[kQueue][kThreads];        // position of a pixel's k-th sample in its warp's list
-  float4 res[kWarps][2 * kChunk];       // lookups of the current chunk: levels l..l+3, two float4 per entry
+  float4 res[2][kWarps][kChunk];        // lookups of the current chunk: levels l, l+1 | l+2, l+3 per entry
+                                        // (two arrays, so a lane's stores and reads are 16-byte
+                                        // strided: no shared-memory bank conflicts)
   float acc[kThreads * kAccStride];     // feature accumulators, see acc_pair()
   LevelConst lv[kMaxLevels];
   uint64_t full[kSlots];                // slot filled (32 cp.async arrivals per fill)
@@ -370,14 +372,14 @@ __global__ void __launch_bounds__(kThreads, 2) blend_kernel(const RenderParams p
         float2 r[4];
 #pragma unroll
         for (int q = 0; q < 4; q++) r[q] = u[q] ? lookup_finish<TableT>(f[q], v[q]) : make_float2(0.f, 0.f);
-        S.res[wid][2 * lane] = make_float4(r[0].x, r[0].y, r[1].x, r[1].y);
-        S.res[wid][2 * lane + 1] = make_float4(r[2].x, r[2].y, r[3].x, r[3].y);
+        S.res[0][wid][lane] = make_float4(r[0].x, r[0].y, r[1].x, r[1].y);
+        S.res[1][wid][lane] = make_float4(r[2].x, r[2].y, r[3].x, r[3].y);
         __syncwarp();
         while (nk < cnt) {
           const int ps = S.pos[nk][t];
           if (ps >= ch + kChunk) break;
-          const float4 r01 = S.res[wid][2 * (ps - ch)];
-          const float4 r23 = S.res[wid][2 * (ps - ch) + 1];
+          const float4 r01 = S.res[0][wid][ps - ch];
+          const float4 r23 = S.res[1][wid][ps - ch];
           const uint32_t mk = S.lvl[nk][t];
           const float w = S.samp[nk][t].w;
           const float2 ww = make_float2(w, w);
