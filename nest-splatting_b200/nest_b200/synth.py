@@ -186,5 +186,5 @@ def config3_cameras(count: int = 64, width: int = 1920, height: int = 1080, elev
     return [orbit_camera(width, height, 60.0, 4.0, 360.0 * i / count, elevation_deg) for i in range(count)]
 
 
-def config3(n: int = 3_000_000, seed: int = 3) -> Scene:
-    return make_scene(n, -5.0, 0.6, 1920, 1080, 60.0, seed, rvq=True)
+def config3(n: int = 3_000_000, table_range: float = 1e-4, seed: int = 3) -> Scene:
+    return make_scene(n, -5.0, 0.6, 1920, 1080, 60.0, seed, rvq=True, table_range=table_range)

@@ -1,10 +1,12 @@
-"""Parity at the benchmarked sizes: BASELINE configs 1 and 2 against the oracle.
+"""Parity at the benchmarked sizes: BASELINE configs 1, 2 and 3 against the oracle.
 
 Config 2 (1M RVQ surfels, 1297x840) goes through the fused frame the bench
 times (FrameRenderer -> ns_render_frame: decode, mix + activation,
 preprocess, binning, blend, MLP). The oracle renders every second tile row
 (row_stride 2; a bounded CPU time) of the same decoded attributes, and the
-GPU outputs are compared on those rows.
+GPU outputs are compared on those rows. Config 3 (3M RVQ surfels, 1920x1080
+orbit views of the 64-view batch) goes through the same frame with the
+batch's camera matrices; the oracle renders every second tile row.
 
 Tables: the parity-stress table U(-1, 1), where every feature channel carries
 values of order one and a gather error cannot hide, and the benchmark table
@@ -69,6 +71,35 @@ def test_config2_frame_parity(table_range):
     compare(out, feats, others, rows=rows, feat_tol=_feat_tol(table_range, out["out_color"][:, rows]))
     assert np.array_equal(fr.radii.cpu().numpy() > 0, pre["radii"] > 0) or \
         (np.asarray(fr.radii.cpu().numpy() > 0) != (pre["radii"] > 0)).mean() < 1e-4
+    rgb_ref = oracle.mlp_oracle(out["out_color"][:, rows], sc.mlp, out["out_others"][1][rows])
+    got = rgb.cpu().numpy()[:, rows]
+    bad = np.abs(got - rgb_ref).max(axis=0) > TOL
+    assert bad.mean() <= 1e-3, (bad.sum(), np.abs(got - rgb_ref).max())
+    assert psnr(got, rgb_ref) >= 60
+
+
+@pytest.mark.parametrize("table_range,view", [(1.0, 8), (1e-4, 40)])
+def test_config3_view_parity(table_range, view):
+    """one 1920x1080 view of the 64-view orbit batch
+    (azimuth 360 view / 64, elevation 20 deg) of the 3M-surfel RVQ scene,
+    rendered by the frame path the multi-view bench times."""
+    import dataclasses
+    sc = synth.config3(table_range=table_range)
+    cam = synth.config3_cameras()[view]
+    fr = FrameRenderer(sc, device="cuda", capacity=24_000_000)
+    rgb = fr.render(cam)
+    torch.cuda.synchronize()
+    decoded = oracle.rvq_decode_np(sc.rvq_idx.numpy(), sc.codebooks.numpy())
+    assert np.array_equal(fr.decoded.cpu().numpy(), decoded), "RVQ decode is not bit-exact"
+    stride = 2
+    sv = dataclasses.replace(sc, camera=cam)
+    out, pre, n = oracle_render(sv, api_inputs(sv, raw_attributes(sv, torch.from_numpy(decoded))),
+                                row_stride=stride)
+    rows = _sampled_rows(cam.height, stride)
+    feats, others = fr.features.cpu().numpy(), fr.others.cpu().numpy()
+    assert others[7][rows].sum() > 5e6
+    compare(out, feats, others, rows=rows, feat_tol=_feat_tol(table_range, out["out_color"][:, rows]))
+    assert (np.asarray(fr.radii.cpu().numpy() > 0) != (pre["radii"] > 0)).mean() < 1e-4
     rgb_ref = oracle.mlp_oracle(out["out_color"][:, rows], sc.mlp, out["out_others"][1][rows])
     got = rgb.cpu().numpy()[:, rows]
     bad = np.abs(got - rgb_ref).max(axis=0) > TOL
