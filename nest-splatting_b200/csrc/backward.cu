@@ -11,11 +11,11 @@
 //   query_feature<true> (hashgrid.h:106-299): table-gradient scatter and dL/dxyz;
 //   preprocessCUDA backward (:2216-2273) with compute_transmat_aabb (:2056-2214).
 //
-// Design (one CTA of 256 threads per 16x16 tile, one thread per pixel, warp w
-// on tile rows 2w, 2w+1, as in the forward blend):
+// Design (one CTA of kThreads = 16 x kRows threads per band of kRows rows of a
+// 16x16 tile, one thread per pixel, warp w on band rows 2w, 2w+1):
 //   * the tile's list is walked back to front only up to the largest last
-//     contributor of its pixels; batches of 256 records are gathered into shared
-//     memory in reverse order;
+//     contributor of the band's pixels; batches of kThreads records are
+//     gathered into shared memory in reverse order;
 //   * phase A: a warp-synchronous walk (all lanes at one record) recomputes the
 //     forward's decisions, divides T by (1 - alpha) and queues each contributing
 //     sample (hit point in [0,1]^3, alpha T, levels, record, T);
@@ -40,10 +40,21 @@
 namespace ns {
 namespace {
 
-constexpr int kThreads = kTilePixels;
+// A tile is split into bands of kRows rows, one CTA each: a CTA's barriers
+// then hold only its band's two warps, which wait less for one another than a
+// whole tile's eight, and the band walks its list only up to its own largest
+// last contributor. Measured on the config-4 step (median backward): 16x16
+// CTAs with 256-record batches 17.24 ms, 16x8 with 128 17.0, 16x4 with 64
+// 16.55 and with 8-deep queues 16.40, 16x2 with 64 17.3-17.7.
+constexpr int kRows = 4;                   // tile rows per CTA
+constexpr int kBands = kTile / kRows;      // CTAs per tile
+constexpr int kThreads = kTile * kRows;    // one thread per pixel of the band
 constexpr int kWarps = kThreads / 32;
-constexpr int kBatch = 256;     // records per batch (gathered back to front, one per thread)
-constexpr int kQueue = 4;       // queued samples per pixel between drains
+constexpr int kBatch = 64;        // records per batch (gathered back to front)
+static_assert(kTile % kRows == 0 && kRows % 2 == 0, "bands of whole warps (two rows each)");
+static_assert(kBatch <= 256, "a sample's record index is one byte");
+constexpr int kQueue = 8;       // queued samples per pixel between drains
+static_assert(kQueue <= 8, "a list entry holds the queue slot in three bits");
 constexpr int kGradWords = 20;  // per-surfel accumulator words (18 used), 80 bytes
 constexpr float kAggScale = 128.f;  // table-gradient aggregation below this level resolution
 
@@ -314,7 +325,7 @@ __device__ __forceinline__ float sh_hybrid_backward(const BackwardParams& p, con
 // variant 1's loop. kFixed: the table gradient goes to p.dL_dtable_fixed in
 // fixed point (deterministic mode).
 template <typename TableT, int kVariant, bool kFixed>
-__global__ void __launch_bounds__(kThreads, 2) blend_backward_kernel(const BackwardParams p) {
+__global__ void __launch_bounds__(kThreads, 2 * kBands) blend_backward_kernel(const BackwardParams p) {
   constexpr bool kAnyKernel = kVariant != 0;
   constexpr bool kSH = kVariant == 2;
   extern __shared__ __align__(16) unsigned char smem_raw[];
@@ -322,10 +333,11 @@ __global__ void __launch_bounds__(kThreads, 2) blend_backward_kernel(const Backw
 
   const int t = threadIdx.x, lane = t & 31, wid = t >> 5;
   const int gx = div_up(p.W, kTile);
-  const int tile = p.tile_order ? (int)p.tile_order[blockIdx.x] : (int)blockIdx.x;  // heaviest first
+  const int slot = (int)blockIdx.x / kBands, band = (int)blockIdx.x % kBands;
+  const int tile = p.tile_order ? (int)p.tile_order[slot] : slot;  // heaviest first
   const int tx = tile % gx, ty = tile / gx;
   const uint32_t px = tx * kTile + (t & (kTile - 1));
-  const uint32_t py = ty * kTile + (t >> 4);
+  const uint32_t py = ty * kTile + band * kRows + (t >> 4);
   const bool inside = px < (uint32_t)p.W && py < (uint32_t)p.H;
   const uint32_t pid = py * p.W + px;
   const float pxf = (float)px, pyf = (float)py;
@@ -422,14 +434,17 @@ __global__ void __launch_bounds__(kThreads, 2) blend_backward_kernel(const Backw
     const int hi = total - r * kBatch;
     const int lo = max(0, hi - kBatch);
     const int todo = hi - lo;
-    if (t < todo) {
-      const uint32_t id = p.point_list[range.x + hi - 1 - t];
-      S.ids[t] = id;
-      const float4* src = reinterpret_cast<const float4*>(p.records + id);
 #pragma unroll
-      for (int q = 0; q < kRecordFloat4; q++) {
-        const unsigned dst = (unsigned)__cvta_generic_to_shared(&S.rec[t][q]);
-        asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src + q));
+    for (int i = t; i < kBatch; i += kThreads) {
+      if (i < todo) {
+        const uint32_t id = p.point_list[range.x + hi - 1 - i];
+        S.ids[i] = id;
+        const float4* src = reinterpret_cast<const float4*>(p.records + id);
+#pragma unroll
+        for (int q = 0; q < kRecordFloat4; q++) {
+          const unsigned dst = (unsigned)__cvta_generic_to_shared(&S.rec[i][q]);
+          asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src + q));
+        }
       }
     }
     asm volatile("cp.async.commit_group;");
@@ -1190,7 +1205,7 @@ int launch_backward3(const BackwardParams& p, int tiles, cudaStream_t stream) {
   const int smem = (int)sizeof(BwSmem);
   NS_CUDA_TRY(cudaFuncSetAttribute(blend_backward_kernel<TableT, kVariant, kFixed>,
                                    cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-  blend_backward_kernel<TableT, kVariant, kFixed><<<tiles, kThreads, smem, stream>>>(p);
+  blend_backward_kernel<TableT, kVariant, kFixed><<<tiles * kBands, kThreads, smem, stream>>>(p);
   NS_LAUNCH_CHECK();
   return NS_OK;
 }
