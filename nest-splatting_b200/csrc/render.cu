@@ -8,12 +8,14 @@
 //   hashgrid.h:53-212), feature compositing (:1914-1916), level colour
 //   (:1945-1957), transmittance record (:1961-1964), outputs (:2008-2048).
 //
-// One CTA of 256 threads per 16x16 tile, one thread per pixel; warp w owns tile
-// rows 2w and 2w+1. The tile's surfel records stream through a ring of four
-// 32-record slots in shared memory (cp.async, completion on an mbarrier per
-// slot); the last warp to finish a batch refills its slot, so warps never meet
-// at a CTA barrier and drift up to three batches apart. Each warp alternates,
-// on its own 32 pixels, between two phases:
+// One CTA of 128 threads per band of eight rows of a 16x16 tile (two CTAs per
+// tile), one thread per pixel; warp w owns band rows 2w and 2w+1. The tile's
+// surfel records stream through a ring of two 32-record slots in shared memory
+// (cp.async, completion on an mbarrier per slot); the last warp to finish a
+// batch refills its slot, so warps never meet at a CTA barrier and drift up to
+// one batch apart. A band whose pixels are all done leaves and frees its SM
+// slot for the next band. Each warp alternates, on its own 32 pixels, between
+// two phases:
 //
 //   Phase A (intersect). The warp walks the batch in the reference's
 //   front-to-back order, all lanes at the same position (a warp-uniform skip
@@ -43,19 +45,28 @@
 namespace ns {
 namespace {
 
-constexpr int kThreads = kTilePixels;  // 256: one pixel per thread
+// Measured on the config-2 frame (blend, CUDA events; same images): 16 rows
+// with four slots 5.034 ms, 8 rows with four 5.27, 8 rows with two 4.922
+// (kept), 4 rows with two 5.52, with four 6.48. Four 8-row CTAs of 47.7 KB per
+// SM keep the 16 warps and the ~60 KB of L1 of two 97 KB 16-row CTAs; the
+// four-slot 8-row ring and the 4-row bands take L1 down to ~28 KB.
+constexpr int kRows = 8;               // tile rows per CTA
+constexpr int kBands = kTile / kRows;  // CTAs per tile
+constexpr int kThreads = kTile * kRows;  // one pixel per thread
 constexpr int kQueue = 8;              // queued samples per pixel between drains
 constexpr int kWarps = kThreads / 32;
 constexpr int kBatch = 32;             // surfel records per ring slot
-constexpr int kSlots = 4;              // ring slots (batches in flight)
+constexpr int kSlots = 2;              // ring slots (batches in flight), a power of two
 constexpr int kChunk = 32;             // compacted samples looked up per warp step (1 per lane)
+static_assert(kTile % kRows == 0 && kRows % 2 == 0, "bands of whole warps (two rows each)");
+static_assert((kSlots & (kSlots - 1)) == 0 && kBatch % 32 == 0, "ring slot index and fill shape");
 constexpr int kMaxChannels = 32;
 
 struct BlendSmem {
   float4 rec[kSlots][kBatch][kRecordFloat4];  // ring of surfel-record batches
   float4 samp[kQueue][kThreads];        // (hit point in [0,1]^3, weight)
   uint8_t lvl[kQueue][kThreads];        // levels to query for the sample (0: none)
-  uint8_t item[kWarps][kThreads];       // per warp: queued samples in k-major order, (k << 5) | lane
+  uint8_t item[kWarps][kQueue * 32];    // per warp: queued samples in k-major order, (k << 5) | lane
   uint8_t pos[kQueue][kThreads];        // position of a pixel's k-th sample in its warp's list
   float4 res[2][kWarps][kChunk];        // lookups of the current chunk: levels l, l+1 | l+2, l+3 per entry
                                         // (two arrays, so a lane's stores and reads are 16-byte
@@ -251,7 +262,7 @@ __device__ __forceinline__ void residual_sh(const RenderParams& p, uint32_t id, 
 // modes 8-11, whose per-sample lookup and SH evaluation would otherwise take
 // registers from variant 1's loop.
 template <typename TableT, int kVariant>
-__global__ void __launch_bounds__(kThreads, 2) blend_kernel(const RenderParams p) {
+__global__ void __launch_bounds__(kThreads, 2 * kBands) blend_kernel(const RenderParams p) {
   constexpr bool kGeneral = kVariant != 0;
   constexpr bool kSH = kVariant == 2;
   extern __shared__ __align__(16) unsigned char smem_raw[];
@@ -259,10 +270,11 @@ __global__ void __launch_bounds__(kThreads, 2) blend_kernel(const RenderParams p
 
   const int t = threadIdx.x;
   const int gx = div_up(p.W, kTile);
-  const int tile = p.tile_order ? (int)p.tile_order[blockIdx.x] : (int)blockIdx.x;  // heaviest first
+  const int slot = (int)blockIdx.x / kBands, band = (int)blockIdx.x % kBands;
+  const int tile = p.tile_order ? (int)p.tile_order[slot] : slot;  // heaviest first
   const int tx = tile % gx, ty = tile / gx;
   const uint32_t px = tx * kTile + (t & (kTile - 1));
-  const uint32_t py = ty * kTile + (t >> 4);
+  const uint32_t py = ty * kTile + band * kRows + (t >> 4);
   const bool inside = px < (uint32_t)p.W && py < (uint32_t)p.H;
   const uint32_t pid = py * p.W + px;
   const float pxf = (float)px, pyf = (float)py;
@@ -292,11 +304,12 @@ __global__ void __launch_bounds__(kThreads, 2) blend_kernel(const RenderParams p
   float pos0 = 0, pos1 = 0, pos2 = 0, vis0 = 0, vis1 = 0;
   bool done = !inside;
 
-  // Record ring: slot s holds batch b (b % kSlots == s). Warp w < kSlots fills
-  // batch w; after that the last warp to finish batch b refills its slot with
-  // batch b + kSlots, so warps drift up to kSlots - 1 batches apart instead of
-  // meeting at a CTA barrier per batch. Each lane of the filling warp copies two
-  // records and arrives on full[s] when its copies have landed.
+  // Record ring: slot s holds batch b (b % kSlots == s). Warp w fills batches
+  // w, w + kWarps, ... below kSlots; after that the last warp to finish batch b
+  // refills its slot with batch b + kSlots, so warps drift up to kSlots - 1
+  // batches apart instead of meeting at a CTA barrier per batch. Each lane of
+  // the filling warp copies one record and arrives on full[s] when its copies
+  // have landed.
   const int lane = t & 31, wid = t >> 5, pbase = wid * 32;
   auto fetch = [&](int b) {
     const int s = b & (kSlots - 1);
@@ -400,7 +413,7 @@ __global__ void __launch_bounds__(kThreads, 2) blend_kernel(const RenderParams p
   };
 
   __syncthreads();  // level table, accumulators and ring barriers are initialised
-  if (wid < kSlots && wid < rounds) fetch(wid);
+  for (int b0 = wid; b0 < kSlots && b0 < rounds; b0 += kWarps) fetch(b0);
   bool wdone = !__any_sync(0xffffffffu, !done);
   if (wdone && lane == 0) atomicAdd(&S.ndone, 1);
   for (int b = 0; b < rounds; b++) {
@@ -659,7 +672,7 @@ int launch_blend(const RenderParams& p, int tiles, cudaStream_t stream) {
   NS_CUDA_TRY(cudaFuncSetAttribute(blend_kernel<TableT, kVariant>,
                                    cudaFuncAttributeMaxDynamicSharedMemorySize,
                                    smem));
-  blend_kernel<TableT, kVariant><<<tiles, kThreads, smem, stream>>>(p);
+  blend_kernel<TableT, kVariant><<<tiles * kBands, kThreads, smem, stream>>>(p);
   NS_LAUNCH_CHECK();
   return NS_OK;
 }
