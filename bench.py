@@ -534,7 +534,7 @@ def run_ours(args):
         "rvq_decode": {"gbs": round(rvq_gbs, 1) if rvq_gbs else None,
                        "frac_of_hbm": round(rvq_gbs / hbm_peak, 4) if rvq_gbs else None,
                        "bytes_per_surfel": fr.stages + 4 * fr.dims},
-        "roofline": {"kernel": "blend_kernel<__half, false>", "bound": "l1/l2 gather",
+        "roofline": {"kernel": "blend_kernel<__half, 0>", "bound": "l1/l2 gather",
                      "achieved": round(gather_gbs, 1), "peak": gpeak["gbs"], "unit": "GB/s",
                      "frac": round(gather_gbs / gpeak["gbs"], 4), "traffic": traffic,
                      "peak_kind": "measured in this run (gather_peak: ns_gather_probe on the same table)",
