@@ -340,6 +340,7 @@ __global__ void __launch_bounds__(kThreads, 2 * kBands) blend_kernel(const Rende
     // samples; neighbouring pixels' k-th samples stay adjacent (coalescing).
     const uint32_t lt = lane_mask_lt();
     int nitems = 0;
+    int nfull = 0;  // leading queue slots that every pixel of the warp fills
 #pragma unroll
     for (int k = 0; k < kQueue; k++) {
       const uint32_t m = __ballot_sync(0xffffffffu, cnt > k);
@@ -348,6 +349,7 @@ __global__ void __launch_bounds__(kThreads, 2 * kBands) blend_kernel(const Rende
         S.item[wid][ps] = (uint8_t)((k << 5) | lane);
         S.pos[k][t] = (uint8_t)ps;
       }
+      if (nfull == k && m == 0xffffffffu) nfull++;
       nitems += __popc(m);
     }
     __syncwarp();
@@ -385,6 +387,16 @@ __global__ void __launch_bounds__(kThreads, 2 * kBands) blend_kernel(const Rende
         float2 r[4];
 #pragma unroll
         for (int q = 0; q < 4; q++) r[q] = u[q] ? lookup_finish<TableT>(f[q], v[q]) : make_float2(0.f, 0.f);
+        if (ch < kChunk * nfull) {
+          // A chunk of a slot that every pixel fills: entry ch + lane is this
+          // lane's own sample nk = ch / 32, so its results stay in registers.
+          const float2 ww = make_float2(sa.w, sa.w);
+#pragma unroll
+          for (int q = 0; q < 4; q++)
+            if (u[q]) c[q] = __ffma2_rn(r[q], ww, c[q]);
+          nk++;
+          continue;
+        }
         S.res[0][wid][lane] = make_float4(r[0].x, r[0].y, r[1].x, r[1].y);
         S.res[1][wid][lane] = make_float4(r[2].x, r[2].y, r[3].x, r[3].y);
         __syncwarp();
