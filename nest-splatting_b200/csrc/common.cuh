@@ -13,7 +13,6 @@ namespace ns {
 // Tile geometry and rasterizer constants (cuda_rasterizer/config.h:17-18,
 // auxiliary.h:42-45 of the reference).
 constexpr int kTile = 16;
-constexpr int kTilePixels = kTile * kTile;
 constexpr float kNear = 0.2f;
 constexpr float kFar = 100.0f;
 constexpr float kFilterSize = 0.707106f;
