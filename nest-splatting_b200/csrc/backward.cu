@@ -56,7 +56,13 @@ static_assert(kBatch <= 256, "a sample's record index is one byte");
 constexpr int kQueue = 8;       // queued samples per pixel between drains
 static_assert(kQueue <= 8, "a list entry holds the queue slot in three bits");
 constexpr int kGradWords = 20;  // per-surfel accumulator words (18 used), 80 bytes
-constexpr float kAggScale = 128.f;  // table-gradient aggregation below this level resolution
+// Table-gradient aggregation on levels below this resolution (cells per axis):
+// float atomics 512, fixed-point atomics (two 64-bit adds per corner, dearer
+// than one float2 reduction) 1024. Measured on the config-4 step (median
+// backward, ms, float / fixed point): 128: 16.42 / 25.34, 256: 16.15 / 23.1,
+// 512: 16.13-16.18 / 22.0, 1024: 16.34-16.39 / 21.7, every level: 16.78 / 21.9.
+constexpr float kAggScaleFloat = 512.f;
+constexpr float kAggScaleFixed = 1024.f;
 
 // Accumulator words of one surfel (80 bytes, five float4 groups; the last group
 // is non-zero only for samples of the rho2d branch and for the shape gradient of
@@ -655,10 +661,10 @@ __global__ void __launch_bounds__(kThreads, 2 * kBands) blend_backward_kernel(co
           const uint32_t act = __ballot_sync(0xffffffffu, on);
           int nxt = -1;
           bool head = true;
-          // Coarse levels only (fewer than kAggScale cells per axis): finer cells
-          // are rarely shared by a warp's samples and their atomics do not
+          // Coarser levels only (fewer than kAggScale* cells per axis): finer
+          // cells are rarely shared by a warp's samples and their atomics do not
           // contend, so the grouping would cost more than it saves.
-          if (on && lcst.scale < kAggScale) {
+          if (on && lcst.scale < (kFixed ? kAggScaleFixed : kAggScaleFloat)) {
             head = false;
             const unsigned long long key =
                 (unsigned long long)gc[0] | ((unsigned long long)gc[1] << 21) | ((unsigned long long)gc[2] << 42);
