@@ -9,11 +9,11 @@
 // Numerics: inputs and weights fp16, fp32 accumulation, each layer's output
 // rounded to fp16 (the next layer's operand and the network output dtype).
 //
-// Tensor-core mapping: mma.sync m16n8k16 (f16 x f16 -> f32). A warp owns 16
-// pixels; layer l's fp32 accumulator fragments are rounded to f16x2 in place
-// and become the A fragments of layer l+1 without touching shared memory. The
-// weights live in shared memory with padded rows (conflict-free fragment
-// loads). The MLP is 14.3 kFLOP per pixel: it is a small share of a frame.
+// Forward: tcgen05.mma on 128-pixel tiles with the accumulators in TMEM
+// (mlp_tc.cuh). Backward: mma.sync (m16n8k16 fp16 for the recomputed forward,
+// m16n8k8 TF32 for the gradients), a warp per 16 pixels, weights in shared
+// memory with padded rows (conflict-free fragment loads). The MLP is 14.3
+// kFLOP per pixel: it is a small share of a frame.
 #include "common.cuh"
 
 namespace ns {
@@ -22,7 +22,6 @@ namespace {
 constexpr int kIn = 32, kHid = 64, kOut = 8;  // output padded to one n-tile
 constexpr int kW1Stride = kIn + 8;            // halves per padded row
 constexpr int kW2Stride = kHid + 8;
-constexpr int kMlpWarps = 4;
 
 struct MlpSmem {
   __half w1[kHid * kW1Stride];
@@ -62,127 +61,9 @@ __device__ void load_weights(MlpSmem& S, const uint16_t* __restrict__ w) {
   }
 }
 
-// MLP of 16 pixels held by one warp. a_in: layer-1 A fragments (2 k-steps).
-// Returns the output fragment (cols 0..7 of rows g and g+8; cols 0..2 valid),
-// already rounded through fp16.
-__device__ __forceinline__ void mlp16(const MlpSmem& S, const uint32_t (&a_in)[2][4],
-                                      float (&y)[4]) {
-  const int lane = threadIdx.x & 31, g = lane >> 2, tig = lane & 3;
-  // Layer 1: [16 x 32] x [32 x 64]
-  float h1[8][4];
-#pragma unroll
-  for (int j = 0; j < 8; j++) {
-    h1[j][0] = h1[j][1] = h1[j][2] = h1[j][3] = 0.f;
-#pragma unroll
-    for (int s = 0; s < 2; s++) {
-      const __half* wr = S.w1 + (8 * j + g) * kW1Stride + 16 * s + 2 * tig;
-      mma16816(h1[j], a_in[s], lds32(wr), lds32(wr + 8));
-    }
-  }
-  uint32_t a2[4][4];
-#pragma unroll
-  for (int s = 0; s < 4; s++) {
-    a2[s][0] = pack_half2(fmaxf(h1[2 * s][0], 0.f), fmaxf(h1[2 * s][1], 0.f));
-    a2[s][1] = pack_half2(fmaxf(h1[2 * s][2], 0.f), fmaxf(h1[2 * s][3], 0.f));
-    a2[s][2] = pack_half2(fmaxf(h1[2 * s + 1][0], 0.f), fmaxf(h1[2 * s + 1][1], 0.f));
-    a2[s][3] = pack_half2(fmaxf(h1[2 * s + 1][2], 0.f), fmaxf(h1[2 * s + 1][3], 0.f));
-  }
-  // Layer 2: [16 x 64] x [64 x 64]
-  float h2[8][4];
-#pragma unroll
-  for (int j = 0; j < 8; j++) {
-    h2[j][0] = h2[j][1] = h2[j][2] = h2[j][3] = 0.f;
-#pragma unroll
-    for (int s = 0; s < 4; s++) {
-      const __half* wr = S.w2 + (8 * j + g) * kW2Stride + 16 * s + 2 * tig;
-      mma16816(h2[j], a2[s], lds32(wr), lds32(wr + 8));
-    }
-  }
-  uint32_t a3[4][4];
-#pragma unroll
-  for (int s = 0; s < 4; s++) {
-    a3[s][0] = pack_half2(fmaxf(h2[2 * s][0], 0.f), fmaxf(h2[2 * s][1], 0.f));
-    a3[s][1] = pack_half2(fmaxf(h2[2 * s][2], 0.f), fmaxf(h2[2 * s][3], 0.f));
-    a3[s][2] = pack_half2(fmaxf(h2[2 * s + 1][0], 0.f), fmaxf(h2[2 * s + 1][1], 0.f));
-    a3[s][3] = pack_half2(fmaxf(h2[2 * s + 1][2], 0.f), fmaxf(h2[2 * s + 1][3], 0.f));
-  }
-  // Layer 3: [16 x 64] x [64 x 8]
-  y[0] = y[1] = y[2] = y[3] = 0.f;
-#pragma unroll
-  for (int s = 0; s < 4; s++) {
-    const __half* wr = S.w3 + g * kW2Stride + 16 * s + 2 * tig;
-    mma16816(y, a3[s], lds32(wr), lds32(wr + 8));
-  }
-#pragma unroll
-  for (int i = 0; i < 4; i++) y[i] = __half2float(__float2half_rn(y[i]));
-}
-
 __device__ __forceinline__ float sigmoidf(float x) { return 1.0f / (1.0f + expf(-x)); }
 
-__global__ void __launch_bounds__(kMlpWarps * 32)
-mlp_kernel(const float* __restrict__ feat, int64_t npix, const uint16_t* __restrict__ weights,
-           const float* __restrict__ alpha, float bg0, float bg1, float bg2, int use_bg,
-           float* __restrict__ rgb) {
-  __shared__ MlpSmem S;
-  load_weights(S, weights);
-  __syncthreads();
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, g = lane >> 2, tig = lane & 3;
-  const int64_t ntiles = div_up64(npix, 16);
-  const int64_t tstride = (int64_t)gridDim.x * kMlpWarps;
-  // The next tile's feature loads are issued before this tile's MMAs (one tile
-  // of loads in flight per warp while the tensor cores run).
-  float fr[2][8];
-  auto fetch = [&](int64_t tl) {
-    const int64_t q0 = tl * 16 + g, q1 = q0 + 8;
-    const bool w0 = tl < ntiles && q0 < npix, w1 = tl < ntiles && q1 < npix;
-#pragma unroll
-    for (int s = 0; s < 2; s++) {
-      const int c = 16 * s + 2 * tig;
-      auto ld = [&](int ch, int64_t px, bool v) { return v ? __ldg(feat + ch * npix + px) : 0.f; };
-      fr[s][0] = ld(c, q0, w0);
-      fr[s][1] = ld(c + 1, q0, w0);
-      fr[s][2] = ld(c, q1, w1);
-      fr[s][3] = ld(c + 1, q1, w1);
-      fr[s][4] = ld(c + 8, q0, w0);
-      fr[s][5] = ld(c + 9, q0, w0);
-      fr[s][6] = ld(c + 8, q1, w1);
-      fr[s][7] = ld(c + 9, q1, w1);
-    }
-  };
-  fetch((int64_t)blockIdx.x * kMlpWarps + warp);
-  for (int64_t tile = (int64_t)blockIdx.x * kMlpWarps + warp; tile < ntiles; tile += tstride) {
-    const int64_t p0 = tile * 16 + g, p1 = p0 + 8;
-    const bool v0 = p0 < npix, v1 = p1 < npix;
-    uint32_t a[2][4];
-#pragma unroll
-    for (int s = 0; s < 2; s++) {
-      a[s][0] = pack_half2(fr[s][0], fr[s][1]);
-      a[s][1] = pack_half2(fr[s][2], fr[s][3]);
-      a[s][2] = pack_half2(fr[s][4], fr[s][5]);
-      a[s][3] = pack_half2(fr[s][6], fr[s][7]);
-    }
-    fetch(tile + tstride);
-
-    float y[4];
-    mlp16(S, a, y);
-    // y[0..1]: row g cols 2tig, 2tig+1; y[2..3]: row g+8.
-#pragma unroll
-    for (int r = 0; r < 2; r++) {
-      const int64_t px = r ? p1 : p0;
-      if (!(r ? v1 : v0)) continue;
-      const float a_px = alpha ? alpha[px] : 1.0f;
-#pragma unroll
-      for (int cc = 0; cc < 2; cc++) {
-        const int col = 2 * tig + cc;
-        if (col >= 3) continue;
-        float v = sigmoidf(y[2 * r + cc]);
-        if (alpha && !(a_px > 0.f)) v = 0.f;
-        if (use_bg) v += (1.0f - a_px) * (col == 0 ? bg0 : col == 1 ? bg1 : bg2);
-        rgb[col * npix + px] = v;
-      }
-    }
-  }
-}
+#include "mlp_tc.cuh"
 
 }  // namespace
 
@@ -205,10 +86,10 @@ int mlp_launch(const float* feat, int in_dims, int64_t npix, const uint16_t* wei
   int dev = 0, sms = 0;
   NS_CUDA_TRY(cudaGetDevice(&dev));
   NS_CUDA_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
-  const int64_t ntiles = div_up64(npix, 16);
-  const int blocks = (int)min64(div_up64(ntiles, kMlpWarps), (int64_t)sms * 8);
-  mlp_kernel<<<blocks, kMlpWarps * 32, 0, stream>>>(feat, npix, weights, alpha, b0, b1, b2, use_bg,
-                                                    rgb);
+  NS_CUDA_TRY(cudaFuncSetAttribute(mlp_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kTcSmemBytes));
+  const int blocks = (int)min64(div_up64(npix, kTcThreads), (int64_t)sms * 4);
+  mlp_tc_kernel<<<blocks, kTcThreads, kTcSmemBytes, stream>>>(feat, npix, weights, alpha, b0, b1, b2, use_bg,
+                                                              rgb);
   NS_LAUNCH_CHECK();
   return NS_OK;
 }
@@ -216,7 +97,7 @@ int mlp_launch(const float* feat, int in_dims, int64_t npix, const uint16_t* wei
 // ---------------------------------------------------------------------------
 // Backward of the colour MLP (the training step's d loss / d features and
 // d loss / d weights), fused: per 16-pixel warp tile the forward is recomputed
-// exactly as mlp_kernel computes it (fp16 operands, fp32 accumulation, each
+// with the forward's roundings (fp16 operands, fp32 accumulation, each
 // layer rounded to fp16, ReLU masks kept as bits), then
 //   dz3 = g * (alpha > 0) * s (1 - s)           s = sigmoid(z3), 3 outputs
 //   dz2 = (dz3 W3) * (z2 > 0),  dz1 = (dz2 W2) * (z1 > 0),  dfeat = dz1 W1
@@ -288,7 +169,7 @@ mlp_backward_kernel(const float* __restrict__ feat, int64_t npix, const uint16_t
   for (int64_t blk = blockIdx.x; blk < nblocks; blk += gridDim.x) {
     const int64_t p0 = blk * kBwPix + r0, p1 = blk * kBwPix + r1;
     const bool v0 = p0 < npix, v1 = p1 < npix;
-    // ---- forward recompute (as mlp16), keeping ReLU masks and staging a1, a2, x.
+    // ---- forward recompute (the forward's layers and roundings), keeping ReLU masks and staging a1, a2, x.
     uint32_t a[2][4];
 #pragma unroll
     for (int s = 0; s < 2; s++) {
