@@ -366,6 +366,25 @@ __global__ void __launch_bounds__(kThreads, 2 * kBands) blend_kernel(const Rende
         c[q] = (uint32_t)q < nl ? *ap[q] : make_float2(0.f, 0.f);
       }
       int nk = 0;
+      // The owners add chunk ch - 32's staged results while chunk ch's corner
+      // loads are in flight; the last staged chunk is added after the loop.
+      bool staged = false;
+      auto owners = [&](int chp) {
+        while (nk < cnt) {
+          const int ps = S.pos[nk][t];
+          if (ps >= chp + kChunk) break;
+          const float4 r01 = S.res[0][wid][ps - chp];
+          const float4 r23 = S.res[1][wid][ps - chp];
+          const uint32_t mk = S.lvl[nk][t];
+          const float w = S.samp[nk][t].w;
+          const float2 ww = make_float2(w, w);
+          if (l < mk) c[0] = __ffma2_rn(make_float2(r01.x, r01.y), ww, c[0]);
+          if (l + 1 < mk && nl > 1) c[1] = __ffma2_rn(make_float2(r01.z, r01.w), ww, c[1]);
+          if (l + 2 < mk && nl > 2) c[2] = __ffma2_rn(make_float2(r23.x, r23.y), ww, c[2]);
+          if (l + 3 < mk && nl > 3) c[3] = __ffma2_rn(make_float2(r23.z, r23.w), ww, c[3]);
+          nk++;
+        }
+      };
       for (int ch = 0; ch < nitems; ch += kChunk) {
         float4 sa = make_float4(0.f, 0.f, 0.f, 0.f);
         uint32_t ma = 0;
@@ -384,12 +403,15 @@ __global__ void __launch_bounds__(kThreads, 2 * kBands) blend_kernel(const Rende
           u[q] = (uint32_t)q < nl && l + q < ma;
           if (u[q]) lookup_issue<TableT>(S.lv[l + q], p.table, sa, half_shift, p.interp, f[q], v[q]);
         }
+        if (staged) {
+          owners(ch - kChunk);
+          __syncwarp();
+          staged = false;
+        }
         float2 r[4];
 #pragma unroll
         for (int q = 0; q < 4; q++) r[q] = u[q] ? lookup_finish<TableT>(f[q], v[q]) : make_float2(0.f, 0.f);
         if (ch < kChunk * nfull) {
-          // A chunk of a slot that every pixel fills: entry ch + lane is this
-          // lane's own sample nk = ch / 32, so its results stay in registers.
           const float2 ww = make_float2(sa.w, sa.w);
 #pragma unroll
           for (int q = 0; q < 4; q++)
@@ -400,20 +422,10 @@ __global__ void __launch_bounds__(kThreads, 2 * kBands) blend_kernel(const Rende
         S.res[0][wid][lane] = make_float4(r[0].x, r[0].y, r[1].x, r[1].y);
         S.res[1][wid][lane] = make_float4(r[2].x, r[2].y, r[3].x, r[3].y);
         __syncwarp();
-        while (nk < cnt) {
-          const int ps = S.pos[nk][t];
-          if (ps >= ch + kChunk) break;
-          const float4 r01 = S.res[0][wid][ps - ch];
-          const float4 r23 = S.res[1][wid][ps - ch];
-          const uint32_t mk = S.lvl[nk][t];
-          const float w = S.samp[nk][t].w;
-          const float2 ww = make_float2(w, w);
-          if (l < mk) c[0] = __ffma2_rn(make_float2(r01.x, r01.y), ww, c[0]);
-          if (l + 1 < mk && nl > 1) c[1] = __ffma2_rn(make_float2(r01.z, r01.w), ww, c[1]);
-          if (l + 2 < mk && nl > 2) c[2] = __ffma2_rn(make_float2(r23.x, r23.y), ww, c[2]);
-          if (l + 3 < mk && nl > 3) c[3] = __ffma2_rn(make_float2(r23.z, r23.w), ww, c[3]);
-          nk++;
-        }
+        staged = true;
+      }
+      if (staged) {
+        owners(((nitems - 1) / kChunk) * kChunk);
         __syncwarp();
       }
 #pragma unroll
