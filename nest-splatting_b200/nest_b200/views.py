@@ -142,7 +142,8 @@ class DecodeRing:
         dev = rvq_idx.device
         self.cuda = dev.type == "cuda"
         if self.cuda:
-            self.stream = torch.cuda.Stream(device=dev)
+            # high priority: the decode's CTAs start as the render's CTAs retire
+            self.stream = torch.cuda.Stream(device=dev, priority=-1)
             self.ready = [torch.cuda.Event() for _ in range(2)]
             self.free = [torch.cuda.Event() for _ in range(2)]
         self.used = [False, False]
