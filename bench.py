@@ -1,4 +1,4 @@
-"""Benchmark of the nest-splatting render hot path on B200.
+"""Benchmark of the nest-splatting render hot path on B200 (benchmark config 2).
 
 One step = one frame of config 2: 1,000,000 surfels whose attributes come from
 an RVQ stream decoded on the fly (6 stages x 256 x 59 fp32 codebooks), rendered
@@ -140,7 +140,7 @@ def profiled_traffic():
 
 
 def train_step_timing(sc, cam, dev, steps, warmup=2):
-    """one training step (forward, MLP, L1 + normal loss,
+    """benchmark config 4: one training step (forward, MLP, L1 + normal loss,
     backward into the surfels, the hash table and the MLP) on the config-2 scene."""
     import torch
 
@@ -263,7 +263,7 @@ def gather_peak(fr, dev, cam, lookups=128, reps=5):
 
 
 def rvq_timing(dev, hbm_peak, sizes=(200_000, 1_000_000, 3_000_000), iters=20, warmup=3):
-    """RVQ decode (BASELINE config 0 codebooks and indices) on the GPU at the
+    """RVQ decode (benchmark config 0 codebooks and indices) on the GPU at the
     sizes the scope names: median device time of `iters` runs after `warmup`,
     L2 flushed before each (the 200k output fits in L2)."""
     import torch
@@ -295,7 +295,7 @@ def rvq_timing(dev, hbm_peak, sizes=(200_000, 1_000_000, 3_000_000), iters=20, w
 
 
 def rvq_cpu_timing(n=200_000, iters=20, warmup=3):
-    """The reference's PyTorch CPU path of the RVQ decode:
+    """The reference's PyTorch CPU path of the RVQ decode (benchmark config 0):
     index_select + in-order adds on the host cores, all of them."""
     import torch
 
@@ -324,7 +324,7 @@ def rvq_cpu_timing(n=200_000, iters=20, warmup=3):
 
 
 def config1_timing(dev, steps=20, warmup=3):
-    """single-view forward render of 200k surfels at 800x800
+    """benchmark config 1: single-view forward render of 200k surfels at 800x800
     (rasterizer forward with its instance-count read-back, then the MLP with the
     alpha mask), device-timed per frame with the L2 flushed before each."""
     import torch
@@ -618,7 +618,7 @@ def graph_timing(fr, cam, view, proj, flush, steps):
 
 
 def exchange_timing(shard, codebooks, dev, P, stages, dims, iters=20):
-    """N > 1: the north_star's exchange (decode this rank's rows, all-gather the
+    """N > 1: the specified exchange (decode this rank's rows, all-gather the
     decoded attributes) against all-gathering the RVQ indices and decoding every
     row on every rank. Device time per exchange, max over ranks; both leave the
     same rows in the frame's attribute buffer."""
@@ -762,7 +762,7 @@ def run_reference(args):
 
 
 def multiview_timing(world, rank, dev, batches=2):
-    """a 64-view batch (1920x1080, 3M RVQ surfels, elevation
+    """benchmark config 3: a 64-view batch (1920x1080, 3M RVQ surfels, elevation
     20 deg, azimuth 360 i / 64) split over the ranks by camera. Per batch: the
     surfel-sharded RVQ decode and its all-gather once, then this rank's views.
     Time per batch = max over ranks (CUDA events), strong scaling in the ranks."""

@@ -17,7 +17,7 @@
  *   ns_mlp_forward        <- INGP.rgb_decode / get_color, hash_encoder/modules.py:587-602
  *                            (tiny-cuda-nn "MLP", no biases, sigmoid on the output)
  *   ns_rvq_decode         <- no reference counterpart: the RVQ attribute decode of
- *                            the BASELINE config-0 definition (new scope)
+ *                            the benchmark config-0 definition (new scope)
  *   ns_render_frame       <- gaussian_renderer/__init__.py:render() baseline branch
  *                            (:178-213, 694-797, 905-1021) fused with an RVQ attribute
  *                            decode: decode -> activate -> rasterize -> MLP -> mask/bg

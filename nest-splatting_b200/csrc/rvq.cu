@@ -1,7 +1,7 @@
 // rvq.cu -- residual-vector-quantised attribute decode.
 //
 // out[n, d] = sum_{k=0..K-1} codebooks[k, idx[n,k], d], accumulated in fp32 from
-// +0.0 in stage order k = 0, 1, ... (the reference repository
+// +0.0 in stage order k = 0, 1, ... (benchmark config 0; the reference repository
 // has no RVQ code, so this is new scope with a bit-exact contract).
 //
 // The whole codebook of the benchmark shape (6 x 256 x 59 fp32 = 354 KB) does

@@ -5,7 +5,7 @@ Modules:
   raster  torch-facing wrappers: rasterizer forward, MLP, RVQ decode, radix sort
   frame   the fused RVQ-driven frame (decode -> rasterize -> MLP)
   camera  pinhole cameras in the reference's conventions
-  synth   seeded synthetic scenes of the BASELINE configurations
+  synth   seeded synthetic scenes of the benchmark configurations
   views   multi-view batches sharded by camera over torch.distributed ranks
 """
 __all__ = ["_lib", "raster", "frame", "camera", "synth"]

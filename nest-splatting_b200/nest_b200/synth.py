@@ -1,11 +1,11 @@
-"""Seeded synthetic scenes for the BASELINE configurations.
+"""Seeded synthetic scenes for the benchmark configurations.
 
 No dataset or trained checkpoint exists on this machine, so every benchmark and
 parity case runs on scenes drawn here. Draw order (one torch.Generator per
 scene, CPU): surfel radii, directions, log-scales, quaternions, opacity logits,
 hash table, MLP weights, then (RVQ scenes) codebooks and indices.
 
-Surfels: means uniform in volume in the shell
+Surfels (benchmark config 1): means uniform in volume in the shell
 0.8 <= r <= 1.2 (r = cbrt(U(0.8^3, 1.2^3)), direction = normalised N(0, I3)),
 log-scales N(mean, std) on two axes, quaternions normalise(N(0, I4)), opacity
 = sigmoid(N(0, 1.5)). Hash grid: L levels x 2^log2_T rows x LD features, rows

@@ -1,4 +1,4 @@
-"""One training step of the baseline render mode, on torch
+"""One training step of the baseline render mode (benchmark config 4), on torch
 autograd around the library's kernels.
 
 Forward: the drop-in rasterizer (ns_rasterize_forward) -> the fp16 MLP

@@ -482,7 +482,7 @@ uint32_t oracle_grid_index(int align_corners, uint32_t hashmap_size, uint32_t re
   return grid_index(align_corners != 0, hashmap_size, res, g);
 }
 
-// RVQ decode (BASELINE config 0 definition; the reference has no RVQ code):
+// RVQ decode (benchmark config 0 definition; the reference has no RVQ code):
 // out[n,:] = sum over stages k = 0..K-1 of codebooks[k, idx[n,k], :], accumulated
 // in fp32 starting from +0.0 in stage order.
 void oracle_rvq_decode(int64_t n, int K, int E, int Dm, const uint8_t* idx, const float* cb,

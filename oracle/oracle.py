@@ -7,7 +7,7 @@ the product path (nest-splatting_b200) never calls it.
 Contents:
   * ctypes wrapper of oracle/_build/libnest_oracle.so (nest_oracle.cpp, the C++
     restatement of preprocess / binning / mode-0 blend / hash query);
-  * rvq_decode_np: numpy restatement of the RVQ decode (BASELINE config 0);
+  * rvq_decode_np: numpy restatement of the RVQ decode (benchmark config 0);
   * rvq_decode_torch: the "reference PyTorch CPU path" timed as the RVQ baseline;
   * mlp_oracle: fp16 MLP restatement (tiny-cuda-nn is not vendored: parity of
     the MLP is unpinned, this fixes one definition);

@@ -3,7 +3,7 @@ torch wrapper and through the drop-in autograd Function) against the CPU
 oracle's restatement of the reference backward (itself pinned to float64
 autograd in test_oracle_backward.py).
 
-Tolerance: every gradient within 1e-3 relative L2 of the
+Tolerance (the target specification): every gradient within 1e-3 relative L2 of the
 oracle. Where the reference's formulas are ill-conditioned in float32 that
 bar cannot be met by any float32 evaluation, the reference's included: with a
 hash table of large entries the hit-point term of the mean / rotation

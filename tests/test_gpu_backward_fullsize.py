@@ -1,5 +1,5 @@
 """Backward parity at the benchmarked size, and on a table without gradient
-discontinuities, with the north_star's 1e-3 relative L2 on whole gradients
+discontinuities, with the specification's 1e-3 relative L2 on whole gradients
 (at size, at most 10 of the 1M surfels left out for three gradients; see
 test_config4_gradients_at_size).
 

@@ -169,7 +169,7 @@ def test_binning_large_tilted_surfels_exact_and_conservative():
 
 
 def test_binning_config1_exact():
-    """BASELINE config 1 (200k surfels, 800x800)."""
+    """benchmark config 1 (200k surfels, 800x800)."""
     sc = synth.config1()
     b = _forward(sc, api_inputs(sc))
     ref_n, n = check_binning(b, sc.camera.width, sc.camera.height)
@@ -177,7 +177,7 @@ def test_binning_config1_exact():
 
 
 def test_binning_config2_exact():
-    """BASELINE config 2 geometry (1M surfels at 1297x840, RVQ-mixed attributes)."""
+    """benchmark config 2 geometry (1M surfels at 1297x840, RVQ-mixed attributes)."""
     from helpers import raw_attributes
 
     sc = synth.config2()

@@ -1,4 +1,4 @@
-"""Parity at the benchmarked sizes: BASELINE configs 1, 2 and 3 against the oracle.
+"""Parity at the benchmarked sizes: benchmark configs 1, 2 and 3 against the oracle.
 
 Config 2 (1M RVQ surfels, 1297x840) goes through the fused frame the bench
 times (FrameRenderer -> ns_render_frame: decode, mix + activation,
@@ -40,7 +40,7 @@ def _feat_tol(table_range, ref_color):
 
 @pytest.mark.parametrize("table_range", [1.0, 1e-4])
 def test_config1_fullsize_parity(table_range):
-    """BASELINE config 1 at full size: 200k surfels, 800x800, every pixel."""
+    """benchmark config 1 at full size: 200k surfels, 800x800, every pixel."""
     from test_gpu_raster import run_api
 
     sc = synth.config1(table_range=table_range)
@@ -55,7 +55,7 @@ def test_config1_fullsize_parity(table_range):
 
 @pytest.mark.parametrize("table_range", [1.0, 1e-4])
 def test_config2_frame_parity(table_range):
-    """the headline frame, RVQ decode included."""
+    """benchmark config 2: the headline frame, RVQ decode included."""
     sc = synth.config2(table_range=table_range)
     fr = FrameRenderer(sc, device="cuda")
     rgb = fr.render(sc.camera)
@@ -80,7 +80,7 @@ def test_config2_frame_parity(table_range):
 
 @pytest.mark.parametrize("table_range,view", [(1.0, 8), (1e-4, 40)])
 def test_config3_view_parity(table_range, view):
-    """one 1920x1080 view of the 64-view orbit batch
+    """benchmark config 3: one 1920x1080 view of the 64-view orbit batch
     (azimuth 360 view / 64, elevation 20 deg) of the 3M-surfel RVQ scene,
     rendered by the frame path the multi-view bench times."""
     import dataclasses

@@ -1,7 +1,7 @@
 """GPU parity of the rasterizer forward through the drop-in Python API
 (diff_surfel_rasterization -> libnest_b200.so C-ABI) against the CPU oracle.
 
-Tolerance: max-abs 2e-3 per channel for features, depth,
+Tolerance (the target specification): max-abs 2e-3 per channel for features, depth,
 normal and alpha, plus PSNR >= 60 dB. The table is drawn U(-1, 1) (the
 parity-stress range) so hash-gather mistakes cannot hide under tiny values.
 """

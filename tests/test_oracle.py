@@ -8,7 +8,7 @@ fix the restatement to hand-derived answers of the reference algorithm:
         pixel (forward.cu:839-929), depth = view z;
   (iv)  early termination on a stack of opacity-0.99 surfels, simulated in fp32
         (forward.cu:921-929: T*(1-a) < 1e-4 stops before blending);
-  (v)   RVQ decode of one-hot codebooks (BASELINE config 0 definition);
+  (v)   RVQ decode of one-hot codebooks (benchmark config 0 definition);
 plus stability of the tile/depth ordering (rasterizer_impl.cu:381-386).
 """
 import math
