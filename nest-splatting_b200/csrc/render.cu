@@ -35,7 +35,10 @@
 //   warp-uniform outer loop (the dense/hashed choice is a uniform branch), four
 //   levels of one list entry (four lookups) in flight per lane, so the list and
 //   the owners' queues are walked once per four levels. Each pixel's owner lane
-//   adds its results in queue order, the reference's per-pixel order.
+//   adds its results in queue order, the reference's per-pixel order: straight
+//   from its own registers for a queue slot that every pixel of the warp fills
+//   (that chunk of the list has lane = pixel), otherwise from a staging area,
+//   while the next chunk's corner loads are in flight.
 //
 // The hash table is read as fp16 (or fp32) pairs through the read-only path;
 // at 16 levels x 2^19 x 2 fp16 it is 32 MB and stays resident in the 126 MB L2.
